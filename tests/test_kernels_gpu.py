@@ -1,0 +1,301 @@
+# Numerics of every sm_100a kernel against a plain PyTorch fp32 reference of
+# the same op, on small shapes that still cover tails and every layout.
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def rel(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / b.norm().clamp(min=1e-12)).item()
+
+
+@pytest.fixture(autouse=True)
+def _seed():
+    torch.manual_seed(0)
+    yield
+    from vagus_b200 import ops
+    torch.cuda.synchronize()
+    ops.check_error()
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 300, 136), (1024, 4104, 1024), (64, 8, 64)])
+def test_gemm_layouts(a_mn, b_mn, M, N, K):
+    from vagus_b200.ops import native
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    Ast = A.t().contiguous() if a_mn else A
+    Bst = B.t().contiguous() if b_mn else B
+    ref = A.float() @ B.float().t()
+    C = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+    native().gemm(Ast, a_mn, Bst, b_mn, C, None, 1.0, 0.0, False, 0, 0)
+    assert rel(C, ref) < 1e-2
+    C32 = torch.empty(M, N, device=DEV, dtype=torch.float32)
+    native().gemm(Ast, a_mn, Bst, b_mn, C32, None, 1.0, 0.0, False, 0, 0)
+    assert rel(C32, ref) < 2e-3
+
+
+def test_gemm_epilogues_and_batch():
+    from vagus_b200.ops import native
+    M, N, K, Bt = 384, 640, 320, 3
+    A = torch.randn(Bt, M, K, device=DEV).bfloat16()
+    B = torch.randn(Bt, N, K, device=DEV).bfloat16()
+    S = torch.randn(Bt, M, N, device=DEV)
+    ref = 0.5 * (A.float() @ B.float().transpose(1, 2)) - 2.0 * S
+    C = torch.empty(Bt, M, N, device=DEV)
+    native().gemm(A, False, B, False, C, S, 0.5, -2.0, False, 0, 0)
+    assert rel(C, ref) < 2e-3
+    # atomic split-K accumulation into an fp32 buffer (weight-gradient shape)
+    T, Dout, Din = 4096, 256, 512
+    dy = torch.randn(T, Dout, device=DEV).bfloat16()
+    x = torch.randn(T, Din, device=DEV).bfloat16()
+    acc = torch.randn(Dout, Din, device=DEV)
+    ref = acc + dy.float().t() @ x.float()
+    native().gemm(dy, True, x, True, acc, None, 1.0, 0.0, True, 0, 0)
+    assert rel(acc, ref) < 2e-3
+    for bn in (128, 256):
+        C = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
+        native().gemm(A[0], False, B[0], False, C, None, 1.0, 0.0, False, 1, bn)
+        assert rel(C, A[0].float() @ B[0].float().t()) < 1e-2
+
+
+def test_linear_autograd():
+    from vagus_b200 import ops
+    x = torch.randn(3, 100, 256, device=DEV, requires_grad=True)
+    w = torch.randn(384, 256, device=DEV, requires_grad=True)
+    r = torch.randn(3, 100, 384, device=DEV, requires_grad=True)
+    y = ops.linear_residual(r, x.bfloat16(), w)
+    xr, wr, rr = (t.detach().clone().requires_grad_(True) for t in (x, w, r))
+    yr = rr + xr.bfloat16().float() @ wr.bfloat16().float().t()
+    g = torch.randn_like(yr)
+    (y * g).sum().backward()
+    (yr * g).sum().backward()
+    assert rel(y, yr) < 1e-2
+    assert rel(x.grad, xr.grad) < 1e-2 and rel(w.grad, wr.grad) < 1e-2 and rel(r.grad, rr.grad) < 1e-6
+
+
+@pytest.mark.parametrize("xdt,odt", [(torch.float32, torch.bfloat16), (torch.bfloat16, torch.bfloat16),
+                                     (torch.float32, torch.float32)])
+def test_rmsnorm(xdt, odt):
+    from vagus_b200 import ops
+    x = torch.randn(333, 1024, device=DEV, dtype=xdt, requires_grad=True)
+    g = (1 + 0.1 * torch.randn(1024, device=DEV)).requires_grad_(True)
+    y = ops.rmsnorm(x, g, 1e-6, out_dtype=odt)
+    xr, gr = x.detach().float().requires_grad_(True), g.detach().clone().requires_grad_(True)
+    yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * gr
+    dy = torch.randn_like(yr)
+    (y.float() * dy).sum().backward()
+    (yr * dy).sum().backward()
+    assert rel(y, yr) < 1e-2
+    assert rel(x.grad, xr.grad) < 1e-2 and rel(g.grad, gr.grad) < 1e-2
+
+
+def test_rmsnorm_gated_and_swiglu_and_sgate():
+    from vagus_b200 import ops
+    o = torch.randn(50, 4, 256, device=DEV).bfloat16().requires_grad_(True)
+    gt = torch.randn(50, 4, 256, device=DEV).bfloat16().requires_grad_(True)
+    gm = (1 + 0.1 * torch.randn(256, device=DEV)).requires_grad_(True)
+    y = ops.rmsnorm_gated(o, gt, gm, 1e-6)
+    orr, gr, gmr = (t.detach().float().requires_grad_(True) for t in (o, gt, gm))
+    yr = orr * torch.rsqrt(orr.pow(2).mean(-1, keepdim=True) + 1e-6) * gmr * F.silu(gr)
+    dy = torch.randn_like(yr)
+    (y.float() * dy).sum().backward()
+    (yr * dy).sum().backward()
+    assert rel(y, yr) < 1e-2
+    for a, b in ((o, orr), (gt, gr), (gm, gmr)):
+        assert rel(a.grad, b.grad) < 2e-2
+    u = torch.randn(77, 2 * 704, device=DEV).bfloat16().requires_grad_(True)
+    s = ops.swiglu(u)
+    ur = u.detach().float().requires_grad_(True)
+    a, b = ur.chunk(2, -1)
+    sr = F.silu(a) * b
+    ds = torch.randn_like(sr)
+    (s.float() * ds).sum().backward()
+    (sr * ds).sum().backward()
+    assert rel(s, sr) < 1e-2 and rel(u.grad, ur.grad) < 1e-2
+    xx = torch.randn(1000, device=DEV).bfloat16().requires_grad_(True)
+    gg = torch.randn(1000, device=DEV).bfloat16().requires_grad_(True)
+    z = ops.sigmoid_gate(xx, gg)
+    xr2, gr2 = xx.detach().float().requires_grad_(True), gg.detach().float().requires_grad_(True)
+    zr = xr2 * torch.sigmoid(gr2)
+    dz = torch.randn_like(zr)
+    (z.float() * dz).sum().backward()
+    (zr * dz).sum().backward()
+    assert rel(z, zr) < 1e-2 and rel(xx.grad, xr2.grad) < 1e-2 and rel(gg.grad, gr2.grad) < 1e-2
+
+
+@pytest.mark.parametrize("norm,rope", [(True, True), (False, True), (True, False)])
+def test_qk_norm_rope(norm, rope):
+    from vagus_b200 import ops
+    from vagus_b200.models.rope import RoPE
+    B, L, H, D = 2, 37, 3, 64
+    x = torch.randn(B, L, H, D, device=DEV).bfloat16().requires_grad_(True)
+    gm = (1 + 0.1 * torch.randn(D, device=DEV)).requires_grad_(True) if norm else None
+    rp = RoPE(H * D, D, 64).to(DEV)
+    tables = rp.tables(L, 5) if rope else None
+    y = ops.qk_norm_rope(x, gm, tables, 1e-6)
+    xr = x.detach().float().requires_grad_(True)
+    gr = gm.detach().clone().requires_grad_(True) if norm else None
+    h = xr
+    if norm:
+        h = (h * torch.rsqrt(h.pow(2).mean(-1, keepdim=True) + 1e-6)) * gr
+    if rope:
+        h = rp(h.transpose(1, 2), 5).transpose(1, 2)
+    dy = torch.randn_like(h)
+    (y.float() * dy).sum().backward()
+    (h * dy).sum().backward()
+    assert rel(y, h) < 1e-2 and rel(x.grad, xr.grad) < 2e-2
+    if norm:
+        assert rel(gm.grad, gr.grad) < 2e-2
+
+
+def _conv_ref(x, w, hd, l2):
+    D, K = w.shape[0], w.shape[-1]
+    y = F.conv1d(F.pad(x.transpose(1, 2), (K - 1, 0)), w, groups=D).transpose(1, 2)
+    z = F.silu(y)
+    if l2:
+        B, L = z.shape[:2]
+        zz = z.view(B, L, D // hd, hd)
+        z = (zz * torch.rsqrt(zz.pow(2).sum(-1, keepdim=True) + 1e-6)).view(B, L, D)
+    return z
+
+
+@pytest.mark.parametrize("l2", [True, False])
+def test_conv_silu(l2):
+    from vagus_b200.ops import native
+    B, L, D, K, hd = 2, 150, 512, 4, 256
+    big = torch.randn(B, L, 3 * D, device=DEV).bfloat16()
+    x = big[:, :, D:2 * D]
+    w = 0.3 * torch.randn(D, 1, K, device=DEV)
+    y, rn = native().conv_silu_fwd(x, w, hd, l2)
+    xr = x.float().detach().requires_grad_(True)
+    wr = w.detach().clone().requires_grad_(True)
+    yr = _conv_ref(xr, wr, hd, l2)
+    assert rel(y, yr) < 1e-2
+    dy = torch.randn_like(yr)
+    (yr * dy).sum().backward()
+    dxbig = torch.zeros_like(big)
+    dw = torch.zeros(D * K, device=DEV)
+    native().conv_silu_bwd(dy.bfloat16(), x, w, rn, dxbig[:, :, D:2 * D], dw, hd, l2)
+    assert rel(dxbig[:, :, D:2 * D], xr.grad) < 2e-2
+    assert rel(dw.view(D, 1, K), wr.grad) < 2e-2
+    assert dxbig[:, :, :D].abs().max().item() == 0
+
+
+def test_gates():
+    from vagus_b200.ops import native
+    T, H = 300, 4
+    ab = torch.randn(T, 2 * H, device=DEV).bfloat16()
+    A_log = torch.rand(H, device=DEV).log1p()
+    dtb = torch.randn(H, device=DEV)
+    g, beta = native().gdn_gates_fwd(ab, A_log, dtb, H)
+    abr = ab.float().requires_grad_(True)
+    Ar, dr = A_log.clone().requires_grad_(True), dtb.clone().requires_grad_(True)
+    gr = -Ar.exp() * F.softplus(abr[:, :H] + dr)
+    br = torch.sigmoid(abr[:, H:])
+    assert rel(g, gr) < 1e-4 and rel(beta, br) < 1e-4
+    dg, db = torch.randn_like(gr), torch.randn_like(br)
+    ((gr * dg).sum() + (br * db).sum()).backward()
+    dab, dA, ddt = native().gdn_gates_bwd(dg, db, ab, A_log, dtb, H)
+    assert rel(dab, abr.grad) < 1e-2 and rel(dA, Ar.grad) < 1e-4 and rel(ddt, dr.grad) < 1e-4
+
+
+def _gdr_inputs(B, L, H, dk, dv):
+    q = F.normalize(torch.randn(B, L, H, dk, device=DEV), dim=-1)
+    k = F.normalize(torch.randn(B, L, H, dk, device=DEV), dim=-1)
+    v = torch.randn(B, L, H, dv, device=DEV)
+    g = F.logsigmoid(torch.randn(B, L, H, device=DEV) + 3)
+    beta = torch.sigmoid(torch.randn(B, L, H, device=DEV))
+    return q, k, v, g, beta
+
+
+@pytest.mark.parametrize("dk,dv", [(128, 128), (256, 256), (128, 256)])
+def test_gdr_chunk_fwd_bwd(dk, dv):
+    from vagus_b200 import ops
+    from vagus_b200.models.scans import chunk_scan
+    B, L, H = 2, 200, 2
+    q, k, v, g, beta = _gdr_inputs(B, L, H, dk, dv)
+    S0 = 0.1 * torch.randn(B, H, dk, dv, device=DEV)
+    scale = dk ** -0.5
+    ins = [t.bfloat16().float() for t in (q, k, v)] + [g, beta, S0]
+    ref_in = [t.clone().requires_grad_(True) for t in ins]
+    o_r, S_r = chunk_scan(*ref_in[:5], ref_in[5], scale=scale, delta=True, chunk_size=64)
+    cu_in = [t.clone().requires_grad_(True) for t in ins]
+    o, S = ops.gdr_chunk(cu_in[0].bfloat16(), cu_in[1].bfloat16(), cu_in[2].bfloat16(), cu_in[3], cu_in[4],
+                         cu_in[5], scale=scale)
+    assert rel(o, o_r) < 2e-2 and rel(S, S_r) < 2e-2
+    do, dS = torch.randn_like(o_r), torch.randn_like(S_r)
+    ((o_r * do).sum() + (S_r * dS).sum()).backward()
+    ((o.float() * do).sum() + (S * dS).sum()).backward()
+    for a, b in zip(cu_in, ref_in):
+        assert rel(a.grad, b.grad) < 5e-2, (a.shape, rel(a.grad, b.grad))
+
+
+def test_gdr_decode():
+    from vagus_b200 import ops
+    from vagus_b200.models.scans import recurrent_scan
+    B, H, dk, dv = 3, 2, 128, 64
+    q, k, v, g, beta = _gdr_inputs(B, 1, H, dk, dv)
+    S = torch.randn(B, H, dk, dv, device=DEV)
+    o_r, S_r = recurrent_scan(q.bfloat16().float(), k.bfloat16().float(), v.bfloat16().float(), g, beta, S,
+                              scale=0.3, delta=True)
+    o, S2 = ops.gdr_decode(q.bfloat16(), k.bfloat16(), v.bfloat16(), g, beta, S, scale=0.3)
+    assert rel(o, o_r) < 1e-2 and rel(S2, S_r) < 1e-4
+
+
+def test_fused_linear_ce():
+    from vagus_b200 import ops
+    N, D, V = 1000, 256, 3000
+    h = torch.randn(N, D, device=DEV).bfloat16().requires_grad_(True)
+    w = (0.05 * torch.randn(V, D, device=DEV)).requires_grad_(True)
+    t = torch.randint(0, V, (N,), device=DEV)
+    loss, z = ops.fused_linear_ce(h, w, t, z_loss=1e-3)
+    hr, wr = h.detach().float().requires_grad_(True), w.detach().clone().requires_grad_(True)
+    lg = hr @ wr.bfloat16().float().t()
+    zr = 1e-3 * torch.logsumexp(lg, -1).pow(2).mean()
+    lr = F.cross_entropy(lg, t) + zr
+    lr.backward()
+    loss.backward()
+    assert abs(loss.item() - lr.item()) < 2e-2 and abs(z.item() - zr.item()) < 1e-3
+    assert rel(h.grad, hr.grad) < 3e-2 and rel(w.grad, wr.grad) < 3e-2
+
+
+def test_embedding():
+    from vagus_b200 import ops
+    w = torch.randn(100, 64, device=DEV, requires_grad=True)
+    t = torch.randint(0, 100, (4, 33), device=DEV)
+    y = ops.embedding(t, w)
+    wr = w.detach().clone().requires_grad_(True)
+    yr = F.embedding(t, wr)
+    dy = torch.randn_like(yr)
+    (y * dy).sum().backward()
+    (yr * dy).sum().backward()
+    assert torch.equal(y, yr) and rel(w.grad, wr.grad) < 1e-5
+
+
+def test_gdn_mixer_matches_torch_path():
+    from vagus_b200.models.gdn import GatedDeltaNet
+    torch.manual_seed(0)
+    m = GatedDeltaNet(256, 2, 128, 128, gate="scalar", impl="cuda").to(DEV)
+    m_ref = GatedDeltaNet(256, 2, 128, 128, gate="scalar", impl="torch").to(DEV)
+    m_ref.load_state_dict(m.state_dict())
+    x = torch.randn(2, 130, 256, device=DEV)
+    xa = x.bfloat16().requires_grad_(True)
+    y = m(xa)
+    xb = x.bfloat16().float().requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        yr = m_ref(xb)
+    dy = torch.randn_like(yr.float())
+    (y.float() * dy).sum().backward()
+    (yr.float() * dy).sum().backward()
+    assert rel(y, yr) < 3e-2
+    assert rel(xa.grad, xb.grad) < 5e-2
+    for (n, p), (_, pr) in zip(m.named_parameters(), m_ref.named_parameters()):
+        assert rel(p.grad, pr.grad) < 8e-2, (n, rel(p.grad, pr.grad))

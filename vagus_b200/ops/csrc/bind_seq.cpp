@@ -1,0 +1,144 @@
+// Bindings of the sequence-mixing kernels: short conv, gate activations,
+// the gated delta-rule recurrence and its decode step.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "kernels.h"
+
+namespace {
+
+using torch::Tensor;
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, "vagus_b200 kernel '", what, "' failed to launch (code ", rc, ")");
+}
+
+const float* fptr(const c10::optional<Tensor>& t) {
+  return (t.has_value() && t->defined()) ? t->data_ptr<float>() : nullptr;
+}
+
+// x: (B, L, >=D) bf16 view with unit inner stride (row pitch x.stride(1));
+// w: (D, 1, K) fp32.  Returns (y (B, L, D) bf16, rnorm (B, L, D/hd) fp32).
+std::vector<Tensor> conv_silu_fwd(Tensor x, Tensor w, int64_t head_dim, bool l2norm) {
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && x.scalar_type() == at::kBFloat16, "conv: (B,L,D) bf16 rows");
+  TORCH_CHECK(x.stride(0) == x.size(1) * x.stride(1), "conv: batch stride must follow the row pitch");
+  const int64_t B = x.size(0), L = x.size(1);
+  const int D = static_cast<int>(w.size(0)), K = static_cast<int>(w.size(-1));
+  auto y = torch::empty({B, L, D}, x.options());
+  auto rn = torch::empty({B, L, l2norm ? D / head_dim : 0}, x.options().dtype(at::kFloat));
+  auto wc = w.contiguous();
+  check(vagus::conv_silu_fwd(x.data_ptr(), x.stride(1), wc.data_ptr<float>(), y.data_ptr(),
+                             l2norm ? rn.data_ptr<float>() : nullptr, B, L, D, K, static_cast<int>(head_dim),
+                             l2norm ? 1 : 0, stream()), "conv_silu_fwd");
+  return {y, rn};
+}
+
+// dx is written into `dx` (a (B, L, >=D) view with its own row pitch); dw (D*K fp32) accumulated.
+void conv_silu_bwd(Tensor dy, Tensor x, Tensor w, Tensor rnorm, Tensor dx, Tensor dw, int64_t head_dim, bool l2norm) {
+  dy = dy.contiguous();
+  TORCH_CHECK(dx.stride(2) == 1 && dx.stride(0) == dx.size(1) * dx.stride(1), "conv_bwd: dx layout");
+  const int64_t B = x.size(0), L = x.size(1);
+  const int D = static_cast<int>(w.size(0)), K = static_cast<int>(w.size(-1));
+  auto wc = w.contiguous();
+  check(vagus::conv_silu_bwd(dy.data_ptr(), x.data_ptr(), x.stride(1), wc.data_ptr<float>(),
+                             l2norm ? rnorm.data_ptr<float>() : nullptr, dx.data_ptr(), dx.stride(1),
+                             dw.data_ptr<float>(), B, L, D, K, static_cast<int>(head_dim), l2norm ? 1 : 0, stream()),
+        "conv_silu_bwd");
+}
+
+// ab: (T, >=2H) bf16 rows -> g, beta (T, H) fp32
+std::vector<Tensor> gdn_gates_fwd(Tensor ab, Tensor A_log, Tensor dt_bias, int64_t H) {
+  TORCH_CHECK(ab.dim() == 2 && ab.stride(1) == 1, "gates: (T, 2H) rows");
+  const int64_t T = ab.size(0);
+  auto g = torch::empty({T, H}, ab.options().dtype(at::kFloat));
+  auto beta = torch::empty({T, H}, ab.options().dtype(at::kFloat));
+  check(vagus::gdn_gates_fwd(ab.data_ptr(), ab.stride(0), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
+                             g.data_ptr<float>(), beta.data_ptr<float>(), T, static_cast<int>(H), stream()),
+        "gdn_gates_fwd");
+  return {g, beta};
+}
+
+std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_log, Tensor dt_bias, int64_t H) {
+  const int64_t T = ab.size(0);
+  auto dab = torch::empty({T, 2 * H}, ab.options());
+  auto dA = torch::zeros({H}, ab.options().dtype(at::kFloat));
+  auto ddt = torch::zeros({H}, ab.options().dtype(at::kFloat));
+  dg = dg.contiguous();
+  dbeta = dbeta.contiguous();
+  check(vagus::gdn_gates_bwd(dg.data_ptr<float>(), dbeta.data_ptr<float>(), ab.data_ptr(), ab.stride(0),
+                             A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), dab.data_ptr(), dA.data_ptr<float>(),
+                             ddt.data_ptr<float>(), T, static_cast<int>(H), stream()), "gdn_gates_bwd");
+  return {dab, dA, ddt};
+}
+
+// Recurrence forward: returns (O, V', states, S_out)
+std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor U, Tensor gC,
+                                c10::optional<Tensor> S0, bool need_states) {
+  const int64_t BH = W.size(0);
+  const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(U.size(3));
+  TORCH_CHECK(W.size(2) == 64, "gdr: chunk size 64");
+  for (auto* t : {&W, &Qh, &Kt, &A, &U}) TORCH_CHECK(t->is_contiguous() && t->scalar_type() == at::kBFloat16, "gdr: bf16");
+  auto O = torch::empty_like(U);
+  auto Vp = torch::empty_like(U);
+  auto states = torch::empty({need_states ? BH : 0, N, DK, DV}, W.options().dtype(at::kFloat));
+  auto S_out = torch::empty({BH, DK, DV}, W.options().dtype(at::kFloat));
+  vagus::GdrRecArgs a{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), U.data_ptr(),
+                      gC.contiguous().data_ptr<float>(), fptr(S0), O.data_ptr(), Vp.data_ptr(),
+                      need_states ? states.data_ptr<float>() : nullptr, S_out.data_ptr<float>(), BH, N, DK, DV};
+  check(vagus::gdr_rec_fwd(a, stream()), "gdr_rec_fwd");
+  return {O, Vp, states, S_out};
+}
+
+// Recurrence backward: returns (dW, dQh, dKt, dA, dU, dgC, dS0)
+std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor Vp, Tensor gC, Tensor states,
+                                Tensor dO, c10::optional<Tensor> dS_final, bool need_dS0) {
+  const int64_t BH = W.size(0);
+  const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(Vp.size(3));
+  dO = dO.contiguous();
+  auto f32 = W.options().dtype(at::kFloat);
+  auto dW = torch::zeros({BH, N, 64, DK}, f32);
+  auto dQh = torch::zeros({BH, N, 64, DK}, f32);
+  auto dKt = torch::zeros({BH, N, 64, DK}, f32);
+  auto dA = torch::zeros({BH, N, 64, 64}, f32);
+  auto dU = torch::empty({BH, N, 64, DV}, W.options());
+  auto dgC = torch::zeros({BH, N}, f32);
+  auto dS0 = torch::empty({need_dS0 ? BH : 0, DK, DV}, f32);
+  vagus::GdrRecBwdArgs a;
+  a.f = vagus::GdrRecArgs{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), nullptr,
+                          gC.contiguous().data_ptr<float>(), nullptr, nullptr, Vp.data_ptr(), states.data_ptr<float>(),
+                          nullptr, BH, N, DK, DV};
+  a.dO = dO.data_ptr();
+  a.dS_final = fptr(dS_final);
+  a.dW = dW.data_ptr<float>(); a.dQh = dQh.data_ptr<float>(); a.dKt = dKt.data_ptr<float>(); a.dA = dA.data_ptr<float>();
+  a.dU = dU.data_ptr(); a.dgC = dgC.data_ptr<float>(); a.dS0 = need_dS0 ? dS0.data_ptr<float>() : nullptr;
+  check(vagus::gdr_rec_bwd(a, stream()), "gdr_rec_bwd");
+  return {dW, dQh, dKt, dA, dU, dgC, dS0};
+}
+
+// q, k (BH, dk) bf16, v (BH, dv) bf16, g, beta (BH) fp32, S (BH, dk, dv) fp32 in place -> o (BH, dv)
+Tensor gdr_decode(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor S, double scale) {
+  const int64_t BH = S.size(0);
+  const int dk = static_cast<int>(S.size(1)), dv = static_cast<int>(S.size(2));
+  TORCH_CHECK(S.is_contiguous() && S.scalar_type() == at::kFloat, "gdr_decode: fp32 contiguous state");
+  auto qc = q.contiguous(), kc = k.contiguous(), vc = v.contiguous();
+  auto gc = g.contiguous(), bc = beta.contiguous();
+  auto o = torch::empty({BH, dv}, q.options());
+  check(vagus::gdr_decode(qc.data_ptr(), kc.data_ptr(), vc.data_ptr(), gc.data_ptr<float>(), bc.data_ptr<float>(),
+                          S.data_ptr<float>(), o.data_ptr(), BH, dk, dv, static_cast<float>(scale), stream()),
+        "gdr_decode");
+  return o;
+}
+
+}  // namespace
+
+void register_seq_ops(pybind11::module& m) {
+  m.def("conv_silu_fwd", &conv_silu_fwd);
+  m.def("conv_silu_bwd", &conv_silu_bwd);
+  m.def("gdn_gates_fwd", &gdn_gates_fwd);
+  m.def("gdn_gates_bwd", &gdn_gates_bwd);
+  m.def("gdr_rec_fwd", &gdr_rec_fwd);
+  m.def("gdr_rec_bwd", &gdr_rec_bwd);
+  m.def("gdr_decode", &gdr_decode);
+}

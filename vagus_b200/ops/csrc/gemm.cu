@@ -1,0 +1,412 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a on the 5th-generation
+// tensor cores.
+//
+//   C[b] = alpha * op(A[b]) @ op(B[b])^T + beta * S[b]       (mode STORE)
+//   C[b] += alpha * op(A[b]) @ op(B[b])^T   (fp32 red.add)    (mode ATOMIC)
+//
+// A is M x K, B is N x K in the math; each operand may sit in memory either
+// K-contiguous ("K-major", the row-major [M][K] / [N][K] tensor) or
+// M/N-contiguous ("MN-major", the row-major [K][M] / [K][N] tensor), so the
+// three GEMMs of a linear layer (y = x W^T, dx = dy W, dW = dy^T x) all read
+// their operands in place without transposes.
+//
+// One CTA per SM loops over output tiles (128 x BN).  Warp roles:
+//   warp 0      TMA producer: 128-byte-swizzled tiles of A and B into a
+//               STAGES-deep shared-memory ring (mbarrier full/empty pairs);
+//   warp 1      TMEM allocator and MMA issuer: one thread issues
+//               tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM
+//               accumulators and tcgen05.commit's the smem slot back;
+//   warps 2-5   epilogue: tcgen05.ld the accumulator (one TMEM lane = one
+//               output row per thread), apply alpha/beta/source, store.
+// The two accumulators let the epilogue of tile i overlap the main loop of
+// tile i+1.  Split-K (mode ATOMIC only) spreads the K range of one tile over
+// several work units when there are fewer tiles than SMs (weight gradients).
+//
+// All waits are bounded (common.cuh); a timeout sets the error word and the
+// CTA winds down, releasing its TMEM.
+#include "common.cuh"
+#include "gemm.h"
+
+#include <algorithm>
+#include <cstdio>
+#include <mutex>
+
+namespace vagus {
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;            // one 128-byte swizzle row of bf16
+constexpr int UMMA_K = 16;
+constexpr int NUM_THREADS = 192;  // 6 warps
+
+template <int BN>
+struct Cfg {
+  static constexpr int STAGES = BN == 256 ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int TMEM_COLS = 2 * BN;   // two accumulators
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+struct KParams {
+  int M, N, K, batch;
+  int tiles_m, tiles_n, splits, kb_total, kb_per_split;
+  void* C;
+  long long ldc, strideC;
+  int c_f32;
+  const void* S;
+  long long lds, strideS;
+  int s_f32;
+  float alpha, beta;
+  int atomic;
+  int vec;          // 16-byte vector access is legal for C and S
+  int* err;
+};
+
+__device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row, int col0, const float* v) {
+  // v: 32 consecutive values of one output row starting at col0
+  if (row >= p.M) return;
+  const bool full = (col0 + 32 <= p.N) && p.vec;
+  if (p.atomic) {
+    float* c = reinterpret_cast<float*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc + col0;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (full || col0 + j < p.N) atomicAdd(c + j, p.alpha * v[j]);
+    return;
+  }
+  float out[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) out[j] = p.alpha * v[j];
+  if (p.S != nullptr && p.beta != 0.f) {
+    if (p.s_f32) {
+      const float* s = reinterpret_cast<const float*>(p.S) + (long long)b * p.strideS + (long long)row * p.lds + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float4 t = *reinterpret_cast<const float4*>(s + j);
+          out[j] += p.beta * t.x; out[j + 1] += p.beta * t.y; out[j + 2] += p.beta * t.z; out[j + 3] += p.beta * t.w;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j) if (col0 + j < p.N) out[j] += p.beta * s[j];
+      }
+    } else {
+      const __nv_bfloat16* s =
+          reinterpret_cast<const __nv_bfloat16*>(p.S) + (long long)b * p.strideS + (long long)row * p.lds + col0;
+      if (full) {
+#pragma unroll
+        for (int j = 0; j < 32; j += 8) {
+          uint4 t = *reinterpret_cast<const uint4*>(s + j);
+          float2 f0 = unpack_bf16x2(t.x), f1 = unpack_bf16x2(t.y), f2 = unpack_bf16x2(t.z), f3 = unpack_bf16x2(t.w);
+          out[j] += p.beta * f0.x; out[j + 1] += p.beta * f0.y; out[j + 2] += p.beta * f1.x; out[j + 3] += p.beta * f1.y;
+          out[j + 4] += p.beta * f2.x; out[j + 5] += p.beta * f2.y; out[j + 6] += p.beta * f3.x; out[j + 7] += p.beta * f3.y;
+        }
+      } else {
+        for (int j = 0; j < 32; ++j) if (col0 + j < p.N) out[j] += p.beta * bf2f(s[j]);
+      }
+    }
+  }
+  if (p.c_f32) {
+    float* c = reinterpret_cast<float*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) *reinterpret_cast<float4*>(c + j) = make_float4(out[j], out[j + 1], out[j + 2], out[j + 3]);
+    } else {
+      for (int j = 0; j < 32; ++j) if (col0 + j < p.N) c[j] = out[j];
+    }
+  } else {
+    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc + col0;
+    if (full) {
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        uint4 t;
+        t.x = pack_bf16x2(out[j], out[j + 1]); t.y = pack_bf16x2(out[j + 2], out[j + 3]);
+        t.z = pack_bf16x2(out[j + 4], out[j + 5]); t.w = pack_bf16x2(out[j + 6], out[j + 7]);
+        *reinterpret_cast<uint4*>(c + j) = t;
+      }
+    } else {
+      for (int j = 0; j < 32; ++j) if (col0 + j < p.N) c[j] = f2bf(out[j]);
+    }
+  }
+}
+
+// Decode a work unit into (batch, tile m, tile n, split).
+__device__ __forceinline__ void decode_unit(const KParams& p, int u, int& b, int& tm, int& tn, int& sp) {
+  sp = u % p.splits;
+  int t = u / p.splits;
+  int per_batch = p.tiles_m * p.tiles_n;
+  b = t / per_batch;
+  t -= b * per_batch;
+  tm = t / p.tiles_n;
+  tn = t - tm * p.tiles_n;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, const KParams p) {
+  using C = Cfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // 1024-byte alignment for the swizzle atoms
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + C::STAGES;
+  uint64_t* acc_full = empty_bar + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mapA);
+    tma_prefetch_desc(&mapB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const int units = p.batch * p.tiles_m * p.tiles_n * p.splits;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        int b, tm, tn, sp;
+        decode_unit(p, u, b, tm, tn, sp);
+        const int kb0 = sp * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) { ok = false; break; }
+          uint8_t* sa = tiles + stage * C::STAGE_BYTES;
+          uint8_t* sb = sa + C::A_BYTES;
+          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
+          const int k0 = kb * BK;
+          if (A_MN) {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_3d(sa + j * 8192, &mapA, &full_bar[stage], tm * BM + 64 * j, k0, b);
+          } else {
+            tma_load_3d(sa, &mapA, &full_bar[stage], k0, tm * BM, b);
+          }
+          if (B_MN) {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * 8192, &mapB, &full_bar[stage], tn * BN + 64 * j, k0, b);
+          } else {
+            tma_load_3d(sb, &mapB, &full_bar[stage], k0, tn * BN, b);
+          }
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
+        int b, tm, tn, sp;
+        decode_unit(p, u, b, tm, tn, sp);
+        const int kb0 = sp * p.kb_per_split;
+        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * BN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(tiles + stage * C::STAGE_BYTES);
+          const uint32_t b_addr = a_addr + C::A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            // K-major: next 16 columns are 32 bytes further along the swizzled row.
+            // MN-major: next 16 K-rows are 16 * 128 bytes further down.
+            const uint64_t ad = A_MN ? make_sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(b_addr + kk * 32, 16, 1024);
+            tc_mma_f16(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty_bar[stage]);
+          if (++stage == C::STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        tc_commit(&acc_full[buf]);
+      }
+      // let every MMA this thread issued retire before TMEM is released
+      tc_commit(drain_bar);
+      mbar_wait(drain_bar, 0, abort_flag, p.err, kErrTimeoutMma);
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int quarter = warp & 3;              // TMEM lane quarter this warp may touch
+    const int row_in_tile = quarter * 32 + lane;
+    int local = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
+      int b, tm, tn, sp;
+      decode_unit(p, u, b, tm, tn, sp);
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row = tm * BM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_ld_wait();
+        const int col0 = tn * BN + c;
+        if (col0 < p.N) store_row_chunk(p, b, row, col0, reinterpret_cast<const float*>(r));
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[buf]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host --
+
+using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                              const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                              CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeFn get_encode() {
+  static EncodeFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeFn>(ptr);
+  });
+  return fn;
+}
+
+// 3-D bf16 tensor map: (inner, rows, batch) with a (64, box_rows, 1) box.
+bool make_map(CUtensorMap* map, const void* base, long long inner, long long rows, long long batch, long long ld,
+              long long bstride, int box_rows) {
+  EncodeFn enc = get_encode();
+  if (!enc) return false;
+  cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(std::max<long long>(bstride, 1) * 2)};
+  cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int num_sms() {
+  static int n = 0;
+  if (n == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+int launch_t(const GemmArgs& a, cudaStream_t stream) {
+  using C = Cfg<BN>;
+  CUtensorMap ma, mb;
+  // A: K-major -> (K, M) rows of K; MN-major -> (M, K) rows of M.
+  bool ok = A_MN ? make_map(&ma, a.A, a.M, a.K, a.batch, a.lda, a.strideA, 64)
+                 : make_map(&ma, a.A, a.K, a.M, a.batch, a.lda, a.strideA, BM);
+  ok = ok && (B_MN ? make_map(&mb, a.B, a.N, a.K, a.batch, a.ldb, a.strideB, 64)
+                   : make_map(&mb, a.B, a.K, a.N, a.batch, a.ldb, a.strideB, BN));
+  if (!ok) return 2;
+  KParams p;
+  p.M = a.M; p.N = a.N; p.K = a.K; p.batch = a.batch;
+  p.tiles_m = (a.M + BM - 1) / BM;
+  p.tiles_n = (a.N + BN - 1) / BN;
+  p.kb_total = (a.K + BK - 1) / BK;
+  const int tiles = p.tiles_m * p.tiles_n * a.batch;
+  int splits = 1;
+  if (a.atomic && a.split_k != 1) {
+    if (a.split_k > 1) splits = a.split_k;
+    else {
+      // enough work units to cover the SMs about twice, each at least 8 k-blocks
+      while (tiles * splits < 2 * num_sms() && p.kb_total / (splits * 2) >= 8) splits *= 2;
+    }
+  }
+  p.kb_per_split = (p.kb_total + splits - 1) / splits;
+  p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+  p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC; p.c_f32 = a.c_f32;
+  p.S = a.S; p.lds = a.lds; p.strideS = a.strideS; p.s_f32 = a.s_f32;
+  p.alpha = a.alpha; p.beta = a.beta; p.atomic = a.atomic; p.err = a.err;
+  {
+    const int ce = a.c_f32 ? 4 : 2, se = a.s_f32 ? 4 : 2;
+    bool v = (reinterpret_cast<uintptr_t>(a.C) % 16 == 0) && ((a.ldc * ce) % 16 == 0) && ((a.strideC * ce) % 16 == 0);
+    if (a.S) v = v && (reinterpret_cast<uintptr_t>(a.S) % 16 == 0) && ((a.lds * se) % 16 == 0) && ((a.strideS * se) % 16 == 0);
+    p.vec = v ? 1 : 0;
+  }
+  const int units = tiles * p.splits;
+  const int grid = std::min(units, num_sms());
+  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+    attr_set = true;
+  }
+  kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+template <int BN>
+int dispatch_major(const GemmArgs& a, cudaStream_t s) {
+  if (!a.a_mn && !a.b_mn) return launch_t<BN, false, false>(a, s);
+  if (!a.a_mn && a.b_mn) return launch_t<BN, false, true>(a, s);
+  if (a.a_mn && !a.b_mn) return launch_t<BN, true, false>(a, s);
+  return launch_t<BN, true, true>(a, s);
+}
+
+}  // namespace
+
+int gemm_launch(const GemmArgs& a, cudaStream_t stream) {
+  if (a.M <= 0 || a.N <= 0 || a.batch <= 0) return 0;
+  if (a.K <= 0) return 4;
+  // TMA: base 16-byte aligned, row pitch a multiple of 16 bytes
+  auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!aligned(a.A) || !aligned(a.B) || (a.lda % 8) || (a.ldb % 8)) return 1;
+  if (a.batch > 1 && ((a.strideA % 8) || (a.strideB % 8))) return 1;
+  const int bn = a.block_n > 0 ? a.block_n : (a.N <= 128 ? 128 : 256);
+  return bn == 128 ? dispatch_major<128>(a, stream) : dispatch_major<256>(a, stream);
+}
+
+}  // namespace vagus

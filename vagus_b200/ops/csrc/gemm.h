@@ -1,0 +1,30 @@
+// Host interface of the sm_100a tcgen05 GEMM (gemm.cu).
+#pragma once
+#include <cuda_runtime.h>
+
+namespace vagus {
+
+struct GemmArgs {
+  // math: C[b] (M x N) = alpha * A[b] (M x K) @ B[b] (N x K)^T + beta * S[b]
+  const void* A = nullptr;   // bf16; a_mn=false: [M][lda] (K contiguous); true: [K][lda] (M contiguous)
+  const void* B = nullptr;   // bf16; b_mn=false: [N][ldb] (K contiguous); true: [K][ldb] (N contiguous)
+  long long lda = 0, ldb = 0, strideA = 0, strideB = 0;
+  bool a_mn = false, b_mn = false;
+  int M = 0, N = 0, K = 0, batch = 1;
+  void* C = nullptr;         // bf16 or fp32, [M][ldc]
+  long long ldc = 0, strideC = 0;
+  int c_f32 = 0;
+  const void* S = nullptr;   // optional source for the beta term (bf16 or fp32), [M][lds]
+  long long lds = 0, strideS = 0;
+  int s_f32 = 0;
+  float alpha = 1.f, beta = 0.f;
+  int atomic = 0;            // 1: C (fp32) += alpha * A @ B^T with red.add (split-K allowed)
+  int split_k = 0;           // 0: automatic (atomic mode only), 1: none, >1: fixed
+  int block_n = 0;           // 0: automatic (128 or 256)
+  int* err = nullptr;        // device error word (bounded-wait timeouts)
+};
+
+// Returns 0 on launch, nonzero on argument / encode / launch failure.
+int gemm_launch(const GemmArgs& args, cudaStream_t stream);
+
+}  // namespace vagus

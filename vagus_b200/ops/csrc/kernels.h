@@ -1,0 +1,102 @@
+// Host-side launchers of the sm_100a kernels (no torch types: the .cu files
+// compile without the torch headers; bindings.cpp owns tensor checking).
+// Every launcher returns 0 on success, nonzero on a launch / argument error.
+#pragma once
+#include <cuda_runtime.h>
+
+namespace vagus {
+
+// norm.cu
+int rmsnorm_fwd(const void* x, int x_f32, const float* gamma, void* y, int y_f32, float* rstd, long long rows, int D,
+                float eps, cudaStream_t s);
+int rmsnorm_bwd(const void* dy, int dy_f32, const void* x, int x_f32, const float* gamma, const float* rstd,
+                const float* dres, void* dx, int dx_f32, float* dgamma, long long rows, int D, cudaStream_t s);
+int rmsnorm_gated_fwd(const void* o, const void* g, long long ldg, int H, const float* gamma, void* y, int y_f32,
+                      float* rstd, long long rows, int D, float eps, cudaStream_t s);
+int rmsnorm_gated_bwd(const void* dy, const void* o, const void* g, long long ldg, int H, const float* gamma,
+                      const float* rstd, void* dO, void* dG, long long lddg, float* dgamma, long long rows, int D,
+                      cudaStream_t s);
+int qk_norm_rope_fwd(const void* x, const float* gamma, const float* cosv, const float* sinv, void* y, float* rstd,
+                     long long rows, int L, int H, int D, float eps, cudaStream_t s);
+int qk_norm_rope_bwd(const void* dy, const void* x, const float* gamma, const float* cosv, const float* sinv,
+                     const float* rstd, void* dx, float* dgamma, long long rows, int L, int H, int D, cudaStream_t s);
+
+// elementwise.cu
+int swiglu_fwd(const void* u, void* s, long long rows, int F, cudaStream_t st);
+int swiglu_bwd(const void* ds, const void* u, void* du, long long rows, int F, cudaStream_t st);
+int sigmoid_gate_fwd(const void* x, const void* g, void* y, long long n, cudaStream_t st);
+int sigmoid_gate_bwd(const void* dy, const void* x, const void* g, void* dx, void* dg, long long n, cudaStream_t st);
+int softmax_ce(void* logits, const long long* targets, float* loss, float* lse, long long rows, int V, float scale,
+               float z_coef, cudaStream_t st);
+int embedding_fwd(const float* W, const long long* tok, void* y, int y_f32, long long n, int D, cudaStream_t st);
+int embedding_bwd(const void* dy, int dy_f32, const long long* tok, float* dW, long long n, int D, cudaStream_t st);
+int adamw_step(float* p, const float* g, float* m, float* v, void* shadow, long long n, float lr, float b1, float b2,
+               float eps, float wd, float bc1, float bc2, float gscale, cudaStream_t st);
+int muon_momentum(const float* g, float* buf, void* upd, long long n, float mu, int nesterov, float gscale,
+                  cudaStream_t st);
+
+// conv.cu: causal depthwise conv (K taps) + SiLU (+ per-head L2 norm) for
+// the q / k / v streams of a GatedDeltaNet layer.
+int conv_silu_fwd(const void* xp, long long ldx, const float* w, void* y, float* rnorm, long long B, long long L,
+                  int D, int K, int head_dim, int l2norm, cudaStream_t st);
+int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w, const float* rnorm, void* dx,
+                  long long lddx, float* dw, long long B, long long L, int D, int K, int head_dim, int l2norm,
+                  cudaStream_t st);
+
+// gdn_gates.cu: per-token scalar gate and write strength from the packed
+// projection: g = -exp(A_log) softplus(a + dt_bias), beta = sigmoid(b).
+int gdn_gates_fwd(const void* ab, long long ld, const float* A_log, const float* dt_bias, float* g, float* beta,
+                  long long T, int H, cudaStream_t st);
+int gdn_gates_bwd(const float* dg, const float* dbeta, const void* ab, long long ld, const float* A_log,
+                  const float* dt_bias, void* dab, float* dA_log, float* ddt_bias, long long T, int H,
+                  cudaStream_t st);
+
+// gdr.cu: inter-chunk state recurrence of the chunked gated delta rule
+// (scalar gate), forward scan and reverse-scan backward (see gdr.cu).
+struct GdrRecArgs {
+  const void* W; const void* Qh; const void* Kt;   // (BH, N, C, DK) bf16
+  const void* A;                                   // (BH, N, C, C) bf16
+  const void* U;                                   // (BH, N, C, DV) bf16
+  const float* gC;                                 // (BH, N)
+  const float* S0;                                 // (BH, DK, DV) or null
+  void* O;                                         // (BH, N, C, DV) bf16
+  void* Vp;                                        // (BH, N, C, DV) bf16: V' (written fwd, read bwd)
+  float* states;                                   // (BH, N, DK, DV) entry states (written fwd, read bwd)
+  float* S_out;                                    // (BH, DK, DV) or null
+  long long BH; int N, DK, DV;
+};
+int gdr_rec_fwd(const GdrRecArgs& a, cudaStream_t st);
+struct GdrRecBwdArgs {
+  GdrRecArgs f;
+  const void* dO;                                  // (BH, N, C, DV) bf16
+  const float* dS_final;                           // (BH, DK, DV) or null
+  float* dW; float* dQh; float* dKt;               // (BH, N, C, DK) fp32, zero-initialised (atomics)
+  float* dA;                                       // (BH, N, C, C) fp32, zero-initialised
+  void* dU;                                        // (BH, N, C, DV) bf16
+  float* dgC;                                      // (BH, N) fp32, zero-initialised
+  float* dS0;                                      // (BH, DK, DV) or null
+};
+int gdr_rec_bwd(const GdrRecBwdArgs& a, cudaStream_t st);
+int gdr_decode(const void* q, const void* k, const void* v, const float* g, const float* beta, float* S, void* o,
+               long long BH, int dk, int dv, float scale, cudaStream_t st);
+
+// attention.cu: causal (lower-right aligned) / full softmax attention.
+struct AttnArgs {
+  const void* q; const void* k; const void* v;  // (B, H, Lq, D), (B, Hk, Lk, D), (B, Hk, Lk, Dv) bf16
+  void* o;                                      // (B, H, Lq, Dv) bf16
+  float* lse;                                   // (B, H, Lq) fp32
+  long long B; int H, Hk, Lq, Lk, D, Dv;
+  long long sq_b, sq_h, sq_l, sk_b, sk_h, sk_l, sv_b, sv_h, sv_l, so_b, so_h, so_l;   // element strides
+  int causal; float scale;
+};
+int attn_fwd(const AttnArgs& a, cudaStream_t st);
+struct AttnBwdArgs {
+  AttnArgs f;
+  const void* dO;            // like o (same strides)
+  void* dq; void* dk; void* dv;   // contiguous (B, H, Lq, D), (B, Hk, Lk, D), (B, Hk, Lk, Dv) bf16
+  float* dq_acc;             // fp32 scratch (B, H, Lq, D)
+  float* delta;              // fp32 scratch (B, H, Lq)
+};
+int attn_bwd(const AttnBwdArgs& a, cudaStream_t st);
+
+}  // namespace vagus

@@ -1,0 +1,299 @@
+// Row-wise normalisation kernels (one warp per row, fp32 statistics):
+//   rmsnorm        y = x * rsqrt(mean(x^2) + eps) * gamma          (fwd / bwd)
+//   rmsnorm_gated  y = rmsnorm(o) * gamma * silu(g)                (fwd / bwd)
+//   qk_norm_rope   per-head RMSNorm (optional) then interleaved-pair RoPE
+//                  (optional), the prologue of softmax attention   (fwd / bwd)
+// gamma gradients are reduced per CTA in shared memory and added to an fp32
+// buffer with one atomic per column per CTA.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace vagus {
+namespace {
+
+template <typename T>
+__device__ __forceinline__ float ld(const T* p, long long i);
+template <>
+__device__ __forceinline__ float ld<float>(const float* p, long long i) { return p[i]; }
+template <>
+__device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p, long long i) { return bf2f(p[i]); }
+
+template <typename T>
+__device__ __forceinline__ void st(T* p, long long i, float v);
+template <>
+__device__ __forceinline__ void st<float>(float* p, long long i, float v) { p[i] = v; }
+template <>
+__device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, long long i, float v) { p[i] = f2bf(v); }
+
+constexpr int ROWS_PER_CTA = 8;   // one warp per row, 8 warps
+constexpr int MAXV = 32;          // up to 32 values per lane (D <= 1024 in registers; larger loops)
+
+// ------------------------------------------------------------- rmsnorm --
+
+template <typename TI, typename TO>
+__global__ void rmsnorm_fwd_k(const TI* __restrict__ x, const float* __restrict__ gamma, TO* __restrict__ y,
+                              float* __restrict__ rstd, int rows, int D, float eps) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + warp;
+  if (r >= rows) return;
+  const TI* xr = x + r * D;
+  float ss = 0.f;
+  for (int c = lane; c < D; c += 32) { float v = ld(xr, c); ss += v * v; }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / D + eps);
+  if (lane == 0 && rstd) rstd[r] = rs;
+  TO* yr = y + r * D;
+  for (int c = lane; c < D; c += 32) st(yr, c, ld(xr, c) * rs * gamma[c]);
+}
+
+// dx = rs * (dy*g - xhat * mean(dy*g*xhat)) (+ dres);  dgamma += sum_rows dy * xhat
+template <typename TI, typename TG, typename TO>
+__global__ void rmsnorm_bwd_k(const TG* __restrict__ dy, const TI* __restrict__ x, const float* __restrict__ gamma,
+                              const float* __restrict__ rstd, const float* __restrict__ dres, TO* __restrict__ dx,
+                              float* __restrict__ dgamma, int rows, int D) {
+  extern __shared__ float sg[];   // [D] partial dgamma of this CTA
+  for (int c = threadIdx.x; c < D; c += blockDim.x) sg[c] = 0.f;
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + warp;
+  if (r < rows) {
+    const TI* xr = x + r * D;
+    const TG* dr = dy + r * D;
+    const float rs = rstd[r];
+    float dot = 0.f;
+    for (int c = lane; c < D; c += 32) dot += ld(dr, c) * gamma[c] * ld(xr, c) * rs;
+    dot = warp_sum(dot) / D;
+    TO* o = dx + r * D;
+    for (int c = lane; c < D; c += 32) {
+      const float xh = ld(xr, c) * rs;
+      const float g = ld(dr, c);
+      float v = rs * (g * gamma[c] - xh * dot);
+      if (dres) v += dres[r * D + c];
+      st(o, c, v);
+      atomicAdd(&sg[c], g * xh);
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
+}
+
+// ------------------------------------------------------- rmsnorm_gated --
+// o: (rows, Dh) with rows = tokens * heads; g: same layout; gamma (Dh)
+
+// The gate may be a column block of a wider packed matrix: row r = (token
+// t, head h) reads g[t * ldg + h * D + c] (ldg = H * D when contiguous).
+template <typename TO_>
+__global__ void rmsnorm_gated_fwd_k(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g,
+                                    long long ldg, int H, const float* __restrict__ gamma, TO_* __restrict__ y,
+                                    float* __restrict__ rstd, long long rows, int D, float eps) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + warp;
+  if (r >= rows) return;
+  const __nv_bfloat16* orow = o + r * D;
+  const __nv_bfloat16* grow = g + (r / H) * ldg + (r % H) * D;
+  float ss = 0.f;
+  for (int c = lane; c < D; c += 32) { float v = bf2f(orow[c]); ss += v * v; }
+  ss = warp_sum(ss);
+  const float rs = rsqrtf(ss / D + eps);
+  if (lane == 0) rstd[r] = rs;
+  for (int c = lane; c < D; c += 32) st(y + r * D, c, bf2f(orow[c]) * rs * gamma[c] * silu_f(bf2f(grow[c])));
+}
+
+__global__ void rmsnorm_gated_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ o,
+                                    const __nv_bfloat16* __restrict__ g, long long ldg, int H,
+                                    const float* __restrict__ gamma, const float* __restrict__ rstd,
+                                    __nv_bfloat16* __restrict__ dO, __nv_bfloat16* __restrict__ dG, long long lddg,
+                                    float* __restrict__ dgamma, long long rows, int D) {
+  extern __shared__ float sg[];
+  for (int c = threadIdx.x; c < D; c += blockDim.x) sg[c] = 0.f;
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + warp;
+  if (r < rows) {
+    const float rs = rstd[r];
+    const __nv_bfloat16* grow = g + (r / H) * ldg + (r % H) * D;
+    __nv_bfloat16* dgrow = dG + (r / H) * lddg + (r % H) * D;
+    float dot = 0.f;
+    for (int c = lane; c < D; c += 32) {
+      const float gv = bf2f(grow[c]);
+      const float dyn = bf2f(dy[r * D + c]) * silu_f(gv);          // grad wrt normalised*gamma
+      dot += dyn * gamma[c] * bf2f(o[r * D + c]) * rs;
+    }
+    dot = warp_sum(dot) / D;
+    for (int c = lane; c < D; c += 32) {
+      const float ov = bf2f(o[r * D + c]);
+      const float gv = bf2f(grow[c]);
+      const float dyv = bf2f(dy[r * D + c]);
+      const float sgm = sigmoid_f(gv);
+      const float silu = gv * sgm;
+      const float xh = ov * rs;
+      const float dyn = dyv * silu;
+      dO[r * D + c] = f2bf(rs * (dyn * gamma[c] - xh * dot));
+      // d silu(g) / dg = s (1 + g (1 - s))
+      dgrow[c] = f2bf(dyv * xh * gamma[c] * sgm * (1.f + gv * (1.f - sgm)));
+      atomicAdd(&sg[c], dyn * xh);
+    }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
+}
+
+// ------------------------------------------------------- qk_norm_rope --
+// x: (B, L, H, Dh) bf16 contiguous; cos/sin: (L, Dh/2) fp32 (already offset).
+// One warp per (b, l, h) row.
+
+__global__ void qk_norm_rope_fwd_k(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma,
+                                   const float* __restrict__ cosv, const float* __restrict__ sinv,
+                                   __nv_bfloat16* __restrict__ y, float* __restrict__ rstd, int rows, int L, int H,
+                                   int D, float eps) {
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + warp;
+  if (r >= rows) return;
+  const int l = static_cast<int>((r / H) % L);
+  const __nv_bfloat16* xr = x + r * D;
+  float rs = 1.f;
+  if (gamma) {
+    float ss = 0.f;
+    for (int c = lane; c < D; c += 32) { float v = bf2f(xr[c]); ss += v * v; }
+    rs = rsqrtf(warp_sum(ss) / D + eps);
+    if (lane == 0) rstd[r] = rs;
+  }
+  const int half = D / 2;
+  for (int i = lane; i < half; i += 32) {
+    float x0 = bf2f(xr[2 * i]) * rs, x1 = bf2f(xr[2 * i + 1]) * rs;
+    if (gamma) {
+      // the reference casts the normalised value back to the input dtype before gamma
+      x0 = bf2f(f2bf(x0)) * gamma[2 * i];
+      x1 = bf2f(f2bf(x1)) * gamma[2 * i + 1];
+    }
+    if (cosv) {
+      const float c = cosv[(long long)l * half + i], s = sinv[(long long)l * half + i];
+      const float y0 = x0 * c - x1 * s, y1 = x0 * s + x1 * c;
+      x0 = y0; x1 = y1;
+    }
+    y[r * D + 2 * i] = f2bf(x0);
+    y[r * D + 2 * i + 1] = f2bf(x1);
+  }
+}
+
+__global__ void qk_norm_rope_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                                   const float* __restrict__ gamma, const float* __restrict__ cosv,
+                                   const float* __restrict__ sinv, const float* __restrict__ rstd,
+                                   __nv_bfloat16* __restrict__ dx, float* __restrict__ dgamma, int rows, int L, int H,
+                                   int D) {
+  extern __shared__ float sg[];
+  if (gamma) {
+    for (int c = threadIdx.x; c < D; c += blockDim.x) sg[c] = 0.f;
+    __syncthreads();
+  }
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const long long r = (long long)blockIdx.x * ROWS_PER_CTA + warp;
+  const int half = D / 2;
+  if (r < rows) {
+    const int l = static_cast<int>((r / H) % L);
+    const float rs = gamma ? rstd[r] : 1.f;
+    float dot = 0.f;
+    // pass 1: un-rotate dy -> dz (grad wrt the normalised*gamma value)
+    for (int i = lane; i < half; i += 32) {
+      float d0 = bf2f(dy[r * D + 2 * i]), d1 = bf2f(dy[r * D + 2 * i + 1]);
+      if (cosv) {
+        const float c = cosv[(long long)l * half + i], s = sinv[(long long)l * half + i];
+        const float e0 = d0 * c + d1 * s, e1 = -d0 * s + d1 * c;
+        d0 = e0; d1 = e1;
+      }
+      if (gamma) {
+        const float xh0 = bf2f(x[r * D + 2 * i]) * rs, xh1 = bf2f(x[r * D + 2 * i + 1]) * rs;
+        dot += d0 * gamma[2 * i] * xh0 + d1 * gamma[2 * i + 1] * xh1;
+        atomicAdd(&sg[2 * i], d0 * xh0);
+        atomicAdd(&sg[2 * i + 1], d1 * xh1);
+      }
+    }
+    if (gamma) dot = warp_sum(dot) / D;
+    for (int i = lane; i < half; i += 32) {
+      float d0 = bf2f(dy[r * D + 2 * i]), d1 = bf2f(dy[r * D + 2 * i + 1]);
+      if (cosv) {
+        const float c = cosv[(long long)l * half + i], s = sinv[(long long)l * half + i];
+        const float e0 = d0 * c + d1 * s, e1 = -d0 * s + d1 * c;
+        d0 = e0; d1 = e1;
+      }
+      if (gamma) {
+        const float xh0 = bf2f(x[r * D + 2 * i]) * rs, xh1 = bf2f(x[r * D + 2 * i + 1]) * rs;
+        d0 = rs * (d0 * gamma[2 * i] - xh0 * dot);
+        d1 = rs * (d1 * gamma[2 * i + 1] - xh1 * dot);
+      }
+      dx[r * D + 2 * i] = f2bf(d0);
+      dx[r * D + 2 * i + 1] = f2bf(d1);
+    }
+  }
+  if (gamma) {
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
+  }
+}
+
+inline int blocks_for(long long rows) { return static_cast<int>((rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA); }
+
+}  // namespace
+
+int rmsnorm_fwd(const void* x, int x_f32, const float* gamma, void* y, int y_f32, float* rstd, long long rows, int D,
+                float eps, cudaStream_t s) {
+  const int g = blocks_for(rows), t = 32 * ROWS_PER_CTA;
+  if (x_f32 && y_f32) rmsnorm_fwd_k<float, float><<<g, t, 0, s>>>((const float*)x, gamma, (float*)y, rstd, rows, D, eps);
+  else if (x_f32) rmsnorm_fwd_k<float, __nv_bfloat16><<<g, t, 0, s>>>((const float*)x, gamma, (__nv_bfloat16*)y, rstd, rows, D, eps);
+  else if (y_f32) rmsnorm_fwd_k<__nv_bfloat16, float><<<g, t, 0, s>>>((const __nv_bfloat16*)x, gamma, (float*)y, rstd, rows, D, eps);
+  else rmsnorm_fwd_k<__nv_bfloat16, __nv_bfloat16><<<g, t, 0, s>>>((const __nv_bfloat16*)x, gamma, (__nv_bfloat16*)y, rstd, rows, D, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int rmsnorm_bwd(const void* dy, int dy_f32, const void* x, int x_f32, const float* gamma, const float* rstd,
+                const float* dres, void* dx, int dx_f32, float* dgamma, long long rows, int D, cudaStream_t s) {
+  const int g = blocks_for(rows), t = 32 * ROWS_PER_CTA;
+  const size_t sm = D * sizeof(float);
+#define RB(TI, TG, TO) rmsnorm_bwd_k<TI, TG, TO><<<g, t, sm, s>>>((const TG*)dy, (const TI*)x, gamma, rstd, dres, (TO*)dx, dgamma, rows, D)
+  if (x_f32) {
+    if (dy_f32) { if (dx_f32) RB(float, float, float); else RB(float, float, __nv_bfloat16); }
+    else { if (dx_f32) RB(float, __nv_bfloat16, float); else RB(float, __nv_bfloat16, __nv_bfloat16); }
+  } else {
+    if (dy_f32) { if (dx_f32) RB(__nv_bfloat16, float, float); else RB(__nv_bfloat16, float, __nv_bfloat16); }
+    else { if (dx_f32) RB(__nv_bfloat16, __nv_bfloat16, float); else RB(__nv_bfloat16, __nv_bfloat16, __nv_bfloat16); }
+  }
+#undef RB
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int rmsnorm_gated_fwd(const void* o, const void* g, long long ldg, int H, const float* gamma, void* y, int y_f32,
+                      float* rstd, long long rows, int D, float eps, cudaStream_t s) {
+  if (y_f32)
+    rmsnorm_gated_fwd_k<float><<<blocks_for(rows), 32 * ROWS_PER_CTA, 0, s>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)g, ldg, H, gamma, (float*)y, rstd, rows, D, eps);
+  else
+    rmsnorm_gated_fwd_k<__nv_bfloat16><<<blocks_for(rows), 32 * ROWS_PER_CTA, 0, s>>>(
+        (const __nv_bfloat16*)o, (const __nv_bfloat16*)g, ldg, H, gamma, (__nv_bfloat16*)y, rstd, rows, D, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int rmsnorm_gated_bwd(const void* dy, const void* o, const void* g, long long ldg, int H, const float* gamma,
+                      const float* rstd, void* dO, void* dG, long long lddg, float* dgamma, long long rows, int D,
+                      cudaStream_t s) {
+  rmsnorm_gated_bwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, D * sizeof(float), s>>>(
+      (const __nv_bfloat16*)dy, (const __nv_bfloat16*)o, (const __nv_bfloat16*)g, ldg, H, gamma, rstd,
+      (__nv_bfloat16*)dO, (__nv_bfloat16*)dG, lddg, dgamma, rows, D);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int qk_norm_rope_fwd(const void* x, const float* gamma, const float* cosv, const float* sinv, void* y, float* rstd,
+                     long long rows, int L, int H, int D, float eps, cudaStream_t s) {
+  qk_norm_rope_fwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, 0, s>>>((const __nv_bfloat16*)x, gamma, cosv, sinv,
+                                                                     (__nv_bfloat16*)y, rstd, rows, L, H, D, eps);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int qk_norm_rope_bwd(const void* dy, const void* x, const float* gamma, const float* cosv, const float* sinv,
+                     const float* rstd, void* dx, float* dgamma, long long rows, int L, int H, int D, cudaStream_t s) {
+  qk_norm_rope_bwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, gamma ? D * sizeof(float) : 0, s>>>(
+      (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, gamma, cosv, sinv, rstd, (__nv_bfloat16*)dx, dgamma, rows, L,
+      H, D);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+}  // namespace vagus
