@@ -11,6 +11,12 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+def _g(*args):
+    from vagus_b200.ops import native
+    rc = native().gemm(*args)
+    assert rc == 0, rc
+
+
 def rel(a, b):
     a, b = a.float(), b.float()
     return ((a - b).norm() / b.norm().clamp(min=1e-12)).item()
@@ -26,7 +32,7 @@ def _seed():
 
 
 @pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, False), (True, True)])
-@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 300, 136), (1024, 4104, 1024), (64, 8, 64)])
+@pytest.mark.parametrize("M,N,K", [(256, 512, 256), (200, 328, 136), (1024, 4104, 1024), (384, 128, 64)])
 def test_gemm_layouts(a_mn, b_mn, M, N, K):
     from vagus_b200.ops import native
     A = torch.randn(M, K, device=DEV).bfloat16()
@@ -35,11 +41,22 @@ def test_gemm_layouts(a_mn, b_mn, M, N, K):
     Bst = B.t().contiguous() if b_mn else B
     ref = A.float() @ B.float().t()
     C = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-    native().gemm(Ast, a_mn, Bst, b_mn, C, None, 1.0, 0.0, False, 0, 0)
+    _g(Ast, a_mn, Bst, b_mn, C, None, 1.0, 0.0, False, 0, 0)
     assert rel(C, ref) < 1e-2
     C32 = torch.empty(M, N, device=DEV, dtype=torch.float32)
-    native().gemm(Ast, a_mn, Bst, b_mn, C32, None, 1.0, 0.0, False, 0, 0)
+    _g(Ast, a_mn, Bst, b_mn, C32, None, 1.0, 0.0, False, 0, 0)
     assert rel(C32, ref) < 2e-3
+
+
+def test_gemm_rejects_boxes_larger_than_tensor():
+    from vagus_b200.ops import native
+    A = torch.randn(64, 64, device=DEV).bfloat16()
+    B = torch.randn(8, 64, device=DEV).bfloat16()
+    C = torch.empty(64, 8, device=DEV, dtype=torch.bfloat16)
+    assert native().gemm(A, False, B, False, C, None, 1.0, 0.0, False, 0, 0) == 6
+    from vagus_b200.ops._core import gemm
+    with pytest.raises(RuntimeError):
+        gemm(A, False, B, False, C)
 
 
 def test_gemm_epilogues_and_batch():
@@ -50,7 +67,7 @@ def test_gemm_epilogues_and_batch():
     S = torch.randn(Bt, M, N, device=DEV)
     ref = 0.5 * (A.float() @ B.float().transpose(1, 2)) - 2.0 * S
     C = torch.empty(Bt, M, N, device=DEV)
-    native().gemm(A, False, B, False, C, S, 0.5, -2.0, False, 0, 0)
+    _g(A, False, B, False, C, S, 0.5, -2.0, False, 0, 0)
     assert rel(C, ref) < 2e-3
     # atomic split-K accumulation into an fp32 buffer (weight-gradient shape)
     T, Dout, Din = 4096, 256, 512
@@ -58,11 +75,11 @@ def test_gemm_epilogues_and_batch():
     x = torch.randn(T, Din, device=DEV).bfloat16()
     acc = torch.randn(Dout, Din, device=DEV)
     ref = acc + dy.float().t() @ x.float()
-    native().gemm(dy, True, x, True, acc, None, 1.0, 0.0, True, 0, 0)
+    _g(dy, True, x, True, acc, None, 1.0, 0.0, True, 0, 0)
     assert rel(acc, ref) < 2e-3
     for bn in (128, 256):
         C = torch.empty(M, N, device=DEV, dtype=torch.bfloat16)
-        native().gemm(A[0], False, B[0], False, C, None, 1.0, 0.0, False, 1, bn)
+        _g(A[0], False, B[0], False, C, None, 1.0, 0.0, False, 1, bn)
         assert rel(C, A[0].float() @ B[0].float().t()) < 1e-2
 
 
@@ -203,7 +220,8 @@ def test_gates():
     assert rel(g, gr) < 1e-4 and rel(beta, br) < 1e-4
     dg, db = torch.randn_like(gr), torch.randn_like(br)
     ((gr * dg).sum() + (br * db).sum()).backward()
-    dab, dA, ddt = native().gdn_gates_bwd(dg, db, ab, A_log, dtb, H)
+    dab = torch.empty_like(ab)
+    dA, ddt = native().gdn_gates_bwd(dg, db, ab, A_log, dtb, H, dab)
     assert rel(dab, abr.grad) < 1e-2 and rel(dA, Ar.grad) < 1e-4 and rel(ddt, dr.grad) < 1e-4
 
 

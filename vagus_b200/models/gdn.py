@@ -199,11 +199,16 @@ class GatedDeltaNet(nn.Module, Mixer):
         return ops.linear(o, self.wo.weight) if self.out_proj else o
 
     def _use_kernels(self, t: torch.Tensor) -> bool:
-        return t.is_cuda and self.impl != "torch" and t.dtype in (torch.bfloat16, torch.float16)
+        """The sm_100a scan kernels take dk in {128, 256}, dv a multiple of 64
+        and 64-token chunks."""
+        return (t.is_cuda and self.impl != "torch" and t.dtype in (torch.bfloat16, torch.float16)
+                and self.key_head_dim in (128, 256) and self.value_head_dim % 64 == 0 and self.chunk_size == 64)
 
     def _fused_ok(self, x: torch.Tensor) -> bool:
         return (x.is_cuda and self.impl != "torch" and self.gate == "scalar" and self.delta
-                and self.short_conv_size is not None and type(self)._write is GatedDeltaNet._write)
+                and self.short_conv_size is not None and type(self)._write is GatedDeltaNet._write
+                and self.key_head_dim in (128, 256) and self.value_head_dim % 64 == 0 and self.chunk_size == 64
+                and self.dim % 64 == 0 and x.shape[0] * x.shape[1] >= 128)
 
     # --- training / stateless ---------------------------------------------
 
@@ -219,7 +224,7 @@ class GatedDeltaNet(nn.Module, Mixer):
         o, _ = self._scan(q, k, v, g, beta, None, w=w)
         return self._output(o, x)
 
-    def forward_pre_out(self, x):
+    def forward_pre_out(self, x, is_causal: bool = True):
         """The gated, normalised head concat (the input of ``wo``).  Lets a
         block fuse ``wo`` with its residual add."""
         if self._fused_ok(x):

@@ -84,6 +84,14 @@ def autocast_bf16() -> bool:
     return torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
 
 
+_GEMM_CODES = {1: "operand base or row pitch not 16-byte aligned", 2: "tensor-map encoding failed",
+               3: "kernel launch failed", 4: "K must be positive", 6: "a TMA box exceeds its tensor (shape too small)"}
+
+
 def gemm(A, a_mn, B, b_mn, C, S=None, alpha=1.0, beta=0.0, atomic=False, split_k=0, block_n=0):
-    native().gemm(A, a_mn, B, b_mn, C, S, alpha, beta, atomic, split_k, block_n)
+    """C = alpha op(A) op(B)^T + beta S on the tcgen05 GEMM (see gemm.cu)."""
+    rc = native().gemm(A, a_mn, B, b_mn, C, S, alpha, beta, atomic, split_k, block_n)
+    if rc:
+        raise RuntimeError(f"vagus_b200 gemm rejected the problem: {_GEMM_CODES.get(rc, rc)} "
+                           f"(A {tuple(A.shape)} mn={a_mn}, B {tuple(B.shape)} mn={b_mn}, C {tuple(C.shape)})")
     return C

@@ -60,9 +60,12 @@ std::vector<Tensor> gdn_gates_fwd(Tensor ab, Tensor A_log, Tensor dt_bias, int64
   return {g, beta};
 }
 
-std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_log, Tensor dt_bias, int64_t H) {
+// dab: (T, 2H) output rows with the same row pitch as ab (e.g. the a|b
+// columns of the packed projection gradient).
+std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_log, Tensor dt_bias, int64_t H,
+                                  Tensor dab) {
   const int64_t T = ab.size(0);
-  auto dab = torch::empty({T, 2 * H}, ab.options());
+  TORCH_CHECK(dab.stride(0) == ab.stride(0) && dab.stride(1) == 1, "gates_bwd: dab must share ab's row pitch");
   auto dA = torch::zeros({H}, ab.options().dtype(at::kFloat));
   auto ddt = torch::zeros({H}, ab.options().dtype(at::kFloat));
   dg = dg.contiguous();
@@ -70,7 +73,7 @@ std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_l
   check(vagus::gdn_gates_bwd(dg.data_ptr<float>(), dbeta.data_ptr<float>(), ab.data_ptr(), ab.stride(0),
                              A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), dab.data_ptr(), dA.data_ptr<float>(),
                              ddt.data_ptr<float>(), T, static_cast<int>(H), stream()), "gdn_gates_bwd");
-  return {dab, dA, ddt};
+  return {dA, ddt};
 }
 
 // Recurrence forward: returns (O, V', states, S_out)

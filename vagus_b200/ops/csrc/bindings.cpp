@@ -62,8 +62,10 @@ void reset_error() {
 // C = alpha * op(A) @ op(B)^T + beta * S, operands given as 2-D or 3-D
 // (batched) row-major tensors with a unit inner stride.  a_mn / b_mn say the
 // operand is stored M- / N-contiguous ([K][M], [K][N]) instead of K-contiguous.
-void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, Tensor C, c10::optional<Tensor> S, double alpha, double beta,
-          bool atomic, int64_t split_k, int64_t block_n) {
+// Returns the launcher's status code (0 = launched) instead of throwing: the
+// caller decides how to report a rejected shape.
+int64_t gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, Tensor C, c10::optional<Tensor> S, double alpha, double beta,
+             bool atomic, int64_t split_k, int64_t block_n) {
   need_cuda(A, "A"); need_cuda(B, "B"); need_cuda(C, "C");
   TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
   TORCH_CHECK(A.dim() == B.dim() && A.dim() == C.dim() && (A.dim() == 2 || A.dim() == 3), "gemm: rank mismatch");
@@ -94,8 +96,7 @@ void gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, Tensor C, c10::optional<Tens
   g.alpha = static_cast<float>(alpha); g.beta = static_cast<float>(beta);
   g.atomic = atomic ? 1 : 0; g.split_k = static_cast<int>(split_k); g.block_n = static_cast<int>(block_n);
   g.err = err_ptr();
-  const c10::cuda::CUDAGuard guard(A.device());
-  check(vagus::gemm_launch(g, stream()), "gemm");
+  return vagus::gemm_launch(g, stream());
 }
 
 // ------------------------------------------------------------------ norms --

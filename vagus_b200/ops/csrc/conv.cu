@@ -40,11 +40,11 @@ __global__ void conv_fwd_k(const __nv_bfloat16* __restrict__ x, long long ldx, c
   float wr[MAXK];
 #pragma unroll
   for (int j = 0; j < MAXK; ++j) wr[j] = j < K ? w[(long long)c * K + j] : 0.f;
-  float hist[MAXK];   // hist[i] = x[t - i]
+  float hist[MAXK];   // before token t is inserted: hist[i] = x[t - 1 - i]
 #pragma unroll
   for (int i = 0; i < MAXK; ++i) {
-    const long long t = t0 - i;
-    hist[i] = (i > 0 && i < K && t >= 0) ? bf2f(x[(b * L + t) * ldx + c]) : 0.f;
+    const long long t = t0 - 1 - i;
+    hist[i] = (i < K - 1 && t >= 0) ? bf2f(x[(b * L + t) * ldx + c]) : 0.f;
   }
   const int nH = D / hd;
   for (int tt = 0; tt < TT; ++tt) {
@@ -83,11 +83,11 @@ __global__ void conv_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bflo
   // du[t] for t in [t0, t0 + TT + K - 1): the dx of token t needs du[t .. t+K-1]
   // Recompute u from x: keep a rolling window.  Process tokens in order and
   // accumulate dx contributions into a small ring: dx[t - i] += w[K-1-i] du[t].
-  float xh[MAXK];      // x[t - i]
+  float xh[MAXK];      // before token t is inserted: xh[i] = x[t - 1 - i]
 #pragma unroll
   for (int i = 0; i < MAXK; ++i) {
-    const long long t = t0 - i;
-    xh[i] = (i > 0 && i < K && t >= 0) ? bf2f(x[(b * L + t) * ldx + c]) : 0.f;
+    const long long t = t0 - 1 - i;
+    xh[i] = (i < K - 1 && t >= 0) ? bf2f(x[(b * L + t) * ldx + c]) : 0.f;
   }
   float acc[MAXK];     // acc[i] = pending dx for token (t - i), i < K
 #pragma unroll

@@ -99,8 +99,9 @@ __global__ void __launch_bounds__(CE_THREADS) softmax_ce_k(__nv_bfloat16* __rest
     s += __expf(f - m);
   }
   // combine across the CTA
+  // threads (or whole warps) that saw no element carry m = -inf, s = 0
   float wm = warp_max(m);
-  float ws = s * __expf(m - wm);
+  float ws = (m == -INFINITY) ? 0.f : s * __expf(m - wm);
   ws = warp_sum(ws);
   if (lane == 0) { red_m[warp] = wm; red_s[warp] = ws; }
   __syncthreads();
@@ -108,11 +109,10 @@ __global__ void __launch_bounds__(CE_THREADS) softmax_ce_k(__nv_bfloat16* __rest
     float mm = lane < CE_THREADS / 32 ? red_m[lane] : -INFINITY;
     float ss = lane < CE_THREADS / 32 ? red_s[lane] : 0.f;
     const float gm = warp_max(mm);
-    ss = warp_sum(lane < CE_THREADS / 32 ? ss * __expf(mm - gm) : 0.f);
+    ss = warp_sum((lane < CE_THREADS / 32 && mm != -INFINITY) ? ss * __expf(mm - gm) : 0.f);
     if (lane == 0) { bc[0] = gm; bc[1] = gm + logf(ss); }
   }
   __syncthreads();
-  const float gmax = bc[0];
   const float lse = bc[1];
   const long long tgt = targets[r];
   const bool valid = tgt >= 0;
@@ -122,8 +122,6 @@ __global__ void __launch_bounds__(CE_THREADS) softmax_ce_k(__nv_bfloat16* __rest
   }
   __syncthreads();   // the target logit is read before being overwritten
   const float zfac = valid ? scale * (1.f + 2.f * z_coef * lse) : 0.f;
-  const float inv = 1.f / __expf(lse - gmax);
-  (void)inv;
   for (int i = threadIdx.x; i < V8; i += CE_THREADS) {
     uint4 t = reinterpret_cast<uint4*>(row)[i];
     uint32_t w[4] = {t.x, t.y, t.z, t.w};

@@ -29,6 +29,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 namespace vagus {
@@ -201,17 +202,22 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) { ok = false; break; }
           uint8_t* sa = tiles + stage * C::STAGE_BYTES;
           uint8_t* sb = sa + C::A_BYTES;
-          mbar_arrive_expect_tx(&full_bar[stage], C::STAGE_BYTES);
           const int k0 = kb * BK;
+          // MN-major operands arrive as 64-wide blocks; a block that starts
+          // past the end of M / N is not loaded (its rows only feed output
+          // rows the epilogue masks), and the byte count says so.
+          int a_blocks = BM / 64, b_blocks = BN / 64;
+          if (A_MN) a_blocks = min(a_blocks, (p.M - tm * BM + 63) / 64);
+          if (B_MN) b_blocks = min(b_blocks, (p.N - tn * BN + 63) / 64);
+          const uint32_t tx = (A_MN ? a_blocks * 8192 : C::A_BYTES) + (B_MN ? b_blocks * 8192 : C::B_BYTES);
+          mbar_arrive_expect_tx(&full_bar[stage], tx);
           if (A_MN) {
-#pragma unroll
-            for (int j = 0; j < BM / 64; ++j) tma_load_3d(sa + j * 8192, &mapA, &full_bar[stage], tm * BM + 64 * j, k0, b);
+            for (int j = 0; j < a_blocks; ++j) tma_load_3d(sa + j * 8192, &mapA, &full_bar[stage], tm * BM + 64 * j, k0, b);
           } else {
             tma_load_3d(sa, &mapA, &full_bar[stage], k0, tm * BM, b);
           }
           if (B_MN) {
-#pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_3d(sb + j * 8192, &mapB, &full_bar[stage], tn * BN + 64 * j, k0, b);
+            for (int j = 0; j < b_blocks; ++j) tma_load_3d(sb + j * 8192, &mapB, &full_bar[stage], tn * BN + 64 * j, k0, b);
           } else {
             tma_load_3d(sb, &mapB, &full_bar[stage], k0, tn * BN, b);
           }
@@ -309,9 +315,10 @@ EncodeFn get_encode() {
   std::call_once(once, [] {
     void* ptr = nullptr;
     cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeFn>(ptr);
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    if (std::getenv("VAGUS_GEMM_DEBUG"))
+      std::fprintf(stderr, "[gemm] entry point rc %d status %d ptr %p\n", (int)e, (int)q, ptr);
+    if (e == cudaSuccess && q == cudaDriverEntryPointSuccess) fn = reinterpret_cast<EncodeFn>(ptr);
   });
   return fn;
 }
@@ -322,12 +329,19 @@ bool make_map(CUtensorMap* map, const void* base, long long inner, long long row
   EncodeFn enc = get_encode();
   if (!enc) return false;
   cuuint64_t dims[3] = {(cuuint64_t)inner, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(std::max<long long>(bstride, 1) * 2)};
+  // a single matrix still needs a legal (16-byte multiple) batch stride
+  if (batch <= 1 || bstride <= 0) bstride = ld * rows;
+  cuuint64_t strides[2] = {(cuuint64_t)(ld * 2), (cuuint64_t)(bstride * 2)};
   cuuint32_t box[3] = {64u, (cuuint32_t)box_rows, 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
+  if (std::getenv("VAGUS_GEMM_DEBUG"))
+    std::fprintf(stderr, "[gemm] map %p base %p dims %llu %llu %llu strides %llu %llu box %u %u\n", (void*)map, base,
+                 (unsigned long long)dims[0], (unsigned long long)dims[1], (unsigned long long)dims[2],
+                 (unsigned long long)strides[0], (unsigned long long)strides[1], box[0], box[1]);
   CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (std::getenv("VAGUS_GEMM_DEBUG")) std::fprintf(stderr, "[gemm] encode -> %d\n", (int)r);
   return r == CUDA_SUCCESS;
 }
 
@@ -384,6 +398,9 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
     attr_set = true;
   }
+  if (std::getenv("VAGUS_GEMM_DEBUG"))
+    std::fprintf(stderr, "[gemm] launch grid %d smem %d M %d N %d K %d units %d\n", grid, C::SMEM_BYTES, a.M, a.N,
+                 a.K, units);
   kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
@@ -405,7 +422,13 @@ int gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!aligned(a.A) || !aligned(a.B) || (a.lda % 8) || (a.ldb % 8)) return 1;
   if (a.batch > 1 && ((a.strideA % 8) || (a.strideB % 8))) return 1;
-  const int bn = a.block_n > 0 ? a.block_n : (a.N <= 128 ? 128 : 256);
+  const int bn = a.block_n > 0 ? a.block_n : (a.N < 256 ? 128 : 256);
+  // Every TMA box must fit inside its tensor (the tensor-map encoder does not
+  // reject an oversized box reliably); callers route smaller problems elsewhere.
+  const long long a_inner = a.a_mn ? a.M : a.K, a_rows = a.a_mn ? a.K : a.M;
+  const long long b_inner = a.b_mn ? a.N : a.K, b_rows = a.b_mn ? a.K : a.N;
+  const long long a_box = a.a_mn ? 64 : BM, b_box = a.b_mn ? 64 : bn;
+  if (a_inner < 64 || a_rows < a_box || b_inner < 64 || b_rows < b_box) return 6;
   return bn == 128 ? dispatch_major<128>(a, stream) : dispatch_major<256>(a, stream);
 }
 

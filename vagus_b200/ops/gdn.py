@@ -140,56 +140,74 @@ def gdr_decode(q, k, v, g, beta, S, *, scale: float):
 
 # ------------------------------------------------------------- fused layer --
 
+def _packed_weight(m):
+    """bf16 rows [wq; wk; wv; wg; wa; wb; 0-pad] of one layer: every input
+    projection of the layer is one GEMM.  The zero rows pad the count to a
+    multiple of 64 (the weight-gradient GEMM reads it in 64-row blocks)."""
+    ws = [m.wq.weight, m.wk.weight, m.wv.weight, m.wg.weight, m.wa.weight, m.wb.weight]
+    n = sum(w.shape[0] for w in ws)
+    pad = (-n) % 64
+    key = ("gdn_pad", pad, m.dim)
+    zeros = _PAD.get(key)
+    if zeros is None or zeros.device != ws[0].device:
+        zeros = torch.zeros(pad, m.dim, device=ws[0].device, dtype=torch.float32)
+        _PAD[key] = zeros
+    return BF16.get_cat(ws + [zeros]), n
+
+
+_PAD: dict = {}
+
+
 class _GDNMixer(torch.autograd.Function):
-    """h (B, L, D) bf16 -> the gated normalised head concat (B, L, H dv)."""
+    """h (B, L, D) bf16 -> the gated normalised head concat (B, L, H dv).
+    Column layout of the packed projection P: [q | k | v | g | a | b | pad]."""
 
     @staticmethod
-    def forward(ctx, h, wq, wk, wv, wg, wa, wb, A_log, dt_bias, cq, ck, cv, gamma, meta):
+    def forward(ctx, h, Wp, wq, wk, wv, wg, wa, wb, A_log, dt_bias, cq, ck, cv, gamma, meta):
         H, dk, dv, eps, scale = meta
         B, L, Dm = h.shape
         Hk, Hv = H * dk, H * dv
         h2 = as_bf16_2d(h)
         T = h2.shape[0]
-        Wp = BF16.get_cat([wq, wk, wv, wg])                                   # (2Hk + 2Hv, D)
         NP = Wp.shape[0]
         P = torch.empty(T, NP, device=h.device, dtype=torch.bfloat16)
         gemm(h2, False, Wp, False, P)
-        Wab = BF16.get_cat([wa, wb])                                          # (2H, D)
-        AB = torch.empty(T, 2 * H, device=h.device, dtype=torch.bfloat16)
-        gemm(h2, False, Wab, False, AB)
         P3 = P.view(B, L, NP)
+        oa = 2 * Hk + 2 * Hv                                                  # a|b column offset
         C = native()
         q, rq = C.conv_silu_fwd(P3[:, :, :Hk], cq, dk, True)
         k, rk = C.conv_silu_fwd(P3[:, :, Hk:2 * Hk], ck, dk, True)
         v, _ = C.conv_silu_fwd(P3[:, :, 2 * Hk:2 * Hk + Hv], cv, dv, False)
-        g, beta = C.gdn_gates_fwd(AB, A_log.float().contiguous(), dt_bias.float().contiguous(), H)
+        g, beta = C.gdn_gates_fwd(P[:, oa:oa + 2 * H], A_log.float().contiguous(), dt_bias.float().contiguous(), H)
         o, _S, gsaved = _gdr_fwd(q.view(B, L, H, dk), k.view(B, L, H, dk), v.view(B, L, H, dv),
                                  g.view(B, L, H), beta.view(B, L, H), None, scale)
         o = o.contiguous()
-        y, rstd = C.rmsnorm_gated_fwd(o.view(T, H, dv), P[:, 2 * Hk + Hv:], gamma.float().contiguous(), eps, H)
+        y, rstd = C.rmsnorm_gated_fwd(o.view(T, H, dv), P[:, 2 * Hk + Hv:oa], gamma.float().contiguous(), eps, H)
         ctx.dims = (B, L, Dm, H, dk, dv, NP)
         ctx.scale = scale
-        ctx.n_gdr = len(gsaved)
-        ctx.save_for_backward(h2, P, AB, rq, rk, o, rstd, wq, wk, wv, wg, wa, wb, A_log, dt_bias, cq, ck, cv,
-                              gamma, *gsaved)
+        ctx.save_for_backward(h2, Wp, P, rq, rk, o, rstd, A_log, dt_bias, cq, ck, cv, gamma, *gsaved)
         return y.view(B, L, Hv)
 
     @staticmethod
     def backward(ctx, dy):
         B, L, Dm, H, dk, dv, NP = ctx.dims
         Hk, Hv = H * dk, H * dv
+        oa = 2 * Hk + 2 * Hv
         sv = ctx.saved_tensors
-        (h2, P, AB, rq, rk, o, rstd, wq, wk, wv, wg, wa, wb, A_log, dt_bias, cq, ck, cv, gamma) = sv[:19]
-        gsaved = sv[19:]
+        h2, Wp, P, rq, rk, o, rstd, A_log, dt_bias, cq, ck, cv, gamma = sv[:13]
+        gsaved = sv[13:]
         T = h2.shape[0]
         C = native()
         dP = torch.empty(T, NP, device=h2.device, dtype=torch.bfloat16)
+        if NP > oa + 2 * H:
+            dP[:, oa + 2 * H:].zero_()
         do, dgamma = C.rmsnorm_gated_bwd(dy.reshape(T, Hv).to(torch.bfloat16), o.view(T, H, dv),
-                                         P[:, 2 * Hk + Hv:], gamma.float().contiguous(), rstd,
-                                         dP[:, 2 * Hk + Hv:], H)
+                                         P[:, 2 * Hk + Hv:oa], gamma.float().contiguous(), rstd,
+                                         dP[:, 2 * Hk + Hv:oa], H)
         gq, gk, gv, gg, gb, _ = _gdr_bwd(gsaved, do.view(B, L, H, dv), None, ctx.scale, False)
-        dAB, dA_log, ddt = C.gdn_gates_bwd(gg.reshape(T, H), gb.reshape(T, H), AB, A_log.float().contiguous(),
-                                           dt_bias.float().contiguous(), H)
+        dA_log, ddt = C.gdn_gates_bwd(gg.reshape(T, H), gb.reshape(T, H), P[:, oa:oa + 2 * H],
+                                      A_log.float().contiguous(), dt_bias.float().contiguous(), H,
+                                      dP[:, oa:oa + 2 * H])
         P3, dP3 = P.view(B, L, NP), dP.view(B, L, NP)
         dcq = torch.zeros(cq.numel(), device=h2.device, dtype=torch.float32)
         dck = torch.zeros(ck.numel(), device=h2.device, dtype=torch.float32)
@@ -198,18 +216,13 @@ class _GDNMixer(torch.autograd.Function):
         C.conv_silu_bwd(gk.reshape(B, L, Hk), P3[:, :, Hk:2 * Hk], ck, rk, dP3[:, :, Hk:2 * Hk], dck, dk, True)
         C.conv_silu_bwd(gv.reshape(B, L, Hv), P3[:, :, 2 * Hk:2 * Hk + Hv], cv, rq, dP3[:, :, 2 * Hk:2 * Hk + Hv],
                         dcv, dv, False)
-        # dh = dP Wp + dAB Wab  (both weights read N-contiguous)
         dh = torch.empty(T, Dm, device=h2.device, dtype=torch.bfloat16)
-        gemm(dP, False, BF16.get_cat([wq, wk, wv, wg]), True, dh)
-        gemm(dAB, False, BF16.get_cat([wa, wb]), True, dh, S=dh, beta=1.0)
+        gemm(dP, False, Wp, True, dh)                                          # dh = dP Wp
         dWp = torch.zeros(NP, Dm, device=h2.device, dtype=torch.float32)
-        gemm(dP, True, h2, True, dWp, atomic=True)
-        dWab = torch.zeros(2 * H, Dm, device=h2.device, dtype=torch.float32)
-        gemm(dAB, True, h2, True, dWab, atomic=True)
-        dwq, dwk, dwv, dwg = dWp.split([Hk, Hk, Hv, Hv], 0)
-        dwa, dwb = dWab.split([H, H], 0)
-        return (dh.view(B, L, Dm), dwq, dwk, dwv, dwg, dwa, dwb, dA_log, ddt, dcq.view_as(cq), dck.view_as(ck),
-                dcv.view_as(cv), dgamma, None)
+        gemm(dP, True, h2, True, dWp, atomic=True)                             # dWp = dP^T h
+        dwq, dwk, dwv, dwg, dwa, dwb = dWp[:oa + 2 * H].split([Hk, Hk, Hv, Hv, H, H], 0)
+        return (dh.view(B, L, Dm), None, dwq, dwk, dwv, dwg, dwa, dwb, dA_log, ddt, dcq.view_as(cq),
+                dck.view_as(ck), dcv.view_as(cv), dgamma, None)
 
 
 def gdn_mixer(m, x):
@@ -220,7 +233,8 @@ def gdn_mixer(m, x):
     pad = (-L) % CHUNK
     if pad:
         x = torch.nn.functional.pad(x, (0, 0, 0, pad))
-    y = _GDNMixer.apply(x.to(torch.bfloat16), m.wq.weight, m.wk.weight, m.wv.weight, m.wg.weight, m.wa.weight,
-                        m.wb.weight, m.A_log, m.dt_bias, m.conv_q.conv.weight, m.conv_k.conv.weight,
+    Wp, _ = _packed_weight(m)
+    y = _GDNMixer.apply(x.to(torch.bfloat16), Wp, m.wq.weight, m.wk.weight, m.wv.weight, m.wg.weight,
+                        m.wa.weight, m.wb.weight, m.A_log, m.dt_bias, m.conv_q.conv.weight, m.conv_k.conv.weight,
                         m.conv_v.conv.weight, m.o_norm.gamma, meta)
     return y[:, :L] if pad else y

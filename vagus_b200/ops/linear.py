@@ -15,6 +15,12 @@ from torch.nn import functional as F
 from ._core import BF16, as_bf16_2d, autocast_bf16, gemm
 
 
+def gemm_ok(T: int, K: int, N: int) -> bool:
+    """Shapes the tcgen05 GEMM takes in all three directions of a linear
+    layer: every TMA box fits inside its tensor and rows are 16-byte pitched."""
+    return T >= 128 and K >= 64 and N >= 128 and K % 8 == 0 and N % 8 == 0
+
+
 def _wgrad(dy2: torch.Tensor, x2: torch.Tensor, shape) -> torch.Tensor:
     """fp32 dW (N x K) = dy^T (T x N)^T @ x (T x K), split-K atomics."""
     dW = torch.zeros(shape, device=dy2.device, dtype=torch.float32)
@@ -82,14 +88,14 @@ def linear(x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         return F.linear(x, w)
     if x.dtype == torch.float32 and w.dtype == torch.float32 and not autocast_bf16():
         return F.linear(x, w)
-    if x.shape[-1] % 8 or w.shape[0] % 8 or x.numel() == 0:
-        # skinny or unaligned shapes (TMA needs 16-byte row pitches)
+    if x.numel() == 0 or not gemm_ok(x.numel() // x.shape[-1], x.shape[-1], w.shape[0]):
+        # skinny shapes (gate projections, tiny test models): plain bf16 matmul
         return F.linear(x.to(torch.bfloat16), w.to(torch.bfloat16))
     return _Linear.apply(x, w)
 
 
 def linear_residual(resid: torch.Tensor, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
     """``resid + x @ w.T`` with the add fused into the GEMM epilogue (fp32 out)."""
-    if not x.is_cuda or x.shape[-1] % 8 or w.shape[0] % 8:
+    if not x.is_cuda or not gemm_ok(x.numel() // x.shape[-1], x.shape[-1], w.shape[0]):
         return resid + linear(x, w)
     return _LinearResidual.apply(resid, x, w)
