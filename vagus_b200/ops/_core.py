@@ -57,6 +57,10 @@ class _Bf16Cache:
 
     def get_cat(self, ws: list[torch.Tensor]) -> torch.Tensor:
         """Row-concatenation of several masters' bf16 copies (one GEMM operand)."""
+        if any(w.dtype != torch.float32 for w in ws):
+            # low-precision compute copies (e.g. all-gathered by FSDP) may be
+            # refilled in place without a version bump: never cache them
+            return torch.cat([w.detach().to(torch.bfloat16) for w in ws], 0).contiguous()
         key = ("cat",) + tuple(id(w) for w in ws)
         vers = tuple((w._version, w.data_ptr()) for w in ws)
         hit = self._d.get(key)

@@ -183,6 +183,64 @@ def find_resume(run_dir: Path) -> Path | None:
 
 # ------------------------------------------------------------------- training --
 
+class StepRunner:
+    """One optimizer step: ``grad_accum_steps`` micro-batches pulled from an
+    iterator of host (x, y) batches, copied to the device (non-blocking from
+    pinned memory), forward + fused CE + backward (DDP: gradient sync only on
+    the last micro-step; FSDP: the root module computes the loss), the
+    replicated-parameter reduction, clipping and the optimizer update.
+    Returns (mean loss, mean z term or None, grad norm) as device tensors --
+    nothing here synchronises with the host."""
+
+    def __init__(self, model, optimizer, ce_fn, device, *, grad_accum_steps: int = 1, grad_clip=1.0,
+                 is_fsdp: bool = False, is_dist: bool = False, replicate_size: int = 1, autocast=None, mesh=None):
+        self.model = model
+        self.optimizer = optimizer
+        self.ce_fn = ce_fn
+        self.device = device
+        self.accum = grad_accum_steps
+        self.grad_clip = grad_clip
+        self.is_fsdp = is_fsdp
+        self.is_dist = is_dist
+        self.replicate_size = replicate_size
+        self.autocast = autocast if autocast is not None else nullcontext()
+        self.mesh = mesh
+        self.head_weight = unwrap(model).head.weight
+        self.last_batch = None
+
+    def step(self, batches):
+        model, ce_fn = self.model, self.ce_fn
+        self.optimizer.zero_grad(set_to_none=True)
+        loss_acc = torch.zeros((), device=self.device)
+        z_acc = torch.zeros((), device=self.device) if ce_fn.tracks_z else None
+        for micro in range(self.accum):
+            x, y = next(batches)
+            x = x.to(self.device, non_blocking=True)
+            y = y.to(self.device, non_blocking=True)
+            last = micro == self.accum - 1
+            if self.is_fsdp:
+                if self.replicate_size > 1:
+                    model.set_requires_all_reduce(last)
+                with self.autocast:
+                    loss = model(x, y)
+                    (loss / self.accum).backward()
+            else:
+                sync = model.no_sync() if self.is_dist and not last else nullcontext()
+                with sync, self.autocast:
+                    hidden = model(x, return_hidden=True)
+                    loss = ce_fn(hidden, self.head_weight, y)
+                    (loss / self.accum).backward()
+            loss_acc += loss.detach()
+            if z_acc is not None:
+                z_acc += ce_fn.last_z
+            self.last_batch = x
+        if self.is_fsdp:
+            reduce_replicated(model, self.mesh)
+        grad_norm = clip_grad_norm(model, self.grad_clip)
+        self.optimizer.step()
+        return loss_acc / self.accum, (None if z_acc is None else z_acc / self.accum), grad_norm
+
+
 _STOP = False
 
 
@@ -318,7 +376,9 @@ def train(config: TrainConfig, teardown: bool = True):
                       slow_interval=config.slow_interval, fast=FAST_METRICS + list(hooks.get("fast", [])),
                       slow=SLOW_METRICS + list(hooks.get("slow", [])), tb_dir=run_dir / "tb" if is_main else None,
                       log_fn=log)
-    head_weight = unwrap(model).head.weight
+    runner = StepRunner(model, optimizer, ce_fn, device, grad_accum_steps=config.grad_accum_steps,
+                        grad_clip=config.grad_clip, is_fsdp=is_fsdp, is_dist=is_dist,
+                        replicate_size=replicate_size, autocast=autocast, mesh=mesh)
     batches = iter(loader)
     model.train()
     last_recent = time.time()
@@ -329,34 +389,8 @@ def train(config: TrainConfig, teardown: bool = True):
             mult = sched(step / steps_total)
             for g in optimizer.param_groups:
                 g["lr"] = g["base_lr"] * mult
-            optimizer.zero_grad(set_to_none=True)
-            loss_acc = torch.zeros((), device=device)
-            z_acc = torch.zeros((), device=device) if ce_fn.tracks_z else None
-            for micro in range(config.grad_accum_steps):
-                x, y = next(batches)
-                x = x.to(device, non_blocking=True)
-                y = y.to(device, non_blocking=True)
-                last = micro == config.grad_accum_steps - 1
-                if is_fsdp:
-                    if replicate_size > 1:
-                        model.set_requires_all_reduce(last)
-                    with autocast:
-                        loss = model(x, y)
-                        (loss / config.grad_accum_steps).backward()
-                else:
-                    sync = model.no_sync() if is_dist and not last else nullcontext()
-                    with sync, autocast:
-                        hidden = model(x, return_hidden=True)
-                        loss = ce_fn(hidden, head_weight, y)
-                        (loss / config.grad_accum_steps).backward()
-                loss_acc += loss.detach()
-                if z_acc is not None:
-                    z_acc += ce_fn.last_z
-                ctx.last_batch = x
-            if is_fsdp:
-                reduce_replicated(model, mesh)
-            grad_norm = clip_grad_norm(model, config.grad_clip)
-            optimizer.step()
+            loss_acc, z_acc, grad_norm = runner.step(batches)
+            ctx.last_batch = runner.last_batch
             tokens_seen += tokens_per_step
             if device.type == "cuda":
                 ops.check_error()
@@ -369,9 +403,7 @@ def train(config: TrainConfig, teardown: bool = True):
             stop = bool(flags[0].item()) or bool(flags[2].item())
             want_recent = bool(flags[1].item())
             stopped_early = stopped_early or stop
-            monitor.observe(step, loss_acc / config.grad_accum_steps, grad_norm, tokens_seen,
-                            final=stop or step == steps_total,
-                            z=None if z_acc is None else z_acc / config.grad_accum_steps)
+            monitor.observe(step, loss_acc, grad_norm, tokens_seen, final=stop or step == steps_total, z=z_acc)
             if config.permanent_ckpt_interval and step % config.permanent_ckpt_interval == 0 and step < steps_total:
                 p = save_checkpoint(run_dir, "permanent", step, tokens_seen, model, optimizer, loader, config,
                                     is_fsdp, is_main)
