@@ -71,6 +71,15 @@ CONFIGS = {
         seq=512, global_tokens=16384, micro=8, label="tiny"),
 }
 
+# Configurations whose reference stock path faulted the GPU on this pool: they
+# are not run again (the fault is recorded in DESIGN.md).
+REFERENCE_FAULTS = {
+    "gdn340m": ("reference stock path (fla chunk_gated_delta_rule, head_dim 256) raised CUDA 'misaligned address' "
+                "in fla prepare_wy_repr_bwd (Triton autotune) on B200; not re-run under the GPU-fault policy"),
+    "hybrid1.3b": ("same fla chunk_gated_delta_rule backward at head_dim 256 as gdn340m, which faulted on B200; "
+                   "not run under the GPU-fault policy"),
+}
+
 MUON = dict(lr=1.75e-3, momentum=0.95, weight_decay=0.1, lr_adjust="rms", ns_coeffs="polar_express",
             adamw=dict(lr=1.75e-3, betas=[0.9, 0.95], weight_decay=0.1))
 ADAMW = dict(lr=3e-4, betas=[0.9, 0.95], weight_decay=0.1)
@@ -356,6 +365,9 @@ def main():
         args.warmup = 3
     if args.impl == "reference" and not (ROOT / "baseline" / "_ref" / "infra").exists():
         print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
+        return
+    if args.impl == "reference" and args.config in REFERENCE_FAULTS:
+        print(json.dumps({"impl": "reference", "unavailable": REFERENCE_FAULTS[args.config]}))
         return
     out = run(args)
     if out is not None:

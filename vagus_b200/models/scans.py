@@ -196,6 +196,8 @@ def chunk_scan(q, k, v, g, beta, S0, *, scale: float, delta: bool, chunk_size: i
         Vn = Um[:, :, n] if Wm is None else Um[:, :, n] - Wm[:, :, n] @ S
         outs.append(Gi[:, :, n, :, None] * (Q[:, :, n] @ S) + Aqk[:, :, n] @ Vn)
         S = Gi[:, :, n, -1, None, None] * S + (K[:, :, n] * Gend[:, :, n, :, None]).transpose(-1, -2) @ Vn
+    if not outs:
+        return q.new_zeros(B, 0, H, dv), S
     o = torch.stack(outs, 2).permute(0, 2, 3, 1, 4).reshape(B, N * C, H, dv)[:, :L]
     return o.to(q.dtype), S
 
@@ -275,5 +277,7 @@ def chunk_scan_vec(q, k, v, g, beta, S0, *, scale: float, delta: bool, chunk_siz
         else:
             on, S = _vec_chunk(*args)
         outs.append(on)
+    if not outs:
+        return q.new_zeros(B, 0, H, dv), S
     o = torch.stack(outs, 2).permute(0, 2, 3, 1, 4).reshape(B, N * C, H, dv)[:, :L]
     return o.to(q.dtype), S
