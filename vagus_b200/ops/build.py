@@ -24,7 +24,8 @@ BUILD_DIR = HERE / "_build"
 
 SOURCES = [
     "bindings.cpp", "bind_seq.cpp", "bind_attn.cpp", "bind_comm.cpp",
-    "gemm.cu", "norm.cu", "elementwise.cu", "conv.cu", "gdn_gates.cu", "gdr.cu", "attention.cu", "comm.cu",
+    "gemm.cu", "norm.cu", "elementwise.cu", "conv.cu", "gdn_gates.cu", "gdr.cu", "gdr_intra.cu", "attention.cu",
+    "comm.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",

@@ -120,6 +120,48 @@ std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
   return {dW, dQh, dKt, dA, dU, dgC, dS0};
 }
 
+// Intra-chunk stage.  q, k (B, L, H, DK), v (B, L, H, DV) bf16 contiguous;
+// g, beta (B, L, H) fp32.  Returns W, Qh, Kt, A, U (chunk-major bf16), gC.
+std::vector<Tensor> gdr_intra_fwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, double scale) {
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && q.scalar_type() == at::kBFloat16,
+              "gdr_intra: contiguous bf16 q/k/v");
+  const int64_t B = q.size(0), L = q.size(1);
+  const int H = static_cast<int>(q.size(2)), DK = static_cast<int>(q.size(3)), DV = static_cast<int>(v.size(3));
+  TORCH_CHECK(L % 64 == 0, "gdr_intra: L must be a multiple of 64");
+  const int64_t N = L / 64;
+  auto bf = q.options();
+  auto W = torch::empty({B * H, N, 64, DK}, bf), Qh = torch::empty({B * H, N, 64, DK}, bf);
+  auto Kt = torch::empty({B * H, N, 64, DK}, bf), A = torch::empty({B * H, N, 64, 64}, bf);
+  auto U = torch::empty({B * H, N, 64, DV}, bf);
+  auto gC = torch::empty({B * H, N}, q.options().dtype(at::kFloat));
+  auto gc = g.contiguous(), bc = beta.contiguous();
+  vagus::GdrIntraArgs a{q.data_ptr(), k.data_ptr(), v.data_ptr(), gc.data_ptr<float>(), bc.data_ptr<float>(),
+                        W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), U.data_ptr(), gC.data_ptr<float>(),
+                        B, L, H, DK, DV, static_cast<float>(scale)};
+  check(vagus::gdr_intra_fwd(a, stream()), "gdr_intra_fwd");
+  return {W, Qh, Kt, A, U, gC};
+}
+
+// Returns dq, dk, dv (token-major bf16), dg, dbeta (fp32).
+std::vector<Tensor> gdr_intra_bwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor dW, Tensor dQh,
+                                  Tensor dKt, Tensor dA, Tensor dU, Tensor dgC, double scale) {
+  const int64_t B = q.size(0), L = q.size(1);
+  const int H = static_cast<int>(q.size(2)), DK = static_cast<int>(q.size(3)), DV = static_cast<int>(v.size(3));
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  auto dg = torch::empty({B, L, H}, q.options().dtype(at::kFloat));
+  auto db = torch::empty({B, L, H}, q.options().dtype(at::kFloat));
+  auto gc = g.contiguous(), bc = beta.contiguous();
+  vagus::GdrIntraBwdArgs a;
+  a.f = vagus::GdrIntraArgs{q.data_ptr(), k.data_ptr(), v.data_ptr(), gc.data_ptr<float>(), bc.data_ptr<float>(),
+                            nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, B, L, H, DK, DV,
+                            static_cast<float>(scale)};
+  a.dW = dW.data_ptr<float>(); a.dQh = dQh.data_ptr<float>(); a.dKt = dKt.data_ptr<float>(); a.dA = dA.data_ptr<float>();
+  a.dU = dU.data_ptr(); a.dgC = dgC.data_ptr<float>();
+  a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr(); a.dg = dg.data_ptr<float>(); a.dbeta = db.data_ptr<float>();
+  check(vagus::gdr_intra_bwd(a, stream()), "gdr_intra_bwd");
+  return {dq, dk, dv, dg, db};
+}
+
 // q, k (BH, dk) bf16, v (BH, dv) bf16, g, beta (BH) fp32, S (BH, dk, dv) fp32 in place -> o (BH, dv)
 Tensor gdr_decode(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor S, double scale) {
   const int64_t BH = S.size(0);
@@ -144,4 +186,6 @@ void register_seq_ops(pybind11::module& m) {
   m.def("gdr_rec_fwd", &gdr_rec_fwd);
   m.def("gdr_rec_bwd", &gdr_rec_bwd);
   m.def("gdr_decode", &gdr_decode);
+  m.def("gdr_intra_fwd", &gdr_intra_fwd);
+  m.def("gdr_intra_bwd", &gdr_intra_bwd);
 }

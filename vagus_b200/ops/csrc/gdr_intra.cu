@@ -1,0 +1,531 @@
+// Intra-chunk stage of the chunked gated delta rule (scalar gate), forward
+// and backward, one CTA per (batch, head, 64-token chunk).
+//
+// With gamma = cumsum(g) inside the chunk, G = exp(gamma), D_ij =
+// exp(gamma_i - gamma_j) (i >= j, masked before the exp), the forward builds
+//     M  = strict_lower(diag(b) (K K^T o D)),   T = (I + M)^{-1}
+//     W  = T diag(b G) K          U  = T diag(b) V
+//     Qh = s diag(G) Q            Kt = diag(G_C / G) K
+//     A  = s (Q K^T o D) (causal, diagonal included),   gC = G_C
+// The unit-lower-triangular inverse is a row-by-row forward substitution in
+// shared memory (fp32; each row combines up to 63 finished rows, the 64
+// columns x 4 partial sums spread over the 256 threads).  The 64 x 64 x dk
+// products run on the tensor cores (mma.sync, bf16 in, fp32 accumulate).
+//
+// The backward takes dW, dQh, dKt, dA (fp32, summed over value tiles by the
+// recurrence backward), dU and dgC and returns dq, dk, dv, dg, dbeta:
+//     dXw = T^T dW,  dXu = T^T dU          (Xw = diag(bG) K, Xu = diag(b) V)
+//     dT  = dW Xw^T + dU Xu^T,  dM = -strict_lower(T^T dT T^T)
+//     dKK = dM o b D,  dQK = s dA o D,  dD = dM o b KK + s dA o QK
+//     dK  = diag(bG) dXw + (dKK + dKK^T) K + dQK^T Q + diag(G_C/G) dKt
+//     dQ  = dQK K + s diag(G) dQh,   dV = diag(b) dXu
+// plus the per-row scalars (dbeta, and dgamma from G, D, G_C and G_C/G),
+// then dg = reverse cumsum(dgamma) within the chunk.
+//
+// Token-major inputs: q, k (B, L, H, DK), v (B, L, H, DV) bf16; g, beta
+// (B, L, H) fp32.  Chunk-major outputs as the recurrence kernels expect.
+#include "common.cuh"
+#include "kernels.h"
+#include "mma.cuh"
+
+namespace vagus {
+namespace {
+
+using namespace mma;
+
+constexpr int C = 64;
+constexpr int THREADS = 256;
+
+template <int DK, int DV>
+struct FwdSmem {
+  __nv_bfloat16 Q[C][DK + PAD];
+  __nv_bfloat16 K[C][DK + PAD];
+  __nv_bfloat16 V[C][DV + PAD];
+  float M[C][C + 1];             // M, then T (in place)
+  __nv_bfloat16 Tb[C][C + PAD];
+  float gam[C], beta[C];
+};
+
+// inclusive prefix sum of g over the chunk (64 values) into gam; warp 0
+__device__ __forceinline__ void chunk_cumsum(const float* g_in, float* gam) {
+  const int lane = threadIdx.x & 31;
+  float a = g_in[2 * lane], b = g_in[2 * lane + 1];
+  float s = a + b;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const float t = __shfl_up_sync(0xffffffffu, s, o);
+    if (lane >= o) s += t;
+  }
+  gam[2 * lane + 1] = s;
+  gam[2 * lane] = s - b;
+}
+
+// T = (I + M)^{-1} in place, M strictly lower triangular (row stride C + 1)
+__device__ __forceinline__ void tri_inverse_inplace(float (*M)[C + 1]) {
+  const int c = threadIdx.x >> 2, part = threadIdx.x & 3;
+  for (int i = 0; i < C; ++i) {
+    float s = 0.f;
+    if (c < i)
+      for (int j = c + part; j < i; j += 4) s += M[i][j] * ((j == c) ? 1.f : M[j][c]);
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    __syncthreads();                       // row i of M read by everyone
+    if (part == 0) M[i][c] = (c < i) ? -s : (c == i ? 1.f : 0.f);
+    __syncthreads();
+  }
+}
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(THREADS)
+intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                 const __nv_bfloat16* __restrict__ v, const float* __restrict__ g, const float* __restrict__ beta,
+                 __nv_bfloat16* __restrict__ Wo, __nv_bfloat16* __restrict__ Qho, __nv_bfloat16* __restrict__ Kto,
+                 __nv_bfloat16* __restrict__ Ao, __nv_bfloat16* __restrict__ Uo, float* __restrict__ gCo, int L, int H,
+                 float scale) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  FwdSmem<DK, DV>& sm = *reinterpret_cast<FwdSmem<DK, DV>*>(smem_raw);
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int N = gridDim.x;
+  const long long bh = (long long)b * H + h;
+  const long long cidx = bh * N + n;
+  const long long tok0 = (long long)b * L + (long long)n * C;
+  const int warp = threadIdx.x / 32;
+
+  load_tile(&sm.Q[0][0], DK + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  load_tile(&sm.V[0][0], DV + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
+  cp_commit();
+  __shared__ float graw[C];
+  if (threadIdx.x < C) {
+    graw[threadIdx.x] = g[(tok0 + threadIdx.x) * H + h];
+    sm.beta[threadIdx.x] = beta[(tok0 + threadIdx.x) * H + h];
+  }
+  __syncthreads();
+  if (warp == 0) chunk_cumsum(graw, sm.gam);
+  cp_wait_all();
+  __syncthreads();
+
+  const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+  {
+    float kk[1][4][4], qk[1][4][4];
+    zero(kk);
+    zero(qk);
+    warp_mma<1, 4, false, false>(kk, &sm.K[0][0], DK + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
+    warp_mma<1, 4, false, false>(qk, &sm.Q[0][0], DK + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+        const float d = (j <= i) ? __expf(sm.gam[i] - sm.gam[j]) : 0.f;
+        sm.M[i][j] = (j < i) ? sm.beta[i] * kk[0][nt][e] * d : 0.f;
+        Ao[(cidx * C + i) * C + j] = f2bf(scale * qk[0][nt][e] * d);
+      }
+  }
+  __syncthreads();
+  tri_inverse_inplace(sm.M);
+
+  // T to bf16; Qh, Kt out; K -> diag(b G) K and V -> diag(b) V in place
+  for (int idx = threadIdx.x; idx < C * C; idx += THREADS) {
+    const int i = idx / C, j = idx % C;
+    sm.Tb[i][j] = f2bf(sm.M[i][j]);
+  }
+  const float glast = sm.gam[C - 1];
+  for (int idx = threadIdx.x; idx < C * (DK / 2); idx += THREADS) {
+    const int i = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
+    const float gi = __expf(sm.gam[i]);
+    const float ei = __expf(glast - sm.gam[i]);
+    const float2 qv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[i][c]));
+    const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
+    *reinterpret_cast<uint32_t*>(Qho + (cidx * C + i) * DK + c) = pack_bf16x2(scale * gi * qv.x, scale * gi * qv.y);
+    *reinterpret_cast<uint32_t*>(Kto + (cidx * C + i) * DK + c) = pack_bf16x2(ei * kv.x, ei * kv.y);
+    const float bg = sm.beta[i] * gi;
+    *reinterpret_cast<uint32_t*>(&sm.K[i][c]) = pack_bf16x2(bg * kv.x, bg * kv.y);
+  }
+  for (int idx = threadIdx.x; idx < C * (DV / 2); idx += THREADS) {
+    const int i = idx / (DV / 2), c = (idx % (DV / 2)) * 2;
+    const float2 vv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.V[i][c]));
+    *reinterpret_cast<uint32_t*>(&sm.V[i][c]) = pack_bf16x2(sm.beta[i] * vv.x, sm.beta[i] * vv.y);
+  }
+  if (threadIdx.x == 0) gCo[cidx] = __expf(glast);
+  __syncthreads();
+
+  // W = T Xw, U = T Xu: warp tile 16 rows x (D / 2) columns
+  {
+    constexpr int NT = DK / 16;
+    float acc[1][NT][4];
+    zero(acc);
+    const int c0 = (warp >> 2) * (DK / 2);
+    warp_mma<1, NT, false, true>(acc, &sm.Tb[0][0], C + PAD, &sm.K[0][0], DK + PAD, m0, c0, C);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(Wo + (cidx * C + i) * DK + c) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
+      }
+  }
+  {
+    constexpr int NT = DV / 16;
+    float acc[1][NT][4];
+    zero(acc);
+    const int c0 = (warp >> 2) * (DV / 2);
+    warp_mma<1, NT, false, true>(acc, &sm.Tb[0][0], C + PAD, &sm.V[0][0], DV + PAD, m0, c0, C);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(Uo + (cidx * C + i) * DV + c) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
+      }
+  }
+}
+
+// ------------------------------------------------------------------ backward --
+
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+template <int DK, int DV>
+struct BwdSmem {
+  static constexpr int DX = cmax(DK, DV);
+  __nv_bfloat16 K[C][DK + PAD];          // B0: K throughout
+  __nv_bfloat16 X1[C][DX + PAD];         // B1: V (phase 1-2), then dQK | dKKsym (bf16 64 x 72 each)
+  __nv_bfloat16 X2[C][DX + PAD];         // B2: Q (phase 1), dW (phase 2), Q again (phase 4)
+  __nv_bfloat16 X3[C][DX + PAD];         // B3: dU (phase 2), then P (fp32 64 x 65)
+  float KK[C][C + 1];                    // KK, then dKK (in place)
+  float QK[C][C + 1];
+  float T[C][C + 1];
+  float dT[C][C + 1];                    // dT, then dM
+  __nv_bfloat16 Tb[C][C + PAD];
+  // dQK | dKKsym (bf16, 64 x 72 each) live in X1 once V is consumed, when X1 is
+  // wide enough; narrower heads get a dedicated buffer
+  static constexpr bool kInX1 = (DX + PAD) >= 2 * (C + PAD);
+  __nv_bfloat16 dQKsep[kInX1 ? 1 : 2 * C][C + PAD];
+  float gam[C], beta[C], graw[C];
+  float rw[C];     // sum_c dXw K         (-> dbeta * G, dG * beta)
+  float ru[C];     // sum_c dXu V         (-> dbeta)
+  float rq[C];     // sum_c dQh Q         (-> dG)
+  float rk[C];     // sum_c dKt K         (-> dgamma via G_C / G)
+  float rm[C];     // sum_j dM KK D       (-> dbeta)
+  float dgam[C];
+};
+
+template <int NT>
+__device__ __forceinline__ void row_dot_accumulate(const float (&acc)[1][NT][4], const __nv_bfloat16* X, int ldx,
+                                                   int m0, int c0, float* out) {
+  // out[i] += sum over this warp's fragment of acc[i][c] * X[i][c]
+  float part[2] = {0.f, 0.f};
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+      part[e >> 1] += acc[0][nt][e] * bf2f(X[i * ldx + c]);
+    }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float s = part[r];
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    if ((threadIdx.x & 3) == 0) atomicAdd(&out[m0 + ((threadIdx.x & 31) >> 2) + 8 * r], s);
+  }
+}
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(THREADS)
+intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                 const __nv_bfloat16* __restrict__ v, const float* __restrict__ g, const float* __restrict__ beta,
+                 const float* __restrict__ dW, const float* __restrict__ dQh, const float* __restrict__ dKt,
+                 const float* __restrict__ dA, const __nv_bfloat16* __restrict__ dU, const float* __restrict__ dgC,
+                 __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
+                 float* __restrict__ dg, float* __restrict__ dbeta, int L, int H, float scale) {
+  using S = BwdSmem<DK, DV>;
+  constexpr int DX = S::DX;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int N = gridDim.x;
+  const long long bh = (long long)b * H + h;
+  const long long cidx = bh * N + n;
+  const long long tok0 = (long long)b * L + (long long)n * C;
+  const int warp = threadIdx.x / 32;
+  const int tid = threadIdx.x;
+  const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+
+  // ---- phase 1: K, V, Q; gates; KK, QK; M -> T
+  load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  load_tile(&sm.X1[0][0], DX + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
+  load_tile(&sm.X2[0][0], DX + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  cp_commit();
+  if (tid < C) {
+    sm.graw[tid] = g[(tok0 + tid) * H + h];
+    sm.beta[tid] = beta[(tok0 + tid) * H + h];
+    sm.rw[tid] = sm.ru[tid] = sm.rq[tid] = sm.rk[tid] = sm.rm[tid] = sm.dgam[tid] = 0.f;
+  }
+  __syncthreads();
+  if (warp == 0) chunk_cumsum(sm.graw, sm.gam);
+  cp_wait_all();
+  __syncthreads();
+  {
+    float kk[1][4][4], qk[1][4][4];
+    zero(kk);
+    zero(qk);
+    warp_mma<1, 4, false, false>(kk, &sm.K[0][0], DK + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
+    warp_mma<1, 4, false, false>(qk, &sm.X2[0][0], DX + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+        const float d = (j <= i) ? __expf(sm.gam[i] - sm.gam[j]) : 0.f;
+        sm.KK[i][j] = kk[0][nt][e];
+        sm.QK[i][j] = qk[0][nt][e];
+        sm.T[i][j] = (j < i) ? sm.beta[i] * kk[0][nt][e] * d : 0.f;
+      }
+  }
+  __syncthreads();
+  tri_inverse_inplace(sm.T);
+  for (int idx = tid; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.T[idx / C][idx % C]);
+
+  // ---- phase 2: dW -> X2, dU -> X3 (bf16)
+  for (int idx = tid; idx < C * (DK / 4); idx += THREADS) {
+    const int i = idx / (DK / 4), c = (idx % (DK / 4)) * 4;
+    const float4 w4 = *reinterpret_cast<const float4*>(dW + (cidx * C + i) * DK + c);
+    *reinterpret_cast<uint2*>(&sm.X2[i][c]) = make_uint2(pack_bf16x2(w4.x, w4.y), pack_bf16x2(w4.z, w4.w));
+  }
+  load_tile(&sm.X3[0][0], DX + PAD, dU + cidx * C * DV, DV, C, DV);
+  cp_commit();
+  cp_wait_all();
+  __syncthreads();
+
+  constexpr int NTK = DK / 16, NTV = DV / 16;
+  const int ck0 = (warp >> 2) * (DK / 2), cv0 = (warp >> 2) * (DV / 2);
+  float dKacc[1][NTK][4];
+  {
+    // dXw = T^T dW  ->  dK = diag(b G) dXw ; rw += dXw . K
+    zero(dKacc);
+    warp_mma<1, NTK, true, true>(dKacc, &sm.Tb[0][0], C + PAD, &sm.X2[0][0], DX + PAD, m0, ck0, C);
+    row_dot_accumulate<NTK>(dKacc, &sm.K[0][0], DK + PAD, m0, ck0, sm.rw);
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + frag_row(0, e);
+        dKacc[0][nt][e] *= sm.beta[i] * __expf(sm.gam[i]);
+      }
+  }
+  {
+    // dXu = T^T dU  ->  dV = diag(b) dXu ; ru += dXu . V
+    float acc[1][NTV][4];
+    zero(acc);
+    warp_mma<1, NTV, true, true>(acc, &sm.Tb[0][0], C + PAD, &sm.X3[0][0], DX + PAD, m0, cv0, C);
+    row_dot_accumulate<NTV>(acc, &sm.X1[0][0], DX + PAD, m0, cv0, sm.ru);
+#pragma unroll
+    for (int nt = 0; nt < NTV; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = cv0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(dv + ((tok0 + i) * H + h) * DV + c) =
+            pack_bf16x2(sm.beta[i] * acc[0][nt][e], sm.beta[i] * acc[0][nt][e + 1]);
+      }
+  }
+  {
+    // dT = (dW K^T) diag(b G) + (dU V^T) diag(b)
+    float a1[1][4][4], a2[1][4][4];
+    zero(a1);
+    zero(a2);
+    warp_mma<1, 4, false, false>(a1, &sm.X2[0][0], DX + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
+    warp_mma<1, 4, false, false>(a2, &sm.X3[0][0], DX + PAD, &sm.X1[0][0], DX + PAD, m0, n0, DV);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+        sm.dT[i][j] = sm.beta[j] * (__expf(sm.gam[j]) * a1[0][nt][e] + a2[0][nt][e]);
+      }
+  }
+  __syncthreads();
+
+  // ---- phase 3: P = T^T dT (fp32, into X3), dM = -strict_lower(P T^T) (into dT)
+  float (*P)[C + 1] = reinterpret_cast<float (*)[C + 1]>(&sm.X3[0][0]);
+  for (int idx = tid; idx < C * C; idx += THREADS) {
+    const int i = idx / C, j = idx % C;
+    float s = 0.f;
+    for (int kk = i; kk < C; ++kk) s += sm.T[kk][i] * sm.dT[kk][j];   // T[kk][i] = 0 for kk < i
+    P[i][j] = s;
+  }
+  __syncthreads();
+  for (int idx = tid; idx < C * C; idx += THREADS) {
+    const int i = idx / C, j = idx % C;
+    float s = 0.f;
+    if (j < i)
+      for (int kk = 0; kk <= j; ++kk) s += P[i][kk] * sm.T[j][kk];  // T[j][kk] = 0 for kk > j
+    sm.dT[i][j] = -s;
+  }
+  __syncthreads();
+
+  // elementwise: dKK (in place of KK), dQK (bf16), D-gradients, dbeta partials
+  __nv_bfloat16 (*dQKb)[C + PAD] = S::kInX1 ? reinterpret_cast<__nv_bfloat16 (*)[C + PAD]>(&sm.X1[0][0])
+                                             : sm.dQKsep;
+  __nv_bfloat16 (*dKKb)[C + PAD] = dQKb + C;
+  for (int idx = tid; idx < C * C; idx += THREADS) {
+    const int i = idx / C, j = idx % C;
+    float dkk = 0.f, dqk = 0.f, dd = 0.f, rmv = 0.f;
+    if (j <= i) {
+      const float d = __expf(sm.gam[i] - sm.gam[j]);
+      const float da = dA[(cidx * C + i) * C + j];
+      dqk = scale * da * d;
+      dd = scale * da * sm.QK[i][j];
+      if (j < i) {
+        const float dm = sm.dT[i][j];
+        dkk = dm * sm.beta[i] * d;
+        rmv = dm * sm.KK[i][j] * d;
+        dd += dm * sm.beta[i] * sm.KK[i][j];
+      }
+      const float t = dd * d;
+      if (j < i) {
+        atomicAdd(&sm.dgam[i], t);
+        atomicAdd(&sm.dgam[j], -t);
+        atomicAdd(&sm.rm[i], rmv);
+      }
+    }
+    sm.KK[i][j] = dkk;
+    dQKb[i][j] = f2bf(dqk);
+  }
+  __syncthreads();
+  for (int idx = tid; idx < C * C; idx += THREADS) {
+    const int i = idx / C, j = idx % C;
+    dKKb[i][j] = f2bf(sm.KK[i][j] + sm.KK[j][i]);
+  }
+  // ---- phase 4: reload Q, dK and dQ GEMMs
+  load_tile(&sm.X2[0][0], DX + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  cp_commit();
+  cp_wait_all();
+  __syncthreads();
+
+  warp_mma<1, NTK, false, true>(dKacc, &dKKb[0][0], C + PAD, &sm.K[0][0], DK + PAD, m0, ck0, C);
+  warp_mma<1, NTK, true, true>(dKacc, &dQKb[0][0], C + PAD, &sm.X2[0][0], DX + PAD, m0, ck0, C);
+  {
+    const float glast = sm.gam[C - 1];
+    float part[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = ck0 + frag_col(nt, e);
+        const float ei = __expf(glast - sm.gam[i]);
+        const float2 dkt = *reinterpret_cast<const float2*>(dKt + (cidx * C + i) * DK + c);
+        const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
+        part[e >> 1] += dkt.x * kv.x + dkt.y * kv.y;
+        *reinterpret_cast<uint32_t*>(dk + ((tok0 + i) * H + h) * DK + c) =
+            pack_bf16x2(dKacc[0][nt][e] + ei * dkt.x, dKacc[0][nt][e + 1] + ei * dkt.y);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float s = part[r];
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      if ((tid & 3) == 0) atomicAdd(&sm.rk[m0 + ((tid & 31) >> 2) + 8 * r], s);
+    }
+  }
+  {
+    float dQacc[1][NTK][4];
+    zero(dQacc);
+    warp_mma<1, NTK, false, true>(dQacc, &dQKb[0][0], C + PAD, &sm.K[0][0], DK + PAD, m0, ck0, C);
+    float part[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = ck0 + frag_col(nt, e);
+        const float gi = __expf(sm.gam[i]);
+        const float2 dqh = *reinterpret_cast<const float2*>(dQh + (cidx * C + i) * DK + c);
+        const float2 qv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.X2[i][c]));
+        part[e >> 1] += dqh.x * qv.x + dqh.y * qv.y;
+        *reinterpret_cast<uint32_t*>(dq + ((tok0 + i) * H + h) * DK + c) =
+            pack_bf16x2(dQacc[0][nt][e] + scale * gi * dqh.x, dQacc[0][nt][e + 1] + scale * gi * dqh.y);
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float s = part[r];
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      if ((tid & 3) == 0) atomicAdd(&sm.rq[m0 + ((tid & 31) >> 2) + 8 * r], s);
+    }
+  }
+  __syncthreads();
+
+  // ---- phase 5: per-row scalars, reverse cumsum
+  if (warp == 0) {
+    const int lane = tid & 31;
+    const float glast = sm.gam[C - 1];
+    float dgl[2], tail = 0.f;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int i = 2 * lane + r;
+      const float gi = __expf(sm.gam[i]);
+      const float ei = __expf(glast - sm.gam[i]);
+      const float dG = sm.beta[i] * sm.rw[i] + scale * sm.rq[i];
+      dgl[r] = sm.dgam[i] + dG * gi - ei * sm.rk[i];
+      tail += ei * sm.rk[i];
+      dbeta[(tok0 + i) * H + h] = gi * sm.rw[i] + sm.ru[i] + sm.rm[i];
+    }
+    tail = warp_sum(tail);
+    if (lane == 31) dgl[1] += tail + dgC[cidx] * __expf(glast);
+    // reverse inclusive cumsum over i (64 values, 2 per lane)
+    float s = dgl[0] + dgl[1];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float t = __shfl_down_sync(0xffffffffu, s, o);
+      if (lane + o < 32) s += t;
+    }
+    // s = sum over lanes >= lane of (dgl0 + dgl1)
+    dg[(tok0 + 2 * lane + 1) * H + h] = s - dgl[0];
+    dg[(tok0 + 2 * lane) * H + h] = s;
+  }
+}
+
+template <int DK, int DV>
+int launch_fwd(const GdrIntraArgs& a, cudaStream_t st) {
+  const size_t sm = sizeof(FwdSmem<DK, DV>);
+  auto kern = intra_fwd_kernel<DK, DV>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  dim3 grid(static_cast<unsigned>(a.L / C), a.H, static_cast<unsigned>(a.B));
+  kern<<<grid, THREADS, sm, st>>>((const __nv_bfloat16*)a.q, (const __nv_bfloat16*)a.k, (const __nv_bfloat16*)a.v,
+                                  a.g, a.beta, (__nv_bfloat16*)a.W, (__nv_bfloat16*)a.Qh, (__nv_bfloat16*)a.Kt,
+                                  (__nv_bfloat16*)a.A, (__nv_bfloat16*)a.U, a.gC, static_cast<int>(a.L), a.H, a.scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+template <int DK, int DV>
+int launch_bwd(const GdrIntraBwdArgs& a, cudaStream_t st) {
+  const size_t sm = sizeof(BwdSmem<DK, DV>);
+  auto kern = intra_bwd_kernel<DK, DV>;
+  cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
+  dim3 grid(static_cast<unsigned>(a.f.L / C), a.f.H, static_cast<unsigned>(a.f.B));
+  kern<<<grid, THREADS, sm, st>>>((const __nv_bfloat16*)a.f.q, (const __nv_bfloat16*)a.f.k,
+                                  (const __nv_bfloat16*)a.f.v, a.f.g, a.f.beta, a.dW, a.dQh, a.dKt, a.dA,
+                                  (const __nv_bfloat16*)a.dU, a.dgC, (__nv_bfloat16*)a.dq, (__nv_bfloat16*)a.dk,
+                                  (__nv_bfloat16*)a.dv, a.dg, a.dbeta, static_cast<int>(a.f.L), a.f.H, a.f.scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+}  // namespace
+
+int gdr_intra_fwd(const GdrIntraArgs& a, cudaStream_t st) {
+  if (a.L % C) return 5;
+  if (a.DK == 256 && a.DV == 256) return launch_fwd<256, 256>(a, st);
+  if (a.DK == 128 && a.DV == 128) return launch_fwd<128, 128>(a, st);
+  if (a.DK == 128 && a.DV == 256) return launch_fwd<128, 256>(a, st);
+  return 5;
+}
+
+int gdr_intra_bwd(const GdrIntraBwdArgs& a, cudaStream_t st) {
+  if (a.f.L % C) return 5;
+  if (a.f.DK == 256 && a.f.DV == 256) return launch_bwd<256, 256>(a, st);
+  if (a.f.DK == 128 && a.f.DV == 128) return launch_bwd<128, 128>(a, st);
+  if (a.f.DK == 128 && a.f.DV == 256) return launch_bwd<128, 256>(a, st);
+  return 5;
+}
+
+}  // namespace vagus

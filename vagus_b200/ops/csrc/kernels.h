@@ -77,6 +77,26 @@ struct GdrRecBwdArgs {
   float* dS0;                                      // (BH, DK, DV) or null
 };
 int gdr_rec_bwd(const GdrRecBwdArgs& a, cudaStream_t st);
+// gdr_intra.cu: intra-chunk WY / UT stage (scalar gate), forward + backward.
+struct GdrIntraArgs {
+  const void* q; const void* k; const void* v;   // (B, L, H, DK|DV) bf16 token-major
+  const float* g; const float* beta;            // (B, L, H)
+  void* W; void* Qh; void* Kt;                  // (B*H, N, C, DK) bf16
+  void* A;                                      // (B*H, N, C, C) bf16
+  void* U;                                      // (B*H, N, C, DV) bf16
+  float* gC;                                    // (B*H, N)
+  long long B, L; int H, DK, DV;
+  float scale;
+};
+int gdr_intra_fwd(const GdrIntraArgs& a, cudaStream_t st);
+struct GdrIntraBwdArgs {
+  GdrIntraArgs f;                               // forward inputs (outputs unused)
+  const float* dW; const float* dQh; const float* dKt; const float* dA;   // from gdr_rec_bwd
+  const void* dU; const float* dgC;
+  void* dq; void* dk; void* dv;                 // (B, L, H, DK|DV) bf16
+  float* dg; float* dbeta;                      // (B, L, H) fp32
+};
+int gdr_intra_bwd(const GdrIntraBwdArgs& a, cudaStream_t st);
 int gdr_decode(const void* q, const void* k, const void* v, const float* g, const float* beta, float* S, void* o,
                long long BH, int dk, int dv, float scale, cudaStream_t st);
 

@@ -1,11 +1,11 @@
 """Gated delta-rule ops on CUDA.
 
-``gdr_chunk``   the chunked scan (scalar gate): the intra-chunk WY algebra
-                (per-chunk 64 x 64 products and the unit-lower-triangular
-                solve) builds W, U, Qh, Kt, A and gC; the sm_100a recurrence
-                kernel (gdr.cu) runs the inter-chunk state scan forward and
-                the reverse scan backward; the intra-chunk stage is
-                differentiated by recomputing it under autograd in backward.
+``gdr_chunk``   the chunked scan (scalar gate): the intra-chunk kernel
+                (gdr_intra.cu) builds W, U, Qh, Kt, A and gC per 64-token
+                chunk, the recurrence kernel (gdr.cu) runs the inter-chunk
+                state scan; backward runs the reverse scan and then the
+                intra-chunk derivative kernel.  ``_intra`` below is the same
+                intra-chunk algebra in PyTorch (the tests' oracle).
 ``gdr_decode``  single-token recurrent step (state updated in place).
 ``gdn_mixer``   one Gated DeltaNet layer up to the input of ``wo`` as a single
                 autograd node: packed q|k|v|g GEMM, packed a|b GEMM, fused
@@ -64,10 +64,10 @@ def _gdr_fwd(q, k, v, g, beta, S0, scale):
     B, L, H, dk = q.shape
     dv = v.shape[-1]
     N = L // CHUNK
-    with torch.no_grad():
-        W, Qh, Kt, A, U, gC = _intra(q, k, v, g, beta, scale)
-    ops16 = [_flat(t).to(torch.bfloat16).contiguous() for t in (W, Qh, Kt, A, U)]
-    gCf = _flat(gC).contiguous()
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    g, beta = g.float().contiguous(), beta.float().contiguous()
+    W, Qh, Kt, A, U, gCf = native().gdr_intra_fwd(q, k, v, g, beta, scale)
+    ops16 = [W, Qh, Kt, A, U]
     S0f = None if S0 is None else S0.float().reshape(B * H, dk, dv).contiguous()
     O, Vp, states, S_out = native().gdr_rec_fwd(*ops16, gCf, S0f, True)
     o = O.view(B, H, N, CHUNK, dv).permute(0, 2, 3, 1, 4).reshape(B, L, H, dv)
@@ -85,15 +85,7 @@ def _gdr_bwd(saved, do, dS, scale, need_dS0):
     dSf = None if dS is None else dS.float().reshape(B * H, dk, dv).contiguous()
     dW, dQh, dKt, dA, dU, dgC, dS0 = native().gdr_rec_bwd(W16, Qh16, Kt16, A16, Vp, gCf, states,
                                                           dO.contiguous(), dSf, need_dS0)
-    with torch.enable_grad():
-        leaves = [t.detach().requires_grad_(True) for t in (q, k, v, g, beta)]
-        outs = _intra(*leaves, scale)
-
-    def shp(t):
-        return t.view(B, H, *t.shape[1:])
-
-    grads = [shp(dW), shp(dQh), shp(dKt), shp(dA), shp(dU).float(), dgC.view(B, H, N)]
-    gq, gk, gv, gg, gb = torch.autograd.grad(outs, leaves, grads, allow_unused=True)
+    gq, gk, gv, gg, gb = native().gdr_intra_bwd(q, k, v, g, beta, dW, dQh, dKt, dA, dU, dgC, scale)
     return gq, gk, gv, gg, gb, (dS0.view(B, H, dk, dv) if need_dS0 else None)
 
 
