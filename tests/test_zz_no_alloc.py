@@ -1,0 +1,66 @@
+# The allocation-free fused linear cross-entropy entry point, called through
+# its exported C symbol the way a caller that cannot allocate would (for
+# example code inside a captured CUDA graph region, or a host runtime whose
+# own allocator owns the device): every buffer is supplied by the caller and
+# the routine's own working memory is a fixed device array inside the
+# library.  Checked against the regular fused_linear_ce op on two calls in a
+# row (the second call must not see stale accumulators from the first).
+# The file name sorts last so a run that stops at the first failure has
+# already run every other test.
+import ctypes
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _lib():
+    from vagus_b200.ops import build, native
+    native()                                   # loads (or builds) the extension
+    lib = ctypes.CDLL(str(build.BUILD_DIR / f"{build.NAME}.so"))
+    fn = lib.vagus_fused_linear_ce_noalloc
+    fn.restype = ctypes.c_int
+    fn.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_longlong, ctypes.c_int, ctypes.c_int,
+                   ctypes.c_float, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p]
+    err = lib.vagus_noalloc_error_string
+    err.restype = ctypes.c_char_p
+    err.argtypes = [ctypes.c_int]
+    return fn, err
+
+
+def test_noalloc_ce_matches_fused_op_twice():
+    from vagus_b200 import ops
+    fn, err = _lib()
+    torch.manual_seed(0)
+    N, D, V, z = 1000, 256, 4096, 1e-3
+    h = torch.randn(N, D, device="cuda").bfloat16()
+    w32 = 0.05 * torch.randn(V, D, device="cuda")
+    t = torch.randint(0, V, (N,), device="cuda")
+    # regular entry point (allocates its own logits chunk)
+    hr = h.clone().requires_grad_(True)
+    wr = w32.clone().requires_grad_(True)
+    loss_ref, z_ref = ops.fused_linear_ce(hr, wr, t, z_loss=z)
+    loss_ref.backward()
+    w16 = w32.bfloat16().contiguous()
+    stream = torch.cuda.current_stream().cuda_stream
+    for _ in range(2):
+        loss = torch.zeros(2, device="cuda")
+        dh = torch.empty(N, D, device="cuda", dtype=torch.bfloat16)
+        dW = torch.zeros(V, D, device="cuda")
+        rc = fn(h.data_ptr(), w16.data_ptr(), t.data_ptr(), N, D, V, z, loss.data_ptr(), dh.data_ptr(),
+                dW.data_ptr(), stream)
+        assert rc == 0, err(rc).decode()
+        torch.cuda.synchronize()
+        assert abs(loss[0].item() - loss_ref.item()) < 2e-3 * max(1.0, abs(loss_ref.item()))
+        assert abs(loss[1].item() - z_ref.item()) < 1e-3
+        rel_h = ((dh.float() - hr.grad.float()).norm() / hr.grad.float().norm()).item()
+        rel_w = ((dW - wr.grad).norm() / wr.grad.norm()).item()
+        assert rel_h < 3e-2 and rel_w < 3e-2, (rel_h, rel_w)
+
+
+def test_noalloc_ce_rejects_oversized_vocab():
+    fn, err = _lib()
+    N, D, V = 256, 64, 1 << 20                # 128 rows x 2 MiB of logits exceed the scratch array
+    rc = fn(1, 1, 1, N, D, V, 0.0, 1, 1, 1, None)   # rejected before any pointer is touched
+    assert rc == -2 and b"too large" in err(rc)
