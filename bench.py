@@ -48,7 +48,7 @@ CONFIGS = {
         model_args=dict(vocab_size=32000, dim=1024, layer_count=24, head_count=4, key_head_dim=256,
                         value_head_dim=256, ffn_hidden_dim=2816, short_conv_size=4, gate="scalar", delta=True,
                         chunk_size=64, context_len=4096, la_impl="auto"),
-        seq=4096, global_tokens=524288, micro=4, label="340M GDN (4x256, chunk 64), FSDP2+Muon"),
+        seq=4096, global_tokens=524288, micro=8, label="340M GDN (4x256, chunk 64), FSDP2+Muon"),
     # BASELINE config #5
     "hybrid1.3b": dict(
         model_name="GDNLM",
@@ -200,7 +200,7 @@ def run(args) -> dict:
                                 timeout=datetime.timedelta(seconds=600))
     dev = torch.device(f"cuda:{local}")
     torch.manual_seed(0)
-    seq, micro = cfg["seq"], cfg["micro"]
+    seq, micro = cfg["seq"], (args.micro or cfg["micro"])
     per_rank_seqs = cfg["global_tokens"] // seq // world
     micro = min(micro, per_rank_seqs)
     accum = per_rank_seqs // micro
@@ -344,6 +344,7 @@ def run(args) -> dict:
                 "d2h_bytes_per_step": 4},
         "gpu_launches": None if launches is None else launches * args.steps,
         "clocks": clocks, "final_loss": round(final_loss, 4), "warmup_s": round(warm_s, 1),
+        "max_mem_gb": round(torch.cuda.max_memory_allocated() / 1e9, 1),
     }
     if args.impl == "reference":
         out["impl"] = "reference"
@@ -360,6 +361,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gdn340m")
+    ap.add_argument("--micro", type=int, default=0, help="sequences per micro-batch (0: the config's default)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -1,0 +1,128 @@
+"""Microbenchmarks of the native kernels on the shapes of the 340M GDN layer.
+
+    python -m vagus_b200.meter.kernels [case ...] [--B 8] [--L 4096] [--iters 20] [--warmup 5]
+
+Every case is timed with CUDA events after warm-up, with a 256 MB L2 flush
+before each timed iteration (``meter.core.bench``), and printed as one line:
+time, the algorithmic bytes or FLOPs of one launch, and the fraction of the
+measured peak (``MEASURED_PEAKS.json`` at the repository root: STREAM-style
+copy bandwidth and the cuBLAS bf16 GEMM rate).  Inputs are random; the
+shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
+of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
+conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
+gdr_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
+case runs.
+
+Used for the committed ncu summaries: run one case with few iterations under
+``ncu -k regex:<kernel> -c 1``.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+from pathlib import Path
+
+import torch
+
+from .core import bench
+
+ROOT = Path(__file__).resolve().parents[2]
+
+
+def _peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"], "src": "of measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "src": "of fallback"}
+
+
+def _cases(B: int, L: int):
+    from ..ops import native
+    C = native()
+    dev = torch.device("cuda")
+    D, hd, H = 1024, 256, 4
+    T = B * L
+    NP = 4 * D + 2 * H + 56          # packed q,k,v,g + a,b, padded to a multiple of 64
+    bf = torch.bfloat16
+    r = lambda *s, dt=bf: torch.randn(*s, device=dev).to(dt)   # noqa: E731
+    cases = {}
+
+    P = r(B, L, NP)
+    x = P[:, :, :D]
+    w = 0.3 * torch.randn(D, 1, 4, device=dev)
+    y, rn = C.conv_silu_fwd(x, w, hd, True)
+    dy = r(B, L, D)
+    dP = torch.empty_like(P)
+    dw = torch.zeros(D * 4, device=dev)
+    mb = T * D * 2
+    cases["conv_fwd"] = (lambda: C.conv_silu_fwd(x, w, hd, True), 2 * mb, None)
+    cases["conv_bwd"] = (lambda: C.conv_silu_bwd(dy, x, w, rn, dP[:, :, :D], dw, hd, True), 3 * mb, None)
+
+    ab = P.reshape(T, NP)[:, 4 * D:4 * D + 2 * H]
+    A_log, dt_bias = torch.randn(H, device=dev), torch.randn(H, device=dev)
+    cases["gates"] = (lambda: C.gdn_gates_fwd(ab, A_log, dt_bias, H), T * 2 * H * (2 + 8), None)
+
+    BH = B * H
+    from ..ops.gdn import _gdr_fwd, _gdr_bwd
+    q = torch.nn.functional.normalize(torch.randn(B, L, H, hd, device=dev), dim=-1).to(bf)
+    k = torch.nn.functional.normalize(torch.randn(B, L, H, hd, device=dev), dim=-1).to(bf)
+    v = r(B, L, H, hd)
+    g = -torch.rand(B, L, H, device=dev) * 0.1
+    beta = torch.rand(B, L, H, device=dev)
+    scale = hd ** -0.5
+    nc = L // 64
+    # per chunk: K K^T, Q K^T, W = T(bGK), U = T(bV): 4 x 2*64*64*256; inverse ~64^3/3
+    intra = BH * nc * (4 * 2 * 64 * 64 * hd + 2 * 64 ** 3 // 3)
+    # per chunk: W S, Qh S, Kt^T V': 3 x 2*64*256*256, plus A V' (2*64*64*256)
+    rec = BH * nc * (3 * 2 * 64 * hd * hd + 2 * 64 * 64 * hd)
+    cases["gdr_intra_fwd"] = (lambda: C.gdr_intra_fwd(q, k, v, g, beta, scale), None, intra)
+    cases["gdr_fwd"] = (lambda: _gdr_fwd(q, k, v, g, beta, None, scale), None, intra + rec)
+    o, _, saved = _gdr_fwd(q, k, v, g, beta, None, scale)
+    do = torch.randn_like(o)
+    cases["gdr_bwd"] = (lambda: _gdr_bwd(saved, do, None, scale, False), None, 2 * (intra + rec))
+
+    from ..ops._core import gemm
+    a = r(T, D)
+    wpk = r(NP, D)
+    c = torch.empty(T, NP, device=dev, dtype=bf)
+    gp = r(T, NP)
+    da = torch.empty(T, D, device=dev, dtype=bf)
+    dwp = torch.zeros(NP, D, device=dev)
+    fl = 2 * T * D * NP
+    cases["gemm_fwd"] = (lambda: gemm(a, False, wpk, False, c), None, fl)            # x W^T
+    cases["gemm_dgrad"] = (lambda: gemm(gp, False, wpk, True, da), None, fl)         # dy W
+    cases["gemm_wgrad"] = (lambda: gemm(gp, True, a, True, dwp, atomic=True), None, fl)  # dW += dy^T x
+
+    xs = r(T, D)
+    gamma = torch.ones(D, device=dev)
+    cases["rmsnorm"] = (lambda: C.rmsnorm_fwd(xs, gamma, 1e-6, False), 2 * T * D * 2, None)
+    return cases
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("case", nargs="*")
+    ap.add_argument("--B", type=int, default=8)
+    ap.add_argument("--L", type=int, default=4096)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    a = ap.parse_args(argv)
+    peaks = _peaks()
+    cases = _cases(a.B, a.L)
+    names = a.case or list(cases)
+    for n in names:
+        fn, nbytes, flops = cases[n]
+        res = bench(fn, name=n, device=torch.device("cuda"), warmup=a.warmup, iters=a.iters)
+        us = res.mean_ms * 1e3
+        if nbytes:
+            gbs = nbytes / us / 1e3
+            print(f"{n:14s} {us:9.1f} us  {gbs:7.0f} GB/s  {gbs / peaks['hbm_gbs']:.2f} {peaks['src']} HBM")
+        else:
+            tf = flops / us / 1e6
+            print(f"{n:14s} {us:9.1f} us  {tf:7.0f} TF/s  {tf / peaks['tflops']:.2f} {peaks['src']} bf16")
+
+
+if __name__ == "__main__":
+    main()

@@ -4,25 +4,36 @@
 //   u[t, c] = sum_{i<K} w[c, K-1-i] x[t-i, c]     (zeros before the start)
 //   z = silu(u);   y = z * rsqrt(sum_head z^2 + 1e-6)   (l2norm) or y = z
 //
-// One warp owns a strip of TPW consecutive tokens of one head; each lane owns
-// VEC = head_dim / 32 adjacent channels (16-byte vector loads for head_dim
-// 256) and slides along the strip keeping the last K inputs in registers.
-// The head norm is a warp reduction (shuffles only).  The input may be a
-// column block of a wider packed matrix (row pitch ldx); dx is written with
-// its own pitch into the packed gradient.  Weight gradients are reduced over
-// the 8 warps of a CTA in shared memory, then one atomic per (channel, tap).
+// Tiling: a CTA (8 warps) owns a tile of T consecutive tokens of one head.
+// The tile's input rows (plus K - 1 rows of left context, and in the backward
+// K - 1 rows of right context) are staged in shared memory with cp.async, so
+// every byte the tile needs is in flight at once without costing registers;
+// then each warp takes whole token rows, one lane per VEC = head_dim / 32
+// adjacent channels, and the head norm is a warp reduction.  The input may be
+// a column block of a wider packed matrix (row pitch ldx); dx is written with
+// its own pitch into the packed gradient.
+//
+// Backward: phase 1 recomputes u, z and forms du = dL/du for T + K - 1 rows
+// into shared memory (fp32); phase 2 gives dx[t] = sum_i w[K-1-i] du[t+i] and
+// accumulates dw in registers.  Backward CTAs are persistent over the tiles of
+// their (batch, head), so dw is reduced over warps in shared memory and added
+// with one atomic per (channel, tap) per CTA.
 #include "common.cuh"
 #include "kernels.h"
+
+#include <algorithm>
 
 namespace vagus {
 namespace {
 
-constexpr int TPW = 16;      // tokens per warp strip
 constexpr int WARPS = 8;
-constexpr int MAXK = 4;      // taps supported by the register window
+constexpr int THREADS = WARPS * 32;
+constexpr int MAXK = 4;       // taps supported by the register window
+constexpr int TF = 64;        // forward tile (tokens)
+constexpr int TB = 32;        // backward tile (tokens)
 
 template <int VEC>
-__device__ __forceinline__ void load_vec(const __nv_bfloat16* p, float (&v)[VEC]) {
+__device__ __forceinline__ void lds_vec(const __nv_bfloat16* p, float (&v)[VEC]) {
   if constexpr (VEC == 8) {
     const uint4 t = *reinterpret_cast<const uint4*>(p);
     const uint32_t w[4] = {t.x, t.y, t.z, t.w};
@@ -32,9 +43,11 @@ __device__ __forceinline__ void load_vec(const __nv_bfloat16* p, float (&v)[VEC]
     const uint2 t = *reinterpret_cast<const uint2*>(p);
     float2 f = unpack_bf16x2(t.x); v[0] = f.x; v[1] = f.y;
     f = unpack_bf16x2(t.y); v[2] = f.x; v[3] = f.y;
+  } else if constexpr (VEC == 2) {
+    const float2 f = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(p));
+    v[0] = f.x; v[1] = f.y;
   } else {
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) v[j] = bf2f(p[j]);
+    v[0] = bf2f(p[0]);
   }
 }
 
@@ -47,178 +60,318 @@ __device__ __forceinline__ void store_vec(__nv_bfloat16* p, const float (&v)[VEC
     *reinterpret_cast<uint4*>(p) = t;
   } else if constexpr (VEC == 4) {
     *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]));
+  } else if constexpr (VEC == 2) {
+    *reinterpret_cast<uint32_t*>(p) = pack_bf16x2(v[0], v[1]);
   } else {
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) p[j] = f2bf(v[j]);
+    p[0] = f2bf(v[0]);
+  }
+}
+
+// 16-byte global -> shared copy; reads nothing and writes zeros when !ok.
+__device__ __forceinline__ void cp16(void* s, const void* g, bool ok) {
+  const uint32_t sa = static_cast<uint32_t>(__cvta_generic_to_shared(s));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(sa), "l"(g), "r"(ok ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_commit_wait() {
+  asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
+}
+
+// rows [t_first, t_first + rows) of one head (HD channels) into s[row][HD];
+// rows outside [0, L) are zero.
+template <int HD>
+__device__ __forceinline__ void stage_rows(__nv_bfloat16* s, const __nv_bfloat16* g, long long pitch, long long b,
+                                           long long L, long long t_first, int rows, int c_base) {
+  constexpr int CPR = HD / 8;
+  for (int i = threadIdx.x; i < rows * CPR; i += THREADS) {
+    const int r = i / CPR, cc = i - r * CPR;
+    const long long t = t_first + r;
+    const bool ok = t >= 0 && t < L;
+    cp16(s + r * HD + cc * 8, g + (b * L + (ok ? t : 0)) * pitch + c_base + cc * 8, ok);
+  }
+}
+
+// The head's taps, transposed into shared memory as ws[tap][channel]: thread
+// c loads channel c's K taps (one coalesced 16-byte load per thread) and a
+// lane then reads its VEC channels of each tap as contiguous vectors.
+// Loading them per lane straight from global memory costs one 32-sector
+// request per tap per warp.
+template <int HD, int K>
+__device__ __forceinline__ void stage_weights(float* ws, const float* __restrict__ w, int c_base) {
+  static_assert(K == 4 && HD <= THREADS, "one float4 of taps per channel");
+  if (threadIdx.x < HD) {
+    const float4 v = *reinterpret_cast<const float4*>(w + (long long)(c_base + threadIdx.x) * K);
+    ws[0 * HD + threadIdx.x] = v.x;
+    ws[1 * HD + threadIdx.x] = v.y;
+    ws[2 * HD + threadIdx.x] = v.z;
+    ws[3 * HD + threadIdx.x] = v.w;
   }
 }
 
 template <int VEC, int K>
-__global__ void __launch_bounds__(WARPS * 32)
+__device__ __forceinline__ void read_weights(const float* ws, int cl, float (&wr)[K][VEC]) {
+  constexpr int HD = VEC * 32;
+#pragma unroll
+  for (int i = 0; i < K; ++i)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) wr[i][j] = ws[i * HD + cl + j];
+}
+
+template <int VEC, int K>
+__global__ void __launch_bounds__(THREADS, 2)
 conv_fwd_k(const __nv_bfloat16* __restrict__ x, long long ldx, const float* __restrict__ w,
            __nv_bfloat16* __restrict__ y, float* __restrict__ rnorm, long long L, int D, int l2) {
+  constexpr int HD = VEC * 32;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* ws = reinterpret_cast<float*>(smem_raw);                     // [HD][K]
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ws + HD * K);  // [TF + K - 1][HD]
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const long long b = blockIdx.z;
   const int head = blockIdx.y;
-  const int hd = VEC * 32;
-  const int c0 = head * hd + lane * VEC;
-  const long long t0 = ((long long)blockIdx.x * WARPS + warp) * TPW;
-  if (t0 >= L) return;
+  const int nH = D / HD;
+  const long long t0 = (long long)blockIdx.x * TF;
+  stage_weights<HD, K>(ws, w, head * HD);
+  stage_rows<HD>(xs, x, ldx, b, L, t0 - (K - 1), TF + K - 1, head * HD);
+  cp_commit_wait();
+  __syncthreads();
   float wr[K][VEC];
+  read_weights<VEC, K>(ws, lane * VEC, wr);
+  // each warp walks RW consecutive tokens with the last K - 1 inputs kept
+  // unpacked in registers: one shared load per token
+  constexpr int RW = TF / WARPS;
+  const int r0 = warp * RW;
+  float win[K - 1][VEC];                    // win[i] = x[t - 1 - i]; token t0 + r is tile row r + K - 1
 #pragma unroll
-  for (int j = 0; j < VEC; ++j)
+  for (int i = 0; i < K - 1; ++i) lds_vec<VEC>(xs + (r0 + K - 2 - i) * HD + lane * VEC, win[i]);
 #pragma unroll
-    for (int i = 0; i < K; ++i) wr[i][j] = w[(long long)(c0 + j) * K + i];
-  float hist[K][VEC];            // before token t is shifted in: hist[i] = x[t - 1 - i]
-#pragma unroll
-  for (int i = 0; i < K; ++i) {
-    const long long t = t0 - 1 - i;
-    if (t >= 0) load_vec<VEC>(x + (b * L + t) * ldx + c0, hist[i]);
-    else
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) hist[i][j] = 0.f;
-  }
-  const int nH = D / hd;
-  const long long t_end = min(L, t0 + TPW);
-  for (long long t = t0; t < t_end; ++t) {
-#pragma unroll
-    for (int i = K - 1; i > 0; --i)
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) hist[i][j] = hist[i - 1][j];
-    load_vec<VEC>(x + (b * L + t) * ldx + c0, hist[0]);
-    float z[VEC];
-    float ss = 0.f;
+  for (int rr = 0; rr < RW; ++rr) {
+    const int r = r0 + rr;
+    float xc[VEC], u[VEC];
+    lds_vec<VEC>(xs + (r + K - 1) * HD + lane * VEC, xc);
 #pragma unroll
     for (int j = 0; j < VEC; ++j) {
-      float u = 0.f;
+      u[j] = wr[K - 1][j] * xc[j];
 #pragma unroll
-      for (int i = 0; i < K; ++i) u += wr[K - 1 - i][j] * hist[i][j];
-      z[j] = silu_f(u);
-      ss += z[j] * z[j];
+      for (int i = 0; i < K - 1; ++i) u[j] += wr[K - 2 - i][j] * win[i][j];
     }
-    if (l2) {
-      const float r = rsqrtf(warp_sum(ss) + 1e-6f);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) z[j] *= r;
-      if (lane == 0) rnorm[(b * L + t) * nH + head] = r;
+    for (int i = K - 2; i > 0; --i)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) win[i][j] = win[i - 1][j];
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) win[0][j] = xc[j];
+    const long long t = t0 + r;
+    if (t < L) {                            // warp-uniform
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) { u[j] = silu_f(u[j]); ss += u[j] * u[j]; }
+      if (l2) {
+        const float rn = rsqrtf(warp_sum(ss) + 1e-6f);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) u[j] *= rn;
+        if (lane == 0) rnorm[(b * L + t) * nH + head] = rn;
+      }
+      store_vec<VEC>(y + (b * L + t) * D + head * HD + lane * VEC, u);
     }
-    store_vec<VEC>(y + (b * L + t) * D + c0, z);
   }
 }
 
 template <int VEC, int K>
-__global__ void __launch_bounds__(WARPS * 32)
+constexpr int bwd_smem_bytes() {
+  constexpr int HD = VEC * 32;
+  return HD * K * 4 + (TB + 2 * (K - 1)) * HD * 2 + (TB + K - 1) * HD * 2 + (TB + K - 1) * HD * 4;
+}
+
+template <int VEC, int K>
+__global__ void __launch_bounds__(THREADS, 2)
 conv_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
            const float* __restrict__ w, const float* __restrict__ rnorm, __nv_bfloat16* __restrict__ dx,
            long long lddx, float* __restrict__ dw, long long L, int D, int l2) {
-  __shared__ float sdw[WARPS][VEC * 32 * K];
+  constexpr int HD = VEC * 32;
+  constexpr int XR = TB + 2 * (K - 1);      // x rows: tokens [t0 - K + 1, t0 + TB + K - 1)
+  constexpr int GR = TB + K - 1;            // dy / du rows: tokens [t0, t0 + TB + K - 1)
+  static_assert(WARPS * K <= GR, "dw reduction reuses the du buffer");
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* ws = reinterpret_cast<float*>(smem_raw);
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(ws + HD * K);
+  __nv_bfloat16* gs = xs + XR * HD;
+  float* dus = reinterpret_cast<float*>(gs + GR * HD);
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const long long b = blockIdx.z;
   const int head = blockIdx.y;
-  const int hd = VEC * 32;
-  const int c0 = head * hd + lane * VEC;
-  const long long t0 = ((long long)blockIdx.x * WARPS + warp) * TPW;
-  const int nH = D / hd;
-  float wr[K][VEC];
-#pragma unroll
-  for (int j = 0; j < VEC; ++j)
-#pragma unroll
-    for (int i = 0; i < K; ++i) wr[i][j] = w[(long long)(c0 + j) * K + i];
-  float dwp[K][VEC];
-#pragma unroll
-  for (int i = 0; i < K; ++i)
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) dwp[i][j] = 0.f;
-  if (t0 < L) {
-    float xh[K][VEC];            // before token t is shifted in: xh[i] = x[t - 1 - i]
-#pragma unroll
-    for (int i = 0; i < K; ++i) {
-      const long long t = t0 - 1 - i;
-      if (t >= 0) load_vec<VEC>(x + (b * L + t) * ldx + c0, xh[i]);
-      else
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) xh[i][j] = 0.f;
-    }
-    float acc[K][VEC];           // acc[i] = pending dx of token t - i
-#pragma unroll
-    for (int i = 0; i < K; ++i)
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) acc[i][j] = 0.f;
-    const long long t_stop = min(L, t0 + TPW + K - 1);   // extra tokens feed dx of the strip's tail
-    for (long long t = t0; t < t_stop; ++t) {
-#pragma unroll
-      for (int i = K - 1; i > 0; --i)
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) { xh[i][j] = xh[i - 1][j]; acc[i][j] = acc[i - 1][j]; }
-      load_vec<VEC>(x + (b * L + t) * ldx + c0, xh[0]);
-      float g[VEC], u[VEC], s[VEC], z[VEC];
-      load_vec<VEC>(dy + (b * L + t) * D + c0, g);
-      float dot = 0.f;
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        u[j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < K; ++i) u[j] += wr[K - 1 - i][j] * xh[i][j];
-        s[j] = sigmoid_f(u[j]);
-        z[j] = u[j] * s[j];
-        dot += g[j] * z[j];
-      }
-      if (l2) {
-        const float r = rnorm[(b * L + t) * nH + head];
-        dot = warp_sum(dot);
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) g[j] = r * g[j] - r * r * r * z[j] * dot;
-      }
-      const bool in_strip = t < t0 + TPW;
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        const float du = g[j] * s[j] * (1.f + u[j] * (1.f - s[j]));
-        acc[0][j] = 0.f;
-#pragma unroll
-        for (int i = 0; i < K; ++i) acc[i][j] += wr[K - 1 - i][j] * du;
-        if (in_strip)
-#pragma unroll
-          for (int i = 0; i < K; ++i) dwp[K - 1 - i][j] += du * xh[i][j];
-      }
-      const long long td = t - (K - 1);
-      if (td >= t0 && td < t0 + TPW) store_vec<VEC>(dx + (b * L + td) * lddx + c0, acc[K - 1]);
-    }
-    // the strip's last K-1 tokens when the sequence ends inside the window
-#pragma unroll
-    for (int i = 0; i < K - 1; ++i) {
-      const long long td = t_stop - 1 - i;
-      if (t_stop == L && td >= t0 && td < t0 + TPW && td > t_stop - K) store_vec<VEC>(dx + (b * L + td) * lddx + c0, acc[i]);
-    }
-  }
-  // reduce dw over the CTA's warps, then one atomic per (channel, tap)
-#pragma unroll
-  for (int i = 0; i < K; ++i)
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) sdw[warp][(lane * VEC + j) * K + i] = dwp[i][j];
+  const int nH = D / HD;
+  const int cl = lane * VEC;                  // lane's first channel within the head
+  stage_weights<HD, K>(ws, w, head * HD);
+  cp_commit_wait();
   __syncthreads();
-  for (int e = threadIdx.x; e < hd * K; e += WARPS * 32) {
+  float wr[K][VEC];
+  read_weights<VEC, K>(ws, cl, wr);
+  float dwa[K][VEC];
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) dwa[k][j] = 0.f;
+  constexpr int RW = TB / WARPS;
+  static_assert(TB % WARPS == 0 && K - 1 <= WARPS, "tile split");
+  const int r0 = warp * RW;
+  float win[K - 1][VEC];
+  // du rows in shared memory: float4 groups interleaved across lanes so a
+  // warp's 16-byte accesses are conflict-free
+  auto du_at = [&](int r, int j) -> float* {
+    if constexpr (VEC >= 4) return dus + r * HD + (j / 4) * 128 + lane * 4 + (j % 4);
+    else return dus + r * HD + cl + j;
+  };
+  auto du_load = [&](int r, float (&v)[VEC]) {
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) v[j] = *du_at(r, j);
+  };
+  long long t0 = 0;
+  auto du_row = [&](int r, float (&u)[VEC]) {
+    const long long t = t0 + r;
+    float g[VEC], s[VEC], z[VEC];
+    lds_vec<VEC>(gs + r * HD + cl, g);
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) {
+      s[j] = sigmoid_f(u[j]);
+      z[j] = u[j] * s[j];
+      dot += g[j] * z[j];
+    }
+    if (l2) {
+      const float rn = t < L ? rnorm[(b * L + t) * nH + head] : 0.f;
+      dot = warp_sum(dot);
+      const float c3 = rn * rn * rn * dot;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) g[j] = rn * g[j] - c3 * z[j];
+    }
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) *du_at(r, j) = g[j] * s[j] * (1.f + u[j] * (1.f - s[j]));
+  };
+  const long long tiles = (L + TB - 1) / TB;
+  for (long long tile = blockIdx.x; tile < tiles; tile += gridDim.x) {
+    t0 = tile * TB;
+    stage_rows<HD>(xs, x, ldx, b, L, t0 - (K - 1), XR, head * HD);
+    stage_rows<HD>(gs, dy, D, b, L, t0, GR, head * HD);
+    cp_commit_wait();
+    __syncthreads();
+    // phase 1: du for tokens t0 + r, r < GR (zero past the end: dy is zero
+    // there).  Rows 0 .. TB-1 in runs of RW per warp with a sliding input
+    // window; the K - 1 right-context rows go to the first warps.
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) lds_vec<VEC>(xs + (r0 + K - 2 - i) * HD + cl, win[i]);
+#pragma unroll
+    for (int rr = 0; rr < RW; ++rr) {
+      const int r = r0 + rr;
+      float xc[VEC], u[VEC];
+      lds_vec<VEC>(xs + (r + K - 1) * HD + cl, xc);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        u[j] = wr[K - 1][j] * xc[j];
+#pragma unroll
+        for (int i = 0; i < K - 1; ++i) u[j] += wr[K - 2 - i][j] * win[i][j];
+      }
+#pragma unroll
+      for (int i = K - 2; i > 0; --i)
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) win[i][j] = win[i - 1][j];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) win[0][j] = xc[j];
+      du_row(r, u);
+    }
+    if (warp < K - 1) {
+      const int r = TB + warp;
+      float u[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) u[j] = 0.f;
+#pragma unroll
+      for (int i = 0; i < K; ++i) {
+        float xv[VEC];
+        lds_vec<VEC>(xs + (r + K - 1 - i) * HD + cl, xv);
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) u[j] += wr[K - 1 - i][j] * xv[j];
+      }
+      du_row(r, u);
+    }
+    __syncthreads();
+    // phase 2: dx and dw for the tile's own tokens
+#pragma unroll
+    for (int rr = 0; rr < RW; ++rr) {
+      const int r = r0 + rr;
+      const long long t = t0 + r;
+      if (t < L) {
+        float acc[VEC], d0[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) acc[j] = 0.f;
+#pragma unroll
+        for (int i = 0; i < K; ++i) {           // du[t + i] weighted by w[K-1-i]
+          float dv[VEC];
+          du_load(r + i, dv);
+          if (i == 0)
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) d0[j] = dv[j];
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) acc[j] += wr[K - 1 - i][j] * dv[j];
+        }
+        store_vec<VEC>(dx + (b * L + t) * lddx + head * HD + cl, acc);
+#pragma unroll
+        for (int k = 0; k < K; ++k) {           // x[t - (K-1-k)] sits at x row r + k
+          float xv[VEC];
+          lds_vec<VEC>(xs + (r + k) * HD + cl, xv);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) dwa[k][j] += d0[j] * xv[j];
+        }
+      }
+    }
+    __syncthreads();
+  }
+  // reduce dw over the warps (reusing the du buffer), one atomic per (channel, tap)
+  float* red = dus;                           // [WARPS][K][HD]
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) red[(warp * K + k) * HD + cl + j] = dwa[k][j];
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < HD * K; idx += THREADS) {
+    const int c = idx / K, k = idx - c * K;
     float s = 0.f;
 #pragma unroll
-    for (int wi = 0; wi < WARPS; ++wi) s += sdw[wi][e];
-    atomicAdd(&dw[(long long)head * hd * K + e], s);
+    for (int q = 0; q < WARPS; ++q) s += red[(q * K + k) * HD + c];
+    atomicAdd(&dw[(long long)(head * HD + c) * K + k], s);
   }
 }
 
 template <int VEC, int K>
-void launch_fwd(const void* xp, long long ldx, const float* w, void* y, float* rnorm, long long B, long long L, int D,
-                int l2, cudaStream_t st) {
-  const int hd = VEC * 32;
-  dim3 grid(static_cast<unsigned>((L + WARPS * TPW - 1) / (WARPS * TPW)), D / hd, static_cast<unsigned>(B));
-  conv_fwd_k<VEC, K><<<grid, WARPS * 32, 0, st>>>((const __nv_bfloat16*)xp, ldx, w, (__nv_bfloat16*)y, rnorm, L, D, l2);
+int launch_fwd(const void* xp, long long ldx, const float* w, void* y, float* rnorm, long long B, long long L, int D,
+               int l2, cudaStream_t st) {
+  constexpr int HD = VEC * 32;
+  const int smem = HD * K * 4 + (TF + K - 1) * HD * 2;
+  dim3 grid(static_cast<unsigned>((L + TF - 1) / TF), D / HD, static_cast<unsigned>(B));
+  conv_fwd_k<VEC, K><<<grid, THREADS, smem, st>>>((const __nv_bfloat16*)xp, ldx, w, (__nv_bfloat16*)y, rnorm, L, D,
+                                                  l2);
+  return 0;
 }
 
 template <int VEC, int K>
-void launch_bwd(const void* dy, const void* xp, long long ldx, const float* w, const float* rnorm, void* dx,
-                long long lddx, float* dw, long long B, long long L, int D, int l2, cudaStream_t st) {
-  const int hd = VEC * 32;
-  dim3 grid(static_cast<unsigned>((L + WARPS * TPW - 1) / (WARPS * TPW)), D / hd, static_cast<unsigned>(B));
-  conv_bwd_k<VEC, K><<<grid, WARPS * 32, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
-                                                   (__nv_bfloat16*)dx, lddx, dw, L, D, l2);
+int launch_bwd(const void* dy, const void* xp, long long ldx, const float* w, const float* rnorm, void* dx,
+               long long lddx, float* dw, long long B, long long L, int D, int l2, cudaStream_t st) {
+  constexpr int HD = VEC * 32;
+  constexpr int smem = bwd_smem_bytes<VEC, K>();
+  static bool attr_set[64] = {};   // the attribute is held per device context
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 3;
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(conv_bwd_k<VEC, K>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+      return 3;
+    attr_set[dev] = true;
+  }
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = (L + TB - 1) / TB;
+  const long long pairs = B * (D / HD);
+  const long long want = 2LL * sms / pairs;    // one wave of 2 CTAs per SM (no tail)
+  const long long bx = std::max<long long>(1, std::min<long long>(tiles, want));
+  dim3 grid(static_cast<unsigned>(bx), D / HD, static_cast<unsigned>(B));
+  conv_bwd_k<VEC, K><<<grid, THREADS, smem, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
+                                                  (__nv_bfloat16*)dx, lddx, dw, L, D, l2);
+  return 0;
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
@@ -227,26 +380,28 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 int conv_silu_fwd(const void* xp, long long ldx, const float* w, void* y, float* rnorm, long long B, long long L,
                   int D, int K, int head_dim, int l2norm, cudaStream_t st) {
-  if (K != MAXK || D % head_dim) return 5;
-  if (head_dim == 256 && aligned16(xp) && ldx % 8 == 0) launch_fwd<8, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
-  else if (head_dim == 128 && ldx % 4 == 0) launch_fwd<4, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
-  else if (head_dim == 64) launch_fwd<2, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
-  else if (head_dim == 32) launch_fwd<1, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
-  else return 5;
+  if (K != MAXK || D % head_dim || !aligned16(xp) || !aligned16(y) || !aligned16(w) || ldx % 8) return 5;
+  int rc = 5;
+  if (head_dim == 256) rc = launch_fwd<8, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
+  else if (head_dim == 128) rc = launch_fwd<4, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
+  else if (head_dim == 64) rc = launch_fwd<2, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
+  else if (head_dim == 32) rc = launch_fwd<1, 4>(xp, ldx, w, y, rnorm, B, L, D, l2norm, st);
+  if (rc) return rc;
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
 int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w, const float* rnorm, void* dx,
                   long long lddx, float* dw, long long B, long long L, int D, int K, int head_dim, int l2norm,
                   cudaStream_t st) {
-  if (K != MAXK || D % head_dim) return 5;
-  if (head_dim == 256 && aligned16(xp) && ldx % 8 == 0 && lddx % 8 == 0 && aligned16(dx))
-    launch_bwd<8, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
-  else if (head_dim == 128 && ldx % 4 == 0 && lddx % 4 == 0)
-    launch_bwd<4, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
-  else if (head_dim == 64) launch_bwd<2, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
-  else if (head_dim == 32) launch_bwd<1, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
-  else return 5;
+  if (K != MAXK || D % head_dim || !aligned16(xp) || !aligned16(dy) || !aligned16(dx) || !aligned16(w) || ldx % 8 ||
+      lddx % 8)
+    return 5;
+  int rc = 5;
+  if (head_dim == 256) rc = launch_bwd<8, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
+  else if (head_dim == 128) rc = launch_bwd<4, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
+  else if (head_dim == 64) rc = launch_bwd<2, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
+  else if (head_dim == 32) rc = launch_bwd<1, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
+  if (rc) return rc;
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
