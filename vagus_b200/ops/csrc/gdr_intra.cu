@@ -36,14 +36,18 @@ using namespace mma;
 constexpr int C = 64;
 constexpr int THREADS = 256;
 
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+// Q and V share one buffer: V is fetched (asynchronously, overlapping the
+// inverse) once Q has been consumed.  About 94 KB for dk = dv = 256, so two
+// CTAs fit on an SM.
 template <int DK, int DV>
 struct FwdSmem {
-  __nv_bfloat16 Q[C][DK + PAD];
+  __nv_bfloat16 QV[C][cmax(DK, DV) + PAD];
   __nv_bfloat16 K[C][DK + PAD];
-  __nv_bfloat16 V[C][DV + PAD];
   float M[C][C + 1];             // M, then T (in place)
   __nv_bfloat16 Tb[C][C + PAD];
-  float gam[C], beta[C];
+  float gam[C], beta[C], graw[C];
 };
 
 // inclusive prefix sum of g over the chunk (64 values) into gam; warp 0
@@ -60,19 +64,80 @@ __device__ __forceinline__ void chunk_cumsum(const float* g_in, float* gam) {
   gam[2 * lane] = s - b;
 }
 
-// T = (I + M)^{-1} in place, M strictly lower triangular (row stride C + 1)
+// T = (I + M)^{-1} in place, M strictly lower triangular (row stride C + 1),
+// blocked over 16 x 16 tiles so the whole CTA works in parallel with only a
+// handful of barriers:
+//   1. the four diagonal blocks X_bb = (I + M_bb)^{-1}: one warp per block,
+//      one lane per column, forward substitution with the column held in
+//      registers (the M rows are warp-wide broadcast reads); written in place;
+//   2. off-diagonal blocks by distance d = i - j = 1, 2, 3:
+//      X_ij = -X_ii (sum_{k=j}^{i-1} M_ik X_kj).
+//      The lower off-diagonal M blocks stay intact until the end (later
+//      distances still read them), so X_ij is parked transposed in the
+//      (all-zero) upper block (j, i), and the partial sum Y goes there first;
+//   3. the parked blocks move to their lower positions, the upper is zeroed.
+// Every product is fp32 on the CUDA cores (about 64 K multiply-adds in all).
+constexpr int TB16 = 16;
+
 __device__ __forceinline__ void tri_inverse_inplace(float (*M)[C + 1]) {
-  const int c = threadIdx.x >> 2, part = threadIdx.x & 3;
-  for (int i = 0; i < C; ++i) {
-    float s = 0.f;
-    if (c < i)
-      for (int j = c + part; j < i; j += 4) s += M[i][j] * ((j == c) ? 1.f : M[j][c]);
-    s += __shfl_xor_sync(0xffffffffu, s, 1);
-    s += __shfl_xor_sync(0xffffffffu, s, 2);
-    __syncthreads();                       // row i of M read by everyone
-    if (part == 0) M[i][c] = (c < i) ? -s : (c == i ? 1.f : 0.f);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (warp < 4 && lane < TB16) {
+    const int o = warp * TB16, c = lane;
+    float x[TB16];
+#pragma unroll
+    for (int i = 0; i < TB16; ++i) {
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < i; ++j) s += M[o + i][o + j] * x[j];
+      x[i] = (i == c) ? 1.f : -s;      // rows above c give s = 0 (x[j] = 0 there)
+    }
+    __syncwarp(0x0000ffffu);
+#pragma unroll
+    for (int i = 0; i < TB16; ++i) M[o + i][o + c] = x[i];
+  }
+  __syncthreads();
+  // thread -> element (r, cc) of a 16 x 16 block
+  const int r = (threadIdx.x >> 4) & 15, cc = threadIdx.x & 15;
+  for (int d = 1; d < 4; ++d) {
+    const int nblk = 4 - d;                   // blocks (t + d, t), t < nblk
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      if (t < nblk) {
+        const int i = t + d, j = t;
+        float y = 0.f;
+#pragma unroll
+        for (int u = 0; u < TB16; ++u) y += M[i * TB16 + r][j * TB16 + u] * M[j * TB16 + u][j * TB16 + cc];
+        for (int k = j + 1; k < i; ++k)       // X_kj parked at (j, k), transposed
+#pragma unroll
+          for (int u = 0; u < TB16; ++u) y += M[i * TB16 + r][k * TB16 + u] * M[j * TB16 + cc][k * TB16 + u];
+        M[j * TB16 + cc][i * TB16 + r] = y;   // Y parked transposed at (j, i)
+      }
+    }
+    __syncthreads();
+    float x[3];
+#pragma unroll
+    for (int t = 0; t < 3; ++t) {
+      x[t] = 0.f;
+      if (t < nblk) {
+        const int i = t + d, j = t;
+#pragma unroll
+        for (int u = 0; u < TB16; ++u) x[t] -= M[i * TB16 + r][i * TB16 + u] * M[j * TB16 + cc][i * TB16 + u];
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 3; ++t)
+      if (t < nblk) M[t * TB16 + cc][(t + d) * TB16 + r] = x[t];
     __syncthreads();
   }
+  for (int idx = threadIdx.x; idx < C * C; idx += THREADS) {
+    const int i = idx / C, j = idx % C;
+    if ((i >> 4) > (j >> 4)) {                // lower off-diagonal: take the parked value
+      M[i][j] = M[j][i];
+      M[j][i] = 0.f;
+    }
+  }
+  __syncthreads();
 }
 
 template <int DK, int DV>
@@ -91,17 +156,16 @@ intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   const long long tok0 = (long long)b * L + (long long)n * C;
   const int warp = threadIdx.x / 32;
 
-  load_tile(&sm.Q[0][0], DK + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  constexpr int QP = cmax(DK, DV) + PAD;
+  load_tile(&sm.QV[0][0], QP, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
   load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
-  load_tile(&sm.V[0][0], DV + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
   cp_commit();
-  __shared__ float graw[C];
   if (threadIdx.x < C) {
-    graw[threadIdx.x] = g[(tok0 + threadIdx.x) * H + h];
+    sm.graw[threadIdx.x] = g[(tok0 + threadIdx.x) * H + h];
     sm.beta[threadIdx.x] = beta[(tok0 + threadIdx.x) * H + h];
   }
   __syncthreads();
-  if (warp == 0) chunk_cumsum(graw, sm.gam);
+  if (warp == 0) chunk_cumsum(sm.graw, sm.gam);
   cp_wait_all();
   __syncthreads();
 
@@ -111,43 +175,77 @@ intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
     zero(kk);
     zero(qk);
     warp_mma<1, 4, false, false>(kk, &sm.K[0][0], DK + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
-    warp_mma<1, 4, false, false>(qk, &sm.Q[0][0], DK + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
+    warp_mma<1, 4, false, false>(qk, &sm.QV[0][0], QP, &sm.K[0][0], DK + PAD, m0, n0, DK);
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
-        const float d = (j <= i) ? __expf(sm.gam[i] - sm.gam[j]) : 0.f;
-        sm.M[i][j] = (j < i) ? sm.beta[i] * kk[0][nt][e] * d : 0.f;
-        Ao[(cidx * C + i) * C + j] = f2bf(scale * qk[0][nt][e] * d);
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);   // j even; (i, j), (i, j + 1)
+        const float d0 = (j <= i) ? __expf(sm.gam[i] - sm.gam[j]) : 0.f;
+        const float d1 = (j + 1 <= i) ? __expf(sm.gam[i] - sm.gam[j + 1]) : 0.f;
+        sm.M[i][j] = (j < i) ? sm.beta[i] * kk[0][nt][e] * d0 : 0.f;
+        sm.M[i][j + 1] = (j + 1 < i) ? sm.beta[i] * kk[0][nt][e + 1] * d1 : 0.f;
+        *reinterpret_cast<uint32_t*>(Ao + (cidx * C + i) * C + j) =
+            pack_bf16x2(scale * qk[0][nt][e] * d0, scale * qk[0][nt][e + 1] * d1);
       }
   }
+  // Qh, Kt out (Q and unscaled K are then free to be overwritten / rescaled)
+  const float glast = sm.gam[C - 1];
+  for (int idx = threadIdx.x; idx < C * (DK / 8); idx += THREADS) {
+    const int i = idx / (DK / 8), c = (idx % (DK / 8)) * 8;
+    const float gi = scale * __expf(sm.gam[i]);
+    const float ei = __expf(glast - sm.gam[i]);
+    const uint4 qv = *reinterpret_cast<const uint4*>(&sm.QV[i][c]);
+    const uint4 kv = *reinterpret_cast<const uint4*>(&sm.K[i][c]);
+    const uint32_t qw[4] = {qv.x, qv.y, qv.z, qv.w}, kw[4] = {kv.x, kv.y, kv.z, kv.w};
+    uint32_t qo[4], ko[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 a2 = unpack_bf16x2(qw[u]), b2 = unpack_bf16x2(kw[u]);
+      qo[u] = pack_bf16x2(gi * a2.x, gi * a2.y);
+      ko[u] = pack_bf16x2(ei * b2.x, ei * b2.y);
+    }
+    *reinterpret_cast<uint4*>(Qho + (cidx * C + i) * DK + c) = make_uint4(qo[0], qo[1], qo[2], qo[3]);
+    *reinterpret_cast<uint4*>(Kto + (cidx * C + i) * DK + c) = make_uint4(ko[0], ko[1], ko[2], ko[3]);
+  }
+  if (threadIdx.x == 0) gCo[cidx] = __expf(glast);
   __syncthreads();
+  // V into the Q buffer while the inverse runs
+  load_tile(&sm.QV[0][0], QP, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
+  cp_commit();
   tri_inverse_inplace(sm.M);
 
-  // T to bf16; Qh, Kt out; K -> diag(b G) K and V -> diag(b) V in place
+  // T to bf16; K -> diag(b G) K in place; then V -> diag(b) V
   for (int idx = threadIdx.x; idx < C * C; idx += THREADS) {
     const int i = idx / C, j = idx % C;
     sm.Tb[i][j] = f2bf(sm.M[i][j]);
   }
-  const float glast = sm.gam[C - 1];
-  for (int idx = threadIdx.x; idx < C * (DK / 2); idx += THREADS) {
-    const int i = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
-    const float gi = __expf(sm.gam[i]);
-    const float ei = __expf(glast - sm.gam[i]);
-    const float2 qv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[i][c]));
-    const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
-    *reinterpret_cast<uint32_t*>(Qho + (cidx * C + i) * DK + c) = pack_bf16x2(scale * gi * qv.x, scale * gi * qv.y);
-    *reinterpret_cast<uint32_t*>(Kto + (cidx * C + i) * DK + c) = pack_bf16x2(ei * kv.x, ei * kv.y);
-    const float bg = sm.beta[i] * gi;
-    *reinterpret_cast<uint32_t*>(&sm.K[i][c]) = pack_bf16x2(bg * kv.x, bg * kv.y);
+  for (int idx = threadIdx.x; idx < C * (DK / 8); idx += THREADS) {
+    const int i = idx / (DK / 8), c = (idx % (DK / 8)) * 8;
+    const float bg = sm.beta[i] * __expf(sm.gam[i]);
+    uint4 kv = *reinterpret_cast<const uint4*>(&sm.K[i][c]);
+    uint32_t* kw = reinterpret_cast<uint32_t*>(&kv);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 b2 = unpack_bf16x2(kw[u]);
+      kw[u] = pack_bf16x2(bg * b2.x, bg * b2.y);
+    }
+    *reinterpret_cast<uint4*>(&sm.K[i][c]) = kv;
   }
-  for (int idx = threadIdx.x; idx < C * (DV / 2); idx += THREADS) {
-    const int i = idx / (DV / 2), c = (idx % (DV / 2)) * 2;
-    const float2 vv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.V[i][c]));
-    *reinterpret_cast<uint32_t*>(&sm.V[i][c]) = pack_bf16x2(sm.beta[i] * vv.x, sm.beta[i] * vv.y);
+  cp_wait_all();
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < C * (DV / 8); idx += THREADS) {
+    const int i = idx / (DV / 8), c = (idx % (DV / 8)) * 8;
+    const float bi = sm.beta[i];
+    uint4 vv = *reinterpret_cast<const uint4*>(&sm.QV[i][c]);
+    uint32_t* vw = reinterpret_cast<uint32_t*>(&vv);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const float2 b2 = unpack_bf16x2(vw[u]);
+      vw[u] = pack_bf16x2(bi * b2.x, bi * b2.y);
+    }
+    *reinterpret_cast<uint4*>(&sm.QV[i][c]) = vv;
   }
-  if (threadIdx.x == 0) gCo[cidx] = __expf(glast);
   __syncthreads();
 
   // W = T Xw, U = T Xu: warp tile 16 rows x (D / 2) columns
@@ -170,7 +268,7 @@ intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
     float acc[1][NT][4];
     zero(acc);
     const int c0 = (warp >> 2) * (DV / 2);
-    warp_mma<1, NT, false, true>(acc, &sm.Tb[0][0], C + PAD, &sm.V[0][0], DV + PAD, m0, c0, C);
+    warp_mma<1, NT, false, true>(acc, &sm.Tb[0][0], C + PAD, &sm.QV[0][0], QP, m0, c0, C);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -182,8 +280,6 @@ intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
 }
 
 // ------------------------------------------------------------------ backward --
-
-constexpr int cmax(int a, int b) { return a > b ? a : b; }
 
 template <int DK, int DV>
 struct BwdSmem {
