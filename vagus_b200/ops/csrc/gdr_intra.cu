@@ -1,5 +1,5 @@
 // Intra-chunk stage of the chunked gated delta rule (scalar gate), forward
-// and backward, one CTA per (batch, head, 64-token chunk).
+// and backward, one CTA per (batch, head, 64-token chunk), two CTAs per SM.
 //
 // With gamma = cumsum(g) inside the chunk, G = exp(gamma), D_ij =
 // exp(gamma_i - gamma_j) (i >= j, masked before the exp), the forward builds
@@ -281,22 +281,19 @@ intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
 
 // ------------------------------------------------------------------ backward --
 
+// Backward shared memory, about 110 KB for dk = dv = 256 (two CTAs per SM):
+// K stays resident; the feature dimension of Q, V, dW and dU is processed in
+// two halves through three half-width buffers.
 template <int DK, int DV>
 struct BwdSmem {
-  static constexpr int DX = cmax(DK, DV);
-  __nv_bfloat16 K[C][DK + PAD];          // B0: K throughout
-  __nv_bfloat16 X1[C][DX + PAD];         // B1: V (phase 1-2), then dQK | dKKsym (bf16 64 x 72 each)
-  __nv_bfloat16 X2[C][DX + PAD];         // B2: Q (phase 1), dW (phase 2), Q again (phase 4)
-  __nv_bfloat16 X3[C][DX + PAD];         // B3: dU (phase 2), then P (fp32 64 x 65)
-  float KK[C][C + 1];                    // KK, then dKK (in place)
-  float QK[C][C + 1];
-  float T[C][C + 1];
-  float dT[C][C + 1];                    // dT, then dM
+  static constexpr int HK = DK / 2, HV = DV / 2;
+  static constexpr int HP = cmax(cmax(HK, HV), C) + PAD;     // half-buffer pitch (elements)
+  __nv_bfloat16 K[C][DK + PAD];
+  __nv_bfloat16 H0[C][HP];     // Q lo (KK/QK) | V half (pass A) | dT bf16 | Q half (pass B)
+  __nv_bfloat16 H1[C][HP];     // Q hi (KK/QK) | dW half (pass A) | P bf16 | dQK bf16
+  __nv_bfloat16 H2[C][HP];     // dU half (pass A) | dW half (pass B)
+  float F[C][C + 1];           // M -> T | dM | dKK, then (C x (C + PAD)) bf16 dKK + dKK^T
   __nv_bfloat16 Tb[C][C + PAD];
-  // dQK | dKKsym (bf16, 64 x 72 each) live in X1 once V is consumed, when X1 is
-  // wide enough; narrower heads get a dedicated buffer
-  static constexpr bool kInX1 = (DX + PAD) >= 2 * (C + PAD);
-  __nv_bfloat16 dQKsep[kInX1 ? 1 : 2 * C][C + PAD];
   float gam[C], beta[C], graw[C];
   float rw[C];     // sum_c dXw K         (-> dbeta * G, dG * beta)
   float ru[C];     // sum_c dXu V         (-> dbeta)
@@ -327,8 +324,18 @@ __device__ __forceinline__ void row_dot_accumulate(const float (&acc)[1][NT][4],
   }
 }
 
+// fp32 (chunk-major, pitch ld) -> bf16 shared tile of rows x cols
+__device__ __forceinline__ void f32_to_smem(__nv_bfloat16* s, int sp, const float* __restrict__ g, int ld, int rows,
+                                            int cols) {
+  for (int idx = threadIdx.x; idx < rows * (cols / 4); idx += THREADS) {
+    const int i = idx / (cols / 4), c = (idx % (cols / 4)) * 4;
+    const float4 w4 = *reinterpret_cast<const float4*>(g + (long long)i * ld + c);
+    *reinterpret_cast<uint2*>(s + i * sp + c) = make_uint2(pack_bf16x2(w4.x, w4.y), pack_bf16x2(w4.z, w4.w));
+  }
+}
+
 template <int DK, int DV>
-__global__ void __launch_bounds__(THREADS)
+__global__ void __launch_bounds__(THREADS, 2)
 intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                  const __nv_bfloat16* __restrict__ v, const float* __restrict__ g, const float* __restrict__ beta,
                  const float* __restrict__ dW, const float* __restrict__ dQh, const float* __restrict__ dKt,
@@ -336,7 +343,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
                  __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
                  float* __restrict__ dg, float* __restrict__ dbeta, int L, int H, float scale) {
   using S = BwdSmem<DK, DV>;
-  constexpr int DX = S::DX;
+  constexpr int HK = S::HK, HV = S::HV, HP = S::HP, KP = DK + PAD;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   S& sm = *reinterpret_cast<S*>(smem_raw);
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -344,14 +351,18 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   const long long bh = (long long)b * H + h;
   const long long cidx = bh * N + n;
   const long long tok0 = (long long)b * L + (long long)n * C;
-  const int warp = threadIdx.x / 32;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
   const int m0 = (warp & 3) * 16, n0 = (warp >> 2) * 32;
+  const __nv_bfloat16* qrow = q + (tok0 * H + h) * DK;
+  const __nv_bfloat16* krow = k + (tok0 * H + h) * DK;
+  const __nv_bfloat16* vrow = v + (tok0 * H + h) * DV;
+  const long long qld = (long long)H * DK, vld = (long long)H * DV;
 
-  // ---- phase 1: K, V, Q; gates; KK, QK; M -> T
-  load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
-  load_tile(&sm.X1[0][0], DX + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
-  load_tile(&sm.X2[0][0], DX + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  // ---- phase 1: K, Q; gates; KK, QK (kept in registers); M -> T
+  load_tile(&sm.K[0][0], KP, krow, qld, C, DK);
+  load_tile(&sm.H0[0][0], HP, qrow, qld, C, HK);
+  load_tile(&sm.H1[0][0], HP, qrow + HK, qld, C, HK);
   cp_commit();
   if (tid < C) {
     sm.graw[tid] = g[(tok0 + tid) * H + h];
@@ -362,199 +373,256 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   if (warp == 0) chunk_cumsum(sm.graw, sm.gam);
   cp_wait_all();
   __syncthreads();
+  float kk[1][4][4], qk[1][4][4];
+  zero(kk);
+  zero(qk);
+  warp_mma<1, 4, false, false>(kk, &sm.K[0][0], KP, &sm.K[0][0], KP, m0, n0, DK);
+  warp_mma<1, 4, false, false>(qk, &sm.H0[0][0], HP, &sm.K[0][0], KP, m0, n0, HK);
+  warp_mma<1, 4, false, false>(qk, &sm.H1[0][0], HP, &sm.K[0][0] + HK, KP, m0, n0, HK);
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+      sm.F[i][j] = (j < i) ? sm.beta[i] * kk[0][nt][e] * __expf(sm.gam[i] - sm.gam[j]) : 0.f;
+    }
+  __syncthreads();
+  tri_inverse_inplace(sm.F);
+  for (int idx = tid; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.F[idx / C][idx % C]);
+
+  // ---- pass A over feature halves: dV, row dots, dT partial products
+  float a1[1][4][4], a2[1][4][4];     // dW K^T and dU V^T
+  zero(a1);
+  zero(a2);
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    __syncthreads();
+    load_tile(&sm.H0[0][0], HP, vrow + hf * HV, vld, C, HV);
+    load_tile(&sm.H2[0][0], HP, dU + cidx * C * DV + hf * HV, DV, C, HV);
+    cp_commit();
+    f32_to_smem(&sm.H1[0][0], HP, dW + cidx * C * DK + hf * HK, DK, C, HK);
+    cp_wait_all();
+    __syncthreads();
+    {
+      // dXu = T^T dU  ->  dV = diag(b) dXu ; ru += dXu . V
+      constexpr int NT = HV / 16;
+      const int c0 = (warp >> 2) * (HV / 2);
+      float acc[1][NT][4];
+      zero(acc);
+      warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &sm.H2[0][0], HP, m0, c0, C);
+      row_dot_accumulate<NT>(acc, &sm.H0[0][0], HP, m0, c0, sm.ru);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+          *reinterpret_cast<uint32_t*>(dv + ((tok0 + i) * H + h) * DV + hf * HV + c) =
+              pack_bf16x2(sm.beta[i] * acc[0][nt][e], sm.beta[i] * acc[0][nt][e + 1]);
+        }
+    }
+    {
+      // dXw = T^T dW ; rw += dXw . K
+      constexpr int NT = HK / 16;
+      const int c0 = (warp >> 2) * (HK / 2);
+      float acc[1][NT][4];
+      zero(acc);
+      warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &sm.H1[0][0], HP, m0, c0, C);
+      row_dot_accumulate<NT>(acc, &sm.K[0][0] + hf * HK, KP, m0, c0, sm.rw);
+    }
+    warp_mma<1, 4, false, false>(a1, &sm.H1[0][0], HP, &sm.K[0][0] + hf * HK, KP, m0, n0, HK);
+    warp_mma<1, 4, false, false>(a2, &sm.H2[0][0], HP, &sm.H0[0][0], HP, m0, n0, HV);
+  }
+  __syncthreads();
+
+  // ---- dT = (dW K^T) diag(b G) + (dU V^T) diag(b)  (bf16 into H0)
+#pragma unroll
+  for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+      const float x0 = sm.beta[j] * (__expf(sm.gam[j]) * a1[0][nt][e] + a2[0][nt][e]);
+      const float x1 = sm.beta[j + 1] * (__expf(sm.gam[j + 1]) * a1[0][nt][e + 1] + a2[0][nt][e + 1]);
+      *reinterpret_cast<uint32_t*>(&sm.H0[i][j]) = pack_bf16x2(x0, x1);
+    }
+  __syncthreads();
+  // P = T^T dT (bf16 into H1), dM = -strict_lower(P T^T) (fragments)
   {
-    float kk[1][4][4], qk[1][4][4];
-    zero(kk);
-    zero(qk);
-    warp_mma<1, 4, false, false>(kk, &sm.K[0][0], DK + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
-    warp_mma<1, 4, false, false>(qk, &sm.X2[0][0], DX + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
+    float p[1][4][4];
+    zero(p);
+    warp_mma<1, 4, true, true>(p, &sm.Tb[0][0], C + PAD, &sm.H0[0][0], HP, m0, n0, C);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(&sm.H1[i][j]) = pack_bf16x2(p[0][nt][e], p[0][nt][e + 1]);
+      }
+  }
+  __syncthreads();
+  float dm[1][4][4];
+  zero(dm);
+  warp_mma<1, 4, false, false>(dm, &sm.H1[0][0], HP, &sm.Tb[0][0], C + PAD, m0, n0, C);
+  __syncthreads();                            // P (H1) consumed
+
+  // ---- elementwise on the fragments: dKK (into F), dQK (bf16 into H1),
+  //      gate gradients of D, dbeta partials
+  {
+    const float* dArow = dA + cidx * C * C;
+    float rowg[2] = {0.f, 0.f}, rowm[2] = {0.f, 0.f}, colg[4][2];
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt) colg[nt][0] = colg[nt][1] = 0.f;
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
-        const float d = (j <= i) ? __expf(sm.gam[i] - sm.gam[j]) : 0.f;
-        sm.KK[i][j] = kk[0][nt][e];
-        sm.QK[i][j] = qk[0][nt][e];
-        sm.T[i][j] = (j < i) ? sm.beta[i] * kk[0][nt][e] * d : 0.f;
+        float dkk = 0.f, dqk = 0.f;
+        if (j <= i) {
+          const float d = __expf(sm.gam[i] - sm.gam[j]);
+          const float da = dArow[i * C + j];
+          dqk = scale * da * d;
+          float dd = scale * da * qk[0][nt][e];
+          if (j < i) {
+            const float dmv = -dm[0][nt][e];
+            dkk = dmv * sm.beta[i] * d;
+            rowm[e >> 1] += dmv * kk[0][nt][e] * d;
+            dd += dmv * sm.beta[i] * kk[0][nt][e];
+            const float t = dd * d;
+            rowg[e >> 1] += t;
+            colg[nt][e & 1] -= t;
+          }
+        }
+        sm.F[i][j] = dkk;
+        dm[0][nt][e] = dqk;                   // reuse the register for dQK
       }
-  }
-  __syncthreads();
-  tri_inverse_inplace(sm.T);
-  for (int idx = tid; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.T[idx / C][idx % C]);
-
-  // ---- phase 2: dW -> X2, dU -> X3 (bf16)
-  for (int idx = tid; idx < C * (DK / 4); idx += THREADS) {
-    const int i = idx / (DK / 4), c = (idx % (DK / 4)) * 4;
-    const float4 w4 = *reinterpret_cast<const float4*>(dW + (cidx * C + i) * DK + c);
-    *reinterpret_cast<uint2*>(&sm.X2[i][c]) = make_uint2(pack_bf16x2(w4.x, w4.y), pack_bf16x2(w4.z, w4.w));
-  }
-  load_tile(&sm.X3[0][0], DX + PAD, dU + cidx * C * DV, DV, C, DV);
-  cp_commit();
-  cp_wait_all();
-  __syncthreads();
-
-  constexpr int NTK = DK / 16, NTV = DV / 16;
-  const int ck0 = (warp >> 2) * (DK / 2), cv0 = (warp >> 2) * (DV / 2);
-  float dKacc[1][NTK][4];
-  {
-    // dXw = T^T dW  ->  dK = diag(b G) dXw ; rw += dXw . K
-    zero(dKacc);
-    warp_mma<1, NTK, true, true>(dKacc, &sm.Tb[0][0], C + PAD, &sm.X2[0][0], DX + PAD, m0, ck0, C);
-    row_dot_accumulate<NTK>(dKacc, &sm.K[0][0], DK + PAD, m0, ck0, sm.rw);
-#pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = m0 + frag_row(0, e);
-        dKacc[0][nt][e] *= sm.beta[i] * __expf(sm.gam[i]);
-      }
-  }
-  {
-    // dXu = T^T dU  ->  dV = diag(b) dXu ; ru += dXu . V
-    float acc[1][NTV][4];
-    zero(acc);
-    warp_mma<1, NTV, true, true>(acc, &sm.Tb[0][0], C + PAD, &sm.X3[0][0], DX + PAD, m0, cv0, C);
-    row_dot_accumulate<NTV>(acc, &sm.X1[0][0], DX + PAD, m0, cv0, sm.ru);
-#pragma unroll
-    for (int nt = 0; nt < NTV; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int i = m0 + frag_row(0, e), c = cv0 + frag_col(nt, e);
-        *reinterpret_cast<uint32_t*>(dv + ((tok0 + i) * H + h) * DV + c) =
-            pack_bf16x2(sm.beta[i] * acc[0][nt][e], sm.beta[i] * acc[0][nt][e + 1]);
-      }
-  }
-  {
-    // dT = (dW K^T) diag(b G) + (dU V^T) diag(b)
-    float a1[1][4][4], a2[1][4][4];
-    zero(a1);
-    zero(a2);
-    warp_mma<1, 4, false, false>(a1, &sm.X2[0][0], DX + PAD, &sm.K[0][0], DK + PAD, m0, n0, DK);
-    warp_mma<1, 4, false, false>(a2, &sm.X3[0][0], DX + PAD, &sm.X1[0][0], DX + PAD, m0, n0, DV);
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
+      for (int e = 0; e < 4; e += 2) {
         const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
-        sm.dT[i][j] = sm.beta[j] * (__expf(sm.gam[j]) * a1[0][nt][e] + a2[0][nt][e]);
+        *reinterpret_cast<uint32_t*>(&sm.H1[i][j]) = pack_bf16x2(dm[0][nt][e], dm[0][nt][e + 1]);
       }
-  }
-  __syncthreads();
-
-  // ---- phase 3: P = T^T dT (fp32, into X3), dM = -strict_lower(P T^T) (into dT)
-  float (*P)[C + 1] = reinterpret_cast<float (*)[C + 1]>(&sm.X3[0][0]);
-  for (int idx = tid; idx < C * C; idx += THREADS) {
-    const int i = idx / C, j = idx % C;
-    float s = 0.f;
-    for (int kk = i; kk < C; ++kk) s += sm.T[kk][i] * sm.dT[kk][j];   // T[kk][i] = 0 for kk < i
-    P[i][j] = s;
-  }
-  __syncthreads();
-  for (int idx = tid; idx < C * C; idx += THREADS) {
-    const int i = idx / C, j = idx % C;
-    float s = 0.f;
-    if (j < i)
-      for (int kk = 0; kk <= j; ++kk) s += P[i][kk] * sm.T[j][kk];  // T[j][kk] = 0 for kk > j
-    sm.dT[i][j] = -s;
-  }
-  __syncthreads();
-
-  // elementwise: dKK (in place of KK), dQK (bf16), D-gradients, dbeta partials
-  __nv_bfloat16 (*dQKb)[C + PAD] = S::kInX1 ? reinterpret_cast<__nv_bfloat16 (*)[C + PAD]>(&sm.X1[0][0])
-                                             : sm.dQKsep;
-  __nv_bfloat16 (*dKKb)[C + PAD] = dQKb + C;
-  for (int idx = tid; idx < C * C; idx += THREADS) {
-    const int i = idx / C, j = idx % C;
-    float dkk = 0.f, dqk = 0.f, dd = 0.f, rmv = 0.f;
-    if (j <= i) {
-      const float d = __expf(sm.gam[i] - sm.gam[j]);
-      const float da = dA[(cidx * C + i) * C + j];
-      dqk = scale * da * d;
-      dd = scale * da * sm.QK[i][j];
-      if (j < i) {
-        const float dm = sm.dT[i][j];
-        dkk = dm * sm.beta[i] * d;
-        rmv = dm * sm.KK[i][j] * d;
-        dd += dm * sm.beta[i] * sm.KK[i][j];
-      }
-      const float t = dd * d;
-      if (j < i) {
-        atomicAdd(&sm.dgam[i], t);
-        atomicAdd(&sm.dgam[j], -t);
-        atomicAdd(&sm.rm[i], rmv);
-      }
-    }
-    sm.KK[i][j] = dkk;
-    dQKb[i][j] = f2bf(dqk);
-  }
-  __syncthreads();
-  for (int idx = tid; idx < C * C; idx += THREADS) {
-    const int i = idx / C, j = idx % C;
-    dKKb[i][j] = f2bf(sm.KK[i][j] + sm.KK[j][i]);
-  }
-  // ---- phase 4: reload Q, dK and dQ GEMMs
-  load_tile(&sm.X2[0][0], DX + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
-  cp_commit();
-  cp_wait_all();
-  __syncthreads();
-
-  warp_mma<1, NTK, false, true>(dKacc, &dKKb[0][0], C + PAD, &sm.K[0][0], DK + PAD, m0, ck0, C);
-  warp_mma<1, NTK, true, true>(dKacc, &dQKb[0][0], C + PAD, &sm.X2[0][0], DX + PAD, m0, ck0, C);
-  {
-    const float glast = sm.gam[C - 1];
-    float part[2] = {0.f, 0.f};
-#pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int i = m0 + frag_row(0, e), c = ck0 + frag_col(nt, e);
-        const float ei = __expf(glast - sm.gam[i]);
-        const float2 dkt = *reinterpret_cast<const float2*>(dKt + (cidx * C + i) * DK + c);
-        const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
-        part[e >> 1] += dkt.x * kv.x + dkt.y * kv.y;
-        *reinterpret_cast<uint32_t*>(dk + ((tok0 + i) * H + h) * DK + c) =
-            pack_bf16x2(dKacc[0][nt][e] + ei * dkt.x, dKacc[0][nt][e + 1] + ei * dkt.y);
-      }
+    // row sums over the 4 lanes of a row, column sums over the 8 lanes of a column
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      float s = part[r];
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      if ((tid & 3) == 0) atomicAdd(&sm.rk[m0 + ((tid & 31) >> 2) + 8 * r], s);
+      float sg = rowg[r], smv = rowm[r];
+      sg += __shfl_xor_sync(0xffffffffu, sg, 1);
+      sg += __shfl_xor_sync(0xffffffffu, sg, 2);
+      smv += __shfl_xor_sync(0xffffffffu, smv, 1);
+      smv += __shfl_xor_sync(0xffffffffu, smv, 2);
+      if ((lane & 3) == 0) {
+        atomicAdd(&sm.dgam[m0 + (lane >> 2) + 8 * r], sg);
+        atomicAdd(&sm.rm[m0 + (lane >> 2) + 8 * r], smv);
+      }
+    }
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float sc = colg[nt][c];
+        sc += __shfl_xor_sync(0xffffffffu, sc, 4);
+        sc += __shfl_xor_sync(0xffffffffu, sc, 8);
+        sc += __shfl_xor_sync(0xffffffffu, sc, 16);
+        if (lane < 4) atomicAdd(&sm.dgam[n0 + nt * 8 + lane * 2 + c], sc);
+      }
+  }
+  __syncthreads();
+  // dKK + dKK^T as bf16 over F's storage (read everything first)
+  __nv_bfloat16 (*dKKb)[C + PAD] = reinterpret_cast<__nv_bfloat16 (*)[C + PAD]>(&sm.F[0][0]);
+  {
+    float sym[C * C / THREADS];
+#pragma unroll
+    for (int u = 0; u < C * C / THREADS; ++u) {
+      const int idx = tid + u * THREADS, i = idx / C, j = idx % C;
+      sym[u] = sm.F[i][j] + sm.F[j][i];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < C * C / THREADS; ++u) {
+      const int idx = tid + u * THREADS, i = idx / C, j = idx % C;
+      dKKb[i][j] = f2bf(sym[u]);
     }
   }
-  {
-    float dQacc[1][NTK][4];
-    zero(dQacc);
-    warp_mma<1, NTK, false, true>(dQacc, &dQKb[0][0], C + PAD, &sm.K[0][0], DK + PAD, m0, ck0, C);
-    float part[2] = {0.f, 0.f};
+
+  // ---- pass B over feature halves: dK, dQ
+  const float glast = sm.gam[C - 1];
+#pragma unroll 1
+  for (int hf = 0; hf < 2; ++hf) {
+    __syncthreads();
+    load_tile(&sm.H0[0][0], HP, qrow + hf * HK, qld, C, HK);
+    cp_commit();
+    f32_to_smem(&sm.H2[0][0], HP, dW + cidx * C * DK + hf * HK, DK, C, HK);
+    cp_wait_all();
+    __syncthreads();
+    constexpr int NT = HK / 16;
+    const int c0 = (warp >> 2) * (HK / 2);
+    const __nv_bfloat16* Kh = &sm.K[0][0] + hf * HK;
+    {
+      // dK = diag(b G) T^T dW + (dKK + dKK^T) K + dQK^T Q + diag(G_C / G) dKt
+      float acc[1][NT][4];
+      zero(acc);
+      warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &sm.H2[0][0], HP, m0, c0, C);
 #pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
+      for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-      for (int e = 0; e < 4; e += 2) {
-        const int i = m0 + frag_row(0, e), c = ck0 + frag_col(nt, e);
-        const float gi = __expf(sm.gam[i]);
-        const float2 dqh = *reinterpret_cast<const float2*>(dQh + (cidx * C + i) * DK + c);
-        const float2 qv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.X2[i][c]));
-        part[e >> 1] += dqh.x * qv.x + dqh.y * qv.y;
-        *reinterpret_cast<uint32_t*>(dq + ((tok0 + i) * H + h) * DK + c) =
-            pack_bf16x2(dQacc[0][nt][e] + scale * gi * dqh.x, dQacc[0][nt][e + 1] + scale * gi * dqh.y);
+        for (int e = 0; e < 4; ++e) {
+          const int i = m0 + frag_row(0, e);
+          acc[0][nt][e] *= sm.beta[i] * __expf(sm.gam[i]);
+        }
+      warp_mma<1, NT, false, true>(acc, &dKKb[0][0], C + PAD, Kh, KP, m0, c0, C);
+      warp_mma<1, NT, true, true>(acc, &sm.H1[0][0], HP, &sm.H0[0][0], HP, m0, c0, C);
+      float part[2] = {0.f, 0.f};
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+          const float ei = __expf(glast - sm.gam[i]);
+          const float2 dkt = *reinterpret_cast<const float2*>(dKt + (cidx * C + i) * DK + hf * HK + c);
+          const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(Kh + i * KP + c));
+          part[e >> 1] += dkt.x * kv.x + dkt.y * kv.y;
+          *reinterpret_cast<uint32_t*>(dk + ((tok0 + i) * H + h) * DK + hf * HK + c) =
+              pack_bf16x2(acc[0][nt][e] + ei * dkt.x, acc[0][nt][e + 1] + ei * dkt.y);
+        }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        float s = part[r];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if ((lane & 3) == 0) atomicAdd(&sm.rk[m0 + (lane >> 2) + 8 * r], s);
       }
+    }
+    {
+      // dQ = dQK K + s diag(G) dQh
+      float acc[1][NT][4];
+      zero(acc);
+      warp_mma<1, NT, false, true>(acc, &sm.H1[0][0], HP, Kh, KP, m0, c0, C);
+      float part[2] = {0.f, 0.f};
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      float s = part[r];
-      s += __shfl_xor_sync(0xffffffffu, s, 1);
-      s += __shfl_xor_sync(0xffffffffu, s, 2);
-      if ((tid & 3) == 0) atomicAdd(&sm.rq[m0 + ((tid & 31) >> 2) + 8 * r], s);
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+          const float gi = __expf(sm.gam[i]);
+          const float2 dqh = *reinterpret_cast<const float2*>(dQh + (cidx * C + i) * DK + hf * HK + c);
+          const float2 qv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.H0[i][c]));
+          part[e >> 1] += dqh.x * qv.x + dqh.y * qv.y;
+          *reinterpret_cast<uint32_t*>(dq + ((tok0 + i) * H + h) * DK + hf * HK + c) =
+              pack_bf16x2(acc[0][nt][e] + scale * gi * dqh.x, acc[0][nt][e + 1] + scale * gi * dqh.y);
+        }
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        float s = part[r];
+        s += __shfl_xor_sync(0xffffffffu, s, 1);
+        s += __shfl_xor_sync(0xffffffffu, s, 2);
+        if ((lane & 3) == 0) atomicAdd(&sm.rq[m0 + (lane >> 2) + 8 * r], s);
+      }
     }
   }
   __syncthreads();
 
-  // ---- phase 5: per-row scalars, reverse cumsum
+  // ---- per-row scalars, reverse cumsum
   if (warp == 0) {
-    const int lane = tid & 31;
-    const float glast = sm.gam[C - 1];
     float dgl[2], tail = 0.f;
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -575,7 +643,6 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
       const float t = __shfl_down_sync(0xffffffffu, s, o);
       if (lane + o < 32) s += t;
     }
-    // s = sum over lanes >= lane of (dgl0 + dgl1)
     dg[(tok0 + 2 * lane + 1) * H + h] = s - dgl[0];
     dg[(tok0 + 2 * lane) * H + h] = s;
   }
