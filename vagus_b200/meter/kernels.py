@@ -10,7 +10,7 @@ copy bandwidth and the cuBLAS bf16 GEMM rate).  Inputs are random; the
 shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
-gdr_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
+gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
 case runs.
 
 Used for the committed ncu summaries: run one case with few iterations under
@@ -82,6 +82,14 @@ def _cases(B: int, L: int):
     o, _, saved = _gdr_fwd(q, k, v, g, beta, None, scale)
     do = torch.randn_like(o)
     cases["gdr_bwd"] = (lambda: _gdr_bwd(saved, do, None, scale, False), None, 2 * (intra + rec))
+    # the two stages separately (inputs from one forward)
+    W_, Qh, Kt, A_, U_, gC = C.gdr_intra_fwd(q, k, v, g, beta, scale)
+    cases["gdr_rec_fwd"] = (lambda: C.gdr_rec_fwd(W_, Qh, Kt, A_, U_, gC, None, True), None, rec)
+    _, Vp, states, _ = C.gdr_rec_fwd(W_, Qh, Kt, A_, U_, gC, None, True)
+    dO = torch.randn(BH, nc, 64, hd, device=dev).to(bf)
+    cases["gdr_rec_bwd"] = (lambda: C.gdr_rec_bwd(W_, Qh, Kt, A_, Vp, gC, states, dO, None, False), None, 2 * rec)
+    rb = C.gdr_rec_bwd(W_, Qh, Kt, A_, Vp, gC, states, dO, None, False)
+    cases["gdr_intra_bwd"] = (lambda: C.gdr_intra_bwd(q, k, v, g, beta, *rb[:6], scale), None, 2 * intra)
 
     from ..ops._core import gemm
     a = r(T, D)

@@ -76,46 +76,52 @@ std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_l
   return {dA, ddt};
 }
 
-// Recurrence forward: returns (O, V', states, S_out)
+// Recurrence forward: returns (O, V', states, S_out).  The per-chunk entry
+// states (bf16) are always produced: the output stage reads them.
 std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor U, Tensor gC,
                                 c10::optional<Tensor> S0, bool need_states) {
+  (void)need_states;
   const int64_t BH = W.size(0);
   const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(U.size(3));
   TORCH_CHECK(W.size(2) == 64, "gdr: chunk size 64");
   for (auto* t : {&W, &Qh, &Kt, &A, &U}) TORCH_CHECK(t->is_contiguous() && t->scalar_type() == at::kBFloat16, "gdr: bf16");
   auto O = torch::empty_like(U);
   auto Vp = torch::empty_like(U);
-  auto states = torch::empty({need_states ? BH : 0, N, DK, DV}, W.options().dtype(at::kFloat));
+  auto states = torch::empty({BH, N, DK, DV}, W.options());
   auto S_out = torch::empty({BH, DK, DV}, W.options().dtype(at::kFloat));
   vagus::GdrRecArgs a{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), U.data_ptr(),
                       gC.contiguous().data_ptr<float>(), fptr(S0), O.data_ptr(), Vp.data_ptr(),
-                      need_states ? states.data_ptr<float>() : nullptr, S_out.data_ptr<float>(), BH, N, DK, DV};
+                      states.data_ptr(), S_out.data_ptr<float>(), BH, N, DK, DV};
   check(vagus::gdr_rec_fwd(a, stream()), "gdr_rec_fwd");
   return {O, Vp, states, S_out};
 }
 
-// Recurrence backward: returns (dW, dQh, dKt, dA, dU, dgC, dS0)
+// Recurrence backward: returns (dW, dQh, dKt (bf16), dA (fp32), dU (bf16), dgC, dS0)
 std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor Vp, Tensor gC, Tensor states,
                                 Tensor dO, c10::optional<Tensor> dS_final, bool need_dS0) {
   const int64_t BH = W.size(0);
   const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(Vp.size(3));
+  TORCH_CHECK(states.scalar_type() == at::kBFloat16 && states.is_contiguous(), "gdr_rec_bwd: bf16 states");
   dO = dO.contiguous();
   auto f32 = W.options().dtype(at::kFloat);
-  auto dW = torch::zeros({BH, N, 64, DK}, f32);
-  auto dQh = torch::zeros({BH, N, 64, DK}, f32);
-  auto dKt = torch::zeros({BH, N, 64, DK}, f32);
-  auto dA = torch::zeros({BH, N, 64, 64}, f32);
-  auto dU = torch::empty({BH, N, 64, DV}, W.options());
+  auto bf = W.options();
+  auto dW = torch::empty({BH, N, 64, DK}, bf);
+  auto dQh = torch::empty({BH, N, 64, DK}, bf);
+  auto dKt = torch::empty({BH, N, 64, DK}, bf);
+  auto dA = torch::empty({BH, N, 64, 64}, f32);
+  auto dU = torch::empty({BH, N, 64, DV}, bf);
   auto dgC = torch::zeros({BH, N}, f32);
   auto dS0 = torch::empty({need_dS0 ? BH : 0, DK, DV}, f32);
+  auto dstates = torch::empty({BH, N, DK, DV}, bf);
   vagus::GdrRecBwdArgs a;
   a.f = vagus::GdrRecArgs{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), nullptr,
-                          gC.contiguous().data_ptr<float>(), nullptr, nullptr, Vp.data_ptr(), states.data_ptr<float>(),
+                          gC.contiguous().data_ptr<float>(), nullptr, nullptr, Vp.data_ptr(), states.data_ptr(),
                           nullptr, BH, N, DK, DV};
   a.dO = dO.data_ptr();
   a.dS_final = fptr(dS_final);
-  a.dW = dW.data_ptr<float>(); a.dQh = dQh.data_ptr<float>(); a.dKt = dKt.data_ptr<float>(); a.dA = dA.data_ptr<float>();
+  a.dW = dW.data_ptr(); a.dQh = dQh.data_ptr(); a.dKt = dKt.data_ptr(); a.dA = dA.data_ptr<float>();
   a.dU = dU.data_ptr(); a.dgC = dgC.data_ptr<float>(); a.dS0 = need_dS0 ? dS0.data_ptr<float>() : nullptr;
+  a.dstates = dstates.data_ptr();
   check(vagus::gdr_rec_bwd(a, stream()), "gdr_rec_bwd");
   return {dW, dQh, dKt, dA, dU, dgC, dS0};
 }
@@ -155,7 +161,9 @@ std::vector<Tensor> gdr_intra_bwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor
   a.f = vagus::GdrIntraArgs{q.data_ptr(), k.data_ptr(), v.data_ptr(), gc.data_ptr<float>(), bc.data_ptr<float>(),
                             nullptr, nullptr, nullptr, nullptr, nullptr, nullptr, B, L, H, DK, DV,
                             static_cast<float>(scale)};
-  a.dW = dW.data_ptr<float>(); a.dQh = dQh.data_ptr<float>(); a.dKt = dKt.data_ptr<float>(); a.dA = dA.data_ptr<float>();
+  TORCH_CHECK(dW.scalar_type() == at::kBFloat16 && dQh.scalar_type() == at::kBFloat16 &&
+              dKt.scalar_type() == at::kBFloat16, "gdr_intra_bwd: bf16 dW / dQh / dKt");
+  a.dW = dW.data_ptr(); a.dQh = dQh.data_ptr(); a.dKt = dKt.data_ptr(); a.dA = dA.data_ptr<float>();
   a.dU = dU.data_ptr(); a.dgC = dgC.data_ptr<float>();
   a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr(); a.dg = dg.data_ptr<float>(); a.dbeta = db.data_ptr<float>();
   check(vagus::gdr_intra_bwd(a, stream()), "gdr_intra_bwd");

@@ -12,8 +12,8 @@
 // columns x 4 partial sums spread over the 256 threads).  The 64 x 64 x dk
 // products run on the tensor cores (mma.sync, bf16 in, fp32 accumulate).
 //
-// The backward takes dW, dQh, dKt, dA (fp32, summed over value tiles by the
-// recurrence backward), dU and dgC and returns dq, dk, dv, dg, dbeta:
+// The backward takes dW, dQh, dKt (bf16), dA (fp32), dU and dgC from the
+// recurrence backward and returns dq, dk, dv, dg, dbeta:
 //     dXw = T^T dW,  dXu = T^T dU          (Xw = diag(bG) K, Xu = diag(b) V)
 //     dT  = dW Xw^T + dU Xu^T,  dM = -strict_lower(T^T dT T^T)
 //     dKK = dM o b D,  dQK = s dA o D,  dD = dM o b KK + s dA o QK
@@ -324,22 +324,12 @@ __device__ __forceinline__ void row_dot_accumulate(const float (&acc)[1][NT][4],
   }
 }
 
-// fp32 (chunk-major, pitch ld) -> bf16 shared tile of rows x cols
-__device__ __forceinline__ void f32_to_smem(__nv_bfloat16* s, int sp, const float* __restrict__ g, int ld, int rows,
-                                            int cols) {
-  for (int idx = threadIdx.x; idx < rows * (cols / 4); idx += THREADS) {
-    const int i = idx / (cols / 4), c = (idx % (cols / 4)) * 4;
-    const float4 w4 = *reinterpret_cast<const float4*>(g + (long long)i * ld + c);
-    *reinterpret_cast<uint2*>(s + i * sp + c) = make_uint2(pack_bf16x2(w4.x, w4.y), pack_bf16x2(w4.z, w4.w));
-  }
-}
-
 template <int DK, int DV>
 __global__ void __launch_bounds__(THREADS, 2)
 intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
                  const __nv_bfloat16* __restrict__ v, const float* __restrict__ g, const float* __restrict__ beta,
-                 const float* __restrict__ dW, const float* __restrict__ dQh, const float* __restrict__ dKt,
-                 const float* __restrict__ dA, const __nv_bfloat16* __restrict__ dU, const float* __restrict__ dgC,
+                 const __nv_bfloat16* __restrict__ dW, const __nv_bfloat16* __restrict__ dQh,
+                 const __nv_bfloat16* __restrict__ dKt, const float* __restrict__ dA, const __nv_bfloat16* __restrict__ dU, const float* __restrict__ dgC,
                  __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk, __nv_bfloat16* __restrict__ dv,
                  float* __restrict__ dg, float* __restrict__ dbeta, int L, int H, float scale) {
   using S = BwdSmem<DK, DV>;
@@ -399,8 +389,8 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
     __syncthreads();
     load_tile(&sm.H0[0][0], HP, vrow + hf * HV, vld, C, HV);
     load_tile(&sm.H2[0][0], HP, dU + cidx * C * DV + hf * HV, DV, C, HV);
+    load_tile(&sm.H1[0][0], HP, dW + cidx * C * DK + hf * HK, DK, C, HK);
     cp_commit();
-    f32_to_smem(&sm.H1[0][0], HP, dW + cidx * C * DK + hf * HK, DK, C, HK);
     cp_wait_all();
     __syncthreads();
     {
@@ -550,8 +540,8 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   for (int hf = 0; hf < 2; ++hf) {
     __syncthreads();
     load_tile(&sm.H0[0][0], HP, qrow + hf * HK, qld, C, HK);
+    load_tile(&sm.H2[0][0], HP, dW + cidx * C * DK + hf * HK, DK, C, HK);
     cp_commit();
-    f32_to_smem(&sm.H2[0][0], HP, dW + cidx * C * DK + hf * HK, DK, C, HK);
     cp_wait_all();
     __syncthreads();
     constexpr int NT = HK / 16;
@@ -578,7 +568,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
         for (int e = 0; e < 4; e += 2) {
           const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
           const float ei = __expf(glast - sm.gam[i]);
-          const float2 dkt = *reinterpret_cast<const float2*>(dKt + (cidx * C + i) * DK + hf * HK + c);
+          const float2 dkt = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dKt + (cidx * C + i) * DK + hf * HK + c));
           const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(Kh + i * KP + c));
           part[e >> 1] += dkt.x * kv.x + dkt.y * kv.y;
           *reinterpret_cast<uint32_t*>(dk + ((tok0 + i) * H + h) * DK + hf * HK + c) =
@@ -604,7 +594,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
         for (int e = 0; e < 4; e += 2) {
           const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
           const float gi = __expf(sm.gam[i]);
-          const float2 dqh = *reinterpret_cast<const float2*>(dQh + (cidx * C + i) * DK + hf * HK + c);
+          const float2 dqh = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(dQh + (cidx * C + i) * DK + hf * HK + c));
           const float2 qv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.H0[i][c]));
           part[e >> 1] += dqh.x * qv.x + dqh.y * qv.y;
           *reinterpret_cast<uint32_t*>(dq + ((tok0 + i) * H + h) * DK + hf * HK + c) =
@@ -667,7 +657,8 @@ int launch_bwd(const GdrIntraBwdArgs& a, cudaStream_t st) {
   cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sm));
   dim3 grid(static_cast<unsigned>(a.f.L / C), a.f.H, static_cast<unsigned>(a.f.B));
   kern<<<grid, THREADS, sm, st>>>((const __nv_bfloat16*)a.f.q, (const __nv_bfloat16*)a.f.k,
-                                  (const __nv_bfloat16*)a.f.v, a.f.g, a.f.beta, a.dW, a.dQh, a.dKt, a.dA,
+                                  (const __nv_bfloat16*)a.f.v, a.f.g, a.f.beta, (const __nv_bfloat16*)a.dW,
+                                  (const __nv_bfloat16*)a.dQh, (const __nv_bfloat16*)a.dKt, a.dA,
                                   (const __nv_bfloat16*)a.dU, a.dgC, (__nv_bfloat16*)a.dq, (__nv_bfloat16*)a.dk,
                                   (__nv_bfloat16*)a.dv, a.dg, a.dbeta, static_cast<int>(a.f.L), a.f.H, a.f.scale);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;

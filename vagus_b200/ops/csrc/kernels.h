@@ -61,7 +61,7 @@ struct GdrRecArgs {
   const float* S0;                                 // (BH, DK, DV) or null
   void* O;                                         // (BH, N, C, DV) bf16
   void* Vp;                                        // (BH, N, C, DV) bf16: V' (written fwd, read bwd)
-  float* states;                                   // (BH, N, DK, DV) entry states (written fwd, read bwd)
+  void* states;                                    // (BH, N, DK, DV) bf16 entry states (written fwd, read bwd)
   float* S_out;                                    // (BH, DK, DV) or null
   long long BH; int N, DK, DV;
 };
@@ -70,11 +70,12 @@ struct GdrRecBwdArgs {
   GdrRecArgs f;
   const void* dO;                                  // (BH, N, C, DV) bf16
   const float* dS_final;                           // (BH, DK, DV) or null
-  float* dW; float* dQh; float* dKt;               // (BH, N, C, DK) fp32, zero-initialised (atomics)
-  float* dA;                                       // (BH, N, C, C) fp32, zero-initialised
+  void* dW; void* dQh; void* dKt;                  // (BH, N, C, DK) bf16
+  float* dA;                                       // (BH, N, C, C) fp32
   void* dU;                                        // (BH, N, C, DV) bf16
-  float* dgC;                                      // (BH, N) fp32, zero-initialised
+  float* dgC;                                      // (BH, N) fp32, zero-initialised (atomics)
   float* dS0;                                      // (BH, DK, DV) or null
+  void* dstates;                                   // (BH, N, DK, DV) bf16 scratch: dL/dS per chunk
 };
 int gdr_rec_bwd(const GdrRecBwdArgs& a, cudaStream_t st);
 // gdr_intra.cu: intra-chunk WY / UT stage (scalar gate), forward + backward.
@@ -91,7 +92,8 @@ struct GdrIntraArgs {
 int gdr_intra_fwd(const GdrIntraArgs& a, cudaStream_t st);
 struct GdrIntraBwdArgs {
   GdrIntraArgs f;                               // forward inputs (outputs unused)
-  const float* dW; const float* dQh; const float* dKt; const float* dA;   // from gdr_rec_bwd
+  const void* dW; const void* dQh; const void* dKt;   // (BH, N, C, DK) bf16, from gdr_rec_bwd
+  const float* dA;
   const void* dU; const float* dgC;
   void* dq; void* dk; void* dv;                 // (B, L, H, DK|DV) bf16
   float* dg; float* dbeta;                      // (B, L, H) fp32
