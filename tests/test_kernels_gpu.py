@@ -330,3 +330,33 @@ def test_gdn_mixer_matches_torch_path():
     assert rel(xa.grad, xb.grad) < 5e-2
     for (n, p), (_, pr) in zip(m.named_parameters(), m_ref.named_parameters()):
         assert rel(p.grad, pr.grad) < 8e-2, (n, rel(p.grad, pr.grad))
+
+
+def test_rmsnorm_pass_fuses_residual_gradient():
+    """The (norm, identity) node adds both gradients in the norm kernel and
+    hands the next linear_residual backward a bf16 copy; gradients match the
+    plain composition."""
+    from vagus_b200 import ops
+    torch.manual_seed(0)
+    T, D = 512, 1024
+    x0 = torch.randn(T, D, device=DEV)
+    gamma = (1 + 0.1 * torch.randn(D, device=DEV)).requires_grad_(True)
+    w = (0.02 * torch.randn(D, D, device=DEV)).requires_grad_(True)
+
+    def run(fused):
+        x = x0.clone().requires_grad_(True)
+        norm = (lambda t: ops.rmsnorm_pass(t, gamma, 1e-6)) if fused else \
+            (lambda t: (ops.rmsnorm(t, gamma, 1e-6, out_dtype=torch.bfloat16), t))
+        h, xp = norm(x)
+        y = ops.linear_residual(xp, h, w)
+        h2, yp = norm(y)
+        z = ops.linear_residual(yp, h2, w)
+        (z.pow(2).sum() * 1e-3).backward()
+        return x.grad.clone(), gamma.grad.clone(), w.grad.clone()
+
+    ref = run(False)
+    gamma.grad = None
+    w.grad = None
+    got = run(True)
+    for a, b in zip(got, ref):
+        assert rel(a, b) < 1e-2

@@ -6,6 +6,8 @@ The mixer is injected (any ``Mixer``) and kept under the attribute ``att``.
 On CUDA the two residual adds are fused into the epilogues of the output GEMMs
 (``wo`` and ``ffn.l2``): the GEMM kernel reads the fp32 residual and writes
 residual + product, so the residual stream makes one round trip per sub-layer.
+In the backward the residual gradient is added inside the norm kernel
+(``ops.rmsnorm_pass``), which also hands the output GEMM a bf16 copy.
 
 Parity: reference ``infra/components/block.py:19-91``.
 """
@@ -43,9 +45,9 @@ class Block(nn.Module, WithCache):
 
     def forward(self, x, is_causal: bool = True):
         if self._fused(x):
-            h = self.rmsnorm1(x, out_dtype=torch.bfloat16)
+            h, x = ops.rmsnorm_pass(x, self.rmsnorm1.gamma, self.rmsnorm1.eps)
             x = ops.linear_residual(x, self.att.forward_pre_out(h, is_causal), self.att.wo.weight)
-            h = self.rmsnorm2(x, out_dtype=torch.bfloat16)
+            h, x = ops.rmsnorm_pass(x, self.rmsnorm2.gamma, self.rmsnorm2.eps)
             return ops.linear_residual(x, self.ffn.hidden(h), self.ffn.l2.weight)
         x = x + self.att(self.rmsnorm1(x), is_causal)
         return x + self.ffn(self.rmsnorm2(x))

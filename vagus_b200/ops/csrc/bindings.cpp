@@ -113,7 +113,7 @@ std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor gamma, double eps, bool out_f32
 }
 
 std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor gamma, Tensor rstd, c10::optional<Tensor> dres,
-                                bool dx_f32) {
+                                bool dx_f32, bool want_bf16) {
   TORCH_CHECK(dy.is_contiguous() && x.is_contiguous(), "rmsnorm_bwd: layout");
   const int D = static_cast<int>(x.size(-1));
   const int64_t rows = x.numel() / D;
@@ -124,9 +124,12 @@ std::vector<Tensor> rmsnorm_bwd(Tensor dy, Tensor x, Tensor gamma, Tensor rstd, 
     TORCH_CHECK(is_f32(*dres) && dres->is_contiguous(), "dres must be contiguous fp32");
     dr = dres->data_ptr<float>();
   }
+  Tensor dx16;
+  if (want_bf16) dx16 = torch::empty(x.sizes(), x.options().dtype(at::kBFloat16));
   check(vagus::rmsnorm_bwd(dy.data_ptr(), is_f32(dy), x.data_ptr(), is_f32(x), gamma.data_ptr<float>(),
                            rstd.data_ptr<float>(), dr, dx.data_ptr(), dx_f32, dgamma.data_ptr<float>(), rows, D,
-                           stream()), "rmsnorm_bwd");
+                           stream(), want_bf16 ? dx16.data_ptr() : nullptr), "rmsnorm_bwd");
+  if (want_bf16) return {dx, dgamma, dx16};
   return {dx, dgamma};
 }
 

@@ -9,8 +9,10 @@ namespace vagus {
 // norm.cu
 int rmsnorm_fwd(const void* x, int x_f32, const float* gamma, void* y, int y_f32, float* rstd, long long rows, int D,
                 float eps, cudaStream_t s);
+// dx16 (optional, bf16): a copy of dx; supported for fp32 x / dx with D in {512, 768, 1024, 1536, 2048}
 int rmsnorm_bwd(const void* dy, int dy_f32, const void* x, int x_f32, const float* gamma, const float* rstd,
-                const float* dres, void* dx, int dx_f32, float* dgamma, long long rows, int D, cudaStream_t s);
+                const float* dres, void* dx, int dx_f32, float* dgamma, long long rows, int D, cudaStream_t s,
+                void* dx16 = nullptr);
 int rmsnorm_gated_fwd(const void* o, const void* g, long long ldg, int H, const float* gamma, void* y, int y_f32,
                       float* rstd, long long rows, int D, float eps, cudaStream_t s);
 int rmsnorm_gated_bwd(const void* dy, const void* o, const void* g, long long ldg, int H, const float* gamma,

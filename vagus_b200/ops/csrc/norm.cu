@@ -8,6 +8,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
+
 namespace vagus {
 namespace {
 
@@ -72,6 +74,74 @@ __global__ void rmsnorm_bwd_k(const TG* __restrict__ dy, const TI* __restrict__ 
       st(o, c, v);
       atomicAdd(&sg[c], g * xh);
     }
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
+}
+
+// Vectorised backward for the residual-stream case: x, dx (and dres) fp32,
+// dy bf16 or fp32, D = 128 * NV.  A persistent grid of 8-warp CTAs walks the
+// rows (one warp per row, lane l owns columns 4 l + 128 j); the gamma
+// gradient stays in registers across all rows of a warp and is reduced once
+// per CTA.  dx16, when given, receives a bf16 copy of dx (the operand the
+// next GEMM backward consumes).
+template <typename TG, int NV>
+__global__ void __launch_bounds__(256, 2)
+rmsnorm_bwd_vec_k(const TG* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
+                  const float* __restrict__ rstd, const float* __restrict__ dres, float* __restrict__ dx,
+                  __nv_bfloat16* __restrict__ dx16, float* __restrict__ dgamma, long long rows) {
+  constexpr int D = 128 * NV;
+  __shared__ __align__(16) float sgam[D];
+  __shared__ float sg[D];
+  for (int c = threadIdx.x; c < D; c += blockDim.x) { sgam[c] = gamma[c]; sg[c] = 0.f; }
+  __syncthreads();
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  float4 acc[NV];
+#pragma unroll
+  for (int j = 0; j < NV; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (long long r = (long long)blockIdx.x * 8 + warp; r < rows; r += (long long)gridDim.x * 8) {
+    const float rs = rstd[r];
+    float4 xv[NV], gv[NV];
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = 4 * lane + 128 * j;
+      xv[j] = *reinterpret_cast<const float4*>(x + r * D + c);
+      if constexpr (sizeof(TG) == 4) {
+        gv[j] = *reinterpret_cast<const float4*>(dy + r * D + c);
+      } else {
+        const uint2 u = *reinterpret_cast<const uint2*>(dy + r * D + c);
+        const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+        gv[j] = make_float4(a.x, a.y, b.x, b.y);
+      }
+    }
+    float dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const float4 gm = *reinterpret_cast<const float4*>(sgam + 4 * lane + 128 * j);
+      dot += gv[j].x * gm.x * xv[j].x + gv[j].y * gm.y * xv[j].y + gv[j].z * gm.z * xv[j].z + gv[j].w * gm.w * xv[j].w;
+    }
+    dot = warp_sum(dot) * rs / D;
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = 4 * lane + 128 * j;
+      const float4 gm = *reinterpret_cast<const float4*>(sgam + c);
+      float4 h = make_float4(xv[j].x * rs, xv[j].y * rs, xv[j].z * rs, xv[j].w * rs);
+      float4 o = make_float4(rs * (gv[j].x * gm.x - h.x * dot), rs * (gv[j].y * gm.y - h.y * dot),
+                             rs * (gv[j].z * gm.z - h.z * dot), rs * (gv[j].w * gm.w - h.w * dot));
+      if (dres) {
+        const float4 d = *reinterpret_cast<const float4*>(dres + r * D + c);
+        o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
+      }
+      *reinterpret_cast<float4*>(dx + r * D + c) = o;
+      if (dx16) *reinterpret_cast<uint2*>(dx16 + r * D + c) = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
+      acc[j].x += gv[j].x * h.x; acc[j].y += gv[j].y * h.y; acc[j].z += gv[j].z * h.z; acc[j].w += gv[j].w * h.w;
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < NV; ++j) {
+    const int c = 4 * lane + 128 * j;
+    atomicAdd(&sg[c], acc[j].x); atomicAdd(&sg[c + 1], acc[j].y);
+    atomicAdd(&sg[c + 2], acc[j].z); atomicAdd(&sg[c + 3], acc[j].w);
   }
   __syncthreads();
   for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
@@ -246,7 +316,24 @@ int rmsnorm_fwd(const void* x, int x_f32, const float* gamma, void* y, int y_f32
 }
 
 int rmsnorm_bwd(const void* dy, int dy_f32, const void* x, int x_f32, const float* gamma, const float* rstd,
-                const float* dres, void* dx, int dx_f32, float* dgamma, long long rows, int D, cudaStream_t s) {
+                const float* dres, void* dx, int dx_f32, float* dgamma, long long rows, int D, cudaStream_t s,
+                void* dx16) {
+  if (x_f32 && dx_f32 && D % 128 == 0 && (D == 512 || D == 768 || D == 1024 || D == 1536 || D == 2048)) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long need = (rows + 7) / 8;
+    const int grid = static_cast<int>(std::min<long long>(need, 2LL * sms));
+#define RV(TG, NV) rmsnorm_bwd_vec_k<TG, NV><<<grid, 256, 0, s>>>((const TG*)dy, (const float*)x, gamma, rstd, dres, \
+                                                                  (float*)dx, (__nv_bfloat16*)dx16, dgamma, rows)
+#define RVD(TG) switch (D) { case 512: RV(TG, 4); break; case 768: RV(TG, 6); break; case 1024: RV(TG, 8); break; \
+                             case 1536: RV(TG, 12); break; default: RV(TG, 16); }
+    if (dy_f32) { RVD(float) } else { RVD(__nv_bfloat16) }
+#undef RVD
+#undef RV
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
+  if (dx16) return 5;
   const int g = blocks_for(rows), t = 32 * ROWS_PER_CTA;
   const size_t sm = D * sizeof(float);
 #define RB(TI, TG, TO) rmsnorm_bwd_k<TI, TG, TO><<<g, t, sm, s>>>((const TG*)dy, (const TI*)x, gamma, rstd, dres, (TO*)dx, dgamma, rows, D)

@@ -30,7 +30,7 @@ class _RMSNorm(torch.autograd.Function):
     def backward(ctx, dy):
         x, gamma, rstd = ctx.saved_tensors
         dx, dg = native().rmsnorm_bwd(dy.contiguous(), x, gamma.float().contiguous(), rstd, None,
-                                      x.dtype == torch.float32)
+                                      x.dtype == torch.float32, False)
         return dx, dg.to(gamma.dtype), None, None
 
 
@@ -44,6 +44,42 @@ def rmsnorm(x, gamma, eps: float = 1e-6, out_dtype=None):
     if out_dtype not in (torch.float32, torch.bfloat16):
         return _rmsnorm_ref(x, gamma, eps).to(out_dtype)
     return _RMSNorm.apply(x, gamma, float(eps), out_dtype == torch.float32)
+
+
+class _RMSNormPass(torch.autograd.Function):
+    """``(rmsnorm(x) in bf16, x)`` as one autograd node.  A pre-norm block
+    reads the residual stream twice (the norm and the residual add); with
+    both uses behind this node the backward receives both gradients at once
+    and the norm kernel adds them, instead of a separate add over the fp32
+    stream.  It also writes a bf16 copy of the summed gradient, attached to
+    the returned tensor as ``_vagus_bf16``, for the GEMM backward that
+    consumes it next (``ops.linear_residual``)."""
+
+    @staticmethod
+    def forward(ctx, x, gamma, eps):
+        xc = x.contiguous()
+        y, rstd = native().rmsnorm_fwd(xc, gamma.float().contiguous(), eps, False)
+        ctx.save_for_backward(xc, gamma, rstd)
+        return y, x.view_as(x)
+
+    @staticmethod
+    def backward(ctx, dy, dpass):
+        x, gamma, rstd = ctx.saved_tensors
+        dres = None if dpass is None else dpass.float().contiguous()
+        out = native().rmsnorm_bwd(dy.contiguous(), x, gamma.float().contiguous(), rstd, dres, True, True)
+        dx, dg = out[0], out[1]
+        if len(out) > 2:
+            dx._vagus_bf16 = (out[2], dx._version)    # stale once dx is modified in place
+        return dx, dg.to(gamma.dtype), None
+
+
+def rmsnorm_pass(x, gamma, eps: float = 1e-6):
+    """Returns ``(rmsnorm(x) as bf16, x)``; see ``_RMSNormPass``.  Falls back
+    to the plain composition where the fused backward does not apply."""
+    if (x.is_cuda and x.dtype == torch.float32 and x.shape[-1] in (512, 768, 1024, 1536, 2048)
+            and torch.is_grad_enabled() and x.requires_grad):
+        return _RMSNormPass.apply(x, gamma, float(eps))
+    return rmsnorm(x, gamma, eps, out_dtype=torch.bfloat16 if x.is_cuda else None), x
 
 
 # ------------------------------------------------------ gated RMSNorm (GDN) --
