@@ -167,6 +167,8 @@ class _GDNMixer(torch.autograd.Function):
         P3 = P.view(B, L, NP)
         oa = 2 * Hk + 2 * Hv                                                  # a|b column offset
         C = native()
+        # the kernels take fp32 taps (a no-op for fp32 masters; bf16 under FSDP mixed precision)
+        cq, ck, cv = cq.float().contiguous(), ck.float().contiguous(), cv.float().contiguous()
         q, rq = C.conv_silu_fwd(P3[:, :, :Hk], cq, dk, True)
         k, rk = C.conv_silu_fwd(P3[:, :, Hk:2 * Hk], ck, dk, True)
         v, _ = C.conv_silu_fwd(P3[:, :, 2 * Hk:2 * Hk + Hv], cv, dv, False)
