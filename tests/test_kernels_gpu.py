@@ -360,3 +360,24 @@ def test_rmsnorm_pass_fuses_residual_gradient():
     got = run(True)
     for a, b in zip(got, ref):
         assert rel(a, b) < 1e-2
+
+
+@pytest.mark.parametrize("a_mn,b_mn", [(False, False), (False, True), (True, True)])
+@pytest.mark.parametrize("M,N,K", [(512, 768, 384), (640, 392, 200), (296, 1000, 128)])
+def test_gemm_cta_pair_matches_single_cta(a_mn, b_mn, M, N, K):
+    """The CTA-pair kernel (block_n 512, 256 x 256 tiles over two SMs) and the
+    one-CTA kernel (block_n 256) agree with the fp32 product, for stores and
+    for split-K atomic accumulation."""
+    A = torch.randn(M, K, device=DEV).bfloat16()
+    B = torch.randn(N, K, device=DEV).bfloat16()
+    Ast = A.t().contiguous() if a_mn else A
+    Bst = B.t().contiguous() if b_mn else B
+    ref = A.float() @ B.float().t()
+    for bn in (512, 256):
+        C = torch.empty(M, N, device=DEV, dtype=torch.float32)
+        _g(Ast, a_mn, Bst, b_mn, C, None, 1.0, 0.0, False, 0, bn)
+        assert rel(C, ref) < 2e-3, bn
+        acc = torch.randn(M, N, device=DEV)
+        want = acc + ref
+        _g(Ast, a_mn, Bst, b_mn, acc, None, 1.0, 0.0, True, 0, bn)
+        assert rel(acc, want) < 2e-3, bn

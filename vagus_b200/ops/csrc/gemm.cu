@@ -52,7 +52,8 @@ struct Cfg {
 
 struct KParams {
   int M, N, K, batch;
-  int tiles_m, tiles_n, splits, kb_total, kb_per_split;
+  int tiles_m, tiles_n, kb_total;
+  int full_tiles, kb_per_split, units;   // see decode_unit
   void* C;
   long long ldc, strideC;
   int c_f32;
@@ -63,6 +64,12 @@ struct KParams {
   int atomic;
   int vec;          // 16-byte vector access is legal for C and S
   int* err;
+  // stream-K (atomic outputs, CTA-pair kernel): worker w takes the global
+  // k-block range [w * kb_per_worker, (w + 1) * kb_per_worker) of the
+  // tiles x kb_total sequence, possibly spanning tiles; partial tiles meet
+  // in the atomic epilogue
+  int streamk;
+  long long kb_per_worker;
 };
 
 __device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row, int col0, const float* v) {
@@ -71,9 +78,16 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row
   const bool full = (col0 + 32 <= p.N) && p.vec;
   if (p.atomic) {
     float* c = reinterpret_cast<float*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc + col0;
+    if (full) {
+      // 16-byte vector reductions: a quarter of the L2 atomic operations
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (full || col0 + j < p.N) atomicAdd(c + j, p.alpha * v[j]);
+      for (int j = 0; j < 32; j += 4)
+        atomicAdd(reinterpret_cast<float4*>(c + j),
+                  make_float4(p.alpha * v[j], p.alpha * v[j + 1], p.alpha * v[j + 2], p.alpha * v[j + 3]));
+    } else {
+      for (int j = 0; j < 32; ++j)
+        if (col0 + j < p.N) atomicAdd(c + j, p.alpha * v[j]);
+    }
     return;
   }
   float out[32];
@@ -131,16 +145,69 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row
   }
 }
 
-// Decode a work unit into (batch, tile m, tile n, split).
-__device__ __forceinline__ void decode_unit(const KParams& p, int u, int& b, int& tm, int& tn, int& sp) {
-  sp = u % p.splits;
-  int t = u / p.splits;
-  int per_batch = p.tiles_m * p.tiles_n;
+// Work units.  The first `full_tiles` units are whole tiles (all of K); the
+// remaining tiles (fewer than one wave) are split `rsplit` ways along K so
+// the last wave fills the machine, and their partial products meet in the
+// atomic epilogue.  Within the split part the split index varies slowest:
+// CTAs running at the same time cover the same K range of neighbouring
+// tiles, so the operand panels they share are read from L2 once.
+__device__ __forceinline__ void decode_unit(const KParams& p, int u, int& b, int& tm, int& tn, int& kb0, int& kb1) {
+  int t;
+  if (u < p.full_tiles) {
+    t = u;
+    kb0 = 0;
+    kb1 = p.kb_total;
+  } else {
+    const int rem = p.batch * p.tiles_m * p.tiles_n - p.full_tiles;
+    const int v = u - p.full_tiles;
+    const int sp = v / rem;
+    t = p.full_tiles + (v - sp * rem);
+    kb0 = sp * p.kb_per_split;
+    kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+  }
+  const int per_batch = p.tiles_m * p.tiles_n;
   b = t / per_batch;
   t -= b * per_batch;
   tm = t / p.tiles_n;
   tn = t - tm * p.tiles_n;
 }
+
+// Work iterator shared by the three roles: strided units (tile, split), or a
+// contiguous stream-K range of k-blocks cut at tile boundaries.
+struct WorkIter {
+  long long g = 0, end = 0;
+  int u = 0, step = 1;
+  __device__ WorkIter(const KParams& p, int worker, int nworkers) {
+    if (p.streamk) {
+      const long long total = (long long)p.batch * p.tiles_m * p.tiles_n * p.kb_total;
+      g = (long long)worker * p.kb_per_worker;
+      end = g + p.kb_per_worker < total ? g + p.kb_per_worker : total;
+    } else {
+      u = worker;
+      step = nworkers;
+    }
+  }
+  __device__ bool next(const KParams& p, int& b, int& tm, int& tn, int& kb0, int& kb1) {
+    if (p.streamk) {
+      if (g >= end) return false;
+      const int t = static_cast<int>(g / p.kb_total);
+      kb0 = static_cast<int>(g - (long long)t * p.kb_total);
+      const long long left = end - g;
+      kb1 = left < p.kb_total - kb0 ? kb0 + static_cast<int>(left) : p.kb_total;
+      g += kb1 - kb0;
+      const int per_batch = p.tiles_m * p.tiles_n;
+      b = t / per_batch;
+      const int r = t - b * per_batch;
+      tm = r / p.tiles_n;
+      tn = r - tm * p.tiles_n;
+      return true;
+    }
+    if (u >= p.units) return false;
+    decode_unit(p, u, b, tm, tn, kb0, kb1);
+    u += step;
+    return true;
+  }
+};
 
 template <int BN, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
@@ -185,19 +252,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  const int units = p.batch * p.tiles_m * p.tiles_n * p.splits;
-
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-        int b, tm, tn, sp;
-        decode_unit(p, u, b, tm, tn, sp);
-        const int kb0 = sp * p.kb_per_split;
-        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+      WorkIter it(p, blockIdx.x, gridDim.x);
+      int b, tm, tn, kb0, kb1;
+      while (ok && it.next(p, b, tm, tn, kb0, kb1)) {
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) { ok = false; break; }
           uint8_t* sa = tiles + stage * C::STAGE_BYTES;
@@ -233,11 +296,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
       uint32_t phase = 0;
       bool ok = true;
       int local = 0;
-      for (int u = blockIdx.x; u < units && ok; u += gridDim.x, ++local) {
-        int b, tm, tn, sp;
-        decode_unit(p, u, b, tm, tn, sp);
-        const int kb0 = sp * p.kb_per_split;
-        const int kb1 = min(p.kb_total, kb0 + p.kb_per_split);
+      WorkIter it(p, blockIdx.x, gridDim.x);
+      int b, tm, tn, kb0, kb1;
+      for (; ok && it.next(p, b, tm, tn, kb0, kb1); ++local) {
         const int buf = local & 1;
         const uint32_t use = static_cast<uint32_t>(local >> 1);
         if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) { ok = false; break; }
@@ -273,9 +334,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
     const int quarter = warp & 3;              // TMEM lane quarter this warp may touch
     const int row_in_tile = quarter * 32 + lane;
     int local = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x, ++local) {
-      int b, tm, tn, sp;
-      decode_unit(p, u, b, tm, tn, sp);
+    WorkIter it(p, blockIdx.x, gridDim.x);
+    int b, tm, tn, kb0, kb1;
+    for (; it.next(p, b, tm, tn, kb0, kb1); ++local) {
       const int buf = local & 1;
       const uint32_t use = static_cast<uint32_t>(local >> 1);
       if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
@@ -300,6 +361,195 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------- CTA-pair kernel --
+// Same roles as above on a cluster of two CTAs (neighbouring SMs) that share
+// 256 x 256 output tiles through tcgen05.mma.cta_group::2 (M = 256, N = 256,
+// K = 16): CTA r of the pair loads A rows [128 r, 128 r + 128) and B columns
+// [128 r, 128 r + 128) of the tile and owns accumulator rows
+// [128 r, 128 r + 128) in its TMEM.  Per CTA and k-step that is 32 KB of
+// operands for a 128 x 256 x 64 share of the product (48 KB in the one-CTA
+// kernel), which is what keeps the tensor pipe fed from L2.
+//   * full barriers live in CTA 0: its producer expects both CTAs' bytes and
+//     the peer's loads complete on CTA 0's barrier (.cta_group::2 loads);
+//   * CTA 0's MMA thread issues everything and commits each stage back to
+//     the empty barriers of both CTAs, and each finished tile to both CTAs'
+//     accumulator-full barriers (one commit per CTA, no broadcast form);
+//   * both CTAs' epilogue warps arrive on CTA 0's accumulator-empty barriers.
+namespace pairk {
+constexpr int ROWS = 128;                 // rows of A / columns of B per CTA
+constexpr int TM = 256, TN = 256;         // pair tile
+constexpr int STAGES = 6;
+constexpr int A_BYTES = ROWS * BK * 2;
+constexpr int B_BYTES = ROWS * BK * 2;
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+constexpr int TMEM_COLS = 2 * TN;         // two accumulators (all 512 columns)
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+}  // namespace pairk
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_pair_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+                 const KParams p) {
+  using namespace pairk;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* tiles = smem;
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_full = empty_bar + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  const uint32_t rank = cluster_ctarank();
+  const int cluster = blockIdx.x >> 1, nclusters = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 8);         // 4 epilogue warps x 2 CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mapA);
+    tma_prefetch_desc(&mapB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();                           // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      WorkIter it(p, cluster, nclusters);
+      int b, tm, tn, kb0, kb1;
+      while (ok && it.next(p, b, tm, tn, kb0, kb1)) {
+        // 64-wide MN-major blocks that start past M / N are not loaded (their
+        // rows only feed masked output); both CTAs' counts go to CTA 0's barrier
+        int a_blk[2], b_blk[2];
+        for (int r = 0; r < 2; ++r) {
+          a_blk[r] = A_MN ? max(0, min(ROWS / 64, (p.M - tm * TM - r * ROWS + 63) / 64)) : ROWS / 64;
+          b_blk[r] = B_MN ? max(0, min(ROWS / 64, (p.N - tn * TN - r * ROWS + 63) / 64)) : ROWS / 64;
+        }
+        const uint32_t tx = (a_blk[0] + a_blk[1] + b_blk[0] + b_blk[1]) * 8192;
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&empty_bar[stage], phase ^ 1, abort_flag, p.err, kErrTimeoutProducer)) { ok = false; break; }
+          uint8_t* sa = tiles + stage * STAGE_BYTES;
+          uint8_t* sb = sa + A_BYTES;
+          const uint32_t fb = mapa_shared(smem_u32(&full_bar[stage]), 0);
+          if (rank == 0) mbar_arrive_expect_tx(&full_bar[stage], tx);
+          const int k0 = kb * BK;
+          const int m0 = tm * TM + (int)rank * ROWS, n0 = tn * TN + (int)rank * ROWS;
+          if (A_MN) {
+            for (int j = 0; j < a_blk[rank]; ++j) tma_load_3d_pair(sa + j * 8192, &mapA, fb, m0 + 64 * j, k0, b);
+          } else {
+            tma_load_3d_pair(sa, &mapA, fb, k0, m0, b);
+          }
+          if (B_MN) {
+            for (int j = 0; j < b_blk[rank]; ++j) tma_load_3d_pair(sb + j * 8192, &mapB, fb, n0 + 64 * j, k0, b);
+          } else {
+            tma_load_3d_pair(sb, &mapB, fb, k0, n0, b);
+          }
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------ MMA (CTA 0 of the pair)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc_bf16(TM, TN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      int local = 0;
+      WorkIter it(p, cluster, nclusters);
+      int b, tm, tn, kb0, kb1;
+      for (; ok && it.next(p, b, tm, tn, kb0, kb1); ++local) {
+        const int buf = local & 1;
+        const uint32_t use = static_cast<uint32_t>(local >> 1);
+        if (!mbar_wait(&acc_empty[buf], (use & 1) ^ 1, abort_flag, p.err, kErrTimeoutMma)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(buf * TN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(&full_bar[stage], phase, abort_flag, p.err, kErrTimeoutMma)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(tiles + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int kk = 0; kk < BK / UMMA_K; ++kk) {
+            const uint64_t ad = A_MN ? make_sw128_desc(a_addr + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(a_addr + kk * 32, 16, 1024);
+            const uint64_t bd = B_MN ? make_sw128_desc(b_addr + kk * 2048, 8192, 1024)
+                                     : make_sw128_desc(b_addr + kk * 32, 16, 1024);
+            tc_mma_f16_pair(d_tmem, ad, bd, idesc, (kb > kb0 || kk > 0) ? 1u : 0u);
+          }
+          const uint32_t e = smem_u32(&empty_bar[stage]);
+          tc_commit_pair(mapa_shared(e, 0));
+          tc_commit_pair(mapa_shared(e, 1));
+          if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        const uint32_t f = smem_u32(&acc_full[buf]);
+        tc_commit_pair(mapa_shared(f, 0));
+        tc_commit_pair(mapa_shared(f, 1));
+      }
+      tc_commit_pair(mapa_shared(smem_u32(drain_bar), 0));
+      mbar_wait(drain_bar, 0, abort_flag, p.err, kErrTimeoutMma);
+    }
+  } else {
+    // ----------------------------------------------------------- epilogue
+    const int quarter = warp & 3;
+    const int row_in_tile = (int)rank * ROWS + quarter * 32 + lane;
+    int local = 0;
+    WorkIter it(p, cluster, nclusters);
+    int b, tm, tn, kb0, kb1;
+    for (; it.next(p, b, tm, tn, kb0, kb1); ++local) {
+      const int buf = local & 1;
+      const uint32_t use = static_cast<uint32_t>(local >> 1);
+      if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
+      tc_fence_after();
+      const int row = tm * TM + row_in_tile;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * TN);
+#pragma unroll 1
+      for (int c = 0; c < TN; c += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(t_row + c, r);
+        tmem_ld_wait();
+        const int col0 = tn * TN + c;
+        if (col0 < p.N) store_row_chunk(p, b, row, col0, reinterpret_cast<const float*>(r));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[buf]), 0));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();                           // the peer's TMEM and smem stay valid until CTA 0 has drained
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -345,6 +595,34 @@ bool make_map(CUtensorMap* map, const void* base, long long inner, long long row
   return r == CUDA_SUCCESS;
 }
 
+// Unit plan (see decode_unit): whole tiles for every complete wave, then the
+// leftover tiles split along K so that they cover the workers about once
+// (atomic outputs only; each split keeps at least 8 k-blocks).  `split_k` > 1
+// forces that many splits of every tile.
+void plan_units(KParams& p, int tiles, int workers, bool atomic, int split_k) {
+  if (atomic && split_k > 1) {
+    p.full_tiles = 0;
+    p.kb_per_split = (p.kb_total + split_k - 1) / split_k;
+  } else if (atomic && split_k != 1) {
+    p.full_tiles = (tiles / workers) * workers;
+    const int rem = tiles - p.full_tiles;
+    // smallest split (at most 8) minimising the makespan ceil(rem * rs / workers) / rs
+    int rs = 1;
+    double best = 1e30;
+    for (int c = 1; rem > 0 && c <= 8 && p.kb_total / c >= 8; ++c) {
+      const double t = static_cast<double>((rem * c + workers - 1) / workers) / c;
+      if (t < best - 1e-9) { best = t; rs = c; }
+    }
+    p.kb_per_split = (p.kb_total + rs - 1) / rs;
+  } else {
+    p.full_tiles = tiles;
+    p.kb_per_split = p.kb_total;
+  }
+  const int rem = tiles - p.full_tiles;
+  const int rsplit = rem > 0 ? (p.kb_total + p.kb_per_split - 1) / p.kb_per_split : 0;
+  p.units = p.full_tiles + rem * rsplit;
+}
+
 int num_sms() {
   static int n = 0;
   if (n == 0) {
@@ -371,16 +649,51 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
   p.tiles_n = (a.N + BN - 1) / BN;
   p.kb_total = (a.K + BK - 1) / BK;
   const int tiles = p.tiles_m * p.tiles_n * a.batch;
-  int splits = 1;
-  if (a.atomic && a.split_k != 1) {
-    if (a.split_k > 1) splits = a.split_k;
-    else {
-      // enough work units to cover the SMs about twice, each at least 8 k-blocks
-      while (tiles * splits < 2 * num_sms() && p.kb_total / (splits * 2) >= 8) splits *= 2;
-    }
+  plan_units(p, tiles, num_sms(), a.atomic != 0, a.split_k);
+  p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC; p.c_f32 = a.c_f32;
+  p.S = a.S; p.lds = a.lds; p.strideS = a.strideS; p.s_f32 = a.s_f32;
+  p.alpha = a.alpha; p.beta = a.beta; p.atomic = a.atomic; p.err = a.err;
+  p.streamk = 0;
+  p.kb_per_worker = 0;
+  {
+    const int ce = a.c_f32 ? 4 : 2, se = a.s_f32 ? 4 : 2;
+    bool v = (reinterpret_cast<uintptr_t>(a.C) % 16 == 0) && ((a.ldc * ce) % 16 == 0) && ((a.strideC * ce) % 16 == 0);
+    if (a.S) v = v && (reinterpret_cast<uintptr_t>(a.S) % 16 == 0) && ((a.lds * se) % 16 == 0) && ((a.strideS * se) % 16 == 0);
+    p.vec = v ? 1 : 0;
   }
-  p.kb_per_split = (p.kb_total + splits - 1) / splits;
-  p.splits = (p.kb_total + p.kb_per_split - 1) / p.kb_per_split;
+  const int grid = std::min(p.units, num_sms());
+  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) != cudaSuccess) return 3;
+    attr_set[dev] = true;
+  }
+  if (std::getenv("VAGUS_GEMM_DEBUG"))
+    std::fprintf(stderr, "[gemm] launch grid %d smem %d M %d N %d K %d units %d\n", grid, C::SMEM_BYTES, a.M, a.N,
+                 a.K, p.units);
+  kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+template <bool A_MN, bool B_MN>
+int launch_pair(const GemmArgs& a, cudaStream_t stream) {
+  using namespace pairk;
+  CUtensorMap ma, mb;
+  bool ok = A_MN ? make_map(&ma, a.A, a.M, a.K, a.batch, a.lda, a.strideA, 64)
+                 : make_map(&ma, a.A, a.K, a.M, a.batch, a.lda, a.strideA, ROWS);
+  ok = ok && (B_MN ? make_map(&mb, a.B, a.N, a.K, a.batch, a.ldb, a.strideB, 64)
+                   : make_map(&mb, a.B, a.K, a.N, a.batch, a.ldb, a.strideB, ROWS));
+  if (!ok) return 2;
+  KParams p;
+  p.M = a.M; p.N = a.N; p.K = a.K; p.batch = a.batch;
+  p.tiles_m = (a.M + TM - 1) / TM;
+  p.tiles_n = (a.N + TN - 1) / TN;
+  p.kb_total = (a.K + BK - 1) / BK;
+  const int clusters_max = num_sms() / 2;
+  const int tiles = p.tiles_m * p.tiles_n * a.batch;
+  plan_units(p, tiles, clusters_max, a.atomic != 0, a.split_k == -1 ? 1 : a.split_k);
   p.C = a.C; p.ldc = a.ldc; p.strideC = a.strideC; p.c_f32 = a.c_f32;
   p.S = a.S; p.lds = a.lds; p.strideS = a.strideS; p.s_f32 = a.s_f32;
   p.alpha = a.alpha; p.beta = a.beta; p.atomic = a.atomic; p.err = a.err;
@@ -390,19 +703,52 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
     if (a.S) v = v && (reinterpret_cast<uintptr_t>(a.S) % 16 == 0) && ((a.lds * se) % 16 == 0) && ((a.strideS * se) % 16 == 0);
     p.vec = v ? 1 : 0;
   }
-  const int units = tiles * p.splits;
-  const int grid = std::min(units, num_sms());
-  auto kern = gemm_kernel<BN, A_MN, B_MN>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
-    attr_set = true;
+  int units = p.units;
+  p.streamk = 0;
+  p.kb_per_worker = 0;
+  if (a.atomic && a.split_k == -1) {
+    // stream-K (opt-in: split_k = -1): every pair gets the same number of
+    // k-blocks (at least 8).  Slower than split-K on long-K weight gradients
+    // here: pairs at different K offsets of one panel lose the L2 sharing.
+    const long long total = (long long)tiles * p.kb_total;
+    const long long workers = std::max<long long>(1, std::min<long long>(clusters_max, total / 8));
+    p.streamk = 1;
+    p.kb_per_worker = (total + workers - 1) / workers;
+    units = static_cast<int>((total + p.kb_per_worker - 1) / p.kb_per_worker);
   }
+  const int clusters = std::min(units, clusters_max);
+  auto kern = gemm_pair_kernel<A_MN, B_MN>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES) != cudaSuccess) return 3;
+    attr_set[dev] = true;
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(2 * clusters), 1, 1);
+  cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (std::getenv("VAGUS_GEMM_DEBUG"))
-    std::fprintf(stderr, "[gemm] launch grid %d smem %d M %d N %d K %d units %d\n", grid, C::SMEM_BYTES, a.M, a.N,
-                 a.K, units);
-  kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p);
+    std::fprintf(stderr, "[gemm] pair launch clusters %d smem %d M %d N %d K %d units %d\n", clusters, SMEM_BYTES,
+                 a.M, a.N, a.K, units);
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, p) != cudaSuccess) return 3;
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int dispatch_pair(const GemmArgs& a, cudaStream_t s) {
+  if (!a.a_mn && !a.b_mn) return launch_pair<false, false>(a, s);
+  if (!a.a_mn && a.b_mn) return launch_pair<false, true>(a, s);
+  if (a.a_mn && !a.b_mn) return launch_pair<true, false>(a, s);
+  return launch_pair<true, true>(a, s);
 }
 
 template <int BN>
@@ -422,13 +768,19 @@ int gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!aligned(a.A) || !aligned(a.B) || (a.lda % 8) || (a.ldb % 8)) return 1;
   if (a.batch > 1 && ((a.strideA % 8) || (a.strideB % 8))) return 1;
-  const int bn = a.block_n > 0 ? a.block_n : (a.N < 256 ? 128 : 256);
+  // block_n: 0 = automatic (CTA pairs with 256 x 256 tiles when M and N
+  // reach 256, unless VAGUS_GEMM_NO_PAIR is set), 128 / 256 = one-CTA tiles
+  // of that width, 512 = CTA pairs.
+  static const bool no_pair = std::getenv("VAGUS_GEMM_NO_PAIR") != nullptr;
+  const bool pair = a.block_n == 512 || (a.block_n == 0 && !no_pair && a.M >= 256 && a.N >= 256);
+  const int bn = pair ? 128 : (a.block_n > 0 ? a.block_n : (a.N < 256 ? 128 : 256));
   // Every TMA box must fit inside its tensor (the tensor-map encoder does not
   // reject an oversized box reliably); callers route smaller problems elsewhere.
   const long long a_inner = a.a_mn ? a.M : a.K, a_rows = a.a_mn ? a.K : a.M;
   const long long b_inner = a.b_mn ? a.N : a.K, b_rows = a.b_mn ? a.K : a.N;
   const long long a_box = a.a_mn ? 64 : BM, b_box = a.b_mn ? 64 : bn;
   if (a_inner < 64 || a_rows < a_box || b_inner < 64 || b_rows < b_box) return 6;
+  if (pair) return dispatch_pair(a, stream);
   return bn == 128 ? dispatch_major<128>(a, stream) : dispatch_major<256>(a, stream);
 }
 

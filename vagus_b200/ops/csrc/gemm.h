@@ -19,7 +19,7 @@ struct GemmArgs {
   int s_f32 = 0;
   float alpha = 1.f, beta = 0.f;
   int atomic = 0;            // 1: C (fp32) += alpha * A @ B^T with red.add (split-K allowed)
-  int split_k = 0;           // 0: automatic (atomic mode only), 1: none, >1: fixed
+  int split_k = 0;           // 0: automatic (atomic mode only), 1: none, >1: fixed, -1: stream-K (CTA pairs)
   int block_n = 0;           // 0: automatic (128 or 256)
   int* err = nullptr;        // device error word (bounded-wait timeouts)
 };
