@@ -10,7 +10,8 @@ copy bandwidth and the cuBLAS bf16 GEMM rate).  Inputs are random; the
 shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
-gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
+gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
+sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
 case runs.
 
 Used for the committed ncu summaries: run one case with few iterations under
@@ -102,6 +103,24 @@ def _cases(B: int, L: int):
     cases["gemm_fwd"] = (lambda: gemm(a, False, wpk, False, c), None, fl)            # x W^T
     cases["gemm_dgrad"] = (lambda: gemm(gp, False, wpk, True, da), None, fl)         # dy W
     cases["gemm_wgrad"] = (lambda: gemm(gp, True, a, True, dwp, atomic=True), None, fl)  # dW += dy^T x
+
+    # causal attention at the Transformer++ 340M shape (16 heads of 64) and
+    # the hybrid 1.3B softmax layers (16 heads of 128)
+    import math as _m
+    from torch.nn import functional as F
+    for hd_a, Ha in ((64, 16), (128, 16)):
+        qa = r(B, Ha, L, hd_a)
+        ka = r(B, Ha, L, hd_a)
+        va = r(B, Ha, L, hd_a)
+        fl_a = 2 * 2 * B * Ha * L * L * hd_a / 2                       # causal half of QK^T and PV
+        sc = 1.0 / _m.sqrt(hd_a)
+        cases[f"attn_fwd_d{hd_a}"] = (lambda qa=qa, ka=ka, va=va, sc=sc: C.attn_fwd(qa, ka, va, True, sc), None, fl_a)
+        cases[f"sdpa_fwd_d{hd_a}"] = (lambda qa=qa, ka=ka, va=va: F.scaled_dot_product_attention(qa, ka, va, is_causal=True),
+                                      None, fl_a)
+        oa, lsea = C.attn_fwd(qa, ka, va, True, sc)
+        doa = torch.randn_like(oa)
+        cases[f"attn_bwd_d{hd_a}"] = (lambda qa=qa, ka=ka, va=va, oa=oa, lsea=lsea, doa=doa, sc=sc:
+                                      C.attn_bwd(qa, ka, va, oa, lsea, doa, True, sc), None, 2.5 * fl_a)
 
     xs = r(T, D)
     gamma = torch.ones(D, device=dev)

@@ -1,0 +1,814 @@
+// Flash attention (causal with lower-right alignment, or full), forward and
+// backward, bf16 in / fp32 statistics, GQA, head dims 64 and 128.
+//
+// Forward: one CTA per (128 queries, batch * head); 8 warps, 16 query rows
+// each.  Key/value tiles of 64 rows stream through a double-buffered
+// cp.async ring; S = Q K^T and O += P V run on the tensor cores (mma.sync
+// m16n8k16, fp32 accumulate) with the online softmax in registers: the S
+// accumulator fragments of two adjacent 8-key tiles are exactly the A
+// fragment of the next product, so P never leaves registers.  Writes O and
+// the row log-sum-exp (natural log) for the backward.
+//
+// Backward: one CTA per (64 keys, batch * kv-head); 8 warps.  The CTA keeps
+// its K / V tile and accumulates dK, dV in registers while it walks the
+// query blocks of every query head that shares the kv head (GQA needs no
+// atomics for dK / dV): P = exp(S - lse), dP = dO V^T, dS = P (dP - delta)
+// with delta = rowsum(dO o O) from a small pre-pass; P and dS go through
+// shared memory as bf16 for dV += P^T dO, dK += dS^T Q and dQ += dS K (fp32
+// atomics into a scratch buffer, scaled and rounded by a last pass).
+//
+// Causal masking is lower-right aligned: query i sits at absolute position
+// Lk - Lq + i and sees keys j <= Lk - Lq + i.  Fully masked tiles are skipped.
+//
+// The forward of problems with Lq, Lk >= 128 and D = Dv in {64, 128} runs on
+// the 5th-generation tensor cores instead (attn_fwd_tc below); the mma.sync
+// forward above serves the small / odd shapes (decode, Lq < 128).
+#include "common.cuh"
+#include "gemm.h"
+#include "kernels.h"
+#include "mma.cuh"
+
+#include <cmath>
+#include <cstdlib>
+
+namespace vagus {
+namespace {
+
+using namespace mma;
+
+constexpr float kLog2e = 1.4426950408889634f;
+
+// ---------------------------------------------------------------- forward --
+
+constexpr int FQ = 128;      // queries per CTA
+constexpr int FK = 64;       // keys per tile
+constexpr int FWARPS = 8;
+
+template <int D, int DV>
+struct FwdSmem {
+  __nv_bfloat16 Q[FQ][D + PAD];
+  __nv_bfloat16 K[2][FK][D + PAD];
+  __nv_bfloat16 V[2][FK][DV + PAD];
+};
+
+template <int D, int DV>
+__global__ void __launch_bounds__(FWARPS * 32, 1)
+attn_fwd_kernel(const AttnArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  FwdSmem<D, DV>& sm = *reinterpret_cast<FwdSmem<D, DV>*>(smem_raw);
+  const int qb = blockIdx.x;
+  const int bh = blockIdx.y;
+  const int b = bh / a.H, h = bh % a.H;
+  const int hk = h / (a.H / a.Hk);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int q0 = qb * FQ;
+  const int offs = a.Lk - a.Lq;                       // lower-right alignment
+  const __nv_bfloat16* Qg = reinterpret_cast<const __nv_bfloat16*>(a.q) + b * a.sq_b + h * a.sq_h;
+  const __nv_bfloat16* Kg = reinterpret_cast<const __nv_bfloat16*>(a.k) + b * a.sk_b + hk * a.sk_h;
+  const __nv_bfloat16* Vg = reinterpret_cast<const __nv_bfloat16*>(a.v) + b * a.sv_b + hk * a.sv_h;
+
+  // tiles: rows past the end are zero-filled
+  auto load_rows = [&](__nv_bfloat16* s, int sp, const __nv_bfloat16* g, long long gp, int r0, int nrows,
+                       int limit, int cols) {
+    const int per_row = cols / 8;
+    for (int i = threadIdx.x; i < nrows * per_row; i += blockDim.x) {
+      const int r = i / per_row, c = (i - r * per_row) * 8;
+      if (r0 + r < limit) cp_async16(s + r * sp + c, g + (long long)(r0 + r) * gp + c);
+      else *reinterpret_cast<uint4*>(s + r * sp + c) = make_uint4(0, 0, 0, 0);
+    }
+  };
+  // last key any query of this CTA may see
+  const int q_last = min(q0 + FQ, a.Lq) - 1;
+  const int k_end = a.causal ? min(a.Lk, q_last + offs + 1) : a.Lk;
+  const int ntiles = (k_end + FK - 1) / FK;
+
+  load_rows(&sm.Q[0][0], D + PAD, Qg, a.sq_l, q0, FQ, a.Lq, D);
+  if (ntiles > 0) {
+    load_rows(&sm.K[0][0][0], D + PAD, Kg, a.sk_l, 0, FK, a.Lk, D);
+    load_rows(&sm.V[0][0][0], DV + PAD, Vg, a.sv_l, 0, FK, a.Lk, DV);
+  }
+  cp_commit();
+
+  constexpr int NO = DV / 8;                          // O n-tiles per warp (all of DV)
+  float o[1][NO][4];
+  zero(o);
+  float m_r[2] = {-INFINITY, -INFINITY}, l_r[2] = {0.f, 0.f};
+  const float sl2 = a.scale * kLog2e;
+  const int r_lo = q0 + warp * 16 + (lane >> 2);       // this thread's two query rows
+  const int rows[2] = {r_lo, r_lo + 8};
+
+  for (int t = 0; t < ntiles; ++t) {
+    const int buf = t & 1;
+    if (t + 1 < ntiles) {
+      load_rows(&sm.K[buf ^ 1][0][0], D + PAD, Kg, a.sk_l, (t + 1) * FK, FK, a.Lk, D);
+      load_rows(&sm.V[buf ^ 1][0][0], DV + PAD, Vg, a.sv_l, (t + 1) * FK, FK, a.Lk, DV);
+    }
+    cp_commit();
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+
+    float s[1][FK / 8][4];
+    zero(s);
+    warp_mma<1, FK / 8, false, false>(s, &sm.Q[0][0], D + PAD, &sm.K[buf][0][0], D + PAD, warp * 16, 0, D);
+
+    // mask, scale to log2 units, running max
+    const int k0 = t * FK;
+    float mx[2] = {m_r[0], m_r[1]};
+#pragma unroll
+    for (int nt = 0; nt < FK / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int kj = k0 + nt * 8 + (lane & 3) * 2 + (e & 1);
+        const int qi = rows[e >> 1];
+        const bool ok = kj < a.Lk && (!a.causal || kj <= qi + offs);
+        const float v = ok ? s[0][nt][e] * sl2 : -INFINITY;
+        s[0][nt][e] = v;
+        mx[e >> 1] = fmaxf(mx[e >> 1], v);
+      }
+    float alpha[2];
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(0xffffffffu, mx[r], 2));
+      alpha[r] = (mx[r] == -INFINITY) ? 1.f : exp2f(m_r[r] - mx[r]);
+      m_r[r] = mx[r];
+    }
+    float ls[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < FK / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float mr = m_r[e >> 1];
+        const float p = (mr == -INFINITY) ? 0.f : exp2f(s[0][nt][e] - mr);
+        s[0][nt][e] = p;
+        ls[e >> 1] += p;
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) l_r[r] = l_r[r] * alpha[r] + ls[r];
+#pragma unroll
+    for (int nt = 0; nt < NO; ++nt) {
+      o[0][nt][0] *= alpha[0]; o[0][nt][1] *= alpha[0];
+      o[0][nt][2] *= alpha[1]; o[0][nt][3] *= alpha[1];
+    }
+    // O += P V: P fragments straight from the S accumulators
+    const int l8 = lane & 7, j = lane >> 3;
+#pragma unroll
+    for (int kk = 0; kk < FK / 16; ++kk) {
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(s[0][2 * kk][0], s[0][2 * kk][1]);
+      pa[1] = pack_bf16x2(s[0][2 * kk][2], s[0][2 * kk][3]);
+      pa[2] = pack_bf16x2(s[0][2 * kk + 1][0], s[0][2 * kk + 1][1]);
+      pa[3] = pack_bf16x2(s[0][2 * kk + 1][2], s[0][2 * kk + 1][3]);
+#pragma unroll
+      for (int nt = 0; nt < NO; nt += 2) {
+        uint32_t bfr[4];
+        ldsm4t(bfr, &sm.V[buf][kk * 16 + l8 + (j & 1) * 8][nt * 8 + (j >> 1) * 8]);
+        mma16816(o[0][nt], pa, bfr[0], bfr[1]);
+        mma16816(o[0][nt + 1], pa, bfr[2], bfr[3]);
+      }
+    }
+    __syncthreads();                                   // buffer reused two tiles on
+  }
+  cp_wait_all();
+
+  // normalise and store
+  float inv[2], lse[2];
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float l = l_r[r];
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    inv[r] = l > 0.f ? 1.f / l : 0.f;
+    lse[r] = l > 0.f ? (m_r[r] + log2f(l)) / kLog2e : -INFINITY;
+  }
+  __nv_bfloat16* Og = reinterpret_cast<__nv_bfloat16*>(a.o) + b * a.so_b + h * a.so_h;
+#pragma unroll
+  for (int nt = 0; nt < NO; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int qi = rows[e >> 1];
+      if (qi < a.Lq) {
+        const int c = nt * 8 + (lane & 3) * 2;
+        *reinterpret_cast<uint32_t*>(Og + (long long)qi * a.so_l + c) =
+            pack_bf16x2(o[0][nt][e] * inv[e >> 1], o[0][nt][e + 1] * inv[e >> 1]);
+      }
+    }
+  if ((lane & 3) == 0) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+      if (rows[r] < a.Lq) a.lse[((long long)b * a.H + h) * a.Lq + rows[r]] = lse[r];
+  }
+}
+
+// ------------------------------------------------------ tcgen05 forward --
+// One CTA per (128 queries, batch * head), 6 warps:
+//   warp 0      TMA: the Q tile once, then K / V tiles of 128 keys into a
+//               two-stage ring;
+//   warp 1      TMEM owner and MMA issuer: S_j = Q K_j^T (M=128, N=128)
+//               into one of two TMEM score buffers, issued one tile ahead,
+//               then O += P_j V_j (M=128, N=D, K=128 keys) into the TMEM
+//               output accumulator;
+//   warps 2-9   softmax, two threads per query row (each half of the key
+//               columns): tcgen05.ld of the score row, running max / sum in
+//               registers (the pair agrees on the max through shared memory),
+//               exponentials on the MUFU ex2 unit, P_j written as bf16 into
+//               shared memory in the 128-byte-swizzled K-major layout the MMA
+//               reads; the output is rescaled in TMEM only when the running
+//               max grows by more than 2^8 (otherwise P is taken against the
+//               stale max, at most 256x larger, harmless in fp32 / bf16).
+// Barriers: q_full, k_full[2] / k_empty[2] and v_full[2] / v_empty[2]
+// (loader <-> MMA; a K stage frees as soon as its score product is done, so
+// K loads run a tile further ahead than V), s_full[2] / s_free[2] (MMA <->
+// softmax), p_full (softmax -> MMA), o_done (MMA -> softmax: P buffer free
+// and O stable).  Every wait is bounded.
+namespace tcfa {
+constexpr int BQ = 128, BKV = 128, THREADS = 320;   // 10 warps
+constexpr float kRescale = 8.f;     // log2 units
+
+template <int D>
+struct Layout {
+  static constexpr int Q_BYTES = BQ * D * 2;      // D/64 K-major chunks of 16 KB
+  static constexpr int K_BYTES = BKV * D * 2;
+  static constexpr int V_BYTES = BKV * D * 2;     // 2 key chunks x D/64 MN-major blocks of 8 KB
+  static constexpr int P_BYTES = BQ * BKV * 2;    // 2 K-major chunks of 16 KB
+  static constexpr int OFF_K = Q_BYTES;
+  static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
+  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+  static constexpr int OFF_BAR = OFF_P + P_BYTES;
+  // at least 120 KB so one CTA holds an SM (and all 512 TMEM columns)
+  // barriers, TMEM slot, then [2][128] row maxima and [2][128] row sums
+  static constexpr int BAR_BYTES = 128 + 2 * 2 * BQ * 4;
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024 > 120 * 1024 ? OFF_BAR + BAR_BYTES + 1024 : 120 * 1024;
+  static constexpr uint32_t TMEM_S = 0, TMEM_O = 256, TMEM_COLS = 512;
+};
+
+struct Params {
+  int Lq, Lk, H, Hk, causal;
+  float sl2;                       // scale * log2(e)
+  void* o;
+  long long so_b, so_h, so_l;
+  float* lse;
+  int* err;
+};
+}  // namespace tcfa
+
+template <int D>
+__global__ void __launch_bounds__(tcfa::THREADS, 1)
+attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+            const __grid_constant__ CUtensorMap mv, const tcfa::Params p) {
+  using namespace tcfa;
+  using Lt = Layout<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sq = sm;
+  uint8_t* sk = sm + Lt::OFF_K;
+  uint8_t* sv = sm + Lt::OFF_V;
+  uint8_t* sp = sm + Lt::OFF_P;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_free = bars + 11;
+  uint64_t* p_full = bars + 13;
+  uint64_t* o_done = bars + 14;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 15);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int qb = blockIdx.x, bh = blockIdx.y;
+  const int b = bh / p.H, h = bh % p.H;
+  const int hk = h / (p.H / p.Hk);
+  const int q0 = qb * BQ;
+  const int offs = p.Lk - p.Lq;
+  const int q_last = min(q0 + BQ, p.Lq) - 1;
+  const int k_end = p.causal ? min(p.Lk, q_last + offs + 1) : p.Lk;
+  const int ntiles = k_end > 0 ? (k_end + BKV - 1) / BKV : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 8);
+    }
+    mbar_init(p_full, 8);
+    mbar_init(o_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mq);
+    tma_prefetch_desc(&mk);
+    tma_prefetch_desc(&mv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Lt::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- loads
+    if (lane == 0 && ntiles > 0) {
+      mbar_arrive_expect_tx(q_full, Lt::Q_BYTES);
+      for (int c = 0; c < D / 64; ++c) tma_load_4d(sq + c * 16384, &mq, q_full, 64 * c, q0, h, b);
+      // order K_0, K_1, V_0, K_2, V_1, ...: K_{j+1} waits for S_{j-1}, V_j for PV_{j-2}
+      auto load_k = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) return false;
+        mbar_arrive_expect_tx(&k_full[s], Lt::K_BYTES);
+        uint8_t* kd = sk + s * Lt::K_BYTES;
+        for (int c = 0; c < D / 64; ++c) tma_load_4d(kd + c * 16384, &mk, &k_full[s], 64 * c, j * BKV, hk, b);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) return false;
+        mbar_arrive_expect_tx(&v_full[s], Lt::V_BYTES);
+        uint8_t* vd = sv + s * Lt::V_BYTES;
+        for (int kc = 0; kc < 2; ++kc)
+          for (int mb = 0; mb < D / 64; ++mb)
+            tma_load_4d(vd + (kc * (D / 64) + mb) * 8192, &mv, &v_full[s], 64 * mb, j * BKV + 64 * kc, hk, b);
+        return true;
+      };
+      bool lok = load_k(0);
+      for (int j = 0; lok && j < ntiles; ++j) {
+        if (j + 1 < ntiles) lok = load_k(j + 1);
+        lok = lok && load_v(j);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA
+    if (lane == 0 && ntiles > 0) {
+      constexpr uint32_t idesc_s = make_idesc_bf16(BQ, BKV, false, false);
+      constexpr uint32_t idesc_o = make_idesc_bf16(BQ, D, false, true);
+      bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrTimeoutMma);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) return false;
+        if (j >= 2 && !mbar_wait(&s_free[s], ((j >> 1) - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) return false;
+        tc_fence_after();
+        const uint32_t d = tmem_base + Lt::TMEM_S + static_cast<uint32_t>(s * BKV);
+        const uint32_t qa = smem_u32(sq), ka = smem_u32(sk + s * Lt::K_BYTES);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(d, make_sw128_desc(qa + c * 16384 + kk * 32, 16, 1024),
+                       make_sw128_desc(ka + c * 16384 + kk * 32, 16, 1024), idesc_s, (c | kk) ? 1u : 0u);
+        tc_commit(&s_full[s]);
+        tc_commit(&k_empty[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (j + 1 < ntiles && !issue_s(j + 1)) break;
+        if (!mbar_wait_spin(p_full, j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        const int s = j & 1;
+        if (!mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d = tmem_base + Lt::TMEM_O;
+        const uint32_t pa = smem_u32(sp), va = smem_u32(sv + s * Lt::V_BYTES);
+#pragma unroll
+        for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(d, make_sw128_desc(pa + kc * 16384 + kk * 32, 16, 1024),
+                       make_sw128_desc(va + kc * (D / 64) * 8192 + kk * 2048, 8192, 1024), idesc_o,
+                       (j > 0 || kc > 0 || kk > 0) ? 1u : 0u);
+        tc_commit(&v_empty[s]);
+        tc_commit(o_done);
+      }
+    }
+  } else {
+    // -------------------------------------------------------------- softmax
+    // 8 warps: the warp pair (w, w + 4) shares TMEM lane quarter w & 3, i.e.
+    // the same 32 query rows, and splits the 128 key columns (and the D
+    // output columns) in halves; the pair agrees on the running max through
+    // shared memory and a named barrier per quarter.
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;
+    const int qi = q0 + row;
+    const uint32_t t_lane = static_cast<uint32_t>(quarter * 32) << 16;
+    float* xmax = reinterpret_cast<float*>(tmem_slot + 2);          // [2][128] partial row maxima
+    float* xsum = xmax + 2 * BQ;                                    // [2][128] partial row sums
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    // a failed (timed-out) wait does not leave the loop: the warp pair must
+    // keep meeting at its named barrier, so the remaining tiles run on
+    // whatever is in the buffers and the error word reports the failure
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j & 1;
+      ok = ok && mbar_wait_spin(&s_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      tc_fence_after();
+      float x[64];
+      const uint32_t sa = tmem_base + t_lane + Lt::TMEM_S + static_cast<uint32_t>(s * BKV + 64 * half);
+      tmem_ld_32x32b_x32(sa, *reinterpret_cast<uint32_t(*)[32]>(&x[0]));
+      tmem_ld_32x32b_x32(sa + 32, *reinterpret_cast<uint32_t(*)[32]>(&x[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[s]);
+      const int k0 = j * BKV + 64 * half;
+      // tiles wholly visible to every row of the CTA skip the per-element mask
+      const bool full = (j * BKV + BKV <= p.Lk) && (!p.causal || j * BKV + BKV - 1 <= q0 + offs);
+      float mt0 = -INFINITY, mt1 = -INFINITY, mt2 = -INFINITY, mt3 = -INFINITY;
+      if (full) {
+#pragma unroll
+        for (int i = 0; i < 64; i += 4) {
+          mt0 = fmaxf(mt0, x[i]); mt1 = fmaxf(mt1, x[i + 1]);
+          mt2 = fmaxf(mt2, x[i + 2]); mt3 = fmaxf(mt3, x[i + 3]);
+        }
+      } else {
+        const int lim = p.causal ? min(p.Lk - 1, qi + offs) : p.Lk - 1;   // last visible key
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+          if (k0 + i > lim) x[i] = -INFINITY;
+          mt0 = fmaxf(mt0, x[i]);
+        }
+      }
+      // raw maxima -> scaled, combined with the partner warp
+      float mt = fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3)) * p.sl2;
+      xmax[half * BQ + row] = mt;
+      asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+      mt = fmaxf(mt, xmax[(half ^ 1) * BQ + row]);
+      const float m_new = fmaxf(m_run, mt);
+      const bool resc = m_new > m_run + kRescale;     // false while the row has seen nothing
+      float alpha = 1.f;
+      if (resc) {
+        alpha = ex2_approx(m_run - m_new);            // 0 when m_run is -inf
+        l_run *= alpha;
+        m_run = m_new;
+      }
+      const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
+      const float sl2 = (m_run == -INFINITY) ? 0.f : p.sl2;
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < 64; i += 2) {
+        x[i] = ex2_approx(fmaf(x[i], sl2, nm));
+        x[i + 1] = ex2_approx(fmaf(x[i + 1], sl2, nm));
+        ls0 += x[i];
+        ls1 += x[i + 1];
+      }
+      if (m_run == -INFINITY) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) x[i] = 0.f;
+        ls0 = ls1 = 0.f;
+      }
+      l_run += ls0 + ls1;
+      // PV_{j-1} must be done before P is overwritten or O rescaled
+      if (j > 0) ok = ok && mbar_wait_spin(o_done, (j - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      if (resc && j > 0) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c) {
+          uint32_t r[32];
+          const uint32_t ta = tmem_base + t_lane + Lt::TMEM_O + static_cast<uint32_t>(half * (D / 2) + 32 * c);
+          tmem_ld_32x32b_x32(ta, r);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
+          tmem_st_32x32b_x32(ta, r);
+        }
+        tmem_st_wait();
+      }
+      // this half's 64 keys are P chunk `half`: bf16, 128-byte-swizzled K-major
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float* v8 = &x[8 * u];
+        const uint4 w = make_uint4(pack_bf16x2(v8[0], v8[1]), pack_bf16x2(v8[2], v8[3]),
+                                   pack_bf16x2(v8[4], v8[5]), pack_bf16x2(v8[6], v8[7]));
+        *reinterpret_cast<uint4*>(sp + half * 16384 + row * 128 + ((u ^ (row & 7)) * 16)) = w;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------------ epilogue
+    xsum[half * BQ + row] = l_run;
+    asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+    const float l_tot = l_run + xsum[(half ^ 1) * BQ + row];
+    __nv_bfloat16* Og = reinterpret_cast<__nv_bfloat16*>(p.o) + b * p.so_b + h * p.so_h;
+    const bool have = ok && ntiles > 0 && mbar_wait(o_done, (ntiles - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+    if (have) tc_fence_after();
+    const float inv = (have && l_tot > 0.f) ? 1.f / l_tot : 0.f;
+#pragma unroll
+    for (int c = 0; c < D / 64; ++c) {
+      uint32_t r[32];
+      const int col = half * (D / 2) + 32 * c;
+      if (have) {
+        tmem_ld_32x32b_x32(tmem_base + t_lane + Lt::TMEM_O + static_cast<uint32_t>(col), r);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = 0u;
+      }
+      if (qi < p.Lq) {
+        __nv_bfloat16* dst = Og + (long long)qi * p.so_l + col;
+#pragma unroll
+        for (int e = 0; e < 32; e += 8) {
+          const float* f = reinterpret_cast<const float*>(&r[e]);
+          *reinterpret_cast<uint4*>(dst + e) =
+              make_uint4(pack_bf16x2(f[0] * inv, f[1] * inv), pack_bf16x2(f[2] * inv, f[3] * inv),
+                         pack_bf16x2(f[4] * inv, f[5] * inv), pack_bf16x2(f[6] * inv, f[7] * inv));
+        }
+      }
+    }
+    if (qi < p.Lq && half == 0)
+      p.lse[((long long)b * p.H + h) * p.Lq + qi] =
+          (have && l_tot > 0.f) ? (m_run + log2f(l_tot)) * 0.6931471805599453f : -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Lt::TMEM_COLS);
+  }
+}
+
+// --------------------------------------------------------------- backward --
+
+constexpr int BKEYS = 64;    // keys per CTA
+constexpr int BQ = 64;       // queries per step
+constexpr int BWARPS = 8;
+
+// delta = rowsum(dO o O), fp32; dq_acc zeroed
+__global__ void attn_bwd_pre(const AttnBwdArgs a) {
+  const long long row = (long long)blockIdx.x * 8 + threadIdx.x / 32;
+  const int lane = threadIdx.x & 31;
+  const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
+  if (row >= rows) return;
+  const int qi = static_cast<int>(row % a.f.Lq);
+  const long long bh = row / a.f.Lq;
+  const int b = static_cast<int>(bh / a.f.H), h = static_cast<int>(bh % a.f.H);
+  const __nv_bfloat16* o = reinterpret_cast<const __nv_bfloat16*>(a.f.o) + b * a.f.so_b + h * a.f.so_h + qi * a.f.so_l;
+  const __nv_bfloat16* d = reinterpret_cast<const __nv_bfloat16*>(a.dO) + b * a.f.so_b + h * a.f.so_h + qi * a.f.so_l;
+  float s = 0.f;
+  for (int c = lane; c < a.f.Dv; c += 32) s += bf2f(o[c]) * bf2f(d[c]);
+  s = warp_sum(s);
+  if (lane == 0) a.delta[row] = s;
+  float* dq = a.dq_acc + row * a.f.D;
+  for (int c = lane; c < a.f.D; c += 32) dq[c] = 0.f;
+}
+
+template <int D, int DV>
+struct BwdSmem {
+  __nv_bfloat16 K[BKEYS][D + PAD];
+  __nv_bfloat16 V[BKEYS][DV + PAD];
+  __nv_bfloat16 Q[BQ][D + PAD];
+  __nv_bfloat16 dO[BQ][DV + PAD];
+  __nv_bfloat16 P[BQ][BKEYS + PAD];
+  __nv_bfloat16 dS[BQ][BKEYS + PAD];
+  float lse[BQ], delta[BQ];
+};
+
+template <int D, int DV>
+__global__ void __launch_bounds__(BWARPS * 32, 1)
+attn_bwd_kernel(const AttnBwdArgs a) {
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  BwdSmem<D, DV>& sm = *reinterpret_cast<BwdSmem<D, DV>*>(smem_raw);
+  const AttnArgs& f = a.f;
+  const int kb = blockIdx.x;
+  const int bhk = blockIdx.y;
+  const int b = bhk / f.Hk, hk = bhk % f.Hk;
+  const int group = f.H / f.Hk;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int k0 = kb * BKEYS;
+  const int offs = f.Lk - f.Lq;
+  const float sl2 = f.scale * kLog2e;
+
+  auto load_rows = [&](__nv_bfloat16* s, int sp, const __nv_bfloat16* g, long long gp, int r0, int nrows, int limit,
+                       int cols) {
+    const int per_row = cols / 8;
+    for (int i = threadIdx.x; i < nrows * per_row; i += blockDim.x) {
+      const int r = i / per_row, c = (i - r * per_row) * 8;
+      if (r0 + r < limit) cp_async16(s + r * sp + c, g + (long long)(r0 + r) * gp + c);
+      else *reinterpret_cast<uint4*>(s + r * sp + c) = make_uint4(0, 0, 0, 0);
+    }
+  };
+  const __nv_bfloat16* Kg = reinterpret_cast<const __nv_bfloat16*>(f.k) + b * f.sk_b + hk * f.sk_h;
+  const __nv_bfloat16* Vg = reinterpret_cast<const __nv_bfloat16*>(f.v) + b * f.sv_b + hk * f.sv_h;
+  load_rows(&sm.K[0][0], D + PAD, Kg, f.sk_l, k0, BKEYS, f.Lk, D);
+  load_rows(&sm.V[0][0], DV + PAD, Vg, f.sv_l, k0, BKEYS, f.Lk, DV);
+  cp_commit();
+
+  // warp tiles: S / dP (64 q x 64 k) as 4 x 2 blocks of 16 x 32;
+  // dK, dV (64 keys x D) as 4 x 2 blocks of 16 x D/2
+  const int sm0 = (warp & 3) * 16, sn0 = (warp >> 2) * 32;
+  constexpr int NK = D / 16, NV = DV / 16;            // n-tiles of the D/2 halves
+  float dk[1][NK][4], dv[1][NV][4];
+  zero(dk);
+  zero(dv);
+  // first query that can see key k0 (causal): qi + offs >= k0
+  const int q_first = f.causal ? max(0, k0 - offs) : 0;
+  const int qb0 = q_first / BQ;
+  const int nqb = (f.Lq + BQ - 1) / BQ;
+
+  for (int hh = 0; hh < group; ++hh) {
+    const int h = hk * group + hh;
+    const __nv_bfloat16* Qg = reinterpret_cast<const __nv_bfloat16*>(f.q) + b * f.sq_b + h * f.sq_h;
+    const __nv_bfloat16* dOg = reinterpret_cast<const __nv_bfloat16*>(a.dO) + b * f.so_b + h * f.so_h;
+    const long long rowbase = ((long long)b * f.H + h) * f.Lq;
+    for (int qb = qb0; qb < nqb; ++qb) {
+      const int q0 = qb * BQ;
+      __syncthreads();                                   // previous step done with Q, dO, P, dS
+      load_rows(&sm.Q[0][0], D + PAD, Qg, f.sq_l, q0, BQ, f.Lq, D);
+      load_rows(&sm.dO[0][0], DV + PAD, dOg, f.so_l, q0, BQ, f.Lq, DV);
+      cp_commit();
+      if (threadIdx.x < BQ) {
+        const int qi = q0 + threadIdx.x;
+        sm.lse[threadIdx.x] = qi < f.Lq ? f.lse[rowbase + qi] : INFINITY;
+        sm.delta[threadIdx.x] = qi < f.Lq ? a.delta[rowbase + qi] : 0.f;
+      }
+      cp_wait_all();
+      __syncthreads();
+      // S and dP blocks; P = exp(S - lse) (masked), dS = P (dP - delta)
+      float s[1][4][4], dp[1][4][4];
+      zero(s);
+      zero(dp);
+      warp_mma<1, 4, false, false>(s, &sm.Q[0][0], D + PAD, &sm.K[0][0], D + PAD, sm0, sn0, D);
+      warp_mma<1, 4, false, false>(dp, &sm.dO[0][0], DV + PAD, &sm.V[0][0], DV + PAD, sm0, sn0, DV);
+#pragma unroll
+      for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; e += 2) {
+          const int r = sm0 + frag_row(0, e), c = sn0 + frag_col(nt, e);
+          const int qi = q0 + r;
+          float pv[2], dsv[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int kj = k0 + c + u;
+            const bool ok = qi < f.Lq && kj < f.Lk && (!f.causal || kj <= qi + offs);
+            const float p = ok ? exp2f(s[0][nt][e + u] * sl2 - sm.lse[r] * kLog2e) : 0.f;
+            pv[u] = p;
+            dsv[u] = p * (dp[0][nt][e + u] - sm.delta[r]);
+          }
+          *reinterpret_cast<uint32_t*>(&sm.P[r][c]) = pack_bf16x2(pv[0], pv[1]);
+          *reinterpret_cast<uint32_t*>(&sm.dS[r][c]) = pack_bf16x2(dsv[0], dsv[1]);
+        }
+      __syncthreads();
+      // dV += P^T dO, dK += dS^T Q   (rows = keys sm0.., columns = half of D)
+      warp_mma<1, NV, true, true>(dv, &sm.P[0][0], BKEYS + PAD, &sm.dO[0][0], DV + PAD, sm0, (warp >> 2) * (DV / 2), BQ);
+      warp_mma<1, NK, true, true>(dk, &sm.dS[0][0], BKEYS + PAD, &sm.Q[0][0], D + PAD, sm0, (warp >> 2) * (D / 2), BQ);
+      // dQ += dS K  (rows = queries sm0.., columns = half of D), fp32 atomics
+      {
+        float dq[1][NK][4];
+        zero(dq);
+        warp_mma<1, NK, false, true>(dq, &sm.dS[0][0], BKEYS + PAD, &sm.K[0][0], D + PAD, sm0, (warp >> 2) * (D / 2),
+                                     BKEYS);
+#pragma unroll
+        for (int nt = 0; nt < NK; ++nt)
+#pragma unroll
+          for (int e = 0; e < 4; e += 2) {
+            const int r = sm0 + frag_row(0, e), c = (warp >> 2) * (D / 2) + frag_col(nt, e);
+            const int qi = q0 + r;
+            if (qi < f.Lq)
+              atomicAdd(reinterpret_cast<float2*>(a.dq_acc + (rowbase + qi) * D + c),
+                        make_float2(dq[0][nt][e], dq[0][nt][e + 1]));
+          }
+      }
+    }
+  }
+  cp_wait_all();                                       // K / V copies (no query block ran)
+  // dK (scaled), dV out
+  __nv_bfloat16* dKg = reinterpret_cast<__nv_bfloat16*>(a.dk) + ((long long)b * f.Hk + hk) * f.Lk * D;
+  __nv_bfloat16* dVg = reinterpret_cast<__nv_bfloat16*>(a.dv) + ((long long)b * f.Hk + hk) * f.Lk * DV;
+#pragma unroll
+  for (int nt = 0; nt < NK; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int r = sm0 + frag_row(0, e), c = (warp >> 2) * (D / 2) + frag_col(nt, e);
+      if (k0 + r < f.Lk)
+        *reinterpret_cast<uint32_t*>(dKg + (long long)(k0 + r) * D + c) =
+            pack_bf16x2(f.scale * dk[0][nt][e], f.scale * dk[0][nt][e + 1]);
+    }
+#pragma unroll
+  for (int nt = 0; nt < NV; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int r = sm0 + frag_row(0, e), c = (warp >> 2) * (DV / 2) + frag_col(nt, e);
+      if (k0 + r < f.Lk)
+        *reinterpret_cast<uint32_t*>(dVg + (long long)(k0 + r) * DV + c) = pack_bf16x2(dv[0][nt][e], dv[0][nt][e + 1]);
+    }
+}
+
+// dq = scale * dq_acc (bf16)
+__global__ void attn_bwd_post(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, long long n, float scale) {
+  const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (i >= n) return;
+  const float4 v = *reinterpret_cast<const float4*>(acc + i);
+  *reinterpret_cast<uint2*>(dq + i) = make_uint2(pack_bf16x2(scale * v.x, scale * v.y), pack_bf16x2(scale * v.z, scale * v.w));
+}
+
+template <typename Kern>
+bool set_smem(Kern kern, size_t bytes) {
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) ==
+         cudaSuccess;
+}
+
+template <int D>
+int launch_fwd_tc(const AttnArgs& a, cudaStream_t st) {
+  using Lt = tcfa::Layout<D>;
+  alignas(64) unsigned char mq[128], mk[128], mv[128];
+  const unsigned long long dq[4] = {(unsigned long long)D, (unsigned long long)a.Lq, (unsigned long long)a.H,
+                                    (unsigned long long)a.B};
+  const unsigned long long sq[3] = {(unsigned long long)a.sq_l * 2, (unsigned long long)a.sq_h * 2,
+                                    (unsigned long long)a.sq_b * 2};
+  const unsigned long long dk[4] = {(unsigned long long)D, (unsigned long long)a.Lk, (unsigned long long)a.Hk,
+                                    (unsigned long long)a.B};
+  const unsigned long long sk[3] = {(unsigned long long)a.sk_l * 2, (unsigned long long)a.sk_h * 2,
+                                    (unsigned long long)a.sk_b * 2};
+  const unsigned long long dv[4] = {(unsigned long long)D, (unsigned long long)a.Lk, (unsigned long long)a.Hk,
+                                    (unsigned long long)a.B};
+  const unsigned long long sv[3] = {(unsigned long long)a.sv_l * 2, (unsigned long long)a.sv_h * 2,
+                                    (unsigned long long)a.sv_b * 2};
+  const unsigned box_qk[4] = {64u, 128u, 1u, 1u}, box_v[4] = {64u, 64u, 1u, 1u};
+  if (!encode_bf16_map(mq, a.q, 4, dq, sq, box_qk) || !encode_bf16_map(mk, a.k, 4, dk, sk, box_qk) ||
+      !encode_bf16_map(mv, a.v, 4, dv, sv, box_v))
+    return 2;
+  tcfa::Params p;
+  p.Lq = a.Lq; p.Lk = a.Lk; p.H = a.H; p.Hk = a.Hk; p.causal = a.causal;
+  p.sl2 = a.scale * kLog2e;
+  p.o = a.o; p.so_b = a.so_b; p.so_h = a.so_h; p.so_l = a.so_l;
+  p.lse = a.lse;
+  p.err = a.err;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(attn_fwd_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess)
+      return 3;
+    attr_set[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((a.Lq + tcfa::BQ - 1) / tcfa::BQ), static_cast<unsigned>(a.B * a.H));
+  attn_fwd_tc<D><<<grid, tcfa::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
+                                                         *reinterpret_cast<const CUtensorMap*>(mk),
+                                                         *reinterpret_cast<const CUtensorMap*>(mv), p);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+template <int D, int DV>
+int launch_fwd(const AttnArgs& a, cudaStream_t st) {
+  const size_t sm = sizeof(FwdSmem<D, DV>);
+  if (!set_smem(attn_fwd_kernel<D, DV>, sm)) return 3;
+  dim3 grid(static_cast<unsigned>((a.Lq + FQ - 1) / FQ), static_cast<unsigned>(a.B * a.H));
+  attn_fwd_kernel<D, DV><<<grid, FWARPS * 32, sm, st>>>(a);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+template <int D, int DV>
+int launch_bwd(const AttnBwdArgs& a, cudaStream_t st) {
+  const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
+  attn_bwd_pre<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+  const size_t sm = sizeof(BwdSmem<D, DV>);
+  if (!set_smem(attn_bwd_kernel<D, DV>, sm)) return 3;
+  dim3 grid(static_cast<unsigned>((a.f.Lk + BKEYS - 1) / BKEYS), static_cast<unsigned>(a.f.B * a.f.Hk));
+  attn_bwd_kernel<D, DV><<<grid, BWARPS * 32, sm, st>>>(a);
+  const long long n = rows * a.f.D;
+  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a.dq_acc, (__nv_bfloat16*)a.dq, n,
+                                                                              a.f.scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool strides_ok(const AttnArgs& a) {
+  // 16-byte rows for cp.async; heads must split evenly for GQA
+  const long long s[] = {a.sq_b, a.sq_h, a.sq_l, a.sk_b, a.sk_h, a.sk_l, a.sv_b, a.sv_h, a.sv_l, a.so_b, a.so_h, a.so_l};
+  for (long long v : s)
+    if (v % 8) return false;
+  return aligned16(a.q) && aligned16(a.k) && aligned16(a.v) && aligned16(a.o) && a.Hk > 0 && a.H % a.Hk == 0;
+}
+
+}  // namespace
+
+int attn_fwd(const AttnArgs& a, cudaStream_t st) {
+  if (!strides_ok(a) || a.Lq <= 0 || a.Lk <= 0) return 5;
+  // tensor-core path: every TMA box (128 rows) fits inside its tensor
+  static const bool no_tc = std::getenv("VAGUS_ATTN_NO_TC") != nullptr;
+  if (!no_tc && a.err && a.Lq >= 128 && a.Lk >= 128 && a.D == a.Dv && (a.D == 64 || a.D == 128))
+    return a.D == 64 ? launch_fwd_tc<64>(a, st) : launch_fwd_tc<128>(a, st);
+  if (a.D == 64 && a.Dv == 64) return launch_fwd<64, 64>(a, st);
+  if (a.D == 128 && a.Dv == 128) return launch_fwd<128, 128>(a, st);
+  if (a.D == 64 && a.Dv == 128) return launch_fwd<64, 128>(a, st);
+  return 5;
+}
+
+int attn_bwd(const AttnBwdArgs& a, cudaStream_t st) {
+  if (!strides_ok(a.f) || !aligned16(a.dO) || a.f.Lq <= 0 || a.f.Lk <= 0) return 5;
+  if (a.f.D == 64 && a.f.Dv == 64) return launch_bwd<64, 64>(a, st);
+  if (a.f.D == 128 && a.f.Dv == 128) return launch_bwd<128, 128>(a, st);
+  if (a.f.D == 64 && a.f.Dv == 128) return launch_bwd<64, 128>(a, st);
+  return 5;
+}
+
+}  // namespace vagus

@@ -1,0 +1,73 @@
+// Bindings of the flash-attention kernels (attention.cu).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "kernels.h"
+
+int* vagus_device_error_ptr();   // bindings.cpp
+
+namespace {
+
+using torch::Tensor;
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check(int rc, const char* what) {
+  TORCH_CHECK(rc == 0, "vagus_b200 kernel '", what, "' rejected the problem or failed to launch (code ", rc, ")");
+}
+
+vagus::AttnArgs make_args(const Tensor& q, const Tensor& k, const Tensor& v, const Tensor& o, const Tensor& lse,
+                          bool causal, double scale) {
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "attention: (B, H, L, D) tensors");
+  for (const Tensor* t : {&q, &k, &v, &o})
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->stride(3) == 1, "attention: bf16 with unit inner stride");
+  vagus::AttnArgs a;
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.o = o.data_ptr();
+  a.lse = lse.data_ptr<float>();
+  a.B = q.size(0); a.H = static_cast<int>(q.size(1)); a.Hk = static_cast<int>(k.size(1));
+  a.Lq = static_cast<int>(q.size(2)); a.Lk = static_cast<int>(k.size(2));
+  a.D = static_cast<int>(q.size(3)); a.Dv = static_cast<int>(v.size(3));
+  a.sq_b = q.stride(0); a.sq_h = q.stride(1); a.sq_l = q.stride(2);
+  a.sk_b = k.stride(0); a.sk_h = k.stride(1); a.sk_l = k.stride(2);
+  a.sv_b = v.stride(0); a.sv_h = v.stride(1); a.sv_l = v.stride(2);
+  a.so_b = o.stride(0); a.so_h = o.stride(1); a.so_l = o.stride(2);
+  a.causal = causal ? 1 : 0;
+  a.scale = static_cast<float>(scale);
+  a.err = vagus_device_error_ptr();
+  return a;
+}
+
+// q (B, H, Lq, D), k (B, Hk, Lk, D), v (B, Hk, Lk, Dv) -> o (B, H, Lq, Dv), lse (B, H, Lq)
+std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double scale) {
+  auto o = torch::empty({q.size(0), q.size(1), q.size(2), v.size(3)}, q.options());
+  auto lse = torch::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat));
+  auto a = make_args(q, k, v, o, lse, causal, scale);
+  check(vagus::attn_fwd(a, stream()), "attn_fwd");
+  return {o, lse};
+}
+
+// o and dO contiguous (as attn_fwd returns them) -> dq, dk, dv contiguous
+std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, Tensor dO, bool causal,
+                             double scale) {
+  TORCH_CHECK(o.is_contiguous() && dO.is_contiguous() && lse.is_contiguous(), "attn_bwd: contiguous o, dO, lse");
+  auto a = make_args(q, k, v, o, lse, causal, scale);
+  vagus::AttnBwdArgs b;
+  b.f = a;
+  b.dO = dO.data_ptr();
+  auto dq = torch::empty({q.size(0), q.size(1), q.size(2), q.size(3)}, q.options());
+  auto dk = torch::empty({k.size(0), k.size(1), k.size(2), k.size(3)}, k.options());
+  auto dv = torch::empty({v.size(0), v.size(1), v.size(2), v.size(3)}, v.options());
+  auto dq_acc = torch::empty({q.size(0), q.size(1), q.size(2), q.size(3)}, q.options().dtype(at::kFloat));
+  auto delta = torch::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat));
+  b.dq = dq.data_ptr(); b.dk = dk.data_ptr(); b.dv = dv.data_ptr();
+  b.dq_acc = dq_acc.data_ptr<float>(); b.delta = delta.data_ptr<float>();
+  check(vagus::attn_bwd(b, stream()), "attn_bwd");
+  return {dq, dk, dv};
+}
+
+}  // namespace
+
+void register_attn_ops(pybind11::module& m) {
+  m.def("attn_fwd", &attn_fwd);
+  m.def("attn_bwd", &attn_bwd);
+}

@@ -29,7 +29,10 @@ void need_bf16_or_f32(const Tensor& t, const char* n) {
 int* g_err_host[64] = {nullptr};
 int* g_err_dev[64] = {nullptr};
 
-int* err_ptr() {
+}  // namespace
+
+// Device pointer of this device's error word (shared with the other binding units).
+int* vagus_device_error_ptr() {
   int dev = 0;
   cudaGetDevice(&dev);
   if (!g_err_host[dev]) {
@@ -43,6 +46,10 @@ int* err_ptr() {
   }
   return g_err_dev[dev];
 }
+
+namespace {
+
+int* err_ptr() { return vagus_device_error_ptr(); }
 
 int error_word() {
   int dev = 0;
@@ -286,7 +293,8 @@ void muon_momentum(Tensor g, Tensor buf, Tensor upd, double mu, bool nesterov, d
 
 }  // namespace
 
-void register_seq_ops(pybind11::module& m);   // bind_seq.cpp: conv, gates, gdr, attention
+void register_seq_ops(pybind11::module& m);   // bind_seq.cpp: conv, gates, gdr
+void register_attn_ops(pybind11::module& m);  // bind_attn.cpp: flash attention
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vagus_b200 sm_100a kernels";
@@ -311,6 +319,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &adamw_step);
   m.def("muon_momentum", &muon_momentum);
   register_seq_ops(m);
+  register_attn_ops(m);
 }
 
 // the error-word accessor shared with bind_seq.cpp

@@ -71,6 +71,32 @@ __device__ __forceinline__ float warp_max(float v) {
 // should (1 + e^-x = inf gives 0)
 __device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 __device__ __forceinline__ float sigmoid_f(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// 2^x on the MUFU unit (flush-to-zero; -inf -> 0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+// 2^x on the FMA / integer pipes, for splitting exponential work with the
+// MUFU unit: Cody-Waite style split x = n + f (n = round(x) through the
+// 1.5 * 2^23 rounding constant, f in [-0.5, 0.5]), 2^f by its Taylor series
+// e^(f ln 2) = sum_k (f ln 2)^k / k! to degree 4 (relative error < 5e-5 on
+// the interval), and 2^n added into the exponent bits.  Inputs below -125
+// are clamped there (the result is < 1e-37).
+__device__ __forceinline__ float ex2_poly(float x) {
+  constexpr float c1 = 0.6931471805599453f;      // ln2
+  constexpr float c2 = 0.2402265069591007f;      // ln2^2 / 2
+  constexpr float c3 = 0.0555041086648216f;      // ln2^3 / 6
+  constexpr float c4 = 0.0096181291076285f;      // ln2^4 / 24
+  constexpr float kRound = 12582912.f;           // 1.5 * 2^23
+  x = fmaxf(x, -125.f);
+  const float t = x + kRound;
+  const int n = __float_as_int(t) - __float_as_int(kRound);
+  const float f = x - (t - kRound);
+  const float q = fmaf(fmaf(fmaf(fmaf(c4, f, c3), f, c2), f, c1), f, 1.f);
+  return __int_as_float(__float_as_int(q) + (n << 23));
+}
+
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // ------------------------------------------------------------ smem addr --
@@ -113,6 +139,38 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.b32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded busy wait without the suspend of try_wait: for short hand-offs on
+// the critical path between warps of one CTA.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                               int code) {
+  if (mbar_test_wait(bar, parity)) return true;
+  unsigned long long t0 = globaltimer_ns();
+  uint32_t spins = 0;
+  while (true) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if (((++spins) & 1023u) == 0u) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > kWaitBudgetNs) {
+        *abort = 1;
+        record_error(err, code);
+        return false;
+      }
+    }
+  }
+}
+
 // Bounded wait.  Returns false (after recording `code`) when the budget runs
 // out or another thread of the CTA already aborted (`*abort` != 0).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
@@ -144,6 +202,16 @@ __device__ __forceinline__ void tma_load_3d(void* smem_dst, const CUtensorMap* m
       "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+// Tiled 4-D bulk-tensor load into this CTA's own shared memory.
+__device__ __forceinline__ void tma_load_4d(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1,
+                                            int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
       : "memory");
 }
 
@@ -208,6 +276,26 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// 32 registers -> 32 lanes x 32 consecutive columns (the inverse of the load).
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0],"
+      " {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16,"
+      " %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};"
+      ::"r"(taddr), "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+        "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+        "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]),
+        "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// generic-proxy shared-memory writes -> visible to the async proxy (tcgen05.mma operands)
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
 
 // ------------------------------------------------- CTA pairs (cta_group::2) --
 // A cluster of two CTAs on neighbouring SMs shares one tcgen05.mma of M = 256:

@@ -27,4 +27,10 @@ struct GemmArgs {
 // Returns 0 on launch, nonzero on argument / encode / launch failure.
 int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 
+// bf16 tiled tensor map with 128-byte swizzle (the driver's tiled encoder):
+// `map` points at a 128-byte CUtensorMap; dims and box in elements
+// (innermost first), strides in bytes for dims 1..rank-1.  False on failure.
+bool encode_bf16_map(void* map, const void* base, int rank, const unsigned long long* dims,
+                     const unsigned long long* strides, const unsigned* box);
+
 }  // namespace vagus

@@ -112,6 +112,7 @@ struct AttnArgs {
   long long B; int H, Hk, Lq, Lk, D, Dv;
   long long sq_b, sq_h, sq_l, sk_b, sk_h, sk_l, sv_b, sv_h, sv_l, so_b, so_h, so_l;   // element strides
   int causal; float scale;
+  int* err = nullptr;                           // device error word (bounded waits of the tcgen05 path)
 };
 int attn_fwd(const AttnArgs& a, cudaStream_t st);
 struct AttnBwdArgs {
