@@ -264,7 +264,7 @@ def run(args) -> dict:
         if is_dist:
             mesh = build_mesh(world, dev, world)
             model = LMLoss(model, ce)
-            apply_fsdp(model, mesh)
+            apply_fsdp(model, mesh, comm=args.comm)
         optimizer = build_optimizer(opt_name, unwrap(model), json.loads(json.dumps(opt_args)))
         runner = StepRunner(model, optimizer, ce, dev, grad_accum_steps=accum, grad_clip=1.0, is_fsdp=is_dist,
                             is_dist=is_dist, mesh=mesh)
@@ -339,6 +339,7 @@ def run(args) -> dict:
         "config": {"model": cfg["label"], "global_batch": cfg["global_tokens"], "seq_len": seq,
                    "micro_batch": micro, "grad_accum": accum,
                    "parallelism": f"fsdp{world}" if world > 1 else "single",
+                   "collectives": ("nccl" if args.impl == "reference" else args.comm) if world > 1 else None,
                    "optimizer": opt_name, "l2": "no flush: every step's working set is >> 126 MB L2"},
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 4},
@@ -357,6 +358,8 @@ def run(args) -> dict:
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--comm", default="nvlink", choices=["nvlink", "nccl"],
+                    help="FSDP2 collectives of our arm: NVLink peer-to-peer kernels or NCCL")
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")

@@ -1,0 +1,106 @@
+"""NVLink peer-to-peer collectives (ops/csrc/comm.cu) against NCCL, on two
+GPUs: raw all-gather / reduce-scatter over several epochs (slot reuse), and
+FSDP2 with the custom collectives installed against FSDP2 on NCCL."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+        torch.cuda.set_device(rank)
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{rank}"),
+                                timeout=datetime.timedelta(seconds=120))
+        from vagus_b200 import ops
+        from vagus_b200.parallel.nvlink import NvlinkAllGather, NvlinkHeap, NvlinkReduceScatter
+        heap = NvlinkHeap(dist.group.WORLD, ag_cap=1 << 20, rs_cap=4 << 20)
+        ag, rs = NvlinkAllGather(heap), NvlinkReduceScatter(heap)
+        errs = []
+        for it in range(5):
+            g = torch.Generator(device="cuda").manual_seed(100 * it + rank)
+            n = 1000 + 37 * it
+            shard = torch.randn(n, device="cuda", generator=g).bfloat16()
+            out = torch.empty(world * n, device="cuda", dtype=torch.bfloat16)
+            out[rank * n:(rank + 1) * n].copy_(shard)
+            ag(out, out[rank * n:(rank + 1) * n], dist.group.WORLD)
+            ref = torch.empty_like(out)
+            dist.all_gather_into_tensor(ref, shard)
+            errs.append(("ag", it, (out.float() - ref.float()).abs().max().item()))
+            full = torch.randn(world * n, device="cuda", generator=g)
+            for op in (dist.ReduceOp.AVG, dist.ReduceOp.SUM):
+                o = torch.empty(n, device="cuda")
+                rs(o, full, dist.group.WORLD, op)
+                r = torch.empty(n, device="cuda")
+                dist.reduce_scatter_tensor(r, full.clone(), op=op)
+                errs.append(("rs", it, (o - r).abs().max().item()))
+        torch.cuda.synchronize()
+        errs.append(("error_word", 0, float(ops.native().error_word())))
+
+        # FSDP2 with the NVLink collectives == FSDP2 on NCCL
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.fsdp import fully_shard
+        from vagus_b200.parallel.nvlink import use_nvlink_collectives
+        mesh = init_device_mesh("cuda", (world,))
+
+        def make():
+            torch.manual_seed(0)
+            m = torch.nn.Sequential(torch.nn.Linear(256, 512, bias=False), torch.nn.GELU(),
+                                    torch.nn.Linear(512, 256, bias=False)).cuda()
+            for layer in m:
+                if isinstance(layer, torch.nn.Linear):
+                    fully_shard(layer, mesh=mesh)
+            fully_shard(m, mesh=mesh)
+            return m
+
+        grads = []
+        for nv in (False, True):
+            m = make()
+            if nv:
+                use_nvlink_collectives(m)
+            x = torch.randn(64, 256, device="cuda", generator=torch.Generator(device="cuda").manual_seed(rank))
+            m(x).pow(2).mean().backward()
+            grads.append([p.grad.full_tensor() for p in m.parameters()])
+        for a, b in zip(*grads):
+            errs.append(("fsdp", 0, (a - b).abs().max().item()))
+        heap.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, errs))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nvlink_collectives_match_nccl():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs in results:
+        assert not isinstance(errs, str), f"rank {rank}: {errs}"
+        for kind, it, e in errs:
+            tol = 0.0 if kind in ("ag", "error_word") else 1e-5
+            assert e <= tol, (rank, kind, it, e)

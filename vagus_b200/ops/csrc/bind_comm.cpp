@@ -1,0 +1,89 @@
+// Bindings of the NVLink peer-to-peer collectives (comm.cu): heap creation
+// and CUDA-IPC sharing, and the all-gather / reduce-scatter launches.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <string>
+
+#include "kernels.h"
+
+int* vagus_device_error_ptr();   // bindings.cpp
+
+namespace {
+
+using torch::Tensor;
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Allocates this rank's heap (zeroed) and returns (device pointer, IPC handle bytes).
+std::tuple<int64_t, pybind11::bytes> comm_heap_create(int64_t bytes) {
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, static_cast<size_t>(bytes)) == cudaSuccess, "comm heap: cudaMalloc failed");
+  TORCH_CHECK(cudaMemset(p, 0, static_cast<size_t>(bytes)) == cudaSuccess, "comm heap: cudaMemset failed");
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(cudaIpcGetMemHandle(&h, p) == cudaSuccess, "comm heap: cudaIpcGetMemHandle failed");
+  return {reinterpret_cast<int64_t>(p), pybind11::bytes(reinterpret_cast<const char*>(&h), sizeof(h))};
+}
+
+// Maps a peer's heap into this process.
+int64_t comm_heap_open(pybind11::bytes handle) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "comm heap: bad IPC handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, s.data(), sizeof(h));
+  void* p = nullptr;
+  TORCH_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess,
+              "comm heap: cudaIpcOpenMemHandle failed");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void comm_heap_close(int64_t ptr, bool own) {
+  if (own) cudaFree(reinterpret_cast<void*>(ptr));
+  else cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr));
+}
+
+vagus::CommPeers peers_of(const std::vector<int64_t>& bases) {
+  TORCH_CHECK(bases.size() >= 2 && bases.size() <= static_cast<size_t>(vagus::kMaxCommPeers), "comm: world size");
+  vagus::CommPeers pr;
+  for (int i = 0; i < vagus::kMaxCommPeers; ++i)
+    pr.base[i] = i < static_cast<int>(bases.size()) ? reinterpret_cast<unsigned char*>(bases[i]) : nullptr;
+  return pr;
+}
+
+// out (world * n elements, this rank's shard already at [rank * n, rank * n + n))
+void comm_all_gather(Tensor out, std::vector<int64_t> bases, int64_t rank, int64_t epoch, int64_t slot_cap) {
+  TORCH_CHECK(out.is_contiguous(), "comm_all_gather: contiguous output");
+  const int world = static_cast<int>(bases.size());
+  const long long total = out.numel() * out.element_size();
+  TORCH_CHECK(total % world == 0, "comm_all_gather: output must split evenly");
+  const int rc = vagus::comm_all_gather(peers_of(bases), static_cast<int>(rank), world, static_cast<unsigned>(epoch),
+                                        out.data_ptr(), total / world, slot_cap, vagus_device_error_ptr(), stream());
+  TORCH_CHECK(rc == 0, "comm_all_gather failed (code ", rc, ")");
+}
+
+// in (world * n), out (n), same dtype (fp32 or bf16): out = scale * sum_r in_r[rank * n : rank * n + n]
+void comm_reduce_scatter(Tensor out, Tensor in, std::vector<int64_t> bases, int64_t rank, int64_t epoch,
+                         double scale, int64_t ag_cap, int64_t slot_cap) {
+  TORCH_CHECK(in.is_contiguous() && out.is_contiguous() && in.scalar_type() == out.scalar_type(),
+              "comm_reduce_scatter: contiguous tensors of one dtype");
+  TORCH_CHECK(in.scalar_type() == at::kFloat || in.scalar_type() == at::kBFloat16, "comm_reduce_scatter: fp32 / bf16");
+  const int world = static_cast<int>(bases.size());
+  TORCH_CHECK(in.numel() == out.numel() * world, "comm_reduce_scatter: sizes");
+  const int rc = vagus::comm_reduce_scatter(peers_of(bases), static_cast<int>(rank), world,
+                                            static_cast<unsigned>(epoch), in.data_ptr(), out.data_ptr(), out.numel(),
+                                            static_cast<int>(in.element_size()), static_cast<float>(scale), ag_cap,
+                                            slot_cap, vagus_device_error_ptr(), stream());
+  TORCH_CHECK(rc == 0, "comm_reduce_scatter failed (code ", rc, ")");
+}
+
+}  // namespace
+
+void register_comm_ops(pybind11::module& m) {
+  m.def("comm_heap_create", &comm_heap_create);
+  m.def("comm_heap_open", &comm_heap_open);
+  m.def("comm_heap_close", &comm_heap_close);
+  m.def("comm_all_gather", &comm_all_gather);
+  m.def("comm_reduce_scatter", &comm_reduce_scatter);
+}

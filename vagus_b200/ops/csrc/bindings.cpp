@@ -295,6 +295,7 @@ void muon_momentum(Tensor g, Tensor buf, Tensor upd, double mu, bool nesterov, d
 
 void register_seq_ops(pybind11::module& m);   // bind_seq.cpp: conv, gates, gdr
 void register_attn_ops(pybind11::module& m);  // bind_attn.cpp: flash attention
+void register_comm_ops(pybind11::module& m);  // bind_comm.cpp: NVLink peer-to-peer collectives
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vagus_b200 sm_100a kernels";
@@ -320,6 +321,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("muon_momentum", &muon_momentum);
   register_seq_ops(m);
   register_attn_ops(m);
+  register_comm_ops(m);
 }
 
 // the error-word accessor shared with bind_seq.cpp

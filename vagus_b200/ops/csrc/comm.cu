@@ -1,0 +1,171 @@
+// NVLink peer-to-peer collectives for the FSDP2 parameter all-gather and the
+// gradient reduce-scatter, as our own kernels instead of NCCL calls.
+//
+// Every rank owns one device "heap" (plain cudaMalloc, shared through CUDA
+// IPC; no multicast objects) laid out as
+//   [AG flags: 64 x u32][RS flags: 64 x u32][pad to 1 KB][AG slot 0][AG slot 1][RS slot 0][RS slot 1]
+// and holds the device pointers of every peer's heap.  A collective of epoch
+// e (a per-kind counter that advances identically on every rank, since FSDP
+// issues its all-gathers and its reduce-scatters in the same order
+// everywhere) uses slot e & 1:
+//   1. stage:   this rank's contribution -> its own slot (local copy);
+//   2. barrier: publish the copy (system-scope release), store e into every
+//               peer's flag word for this rank, then wait until every peer's
+//               flag in this heap reads >= e (acquire; bounded by a 2 s
+//               budget, after which the error word is set and the kernel
+//               returns);
+//   3. combine: all-gather copies each peer's slot into its place in the
+//               output; reduce-scatter sums this rank's rows of every peer's
+//               slot in fp32, scales (1/world for an average) and casts into
+//               the output shard.
+// A slot is rewritten two epochs later; by then every peer has passed the
+// barrier of the epoch in between, which it reaches only after finishing its
+// reads of the slot, so two slots need no second barrier per call.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cstdint>
+
+namespace vagus {
+namespace {
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// byte copy with 16-byte vectors for the aligned body
+__device__ __forceinline__ void copy_bytes(uint8_t* dst, const uint8_t* src, long long n, long long tid,
+                                           long long nthreads) {
+  const bool al = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15u) == 0;
+  long long body = al ? (n / 16) * 16 : 0;
+  for (long long i = tid * 16; i < body; i += nthreads * 16)
+    *reinterpret_cast<uint4*>(dst + i) = *reinterpret_cast<const uint4*>(src + i);
+  for (long long i = body + tid; i < n; i += nthreads) dst[i] = src[i];
+}
+
+__global__ void stage_k(uint8_t* slot, const uint8_t* src, long long n) {
+  copy_bytes(slot, src, n, (long long)blockIdx.x * blockDim.x + threadIdx.x, (long long)gridDim.x * blockDim.x);
+}
+
+// one warp: lane p < world signals peer p and waits for peer p's flag
+__global__ void barrier_k(const CommPeers peers, int rank, int world, int flag_off, uint32_t epoch, int* err) {
+  const int lane = threadIdx.x;
+  __threadfence_system();          // the staging copy (previous kernel) is visible system-wide
+  if (lane < world) {
+    uint32_t* remote = reinterpret_cast<uint32_t*>(peers.base[lane] + flag_off) + rank;
+    st_release_sys(remote, epoch);
+  }
+  bool ok = true;
+  if (lane < world) {
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(peers.base[rank] + flag_off) + lane;
+    if (ld_acquire_sys(mine) < epoch) {
+      const unsigned long long t0 = globaltimer_ns();
+      uint32_t spins = 0;
+      while (ld_acquire_sys(mine) < epoch) {
+        if (((++spins) & 1023u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) {
+          ok = false;
+          break;
+        }
+      }
+    }
+  }
+  if (!ok) record_error(err, kErrTimeoutPeer);
+  __syncwarp();
+  __threadfence_system();
+}
+
+__global__ void gather_k(const CommPeers peers, int rank, int world, long long slot_off, uint8_t* out,
+                         long long n) {
+  // blockIdx.y = source rank
+  const int src = blockIdx.y;
+  if (src == rank) return;         // already in place
+  copy_bytes(out + (long long)src * n, peers.base[src] + slot_off, n, (long long)blockIdx.x * blockDim.x + threadIdx.x,
+             (long long)gridDim.x * blockDim.x);
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return bf2f(v); }
+
+template <typename T>
+__global__ void reduce_k(const CommPeers peers, int rank, int world, long long slot_off, T* out, long long n,
+                         float scale) {
+  // this rank's rows [rank * n, rank * n + n) of every peer's slot
+  const long long stride = (long long)gridDim.x * blockDim.x;
+  const long long t0 = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if constexpr (sizeof(T) == 4) {
+    if ((n & 3) == 0) {
+      for (long long i = t0 * 4; i < n; i += stride * 4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = 0; p < world; ++p) {
+          const float* s = reinterpret_cast<const float*>(peers.base[p] + slot_off) + (long long)rank * n + i;
+          const float4 v = *reinterpret_cast<const float4*>(s);
+          acc.x += v.x; acc.y += v.y; acc.z += v.z; acc.w += v.w;
+        }
+        *reinterpret_cast<float4*>(out + i) =
+            make_float4(scale * acc.x, scale * acc.y, scale * acc.z, scale * acc.w);
+      }
+      return;
+    }
+  }
+  for (long long i = t0; i < n; i += stride) {
+    float acc = 0.f;
+    for (int p = 0; p < world; ++p) {
+      const T* s = reinterpret_cast<const T*>(peers.base[p] + slot_off) + (long long)rank * n + i;
+      acc += to_f<T>(*s);
+    }
+    if constexpr (sizeof(T) == 4) out[i] = scale * acc;
+    else out[i] = f2bf(scale * acc);
+  }
+}
+
+int grid_for(long long bytes) {
+  long long b = (bytes / 16 + 255) / 256;
+  if (b < 1) b = 1;
+  if (b > 1184) b = 1184;          // 8 CTAs per SM is plenty for a copy
+  return static_cast<int>(b);
+}
+
+}  // namespace
+
+int comm_all_gather(const CommPeers& peers, int rank, int world, uint32_t epoch, void* out, long long shard_bytes,
+                    long long slot_cap, int* err, cudaStream_t st) {
+  if (world < 2 || world > kMaxCommPeers || shard_bytes > slot_cap) return 5;
+  const long long slot_off = kCommHeaderBytes + (long long)(epoch & 1u) * slot_cap;
+  uint8_t* mine = peers.base[rank] + slot_off;
+  uint8_t* o = static_cast<uint8_t*>(out);
+  stage_k<<<grid_for(shard_bytes), 256, 0, st>>>(mine, o + (long long)rank * shard_bytes, shard_bytes);
+  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, kCommAgFlags, epoch, err);
+  dim3 g(static_cast<unsigned>(grid_for(shard_bytes)), static_cast<unsigned>(world));
+  gather_k<<<g, 256, 0, st>>>(peers, rank, world, slot_off, o, shard_bytes);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int comm_reduce_scatter(const CommPeers& peers, int rank, int world, uint32_t epoch, const void* in, void* out,
+                        long long shard_elems, int elem_bytes, float scale, long long ag_cap, long long slot_cap,
+                        int* err, cudaStream_t st) {
+  const long long in_bytes = shard_elems * world * elem_bytes;
+  if (world < 2 || world > kMaxCommPeers || in_bytes > slot_cap || (elem_bytes != 4 && elem_bytes != 2)) return 5;
+  const long long slot_off = kCommHeaderBytes + 2 * ag_cap + (long long)(epoch & 1u) * slot_cap;
+  stage_k<<<grid_for(in_bytes), 256, 0, st>>>(peers.base[rank] + slot_off, static_cast<const uint8_t*>(in),
+                                              in_bytes);
+  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, kCommRsFlags, epoch, err);
+  const int g = grid_for(shard_elems * elem_bytes);
+  if (elem_bytes == 4)
+    reduce_k<float><<<g, 256, 0, st>>>(peers, rank, world, slot_off, static_cast<float*>(out), shard_elems, scale);
+  else
+    reduce_k<__nv_bfloat16><<<g, 256, 0, st>>>(peers, rank, world, slot_off, static_cast<__nv_bfloat16*>(out),
+                                               shard_elems, scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+}  // namespace vagus

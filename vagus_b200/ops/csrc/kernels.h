@@ -124,4 +124,19 @@ struct AttnBwdArgs {
 };
 int attn_bwd(const AttnBwdArgs& a, cudaStream_t st);
 
+// comm.cu: NVLink peer-to-peer all-gather / reduce-scatter over CUDA-IPC
+// shared heaps (see comm.cu for the heap layout and the epoch protocol).
+constexpr int kMaxCommPeers = 16;
+constexpr int kCommAgFlags = 0;                 // byte offsets inside a heap
+constexpr int kCommRsFlags = 256;
+constexpr long long kCommHeaderBytes = 1024;
+struct CommPeers {
+  unsigned char* base[kMaxCommPeers];           // every rank's heap, mapped into this process
+};
+int comm_all_gather(const CommPeers& peers, int rank, int world, unsigned epoch, void* out, long long shard_bytes,
+                    long long slot_cap, int* err, cudaStream_t st);
+int comm_reduce_scatter(const CommPeers& peers, int rank, int world, unsigned epoch, const void* in, void* out,
+                        long long shard_elems, int elem_bytes, float scale, long long ag_cap, long long slot_cap,
+                        int* err, cudaStream_t st);
+
 }  // namespace vagus

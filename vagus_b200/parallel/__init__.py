@@ -91,9 +91,14 @@ class LMLoss(nn.Module):
 
 
 def apply_fsdp(root: LMLoss, mesh, param_dtype: str = "bfloat16", reduce_dtype: str = "float32",
-               reshard_after_forward: bool = True) -> None:
+               reshard_after_forward: bool = True, comm: str = "nccl") -> None:
     """One FSDP2 unit per block plus the root; every 1-D parameter is left out
-    (replicated fp32, averaged by ``reduce_replicated``)."""
+    (replicated fp32, averaged by ``reduce_replicated``).
+
+    ``comm="nvlink"`` runs FSDP2's parameter all-gathers and gradient
+    reduce-scatters on our NVLink peer-to-peer kernels (``parallel.nvlink``)
+    instead of NCCL; it applies to a 1-D (pure FSDP) mesh on CUDA, and a 2-D
+    HSDP mesh keeps NCCL."""
     pd, rd = DTYPES[param_dtype], DTYPES[reduce_dtype]
     blocks_mp = MixedPrecisionPolicy(param_dtype=None if pd is torch.float32 else pd, reduce_dtype=rd,
                                      cast_forward_inputs=False)
@@ -104,6 +109,12 @@ def apply_fsdp(root: LMLoss, mesh, param_dtype: str = "bfloat16", reduce_dtype: 
         fully_shard(blk, mesh=mesh, mp_policy=blocks_mp, ignored_params=ignored,
                     reshard_after_forward=reshard_after_forward)
     fully_shard(root, mesh=mesh, mp_policy=root_mp, ignored_params=ignored)
+    root.nvlink_heap = None
+    if comm == "nvlink" and mesh.ndim == 1 and mesh.device_type == "cuda" and mesh.size() > 1:
+        from .nvlink import use_nvlink_collectives
+        root.nvlink_heap = use_nvlink_collectives(root, mesh.get_group())
+    elif comm not in ("nccl", "nvlink"):
+        raise ValueError(f"unknown FSDP collective backend {comm!r} (nccl | nvlink)")
 
 
 def reduce_replicated(root: LMLoss, mesh=None) -> None:

@@ -1,0 +1,149 @@
+"""FSDP2's parameter all-gather and gradient reduce-scatter on our own NVLink
+peer-to-peer kernels (``ops/csrc/comm.cu``) instead of NCCL.
+
+FSDP2 lets a module take custom collective objects
+(``FSDPModule.set_custom_all_gather`` / ``set_custom_reduce_scatter``);
+``use_nvlink_collectives(root, group)`` installs ours on every FSDP unit of a
+model.  Each rank allocates one device heap (plain ``cudaMalloc``), shares it
+with the other ranks of the group through CUDA IPC (no NVLink multicast
+objects), and every collective is three launches on the stream FSDP chose:
+stage this rank's contribution into its heap slot, a cross-GPU epoch barrier
+(bounded wait; a timeout sets the device error word that
+``ops.check_error()`` raises), and the combine step that reads the peers'
+slots over NVLink (all-gather: copy into place; reduce-scatter: fp32 sum of
+this rank's rows, scale by 1 / world for an average, cast).
+
+Calls the kernels cannot take (a reduction other than sum / average, a
+buffer larger than the heap slots) go to NCCL; the decision depends only on
+sizes and the op, which are identical on every rank, so the per-kind epoch
+counters stay in step.
+
+Parity: the reference runs these collectives inside FSDP2 on NCCL
+(``infra/train/main.py:253-275``); the gradient reduction semantics (average
+over the data-parallel group, fp32) are the same.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+from torch.distributed.fsdp._fully_shard._fsdp_api import AllGather, ReduceScatter
+
+from ..ops import native
+
+HEADER = 1024                      # flag words, as comm.cu lays them out
+
+
+class NvlinkHeap:
+    """One IPC-shared device heap per rank of ``group``: 2 all-gather slots of
+    ``ag_cap`` bytes and 2 reduce-scatter slots of ``rs_cap`` bytes."""
+
+    def __init__(self, group, ag_cap: int, rs_cap: int):
+        C = native()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.ag_cap = (int(ag_cap) + 255) // 256 * 256
+        self.rs_cap = (int(rs_cap) + 255) // 256 * 256
+        ptr, handle = C.comm_heap_create(HEADER + 2 * self.ag_cap + 2 * self.rs_cap)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.own = ptr
+        self.bases = [ptr if r == self.rank else C.comm_heap_open(h) for r, h in enumerate(handles)]
+        self.ag_epoch = 0
+        self.rs_epoch = 0
+        dist.barrier(group=group)
+
+    def close(self):
+        C = native()
+        for r, b in enumerate(self.bases):
+            C.comm_heap_close(b, r == self.rank)
+        self.bases = []
+
+
+class NvlinkAllGather(AllGather):
+    def __init__(self, heap: NvlinkHeap):
+        self.heap = heap
+
+    def allocate(self, size, *, dtype, device):
+        return torch.empty(*size, dtype=dtype, device=device)
+
+    def __call__(self, output_tensor, input_tensor, group, async_op: bool = False):
+        h = self.heap
+        shard_bytes = input_tensor.numel() * input_tensor.element_size()
+        if shard_bytes > h.ag_cap or not output_tensor.is_contiguous():
+            return dist.all_gather_into_tensor(output_tensor, input_tensor, group=group, async_op=async_op)
+        n = input_tensor.numel()
+        mine = output_tensor.view(-1)[h.rank * n:(h.rank + 1) * n]
+        if mine.data_ptr() != input_tensor.data_ptr():
+            mine.copy_(input_tensor.view(-1))
+        h.ag_epoch += 1
+        native().comm_all_gather(output_tensor, h.bases, h.rank, h.ag_epoch, h.ag_cap)
+        return None
+
+
+class NvlinkReduceScatter(ReduceScatter):
+    def __init__(self, heap: NvlinkHeap):
+        self.heap = heap
+
+    def allocate(self, size, *, dtype, device):
+        return torch.empty(*size, dtype=dtype, device=device)
+
+    def __call__(self, output_tensor, input_tensor, group, op, async_op: bool = False):
+        h = self.heap
+        if op == dist.ReduceOp.SUM:
+            scale = 1.0
+        elif op == dist.ReduceOp.AVG:
+            scale = 1.0 / h.world
+        else:
+            scale = None
+        nbytes = input_tensor.numel() * input_tensor.element_size()
+        if (scale is None or nbytes > h.rs_cap or input_tensor.dtype not in (torch.float32, torch.bfloat16)
+                or input_tensor.dtype != output_tensor.dtype):
+            return dist.reduce_scatter_tensor(output_tensor, input_tensor, op=op, group=group, async_op=async_op)
+        h.rs_epoch += 1
+        native().comm_reduce_scatter(output_tensor, input_tensor.contiguous(), h.bases, h.rank, h.rs_epoch, scale,
+                                     h.ag_cap, h.rs_cap)
+        return None
+
+
+def _unit_sizes(root, world: int):
+    """Largest FSDP unit (sum of padded parameter numels) among the blocks
+    and the root's own parameters; 1-D parameters are replicated, not sharded."""
+    from torch.distributed.fsdp import FSDPModule
+
+    def managed(mod, skip):
+        total = 0
+        for p in mod.parameters():
+            if id(p) in skip or p.dim() < 2:
+                continue
+            d0 = p.shape[0]
+            total += ((d0 + world - 1) // world * world) * (p.numel() // max(1, d0))
+        return total
+
+    units = [m for m in root.modules() if isinstance(m, FSDPModule)]
+    seen: set = set()
+    sizes = []
+    for m in units:
+        if m is root:
+            continue
+        sizes.append(managed(m, seen))
+        seen.update(id(p) for p in m.parameters())
+    sizes.append(managed(root, seen))
+    return max(sizes) if sizes else 0
+
+
+def use_nvlink_collectives(root, group=None) -> NvlinkHeap:
+    """Install the NVLink collectives on every FSDP unit under ``root``
+    (after ``fully_shard``).  Returns the heap (keep it alive)."""
+    from torch.distributed.fsdp import FSDPModule
+    group = group or dist.group.WORLD
+    world = dist.get_world_size(group)
+    biggest = _unit_sizes(root, world)
+    heap = NvlinkHeap(group, ag_cap=(biggest // world + 64) * 4, rs_cap=(biggest + 64 * world) * 4)
+    ag, rs = NvlinkAllGather(heap), NvlinkReduceScatter(heap)
+    for m in root.modules():
+        if isinstance(m, FSDPModule):
+            m.set_custom_all_gather(ag)
+            m.set_custom_reduce_scatter(rs)
+    return heap

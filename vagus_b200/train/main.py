@@ -84,6 +84,7 @@ class TrainConfig:
     fsdp_param_dtype: str = "bfloat16"
     fsdp_reduce_dtype: str = "float32"
     fsdp_reshard_after_forward: bool = True
+    fsdp_comm: str = "nvlink"          # FSDP2 all-gather / reduce-scatter: our NVLink kernels or "nccl"
     grad_clip: float | None = 1.0
     z_loss: float | None = None
     ce_impl: str = "liger"
@@ -317,7 +318,8 @@ def train(config: TrainConfig, teardown: bool = True):
     params_by_group = {k: sum(p.numel() for p in v) for k, v in model.param_groups().items()}
     if is_fsdp:
         model = LMLoss(model, ce_fn)
-        apply_fsdp(model, mesh, config.fsdp_param_dtype, config.fsdp_reduce_dtype, config.fsdp_reshard_after_forward)
+        apply_fsdp(model, mesh, config.fsdp_param_dtype, config.fsdp_reduce_dtype, config.fsdp_reshard_after_forward,
+                   comm=config.fsdp_comm if device.type == "cuda" else "nccl")
     elif is_dist:
         from torch.nn.parallel import DistributedDataParallel as DDP
         model = DDP(model, device_ids=[device.index] if device.type == "cuda" else None,
