@@ -1,0 +1,94 @@
+"""Multi-process parity on CPU (gloo, world size 2): FSDP2 (shard 2) and
+DDP give the same loss and gradient-norm traces for fp32 AdamW and Muon
+(the FSDP path runs the sharded Newton-Schulz with its all-gathers)."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+MODEL = dict(vocab_size=300, dim=64, layer_count=2, head_dim=32, context_len=64, ffn_hidden_dim=128)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _run(mode, opt_name, rank, steps=3):
+    import torch.distributed as dist
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    from vagus_b200.models import build_model
+    from vagus_b200.models.losses import make_ce
+    from vagus_b200.optim import build_optimizer
+    from vagus_b200.parallel import LMLoss, apply_fsdp, build_mesh, unwrap
+    from vagus_b200.train.main import StepRunner
+    torch.manual_seed(0)
+    model = build_model("TransformerPP", MODEL)
+    ce = make_ce("full")
+    dev = torch.device("cpu")
+    mesh = None
+    if mode == "fsdp":
+        mesh = build_mesh(2, dev, 2)
+        model = LMLoss(model, ce)
+        apply_fsdp(model, mesh, "float32", "float32")
+    else:
+        model = DDP(model)
+    args = dict(lr=1e-2, weight_decay=0.1) if opt_name == "adamw" else \
+        dict(lr=2e-2, weight_decay=0.1, adamw=dict(lr=1e-2, weight_decay=0.1))
+    opt = build_optimizer(opt_name, unwrap(model), args)
+    runner = StepRunner(model, opt, ce, dev, grad_accum_steps=2, grad_clip=1.0, is_fsdp=mode == "fsdp",
+                        is_dist=True, mesh=mesh)
+    g = torch.Generator().manual_seed(123 + rank)
+    batches = []
+    for _ in range(steps * 2):
+        t = torch.randint(0, 300, (2, 33), generator=g)
+        batches.append((t[:, :-1], t[:, 1:]))
+    it = iter(batches)
+    out = []
+    for _ in range(steps):
+        loss, _z, gn = runner.step(it)
+        out.append((loss.item(), float(gn)))
+    dist.barrier()
+    return out
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                          LOCAL_RANK=str(rank))
+        from vagus_b200.parallel import setup_distributed
+        setup_distributed("cpu", timeout_s=120)
+        import torch.distributed as dist
+        res = {}
+        for opt_name in ("adamw", "muon"):
+            res[opt_name] = {m: _run(m, opt_name, rank) for m in ("ddp", "fsdp")}
+        dist.destroy_process_group()
+        q.put((rank, res))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+        q.put((rank, traceback.format_exc() + repr(e)))
+
+
+def test_fsdp_matches_ddp_gloo():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for rank, res in results.items():
+        assert not isinstance(res, str), res
+        for opt_name, tol in (("adamw", 1e-5), ("muon", 2e-3)):
+            for (la, ga), (lb, gb) in zip(res[opt_name]["ddp"], res[opt_name]["fsdp"]):
+                assert abs(la - lb) <= tol * max(1.0, abs(la)), (opt_name, la, lb)
+                assert abs(ga - gb) <= tol * max(1.0, abs(ga)) * 10, (opt_name, ga, gb)

@@ -1,0 +1,114 @@
+"""Kalman-delta scans (fp64 oracles) and the evaluation harness end to end
+on a tiny checkpoint trained here (record layout, determinism, pairing)."""
+
+import json
+
+import pytest
+import torch
+
+from vagus_b200.eval.main import EvalConfig, evaluate
+from vagus_b200.eval.pairs import paired
+from vagus_b200.models.kalman import kalman_gain_diag, kalman_gain_iso, mobius_scan
+
+torch.set_default_dtype(torch.float64)
+
+
+def _pos(*shape):
+    return torch.rand(*shape) + 0.1
+
+
+def test_mobius_parallel_and_blocked_match_recurrent():
+    torch.manual_seed(0)
+    B, L, H = 2, 300, 3
+    A, Bq, C, D = _pos(B, L, H), _pos(B, L, H), _pos(B, L, H), _pos(B, L, H)
+    x0 = _pos(B, H)
+    ref = mobius_scan(A, Bq, C, D, x0, impl="recurrent")
+    par = mobius_scan(A, Bq, C, D, x0, impl="parallel", block=None)
+    blk = mobius_scan(A, Bq, C, D, x0, impl="parallel", block=64)
+    assert torch.allclose(par, ref, rtol=1e-10, atol=1e-12)
+    assert torch.allclose(blk, ref, rtol=1e-10, atol=1e-12)
+    long = mobius_scan(_pos(1, 1024, 1), _pos(1, 1024, 1), _pos(1, 1024, 1), _pos(1, 1024, 1), _pos(1, 1),
+                       impl="parallel", block=None)
+    assert torch.isfinite(long).all()
+
+
+def test_iso_gain_matches_hand_recurrence():
+    torch.manual_seed(1)
+    B, L, H, dk = 1, 20, 2, 8
+    k = torch.randn(B, L, H, dk)
+    alpha = torch.rand(B, L, H, dk) * 0.5 + 0.5
+    omega, r = _pos(B, L, H), _pos(B, L, H)
+    c0 = _pos(B, H)
+    beta, c_fin = kalman_gain_iso(k, alpha, omega, r, c0, info_scale=1.0)
+    # precision c, prior variance bhat = a / c_prev + omega, gain = bhat / (r + bhat |k|^2)
+    c = c0.clone()
+    for t in range(L):
+        a = alpha[:, t].square().mean(-1)
+        kn2 = k[:, t].square().sum(-1)
+        bhat = a / c + omega[:, t]
+        assert torch.allclose(beta[:, t], bhat / (r[:, t] + bhat * kn2), rtol=1e-10)
+        m = kn2 / dk / r[:, t]
+        c = ((1 + m * omega[:, t]) * c + m * a) / (omega[:, t] * c + a)
+    assert torch.allclose(c_fin, c, rtol=1e-10)
+
+
+def test_diag_gain_shapes_and_positivity():
+    torch.manual_seed(2)
+    B, L, H, dk = 1, 12, 2, 4
+    k = torch.randn(B, L, H, dk)
+    alpha = torch.rand(B, L, H, dk) * 0.5 + 0.5
+    kappa, p = kalman_gain_diag(k, alpha, _pos(B, L, H, dk), _pos(B, L, H), _pos(B, H, dk), info_scale=1.0)
+    assert kappa.shape == (B, L, H, dk) and p.shape == (B, H, dk) and (p > 0).all()
+
+
+def test_paired_statistics():
+    a = [1.0, 2.0, 3.0, 4.0]
+    b = [1.5, 2.5, 3.5, 4.5]
+    r = paired(a, b, n_boot=200, seed=0)
+    assert r["mean_diff"] == pytest.approx(0.5)
+    assert r["frac_positive"] == pytest.approx(1.0) and r["n"] == 4
+    assert r["ci95"][0] <= 0.5 <= r["ci95"][1]
+
+
+@pytest.fixture(scope="module")
+def trained(tmp_path_factory):
+    torch.set_default_dtype(torch.float32)
+    from vagus_b200.data.prepare import synthetic_store
+    from vagus_b200.train import main as tm
+    root = tmp_path_factory.mktemp("ev")
+    data = root / "tok"
+    synthetic_store(data, tokens=40_000, vocab=400, seed=4, doc_len=200, bos=1)
+    model = dict(vocab_size=400, dim=64, layer_count=2, head_count=2, key_head_dim=32, value_head_dim=32,
+                 ffn_hidden_dim=128, context_len=128, gate="scalar", delta=True, chunk_size=16)
+    cfg = tm.TrainConfig(run_name="e", data_dir=str(data), model_name="GDNLM", model_args=model,
+                         optimizer_name="adamw", optimizer_args=dict(lr=3e-3), context_len=64, batch_size=2,
+                         train_tokens=4 * 2 * 64, device="cpu", dtype="float32", compile=False, ce_impl="full",
+                         run_dir=str(root / "run"), log_interval=1, slow_interval=1000, deadline_margin_s=None)
+    run = tm.train(cfg)
+    return root, data, run
+
+
+def _eval(root, data, run, name):
+    tasks = [{"name": "holdout", "args": {"data_dir": str(data), "n_seq": 3, "context_len": [64]}}]
+    subj = [{"run": str(run), "label": lab, "tokenizer_id": "mistral32k"} for lab in ("a", "b")]
+    cfg = EvalConfig(eval_name=name, subjects=subj,
+                     tasks=tasks, device="cpu", dtype="float32", run_dir=str(root / name),
+                     registry_dir=str(root / "registry"), n_boot=50)
+    return evaluate(cfg)
+
+
+def test_eval_record_and_determinism(trained):
+    torch.set_default_dtype(torch.float32)
+    root, data, run = trained
+    d1 = _eval(root, data, run, "e1")
+    d2 = _eval(root, data, run, "e2")
+    r1 = json.loads((d1 / "results.json").read_text())
+    r2 = json.loads((d2 / "results.json").read_text())
+    assert set(r1["holdout"]["subjects"]) == {"a", "b"}
+    assert r1["holdout"]["subjects"]["a"]["items"] == r2["holdout"]["subjects"]["a"]["items"]
+    assert "b" in r1["holdout"]["pairs"]
+    meta = json.loads((d1 / "meta.json").read_text())
+    assert meta["reference"] == "a" and len(meta["subjects"]) == 2
+    assert (root / "registry" / "e1.json").exists()
+    with pytest.raises(Exception):
+        _eval(root, data, run, "e1")          # refuses to overwrite an existing record

@@ -1,0 +1,125 @@
+"""Optimizer (Newton-Schulz, Muon, coverage, schedules) and the trainer:
+a short CPU run, checkpoints, resume == uninterrupted run, stop request."""
+
+import shutil
+
+import pytest
+import torch
+
+from vagus_b200.data.prepare import synthetic_store
+from vagus_b200.models import build_model
+from vagus_b200.optim import build_optimizer
+from vagus_b200.optim.muon import newton_schulz
+from vagus_b200.train import main as tm
+from vagus_b200.train.schedule import build_schedule, cosine, linear, wsd
+
+
+@pytest.mark.parametrize("scheme", ["jordan", "polar_express"])
+def test_newton_schulz_orthogonalises(scheme):
+    torch.manual_seed(0)
+    for shape in [(64, 32), (32, 64), (48, 48)]:
+        G = torch.randn(*shape, dtype=torch.float32)
+        X = newton_schulz(G, steps=5, scheme=scheme).float()
+        s = torch.linalg.svdvals(X)
+        assert s.max() < 1.3 and s.min() > 0.5, (scheme, shape, s.min().item(), s.max().item())
+        # same column space as G: X ~ U V^T
+        U, _, Vh = torch.linalg.svd(G, full_matrices=False)
+        cos = torch.nn.functional.cosine_similarity((U @ Vh).flatten(), X.flatten(), dim=0)
+        assert cos > 0.95
+
+
+def test_schedules():
+    assert cosine(0.0, warmup=0.1) == pytest.approx(0.0, abs=1e-6)
+    assert cosine(1.0, warmup=0.1, min_ratio=0.1) == pytest.approx(0.1, abs=1e-6)
+    assert linear(0.55, warmup=0.1, min_ratio=0.0) == pytest.approx(0.5, abs=1e-6)
+    assert wsd(0.5, warmup=0.01, decay=0.2) == pytest.approx(1.0)
+    assert wsd(1.0, warmup=0.01, decay=0.2, min_ratio=0.0) == pytest.approx(0.0, abs=1e-6)
+    f = build_schedule("wsd", {"warmup": 0.01, "decay": 0.2})
+    assert 0.0 <= f(0.95) < 1.0
+    with pytest.raises(Exception):
+        build_schedule("nope", {})
+
+
+MODEL = dict(vocab_size=500, dim=64, layer_count=2, head_dim=32, context_len=64, ffn_hidden_dim=128)
+
+
+@pytest.mark.parametrize("name", ["adamw", "muon"])
+def test_optimizer_covers_every_parameter_and_steps(name):
+    torch.manual_seed(0)
+    m = build_model("TransformerPP", MODEL)
+    args = dict(lr=1e-2, weight_decay=0.0) if name == "adamw" else dict(lr=2e-2, adamw=dict(lr=1e-2))
+    opt = build_optimizer(name, m, args)
+    x = torch.randint(0, 500, (2, 33))
+    losses = []
+    for _ in range(5):
+        opt.zero_grad()
+        logits = m(x[:, :-1])
+        loss = torch.nn.functional.cross_entropy(logits.flatten(0, 1).float(), x[:, 1:].flatten())
+        loss.backward()
+        opt.step()
+        losses.append(loss.item())
+    assert losses[-1] < losses[0]
+    for g in opt.param_groups:
+        assert "base_lr" in g
+
+
+def _config(tmp_path, run, steps, **kw):
+    data = tmp_path / "tok"
+    if not data.exists():
+        synthetic_store(data, tokens=60_000, vocab=500, seed=1)
+    base = dict(run_name="t", data_dir=str(data), model_name="TransformerPP", model_args=MODEL,
+                optimizer_name="muon", optimizer_args=dict(lr=2e-2, adamw=dict(lr=1e-2)),
+                context_len=32, batch_size=2, grad_accum_steps=2, train_tokens=steps * 2 * 2 * 32,
+                device="cpu", dtype="float32", compile=False, ce_impl="full", run_dir=str(tmp_path / run),
+                log_interval=1, slow_interval=1000, deadline_margin_s=None, recent_ckpt_minutes=1e9)
+    base.update(kw)
+    return tm.TrainConfig(**base)
+
+
+def test_train_checkpoints_and_exact_resume(tmp_path):
+    run_a = tm.train(_config(tmp_path, "a", 6, permanent_ckpt_interval=3))
+    assert (run_a / "ckpt-00000003.pt").exists() and (run_a / "ckpt-00000006.pt").exists()
+    assert (run_a / "model-final.pt").exists() and (run_a / "config.yaml").exists()
+    # resume a copy of the step-3 checkpoint and finish: same weights as the straight run
+    run_b = tmp_path / "b"
+    run_b.mkdir()
+    shutil.copy(run_a / "ckpt-00000003.pt", run_b / "ckpt-00000003.pt")
+    tm.train(_config(tmp_path, "b", 6, permanent_ckpt_interval=3))
+    a = torch.load(run_a / "ckpt-00000006.pt", weights_only=False)
+    b = torch.load(run_b / "ckpt-00000006.pt", weights_only=False)
+    assert a["step"] == b["step"] == 6 and a["tokens_seen"] == b["tokens_seen"]
+    for k in a["model"]:
+        assert torch.equal(a["model"][k], b["model"][k]), k
+
+
+def test_stop_request_checkpoints_and_exits(tmp_path, monkeypatch):
+    calls = {"n": 0}
+    real = tm.StepRunner.step
+
+    def step(self, batches):
+        calls["n"] += 1
+        if calls["n"] == 2:
+            tm.request_stop()
+        return real(self, batches)
+
+    monkeypatch.setattr(tm.StepRunner, "step", step)
+    run = tm.train(_config(tmp_path, "s", 10))
+    state = torch.load(run / "recent.pt", weights_only=False)
+    assert state["step"] == 2
+    assert not (run / "model-final.pt").exists()
+
+
+def test_refuses_to_overwrite_a_run_without_checkpoints(tmp_path):
+    (tmp_path / "x").mkdir()
+    (tmp_path / "x" / "junk.txt").write_text("x")
+    with pytest.raises(FileExistsError):
+        tm.train(_config(tmp_path, "x", 2))
+
+
+def test_from_yaml_with_model_recipe(tmp_path):
+    (tmp_path / "m.yaml").write_text("model_name: TransformerPP\nmodel_args: {dim: 64}\n")
+    (tmp_path / "t.yaml").write_text("model_recipe: m.yaml\nrun_name: r\ndata_dir: d\nbatch_size: 4\n")
+    cfg = tm.TrainConfig.from_yaml(tmp_path / "t.yaml", ["batch_size=8"])
+    assert cfg.model_args == {"dim": 64} and cfg.batch_size == 8
+    with pytest.raises(TypeError):
+        tm.TrainConfig.from_yaml(tmp_path / "t.yaml", ["nonsense_key=1"])
