@@ -85,9 +85,9 @@ def _cases(B: int, L: int):
     cases["gdr_bwd"] = (lambda: _gdr_bwd(saved, do, None, scale, False), None, 2 * (intra + rec))
     # the two stages separately (inputs from one forward)
     W_, Qh, Kt, A_, U_, gC = C.gdr_intra_fwd(q, k, v, g, beta, scale)
-    cases["gdr_rec_fwd"] = (lambda: C.gdr_rec_fwd(W_, Qh, Kt, A_, U_, gC, None, True), None, rec)
-    _, Vp, states, _ = C.gdr_rec_fwd(W_, Qh, Kt, A_, U_, gC, None, True)
-    dO = torch.randn(BH, nc, 64, hd, device=dev).to(bf)
+    cases["gdr_rec_fwd"] = (lambda: C.gdr_rec_fwd(W_, Qh, Kt, A_, U_, gC, None, True, H), None, rec)
+    _, Vp, states, _ = C.gdr_rec_fwd(W_, Qh, Kt, A_, U_, gC, None, True, H)
+    dO = torch.randn(B, L, H, hd, device=dev).to(bf)
     cases["gdr_rec_bwd"] = (lambda: C.gdr_rec_bwd(W_, Qh, Kt, A_, Vp, gC, states, dO, None, False), None, 2 * rec)
     rb = C.gdr_rec_bwd(W_, Qh, Kt, A_, Vp, gC, states, dO, None, False)
     cases["gdr_intra_bwd"] = (lambda: C.gdr_intra_bwd(q, k, v, g, beta, *rb[:6], scale), None, 2 * intra)

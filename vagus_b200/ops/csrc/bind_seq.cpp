@@ -79,30 +79,34 @@ std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_l
 // Recurrence forward: returns (O, V', states, S_out).  The per-chunk entry
 // states (bf16) are always produced: the output stage reads them.
 std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor U, Tensor gC,
-                                c10::optional<Tensor> S0, bool need_states) {
+                                c10::optional<Tensor> S0, bool need_states, int64_t H) {
   (void)need_states;
   const int64_t BH = W.size(0);
+  TORCH_CHECK(H > 0 && BH % H == 0, "gdr_rec_fwd: heads must divide B*H");
   const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(U.size(3));
   TORCH_CHECK(W.size(2) == 64, "gdr: chunk size 64");
   for (auto* t : {&W, &Qh, &Kt, &A, &U}) TORCH_CHECK(t->is_contiguous() && t->scalar_type() == at::kBFloat16, "gdr: bf16");
-  auto O = torch::empty_like(U);
+  auto O = torch::empty({BH / H, static_cast<int64_t>(N) * 64, H, DV}, U.options());   // token-major
   auto Vp = torch::empty_like(U);
   auto states = torch::empty({BH, N, DK, DV}, W.options());
   auto S_out = torch::empty({BH, DK, DV}, W.options().dtype(at::kFloat));
   vagus::GdrRecArgs a{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), U.data_ptr(),
                       gC.contiguous().data_ptr<float>(), fptr(S0), O.data_ptr(), Vp.data_ptr(),
-                      states.data_ptr(), S_out.data_ptr<float>(), BH, N, DK, DV};
+                      states.data_ptr(), S_out.data_ptr<float>(), BH, N, DK, DV, static_cast<int>(H)};
   check(vagus::gdr_rec_fwd(a, stream()), "gdr_rec_fwd");
   return {O, Vp, states, S_out};
 }
 
 // Recurrence backward: returns (dW, dQh, dKt (bf16), dA (fp32), dU (bf16), dgC, dS0)
+// dO: token-major (B, L, H, DV) bf16
 std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor Vp, Tensor gC, Tensor states,
                                 Tensor dO, c10::optional<Tensor> dS_final, bool need_dS0) {
   const int64_t BH = W.size(0);
   const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(Vp.size(3));
   TORCH_CHECK(states.scalar_type() == at::kBFloat16 && states.is_contiguous(), "gdr_rec_bwd: bf16 states");
   dO = dO.contiguous();
+  TORCH_CHECK(dO.dim() == 4 && dO.size(3) == DV && dO.scalar_type() == at::kBFloat16, "gdr_rec_bwd: dO (B, L, H, DV) bf16");
+  const int H = static_cast<int>(dO.size(2));
   auto f32 = W.options().dtype(at::kFloat);
   auto bf = W.options();
   auto dW = torch::empty({BH, N, 64, DK}, bf);
@@ -116,7 +120,7 @@ std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
   vagus::GdrRecBwdArgs a;
   a.f = vagus::GdrRecArgs{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), nullptr,
                           gC.contiguous().data_ptr<float>(), nullptr, nullptr, Vp.data_ptr(), states.data_ptr(),
-                          nullptr, BH, N, DK, DV};
+                          nullptr, BH, N, DK, DV, H};
   a.dO = dO.data_ptr();
   a.dS_final = fptr(dS_final);
   a.dW = dW.data_ptr(); a.dQh = dQh.data_ptr(); a.dKt = dKt.data_ptr(); a.dA = dA.data_ptr<float>();

@@ -26,7 +26,8 @@
 // The snapshots are bf16, the precision the tensor-core products consume.
 //
 // Layouts (all chunk-major, contiguous):
-//   W, Qh, Kt: (BH, N, C, DK) bf16   A: (BH, N, C, C) bf16   U, V', O, dO, dU: (BH, N, C, DV) bf16
+//   W, Qh, Kt: (BH, N, C, DK) bf16   A: (BH, N, C, C) bf16   U, V', dU: (BH, N, C, DV) bf16
+//   O, dO: token-major (B, N * C, H, DV) bf16 (BH = B * H), the layout of the model's activations
 //   gC, dgC: (BH, N) fp32   states, dstates: (BH, N, DK, DV) bf16
 //   dW, dQh, dKt: (BH, N, C, DK) bf16   dA: (BH, N, C, C) fp32
 #include "common.cuh"
@@ -41,6 +42,13 @@ using namespace mma;
 constexpr int C = 64;        // chunk length
 constexpr int DVT = 64;      // value tile
 constexpr int THREADS = 256;
+
+// O and dO are token-major (B, L, H, DV): the first row of chunk n of
+// sequence bh = b * H + h, and the pitch between its rows
+__device__ __forceinline__ long long tok_row0(long long bh, int n, int N, int H, int DV) {
+  const long long b = bh / H, h = bh - b * H;
+  return ((b * N * C + (long long)n * C) * H + h) * DV;
+}
 
 __device__ __forceinline__ void cp_wait_1() { asm volatile("cp.async.wait_group 1;" ::: "memory"); }
 __device__ __forceinline__ void cp_wait_2() { asm volatile("cp.async.wait_group 2;" ::: "memory"); }
@@ -177,7 +185,7 @@ template <int DK>
 __global__ void __launch_bounds__(THREADS, 2)
 gdr_fwd_out(const __nv_bfloat16* __restrict__ Qh, const __nv_bfloat16* __restrict__ A,
             const __nv_bfloat16* __restrict__ Vp, const __nv_bfloat16* __restrict__ states,
-            __nv_bfloat16* __restrict__ O, int DV) {
+            __nv_bfloat16* __restrict__ O, int DV, int N, int H) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   OutSmem<DK>& sm = *reinterpret_cast<OutSmem<DK>*>(smem_raw);
   const long long cidx = blockIdx.x;
@@ -204,7 +212,8 @@ gdr_fwd_out(const __nv_bfloat16* __restrict__ Qh, const __nv_bfloat16* __restric
       *reinterpret_cast<uint32_t*>(&sm.V[r][c]) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
     }
   __syncthreads();
-  store_tile(O + cidx * C * DV + v0, DV, &sm.V[0][0], DVT + PAD, C, DVT);
+  store_tile(O + tok_row0(cidx / N, static_cast<int>(cidx % N), N, H, DV) + v0, (long long)H * DV, &sm.V[0][0],
+             DVT + PAD, C, DVT);
 }
 
 // ------------------------------------------------------------ backward scan --
@@ -226,7 +235,7 @@ gdr_bwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
              const __nv_bfloat16* __restrict__ Kt, const __nv_bfloat16* __restrict__ A,
              const float* __restrict__ gC, const __nv_bfloat16* __restrict__ dO, const float* __restrict__ dS_final,
              __nv_bfloat16* __restrict__ dU, __nv_bfloat16* __restrict__ dstates, float* __restrict__ dS0, int N,
-             int DV) {
+             int DV, int H) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   BwdScanSmem<DK>& sm = *reinterpret_cast<BwdScanSmem<DK>*>(smem_raw);
   constexpr int SMT = DK / 8 / 16;
@@ -244,7 +253,7 @@ gdr_bwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
     const int b = n & 1;
     load_tile(&sm.K[b][0][0], DK + PAD, Kt + cidx * C * DK, DK, C, DK);
     load_tile(&sm.A[b][0][0], C + PAD, A + cidx * C * C, C, C, C);
-    load_tile(&sm.dO[b][0][0], DVT + PAD, dO + cidx * C * DV + v0, DV, C, DVT);
+    load_tile(&sm.dO[b][0][0], DVT + PAD, dO + tok_row0(bh, n, N, H, DV) + v0, (long long)H * DV, C, DVT);
   };
   auto issue2 = [&](int n) {
     const long long cidx = bh * N + n;
@@ -351,7 +360,7 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
               const __nv_bfloat16* __restrict__ Vp, const __nv_bfloat16* __restrict__ states,
               const __nv_bfloat16* __restrict__ dstates, __nv_bfloat16* __restrict__ dW,
               __nv_bfloat16* __restrict__ dQh, __nv_bfloat16* __restrict__ dKt, float* __restrict__ dA,
-              float* __restrict__ dgC, int DK, int DV) {
+              float* __restrict__ dgC, int DK, int DV, int N, int H) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   ParSmem& sm = *reinterpret_cast<ParSmem*>(smem_raw);
   const long long cidx = blockIdx.x;
@@ -362,7 +371,8 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
   auto issue = [&](int vb) {
     const int b = vb & 1, v0 = vb * DVT;
     load_tile(&sm.dV[b][0][0], DVT + PAD, dU + cidx * C * DV + v0, DV, C, DVT);
-    load_tile(&sm.dO[b][0][0], DVT + PAD, dO + cidx * C * DV + v0, DV, C, DVT);
+    load_tile(&sm.dO[b][0][0], DVT + PAD, dO + tok_row0(cidx / N, static_cast<int>(cidx % N), N, H, DV) + v0,
+              (long long)H * DV, C, DVT);
     load_tile(&sm.V[b][0][0], DVT + PAD, Vp + cidx * C * DV + v0, DV, C, DVT);
     load_tile(&sm.S[b][0][0], DVT + PAD, states + (cidx * DK + k0) * DV + v0, DV, 64, DVT);
     load_tile(&sm.dS[b][0][0], DVT + PAD, dstates + (cidx * DK + k0) * DV + v0, DV, 64, DVT);
@@ -464,7 +474,7 @@ int launch_fwd(const GdrRecArgs& a, cudaStream_t st) {
   dim3 g2(static_cast<unsigned>(a.BH * a.N), a.DV / DVT);
   gdr_fwd_out<DK><<<g2, THREADS, s2, st>>>((const __nv_bfloat16*)a.Qh, (const __nv_bfloat16*)a.A,
                                            (const __nv_bfloat16*)a.Vp, (const __nv_bfloat16*)a.states,
-                                           (__nv_bfloat16*)a.O, a.DV);
+                                           (__nv_bfloat16*)a.O, a.DV, a.N, a.H);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -476,26 +486,27 @@ int launch_bwd(const GdrRecBwdArgs& a, cudaStream_t st) {
   gdr_bwd_scan<DK><<<grid, THREADS, s1, st>>>((const __nv_bfloat16*)a.f.W, (const __nv_bfloat16*)a.f.Qh,
                                               (const __nv_bfloat16*)a.f.Kt, (const __nv_bfloat16*)a.f.A, a.f.gC,
                                               (const __nv_bfloat16*)a.dO, a.dS_final, (__nv_bfloat16*)a.dU,
-                                              (__nv_bfloat16*)a.dstates, a.dS0, a.f.N, a.f.DV);
+                                              (__nv_bfloat16*)a.dstates, a.dS0, a.f.N, a.f.DV, a.f.H);
   dim3 g2(static_cast<unsigned>(a.f.BH * a.f.N), DK / 64);
   gdr_bwd_chunk<<<g2, THREADS, s2, st>>>((const __nv_bfloat16*)a.dU, (const __nv_bfloat16*)a.dO,
                                          (const __nv_bfloat16*)a.f.Vp, (const __nv_bfloat16*)a.f.states,
                                          (const __nv_bfloat16*)a.dstates, (__nv_bfloat16*)a.dW,
-                                         (__nv_bfloat16*)a.dQh, (__nv_bfloat16*)a.dKt, a.dA, a.dgC, DK, a.f.DV);
+                                         (__nv_bfloat16*)a.dQh, (__nv_bfloat16*)a.dKt, a.dA, a.dgC, DK, a.f.DV,
+                                         a.f.N, a.f.H);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
 }  // namespace
 
 int gdr_rec_fwd(const GdrRecArgs& a, cudaStream_t st) {
-  if (a.DV % DVT) return 5;
+  if (a.DV % DVT || a.H <= 0 || a.BH % a.H) return 5;
   if (a.DK == 256) return launch_fwd<256>(a, st);
   if (a.DK == 128) return launch_fwd<128>(a, st);
   return 5;
 }
 
 int gdr_rec_bwd(const GdrRecBwdArgs& a, cudaStream_t st) {
-  if (a.f.DV % DVT) return 5;
+  if (a.f.DV % DVT || a.f.H <= 0 || a.f.BH % a.f.H) return 5;
   if (a.f.DK == 256) return launch_bwd<256>(a, st);
   if (a.f.DK == 128) return launch_bwd<128>(a, st);
   return 5;

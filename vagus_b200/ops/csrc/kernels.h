@@ -61,16 +61,17 @@ struct GdrRecArgs {
   const void* U;                                   // (BH, N, C, DV) bf16
   const float* gC;                                 // (BH, N)
   const float* S0;                                 // (BH, DK, DV) or null
-  void* O;                                         // (BH, N, C, DV) bf16
+  void* O;                                         // (B, N*C, H, DV) bf16, token-major
   void* Vp;                                        // (BH, N, C, DV) bf16: V' (written fwd, read bwd)
   void* states;                                    // (BH, N, DK, DV) bf16 entry states (written fwd, read bwd)
   float* S_out;                                    // (BH, DK, DV) or null
   long long BH; int N, DK, DV;
+  int H;                                           // heads (BH = B * H)
 };
 int gdr_rec_fwd(const GdrRecArgs& a, cudaStream_t st);
 struct GdrRecBwdArgs {
   GdrRecArgs f;
-  const void* dO;                                  // (BH, N, C, DV) bf16
+  const void* dO;                                  // (B, N*C, H, DV) bf16, token-major
   const float* dS_final;                           // (BH, DK, DV) or null
   void* dW; void* dQh; void* dKt;                  // (BH, N, C, DK) bf16
   float* dA;                                       // (BH, N, C, C) fp32

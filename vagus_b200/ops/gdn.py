@@ -69,8 +69,7 @@ def _gdr_fwd(q, k, v, g, beta, S0, scale):
     W, Qh, Kt, A, U, gCf = native().gdr_intra_fwd(q, k, v, g, beta, scale)
     ops16 = [W, Qh, Kt, A, U]
     S0f = None if S0 is None else S0.float().reshape(B * H, dk, dv).contiguous()
-    O, Vp, states, S_out = native().gdr_rec_fwd(*ops16, gCf, S0f, True)
-    o = O.view(B, H, N, CHUNK, dv).permute(0, 2, 3, 1, 4).reshape(B, L, H, dv)
+    o, Vp, states, S_out = native().gdr_rec_fwd(*ops16, gCf, S0f, True, H)     # o token-major (B, L, H, dv)
     saved = (q, k, v, g, beta, ops16[0], ops16[1], ops16[2], ops16[3], Vp, gCf, states)
     return o, S_out.view(B, H, dk, dv), saved
 
@@ -81,10 +80,10 @@ def _gdr_bwd(saved, do, dS, scale, need_dS0):
     B, L, H, dk = q.shape
     dv = v.shape[-1]
     N = L // CHUNK
-    dO = do.to(torch.bfloat16).reshape(B, N, CHUNK, H, dv).permute(0, 3, 1, 2, 4).reshape(B * H, N, CHUNK, dv)
+    dO = do.to(torch.bfloat16).reshape(B, L, H, dv).contiguous()          # token-major, as the kernels read it
     dSf = None if dS is None else dS.float().reshape(B * H, dk, dv).contiguous()
     dW, dQh, dKt, dA, dU, dgC, dS0 = native().gdr_rec_bwd(W16, Qh16, Kt16, A16, Vp, gCf, states,
-                                                          dO.contiguous(), dSf, need_dS0)
+                                                          dO, dSf, need_dS0)
     gq, gk, gv, gg, gb = native().gdr_intra_bwd(q, k, v, g, beta, dW, dQh, dKt, dA, dU, dgC, scale)
     return gq, gk, gv, gg, gb, (dS0.view(B, H, dk, dv) if need_dS0 else None)
 
