@@ -115,3 +115,19 @@ def test_utils(tmp_path):
     assert set(g) >= {"commit", "dirty"}
     t = torch.zeros(2, dtype=torch.bfloat16)
     assert infer_device((t,), {}).type == "cpu" and infer_dtype((t,), {}) == torch.bfloat16
+
+
+def test_every_recipe_loads_and_builds():
+    """Each committed train recipe (with its model recipe) parses, keeps its
+    declared global batch, and builds its model (on the meta device)."""
+    from pathlib import Path
+    from vagus_b200.models import build_model
+    from vagus_b200.train.main import TrainConfig
+    recipes = sorted((Path(__file__).resolve().parents[1] / "recipe" / "train").glob("*.yaml"))
+    assert recipes
+    for f in recipes:
+        c = TrainConfig.from_yaml(f)
+        if c.global_batch_tokens is not None:
+            assert c.world_size * c.batch_size * c.grad_accum_steps * c.context_len == c.global_batch_tokens, f
+        with torch.device("meta"):
+            build_model(c.model_name, c.model_args)

@@ -123,3 +123,16 @@ def test_from_yaml_with_model_recipe(tmp_path):
     assert cfg.model_args == {"dim": 64} and cfg.batch_size == 8
     with pytest.raises(TypeError):
         tm.TrainConfig.from_yaml(tmp_path / "t.yaml", ["nonsense_key=1"])
+
+
+def test_registry_record(tmp_path):
+    import json
+    from vagus_b200.registry import write_record
+    run = tm.train(_config(tmp_path, "r", 3))
+    assert (run / "metrics.jsonl").exists()
+    path = write_record(run, tmp_path / "registry", incidents=["none"], note="unit")
+    rec = json.loads(path.read_text())
+    assert set(rec) >= {"run", "recipe", "data", "results", "incidents", "archive"}
+    assert rec["results"]["final_step"] == 3 and rec["results"]["loss_tail5"] is not None
+    assert any(a["file"] == "model-final.pt" for a in rec["archive"])
+    assert (run / "SHA256SUMS").read_text().count("\n") == len(rec["archive"])

@@ -377,7 +377,7 @@ def train(config: TrainConfig, teardown: bool = True):
     monitor = Monitor(ctx, tokens_per_step, steps_total, log_interval=config.log_interval,
                       slow_interval=config.slow_interval, fast=FAST_METRICS + list(hooks.get("fast", [])),
                       slow=SLOW_METRICS + list(hooks.get("slow", [])), tb_dir=run_dir / "tb" if is_main else None,
-                      log_fn=log)
+                      log_fn=log, jsonl_path=run_dir / "metrics.jsonl" if is_main else None)
     runner = StepRunner(model, optimizer, ce_fn, device, grad_accum_steps=config.grad_accum_steps,
                         grad_clip=config.grad_clip, is_fsdp=is_fsdp, is_dist=is_dist,
                         replicate_size=replicate_size, autocast=autocast, mesh=mesh)

@@ -13,6 +13,7 @@ Parity: reference ``infra/train/metrics.py:59-267``.
 from __future__ import annotations
 
 import math
+import json
 import time
 from contextlib import nullcontext
 from dataclasses import dataclass
@@ -135,7 +136,7 @@ SLOW_METRICS = [metric_param_norms, metric_update_ratio]
 class Monitor:
     def __init__(self, ctx: MetricCtx, tokens_per_step: int, steps_total: int, *, log_interval: int,
                  slow_interval: int, tb_dir=None, meta_text: str | None = None, log_fn: Callable = print,
-                 print_every: int = 10, fast=FAST_METRICS, slow=SLOW_METRICS):
+                 print_every: int = 10, fast=FAST_METRICS, slow=SLOW_METRICS, jsonl_path=None):
         self.ctx = ctx
         self.tokens_per_step = tokens_per_step
         self.steps_total = steps_total
@@ -147,6 +148,8 @@ class Monitor:
         self.slow = slow
         self.writer = None
         self.history: list[dict] = []
+        # one JSON line per logged step (the run registry reads it)
+        self.jsonl = open(jsonl_path, "a", encoding="utf-8") if jsonl_path is not None else None
         if tb_dir is not None:
             try:
                 from torch.utils.tensorboard import SummaryWriter
@@ -186,7 +189,11 @@ class Monitor:
             with (c.slow_context() if c.slow_context is not None else nullcontext()):
                 for fn in self.slow:
                     scalars |= fn(c)
-        self.history.append({"step": step, **{k: v for k, v in scalars.items() if isinstance(v, (int, float))}})
+        row = {"step": step, **{k: v for k, v in scalars.items() if isinstance(v, (int, float))}}
+        self.history.append(row)
+        if self.jsonl is not None:
+            self.jsonl.write(json.dumps(row) + "\n")
+            self.jsonl.flush()
         if self.writer is not None:
             for k, v in scalars.items():
                 self.writer.add_scalar(k, v, step)
@@ -195,5 +202,8 @@ class Monitor:
                         f"lr {c.lr:.2e} | gnorm {c.grad_norm:.2f} | {c.tokens_per_s / 1e6:.2f} Mtok/s")
 
     def close(self):
+        if self.jsonl is not None:
+            self.jsonl.close()
+            self.jsonl = None
         if self.writer is not None:
             self.writer.close()
