@@ -709,6 +709,282 @@ __global__ void attn_bwd_post(const float* __restrict__ acc, __nv_bfloat16* __re
   *reinterpret_cast<uint2*>(dq + i) = make_uint2(pack_bf16x2(scale * v.x, scale * v.y), pack_bf16x2(scale * v.z, scale * v.w));
 }
 
+// ----------------------------------------------------- tcgen05 backward --
+// One CTA per (128 keys, batch * kv head), walking every (query head of the
+// group, 128-query block) step; 10 warps:
+//   warp 0      TMA: K and V once, then Q and dO of each step (single buffer,
+//               refilled when the step's last products are done);
+//   warp 1      TMEM owner and MMA issuer, per step
+//                 S^T = K Q^T and dP^T = V dO^T          (M = 128 keys, N = 128 queries)
+//                 dV += P^T dO, dK += dS^T Q               (M = 128 keys, N = D)
+//                 dQ  = dS K                               (M = 128 queries, N = D)
+//               with dQ written into the score columns once they are read;
+//   warps 2-9   two threads per key row (one per half of the query columns):
+//               P^T = exp(S^T scale - lse), dS^T = P^T (dP^T - delta) into
+//               shared memory as bf16 (the K-major / MN-major operand of the
+//               next products), then two threads per query row add the dQ
+//               rows to the fp32 dq accumulator with 16-byte atomics; at the
+//               end the same warps write dK (scaled) and dV.
+// delta = rowsum(dO o O) comes from the pre-pass and dq is scaled / rounded
+// by the post-pass of the mma.sync backward above.  Every wait is bounded.
+namespace tcbw {
+constexpr int KROWS = 128, QROWS = 128, THREADS = 320;
+template <int D>
+struct Layout {
+  static constexpr int T_BYTES = 128 * D * 2;     // K, V, Q, dO tiles: D/64 K-major chunks of 16 KB
+  static constexpr int P_BYTES = 128 * 128 * 2;   // P^T, dS^T: 2 chunks of 64 query columns
+  static constexpr int OFF_V = T_BYTES, OFF_Q = 2 * T_BYTES, OFF_DO = 3 * T_BYTES;
+  static constexpr int OFF_P = 4 * T_BYTES, OFF_DS = OFF_P + P_BYTES;
+  static constexpr int OFF_STAT = OFF_DS + P_BYTES;            // lse[128], delta[128]
+  static constexpr int OFF_BAR = OFF_STAT + 1024;
+  static constexpr int RAW = OFF_BAR + 128 + 1024;
+  static constexpr int SMEM = RAW > 120 * 1024 ? RAW : 120 * 1024;
+  static constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 256 + D, COLS = 512;
+};
+struct Params {
+  int Lq, Lk, H, Hk, causal;
+  float sl2, scale;
+  const float* lse;
+  const float* delta;
+  float* dq_acc;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  int* err;
+};
+}  // namespace tcbw
+
+template <int D>
+__global__ void __launch_bounds__(tcbw::THREADS, 1)
+attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
+            const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo, const tcbw::Params p) {
+  using namespace tcbw;
+  using Lt = Layout<D>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sk = sm, *sv = sm + Lt::OFF_V, *sq = sm + Lt::OFF_Q, *sdo = sm + Lt::OFF_DO;
+  uint8_t *spt = sm + Lt::OFF_P, *sdst = sm + Lt::OFF_DS;
+  float* s_lse = reinterpret_cast<float*>(sm + Lt::OFF_STAT);
+  float* s_delta = s_lse + 128;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
+  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 2, *s_full = bars + 3, *p_full = bars + 4,
+           *mma2 = bars + 5, *dq_free = bars + 6;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int kb = blockIdx.x, bhk = blockIdx.y;
+  const int b = bhk / p.Hk, hk = bhk % p.Hk;
+  const int group = p.H / p.Hk;
+  const int k0 = kb * KROWS;
+  const int offs = p.Lk - p.Lq;
+  const int q_first = p.causal ? max(0, k0 - offs) : 0;
+  const int qb0 = q_first / QROWS, nqb = (p.Lq + QROWS - 1) / QROWS;
+  const int per_head = max(0, nqb - qb0);
+  const int nsteps = group * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(q_empty, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_full, 8);
+    mbar_init(mma2, 1);
+    mbar_init(dq_free, 8);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mq);
+    tma_prefetch_desc(&mk);
+    tma_prefetch_desc(&mv);
+    tma_prefetch_desc(&mdo);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Lt::COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0 && nsteps > 0) {
+      mbar_arrive_expect_tx(kv_full, 2 * Lt::T_BYTES);
+      for (int c = 0; c < D / 64; ++c) {
+        tma_load_4d(sk + c * 16384, &mk, kv_full, 64 * c, k0, hk, b);
+        tma_load_4d(sv + c * 16384, &mv, kv_full, 64 * c, k0, hk, b);
+      }
+      for (int st = 0; st < nsteps; ++st) {
+        const int h = hk * group + st / per_head, q0 = (qb0 + st % per_head) * QROWS;
+        if (!mbar_wait(q_empty, (st & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(q_full, 2 * Lt::T_BYTES);
+        for (int c = 0; c < D / 64; ++c) {
+          tma_load_4d(sq + c * 16384, &mq, q_full, 64 * c, q0, h, b);
+          tma_load_4d(sdo + c * 16384, &mdo, q_full, 64 * c, q0, h, b);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nsteps > 0) {
+      constexpr uint32_t id_s = make_idesc_bf16(KROWS, QROWS, false, false);
+      constexpr uint32_t id_kv = make_idesc_bf16(KROWS, D, false, true);
+      constexpr uint32_t id_q = make_idesc_bf16(QROWS, D, true, true);
+      const uint32_t ak = smem_u32(sk), av = smem_u32(sv), aq = smem_u32(sq), ado = smem_u32(sdo);
+      const uint32_t ap = smem_u32(spt), ads = smem_u32(sdst);
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
+      for (int st = 0; ok && st < nsteps; ++st) {
+        if (!mbar_wait(q_full, st & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        if (st > 0 && !mbar_wait(dq_free, (st - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acc = (c | kk) ? 1u : 0u;
+            tc_mma_f16(tb + Lt::C_S, make_sw128_desc(ak + c * 16384 + kk * 32, 16, 1024),
+                       make_sw128_desc(aq + c * 16384 + kk * 32, 16, 1024), id_s, acc);
+            tc_mma_f16(tb + Lt::C_DP, make_sw128_desc(av + c * 16384 + kk * 32, 16, 1024),
+                       make_sw128_desc(ado + c * 16384 + kk * 32, 16, 1024), id_s, acc);
+          }
+        tc_commit(s_full);
+        if (!mbar_wait(p_full, st & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        // dV += P^T dO, dK += dS^T Q: K = the 128 queries (2 chunks x 4 steps of 16)
+#pragma unroll
+        for (int kc = 0; kc < 2; ++kc)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint32_t acc = (st > 0 || kc > 0 || kk > 0) ? 1u : 0u;
+            const uint32_t row = static_cast<uint32_t>((kc * 4 + kk) * 2048);
+            tc_mma_f16(tb + Lt::C_DV, make_sw128_desc(ap + kc * 16384 + kk * 32, 16, 1024),
+                       make_sw128_desc(ado + row, 16384, 1024), id_kv, acc);
+            tc_mma_f16(tb + Lt::C_DK, make_sw128_desc(ads + kc * 16384 + kk * 32, 16, 1024),
+                       make_sw128_desc(aq + row, 16384, 1024), id_kv, acc);
+          }
+        // dQ = dS K into the score columns: K = the 128 keys (8 steps of 16 rows)
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          tc_mma_f16(tb + Lt::C_S, make_sw128_desc(ads + kk * 2048, 16384, 1024),
+                     make_sw128_desc(ak + kk * 2048, 16384, 1024), id_q, kk ? 1u : 0u);
+        tc_commit(mma2);
+        tc_commit(q_empty);
+      }
+    }
+  } else {
+    const int quarter = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const int row = quarter * 32 + lane;                 // key row (S^T, dK, dV) / query row (dQ)
+    const uint32_t tl = tb + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int t = threadIdx.x - 64;                      // 0..255 over the softmax warps
+    const int kj = k0 + row;
+    bool ok = true;
+    for (int st = 0; st < nsteps; ++st) {
+      const int h = hk * group + st / per_head, q0 = (qb0 + st % per_head) * QROWS;
+      const long long rowbase = ((long long)b * p.H + h) * p.Lq;
+      asm volatile("bar.sync 1, 256;" ::: "memory");     // the previous step's statistics are consumed
+      if (t < 128) {
+        const int qi = q0 + t;
+        s_lse[t] = qi < p.Lq ? p.lse[rowbase + qi] * kLog2e : INFINITY;
+      } else {
+        const int qi = q0 + t - 128;
+        s_delta[t - 128] = qi < p.Lq ? p.delta[rowbase + qi] : 0.f;
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      ok = ok && mbar_wait_spin(s_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      tc_fence_after();
+      float sv[64], dp[64];
+      const uint32_t cs = tl + Lt::C_S + static_cast<uint32_t>(64 * half);
+      const uint32_t cd = tl + Lt::C_DP + static_cast<uint32_t>(64 * half);
+      tmem_ld_32x32b_x32(cs, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_ld_32x32b_x32(cs + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      tmem_ld_32x32b_x32(cd, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+      tmem_ld_32x32b_x32(cd + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
+      tmem_ld_wait();
+      const int qbase = q0 + 64 * half;
+      const bool full = (k0 + KROWS <= p.Lk) && (q0 + QROWS <= p.Lq) && (!p.causal || k0 + KROWS - 1 <= q0 + offs);
+#pragma unroll
+      for (int i = 0; i < 64; ++i) {
+        const bool vis = full || (kj < p.Lk && qbase + i < p.Lq && (!p.causal || kj <= qbase + i + offs));
+        const float pr = vis ? ex2_approx(fmaf(sv[i], p.sl2, -s_lse[64 * half + i])) : 0.f;
+        sv[i] = pr;
+        dp[i] = pr * (dp[i] - s_delta[64 * half + i]);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const uint32_t off = static_cast<uint32_t>(half * 16384 + row * 128 + ((u ^ (row & 7)) * 16));
+        const float* a8 = &sv[8 * u];
+        const float* d8 = &dp[8 * u];
+        *reinterpret_cast<uint4*>(spt + off) = make_uint4(pack_bf16x2(a8[0], a8[1]), pack_bf16x2(a8[2], a8[3]),
+                                                          pack_bf16x2(a8[4], a8[5]), pack_bf16x2(a8[6], a8[7]));
+        *reinterpret_cast<uint4*>(sdst + off) = make_uint4(pack_bf16x2(d8[0], d8[1]), pack_bf16x2(d8[2], d8[3]),
+                                                           pack_bf16x2(d8[4], d8[5]), pack_bf16x2(d8[6], d8[7]));
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+      // dQ rows (this thread: query q0 + row, columns half * D / 2 ..) -> fp32 accumulator
+      ok = ok && mbar_wait_spin(mma2, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      tc_fence_after();
+      const int qi = q0 + row;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t r[32];
+        const int col = half * (D / 2) + 32 * c;
+        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(col), r);
+        tmem_ld_wait();
+        if (ok && qi < p.Lq) {
+          float* dst = p.dq_acc + (rowbase + qi) * D + col;
+#pragma unroll
+          for (int e = 0; e < 32; e += 4)
+            atomicAdd(reinterpret_cast<float4*>(dst + e),
+                      make_float4(__uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
+                                  __uint_as_float(r[e + 3])));
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+    }
+    // dK (scaled) and dV rows of this CTA's keys
+    const bool have = ok && nsteps > 0;
+    if (have) tc_fence_after();
+#pragma unroll
+    for (int which = 0; which < 2; ++which) {
+      __nv_bfloat16* out = (which == 0 ? p.dk : p.dv) + (((long long)b * p.Hk + hk) * p.Lk) * D;
+      const uint32_t base = which == 0 ? Lt::C_DK : Lt::C_DV;
+      const float sc = which == 0 ? p.scale : 1.f;
+#pragma unroll
+      for (int c = 0; c < D / 64; ++c) {
+        uint32_t r[32];
+        const int col = half * (D / 2) + 32 * c;
+        if (have) {
+          tmem_ld_32x32b_x32(tl + base + static_cast<uint32_t>(col), r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) r[e] = 0u;
+        }
+        if (kj < p.Lk) {
+          __nv_bfloat16* dst = out + (long long)kj * D + col;
+#pragma unroll
+          for (int e = 0; e < 32; e += 8) {
+            const float* f = reinterpret_cast<const float*>(&r[e]);
+            *reinterpret_cast<uint4*>(dst + e) =
+                make_uint4(pack_bf16x2(sc * f[0], sc * f[1]), pack_bf16x2(sc * f[2], sc * f[3]),
+                           pack_bf16x2(sc * f[4], sc * f[5]), pack_bf16x2(sc * f[6], sc * f[7]));
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tb, Lt::COLS);
+  }
+}
+
 template <typename Kern>
 bool set_smem(Kern kern, size_t bytes) {
   return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)) ==
@@ -765,6 +1041,53 @@ int launch_fwd(const AttnArgs& a, cudaStream_t st) {
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+template <int D>
+int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
+  using Lt = tcbw::Layout<D>;
+  const AttnArgs& f = a.f;
+  alignas(64) unsigned char mq[128], mk[128], mv[128], mdo[128];
+  const unsigned long long dq[4] = {(unsigned long long)D, (unsigned long long)f.Lq, (unsigned long long)f.H,
+                                    (unsigned long long)f.B};
+  const unsigned long long dk[4] = {(unsigned long long)D, (unsigned long long)f.Lk, (unsigned long long)f.Hk,
+                                    (unsigned long long)f.B};
+  const unsigned long long sq[3] = {(unsigned long long)f.sq_l * 2, (unsigned long long)f.sq_h * 2,
+                                    (unsigned long long)f.sq_b * 2};
+  const unsigned long long sk[3] = {(unsigned long long)f.sk_l * 2, (unsigned long long)f.sk_h * 2,
+                                    (unsigned long long)f.sk_b * 2};
+  const unsigned long long sv[3] = {(unsigned long long)f.sv_l * 2, (unsigned long long)f.sv_h * 2,
+                                    (unsigned long long)f.sv_b * 2};
+  const unsigned long long so[3] = {(unsigned long long)f.so_l * 2, (unsigned long long)f.so_h * 2,
+                                    (unsigned long long)f.so_b * 2};
+  const unsigned box[4] = {64u, 128u, 1u, 1u};
+  if (!encode_bf16_map(mq, f.q, 4, dq, sq, box) || !encode_bf16_map(mk, f.k, 4, dk, sk, box) ||
+      !encode_bf16_map(mv, f.v, 4, dk, sv, box) || !encode_bf16_map(mdo, a.dO, 4, dq, so, box))
+    return 2;
+  tcbw::Params p;
+  p.Lq = f.Lq; p.Lk = f.Lk; p.H = f.H; p.Hk = f.Hk; p.causal = f.causal;
+  p.sl2 = f.scale * kLog2e; p.scale = f.scale;
+  p.lse = f.lse; p.delta = a.delta; p.dq_acc = a.dq_acc;
+  p.dk = (__nv_bfloat16*)a.dk; p.dv = (__nv_bfloat16*)a.dv; p.err = f.err;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr_set[dev]) {
+    if (cudaFuncSetAttribute(attn_bwd_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess)
+      return 3;
+    attr_set[dev] = true;
+  }
+  const long long rows = (long long)f.B * f.H * f.Lq;
+  attn_bwd_pre<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+  dim3 grid(static_cast<unsigned>((f.Lk + tcbw::KROWS - 1) / tcbw::KROWS), static_cast<unsigned>(f.B * f.Hk));
+  attn_bwd_tc<D><<<grid, tcbw::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
+                                                         *reinterpret_cast<const CUtensorMap*>(mk),
+                                                         *reinterpret_cast<const CUtensorMap*>(mv),
+                                                         *reinterpret_cast<const CUtensorMap*>(mdo), p);
+  const long long n = rows * D;
+  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a.dq_acc, (__nv_bfloat16*)a.dq, n,
+                                                                              f.scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
 template <int D, int DV>
 int launch_bwd(const AttnBwdArgs& a, cudaStream_t st) {
   const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
@@ -805,6 +1128,9 @@ int attn_fwd(const AttnArgs& a, cudaStream_t st) {
 
 int attn_bwd(const AttnBwdArgs& a, cudaStream_t st) {
   if (!strides_ok(a.f) || !aligned16(a.dO) || a.f.Lq <= 0 || a.f.Lk <= 0) return 5;
+  static const bool no_tc = std::getenv("VAGUS_ATTN_NO_TC") != nullptr;
+  if (!no_tc && a.f.err && a.f.Lq >= 128 && a.f.Lk >= 128 && a.f.D == a.f.Dv && (a.f.D == 64 || a.f.D == 128))
+    return a.f.D == 64 ? launch_bwd_tc<64>(a, st) : launch_bwd_tc<128>(a, st);
   if (a.f.D == 64 && a.f.Dv == 64) return launch_bwd<64, 64>(a, st);
   if (a.f.D == 128 && a.f.Dv == 128) return launch_bwd<128, 128>(a, st);
   if (a.f.D == 64 && a.f.Dv == 128) return launch_bwd<64, 128>(a, st);
