@@ -56,7 +56,7 @@ CONFIGS = {
                         value_head_dim=256, ffn_hidden_dim=5632, short_conv_size=4, gate="scalar", delta=True,
                         chunk_size=64, layer_pattern="gdn,gdn,gdn,softmax", softmax_head_dim=128,
                         context_len=4096, la_impl="auto"),
-        seq=4096, global_tokens=1048576, micro=2, label="1.3B hybrid GDN/softmax 3:1"),
+        seq=4096, global_tokens=1048576, micro=4, label="1.3B hybrid GDN/softmax 3:1"),
     # BASELINE config #2
     "tpp340m": dict(
         model_name="TransformerPP",

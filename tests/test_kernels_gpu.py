@@ -413,3 +413,24 @@ def test_flash_attention_fwd_bwd(D, causal, H, Hk, Lq, Lk):
     assert rel(q.grad, qf.grad) < 2e-2
     assert rel(k.grad, kf.grad) < 2e-2
     assert rel(v.grad, vf.grad) < 2e-2
+
+
+@pytest.mark.parametrize("D", [512, 1024, 2048])
+def test_rmsnorm_backward_wide_rows(D):
+    """The vectorised residual-stream backward (register and shared-memory
+    gamma-partial variants) against the fp32 autograd reference."""
+    from vagus_b200.ops import native
+    T = 1000
+    x = torch.randn(T, D, device=DEV)
+    gamma = 1 + 0.1 * torch.randn(D, device=DEV)
+    dy = torch.randn(T, D, device=DEV).bfloat16()
+    dres = torch.randn(T, D, device=DEV)
+    y, rstd = native().rmsnorm_fwd(x, gamma, 1e-6, False)
+    dx, dg, dx16 = native().rmsnorm_bwd(dy, x, gamma, rstd, dres, True, True)
+    xr = x.clone().requires_grad_(True)
+    gr = gamma.clone().requires_grad_(True)
+    yr = xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-6) * gr
+    (yr * dy.float()).sum().backward()
+    assert rel(dx, xr.grad + dres) < 1e-4
+    assert rel(dg, gr.grad) < 1e-4
+    assert rel(dx16.float(), dx) < 1e-2

@@ -86,65 +86,94 @@ __global__ void rmsnorm_bwd_k(const TG* __restrict__ dy, const TI* __restrict__ 
 // per CTA.  dx16, when given, receives a bf16 copy of dx (the operand the
 // next GEMM backward consumes).
 template <typename TG, int NV>
-__global__ void __launch_bounds__(256, 2)
+__global__ void __launch_bounds__(256, NV >= 8 ? 1 : 2)
 rmsnorm_bwd_vec_k(const TG* __restrict__ dy, const float* __restrict__ x, const float* __restrict__ gamma,
                   const float* __restrict__ rstd, const float* __restrict__ dres, float* __restrict__ dx,
                   __nv_bfloat16* __restrict__ dx16, float* __restrict__ dgamma, long long rows) {
   constexpr int D = 128 * NV;
+  // rows wider than 1024 keep the gamma-gradient partials in a per-warp
+  // shared-memory row (each lane owns its columns: no atomics) instead of
+  // registers, which would spill
+  constexpr bool kSmemAcc = NV > 8;
   __shared__ __align__(16) float sgam[D];
   __shared__ float sg[D];
+  extern __shared__ __align__(16) float sacc[];     // [8][D] when kSmemAcc
   for (int c = threadIdx.x; c < D; c += blockDim.x) { sgam[c] = gamma[c]; sg[c] = 0.f; }
-  __syncthreads();
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  float4 acc[NV];
+  float* wacc = kSmemAcc ? sacc + warp * D : nullptr;
+  if constexpr (kSmemAcc) {
+    for (int c = lane * 4; c < D; c += 128) *reinterpret_cast<float4*>(wacc + c) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __syncthreads();
+  float4 acc[kSmemAcc ? 1 : NV];
 #pragma unroll
-  for (int j = 0; j < NV; ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int j = 0; j < (kSmemAcc ? 1 : NV); ++j) acc[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // two passes over the row (the second re-reads x and dy, which are in L1
+  // by then)
+  auto load_row = [&](long long r, int j, float4& xv, float4& gv) {
+    const int c = 4 * lane + 128 * j;
+    xv = *reinterpret_cast<const float4*>(x + r * D + c);
+    if constexpr (sizeof(TG) == 4) {
+      gv = *reinterpret_cast<const float4*>(dy + r * D + c);
+    } else {
+      const uint2 u = *reinterpret_cast<const uint2*>(dy + r * D + c);
+      const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+      gv = make_float4(a.x, a.y, b.x, b.y);
+    }
+  };
   for (long long r = (long long)blockIdx.x * 8 + warp; r < rows; r += (long long)gridDim.x * 8) {
     const float rs = rstd[r];
-    float4 xv[NV], gv[NV];
-#pragma unroll
-    for (int j = 0; j < NV; ++j) {
-      const int c = 4 * lane + 128 * j;
-      xv[j] = *reinterpret_cast<const float4*>(x + r * D + c);
-      if constexpr (sizeof(TG) == 4) {
-        gv[j] = *reinterpret_cast<const float4*>(dy + r * D + c);
-      } else {
-        const uint2 u = *reinterpret_cast<const uint2*>(dy + r * D + c);
-        const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
-        gv[j] = make_float4(a.x, a.y, b.x, b.y);
-      }
-    }
     float dot = 0.f;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
+      float4 xv, gv;
+      load_row(r, j, xv, gv);
       const float4 gm = *reinterpret_cast<const float4*>(sgam + 4 * lane + 128 * j);
-      dot += gv[j].x * gm.x * xv[j].x + gv[j].y * gm.y * xv[j].y + gv[j].z * gm.z * xv[j].z + gv[j].w * gm.w * xv[j].w;
+      dot += gv.x * gm.x * xv.x + gv.y * gm.y * xv.y + gv.z * gm.z * xv.z + gv.w * gm.w * xv.w;
     }
     dot = warp_sum(dot) * rs / D;
 #pragma unroll
     for (int j = 0; j < NV; ++j) {
       const int c = 4 * lane + 128 * j;
+      float4 xv, gv;
+      load_row(r, j, xv, gv);
       const float4 gm = *reinterpret_cast<const float4*>(sgam + c);
-      float4 h = make_float4(xv[j].x * rs, xv[j].y * rs, xv[j].z * rs, xv[j].w * rs);
-      float4 o = make_float4(rs * (gv[j].x * gm.x - h.x * dot), rs * (gv[j].y * gm.y - h.y * dot),
-                             rs * (gv[j].z * gm.z - h.z * dot), rs * (gv[j].w * gm.w - h.w * dot));
+      const float4 h = make_float4(xv.x * rs, xv.y * rs, xv.z * rs, xv.w * rs);
+      float4 o = make_float4(rs * (gv.x * gm.x - h.x * dot), rs * (gv.y * gm.y - h.y * dot),
+                             rs * (gv.z * gm.z - h.z * dot), rs * (gv.w * gm.w - h.w * dot));
       if (dres) {
         const float4 d = *reinterpret_cast<const float4*>(dres + r * D + c);
         o.x += d.x; o.y += d.y; o.z += d.z; o.w += d.w;
       }
       *reinterpret_cast<float4*>(dx + r * D + c) = o;
       if (dx16) *reinterpret_cast<uint2*>(dx16 + r * D + c) = make_uint2(pack_bf16x2(o.x, o.y), pack_bf16x2(o.z, o.w));
-      acc[j].x += gv[j].x * h.x; acc[j].y += gv[j].y * h.y; acc[j].z += gv[j].z * h.z; acc[j].w += gv[j].w * h.w;
+      if constexpr (kSmemAcc) {
+        float4 a4 = *reinterpret_cast<float4*>(wacc + c);
+        a4.x += gv.x * h.x; a4.y += gv.y * h.y; a4.z += gv.z * h.z; a4.w += gv.w * h.w;
+        *reinterpret_cast<float4*>(wacc + c) = a4;
+      } else {
+        acc[j].x += gv.x * h.x; acc[j].y += gv.y * h.y; acc[j].z += gv.z * h.z; acc[j].w += gv.w * h.w;
+      }
     }
   }
+  if constexpr (kSmemAcc) {
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) {
+      float t = 0.f;
 #pragma unroll
-  for (int j = 0; j < NV; ++j) {
-    const int c = 4 * lane + 128 * j;
-    atomicAdd(&sg[c], acc[j].x); atomicAdd(&sg[c + 1], acc[j].y);
-    atomicAdd(&sg[c + 2], acc[j].z); atomicAdd(&sg[c + 3], acc[j].w);
+      for (int w = 0; w < 8; ++w) t += sacc[w * D + c];
+      atomicAdd(&dgamma[c], t);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < NV; ++j) {
+      const int c = 4 * lane + 128 * j;
+      atomicAdd(&sg[c], acc[j].x); atomicAdd(&sg[c + 1], acc[j].y);
+      atomicAdd(&sg[c + 2], acc[j].z); atomicAdd(&sg[c + 3], acc[j].w);
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
   }
-  __syncthreads();
-  for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
 }
 
 // ------------------------------------------------------- rmsnorm_gated --
@@ -323,9 +352,17 @@ int rmsnorm_bwd(const void* dy, int dy_f32, const void* x, int x_f32, const floa
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const long long need = (rows + 7) / 8;
-    const int grid = static_cast<int>(std::min<long long>(need, 2LL * sms));
-#define RV(TG, NV) rmsnorm_bwd_vec_k<TG, NV><<<grid, 256, 0, s>>>((const TG*)dy, (const float*)x, gamma, rstd, dres, \
-                                                                  (float*)dx, (__nv_bfloat16*)dx16, dgamma, rows)
+    const int per_sm = D >= 1024 ? 1 : 2;      // the wide rows keep their gamma partials in 255 registers
+    const int grid = static_cast<int>(std::min<long long>(need, (long long)per_sm * sms));
+#define RV(TG, NV)                                                                                       \
+  do {                                                                                                   \
+    const int dyn = NV > 8 ? 8 * 128 * NV * 4 : 0;                                                       \
+    if (dyn && cudaFuncSetAttribute(rmsnorm_bwd_vec_k<TG, NV>, cudaFuncAttributeMaxDynamicSharedMemorySize, \
+                                    dyn) != cudaSuccess)                                                 \
+      return 3;                                                                                          \
+    rmsnorm_bwd_vec_k<TG, NV><<<grid, 256, dyn, s>>>((const TG*)dy, (const float*)x, gamma, rstd, dres,   \
+                                                     (float*)dx, (__nv_bfloat16*)dx16, dgamma, rows);    \
+  } while (0)
 #define RVD(TG) switch (D) { case 512: RV(TG, 4); break; case 768: RV(TG, 6); break; case 1024: RV(TG, 8); break; \
                              case 1536: RV(TG, 12); break; default: RV(TG, 16); }
     if (dy_f32) { RVD(float) } else { RVD(__nv_bfloat16) }
