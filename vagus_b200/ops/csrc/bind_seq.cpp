@@ -5,6 +5,8 @@
 
 #include "kernels.h"
 
+int* vagus_device_error_ptr();   // bindings.cpp
+
 namespace {
 
 using torch::Tensor;
@@ -76,8 +78,9 @@ std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_l
   return {dA, ddt};
 }
 
-// Recurrence forward: returns (O, V', states, S_out).  The per-chunk entry
-// states (bf16) are always produced: the output stage reads them.
+// Recurrence forward: returns (O, V'^T, states, S_out).  The per-chunk entry
+// states (bf16, stored transposed as S_n^T (BH, N, DV, DK)) are always
+// produced: the output stage reads them.  V'^T is (BH, N, DV, 64).
 std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor U, Tensor gC,
                                 c10::optional<Tensor> S0, bool need_states, int64_t H) {
   (void)need_states;
@@ -87,12 +90,13 @@ std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
   TORCH_CHECK(W.size(2) == 64, "gdr: chunk size 64");
   for (auto* t : {&W, &Qh, &Kt, &A, &U}) TORCH_CHECK(t->is_contiguous() && t->scalar_type() == at::kBFloat16, "gdr: bf16");
   auto O = torch::empty({BH / H, static_cast<int64_t>(N) * 64, H, DV}, U.options());   // token-major
-  auto Vp = torch::empty_like(U);
-  auto states = torch::empty({BH, N, DK, DV}, W.options());
+  auto Vp = torch::empty({BH, N, DV, 64}, U.options());           // V'^T per chunk (value-major)
+  auto states = torch::empty({BH, N, DV, DK}, W.options());       // S_n^T per chunk (value-major)
   auto S_out = torch::empty({BH, DK, DV}, W.options().dtype(at::kFloat));
   vagus::GdrRecArgs a{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), U.data_ptr(),
                       gC.contiguous().data_ptr<float>(), fptr(S0), O.data_ptr(), Vp.data_ptr(),
-                      states.data_ptr(), S_out.data_ptr<float>(), BH, N, DK, DV, static_cast<int>(H)};
+                      states.data_ptr(), S_out.data_ptr<float>(), BH, N, DK, DV, static_cast<int>(H),
+                      vagus_device_error_ptr()};
   check(vagus::gdr_rec_fwd(a, stream()), "gdr_rec_fwd");
   return {O, Vp, states, S_out};
 }
@@ -102,7 +106,8 @@ std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
 std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor Vp, Tensor gC, Tensor states,
                                 Tensor dO, c10::optional<Tensor> dS_final, bool need_dS0) {
   const int64_t BH = W.size(0);
-  const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(Vp.size(3));
+  const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(Vp.size(2));
+  TORCH_CHECK(Vp.size(3) == 64 && states.size(2) == DV && states.size(3) == DK, "gdr_rec_bwd: value-major V', states");
   TORCH_CHECK(states.scalar_type() == at::kBFloat16 && states.is_contiguous(), "gdr_rec_bwd: bf16 states");
   dO = dO.contiguous();
   TORCH_CHECK(dO.dim() == 4 && dO.size(3) == DV && dO.scalar_type() == at::kBFloat16, "gdr_rec_bwd: dO (B, L, H, DV) bf16");

@@ -31,8 +31,11 @@
 //   gC, dgC: (BH, N) fp32   states, dstates: (BH, N, DK, DV) bf16
 //   dW, dQh, dKt: (BH, N, C, DK) bf16   dA: (BH, N, C, C) fp32
 #include "common.cuh"
+#include "gemm.h"
 #include "kernels.h"
 #include "mma.cuh"
+
+#include <cstdlib>
 
 namespace vagus {
 namespace {
@@ -60,6 +63,20 @@ __device__ __forceinline__ void store_tile(__nv_bfloat16* g, long long gp, const
   for (int i = threadIdx.x; i < rows * per_row; i += blockDim.x) {
     const int r = i / per_row, c = (i - r * per_row) * 8;
     *reinterpret_cast<uint4*>(g + r * gp + c) = *reinterpret_cast<const uint4*>(s + r * sp + c);
+  }
+}
+
+// smem tile [rows][cols] (pitch sp) -> global transposed g[c * gp + r]; rows % 8 == 0
+__device__ __forceinline__ void store_tile_t(__nv_bfloat16* g, long long gp, const __nv_bfloat16* s, int sp, int rows,
+                                             int cols) {
+  for (int i = threadIdx.x; i < cols * (rows / 8); i += blockDim.x) {
+    const int c = i % cols, r = (i / cols) * 8;
+    uint32_t w[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w[j] = static_cast<uint32_t>(__bfloat16_as_ushort(s[(r + 2 * j) * sp + c])) |
+             (static_cast<uint32_t>(__bfloat16_as_ushort(s[(r + 2 * j + 1) * sp + c])) << 16);
+    *reinterpret_cast<uint4*>(g + c * gp + r) = make_uint4(w[0], w[1], w[2], w[3]);
   }
 }
 
@@ -127,7 +144,7 @@ gdr_fwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
         }
     cp_wait_1();
     __syncthreads();
-    if (states) store_tile(states + cidx * DK * DV + v0, DV, &sm.S[0][0], DVT + PAD, DK, DVT);
+    if (states) store_tile_t(states + (cidx * DV + v0) * DK, DK, &sm.S[0][0], DVT + PAD, DK, DVT);
 
     // V' = U - W S
     {
@@ -144,7 +161,7 @@ gdr_fwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
         }
     }
     __syncthreads();
-    store_tile(Vp + cidx * C * DV + v0, DV, &sm.V[0][0], DVT + PAD, C, DVT);
+    store_tile_t(Vp + (cidx * DV + v0) * C, C, &sm.V[0][0], DVT + PAD, C, DVT);
 
     // S <- gC S + Kt^T V'
     const float g = gC[cidx];
@@ -170,15 +187,290 @@ gdr_fwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
   }
 }
 
+// ------------------------------------------------------ tcgen05 forward scan --
+// The same chain on the 5th-generation tensor cores, transposed so the value
+// tile is the MMA's M = 128: one CTA per (sequence, 128-wide value tile),
+// S^T (value x key, fp32) lives in TMEM, and per chunk
+//   D1   = S^T W^T                  (M = 128 values, N = 64 tokens, K = DK)
+//   V'^T = U^T - D1                  (state warps: TMEM -> registers -> bf16 smem)
+//   S^T += V'^T Kt                   (M = 128, N = DK, K = 64 tokens)
+// with S^T copied to bf16 shared memory (the A operand of the next D1) and
+// scaled by gC in TMEM by the state warps between the chunks.  Warp 0
+// streams W and Kt with TMA into a two-stage ring; warp 1 issues the MMAs and
+// the TMA stores of the bf16 S^T (the chunk-entry snapshot) and of V'^T
+// straight from the operand tiles, so the snapshots cost the state warps
+// nothing; warps 2-9 (two per TMEM lane quarter, one value row and half of
+// the columns per thread) do the rest.  Every wait is bounded.
+namespace tscan {
+constexpr int VT = 128;                  // value tile (MMA M)
+template <int DK>
+struct Layout {
+  static constexpr int W_BYTES = C * DK * 2;     // DK/64 chunks of [64 tokens x 128 B]
+  static constexpr int ST_BYTES = VT * DK * 2;   // DK/64 chunks of [128 values x 128 B]
+  static constexpr int VTB_BYTES = VT * C * 2;   // [128 values x 64 tokens]
+  static constexpr int U_BYTES = C * VT * 2;     // plain row-major [64 tokens][128 values]
+  static constexpr int OFF_K = 2 * W_BYTES;
+  static constexpr int OFF_ST = 4 * W_BYTES;
+  static constexpr int OFF_VT = OFF_ST + ST_BYTES;
+  static constexpr int OFF_U = OFF_VT + VTB_BYTES;
+  static constexpr int OFF_BAR = OFF_U + U_BYTES;
+  static constexpr int SMEM = OFF_BAR + 128 + 1024;
+  static constexpr uint32_t C_S = 0, C_D1 = DK, COLS = 512;
+};
+}  // namespace tscan
+
+template <int DK>
+__global__ void __launch_bounds__(320, 1)
+gdr_fwd_scan_tc(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mk,
+                const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mv,
+                const __nv_bfloat16* __restrict__ U, const float* __restrict__ gC, const float* __restrict__ S0,
+                float* __restrict__ S_out, int N, int DV, int* err) {
+  using namespace tscan;
+  using Lt = Layout<DK>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];   // re-aligned to 1024 (the swizzle atom) below
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sw = sm, *skt = sm + Lt::OFF_K, *sst = sm + Lt::OFF_ST, *svt = sm + Lt::OFF_VT;
+  __nv_bfloat16* su = reinterpret_cast<__nv_bfloat16*>(sm + Lt::OFF_U);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
+  uint64_t *w_full = bars, *w_empty = bars + 2, *s_ready = bars + 4, *d1_full = bars + 5, *v_full = bars + 6,
+           *s2_done = bars + 7;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 8);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int tiles_v = DV / VT;
+  const long long bh = blockIdx.x / tiles_v;
+  const int v0 = (blockIdx.x % tiles_v) * VT;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&w_full[i], 1);
+      mbar_init(&w_empty[i], 1);
+    }
+    mbar_init(s_ready, 8);
+    mbar_init(d1_full, 1);
+    mbar_init(v_full, 8);
+    mbar_init(s2_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&mw);
+    tma_prefetch_desc(&mk);
+    tma_prefetch_desc(&ms);
+    tma_prefetch_desc(&mv);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Lt::COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int n = 0; n < N; ++n) {
+        const int s = n & 1;
+        if (!mbar_wait(&w_empty[s], ((n >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&w_full[s], 2 * Lt::W_BYTES);
+        const int row = static_cast<int>((bh * N + n) * C);
+        for (int c = 0; c < DK / 64; ++c) {
+          tma_load_2d(sw + s * Lt::W_BYTES + c * 8192, &mw, &w_full[s], 64 * c, row);
+          tma_load_2d(skt + s * Lt::W_BYTES + c * 8192, &mk, &w_full[s], 64 * c, row);
+        }
+      }
+      // the last two stages' releases land before the CTA retires
+      for (int n = N; n < N + 2; ++n)
+        if (!mbar_wait(&w_empty[n & 1], ((n >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id1 = make_idesc_bf16(VT, C, false, false);
+      constexpr uint32_t id2 = make_idesc_bf16(VT, DK, false, true);
+      const uint32_t ast = smem_u32(sst), avt = smem_u32(svt);
+      for (int n = 0; n < N; ++n) {
+        const int s = n & 1;
+        const int srow = static_cast<int>((bh * N + n) * DV + v0);   // row of this tile in the value-major outputs
+        if (!mbar_wait(&w_full[s], (n >> 1) & 1, abort_flag, err, kErrTimeoutMma)) break;
+        if (!mbar_wait(s_ready, n & 1, abort_flag, err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t aw = smem_u32(sw + s * Lt::W_BYTES), ak = smem_u32(skt + s * Lt::W_BYTES);
+#pragma unroll
+        for (int c = 0; c < DK / 64; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(tb + Lt::C_D1, make_sw128_desc(ast + c * 16384 + kk * 32, 16, 1024),
+                       make_sw128_desc(aw + c * 8192 + kk * 32, 16, 1024), id1, (c | kk) ? 1u : 0u);
+        bulk_wait_read<0>();              // the previous V'^T store has read its tile
+        tc_commit(d1_full);
+        for (int c = 0; c < DK / 64; ++c) tma_store_2d(&ms, sst + c * 16384, 64 * c, srow);   // states[n] = S_n^T
+        bulk_commit();
+        if (!mbar_wait(v_full, n & 1, abort_flag, err, kErrTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_f16(tb + Lt::C_S, make_sw128_desc(avt + kk * 32, 16, 1024),
+                     make_sw128_desc(ak + kk * 2048, 8192, 1024), id2, 1u);
+        tma_store_2d(&mv, svt, 0, srow);  // V'^T
+        bulk_commit();
+        bulk_wait_read<1>();              // the S_n^T store has read its tile
+        tc_commit(s2_done);
+        tc_commit(&w_empty[s]);
+      }
+      bulk_wait<0>();
+    }
+  } else {
+    // ------------------------------------------------------------ state warps
+    // eight warps, two per TMEM lane quarter: thread (quarter, lane) owns value
+    // row v; `half` picks the columns (keys of S^T, tokens of V'^T) it handles
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int v = quarter * 32 + lane;
+    const uint32_t tl = tb + (static_cast<uint32_t>(quarter * 32) << 16);
+    const int t = threadIdx.x - 64;                     // 0..255
+    constexpr int NB = DK / 64;                         // 32-column blocks of S^T per half
+    const int b0 = half * NB;
+    bool ok = true;
+    // U_n: plain [64][128] bf16 via cp.async by the eight warps
+    auto load_u = [&](int n) {
+      const __nv_bfloat16* src = U + (bh * N + n) * (long long)C * DV + v0;
+      for (int i = t; i < C * (VT / 8); i += 256) {
+        const int r = i / (VT / 8), c8 = (i % (VT / 8)) * 8;
+        cp_async16(su + r * VT + c8, src + (long long)r * DV + c8);
+      }
+      cp_commit();
+    };
+    // 32 fp32 of row v (S^T columns 32 j ..) -> bf16 into the 128-byte swizzled K-major A operand
+    auto put_bf16 = [&](int j, const uint32_t (&r)[32]) {
+      uint8_t* base = sst + (j >> 1) * 16384 + v * 128;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(base + ((((j & 1) * 4 + u) ^ (v & 7)) * 16)) =
+            make_uint4(pack_bf16x2(__uint_as_float(r[8 * u]), __uint_as_float(r[8 * u + 1])),
+                       pack_bf16x2(__uint_as_float(r[8 * u + 2]), __uint_as_float(r[8 * u + 3])),
+                       pack_bf16x2(__uint_as_float(r[8 * u + 4]), __uint_as_float(r[8 * u + 5])),
+                       pack_bf16x2(__uint_as_float(r[8 * u + 6]), __uint_as_float(r[8 * u + 7])));
+    };
+    // this thread's part of S^T (fp32) -> bf16 A operand of the next D1
+    auto copy_state = [&]() {
+      if constexpr (NB == 1) {
+        uint32_t r0[32];
+        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * b0), r0);
+        tmem_ld_wait();
+        put_bf16(b0, r0);
+      } else {
+#pragma unroll 1
+        for (int j = b0; j < b0 + NB; j += 2) {
+          uint32_t r0[32], r1[32];
+          tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j), r0);
+          tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j + 32), r1);
+          tmem_ld_wait();
+          put_bf16(j, r0);
+          put_bf16(j + 1, r1);
+        }
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(s_ready);
+    };
+    // S^T *= g in TMEM (overlaps the next D1, which reads only the bf16 copy)
+    auto scale_state = [&](float g) {
+#pragma unroll 1
+      for (int j = b0; j < b0 + NB; ++j) {
+        uint32_t r0[32];
+        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j), r0);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r0[e] = __float_as_uint(__uint_as_float(r0[e]) * g);
+        tmem_st_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j), r0);
+      }
+      tmem_st_wait();
+    };
+    // initial state into TMEM
+#pragma unroll 1
+    for (int j = b0; j < b0 + NB; ++j) {
+      uint32_t r[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        r[e] = __float_as_uint(S0 ? S0[(bh * DK + 32 * j + e) * DV + v0 + v] : 0.f);
+      tmem_st_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j), r);
+    }
+    tmem_st_wait();
+    load_u(0);
+    copy_state();
+    if (N > 0) scale_state(gC[bh * N]);
+    for (int n = 0; n < N; ++n) {
+      const long long cidx = bh * N + n;
+      const float g_next = n + 1 < N ? gC[cidx + 1] : 1.f;
+      cp_wait_all();
+      asm volatile("bar.sync 1, 256;" ::: "memory");     // U_n complete for all eight warps
+      uint32_t uu[16];                                   // U_n[32 half + c][v] as bf16 pairs
+#pragma unroll
+      for (int c = 0; c < 32; c += 2)
+        uu[c / 2] = static_cast<uint32_t>(__bfloat16_as_ushort(su[(32 * half + c) * VT + v])) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(su[(32 * half + c + 1) * VT + v])) << 16);
+      asm volatile("bar.sync 1, 256;" ::: "memory");     // every warp has read U_n
+      if (n + 1 < N) load_u(n + 1);
+      // V'^T row v, tokens 32 half .. 32 half + 31 = U^T - D1
+      ok = ok && mbar_wait_spin(d1_full, n & 1, abort_flag, err, kErrTimeoutEpilogue);
+      tc_fence_after();
+      uint32_t d[32];
+      tmem_ld_32x32b_x32(tl + Lt::C_D1 + static_cast<uint32_t>(32 * half), d);
+      tmem_ld_wait();
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        uint32_t w[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int c = 8 * u + 2 * j;
+          const float2 uf = unpack_bf16x2(uu[c / 2]);
+          w[j] = pack_bf16x2(uf.x - __uint_as_float(d[c]), uf.y - __uint_as_float(d[c + 1]));
+        }
+        *reinterpret_cast<uint4*>(svt + v * 128 + (((4 * half + u) ^ (v & 7)) * 16)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(v_full);
+      // S_{n+1}: bf16 copy for the next D1, then scaled by gC_{n+1} in TMEM
+      ok = ok && mbar_wait_spin(s2_done, n & 1, abort_flag, err, kErrTimeoutEpilogue);
+      tc_fence_after();
+      if (n + 1 < N) {
+        copy_state();
+        scale_state(g_next);
+      }
+    }
+    if (S_out) {
+#pragma unroll 1
+      for (int j = b0; j < b0 + NB; ++j) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) S_out[(bh * DK + 32 * j + e) * DV + v0 + v] = __uint_as_float(r[e]);
+      }
+    }
+    cp_wait_all();
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tb, Lt::COLS);
+  }
+}
+
 // ------------------------------------------------------------ forward output --
 // O[:, tile] = Qh S_n[:, tile] + A V'[:, tile]; grid (BH * N, DV / 64)
 
 template <int DK>
 struct OutSmem {
   __nv_bfloat16 Q[C][DK + PAD];
-  __nv_bfloat16 S[DK][DVT + PAD];
+  __nv_bfloat16 ST[DVT][DK + PAD];     // S_n^T (states are stored value-major)
   __nv_bfloat16 A[C][C + PAD];
-  __nv_bfloat16 V[C][DVT + PAD];
+  __nv_bfloat16 VT[DVT][C + PAD];      // V'^T
+  __nv_bfloat16 O[C][DVT + PAD];
 };
 
 template <int DK>
@@ -193,26 +485,25 @@ gdr_fwd_out(const __nv_bfloat16* __restrict__ Qh, const __nv_bfloat16* __restric
   const int warp = threadIdx.x / 32;
   const int wm0 = (warp & 3) * 16, wn0 = (warp >> 2) * 32;
   load_tile(&sm.Q[0][0], DK + PAD, Qh + cidx * C * DK, DK, C, DK);
-  load_tile(&sm.S[0][0], DVT + PAD, states + cidx * DK * DV + v0, DV, DK, DVT);
+  load_tile(&sm.ST[0][0], DK + PAD, states + (cidx * DV + v0) * DK, DK, DVT, DK);
   load_tile(&sm.A[0][0], C + PAD, A + cidx * C * C, C, C, C);
-  load_tile(&sm.V[0][0], DVT + PAD, Vp + cidx * C * DV + v0, DV, C, DVT);
+  load_tile(&sm.VT[0][0], C + PAD, Vp + (cidx * DV + v0) * C, C, DVT, C);
   cp_commit();
   cp_wait_all();
   __syncthreads();
   float acc[1][4][4];
   zero(acc);
-  warp_mma<1, 4, false, true>(acc, &sm.Q[0][0], DK + PAD, &sm.S[0][0], DVT + PAD, wm0, wn0, DK);
-  warp_mma<1, 4, false, true>(acc, &sm.A[0][0], C + PAD, &sm.V[0][0], DVT + PAD, wm0, wn0, C);
-  __syncthreads();                          // V tile reused for the bf16 output
+  warp_mma<1, 4, false, false>(acc, &sm.Q[0][0], DK + PAD, &sm.ST[0][0], DK + PAD, wm0, wn0, DK);
+  warp_mma<1, 4, false, false>(acc, &sm.A[0][0], C + PAD, &sm.VT[0][0], C + PAD, wm0, wn0, C);
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       const int r = wm0 + frag_row(0, e), c = wn0 + frag_col(nt, e);
-      *reinterpret_cast<uint32_t*>(&sm.V[r][c]) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
+      *reinterpret_cast<uint32_t*>(&sm.O[r][c]) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
     }
   __syncthreads();
-  store_tile(O + tok_row0(cidx / N, static_cast<int>(cidx % N), N, H, DV) + v0, (long long)H * DV, &sm.V[0][0],
+  store_tile(O + tok_row0(cidx / N, static_cast<int>(cidx % N), N, H, DV) + v0, (long long)H * DV, &sm.O[0][0],
              DVT + PAD, C, DVT);
 }
 
@@ -349,8 +640,8 @@ gdr_bwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
 struct ParSmem {
   __nv_bfloat16 dV[2][C][DVT + PAD];     // dU = dV'
   __nv_bfloat16 dO[2][C][DVT + PAD];
-  __nv_bfloat16 V[2][C][DVT + PAD];      // V'
-  __nv_bfloat16 S[2][64][DVT + PAD];     // S_n rows k0..k0+63
+  __nv_bfloat16 VT[2][DVT][C + PAD];     // V'^T
+  __nv_bfloat16 ST[2][DVT][64 + PAD];    // S_n^T columns k0..k0+63
   __nv_bfloat16 dS[2][64][DVT + PAD];
   float red[THREADS / 32];
 };
@@ -373,8 +664,8 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
     load_tile(&sm.dV[b][0][0], DVT + PAD, dU + cidx * C * DV + v0, DV, C, DVT);
     load_tile(&sm.dO[b][0][0], DVT + PAD, dO + tok_row0(cidx / N, static_cast<int>(cidx % N), N, H, DV) + v0,
               (long long)H * DV, C, DVT);
-    load_tile(&sm.V[b][0][0], DVT + PAD, Vp + cidx * C * DV + v0, DV, C, DVT);
-    load_tile(&sm.S[b][0][0], DVT + PAD, states + (cidx * DK + k0) * DV + v0, DV, 64, DVT);
+    load_tile(&sm.VT[b][0][0], C + PAD, Vp + (cidx * DV + v0) * C, C, DVT, C);
+    load_tile(&sm.ST[b][0][0], 64 + PAD, states + (cidx * DV + v0) * DK + k0, DK, DVT, 64);
     load_tile(&sm.dS[b][0][0], DVT + PAD, dstates + (cidx * DK + k0) * DV + v0, DV, 64, DVT);
   };
   float aw[1][4][4], aq[1][4][4], ak[1][4][4], aa[1][4][4];
@@ -390,15 +681,13 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
     cp_wait_1();
     __syncthreads();
     // dW = -dV' S^T, dQh = dO S^T, dKt = V' dS^T   (64 x 64 blocks, K = value)
-    warp_mma<1, 4, false, false>(aw, &sm.dV[b][0][0], DVT + PAD, &sm.S[b][0][0], DVT + PAD, wm0, wn0, DVT);
-    warp_mma<1, 4, false, false>(aq, &sm.dO[b][0][0], DVT + PAD, &sm.S[b][0][0], DVT + PAD, wm0, wn0, DVT);
-    warp_mma<1, 4, false, false>(ak, &sm.V[b][0][0], DVT + PAD, &sm.dS[b][0][0], DVT + PAD, wm0, wn0, DVT);
-    if (do_dA) warp_mma<1, 4, false, false>(aa, &sm.dO[b][0][0], DVT + PAD, &sm.V[b][0][0], DVT + PAD, wm0, wn0, DVT);
-    for (int i = threadIdx.x; i < 64 * (DVT / 2); i += THREADS) {
-      const int r = i / (DVT / 2), c = (i % (DVT / 2)) * 2;
-      const float2 sv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.S[b][r][c]));
-      const float2 dv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.dS[b][r][c]));
-      dot += sv.x * dv.x + sv.y * dv.y;
+    warp_mma<1, 4, false, true>(aw, &sm.dV[b][0][0], DVT + PAD, &sm.ST[b][0][0], 64 + PAD, wm0, wn0, DVT);
+    warp_mma<1, 4, false, true>(aq, &sm.dO[b][0][0], DVT + PAD, &sm.ST[b][0][0], 64 + PAD, wm0, wn0, DVT);
+    warp_mma<1, 4, true, false>(ak, &sm.VT[b][0][0], C + PAD, &sm.dS[b][0][0], DVT + PAD, wm0, wn0, DVT);
+    if (do_dA) warp_mma<1, 4, false, true>(aa, &sm.dO[b][0][0], DVT + PAD, &sm.VT[b][0][0], C + PAD, wm0, wn0, DVT);
+    for (int i = threadIdx.x; i < 64 * DVT; i += THREADS) {
+      const int r = i / DVT, c = i % DVT;           // key r, value c
+      dot += bf2f(sm.ST[b][c][r]) * bf2f(sm.dS[b][r][c]);
     }
     __syncthreads();
   }
@@ -467,10 +756,33 @@ template <int DK>
 int launch_fwd(const GdrRecArgs& a, cudaStream_t st) {
   const size_t s1 = sizeof(FwdScanSmem<DK>), s2 = sizeof(OutSmem<DK>);
   if (!set_smem(gdr_fwd_scan<DK>, s1) || !set_smem(gdr_fwd_out<DK>, s2)) return 3;
-  const int grid = static_cast<int>(a.BH * (a.DV / DVT));
-  gdr_fwd_scan<DK><<<grid, THREADS, s1, st>>>((const __nv_bfloat16*)a.W, (const __nv_bfloat16*)a.Kt,
-                                              (const __nv_bfloat16*)a.U, a.gC, a.S0, (__nv_bfloat16*)a.Vp,
-                                              (__nv_bfloat16*)a.states, a.S_out, a.N, a.DV);
+  static const bool no_tc = std::getenv("VAGUS_GDR_NO_TC") != nullptr;
+  if (!no_tc && a.err && a.DV % tscan::VT == 0) {
+    using Lt = tscan::Layout<DK>;
+    alignas(64) unsigned char mw[128], mk[128], ms[128], mv[128];
+    const unsigned long long dims[2] = {(unsigned long long)DK, (unsigned long long)a.BH * a.N * C};
+    const unsigned long long strides[1] = {(unsigned long long)DK * 2};
+    const unsigned box[2] = {64u, 64u};
+    // value-major outputs: states [BH][N][DV][DK], V' [BH][N][DV][C]; 128-row boxes
+    const unsigned long long dims_s[2] = {(unsigned long long)DK, (unsigned long long)a.BH * a.N * a.DV};
+    const unsigned long long dims_v[2] = {(unsigned long long)C, (unsigned long long)a.BH * a.N * a.DV};
+    const unsigned long long strides_v[1] = {(unsigned long long)C * 2};
+    const unsigned box_o[2] = {64u, static_cast<unsigned>(tscan::VT)};
+    if (!encode_bf16_map(mw, a.W, 2, dims, strides, box) || !encode_bf16_map(mk, a.Kt, 2, dims, strides, box) ||
+        !encode_bf16_map(ms, a.states, 2, dims_s, strides, box_o) ||
+        !encode_bf16_map(mv, a.Vp, 2, dims_v, strides_v, box_o))
+      return 2;
+    if (!set_smem(gdr_fwd_scan_tc<DK>, Lt::SMEM)) return 3;
+    gdr_fwd_scan_tc<DK><<<static_cast<unsigned>(a.BH * (a.DV / tscan::VT)), 320, Lt::SMEM, st>>>(
+        *reinterpret_cast<const CUtensorMap*>(mw), *reinterpret_cast<const CUtensorMap*>(mk),
+        *reinterpret_cast<const CUtensorMap*>(ms), *reinterpret_cast<const CUtensorMap*>(mv),
+        (const __nv_bfloat16*)a.U, a.gC, a.S0, a.S_out, a.N, a.DV, a.err);
+  } else {
+    const int grid = static_cast<int>(a.BH * (a.DV / DVT));
+    gdr_fwd_scan<DK><<<grid, THREADS, s1, st>>>((const __nv_bfloat16*)a.W, (const __nv_bfloat16*)a.Kt,
+                                                (const __nv_bfloat16*)a.U, a.gC, a.S0, (__nv_bfloat16*)a.Vp,
+                                                (__nv_bfloat16*)a.states, a.S_out, a.N, a.DV);
+  }
   dim3 g2(static_cast<unsigned>(a.BH * a.N), a.DV / DVT);
   gdr_fwd_out<DK><<<g2, THREADS, s2, st>>>((const __nv_bfloat16*)a.Qh, (const __nv_bfloat16*)a.A,
                                            (const __nv_bfloat16*)a.Vp, (const __nv_bfloat16*)a.states,

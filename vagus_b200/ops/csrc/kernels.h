@@ -67,6 +67,7 @@ struct GdrRecArgs {
   float* S_out;                                    // (BH, DK, DV) or null
   long long BH; int N, DK, DV;
   int H;                                           // heads (BH = B * H)
+  int* err = nullptr;                              // device error word (the tcgen05 scan's bounded waits)
 };
 int gdr_rec_fwd(const GdrRecArgs& a, cudaStream_t st);
 struct GdrRecBwdArgs {
