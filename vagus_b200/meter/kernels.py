@@ -11,7 +11,7 @@ shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
 gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
-sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
+sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
 case runs.
 
 Used for the committed ncu summaries: run one case with few iterations under
@@ -121,6 +121,10 @@ def _cases(B: int, L: int):
         doa = torch.randn_like(oa)
         cases[f"attn_bwd_d{hd_a}"] = (lambda qa=qa, ka=ka, va=va, oa=oa, lsea=lsea, doa=doa, sc=sc:
                                       C.attn_bwd(qa, ka, va, oa, lsea, doa, True, sc), None, 2.5 * fl_a)
+        qg, kg, vg = (t.detach().clone().requires_grad_(True) for t in (qa, ka, va))
+        og = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
+        cases[f"sdpa_bwd_d{hd_a}"] = (lambda og=og, doa=doa, ins=(qg, kg, vg):
+                                      torch.autograd.grad(og, ins, doa, retain_graph=True), None, 2.5 * fl_a)
 
     xs = r(T, D)
     gamma = torch.ones(D, device=dev)

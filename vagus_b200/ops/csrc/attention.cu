@@ -711,35 +711,48 @@ __global__ void attn_bwd_post(const float* __restrict__ acc, __nv_bfloat16* __re
 
 // ----------------------------------------------------- tcgen05 backward --
 // One CTA per (128 keys, batch * kv head), walking every (query head of the
-// group, 128-query block) step; 10 warps:
-//   warp 0      TMA: K and V once, then Q and dO of each step (single buffer,
-//               refilled when the step's last products are done);
+// group, query block) step; 10 warps:
+//   warp 0      TMA: K and V once, then Q and dO of each step into a
+//               two-stage ring (the next block loads during this one);
 //   warp 1      TMEM owner and MMA issuer, per step
-//                 S^T = K Q^T and dP^T = V dO^T          (M = 128 keys, N = 128 queries)
-//                 dV += P^T dO, dK += dS^T Q               (M = 128 keys, N = D)
-//                 dQ  = dS K                               (M = 128 queries, N = D)
-//               with dQ written into the score columns once they are read;
-//   warps 2-9   two threads per key row (one per half of the query columns):
-//               P^T = exp(S^T scale - lse), dS^T = P^T (dP^T - delta) into
-//               shared memory as bf16 (the K-major / MN-major operand of the
-//               next products), then two threads per query row add the dQ
-//               rows to the fp32 dq accumulator with 16-byte atomics; at the
-//               end the same warps write dK (scaled) and dV.
+//                 S^T = K Q^T and dP^T = V dO^T     (M = 128 keys, N = the block's queries)
+//                 dV += P^T dO, dK += dS^T Q          (M = 128 keys, N = D)
+//                 dQ into its own TMEM columns:
+//                   D = 64:  dQ   = dS K     (M = 128 queries, N = 64)
+//                   D = 128: dQ^T = K^T dS^T (M = 128 dims,    N = 64 queries)
+//               so the next block's S^T / dP^T products run while dQ is
+//               read out;
+//   warps 2-9   two threads per key row (one per half of the block's query
+//               columns): P^T = exp(S^T scale - lse), dS^T = P^T (dP^T - delta)
+//               into shared memory as bf16 (the K-major / MN-major operand of
+//               the next products), then stage the dQ rows or columns in
+//               shared memory for one bulk tensor reduction (TMA add) into
+//               the fp32 dq accumulator -- per-thread global atomics here
+//               slowed the tensor core's operand reads several-fold; lse /
+//               delta of the next block are fetched while dQ is awaited.  At
+//               the end the same warps write dK (scaled) and dV.
+// Query blocks are 128 rows for D = 64 and 64 rows for D = 128 (so the Q / dO
+// ring fits next to K, V, P^T and dS^T in shared memory, and dQ^T has M = 128).
 // delta = rowsum(dO o O) comes from the pre-pass and dq is scaled / rounded
 // by the post-pass of the mma.sync backward above.  Every wait is bounded.
 namespace tcbw {
-constexpr int KROWS = 128, QROWS = 128, THREADS = 320;
+constexpr int KROWS = 128, THREADS = 320;
 template <int D>
 struct Layout {
-  static constexpr int T_BYTES = 128 * D * 2;     // K, V, Q, dO tiles: D/64 K-major chunks of 16 KB
-  static constexpr int P_BYTES = 128 * 128 * 2;   // P^T, dS^T: 2 chunks of 64 query columns
-  static constexpr int OFF_V = T_BYTES, OFF_Q = 2 * T_BYTES, OFF_DO = 3 * T_BYTES;
-  static constexpr int OFF_P = 4 * T_BYTES, OFF_DS = OFF_P + P_BYTES;
-  static constexpr int OFF_STAT = OFF_DS + P_BYTES;            // lse[128], delta[128]
-  static constexpr int OFF_BAR = OFF_STAT + 1024;
-  static constexpr int RAW = OFF_BAR + 128 + 1024;
-  static constexpr int SMEM = RAW > 120 * 1024 ? RAW : 120 * 1024;
-  static constexpr uint32_t C_S = 0, C_DP = 128, C_DV = 256, C_DK = 256 + D, COLS = 512;
+  static constexpr int QROWS = D == 64 ? 128 : 64;
+  static constexpr int KV_BYTES = KROWS * D * 2;      // K, V: D/64 K-major chunks of [128 keys x 128 B]
+  static constexpr int Q_BYTES = QROWS * D * 2;       // Q, dO: D/64 chunks of [QROWS x 128 B]
+  static constexpr int QCHUNK = QROWS * 128;          // bytes of one 64-wide chunk of a Q / dO tile
+  static constexpr int P_BYTES = KROWS * QROWS * 2;   // P^T, dS^T: QROWS/64 chunks of [128 keys x 128 B]
+  static constexpr int OFF_V = KV_BYTES, OFF_Q = 2 * KV_BYTES, OFF_DO = OFF_Q + 2 * Q_BYTES;
+  static constexpr int OFF_P = OFF_DO + 2 * Q_BYTES, OFF_DS = OFF_P + P_BYTES;
+  static constexpr int OFF_DQ = OFF_DS + P_BYTES;     // fp32 dQ staging for the bulk reduction (32 KB)
+  static constexpr int OFF_STAT = OFF_DQ + 32768;     // lse[2][QROWS], delta[2][QROWS]
+  static constexpr int OFF_BAR = OFF_STAT + 4 * QROWS * 4;
+  static constexpr int SMEM = OFF_BAR + 128 + 1024;
+  static constexpr uint32_t C_S = 0, C_DP = QROWS, C_DV = 2 * QROWS, C_DK = 2 * QROWS + D, C_DQ = 384,
+                            COLS = 512;
+  static_assert(C_DK + D <= C_DQ, "TMEM columns");
 };
 struct Params {
   int Lq, Lk, H, Hk, causal;
@@ -750,25 +763,32 @@ struct Params {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   int* err;
+  unsigned long long* trace;   // phase clock of CTA (0, 0), [step][16]; null: off
 };
 }  // namespace tcbw
+
+// host side of the phase trace (attn_set_trace)
+unsigned long long* g_attn_trace = nullptr;
 
 template <int D>
 __global__ void __launch_bounds__(tcbw::THREADS, 1)
 attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
-            const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo, const tcbw::Params p) {
+            const __grid_constant__ CUtensorMap mv, const __grid_constant__ CUtensorMap mdo,
+            const __grid_constant__ CUtensorMap mdq, const tcbw::Params p) {
   using namespace tcbw;
   using Lt = Layout<D>;
+  constexpr int QROWS = Lt::QROWS;
+  constexpr int HALF = QROWS / 2;                      // query columns per softmax thread
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sk = sm, *sv = sm + Lt::OFF_V, *sq = sm + Lt::OFF_Q, *sdo = sm + Lt::OFF_DO;
-  uint8_t *spt = sm + Lt::OFF_P, *sdst = sm + Lt::OFF_DS;
-  float* s_lse = reinterpret_cast<float*>(sm + Lt::OFF_STAT);
-  float* s_delta = s_lse + 128;
+  uint8_t *spt = sm + Lt::OFF_P, *sdst = sm + Lt::OFF_DS, *sdq = sm + Lt::OFF_DQ;
+  float* s_lse = reinterpret_cast<float*>(sm + Lt::OFF_STAT);   // [2][QROWS]
+  float* s_delta = s_lse + 2 * QROWS;                            // [2][QROWS]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
-  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 2, *s_full = bars + 3, *p_full = bars + 4,
-           *mma2 = bars + 5, *dq_free = bars + 6;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 7);
+  uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 6,
+           *dq_full = bars + 7, *dq_free = bars + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -781,14 +801,21 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   const int qb0 = q_first / QROWS, nqb = (p.Lq + QROWS - 1) / QROWS;
   const int per_head = max(0, nqb - qb0);
   const int nsteps = group * per_head;
+  const bool tracing = p.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0;
+#define VAGUS_TR(step, ev)                                                      \
+  do {                                                                          \
+    if (tracing && (step) < 32) p.trace[(step) * 16 + (ev)] = clock64();        \
+  } while (0)
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
-    mbar_init(q_full, 1);
-    mbar_init(q_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_empty[i], 1);
+    }
     mbar_init(s_full, 1);
     mbar_init(p_full, 8);
-    mbar_init(mma2, 1);
+    mbar_init(dq_full, 1);
     mbar_init(dq_free, 8);
     *abort_flag = 0;
     fence_mbar_init();
@@ -796,6 +823,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     tma_prefetch_desc(&mk);
     tma_prefetch_desc(&mv);
     tma_prefetch_desc(&mdo);
+    tma_prefetch_desc(&mdq);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, Lt::COLS);
@@ -808,143 +836,224 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
 
   if (warp == 0) {
     if (lane == 0 && nsteps > 0) {
-      mbar_arrive_expect_tx(kv_full, 2 * Lt::T_BYTES);
+      mbar_arrive_expect_tx(kv_full, 2 * Lt::KV_BYTES);
       for (int c = 0; c < D / 64; ++c) {
         tma_load_4d(sk + c * 16384, &mk, kv_full, 64 * c, k0, hk, b);
         tma_load_4d(sv + c * 16384, &mv, kv_full, 64 * c, k0, hk, b);
       }
       for (int st = 0; st < nsteps; ++st) {
         const int h = hk * group + st / per_head, q0 = (qb0 + st % per_head) * QROWS;
-        if (!mbar_wait(q_empty, (st & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
-        mbar_arrive_expect_tx(q_full, 2 * Lt::T_BYTES);
+        const int s = st & 1;
+        if (!mbar_wait(&q_empty[s], ((st >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&q_full[s], 2 * Lt::Q_BYTES);
         for (int c = 0; c < D / 64; ++c) {
-          tma_load_4d(sq + c * 16384, &mq, q_full, 64 * c, q0, h, b);
-          tma_load_4d(sdo + c * 16384, &mdo, q_full, 64 * c, q0, h, b);
+          tma_load_4d(sq + s * Lt::Q_BYTES + c * Lt::QCHUNK, &mq, &q_full[s], 64 * c, q0, h, b);
+          tma_load_4d(sdo + s * Lt::Q_BYTES + c * Lt::QCHUNK, &mdo, &q_full[s], 64 * c, q0, h, b);
         }
       }
+      // the ring's last releases land before the CTA retires
+      for (int st = nsteps; st < nsteps + 2; ++st)
+        if (!mbar_wait(&q_empty[st & 1], ((st >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) break;
     }
   } else if (warp == 1) {
     if (lane == 0 && nsteps > 0) {
       constexpr uint32_t id_s = make_idesc_bf16(KROWS, QROWS, false, false);
       constexpr uint32_t id_kv = make_idesc_bf16(KROWS, D, false, true);
-      constexpr uint32_t id_q = make_idesc_bf16(QROWS, D, true, true);
-      const uint32_t ak = smem_u32(sk), av = smem_u32(sv), aq = smem_u32(sq), ado = smem_u32(sdo);
-      const uint32_t ap = smem_u32(spt), ads = smem_u32(sdst);
+      // D = 64: dQ = dS K (A = dS^T tile read MN-major, B = K MN-major);
+      // D = 128: dQ^T = K^T dS^T (A = K tile MN-major, B = dS^T tile MN-major)
+      constexpr uint32_t id_q = make_idesc_bf16(128, 64, true, true);
+      // base descriptors; every product below offsets them by a compile-time byte count
+      const uint64_t dk_k = make_sw128_desc(smem_u32(sk), 16, 1024), dv_k = make_sw128_desc(smem_u32(sv), 16, 1024);
+      const uint64_t dp_k = make_sw128_desc(smem_u32(spt), 16, 1024), ds_k = make_sw128_desc(smem_u32(sdst), 16, 1024);
+      const uint64_t ds_mn = make_sw128_desc(smem_u32(sdst), 16384, 1024);
+      const uint64_t dk_mn = make_sw128_desc(smem_u32(sk), 16384, 1024);
       bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
       for (int st = 0; ok && st < nsteps; ++st) {
-        if (!mbar_wait(q_full, st & 1, abort_flag, p.err, kErrTimeoutMma)) break;
-        if (st > 0 && !mbar_wait(dq_free, (st - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        const int s = st & 1;
+        const uint64_t dq_k = make_sw128_desc(smem_u32(sq + s * Lt::Q_BYTES), 16, 1024);
+        const uint64_t ddo_k = make_sw128_desc(smem_u32(sdo + s * Lt::Q_BYTES), 16, 1024);
+        const uint64_t dq_mn = make_sw128_desc(smem_u32(sq + s * Lt::Q_BYTES), Lt::QCHUNK, 1024);
+        const uint64_t ddo_mn = make_sw128_desc(smem_u32(sdo + s * Lt::Q_BYTES), Lt::QCHUNK, 1024);
+        if (!mbar_wait(&q_full[s], (st >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
+        // S^T, dP^T: K = D (D/64 chunks x 4 steps of 16)
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t acc = (c | kk) ? 1u : 0u;
-            tc_mma_f16(tb + Lt::C_S, make_sw128_desc(ak + c * 16384 + kk * 32, 16, 1024),
-                       make_sw128_desc(aq + c * 16384 + kk * 32, 16, 1024), id_s, acc);
-            tc_mma_f16(tb + Lt::C_DP, make_sw128_desc(av + c * 16384 + kk * 32, 16, 1024),
-                       make_sw128_desc(ado + c * 16384 + kk * 32, 16, 1024), id_s, acc);
-          }
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(tb + Lt::C_S, desc_add(dk_k, c * 16384 + kk * 32), desc_add(dq_k, c * Lt::QCHUNK + kk * 32), id_s,
+                       (c | kk) ? 1u : 0u);
+#pragma unroll
+        for (int c = 0; c < D / 64; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(tb + Lt::C_DP, desc_add(dv_k, c * 16384 + kk * 32), desc_add(ddo_k, c * Lt::QCHUNK + kk * 32),
+                       id_s, (c | kk) ? 1u : 0u);
         tc_commit(s_full);
         if (!mbar_wait(p_full, st & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
-        // dV += P^T dO, dK += dS^T Q: K = the 128 queries (2 chunks x 4 steps of 16)
+        // dV += P^T dO, dK += dS^T Q: K = the block's queries (16 per step)
 #pragma unroll
-        for (int kc = 0; kc < 2; ++kc)
+        for (int j = 0; j < QROWS / 16; ++j) {
+          const uint32_t acc = (st > 0 || j > 0) ? 1u : 0u;
+          const uint32_t a_off = static_cast<uint32_t>((j >> 2) * 16384 + (j & 3) * 32);
+          tc_mma_f16(tb + Lt::C_DV, desc_add(dp_k, a_off), desc_add(ddo_mn, j * 2048), id_kv, acc);
+          tc_mma_f16(tb + Lt::C_DK, desc_add(ds_k, a_off), desc_add(dq_mn, j * 2048), id_kv, acc);
+        }
+        if (st > 0 && !mbar_wait(dq_free, (st - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        // dQ: K = the 128 keys (8 steps of 16 rows)
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint32_t acc = (st > 0 || kc > 0 || kk > 0) ? 1u : 0u;
-            const uint32_t row = static_cast<uint32_t>((kc * 4 + kk) * 2048);
-            tc_mma_f16(tb + Lt::C_DV, make_sw128_desc(ap + kc * 16384 + kk * 32, 16, 1024),
-                       make_sw128_desc(ado + row, 16384, 1024), id_kv, acc);
-            tc_mma_f16(tb + Lt::C_DK, make_sw128_desc(ads + kc * 16384 + kk * 32, 16, 1024),
-                       make_sw128_desc(aq + row, 16384, 1024), id_kv, acc);
-          }
-        // dQ = dS K into the score columns: K = the 128 keys (8 steps of 16 rows)
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          tc_mma_f16(tb + Lt::C_S, make_sw128_desc(ads + kk * 2048, 16384, 1024),
-                     make_sw128_desc(ak + kk * 2048, 16384, 1024), id_q, kk ? 1u : 0u);
-        tc_commit(mma2);
-        tc_commit(q_empty);
+        for (int kk = 0; kk < 8; ++kk) {
+          if constexpr (D == 64)
+            tc_mma_f16(tb + Lt::C_DQ, desc_add(ds_mn, kk * 2048), desc_add(dk_mn, kk * 2048), id_q, kk ? 1u : 0u);
+          else
+            tc_mma_f16(tb + Lt::C_DQ, desc_add(dk_mn, kk * 2048), desc_add(ds_mn, kk * 2048), id_q, kk ? 1u : 0u);
+        }
+        tc_commit(dq_full);
+        tc_commit(&q_empty[s]);
+        VAGUS_TR(st, 5);
       }
     }
   } else {
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
-    const int row = quarter * 32 + lane;                 // key row (S^T, dK, dV) / query row (dQ)
+    const int row = quarter * 32 + lane;                 // key row (S^T, dK, dV); query row / dim for dQ
     const uint32_t tl = tb + (static_cast<uint32_t>(quarter * 32) << 16);
     const int t = threadIdx.x - 64;                      // 0..255 over the softmax warps
     const int kj = k0 + row;
     bool ok = true;
+    // lse (log2 units) / delta of step st's query block, fetched by threads t < 2 QROWS
+    auto fetch_stat = [&](int st) -> float {
+      if (st >= nsteps || t >= 2 * QROWS) return 0.f;
+      const int h = hk * group + st / per_head, q0 = (qb0 + st % per_head) * QROWS;
+      const long long rowbase = ((long long)b * p.H + h) * p.Lq;
+      const int qi = q0 + (t < QROWS ? t : t - QROWS);
+      if (t < QROWS) return qi < p.Lq ? p.lse[rowbase + qi] * kLog2e : INFINITY;
+      return qi < p.Lq ? p.delta[rowbase + qi] : 0.f;
+    };
+    auto put_stat = [&](int st, float v) {
+      if (t < QROWS) s_lse[(st & 1) * QROWS + t] = v;
+      else if (t < 2 * QROWS) s_delta[(st & 1) * QROWS + t - QROWS] = v;
+    };
+    put_stat(0, fetch_stat(0));
+    // kernel parameters in registers: the lambdas above take `p` by reference,
+    // and reads through that reference inside the hot loop are memory loads
+    const float sl2 = p.sl2;
+    const int Lk = p.Lk, Lq = p.Lq;
+    const bool causal = p.causal != 0;
     for (int st = 0; st < nsteps; ++st) {
       const int h = hk * group + st / per_head, q0 = (qb0 + st % per_head) * QROWS;
       const long long rowbase = ((long long)b * p.H + h) * p.Lq;
-      asm volatile("bar.sync 1, 256;" ::: "memory");     // the previous step's statistics are consumed
-      if (t < 128) {
-        const int qi = q0 + t;
-        s_lse[t] = qi < p.Lq ? p.lse[rowbase + qi] * kLog2e : INFINITY;
-      } else {
-        const int qi = q0 + t - 128;
-        s_delta[t - 128] = qi < p.Lq ? p.delta[rowbase + qi] : 0.f;
-      }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
+      const float* lse_s = s_lse + (st & 1) * QROWS + HALF * half;
+      const float* del_s = s_delta + (st & 1) * QROWS + HALF * half;
+      asm volatile("bar.sync 1, 256;" ::: "memory");     // this step's statistics are in place
       ok = ok && mbar_wait_spin(s_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      if (t == 0) VAGUS_TR(st, 6);
       tc_fence_after();
-      float sv[64], dp[64];
-      const uint32_t cs = tl + Lt::C_S + static_cast<uint32_t>(64 * half);
-      const uint32_t cd = tl + Lt::C_DP + static_cast<uint32_t>(64 * half);
-      tmem_ld_32x32b_x32(cs, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld_32x32b_x32(cs + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-      tmem_ld_32x32b_x32(cd, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
-      tmem_ld_32x32b_x32(cd + 32, *reinterpret_cast<uint32_t(*)[32]>(&dp[32]));
-      tmem_ld_wait();
-      const int qbase = q0 + 64 * half;
+      const uint32_t cs = tl + Lt::C_S + static_cast<uint32_t>(HALF * half);
+      const uint32_t cd = tl + Lt::C_DP + static_cast<uint32_t>(HALF * half);
+      const int qbase = q0 + HALF * half;
       const bool full = (k0 + KROWS <= p.Lk) && (q0 + QROWS <= p.Lq) && (!p.causal || k0 + KROWS - 1 <= q0 + offs);
+      // 32 query columns at a time: scores and dP from TMEM, P^T and dS^T as bf16 into the
+      // 128-byte swizzled tiles (16-byte unit u of the 32 columns)
 #pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const bool vis = full || (kj < p.Lk && qbase + i < p.Lq && (!p.causal || kj <= qbase + i + offs));
-        const float pr = vis ? ex2_approx(fmaf(sv[i], p.sl2, -s_lse[64 * half + i])) : 0.f;
-        sv[i] = pr;
-        dp[i] = pr * (dp[i] - s_delta[64 * half + i]);
-      }
+      for (int c = 0; c < HALF / 32; ++c) {
+        float sv[32], dp[32];
+        tmem_ld_32x32b_x32(cs + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        tmem_ld_32x32b_x32(cd + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
+        tmem_ld_wait();
+        if (t == 0 && c == 0) VAGUS_TR(st, 7);
+        float ls[32], dl[32];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const uint32_t off = static_cast<uint32_t>(half * 16384 + row * 128 + ((u ^ (row & 7)) * 16));
-        const float* a8 = &sv[8 * u];
-        const float* d8 = &dp[8 * u];
-        *reinterpret_cast<uint4*>(spt + off) = make_uint4(pack_bf16x2(a8[0], a8[1]), pack_bf16x2(a8[2], a8[3]),
-                                                          pack_bf16x2(a8[4], a8[5]), pack_bf16x2(a8[6], a8[7]));
-        *reinterpret_cast<uint4*>(sdst + off) = make_uint4(pack_bf16x2(d8[0], d8[1]), pack_bf16x2(d8[2], d8[3]),
-                                                           pack_bf16x2(d8[4], d8[5]), pack_bf16x2(d8[6], d8[7]));
+        for (int i = 0; i < 32; i += 4) {
+          const float4 a4 = *reinterpret_cast<const float4*>(lse_s + 32 * c + i);
+          const float4 d4 = *reinterpret_cast<const float4*>(del_s + 32 * c + i);
+          ls[i] = a4.x; ls[i + 1] = a4.y; ls[i + 2] = a4.z; ls[i + 3] = a4.w;
+          dl[i] = d4.x; dl[i + 1] = d4.y; dl[i + 2] = d4.z; dl[i + 3] = d4.w;
+        }
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float pr = ex2_approx(fmaf(sv[i], sl2, -ls[i]));
+            sv[i] = pr;
+            dp[i] = pr * (dp[i] - dl[i]);
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int qi = qbase + 32 * c + i;
+            const bool vis = kj < Lk && qi < Lq && (!causal || kj <= qi + offs);
+            const float pr = vis ? ex2_approx(fmaf(sv[i], sl2, -ls[i])) : 0.f;
+            sv[i] = pr;
+            dp[i] = pr * (dp[i] - dl[i]);
+          }
+        }
+        if (t == 0) VAGUS_TR(st, c == 0 ? 13 : 15);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int col = HALF * half + 32 * c + 8 * u;  // query column inside the block
+          const uint32_t off =
+              static_cast<uint32_t>((col >> 6) * 16384 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) * 16));
+          const float* a8 = &sv[8 * u];
+          const float* d8 = &dp[8 * u];
+          *reinterpret_cast<uint4*>(spt + off) = make_uint4(pack_bf16x2(a8[0], a8[1]), pack_bf16x2(a8[2], a8[3]),
+                                                            pack_bf16x2(a8[4], a8[5]), pack_bf16x2(a8[6], a8[7]));
+          *reinterpret_cast<uint4*>(sdst + off) = make_uint4(pack_bf16x2(d8[0], d8[1]), pack_bf16x2(d8[2], d8[3]),
+                                                             pack_bf16x2(d8[4], d8[5]), pack_bf16x2(d8[6], d8[7]));
+        }
+        if (t == 0 && c == 0) VAGUS_TR(st, 14);
       }
+      if (t == 0) VAGUS_TR(st, 12);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
+      if (t == 0) VAGUS_TR(st, 8);
       if (lane == 0) mbar_arrive(p_full);
-      // dQ rows (this thread: query q0 + row, columns half * D / 2 ..) -> fp32 accumulator
-      ok = ok && mbar_wait_spin(mma2, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      const float nxt = fetch_stat(st + 1);              // in flight while dQ is awaited
+      ok = ok && mbar_wait_spin(dq_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      if (t == 0) VAGUS_TR(st, 9);
       tc_fence_after();
-      const int qi = q0 + row;
-#pragma unroll
-      for (int c = 0; c < D / 64; ++c) {
-        uint32_t r[32];
-        const int col = half * (D / 2) + 32 * c;
-        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(col), r);
-        tmem_ld_wait();
-        if (ok && qi < p.Lq) {
-          float* dst = p.dq_acc + (rowbase + qi) * D + col;
-#pragma unroll
-          for (int e = 0; e < 32; e += 4)
-            atomicAdd(reinterpret_cast<float4*>(dst + e),
-                      make_float4(__uint_as_float(r[e]), __uint_as_float(r[e + 1]), __uint_as_float(r[e + 2]),
-                                  __uint_as_float(r[e + 3])));
-        }
-      }
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tl + Lt::C_DQ + static_cast<uint32_t>(32 * half), r);
+      tmem_ld_wait();
+      if (t == 0) VAGUS_TR(st, 10);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(dq_free);
+      // dQ -> fp32 staging tile -> one bulk reduction into dq_acc (the tensor map
+      // clips rows past Lq)
+      if (t == 0) bulk_wait_read<0>();                  // the previous step's reduction has read the tile
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if constexpr (D == 64) {
+        // dQ row `row` (query q0 + row), dims 32 half ..: 128-byte swizzled [128 rows][32 fp32] tile per half
+        uint8_t* base = sdq + half * 16384 + row * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(base + ((u ^ (row & 7)) * 16)) = make_uint4(r[4 * u], r[4 * u + 1], r[4 * u + 2],
+                                                                                 r[4 * u + 3]);
+      } else {
+        // dQ^T row = dim `row`, columns = queries 32 half ..: plain [64 queries][128 dims] tile
+        float* base = reinterpret_cast<float*>(sdq) + (32 * half) * 128 + row;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) base[e * 128] = __uint_as_float(r[e]);
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (t == 0 && ok) {
+        const int bh = b * p.H + h;
+        if constexpr (D == 64) {
+          tma_reduce_add_3d(&mdq, sdq, 0, q0, bh);
+          tma_reduce_add_3d(&mdq, sdq + 16384, 32, q0, bh);
+        } else {
+          tma_reduce_add_3d(&mdq, sdq, 0, q0, bh);
+        }
+        bulk_commit();
+      }
+      put_stat(st + 1, nxt);
+      if (t == 0) VAGUS_TR(st, 11);
     }
+    if (t == 0) bulk_wait<0>();                          // reductions performed before the CTA retires
     // dK (scaled) and dV rows of this CTA's keys
     const bool have = ok && nsteps > 0;
     if (have) tc_fence_after();
@@ -983,6 +1092,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     tc_fence_after();
     tmem_dealloc(tb, Lt::COLS);
   }
+#undef VAGUS_TR
 }
 
 template <typename Kern>
@@ -1058,15 +1168,23 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
                                     (unsigned long long)f.sv_b * 2};
   const unsigned long long so[3] = {(unsigned long long)f.so_l * 2, (unsigned long long)f.so_h * 2,
                                     (unsigned long long)f.so_b * 2};
-  const unsigned box[4] = {64u, 128u, 1u, 1u};
-  if (!encode_bf16_map(mq, f.q, 4, dq, sq, box) || !encode_bf16_map(mk, f.k, 4, dk, sk, box) ||
-      !encode_bf16_map(mv, f.v, 4, dk, sv, box) || !encode_bf16_map(mdo, a.dO, 4, dq, so, box))
+  const unsigned box[4] = {64u, 128u, 1u, 1u}, box_q[4] = {64u, static_cast<unsigned>(Lt::QROWS), 1u, 1u};
+  if (!encode_bf16_map(mq, f.q, 4, dq, sq, box_q) || !encode_bf16_map(mk, f.k, 4, dk, sk, box) ||
+      !encode_bf16_map(mv, f.v, 4, dk, sv, box) || !encode_bf16_map(mdo, a.dO, 4, dq, so, box_q))
     return 2;
+  // dq_acc (B * H, Lq, D) fp32: D = 64 reduces [128 queries][32 dims] boxes (128-byte
+  // swizzle), D = 128 one [64 queries][128 dims] box
+  alignas(64) unsigned char mdq[128];
+  const unsigned long long ddq[3] = {(unsigned long long)D, (unsigned long long)f.Lq, (unsigned long long)f.B * f.H};
+  const unsigned long long sdq[2] = {(unsigned long long)D * 4, (unsigned long long)f.Lq * D * 4};
+  const unsigned box_dq[3] = {D == 64 ? 32u : 128u, static_cast<unsigned>(Lt::QROWS), 1u};
+  if (!encode_f32_map(mdq, a.dq_acc, 3, ddq, sdq, box_dq, D == 64)) return 2;
   tcbw::Params p;
   p.Lq = f.Lq; p.Lk = f.Lk; p.H = f.H; p.Hk = f.Hk; p.causal = f.causal;
   p.sl2 = f.scale * kLog2e; p.scale = f.scale;
   p.lse = f.lse; p.delta = a.delta; p.dq_acc = a.dq_acc;
   p.dk = (__nv_bfloat16*)a.dk; p.dv = (__nv_bfloat16*)a.dv; p.err = f.err;
+  p.trace = g_attn_trace;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -1081,7 +1199,8 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
   attn_bwd_tc<D><<<grid, tcbw::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
                                                          *reinterpret_cast<const CUtensorMap*>(mk),
                                                          *reinterpret_cast<const CUtensorMap*>(mv),
-                                                         *reinterpret_cast<const CUtensorMap*>(mdo), p);
+                                                         *reinterpret_cast<const CUtensorMap*>(mdo),
+                                                         *reinterpret_cast<const CUtensorMap*>(mdq), p);
   const long long n = rows * D;
   attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a.dq_acc, (__nv_bfloat16*)a.dq, n,
                                                                               f.scale);
@@ -1125,6 +1244,8 @@ int attn_fwd(const AttnArgs& a, cudaStream_t st) {
   if (a.D == 64 && a.Dv == 128) return launch_fwd<64, 128>(a, st);
   return 5;
 }
+
+void attn_set_trace(unsigned long long* buf) { g_attn_trace = buf; }
 
 int attn_bwd(const AttnBwdArgs& a, cudaStream_t st) {
   if (!strides_ok(a.f) || !aligned16(a.dO) || a.f.Lq <= 0 || a.f.Lk <= 0) return 5;

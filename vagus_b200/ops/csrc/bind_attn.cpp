@@ -70,4 +70,9 @@ std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse,
 void register_attn_ops(pybind11::module& m) {
   m.def("attn_fwd", &attn_fwd);
   m.def("attn_bwd", &attn_bwd);
+  // buf: int64 device tensor of 512 entries, or None
+  m.def("attn_set_trace", [](c10::optional<Tensor> buf) {
+    if (buf) TORCH_CHECK(buf->is_cuda() && buf->numel() >= 512 && buf->element_size() == 8, "attn_set_trace: 512 x u64");
+    vagus::attn_set_trace(buf ? reinterpret_cast<unsigned long long*>(buf->data_ptr()) : nullptr);
+  });
 }

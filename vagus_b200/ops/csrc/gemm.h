@@ -32,5 +32,8 @@ int gemm_launch(const GemmArgs& args, cudaStream_t stream);
 // (innermost first), strides in bytes for dims 1..rank-1.  False on failure.
 bool encode_bf16_map(void* map, const void* base, int rank, const unsigned long long* dims,
                      const unsigned long long* strides, const unsigned* box);
+// fp32 tiled tensor map, 128-byte swizzle or none (e.g. for bulk reductions).
+bool encode_f32_map(void* map, const void* base, int rank, const unsigned long long* dims,
+                    const unsigned long long* strides, const unsigned* box, bool swizzle128);
 
 }  // namespace vagus

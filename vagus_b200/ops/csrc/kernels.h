@@ -125,6 +125,10 @@ struct AttnBwdArgs {
   float* delta;              // fp32 scratch (B, H, Lq)
 };
 int attn_bwd(const AttnBwdArgs& a, cudaStream_t st);
+// Phase clock of the tcgen05 backward's CTA (0, 0): clock64() at 16 phase
+// boundaries for each of the first 32 steps into buf[step * 16 + event]
+// (device memory, 512 u64); null switches it off.
+void attn_set_trace(unsigned long long* buf);
 
 // comm.cu: NVLink peer-to-peer all-gather / reduce-scatter over CUDA-IPC
 // shared heaps (see comm.cu for the heap layout and the epoch protocol).
