@@ -787,8 +787,8 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   float* s_delta = s_lse + 2 * QROWS;                            // [2][QROWS]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
   uint64_t *kv_full = bars, *q_full = bars + 1, *q_empty = bars + 3, *s_full = bars + 5, *p_full = bars + 6,
-           *dq_full = bars + 7, *dq_free = bars + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 9);
+           *dq_full = bars + 7, *dq_free = bars + 8, *s_free = bars + 9;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
@@ -817,6 +817,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     mbar_init(p_full, 8);
     mbar_init(dq_full, 1);
     mbar_init(dq_free, 8);
+    mbar_init(s_free, 8);
     *abort_flag = 0;
     fence_mbar_init();
     tma_prefetch_desc(&mq);
@@ -867,16 +868,11 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       const uint64_t dp_k = make_sw128_desc(smem_u32(spt), 16, 1024), ds_k = make_sw128_desc(smem_u32(sdst), 16, 1024);
       const uint64_t ds_mn = make_sw128_desc(smem_u32(sdst), 16384, 1024);
       const uint64_t dk_mn = make_sw128_desc(smem_u32(sk), 16384, 1024);
-      bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma);
-      for (int st = 0; ok && st < nsteps; ++st) {
+      // S^T and dP^T of step st into their TMEM columns
+      auto issue_sdp = [&](int st) {
         const int s = st & 1;
         const uint64_t dq_k = make_sw128_desc(smem_u32(sq + s * Lt::Q_BYTES), 16, 1024);
         const uint64_t ddo_k = make_sw128_desc(smem_u32(sdo + s * Lt::Q_BYTES), 16, 1024);
-        const uint64_t dq_mn = make_sw128_desc(smem_u32(sq + s * Lt::Q_BYTES), Lt::QCHUNK, 1024);
-        const uint64_t ddo_mn = make_sw128_desc(smem_u32(sdo + s * Lt::Q_BYTES), Lt::QCHUNK, 1024);
-        if (!mbar_wait(&q_full[s], (st >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
-        tc_fence_after();
-        // S^T, dP^T: K = D (D/64 chunks x 4 steps of 16)
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
 #pragma unroll
@@ -890,7 +886,30 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
             tc_mma_f16(tb + Lt::C_DP, desc_add(dv_k, c * 16384 + kk * 32), desc_add(ddo_k, c * Lt::QCHUNK + kk * 32),
                        id_s, (c | kk) ? 1u : 0u);
         tc_commit(s_full);
+      };
+      // Schedule: S^T / dP^T of step st + 1 go in as soon as the softmax warps
+      // have read step st's scores (s_free), so they run while those warps
+      // compute P and dS; then step st's dV, dK and dQ.
+      bool ok = mbar_wait(kv_full, 0, abort_flag, p.err, kErrTimeoutMma) &&
+                mbar_wait(&q_full[0], 0, abort_flag, p.err, kErrTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0);
+      }
+      for (int st = 0; ok && st < nsteps; ++st) {
+        const int s = st & 1;
+        VAGUS_TR(st, 0);
+        if (st + 1 < nsteps) {
+          if (!mbar_wait(&q_full[s ^ 1], ((st + 1) >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+          if (!mbar_wait(s_free, st & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+          tc_fence_after();
+          issue_sdp(st + 1);
+        }
+        VAGUS_TR(st, 1);
+        const uint64_t dq_mn = make_sw128_desc(smem_u32(sq + s * Lt::Q_BYTES), Lt::QCHUNK, 1024);
+        const uint64_t ddo_mn = make_sw128_desc(smem_u32(sdo + s * Lt::Q_BYTES), Lt::QCHUNK, 1024);
         if (!mbar_wait(p_full, st & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        VAGUS_TR(st, 2);
         tc_fence_after();
         // dV += P^T dO, dK += dS^T Q: K = the block's queries (16 per step)
 #pragma unroll
@@ -900,7 +919,9 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           tc_mma_f16(tb + Lt::C_DV, desc_add(dp_k, a_off), desc_add(ddo_mn, j * 2048), id_kv, acc);
           tc_mma_f16(tb + Lt::C_DK, desc_add(ds_k, a_off), desc_add(dq_mn, j * 2048), id_kv, acc);
         }
+        VAGUS_TR(st, 3);
         if (st > 0 && !mbar_wait(dq_free, (st - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        VAGUS_TR(st, 4);
         tc_fence_after();
         // dQ: K = the 128 keys (8 steps of 16 rows)
 #pragma unroll
@@ -910,7 +931,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           else
             tc_mma_f16(tb + Lt::C_DQ, desc_add(dk_mn, kk * 2048), desc_add(ds_mn, kk * 2048), id_q, kk ? 1u : 0u);
         }
-        tc_commit(dq_full);
+        tc_commit(dq_full);                              // also: P^T / dS^T of step st consumed
         tc_commit(&q_empty[s]);
         VAGUS_TR(st, 5);
       }
@@ -936,6 +957,41 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       if (t < QROWS) s_lse[(st & 1) * QROWS + t] = v;
       else if (t < 2 * QROWS) s_delta[(st & 1) * QROWS + t - QROWS] = v;
     };
+    // dQ of step sto (complete in TMEM) -> fp32 staging tile -> one bulk
+    // reduction into dq_acc (the tensor map clips rows past Lq)
+    auto dq_out = [&](int sto) {
+      const int h = hk * group + sto / per_head, q0 = (qb0 + sto % per_head) * QROWS;
+      tc_fence_after();
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tl + Lt::C_DQ + static_cast<uint32_t>(32 * half), r);
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      if (t == 0) bulk_wait_read<0>();                  // the previous reduction has read the tile
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if constexpr (D == 64) {
+        // dQ row `row` (query q0 + row), dims 32 half ..: 128-byte swizzled [128 rows][32 fp32] tile per half
+        uint8_t* base = sdq + half * 16384 + row * 128;
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+          *reinterpret_cast<uint4*>(base + ((u ^ (row & 7)) * 16)) = make_uint4(r[4 * u], r[4 * u + 1], r[4 * u + 2],
+                                                                                 r[4 * u + 3]);
+      } else {
+        // dQ^T row = dim `row`, columns = queries 32 half ..: plain [64 queries][128 dims] tile
+        float* base = reinterpret_cast<float*>(sdq) + (32 * half) * 128 + row;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) base[e * 128] = __uint_as_float(r[e]);
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (t == 0 && ok) {
+        const int bh = b * p.H + h;
+        tma_reduce_add_3d(&mdq, sdq, 0, q0, bh);
+        if constexpr (D == 64) tma_reduce_add_3d(&mdq, sdq + 16384, 32, q0, bh);
+        bulk_commit();
+      }
+    };
     put_stat(0, fetch_stat(0));
     // kernel parameters in registers: the lambdas above take `p` by reference,
     // and reads through that reference inside the hot loop are memory loads
@@ -943,8 +999,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     const int Lk = p.Lk, Lq = p.Lq;
     const bool causal = p.causal != 0;
     for (int st = 0; st < nsteps; ++st) {
-      const int h = hk * group + st / per_head, q0 = (qb0 + st % per_head) * QROWS;
-      const long long rowbase = ((long long)b * p.H + h) * p.Lq;
+      const int q0 = (qb0 + st % per_head) * QROWS;
       const float* lse_s = s_lse + (st & 1) * QROWS + HALF * half;
       const float* del_s = s_delta + (st & 1) * QROWS + HALF * half;
       asm volatile("bar.sync 1, 256;" ::: "memory");     // this step's statistics are in place
@@ -954,15 +1009,21 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       const uint32_t cs = tl + Lt::C_S + static_cast<uint32_t>(HALF * half);
       const uint32_t cd = tl + Lt::C_DP + static_cast<uint32_t>(HALF * half);
       const int qbase = q0 + HALF * half;
-      const bool full = (k0 + KROWS <= p.Lk) && (q0 + QROWS <= p.Lq) && (!p.causal || k0 + KROWS - 1 <= q0 + offs);
-      // 32 query columns at a time: scores and dP from TMEM, P^T and dS^T as bf16 into the
-      // 128-byte swizzled tiles (16-byte unit u of the 32 columns)
+      const bool full = (k0 + KROWS <= Lk) && (q0 + QROWS <= Lq) && (!causal || k0 + KROWS - 1 <= q0 + offs);
+      // 32 query columns at a time: scores and dP from TMEM (the MMA warp may
+      // refill them once the last chunk is read), P^T and dS^T as bf16 into
+      // the 128-byte swizzled tiles once the previous step's products are done
 #pragma unroll
       for (int c = 0; c < HALF / 32; ++c) {
         float sv[32], dp[32];
         tmem_ld_32x32b_x32(cs + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
         tmem_ld_32x32b_x32(cd + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&dp[0]));
         tmem_ld_wait();
+        if (c == HALF / 32 - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(s_free);
+        }
         if (t == 0 && c == 0) VAGUS_TR(st, 7);
         float ls[32], dl[32];
 #pragma unroll
@@ -990,6 +1051,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           }
         }
         if (t == 0) VAGUS_TR(st, c == 0 ? 13 : 15);
+        if (c == 0 && st > 0) ok = ok && mbar_wait_spin(dq_full, (st - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int col = HALF * half + 32 * c + 8 * u;  // query column inside the block
@@ -1010,48 +1072,14 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       __syncwarp();
       if (t == 0) VAGUS_TR(st, 8);
       if (lane == 0) mbar_arrive(p_full);
-      const float nxt = fetch_stat(st + 1);              // in flight while dQ is awaited
-      ok = ok && mbar_wait_spin(dq_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
-      if (t == 0) VAGUS_TR(st, 9);
-      tc_fence_after();
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tl + Lt::C_DQ + static_cast<uint32_t>(32 * half), r);
-      tmem_ld_wait();
-      if (t == 0) VAGUS_TR(st, 10);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
-      // dQ -> fp32 staging tile -> one bulk reduction into dq_acc (the tensor map
-      // clips rows past Lq)
-      if (t == 0) bulk_wait_read<0>();                  // the previous step's reduction has read the tile
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if constexpr (D == 64) {
-        // dQ row `row` (query q0 + row), dims 32 half ..: 128-byte swizzled [128 rows][32 fp32] tile per half
-        uint8_t* base = sdq + half * 16384 + row * 128;
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<uint4*>(base + ((u ^ (row & 7)) * 16)) = make_uint4(r[4 * u], r[4 * u + 1], r[4 * u + 2],
-                                                                                 r[4 * u + 3]);
-      } else {
-        // dQ^T row = dim `row`, columns = queries 32 half ..: plain [64 queries][128 dims] tile
-        float* base = reinterpret_cast<float*>(sdq) + (32 * half) * 128 + row;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) base[e * 128] = __uint_as_float(r[e]);
-      }
-      fence_proxy_async_smem();
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (t == 0 && ok) {
-        const int bh = b * p.H + h;
-        if constexpr (D == 64) {
-          tma_reduce_add_3d(&mdq, sdq, 0, q0, bh);
-          tma_reduce_add_3d(&mdq, sdq + 16384, 32, q0, bh);
-        } else {
-          tma_reduce_add_3d(&mdq, sdq, 0, q0, bh);
-        }
-        bulk_commit();
-      }
-      put_stat(st + 1, nxt);
+      const float nxt = fetch_stat(st + 1);              // in flight during the dQ readout
+      if (st > 0) dq_out(st - 1);
       if (t == 0) VAGUS_TR(st, 11);
+      put_stat(st + 1, nxt);
+    }
+    if (nsteps > 0) {
+      ok = ok && mbar_wait_spin(dq_full, (nsteps - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      dq_out(nsteps - 1);
     }
     if (t == 0) bulk_wait<0>();                          // reductions performed before the CTA retires
     // dK (scaled) and dV rows of this CTA's keys
