@@ -402,6 +402,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     float* xsum = xmax + 2 * BQ;                                    // [2][128] partial row sums
     float m_run = -INFINITY, l_run = 0.f;
     bool ok = true;
+    // kernel parameters in registers (the lambdas above take `p` by reference,
+    // so reads through it in this loop would be memory loads)
+    const float psl2 = p.sl2;
+    const int Lk = p.Lk;
+    const bool causal = p.causal != 0;
     // a failed (timed-out) wait does not leave the loop: the warp pair must
     // keep meeting at its named barrier, so the remaining tiles run on
     // whatever is in the buffers and the error word reports the failure
@@ -419,7 +424,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       if (lane == 0) mbar_arrive(&s_free[s]);
       const int k0 = j * BKV + 64 * half;
       // tiles wholly visible to every row of the CTA skip the per-element mask
-      const bool full = (j * BKV + BKV <= p.Lk) && (!p.causal || j * BKV + BKV - 1 <= q0 + offs);
+      const bool full = (j * BKV + BKV <= Lk) && (!causal || j * BKV + BKV - 1 <= q0 + offs);
       float mt0 = -INFINITY, mt1 = -INFINITY, mt2 = -INFINITY, mt3 = -INFINITY;
       if (full) {
 #pragma unroll
@@ -428,7 +433,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           mt2 = fmaxf(mt2, x[i + 2]); mt3 = fmaxf(mt3, x[i + 3]);
         }
       } else {
-        const int lim = p.causal ? min(p.Lk - 1, qi + offs) : p.Lk - 1;   // last visible key
+        const int lim = causal ? min(Lk - 1, qi + offs) : Lk - 1;   // last visible key
 #pragma unroll
         for (int i = 0; i < 64; ++i) {
           if (k0 + i > lim) x[i] = -INFINITY;
@@ -436,7 +441,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         }
       }
       // raw maxima -> scaled, combined with the partner warp
-      float mt = fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3)) * p.sl2;
+      float mt = fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3)) * psl2;
       xmax[half * BQ + row] = mt;
       asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
       mt = fmaxf(mt, xmax[(half ^ 1) * BQ + row]);
@@ -449,7 +454,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         m_run = m_new;
       }
       const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
-      const float sl2 = (m_run == -INFINITY) ? 0.f : p.sl2;
+      const float sl2 = (m_run == -INFINITY) ? 0.f : psl2;
       float ls0 = 0.f, ls1 = 0.f;
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
