@@ -104,3 +104,62 @@ def test_nvlink_collectives_match_nccl():
         for kind, it, e in errs:
             tol = 0.0 if kind in ("ag", "error_word") else 1e-5
             assert e <= tol, (rank, kind, it, e)
+
+
+def _muon_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+        torch.cuda.set_device(rank)
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{rank}"),
+                                timeout=datetime.timedelta(seconds=120))
+        from torch.distributed.device_mesh import init_device_mesh
+        from torch.distributed.tensor import Shard, distribute_tensor
+        from vagus_b200 import ops
+        from vagus_b200.optim.muon import muon_update_sharded
+        mesh = init_device_mesh("cuda", (world,))
+        shapes = [(256, 512)] * 3 + [(512, 256)] * 2 + [(128, 384)]
+        g = torch.Generator().manual_seed(0)
+        full_p = [torch.randn(s, generator=g) for s in shapes]
+        full_g = [torch.randn(s, generator=g) for s in shapes]
+        results = []
+        exchanges = {}
+        for use in (None, exchanges):
+            P = [distribute_tensor(t.clone().cuda(), mesh, [Shard(0)]) for t in full_p]
+            Gr = [distribute_tensor(t.clone().cuda(), mesh, [Shard(0)]) for t in full_g]
+            M = [distribute_tensor(torch.zeros(s, device="cuda"), mesh, [Shard(0)]) for s in shapes]
+            for _ in range(3):          # three epochs: both slots and a reuse
+                muon_update_sharded(P, Gr, M, lr=0.02, momentum=0.95, weight_decay=0.01, nesterov=True,
+                                    ns_steps=5, eps=1e-7, exchanges=use)
+            torch.cuda.synchronize()
+            results.append([p.to_local().clone() for p in P])
+        errs = [("muon", i, (a - b).abs().max().item()) for i, (a, b) in enumerate(zip(*results))]
+        errs.append(("fused_used", 0, 0.0 if exchanges else 1.0))
+        errs.append(("error_word", 0, float(ops.native().error_word())))
+        for ex in exchanges.values():
+            ex.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, errs))
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_muon_fused_scatter_matches_allgather():
+    """The sharded Muon step with the Newton-Schulz product scattered to the
+    row owners from the GEMM epilogue equals the all-gather path bit for bit."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_muon_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs in results:
+        assert not isinstance(errs, str), f"rank {rank}: {errs}"
+        for kind, i, e in errs:
+            assert e == 0.0, (rank, kind, i, e)

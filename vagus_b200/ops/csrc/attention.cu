@@ -221,6 +221,7 @@ attn_fwd_kernel(const AttnArgs a) {
 // K loads run a tile further ahead than V), s_full[2] / s_free[2] (MMA <->
 // softmax), p_full (softmax -> MMA), o_done (MMA -> softmax: P buffer free
 // and O stable).  Every wait is bounded.
+extern unsigned long long* g_attn_trace;   // host side of the phase trace (attn_set_trace)
 namespace tcfa {
 constexpr int BQ = 128, BKV = 128, THREADS = 320;   // 10 warps
 constexpr float kRescale = 8.f;     // log2 units
@@ -249,6 +250,7 @@ struct Params {
   long long so_b, so_h, so_l;
   float* lse;
   int* err;
+  unsigned long long* trace;       // phase clock of the last query block of head 0, [tile][16]; null: off
 };
 }  // namespace tcfa
 
@@ -286,6 +288,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   const int q_last = min(q0 + BQ, p.Lq) - 1;
   const int k_end = p.causal ? min(p.Lk, q_last + offs + 1) : p.Lk;
   const int ntiles = k_end > 0 ? (k_end + BKV - 1) / BKV : 0;
+  const bool tracing = p.trace != nullptr && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0;
+#define VAGUS_TRF(tile, ev)                                                     \
+  do {                                                                          \
+    if (tracing && (tile) < 32) p.trace[(tile) * 16 + (ev)] = clock64();        \
+  } while (0)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -370,7 +377,9 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       if (ok) ok = issue_s(0);
       for (int j = 0; ok && j < ntiles; ++j) {
         if (j + 1 < ntiles && !issue_s(j + 1)) break;
+        VAGUS_TRF(j, 0);
         if (!mbar_wait_spin(p_full, j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        VAGUS_TRF(j, 1);
         const int s = j & 1;
         if (!mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
@@ -385,6 +394,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
                        (j > 0 || kc > 0 || kk > 0) ? 1u : 0u);
         tc_commit(&v_empty[s]);
         tc_commit(o_done);
+        VAGUS_TRF(j, 2);
       }
     }
   } else {
@@ -413,6 +423,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     for (int j = 0; j < ntiles; ++j) {
       const int s = j & 1;
       ok = ok && mbar_wait_spin(&s_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 3);
       tc_fence_after();
       float x[64];
       const uint32_t sa = tmem_base + t_lane + Lt::TMEM_S + static_cast<uint32_t>(s * BKV + 64 * half);
@@ -422,6 +433,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[s]);
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 4);
       const int k0 = j * BKV + 64 * half;
       // tiles wholly visible to every row of the CTA skip the per-element mask
       const bool full = (j * BKV + BKV <= Lk) && (!causal || j * BKV + BKV - 1 <= q0 + offs);
@@ -442,8 +454,10 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       }
       // raw maxima -> scaled, combined with the partner warp
       float mt = fmaxf(fmaxf(mt0, mt1), fmaxf(mt2, mt3)) * psl2;
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 5);
       xmax[half * BQ + row] = mt;
       asm volatile("bar.sync %0, 64;" ::"r"(1 + quarter) : "memory");
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 6);
       mt = fmaxf(mt, xmax[(half ^ 1) * BQ + row]);
       const float m_new = fmaxf(m_run, mt);
       const bool resc = m_new > m_run + kRescale;     // false while the row has seen nothing
@@ -456,12 +470,16 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
       const float sl2 = (m_run == -INFINITY) ? 0.f : psl2;
       float ls0 = 0.f, ls1 = 0.f;
+      // one exponential in four on the FMA pipe (ex2_poly), the rest on the
+      // MUFU unit, whose 16 results per clock per SM otherwise bound this loop
 #pragma unroll
-      for (int i = 0; i < 64; i += 2) {
+      for (int i = 0; i < 64; i += 4) {
         x[i] = ex2_approx(fmaf(x[i], sl2, nm));
         x[i + 1] = ex2_approx(fmaf(x[i + 1], sl2, nm));
-        ls0 += x[i];
-        ls1 += x[i + 1];
+        x[i + 2] = ex2_approx(fmaf(x[i + 2], sl2, nm));
+        x[i + 3] = ex2_poly(fmaf(x[i + 3], sl2, nm));
+        ls0 += x[i] + x[i + 2];
+        ls1 += x[i + 1] + x[i + 3];
       }
       if (m_run == -INFINITY) {
 #pragma unroll
@@ -469,8 +487,10 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         ls0 = ls1 = 0.f;
       }
       l_run += ls0 + ls1;
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 7);
       // PV_{j-1} must be done before P is overwritten or O rescaled
       if (j > 0) ok = ok && mbar_wait_spin(o_done, (j - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 8);
       if (resc && j > 0) {
         tc_fence_after();
 #pragma unroll
@@ -493,10 +513,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
                                    pack_bf16x2(v8[4], v8[5]), pack_bf16x2(v8[6], v8[7]));
         *reinterpret_cast<uint4*>(sp + half * 16384 + row * 128 + ((u ^ (row & 7)) * 16)) = w;
       }
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 9);
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(p_full);
+      if (warp == 2 && lane == 0) VAGUS_TRF(j, 10);
     }
     // ------------------------------------------------------------ epilogue
     xsum[half * BQ + row] = l_run;
@@ -538,6 +560,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     tc_fence_after();
     tmem_dealloc(tmem_base, Lt::TMEM_COLS);
   }
+#undef VAGUS_TRF
 }
 
 // --------------------------------------------------------------- backward --
@@ -1008,7 +1031,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       const float* lse_s = s_lse + (st & 1) * QROWS + HALF * half;
       const float* del_s = s_delta + (st & 1) * QROWS + HALF * half;
       asm volatile("bar.sync 1, 256;" ::: "memory");     // this step's statistics are in place
-      ok = ok && mbar_wait_spin(s_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      ok = ok && mbar_wait(s_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
       if (t == 0) VAGUS_TR(st, 6);
       tc_fence_after();
       const uint32_t cs = tl + Lt::C_S + static_cast<uint32_t>(HALF * half);
@@ -1056,7 +1079,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           }
         }
         if (t == 0) VAGUS_TR(st, c == 0 ? 13 : 15);
-        if (c == 0 && st > 0) ok = ok && mbar_wait_spin(dq_full, (st - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+        if (c == 0 && st > 0) ok = ok && mbar_wait(dq_full, (st - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int col = HALF * half + 32 * c + 8 * u;  // query column inside the block
@@ -1083,7 +1106,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       put_stat(st + 1, nxt);
     }
     if (nsteps > 0) {
-      ok = ok && mbar_wait_spin(dq_full, (nsteps - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      ok = ok && mbar_wait(dq_full, (nsteps - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
       dq_out(nsteps - 1);
     }
     if (t == 0) bulk_wait<0>();                          // reductions performed before the CTA retires
@@ -1160,6 +1183,7 @@ int launch_fwd_tc(const AttnArgs& a, cudaStream_t st) {
   p.o = a.o; p.so_b = a.so_b; p.so_h = a.so_h; p.so_l = a.so_l;
   p.lse = a.lse;
   p.err = a.err;
+  p.trace = g_attn_trace;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);

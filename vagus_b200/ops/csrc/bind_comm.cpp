@@ -78,9 +78,30 @@ void comm_reduce_scatter(Tensor out, Tensor in, std::vector<int64_t> bases, int6
   TORCH_CHECK(rc == 0, "comm_reduce_scatter failed (code ", rc, ")");
 }
 
+// Epoch barrier over the heaps (the generic flag block).
+void comm_barrier(std::vector<int64_t> bases, int64_t rank, int64_t epoch) {
+  const int rc = vagus::comm_barrier(peers_of(bases), static_cast<int>(rank), static_cast<int>(bases.size()),
+                                     vagus::kCommBarFlags, static_cast<unsigned>(epoch), vagus_device_error_ptr(),
+                                     stream());
+  TORCH_CHECK(rc == 0, "comm_barrier failed (code ", rc, ")");
+}
+
+// A tensor over `numel` elements of this process's heap at byte offset
+// `offset` (no ownership: the heap outlives it).
+Tensor comm_heap_view(int64_t ptr, int64_t offset, int64_t numel, at::ScalarType dtype) {
+  const int64_t es = c10::elementSize(dtype);
+  TORCH_CHECK(offset % es == 0 && numel >= 0, "comm_heap_view: alignment");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  auto opts = torch::TensorOptions().dtype(dtype).device(torch::kCUDA, dev);
+  return torch::from_blob(reinterpret_cast<char*>(ptr) + offset, {numel}, [](void*) {}, opts);
+}
+
 }  // namespace
 
 void register_comm_ops(pybind11::module& m) {
+  m.def("comm_barrier", &comm_barrier);
+  m.def("comm_heap_view", &comm_heap_view);
   m.def("comm_heap_create", &comm_heap_create);
   m.def("comm_heap_open", &comm_heap_open);
   m.def("comm_heap_close", &comm_heap_close);

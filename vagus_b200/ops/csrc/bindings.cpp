@@ -106,6 +106,50 @@ int64_t gemm(Tensor A, bool a_mn, Tensor B, bool b_mn, Tensor C, c10::optional<T
   return vagus::gemm_launch(g, stream());
 }
 
+// GEMM whose bf16 product is not written to a local C but scattered by row
+// blocks (mode 1) or column blocks (mode 2) of `span` to the buffers at the
+// addresses in `dst` (peer mappings of other GPUs' memory for a fused
+// product + all-to-all over NVLink): block o goes to dst[o] at
+// [batch0 + b][local row][local col] with row pitch dst_ld, batch stride
+// dst_stride (elements).
+int64_t gemm_scatter(Tensor A, bool a_mn, Tensor B, bool b_mn, c10::optional<Tensor> S, double alpha, double beta,
+                     std::vector<int64_t> dst, int64_t mode, int64_t span, int64_t dst_ld, int64_t dst_stride,
+                     int64_t batch0) {
+  need_cuda(A, "A"); need_cuda(B, "B");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && B.scalar_type() == at::kBFloat16, "gemm operands must be bf16");
+  TORCH_CHECK(A.dim() == B.dim() && (A.dim() == 2 || A.dim() == 3), "gemm_scatter: rank mismatch");
+  TORCH_CHECK(A.stride(-1) == 1 && B.stride(-1) == 1, "gemm_scatter: inner stride must be 1");
+  TORCH_CHECK(!dst.empty() && dst.size() <= 16, "gemm_scatter: 1..16 destinations");
+  const bool batched = A.dim() == 3;
+  vagus::GemmArgs g;
+  g.batch = batched ? static_cast<int>(A.size(0)) : 1;
+  g.a_mn = a_mn; g.b_mn = b_mn;
+  const int64_t ar = A.size(-2), ac = A.size(-1), br = B.size(-2), bc = B.size(-1);
+  g.M = static_cast<int>(a_mn ? ac : ar);
+  g.K = static_cast<int>(a_mn ? ar : ac);
+  g.N = static_cast<int>(b_mn ? bc : br);
+  TORCH_CHECK((b_mn ? br : bc) == g.K, "gemm_scatter: K mismatch");
+  g.A = A.data_ptr(); g.B = B.data_ptr();
+  g.lda = A.stride(-2); g.ldb = B.stride(-2);
+  g.strideA = batched ? A.stride(0) : 0; g.strideB = batched ? B.stride(0) : 0;
+  g.C = nullptr; g.ldc = 0; g.strideC = 0; g.c_f32 = 0;
+  if (S.has_value() && S->defined()) {
+    const Tensor& s = *S;
+    need_bf16_or_f32(s, "S");
+    TORCH_CHECK(s.size(-2) == g.M && s.size(-1) == g.N && s.stride(-1) == 1, "gemm_scatter: S shape mismatch");
+    g.S = s.data_ptr(); g.lds = s.stride(-2); g.strideS = batched ? s.stride(0) : 0; g.s_f32 = is_f32(s);
+  }
+  g.alpha = static_cast<float>(alpha); g.beta = static_cast<float>(beta);
+  g.split_k = 1;
+  g.scatter = static_cast<int>(mode);
+  g.scatter_span = static_cast<int>(span);
+  g.scatter_n = static_cast<int>(dst.size());
+  for (size_t i = 0; i < dst.size(); ++i) g.scatter_dst[i] = reinterpret_cast<void*>(dst[i]);
+  g.dst_ld = dst_ld; g.dst_stride = dst_stride; g.scatter_batch0 = static_cast<int>(batch0);
+  g.err = err_ptr();
+  return vagus::gemm_launch(g, stream());
+}
+
 // ------------------------------------------------------------------ norms --
 std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor gamma, double eps, bool out_f32) {
   need_cuda(x, "x"); need_bf16_or_f32(x, "x");
@@ -301,6 +345,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vagus_b200 sm_100a kernels";
   m.def("error_word", &error_word, "device error word (bounded-wait timeouts); 0 = none");
   m.def("reset_error", &reset_error);
+  m.def("gemm_scatter", &gemm_scatter);
   m.def("gemm", &gemm, "tcgen05 GEMM", py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("C"),
         py::arg("S") = py::none(), py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("atomic") = false,
         py::arg("split_k") = 0, py::arg("block_n") = 0);

@@ -168,4 +168,10 @@ int comm_reduce_scatter(const CommPeers& peers, int rank, int world, uint32_t ep
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, uint32_t epoch, int* err, cudaStream_t st) {
+  if (world < 2 || world > kMaxCommPeers || flag_off < 0 || flag_off + 4 * kMaxCommPeers > kCommHeaderBytes) return 5;
+  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, flag_off, epoch, err);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
 }  // namespace vagus

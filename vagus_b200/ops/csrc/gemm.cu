@@ -70,6 +70,10 @@ struct KParams {
   // in the atomic epilogue
   int streamk;
   long long kb_per_worker;
+  // scatter epilogue (see GemmArgs)
+  int scatter, scatter_span, scatter_batch0;
+  long long dst_ld, dst_stride;
+  void* scatter_dst[16];
 };
 
 __device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row, int col0, const float* v) {
@@ -130,7 +134,18 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row
       for (int j = 0; j < 32; ++j) if (col0 + j < p.N) c[j] = out[j];
     }
   } else {
-    __nv_bfloat16* c = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc + col0;
+    __nv_bfloat16* c;
+    if (p.scatter == 1) {
+      const int o = row / p.scatter_span;
+      c = reinterpret_cast<__nv_bfloat16*>(p.scatter_dst[o]) + (long long)(p.scatter_batch0 + b) * p.dst_stride +
+          (long long)(row - o * p.scatter_span) * p.dst_ld + col0;
+    } else if (p.scatter == 2) {
+      const int o = col0 / p.scatter_span;       // span % 32 == 0: one owner per 32-column chunk
+      c = reinterpret_cast<__nv_bfloat16*>(p.scatter_dst[o]) + (long long)(p.scatter_batch0 + b) * p.dst_stride +
+          (long long)row * p.dst_ld + (col0 - o * p.scatter_span);
+    } else {
+      c = reinterpret_cast<__nv_bfloat16*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc + col0;
+    }
     if (full) {
 #pragma unroll
       for (int j = 0; j < 32; j += 8) {
@@ -633,6 +648,8 @@ int num_sms() {
   return n;
 }
 
+bool fill_scatter(KParams& p, const GemmArgs& a);
+
 template <int BN, bool A_MN, bool B_MN>
 int launch_t(const GemmArgs& a, cudaStream_t stream) {
   using C = Cfg<BN>;
@@ -661,6 +678,7 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
     if (a.S) v = v && (reinterpret_cast<uintptr_t>(a.S) % 16 == 0) && ((a.lds * se) % 16 == 0) && ((a.strideS * se) % 16 == 0);
     p.vec = v ? 1 : 0;
   }
+  if (!fill_scatter(p, a)) return 5;
   const int grid = std::min(p.units, num_sms());
   auto kern = gemm_kernel<BN, A_MN, B_MN>;
   static bool attr_set[64] = {};
@@ -675,6 +693,31 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
                  a.K, p.units);
   kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+// Scatter-epilogue fields and the 16-byte vector rule for the destinations;
+// false when the request is malformed.
+bool fill_scatter(KParams& p, const GemmArgs& a) {
+  p.scatter = a.scatter;
+  p.scatter_span = a.scatter_span;
+  p.scatter_batch0 = a.scatter_batch0;
+  p.dst_ld = a.dst_ld;
+  p.dst_stride = a.dst_stride;
+  for (int i = 0; i < 16; ++i) p.scatter_dst[i] = i < a.scatter_n ? a.scatter_dst[i] : nullptr;
+  if (!a.scatter) return true;
+  if (a.scatter != 1 && a.scatter != 2) return false;
+  if (a.c_f32 || a.atomic || a.scatter_span <= 0 || a.scatter_n < 1 || a.scatter_n > 16) return false;
+  const int extent = a.scatter == 1 ? a.M : a.N;
+  if ((extent + a.scatter_span - 1) / a.scatter_span > a.scatter_n) return false;
+  if (a.scatter == 2 && a.scatter_span % 32) return false;
+  bool v = (a.dst_ld * 2) % 16 == 0 && (a.dst_stride * 2) % 16 == 0;
+  for (int i = 0; i < a.scatter_n; ++i) {
+    if (!a.scatter_dst[i]) return false;
+    v = v && reinterpret_cast<uintptr_t>(a.scatter_dst[i]) % 16 == 0;
+  }
+  if (a.scatter == 2) v = v && (a.scatter_span * 2) % 16 == 0;
+  if (!v) p.vec = 0;
+  return true;
 }
 
 template <bool A_MN, bool B_MN>
@@ -703,6 +746,7 @@ int launch_pair(const GemmArgs& a, cudaStream_t stream) {
     if (a.S) v = v && (reinterpret_cast<uintptr_t>(a.S) % 16 == 0) && ((a.lds * se) % 16 == 0) && ((a.strideS * se) % 16 == 0);
     p.vec = v ? 1 : 0;
   }
+  if (!fill_scatter(p, a)) return 5;
   int units = p.units;
   p.streamk = 0;
   p.kb_per_worker = 0;

@@ -22,6 +22,18 @@ struct GemmArgs {
   int split_k = 0;           // 0: automatic (atomic mode only), 1: none, >1: fixed, -1: stream-K (CTA pairs)
   int block_n = 0;           // 0: automatic (128 or 256)
   int* err = nullptr;        // device error word (bounded-wait timeouts)
+  // Scatter epilogue (bf16 C, not atomic): the output's rows (scatter = 1) or
+  // columns (scatter = 2) fall into blocks of scatter_span; block o is written
+  // to scatter_dst[o] -- typically another GPU's buffer through a peer mapping,
+  // so the product travels over NVLink from the epilogue itself -- as
+  // [scatter_batch0 + b][row - o span | row][col | col - o span] with row pitch
+  // dst_ld and batch stride dst_stride (elements).  C is not written.
+  int scatter = 0;
+  int scatter_span = 0;
+  int scatter_n = 0;         // number of destinations (<= 16)
+  void* scatter_dst[16] = {};
+  long long dst_ld = 0, dst_stride = 0;
+  int scatter_batch0 = 0;
 };
 
 // Returns 0 on launch, nonzero on argument / encode / launch failure.

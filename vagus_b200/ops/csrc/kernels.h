@@ -144,5 +144,10 @@ int comm_all_gather(const CommPeers& peers, int rank, int world, unsigned epoch,
 int comm_reduce_scatter(const CommPeers& peers, int rank, int world, unsigned epoch, const void* in, void* out,
                         long long shard_elems, int elem_bytes, float scale, long long ag_cap, long long slot_cap,
                         int* err, cudaStream_t st);
+// Cross-GPU epoch barrier on the flag words at byte offset flag_off of every
+// heap (kMaxCommPeers u32 per heap): publishes this stream's earlier writes
+// (system-scope release), then waits (bounded) until every peer reached epoch.
+constexpr int kCommBarFlags = 512;
+int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, unsigned epoch, int* err, cudaStream_t st);
 
 }  // namespace vagus

@@ -59,7 +59,10 @@ def _ns_torch(X: Tensor, coeffs) -> Tensor:
     return X
 
 
-def _ns_kernels(X: Tensor, coeffs) -> Tensor:
+def _ns_kernels(X: Tensor, coeffs, last=None) -> Tensor | None:
+    """Newton-Schulz on the tcgen05 GEMM.  With ``last``, the final product
+    X' = B X + a X is not formed here: ``last(B, X, a)`` is called instead
+    (the fused product + scatter over NVLink) and None is returned."""
     from ..ops._core import gemm
     batched = X.dim() == 3
     Xb = X if batched else X[None]
@@ -68,16 +71,19 @@ def _ns_kernels(X: Tensor, coeffs) -> Tensor:
     A = torch.empty(n, m, m, device=X.device, dtype=torch.bfloat16)
     Bm = torch.empty_like(A)
     Y = torch.empty_like(Xb)
-    for a, b, c in coeffs:
+    for i, (a, b, c) in enumerate(coeffs):
         gemm(Xb, False, Xb, False, A)                              # A = X X^T
         gemm(A, False, A, False, Bm, S=A, alpha=c, beta=b)         # B = c A A^T + b A
+        if last is not None and i == len(coeffs) - 1:
+            last(Bm, Xb, a)
+            return None
         gemm(Bm, False, Xb, True, Y, S=Xb, alpha=1.0, beta=a)      # X' = B X + a X
         Xb, Y = Y, Xb
     return Xb if batched else Xb[0]
 
 
-def newton_schulz(G: Tensor, steps: int = 5, eps: float = 1e-7, scheme: str = "jordan") -> Tensor:
-    """Approximate U V^T of G (..., m, n) by quintic Newton-Schulz in bf16."""
+def _ns_prepare(G: Tensor, steps: int, eps: float, scheme: str):
+    """(X, coeffs, transposed): G in bf16, wide orientation, Frobenius-normalised."""
     coeffs, slack = NS_SCHEMES[scheme]
     if len(coeffs) == 1:
         coeffs = coeffs * steps
@@ -86,7 +92,17 @@ def newton_schulz(G: Tensor, steps: int = 5, eps: float = 1e-7, scheme: str = "j
     if transposed:
         X = X.mT
     X = X / (X.norm(dim=(-2, -1), keepdim=True) * (1 + slack) + eps)
-    if X.is_cuda and X.size(-1) % 8 == 0 and X.size(-2) % 8 == 0 and X.dim() in (2, 3):
+    return X, coeffs, transposed
+
+
+def _ns_on_kernels(X: Tensor) -> bool:
+    return X.is_cuda and X.size(-1) % 8 == 0 and X.size(-2) % 8 == 0 and X.dim() in (2, 3)
+
+
+def newton_schulz(G: Tensor, steps: int = 5, eps: float = 1e-7, scheme: str = "jordan") -> Tensor:
+    """Approximate U V^T of G (..., m, n) by quintic Newton-Schulz in bf16."""
+    X, coeffs, transposed = _ns_prepare(G, steps, eps, scheme)
+    if _ns_on_kernels(X):
         X = _ns_kernels(X.contiguous(), coeffs)
     else:
         X = _ns_torch(X, coeffs)
@@ -145,8 +161,16 @@ def _shard_layout(p):
 
 
 def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_decay, nesterov, ns_steps, eps,
-                        lr_adjust="shape", ns_coeffs="jordan", compile_ns=False) -> None:
-    """Muon for row-sharded DTensor parameters (FSDP2 / HSDP)."""
+                        lr_adjust="shape", ns_coeffs="jordan", compile_ns=False, exchanges=None) -> None:
+    """Muon for row-sharded DTensor parameters (FSDP2 / HSDP).
+
+    ``exchanges`` (a dict, kept by the optimizer) turns on the fused NVLink
+    path on CUDA: the final Newton-Schulz product of each orthogonalised
+    matrix is written by the GEMM epilogue straight into the row owners'
+    receive buffers on the other GPUs (``parallel.nvlink.MuonExchange``), one
+    epoch barrier follows, and each rank applies the rows it received -- in
+    place of an all-gather of every full result, which moves ``world`` times
+    the bytes.  Buckets the fused path cannot take keep the all-gather."""
     P = [p.to_local() for p in params]
     G = [g.to_local() for g in grads]
     Bf = [b.to_local() for b in momentum_bufs]
@@ -156,8 +180,32 @@ def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_de
     buckets: dict[tuple, list[int]] = {}
     for i, p in enumerate(params):
         buckets.setdefault((tuple(p.shape), p.dtype, p.device, id(p.device_mesh), p.placements), []).append(i)
+    plan = []
     for (shape, dtype, device, _, _), idx in buckets.items():
         group, ws, rank = _shard_layout(params[idx[0]])
+        plan.append((shape, dtype, device, idx, group, ws, rank))
+    # fused-path layout: per group, one receive block per eligible bucket (identical on every rank)
+    fused: dict[int, tuple] = {}
+    if exchanges is not None:
+        from ..parallel.nvlink import MuonExchange
+        sizes: dict[int, int] = {}
+        for j, (shape, dtype, device, idx, group, ws, rank) in enumerate(plan):
+            if not MuonExchange.eligible(shape, ws, device):
+                continue
+            rows, cols = shape
+            chunk = -(-len(idx) // ws)
+            off = sizes.get(id(group), 0)
+            fused[j] = (off, chunk)
+            sizes[id(group)] = off + MuonExchange.block_bytes(chunk * ws, rows // ws, cols)
+        for j, (shape, dtype, device, idx, group, ws, rank) in enumerate(plan):
+            if j in fused and id(group) not in exchanges:
+                exchanges[id(group)] = MuonExchange(group, sizes[id(group)])
+        for j in list(fused):
+            ex = exchanges[id(plan[j][4])]
+            if ex.slot_bytes < sizes[id(plan[j][4])]:
+                del fused[j]            # the buckets grew past the heap: all-gather this step
+    pending = []
+    for j, (shape, dtype, device, idx, group, ws, rank) in enumerate(plan):
         rows, cols = shape
         n = len(idx)
         local = torch.stack([updates[i] for i in idx]).to(torch.bfloat16)
@@ -175,6 +223,13 @@ def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_de
         mine = full[rank * chunk:(rank + 1) * chunk]
         if mine.size(0) < chunk:
             mine = torch.cat([mine, full.new_zeros((chunk - mine.size(0), rows, cols))])
+        if j in fused:
+            ex = exchanges[id(group)]
+            off = fused[j][0]
+            X, coeffs, transposed = _ns_prepare(mine, ns_steps, eps, ns_coeffs)
+            _ns_kernels(X.contiguous(), coeffs, last=ex.scatter_fn(off, rank * chunk, rows_l, cols, transposed))
+            pending.append((ex, off, idx, shape, dtype, rows_l, transposed))
+            continue
         mine = newton_schulz(mine, steps=ns_steps, eps=eps, scheme=ns_coeffs)
         if ws > 1:
             out = torch.empty((chunk * ws, rows, cols), dtype=mine.dtype, device=device)
@@ -184,6 +239,13 @@ def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_de
             O = mine[:n]
         torch._foreach_add_([P[i] for i in idx], list(O.to(dtype).unbind(0)),
                             alpha=-lr * lr_scale(shape, lr_adjust))
+    if pending:
+        for ex in {id(e[0]): e[0] for e in pending}.values():
+            ex.barrier()                 # every peer's products have landed in this rank's buffer
+        for ex, off, idx, shape, dtype, rows_l, transposed in pending:
+            O = ex.received(off, len(idx), rows_l, shape[1], transposed)
+            torch._foreach_add_([P[i] for i in idx], list(O.to(dtype).unbind(0)),
+                                alpha=-lr * lr_scale(shape, lr_adjust))
 
 
 class Muon(Optimizer):
@@ -210,6 +272,9 @@ class Muon(Optimizer):
         # machine-local knobs: deliberately not in defaults / state_dict
         self._compile_ns = bool(compile_ns)
         self._shard = shard
+        # fused NVLink exchange of the sharded path (VAGUS_MUON_NCCL=1 keeps the all-gathers)
+        import os
+        self._exchanges = None if os.environ.get("VAGUS_MUON_NCCL") else {}
         for group in self.param_groups:
             for p in group["params"]:
                 if p.dim() != 2:
@@ -256,7 +321,8 @@ class Muon(Optimizer):
             if plain[0]:
                 muon_update(*plain, **common, world_size=world_size, rank=rank)
             if sharded[0]:
-                muon_update_sharded(*sharded, **common)
+                ex = self._exchanges if sharded[0][0].device.type == "cuda" else None
+                muon_update_sharded(*sharded, **common, exchanges=ex)
         return loss
 
 

@@ -18,9 +18,16 @@ buffer larger than the heap slots) go to NCCL; the decision depends only on
 sizes and the op, which are identical on every rank, so the per-kind epoch
 counters stay in step.
 
+``MuonExchange`` is the fused product + all-to-all of the sharded Muon
+step: the last Newton-Schulz GEMM of each orthogonalised matrix scatters its
+output rows from the epilogue straight into the owning ranks' receive buffers
+(peer stores over NVLink), then one epoch barrier.
+
 Parity: the reference runs these collectives inside FSDP2 on NCCL
 (``infra/train/main.py:253-275``); the gradient reduction semantics (average
-over the data-parallel group, fp32) are the same.
+over the data-parallel group, fp32) are the same.  Its sharded Muon
+(``infra/optimizer/muon.py``) all-gathers the Newton-Schulz results; the
+update each rank applies is the same.
 """
 
 from __future__ import annotations
@@ -147,3 +154,80 @@ def use_nvlink_collectives(root, group=None) -> NvlinkHeap:
             m.set_custom_all_gather(ag)
             m.set_custom_reduce_scatter(rs)
     return heap
+
+
+class MuonExchange:
+    """IPC-shared receive buffers for the sharded Muon step's fused
+    Newton-Schulz product + scatter (a GEMM followed by an all-to-all, as one
+    kernel over NVLink).
+
+    Each rank's heap holds two slots (alternating by epoch) of ``slot_bytes``;
+    a bucket of ``n`` same-shape matrices, row-sharded ``world`` ways, owns a
+    block of ``n_pad x rows_l x cols`` bf16 in every slot (``n_pad`` = the
+    bucket padded to a multiple of ``world``).  The rank that orthogonalises
+    matrix ``g`` writes its rows ``[o rows_l, (o + 1) rows_l)`` into rank
+    ``o``'s block at ``g`` (for a tall matrix, processed transposed, the
+    column block, stored as ``cols x rows_l``).  A slot is rewritten two
+    epochs later, after every peer passed the barrier in between, which it
+    reaches only after applying what it read from the slot."""
+
+    def __init__(self, group, slot_bytes: int):
+        C = native()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.slot_bytes = (int(slot_bytes) + 255) // 256 * 256
+        ptr, handle = C.comm_heap_create(HEADER + 2 * self.slot_bytes)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.own = ptr
+        self.bases = [ptr if r == self.rank else C.comm_heap_open(h) for r, h in enumerate(handles)]
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    @staticmethod
+    def eligible(shape, world: int, device) -> bool:
+        rows, cols = shape
+        if world < 2 or world > 16 or device.type != "cuda" or rows % world or rows % 8 or cols % 8:
+            return False
+        rows_l = rows // world
+        # a tall matrix scatters 32-column chunks of its transposed product
+        return rows <= cols or rows_l % 32 == 0
+
+    @staticmethod
+    def block_bytes(n_pad: int, rows_l: int, cols: int) -> int:
+        return (n_pad * rows_l * cols * 2 + 255) // 256 * 256
+
+    def _slot(self, epoch: int) -> int:
+        return HEADER + (epoch & 1) * self.slot_bytes
+
+    def scatter_fn(self, off: int, batch0: int, rows_l: int, cols: int, transposed: bool):
+        """The final product X' = B X + a X of ``_ns_kernels``, scattered into
+        the next epoch's slot of every rank."""
+        slot = self._slot(self.epoch + 1)
+        dst = [b + slot + off for b in self.bases]
+        if transposed:      # X' is (cols, rows): column blocks of rows_l, stored (cols, rows_l)
+            mode, ld, stride = 2, rows_l, cols * rows_l
+        else:               # X' is (rows, cols): row blocks of rows_l, stored (rows_l, cols)
+            mode, ld, stride = 1, cols, rows_l * cols
+
+        def last(Bm, X, a):
+            rc = native().gemm_scatter(Bm, False, X, True, X, 1.0, a, dst, mode, rows_l, ld, stride, batch0)
+            if rc:
+                raise RuntimeError(f"gemm_scatter rejected the problem (code {rc})")
+        return last
+
+    def barrier(self):
+        self.epoch += 1
+        native().comm_barrier(self.bases, self.rank, self.epoch)
+
+    def received(self, off: int, n: int, rows_l: int, cols: int, transposed: bool) -> torch.Tensor:
+        """This rank's rows of the bucket's n matrices, (n, rows_l, cols) bf16."""
+        t = native().comm_heap_view(self.own, self._slot(self.epoch) + off, n * rows_l * cols, torch.bfloat16)
+        return t.view(n, cols, rows_l).transpose(1, 2) if transposed else t.view(n, rows_l, cols)
+
+    def close(self):
+        C = native()
+        for r, b in enumerate(self.bases):
+            C.comm_heap_close(b, r == self.rank)
+        self.bases = []
