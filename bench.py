@@ -326,6 +326,20 @@ def run(args) -> dict:
     e2e_ms = _max_over_ranks((time.perf_counter() - w0) * 1e3 / args.steps, is_dist)
     clocks = sampler.stop() if rank == 0 else None
 
+    # the optimizer step alone (Muon: momentum, Newton-Schulz, its collectives),
+    # on the gradients of the last step; device time, max over ranks
+    optimizer.step()
+    if is_dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    o0, o1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    o0.record()
+    for _ in range(3):
+        optimizer.step()
+    o1.record()
+    torch.cuda.synchronize()
+    opt_ms = _max_over_ranks(o0.elapsed_time(o1) / 3, is_dist)
+
     tokens_per_step = cfg["global_tokens"]
     value = tokens_per_step / (ms / 1e3)
     e2e = tokens_per_step / (e2e_ms / 1e3)
@@ -346,6 +360,7 @@ def run(args) -> dict:
         "gpu_launches": None if launches is None else launches * args.steps,
         "clocks": clocks, "final_loss": round(final_loss, 4), "warmup_s": round(warm_s, 1),
         "max_mem_gb": round(torch.cuda.max_memory_allocated() / 1e9, 1),
+        "optimizer_step_ms": round(opt_ms, 2),
     }
     if args.impl == "reference":
         out["impl"] = "reference"
