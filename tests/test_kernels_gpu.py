@@ -256,6 +256,32 @@ def test_gdr_chunk_fwd_bwd(dk, dv):
         assert rel(a.grad, b.grad) < 5e-2, (a.shape, rel(a.grad, b.grad))
 
 
+@pytest.mark.parametrize("dk,dv,L", [(128, 256, 200), (128, 128, 256)])
+def test_kda_chunk_fwd_bwd(dk, dv, L):
+    """Per-channel gate (KDA): torch intra stage + recurrence kernels vs the
+    fp32 chunk oracle, outputs, final state and every input gradient."""
+    from vagus_b200 import ops
+    from vagus_b200.models.scans import chunk_scan_vec
+    B, H = 2, 2
+    q, k, v, _, beta = _gdr_inputs(B, L, H, dk, dv)
+    g = F.logsigmoid(torch.randn(B, L, H, dk, device=DEV) + 2) * 0.5
+    S0 = 0.1 * torch.randn(B, H, dk, dv, device=DEV)
+    scale = dk ** -0.5
+    ins = [t.bfloat16().float() for t in (q, k, v)] + [g, beta, S0]
+    ref_in = [t.clone().requires_grad_(True) for t in ins]
+    o_r, S_r = chunk_scan_vec(ref_in[0], ref_in[1], ref_in[2], ref_in[3], ref_in[4], ref_in[5], scale=scale,
+                              delta=True, chunk_size=64)
+    cu_in = [t.clone().requires_grad_(True) for t in ins]
+    o, S = ops.kda_chunk(cu_in[0].bfloat16(), cu_in[1].bfloat16(), cu_in[2].bfloat16(), cu_in[3], cu_in[4],
+                         cu_in[5], scale=scale)
+    assert rel(o, o_r) < 2e-2 and rel(S, S_r) < 2e-2, (rel(o, o_r), rel(S, S_r))
+    do, dS = torch.randn_like(o_r), torch.randn_like(S_r)
+    ((o_r * do).sum() + (S_r * dS).sum()).backward()
+    ((o.float() * do).sum() + (S * dS).sum()).backward()
+    for name, a, b in zip("q k v g beta S0".split(), cu_in, ref_in):
+        assert rel(a.grad, b.grad) < 5e-2, (name, rel(a.grad, b.grad))
+
+
 @pytest.mark.parametrize("dk,dv", [(128, 128), (256, 256), (128, 256)])
 def test_gdr_intra_kernel_matches_torch(dk, dv):
     from vagus_b200.ops import native

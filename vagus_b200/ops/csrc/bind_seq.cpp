@@ -84,6 +84,7 @@ std::vector<Tensor> gdn_gates_bwd(Tensor dg, Tensor dbeta, Tensor ab, Tensor A_l
 std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor U, Tensor gC,
                                 c10::optional<Tensor> S0, bool need_states, int64_t H) {
   (void)need_states;
+  gC = gC.contiguous();
   const int64_t BH = W.size(0);
   TORCH_CHECK(H > 0 && BH % H == 0, "gdr_rec_fwd: heads must divide B*H");
   const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(U.size(3));
@@ -94,17 +95,22 @@ std::vector<Tensor> gdr_rec_fwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
   auto states = torch::empty({BH, N, DV, DK}, W.options());       // S_n^T per chunk (value-major)
   auto S_out = torch::empty({BH, DK, DV}, W.options().dtype(at::kFloat));
   vagus::GdrRecArgs a{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), U.data_ptr(),
-                      gC.contiguous().data_ptr<float>(), fptr(S0), O.data_ptr(), Vp.data_ptr(),
+                      gC.data_ptr<float>(), fptr(S0), O.data_ptr(), Vp.data_ptr(),
                       states.data_ptr(), S_out.data_ptr<float>(), BH, N, DK, DV, static_cast<int>(H),
                       vagus_device_error_ptr()};
+  a.gvec = gC.dim() == 3 ? 1 : 0;
+  TORCH_CHECK(gC.scalar_type() == at::kFloat && gC.size(0) == BH && gC.size(1) == N &&
+                  (gC.dim() == 2 || (gC.dim() == 3 && gC.size(2) == DK)),
+              "gdr_rec_fwd: gC (BH, N) or (BH, N, DK) fp32");
   check(vagus::gdr_rec_fwd(a, stream()), "gdr_rec_fwd");
   return {O, Vp, states, S_out};
 }
 
-// Recurrence backward: returns (dW, dQh, dKt (bf16), dA (fp32), dU (bf16), dgC, dS0)
+// Recurrence backward: returns (dW, dQh, dKt (bf16), dA (fp32), dU (bf16), dgC (gC's shape), dS0)
 // dO: token-major (B, L, H, DV) bf16
 std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor Vp, Tensor gC, Tensor states,
                                 Tensor dO, c10::optional<Tensor> dS_final, bool need_dS0) {
+  gC = gC.contiguous();
   const int64_t BH = W.size(0);
   const int N = static_cast<int>(W.size(1)), DK = static_cast<int>(W.size(3)), DV = static_cast<int>(Vp.size(2));
   TORCH_CHECK(Vp.size(3) == 64 && states.size(2) == DV && states.size(3) == DK, "gdr_rec_bwd: value-major V', states");
@@ -119,18 +125,21 @@ std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
   auto dKt = torch::empty({BH, N, 64, DK}, bf);
   auto dA = torch::empty({BH, N, 64, 64}, f32);
   auto dU = torch::empty({BH, N, 64, DV}, bf);
-  auto dgC = torch::zeros({BH, N}, f32);
+  auto dgC = torch::zeros(gC.sizes(), f32);
   auto dS0 = torch::empty({need_dS0 ? BH : 0, DK, DV}, f32);
   auto dstates = torch::empty({BH, N, DK, DV}, bf);
   vagus::GdrRecBwdArgs a;
   a.f = vagus::GdrRecArgs{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), nullptr,
-                          gC.contiguous().data_ptr<float>(), nullptr, nullptr, Vp.data_ptr(), states.data_ptr(),
+                          gC.data_ptr<float>(), nullptr, nullptr, Vp.data_ptr(), states.data_ptr(),
                           nullptr, BH, N, DK, DV, H};
   a.dO = dO.data_ptr();
   a.dS_final = fptr(dS_final);
   a.dW = dW.data_ptr(); a.dQh = dQh.data_ptr(); a.dKt = dKt.data_ptr(); a.dA = dA.data_ptr<float>();
   a.dU = dU.data_ptr(); a.dgC = dgC.data_ptr<float>(); a.dS0 = need_dS0 ? dS0.data_ptr<float>() : nullptr;
   a.dstates = dstates.data_ptr();
+  a.f.gvec = gC.dim() == 3 ? 1 : 0;
+  TORCH_CHECK(gC.scalar_type() == at::kFloat && (gC.dim() == 2 || (gC.dim() == 3 && gC.size(2) == DK)),
+              "gdr_rec_bwd: gC (BH, N) or (BH, N, DK) fp32");
   check(vagus::gdr_rec_bwd(a, stream()), "gdr_rec_bwd");
   return {dW, dQh, dKt, dA, dU, dgC, dS0};
 }

@@ -28,7 +28,9 @@
 // Layouts (all chunk-major, contiguous):
 //   W, Qh, Kt: (BH, N, C, DK) bf16   A: (BH, N, C, C) bf16   U, V', dU: (BH, N, C, DV) bf16
 //   O, dO: token-major (B, N * C, H, DV) bf16 (BH = B * H), the layout of the model's activations
-//   gC, dgC: (BH, N) fp32   states, dstates: (BH, N, DK, DV) bf16
+//   gC, dgC: (BH, N) fp32, or (BH, N, DK) for a per-channel (KDA) gate, where
+//   gC S scales row k of S by gC[k] and dgC[k] = <S_n row k, dS row k>
+//   states: (BH, N, DV, DK) bf16 (S_n^T)   dstates: (BH, N, DK, DV) bf16
 //   dW, dQh, dKt: (BH, N, C, DK) bf16   dA: (BH, N, C, C) fp32
 #include "common.cuh"
 #include "gemm.h"
@@ -96,7 +98,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 gdr_fwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restrict__ Kt,
              const __nv_bfloat16* __restrict__ U, const float* __restrict__ gC, const float* __restrict__ S0,
              __nv_bfloat16* __restrict__ Vp, __nv_bfloat16* __restrict__ states, float* __restrict__ S_out, int N,
-             int DV) {
+             int DV, int gvec) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   FwdScanSmem<DK>& sm = *reinterpret_cast<FwdScanSmem<DK>*>(smem_raw);
   constexpr int SMT = DK / 8 / 16;          // state rows per warp / 16
@@ -163,14 +165,15 @@ gdr_fwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
     __syncthreads();
     store_tile_t(Vp + (cidx * DV + v0) * C, C, &sm.V[0][0], DVT + PAD, C, DVT);
 
-    // S <- gC S + Kt^T V'
-    const float g = gC[cidx];
+    // S <- gC S + Kt^T V'  (row k scaled by gC[k] for a per-channel gate)
+    const float g = gvec ? 0.f : gC[cidx];
 #pragma unroll
     for (int mt = 0; mt < SMT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) S[mt][nt][e] *= g;
+        for (int e = 0; e < 4; ++e)
+          S[mt][nt][e] *= gvec ? gC[cidx * DK + srow0 + frag_row(mt, e)] : g;
     warp_mma<SMT, 8, true, true>(S, &sm.K[b][0][0], DK + PAD, &sm.V[0][0], DVT + PAD, srow0, 0, C);
     __syncthreads();   // every warp is done with this chunk's tiles
   }
@@ -224,7 +227,7 @@ __global__ void __launch_bounds__(320, 1)
 gdr_fwd_scan_tc(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mk,
                 const __grid_constant__ CUtensorMap ms, const __grid_constant__ CUtensorMap mv,
                 const __nv_bfloat16* __restrict__ U, const float* __restrict__ gC, const float* __restrict__ S0,
-                float* __restrict__ S_out, int N, int DV, int* err) {
+                float* __restrict__ S_out, int N, int DV, int gvec, int* err) {
   using namespace tscan;
   using Lt = Layout<DK>;
   extern __shared__ __align__(128) uint8_t smem_raw[];   // re-aligned to 1024 (the swizzle atom) below
@@ -373,15 +376,18 @@ gdr_fwd_scan_tc(const __grid_constant__ CUtensorMap mw, const __grid_constant__ 
       __syncwarp();
       if (lane == 0) mbar_arrive(s_ready);
     };
-    // S^T *= g in TMEM (overlaps the next D1, which reads only the bf16 copy)
-    auto scale_state = [&](float g) {
+    // S^T *= gC of chunk `ci` in TMEM (overlaps the next D1, which reads only the
+    // bf16 copy); a per-channel gate scales column k by gC[ci][k]
+    auto scale_state = [&](long long ci) {
+      const float g = gvec ? 0.f : gC[ci];
+      const float* gv = gC + ci * DK;
 #pragma unroll 1
       for (int j = b0; j < b0 + NB; ++j) {
         uint32_t r0[32];
         tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j), r0);
         tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) r0[e] = __float_as_uint(__uint_as_float(r0[e]) * g);
+        for (int e = 0; e < 32; ++e) r0[e] = __float_as_uint(__uint_as_float(r0[e]) * (gvec ? gv[32 * j + e] : g));
         tmem_st_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * j), r0);
       }
       tmem_st_wait();
@@ -398,10 +404,9 @@ gdr_fwd_scan_tc(const __grid_constant__ CUtensorMap mw, const __grid_constant__ 
     tmem_st_wait();
     load_u(0);
     copy_state();
-    if (N > 0) scale_state(gC[bh * N]);
+    if (N > 0) scale_state(bh * N);
     for (int n = 0; n < N; ++n) {
       const long long cidx = bh * N + n;
-      const float g_next = n + 1 < N ? gC[cidx + 1] : 1.f;
       cp_wait_all();
       asm volatile("bar.sync 1, 256;" ::: "memory");     // U_n complete for all eight warps
       uint32_t uu[16];                                   // U_n[32 half + c][v] as bf16 pairs
@@ -438,7 +443,7 @@ gdr_fwd_scan_tc(const __grid_constant__ CUtensorMap mw, const __grid_constant__ 
       tc_fence_after();
       if (n + 1 < N) {
         copy_state();
-        scale_state(g_next);
+        scale_state(cidx + 1);
       }
     }
     if (S_out) {
@@ -526,7 +531,7 @@ gdr_bwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
              const __nv_bfloat16* __restrict__ Kt, const __nv_bfloat16* __restrict__ A,
              const float* __restrict__ gC, const __nv_bfloat16* __restrict__ dO, const float* __restrict__ dS_final,
              __nv_bfloat16* __restrict__ dU, __nv_bfloat16* __restrict__ dstates, float* __restrict__ dS0, int N,
-             int DV, int H) {
+             int DV, int H, int gvec) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   BwdScanSmem<DK>& sm = *reinterpret_cast<BwdScanSmem<DK>*>(smem_raw);
   constexpr int SMT = DK / 8 / 16;
@@ -604,14 +609,15 @@ gdr_bwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
     cp_wait_1();                              // G2(n) done
     __syncthreads();
 
-    // dS <- gC dS + Qh^T dO - W^T dV'
-    const float g = gC[cidx];
+    // dS <- gC dS + Qh^T dO - W^T dV'  (row k scaled by gC[k] for a per-channel gate)
+    const float g = gvec ? 0.f : gC[cidx];
 #pragma unroll
     for (int mt = 0; mt < SMT; ++mt)
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) dS[mt][nt][e] *= g;
+        for (int e = 0; e < 4; ++e)
+          dS[mt][nt][e] *= gvec ? gC[cidx * DK + srow0 + frag_row(mt, e)] : g;
     warp_mma<SMT, 8, true, true>(dS, &sm.Q[0][0], DK + PAD, &sm.dO[b][0][0], DVT + PAD, srow0, 0, C);
     warp_mma<SMT, 8, true, true>(dS, &sm.W[0][0], DK + PAD, &sm.dVn[0][0], DVT + PAD, srow0, 0, C);
     __syncthreads();
@@ -644,6 +650,7 @@ struct ParSmem {
   __nv_bfloat16 ST[2][DVT][64 + PAD];    // S_n^T columns k0..k0+63
   __nv_bfloat16 dS[2][64][DVT + PAD];
   float red[THREADS / 32];
+  float rowdot[THREADS];                 // per-channel gate: per-row partial sums
 };
 
 __global__ void __launch_bounds__(THREADS, 2)
@@ -651,7 +658,7 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
               const __nv_bfloat16* __restrict__ Vp, const __nv_bfloat16* __restrict__ states,
               const __nv_bfloat16* __restrict__ dstates, __nv_bfloat16* __restrict__ dW,
               __nv_bfloat16* __restrict__ dQh, __nv_bfloat16* __restrict__ dKt, float* __restrict__ dA,
-              float* __restrict__ dgC, int DK, int DV, int N, int H) {
+              float* __restrict__ dgC, int DK, int DV, int N, int H, int gvec) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   ParSmem& sm = *reinterpret_cast<ParSmem*>(smem_raw);
   const long long cidx = blockIdx.x;
@@ -685,11 +692,22 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
     warp_mma<1, 4, false, true>(aq, &sm.dO[b][0][0], DVT + PAD, &sm.ST[b][0][0], 64 + PAD, wm0, wn0, DVT);
     warp_mma<1, 4, true, false>(ak, &sm.VT[b][0][0], C + PAD, &sm.dS[b][0][0], DVT + PAD, wm0, wn0, DVT);
     if (do_dA) warp_mma<1, 4, false, true>(aa, &sm.dO[b][0][0], DVT + PAD, &sm.VT[b][0][0], C + PAD, wm0, wn0, DVT);
+    // THREADS is a multiple of 64: every pass of a thread is on key row threadIdx.x % 64
     for (int i = threadIdx.x; i < 64 * DVT; i += THREADS) {
-      const int r = i / DVT, c = i % DVT;           // key r, value c
+      const int r = i % 64, c = i / 64;             // key r, value c
       dot += bf2f(sm.ST[b][c][r]) * bf2f(sm.dS[b][r][c]);
     }
     __syncthreads();
+  }
+  if (gvec) {
+    // dgC[k0 + r]: the THREADS / 64 partial sums of row r
+    sm.rowdot[threadIdx.x] = dot;
+    __syncthreads();
+    if (threadIdx.x < 64) {
+      float t = 0.f;
+      for (int i = threadIdx.x; i < THREADS; i += 64) t += sm.rowdot[i];
+      atomicAdd(&dgC[cidx * DK + k0 + threadIdx.x], t);
+    }
   }
   dot = warp_sum(dot);
   if (lane == 0) sm.red[warp] = dot;
@@ -706,7 +724,7 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
         *reinterpret_cast<float2*>(dA + (cidx * C + r) * C + c) = make_float2(aa[0][nt][e], aa[0][nt][e + 1]);
     }
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && !gvec) {
     float t = 0.f;
     for (int i = 0; i < THREADS / 32; ++i) t += sm.red[i];
     atomicAdd(&dgC[cidx], t);
@@ -776,12 +794,12 @@ int launch_fwd(const GdrRecArgs& a, cudaStream_t st) {
     gdr_fwd_scan_tc<DK><<<static_cast<unsigned>(a.BH * (a.DV / tscan::VT)), 320, Lt::SMEM, st>>>(
         *reinterpret_cast<const CUtensorMap*>(mw), *reinterpret_cast<const CUtensorMap*>(mk),
         *reinterpret_cast<const CUtensorMap*>(ms), *reinterpret_cast<const CUtensorMap*>(mv),
-        (const __nv_bfloat16*)a.U, a.gC, a.S0, a.S_out, a.N, a.DV, a.err);
+        (const __nv_bfloat16*)a.U, a.gC, a.S0, a.S_out, a.N, a.DV, a.gvec, a.err);
   } else {
     const int grid = static_cast<int>(a.BH * (a.DV / DVT));
     gdr_fwd_scan<DK><<<grid, THREADS, s1, st>>>((const __nv_bfloat16*)a.W, (const __nv_bfloat16*)a.Kt,
                                                 (const __nv_bfloat16*)a.U, a.gC, a.S0, (__nv_bfloat16*)a.Vp,
-                                                (__nv_bfloat16*)a.states, a.S_out, a.N, a.DV);
+                                                (__nv_bfloat16*)a.states, a.S_out, a.N, a.DV, a.gvec);
   }
   dim3 g2(static_cast<unsigned>(a.BH * a.N), a.DV / DVT);
   gdr_fwd_out<DK><<<g2, THREADS, s2, st>>>((const __nv_bfloat16*)a.Qh, (const __nv_bfloat16*)a.A,
@@ -798,13 +816,13 @@ int launch_bwd(const GdrRecBwdArgs& a, cudaStream_t st) {
   gdr_bwd_scan<DK><<<grid, THREADS, s1, st>>>((const __nv_bfloat16*)a.f.W, (const __nv_bfloat16*)a.f.Qh,
                                               (const __nv_bfloat16*)a.f.Kt, (const __nv_bfloat16*)a.f.A, a.f.gC,
                                               (const __nv_bfloat16*)a.dO, a.dS_final, (__nv_bfloat16*)a.dU,
-                                              (__nv_bfloat16*)a.dstates, a.dS0, a.f.N, a.f.DV, a.f.H);
+                                              (__nv_bfloat16*)a.dstates, a.dS0, a.f.N, a.f.DV, a.f.H, a.f.gvec);
   dim3 g2(static_cast<unsigned>(a.f.BH * a.f.N), DK / 64);
   gdr_bwd_chunk<<<g2, THREADS, s2, st>>>((const __nv_bfloat16*)a.dU, (const __nv_bfloat16*)a.dO,
                                          (const __nv_bfloat16*)a.f.Vp, (const __nv_bfloat16*)a.f.states,
                                          (const __nv_bfloat16*)a.dstates, (__nv_bfloat16*)a.dW,
                                          (__nv_bfloat16*)a.dQh, (__nv_bfloat16*)a.dKt, a.dA, a.dgC, DK, a.f.DV,
-                                         a.f.N, a.f.H);
+                                         a.f.N, a.f.H, a.f.gvec);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

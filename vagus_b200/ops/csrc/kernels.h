@@ -59,15 +59,16 @@ struct GdrRecArgs {
   const void* W; const void* Qh; const void* Kt;   // (BH, N, C, DK) bf16
   const void* A;                                   // (BH, N, C, C) bf16
   const void* U;                                   // (BH, N, C, DV) bf16
-  const float* gC;                                 // (BH, N)
+  const float* gC;                                 // (BH, N), or (BH, N, DK) when gvec
   const float* S0;                                 // (BH, DK, DV) or null
   void* O;                                         // (B, N*C, H, DV) bf16, token-major
-  void* Vp;                                        // (BH, N, C, DV) bf16: V' (written fwd, read bwd)
-  void* states;                                    // (BH, N, DK, DV) bf16 entry states (written fwd, read bwd)
+  void* Vp;                                        // (BH, N, DV, C) bf16: V'^T (written fwd, read bwd)
+  void* states;                                    // (BH, N, DV, DK) bf16 entry states S_n^T (written fwd, read bwd)
   float* S_out;                                    // (BH, DK, DV) or null
   long long BH; int N, DK, DV;
   int H;                                           // heads (BH = B * H)
   int* err = nullptr;                              // device error word (the tcgen05 scan's bounded waits)
+  int gvec = 0;                                    // 1: per-channel (KDA) chunk decay gC[k]
 };
 int gdr_rec_fwd(const GdrRecArgs& a, cudaStream_t st);
 struct GdrRecBwdArgs {

@@ -1,0 +1,126 @@
+"""Chunked delta rule with a per-channel (Kimi-delta, KDA) gate on CUDA.
+
+The intra-chunk stage runs in torch, chunk-parallel over the whole sequence
+(fp32); the sequential state recurrence runs on the GDR recurrence kernels
+(``csrc/gdr.cu``: tcgen05 forward scan, chunk-parallel output and gradient
+kernels), whose chunk decay gC becomes a per-key-channel vector.
+
+Per chunk of C = 64 tokens with in-chunk cumulative log decay g_i (a dk
+vector, non-increasing in i), gated inner products
+<x_i, y_j>_g = sum_c x_ic y_jc exp(g_ic - g_jc) (i >= j) give
+    M = tril(diag(beta) <K, K>_g, -1),  T = (I + M)^-1
+    W = T diag(beta) (K o e^g),  U = T diag(beta) V
+    Qh = scale Q o e^g,  Kt = K o e^(g_last - g),  A = scale tril(<Q, K>_g)
+    gamma = e^(g_last)
+and the recurrence V' = U - W S, O = Qh S + A V', S <- diag(gamma) S + Kt^T V'.
+The gated products are formed on 16-row sub-chunks: across sub-chunks the
+decay factorises through the sub-chunk boundaries with every exponent <= 0
+(no overflow for fast channels), inside a sub-chunk the 16 x 16 x dk decay
+is taken elementwise.
+
+Parity: the reference runs fla's ``chunk_kda`` Triton kernels
+(``infra/components/linear_attention.py``); the math is the chunk form of
+its recurrence (``models/scans.py`` ``chunk_scan_vec`` is the oracle).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._core import native
+
+CHUNK = 64
+SUB = 16
+
+
+def _gated(X: torch.Tensor, Y: torch.Tensor, g: torch.Tensor, strict: bool) -> torch.Tensor:
+    """sum_c X_ic Y_jc exp(g_ic - g_jc) for j <= i (j < i when strict), zero
+    above; X, Y, g (..., C, dk) fp32 -> (..., C, C)."""
+    *lead, C, dk = X.shape
+    nb = C // SUB
+    Xb, Yb, gb = (t.reshape(*lead, nb, SUB, dk) for t in (X, Y, g))
+    first = gb[..., :, :1, :]                                   # (..., nb, 1, dk): g at each sub-chunk start
+    # across sub-chunks (block I > J): exp(g_i - g_j) = exp(g_i - f_I) exp(f_I - f_{J+1}) exp(f_{J+1} - g_j)
+    Xs = Xb * (gb - first).exp()                                # rows scaled to their sub-chunk start
+    nxt = torch.cat([first[..., 1:, :, :], gb[..., -1:, -1:, :]], dim=-3)   # f_{J+1} (last block: unused)
+    Ys = Yb * (nxt - gb).exp()                                  # columns scaled to the next sub-chunk start
+    f = first.squeeze(-2)                                       # (..., nb, dk)
+    fn = nxt.squeeze(-2)
+    Dm = (f[..., :, None, :] - fn[..., None, :, :])             # (..., I, J, dk): f_I - f_{J+1}
+    low = torch.ones(nb, nb, dtype=torch.bool, device=X.device).tril(-1)
+    Dm = Dm.masked_fill(~low[..., None], float("-inf")).exp()   # zero unless J < I
+    out = torch.einsum("...isc,...ijc,...jtc->...isjt", Xs, Dm, Ys)          # (..., I, 16, J, 16)
+    # inside a sub-chunk: the decay elementwise
+    E = gb[..., :, :, None, :] - gb[..., :, None, :, :]          # (..., nb, 16, 16, dk)
+    tri = torch.ones(SUB, SUB, dtype=torch.bool, device=X.device).tril(-1 if strict else 0)
+    E = E.masked_fill(~tri[..., None], float("-inf")).exp()
+    diag = torch.einsum("...bic,...bijc,...bjc->...bij", Xb, E, Yb)           # (..., nb, 16, 16)
+    eye = torch.eye(nb, dtype=X.dtype, device=X.device)
+    out = out + diag[..., :, :, None, :] * eye[:, None, :, None]
+    return out.reshape(*lead, C, C)
+
+
+def kda_intra(q, k, v, g, beta, scale: float):
+    """(W, Qh, Kt, A, U, gamma) of every chunk, fp32, (B, H, N, C, .) layout;
+    q, k (B, L, H, dk), v (B, L, H, dv), g (B, L, H, dk) log decay, beta (B, L, H)."""
+    B, L, H, dk = q.shape
+    dv = v.shape[-1]
+    N = L // CHUNK
+    to_c = lambda t, d: t.float().reshape(B, N, CHUNK, H, d).permute(0, 3, 1, 2, 4)   # noqa: E731
+    Q, K, V = to_c(q, dk), to_c(k, dk), to_c(v, dv)
+    gam = to_c(g, dk).cumsum(3)                                  # (B, H, N, C, dk)
+    b = beta.float().reshape(B, N, CHUNK, H).permute(0, 3, 1, 2)[..., None]   # (B, H, N, C, 1)
+    Akk = _gated(K, K, gam, strict=True) * b
+    Tm = Akk + torch.eye(CHUNK, device=q.device, dtype=Akk.dtype)
+    G = gam.exp()
+    W = torch.linalg.solve_triangular(Tm, b * K * G, upper=False, unitriangular=True)
+    U = torch.linalg.solve_triangular(Tm, b * V, upper=False, unitriangular=True)
+    Qh = Q * G * scale
+    Kt = K * (gam[..., -1:, :] - gam).exp()
+    A = _gated(Q, K, gam, strict=False) * scale
+    return W, Qh, Kt, A, U, G[..., -1, :]
+
+
+class _KDARec(torch.autograd.Function):
+    """The state recurrence on the GDR kernels (per-channel decay)."""
+
+    @staticmethod
+    def forward(ctx, W, Qh, Kt, A, U, gam, S0, H: int):
+        B, Hh, N, C, dk = W.shape
+        dv = U.shape[-1]
+        f16 = lambda t: t.to(torch.bfloat16).reshape(B * Hh, *t.shape[2:]).contiguous()   # noqa: E731
+        W16, Qh16, Kt16, A16, U16 = (f16(t) for t in (W, Qh, Kt, A, U))
+        gf = gam.float().reshape(B * Hh, N, dk).contiguous()
+        S0f = None if S0 is None else S0.float().reshape(B * Hh, dk, dv).contiguous()
+        o, Vp, states, S_out = native().gdr_rec_fwd(W16, Qh16, Kt16, A16, U16, gf, S0f, True, H)
+        ctx.save_for_backward(W16, Qh16, Kt16, A16, Vp, gf, states)
+        ctx.shape = (B, Hh, N, C, dk, dv)
+        ctx.has_S0 = S0 is not None
+        return o, S_out.view(B, Hh, dk, dv)
+
+    @staticmethod
+    def backward(ctx, do, dS):
+        W16, Qh16, Kt16, A16, Vp, gf, states = ctx.saved_tensors
+        B, Hh, N, C, dk, dv = ctx.shape
+        dO = do.to(torch.bfloat16).contiguous()
+        dSf = None if dS is None else dS.float().reshape(B * Hh, dk, dv).contiguous()
+        dW, dQh, dKt, dA, dU, dg, dS0 = native().gdr_rec_bwd(W16, Qh16, Kt16, A16, Vp, gf, states, dO, dSf,
+                                                             ctx.has_S0)
+        un = lambda t: t.float().view(B, Hh, N, *t.shape[2:])   # noqa: E731
+        return (un(dW), un(dQh), un(dKt), un(dA), un(dU), dg.view(B, Hh, N, dk),
+                dS0.view(B, Hh, dk, dv) if ctx.has_S0 else None, None)
+
+
+def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64):
+    """Chunked delta rule with a per-channel gate g (B, L, H, dk) (log decay)
+    on CUDA.  Returns (o (B, L, H, dv) bf16, S (B, H, dk, dv) fp32)."""
+    assert chunk_size == CHUNK, "the sm_100a recurrence runs 64-token chunks"
+    B, L, H, dk = q.shape
+    pad = (-L) % CHUNK
+    if pad:
+        # zero gate and zero write strength: padded tokens leave the state alone
+        pz = lambda t: torch.nn.functional.pad(t, [0, 0] * (t.dim() - 2) + [0, pad])   # noqa: E731
+        q, k, v, g, beta = pz(q), pz(k), pz(v), pz(g), pz(beta)
+    parts = kda_intra(q, k, v, g, beta, scale)
+    o, S = _KDARec.apply(*parts, S0, H)
+    return (o[:, :L] if pad else o), S
