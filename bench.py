@@ -57,6 +57,14 @@ CONFIGS = {
                         chunk_size=64, layer_pattern="gdn,gdn,gdn,softmax", softmax_head_dim=128,
                         context_len=4096, la_impl="auto"),
         seq=4096, global_tokens=1048576, micro=4, label="1.3B hybrid GDN/softmax 3:1"),
+    # BASELINE config #4 (recipe/model/kda_hybrid_340M.yaml)
+    "kda_hybrid340m": dict(
+        model_name="GDNLM",
+        model_args=dict(vocab_size=32000, dim=1024, layer_count=24, head_count=4, key_head_dim=128,
+                        value_head_dim=256, ffn_hidden_dim=2816, short_conv_size=4, gate="vector", gate_rank=64,
+                        delta=True, chunk_size=64, layer_pattern="gdn,gdn,gdn,softmax", softmax_head_dim=64,
+                        softmax_rope=True, context_len=4096, la_impl="auto"),
+        seq=4096, global_tokens=524288, micro=4, label="340M hybrid KDA/softmax 3:1"),
     # BASELINE config #2
     "tpp340m": dict(
         model_name="TransformerPP",

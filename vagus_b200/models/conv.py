@@ -39,7 +39,9 @@ class ShortConv(nn.Module):
     def forward(self, x: torch.Tensor, activation: str | None = None) -> torch.Tensor:
         """(B, L, D) -> (B, L, D), causal."""
         if self.impl == "conv1d":
-            y = self.conv(F.pad(x.transpose(1, 2), (self.kernel - 1, 0))).transpose(1, 2)
+            # the weight in the activations' dtype (bf16 activations over fp32 master weights)
+            y = F.conv1d(F.pad(x.transpose(1, 2), (self.kernel - 1, 0)), self.conv.weight.to(x.dtype),
+                         groups=self.conv.groups).transpose(1, 2)
         else:
             y = self.shifted(x)
         return _act(y, activation)

@@ -202,9 +202,42 @@ Tensor gdr_decode(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor S,
   return o;
 }
 
+// Gated inner products of the per-channel-gate chunk form (kda.cu).
+// Q, K, G: (..., 64, dk) fp32 contiguous -> (Aqk, Akk) (..., 64, 64) fp32.
+std::vector<Tensor> kda_gated_fwd(Tensor Q, Tensor K, Tensor G) {
+  for (auto* t : {&Q, &K, &G})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->sizes() == Q.sizes(),
+                "kda_gated_fwd: Q, K, G (..., 64, dk) fp32 contiguous");
+  TORCH_CHECK(Q.dim() >= 2 && Q.size(-2) == 64, "kda_gated_fwd: 64-token chunks");
+  const int dk = static_cast<int>(Q.size(-1));
+  const long long chunks = Q.numel() / (64LL * dk);
+  auto shape = Q.sizes().vec();
+  shape.back() = 64;
+  auto Aqk = torch::empty(shape, Q.options()), Akk = torch::empty(shape, Q.options());
+  check(vagus::kda_gated_fwd(Q.data_ptr<float>(), K.data_ptr<float>(), G.data_ptr<float>(), Aqk.data_ptr<float>(),
+                             Akk.data_ptr<float>(), chunks, dk, stream()), "kda_gated_fwd");
+  return {Aqk, Akk};
+}
+
+// -> (dQ, dK, dG) (..., 64, dk) fp32
+std::vector<Tensor> kda_gated_bwd(Tensor Q, Tensor K, Tensor G, Tensor dAqk, Tensor dAkk) {
+  dAqk = dAqk.contiguous().to(at::kFloat);
+  dAkk = dAkk.contiguous().to(at::kFloat);
+  const int dk = static_cast<int>(Q.size(-1));
+  const long long chunks = Q.numel() / (64LL * dk);
+  TORCH_CHECK(dAqk.numel() == chunks * 64 * 64 && dAkk.numel() == chunks * 64 * 64, "kda_gated_bwd: dA shapes");
+  auto dQ = torch::empty_like(Q), dK = torch::empty_like(K), dG = torch::empty_like(G);
+  check(vagus::kda_gated_bwd(Q.data_ptr<float>(), K.data_ptr<float>(), G.data_ptr<float>(), dAqk.data_ptr<float>(),
+                             dAkk.data_ptr<float>(), dQ.data_ptr<float>(), dK.data_ptr<float>(), dG.data_ptr<float>(),
+                             chunks, dk, stream()), "kda_gated_bwd");
+  return {dQ, dK, dG};
+}
+
 }  // namespace
 
 void register_seq_ops(pybind11::module& m) {
+  m.def("kda_gated_fwd", &kda_gated_fwd);
+  m.def("kda_gated_bwd", &kda_gated_bwd);
   m.def("conv_silu_fwd", &conv_silu_fwd);
   m.def("conv_silu_bwd", &conv_silu_bwd);
   m.def("gdn_gates_fwd", &gdn_gates_fwd);

@@ -131,6 +131,13 @@ int attn_bwd(const AttnBwdArgs& a, cudaStream_t st);
 // (device memory, 512 u64); null switches it off.
 void attn_set_trace(unsigned long long* buf);
 
+// kda.cu: the gated inner products of the per-channel-gate chunk form.
+// Q, K, G (chunks, 64, dk) fp32; Aqk (j <= i), Akk (j < i): (chunks, 64, 64) fp32.
+int kda_gated_fwd(const float* Q, const float* K, const float* G, float* Aqk, float* Akk, long long chunks, int dk,
+                  cudaStream_t st);
+int kda_gated_bwd(const float* Q, const float* K, const float* G, const float* dAqk, const float* dAkk, float* dQ,
+                  float* dK, float* dG, long long chunks, int dk, cudaStream_t st);
+
 // comm.cu: NVLink peer-to-peer all-gather / reduce-scatter over CUDA-IPC
 // shared heaps (see comm.cu for the heap layout and the epoch protocol).
 constexpr int kMaxCommPeers = 16;

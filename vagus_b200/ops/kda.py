@@ -13,7 +13,9 @@ vector, non-increasing in i), gated inner products
     Qh = scale Q o e^g,  Kt = K o e^(g_last - g),  A = scale tril(<Q, K>_g)
     gamma = e^(g_last)
 and the recurrence V' = U - W S, O = Qh S + A V', S <- diag(gamma) S + Kt^T V'.
-The gated products are formed on 16-row sub-chunks: across sub-chunks the
+On CUDA the gated products come from ``csrc/kda.cu`` (the pairwise decay
+elementwise, one exponential per (i, j, channel) shared by both products);
+the torch fallback forms them on 16-row sub-chunks: across sub-chunks the
 decay factorises through the sub-chunk boundaries with every exponent <= 0
 (no overflow for fast channels), inside a sub-chunk the 16 x 16 x dk decay
 is taken elementwise.
@@ -60,6 +62,25 @@ def _gated(X: torch.Tensor, Y: torch.Tensor, g: torch.Tensor, strict: bool) -> t
     return out.reshape(*lead, C, C)
 
 
+class _GatedProducts(torch.autograd.Function):
+    """(Aqk causal, Akk strict) of every chunk on the CUDA kernels (kda.cu)."""
+
+    @staticmethod
+    def forward(ctx, Q, K, gam):
+        Q, K, gam = Q.contiguous(), K.contiguous(), gam.contiguous()
+        Aqk, Akk = native().kda_gated_fwd(Q, K, gam)
+        ctx.save_for_backward(Q, K, gam)
+        return Aqk, Akk
+
+    @staticmethod
+    def backward(ctx, dAqk, dAkk):
+        Q, K, gam = ctx.saved_tensors
+        zeros = lambda: torch.zeros(*Q.shape[:-1], Q.shape[-2], device=Q.device)   # noqa: E731
+        dQ, dK, dG = native().kda_gated_bwd(Q, K, gam, dAqk if dAqk is not None else zeros(),
+                                            dAkk if dAkk is not None else zeros())
+        return dQ, dK, dG
+
+
 def kda_intra(q, k, v, g, beta, scale: float):
     """(W, Qh, Kt, A, U, gamma) of every chunk, fp32, (B, H, N, C, .) layout;
     q, k (B, L, H, dk), v (B, L, H, dv), g (B, L, H, dk) log decay, beta (B, L, H)."""
@@ -70,14 +91,18 @@ def kda_intra(q, k, v, g, beta, scale: float):
     Q, K, V = to_c(q, dk), to_c(k, dk), to_c(v, dv)
     gam = to_c(g, dk).cumsum(3)                                  # (B, H, N, C, dk)
     b = beta.float().reshape(B, N, CHUNK, H).permute(0, 3, 1, 2)[..., None]   # (B, H, N, C, 1)
-    Akk = _gated(K, K, gam, strict=True) * b
+    if q.is_cuda:
+        Aqk, Akk = _GatedProducts.apply(Q, K, gam)
+    else:
+        Aqk, Akk = _gated(Q, K, gam, strict=False), _gated(K, K, gam, strict=True)
+    Akk = Akk * b
     Tm = Akk + torch.eye(CHUNK, device=q.device, dtype=Akk.dtype)
     G = gam.exp()
     W = torch.linalg.solve_triangular(Tm, b * K * G, upper=False, unitriangular=True)
     U = torch.linalg.solve_triangular(Tm, b * V, upper=False, unitriangular=True)
     Qh = Q * G * scale
     Kt = K * (gam[..., -1:, :] - gam).exp()
-    A = _gated(Q, K, gam, strict=False) * scale
+    A = Aqk * scale
     return W, Qh, Kt, A, U, G[..., -1, :]
 
 
