@@ -64,7 +64,7 @@ CONFIGS = {
                         value_head_dim=256, ffn_hidden_dim=2816, short_conv_size=4, gate="vector", gate_rank=64,
                         delta=True, chunk_size=64, layer_pattern="gdn,gdn,gdn,softmax", softmax_head_dim=64,
                         softmax_rope=True, context_len=4096, la_impl="auto"),
-        seq=4096, global_tokens=524288, micro=4, label="340M hybrid KDA/softmax 3:1"),
+        seq=4096, global_tokens=524288, micro=8, label="340M hybrid KDA/softmax 3:1"),
     # BASELINE config #2
     "tpp340m": dict(
         model_name="TransformerPP",

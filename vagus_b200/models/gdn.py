@@ -170,6 +170,11 @@ class GatedDeltaNet(nn.Module, Mixer):
     def _heads(self, qp, kp, vp, *, conv: bool = True):
         B, L = qp.shape[0], qp.shape[1]
         H, dk, dv = self.head_count, self.key_head_dim, self.value_head_dim
+        if conv and self.short_conv_size is not None and self._use_kernels(qp):
+            # conv + SiLU (+ L2 norm of q, k) on the conv kernels
+            q = ops.conv_silu(qp, self.conv_q.conv.weight, dk, True).view(B, L, H, dk)
+            k = ops.conv_silu(kp, self.conv_k.conv.weight, dk, True).view(B, L, H, dk)
+            return q, k, ops.conv_silu(vp, self.conv_v.conv.weight, dv, False).view(B, L, H, dv)
         if conv and self.short_conv_size is not None:
             qp, kp, vp = self.conv_q(qp, "silu"), self.conv_k(kp, "silu"), self.conv_v(vp, "silu")
         else:

@@ -10,7 +10,7 @@ falling back to eager PyTorch.
 from ._core import BF16, check_error, kernels_active, native  # noqa: F401
 from .attention import attention, attention_ref  # noqa: F401
 from .ce import fused_linear_ce  # noqa: F401
-from .gdn import gdn_mixer, gdr_chunk, gdr_decode  # noqa: F401
+from .gdn import conv_silu, gdn_mixer, gdr_chunk, gdr_decode  # noqa: F401
 from .kda import kda_chunk  # noqa: F401
 from .linear import linear, linear_residual  # noqa: F401
 from .pointwise import (embedding, qk_norm_rope, rmsnorm, rmsnorm_gated, rmsnorm_pass, sigmoid_gate,  # noqa: F401

@@ -129,6 +129,37 @@ def gdr_decode(q, k, v, g, beta, S, *, scale: float):
     return o.view(B, 1, H, dv).to(q.dtype), S2
 
 
+# ------------------------------------------------- short conv as an op --
+
+class _ConvSilu(torch.autograd.Function):
+    """Causal depthwise conv + SiLU (+ per-head L2 norm) on the conv kernels,
+    for layers outside the fused mixer (the per-channel-gate path)."""
+
+    @staticmethod
+    def forward(ctx, x, w, head_dim: int, l2norm: bool):
+        x = x.to(torch.bfloat16).contiguous()
+        wf = w.float().contiguous()
+        y, rn = native().conv_silu_fwd(x, wf, head_dim, l2norm)
+        ctx.save_for_backward(x, wf, rn)
+        ctx.cfg = (head_dim, l2norm, w.dtype)
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        x, wf, rn = ctx.saved_tensors
+        head_dim, l2norm, wdt = ctx.cfg
+        dx = torch.empty_like(x)
+        dw = torch.zeros(wf.numel(), device=x.device, dtype=torch.float32)
+        native().conv_silu_bwd(dy.to(torch.bfloat16).contiguous(), x, wf, rn, dx, dw, head_dim, l2norm)
+        return dx, dw.view(wf.shape).to(wdt), None, None
+
+
+def conv_silu(x, w, head_dim: int, l2norm: bool):
+    """x (B, L, D) -> SiLU(causal depthwise conv(x, w)) (B, L, D) bf16, each
+    head_dim group L2-normalised when ``l2norm``; w (D, 1, K)."""
+    return _ConvSilu.apply(x, w, head_dim, l2norm)
+
+
 # ------------------------------------------------------------- fused layer --
 
 def _packed_weight(m):

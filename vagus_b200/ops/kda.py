@@ -98,8 +98,9 @@ def kda_intra(q, k, v, g, beta, scale: float):
     Akk = Akk * b
     Tm = Akk + torch.eye(CHUNK, device=q.device, dtype=Akk.dtype)
     G = gam.exp()
-    W = torch.linalg.solve_triangular(Tm, b * K * G, upper=False, unitriangular=True)
-    U = torch.linalg.solve_triangular(Tm, b * V, upper=False, unitriangular=True)
+    # one triangular solve for both right-hand sides (W | U)
+    WU = torch.linalg.solve_triangular(Tm, torch.cat([b * K * G, b * V], dim=-1), upper=False, unitriangular=True)
+    W, U = WU[..., :dk], WU[..., dk:]
     Qh = Q * G * scale
     Kt = K * (gam[..., -1:, :] - gam).exp()
     A = Aqk * scale
