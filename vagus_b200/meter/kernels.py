@@ -11,7 +11,8 @@ shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
 gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
-sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no case names every
+sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no
+case names every
 case runs.
 
 Used for the committed ncu summaries: run one case with few iterations under
@@ -91,6 +92,17 @@ def _cases(B: int, L: int):
     cases["gdr_rec_bwd"] = (lambda: C.gdr_rec_bwd(W_, Qh, Kt, A_, Vp, gC, states, dO, None, False), None, 2 * rec)
     rb = C.gdr_rec_bwd(W_, Qh, Kt, A_, Vp, gC, states, dO, None, False)
     cases["gdr_intra_bwd"] = (lambda: C.gdr_intra_bwd(q, k, v, g, beta, *rb[:6], scale), None, 2 * intra)
+
+    # KDA gated intra-chunk products at the 340M KDA shape (4 heads, dk 128)
+    dkk = 128
+    Nq = B * 4 * (L // 64)
+    Qg = torch.randn(Nq, 64, dkk, device=dev)
+    Kg = torch.randn(Nq, 64, dkk, device=dev)
+    Gg = (-torch.rand(Nq, 64, dkk, device=dev) * 0.05).cumsum(1)
+    dA1, dA2 = torch.randn(Nq, 64, 64, device=dev), torch.randn(Nq, 64, 64, device=dev)
+    kfl = Nq * 64 * 65 // 2 * dkk * 4                 # pairs x channels x (exp-weighted FMAs)
+    cases["kda_gated_fwd"] = (lambda: C.kda_gated_fwd(Qg, Kg, Gg), None, kfl)
+    cases["kda_gated_bwd"] = (lambda: C.kda_gated_bwd(Qg, Kg, Gg, dA1, dA2), None, 2 * kfl)
 
     from ..ops._core import gemm
     a = r(T, D)

@@ -17,7 +17,7 @@ namespace vagus {
 namespace {
 
 constexpr int KC = 64;           // chunk
-constexpr int KT = 256;          // threads
+constexpr int KT = 512;          // threads: one CTA per SM (shared memory), so 16 warps hide the latency
 
 __device__ __forceinline__ void load_rows(float* s, const float* g, int dk, int sp) {
   for (int i = threadIdx.x; i < KC * dk / 4; i += KT) {
