@@ -151,3 +151,38 @@ def test_shortconv_shift_matches_conv1d():
     y2.sum().backward()
     assert torch.allclose(x1.grad, x2.grad, atol=1e-12)
     assert torch.allclose(c1.conv.weight.grad, c2.conv.weight.grad, atol=1e-12)
+
+
+def test_kda_intra_stage_matches_vector_oracle():
+    """The per-channel-gate intra stage of ops/kda.py (its CPU path: gated
+    products on 16-row sub-chunks) followed by the chunk recurrence
+    V' = U - W S, O = Qh S + A V', S <- diag(gamma) S + Kt^T V' equals the
+    pairwise-decay oracle chunk_scan_vec."""
+    from vagus_b200.ops.kda import _gated, kda_intra
+    torch.manual_seed(0)
+    B, L, H, dk, dv = 1, 128, 2, 16, 8
+    q = F.normalize(torch.randn(B, L, H, dk, dtype=torch.float64), dim=-1)
+    k = F.normalize(torch.randn(B, L, H, dk, dtype=torch.float64), dim=-1)
+    v = torch.randn(B, L, H, dv, dtype=torch.float64)
+    g = F.logsigmoid(torch.randn(B, L, H, dk, dtype=torch.float64) + 2) * 0.5
+    beta = torch.sigmoid(torch.randn(B, L, H, dtype=torch.float64))
+    S0 = 0.1 * torch.randn(B, H, dk, dv, dtype=torch.float64)
+    scale = dk ** -0.5
+    o_r, S_r = chunk_scan_vec(q, k, v, g, beta, S0, scale=scale, delta=True, chunk_size=64)
+    W, Qh, Kt, A, U, gam = kda_intra(q, k, v, g, beta, scale)
+    S = S0.float()
+    outs = []
+    for n in range(L // 64):
+        Vp = U[:, :, n] - W[:, :, n] @ S
+        outs.append(Qh[:, :, n] @ S + A[:, :, n] @ Vp)
+        S = gam[:, :, n, :, None] * S + Kt[:, :, n].transpose(-1, -2) @ Vp
+    o = torch.stack(outs, 2).permute(0, 2, 3, 1, 4).reshape(B, L, H, dv)
+    assert (o - o_r.float()).abs().max() < 1e-5 and (S - S_r.float()).abs().max() < 1e-5
+    # the sub-chunk factorisation equals the pairwise definition, also for fast channels
+    X, Y = torch.randn(2, 64, 8, dtype=torch.float64), torch.randn(2, 64, 8, dtype=torch.float64)
+    gg = (-torch.rand(2, 64, 8, dtype=torch.float64) * 6).cumsum(-2)
+    for strict in (True, False):
+        E = (gg[..., :, None, :] - gg[..., None, :, :])
+        mask = torch.ones(64, 64, dtype=torch.bool).tril(-1 if strict else 0)
+        ref = torch.einsum("...ic,...ijc,...jc->...ij", X, E.masked_fill(~mask[..., None], float("-inf")).exp(), Y)
+        assert torch.allclose(_gated(X, Y, gg, strict), ref, atol=1e-12)

@@ -136,3 +136,21 @@ def test_registry_record(tmp_path):
     assert rec["results"]["final_step"] == 3 and rec["results"]["loss_tail5"] is not None
     assert any(a["file"] == "model-final.pt" for a in rec["archive"])
     assert (run / "SHA256SUMS").read_text().count("\n") == len(rec["archive"])
+
+
+def test_muon_exchange_eligibility_and_layout():
+    """The fused Newton-Schulz scatter takes a bucket only when every rank can
+    place its rows: even row split, dims multiples of 8, and for tall matrices
+    (processed transposed, scattered by 32-column chunks) rows / world a
+    multiple of 32; receive blocks are 256-byte aligned."""
+    from vagus_b200.parallel.nvlink import MuonExchange
+    cuda = torch.device("cuda")
+    assert MuonExchange.eligible((1024, 1024), 8, cuda)
+    assert MuonExchange.eligible((2816, 1024), 8, cuda)          # tall: 352 rows per rank
+    assert not MuonExchange.eligible((4160, 1024), 8, cuda)      # tall: 520 rows per rank
+    assert MuonExchange.eligible((1024, 2816), 8, cuda)          # wide: row blocks of 128
+    assert not MuonExchange.eligible((1000, 1024), 16, cuda)     # uneven split
+    assert not MuonExchange.eligible((1024, 1024), 1, cuda)      # nothing to exchange
+    assert not MuonExchange.eligible((1024, 1024), 2, torch.device("cpu"))
+    assert MuonExchange.block_bytes(4, 128, 1024) == 4 * 128 * 1024 * 2
+    assert MuonExchange.block_bytes(3, 10, 10) % 256 == 0
