@@ -10,7 +10,15 @@ from vagus_b200.eval.main import EvalConfig, evaluate
 from vagus_b200.eval.pairs import paired
 from vagus_b200.models.kalman import kalman_gain_diag, kalman_gain_iso, mobius_scan
 
-torch.set_default_dtype(torch.float64)
+@pytest.fixture(autouse=True)
+def _fp64_default(request):
+    """fp64 default dtype for the scan oracles of this module only (restored
+    after each test, so modules collected after this one keep fp32)."""
+    prev = torch.get_default_dtype()
+    if "trained" not in request.fixturenames:
+        torch.set_default_dtype(torch.float64)
+    yield
+    torch.set_default_dtype(prev)
 
 
 def _pos(*shape):
