@@ -138,6 +138,7 @@ std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
   a.dU = dU.data_ptr(); a.dgC = dgC.data_ptr<float>(); a.dS0 = need_dS0 ? dS0.data_ptr<float>() : nullptr;
   a.dstates = dstates.data_ptr();
   a.f.gvec = gC.dim() == 3 ? 1 : 0;
+  a.f.err = vagus_device_error_ptr();
   TORCH_CHECK(gC.scalar_type() == at::kFloat && (gC.dim() == 2 || (gC.dim() == 3 && gC.size(2) == DK)),
               "gdr_rec_bwd: gC (BH, N) or (BH, N, DK) fp32");
   check(vagus::gdr_rec_bwd(a, stream()), "gdr_rec_bwd");

@@ -731,6 +731,223 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
   }
 }
 
+// ------------------------------------------- backward, per chunk, tcgen05 --
+// One CTA per chunk: with the value dimension as the contraction (K), the
+// chunk's gradient products are all M = 128 tiles over the key dimension:
+//   dW^T  = -S dV'^T      dQh^T = S dO^T      dKt^T = dS V'^T      (DK x C)
+//   dA    = dO V'^T       (C x C; M = 128 with the upper 64 rows unused)
+// S arrives as the value-major snapshot S^T (read MN-major), dS as dL/dS_n
+// (K-major), dV' = dU, dO (token-major) and V'^T all by TMA, one 64-wide value
+// block per stage of a two-stage ring; the accumulators live in TMEM.  Warps
+// 2-5 form dgC = <S, dS> (per key row for a per-channel gate) from the staged
+// tiles while the tensor core runs, then write the products.  Every wait is
+// bounded.
+namespace tchunk {
+template <int DK>
+struct Layout {
+  static constexpr int ST_BYTES = 64 * DK * 2;    // S^T block: DK/64 chunks of [64 v][64 k]
+  static constexpr int DS_BYTES = DK * 64 * 2;    // dS block: [DK k][64 v]
+  static constexpr int T_BYTES = 64 * 64 * 2;     // dO, dU: [64 c][64 v]; V'^T: [64 v][64 c]
+  static constexpr int OFF_DO = 0, OFF_DU = T_BYTES, OFF_VT = 2 * T_BYTES, OFF_ST = 3 * T_BYTES;
+  static constexpr int OFF_DS = OFF_ST + ST_BYTES;
+  static constexpr int STAGE = OFF_DS + DS_BYTES;
+  static constexpr int OFF_BAR = 2 * STAGE;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr int MT = DK / 128;             // M tiles over the keys
+  static constexpr uint32_t C_DW = 0, C_DQ = 64 * MT, C_DK = 128 * MT, C_DA = 192 * MT;
+  static constexpr uint32_t COLS = DK == 256 ? 512 : 256;
+};
+}  // namespace tchunk
+
+template <int DK>
+__global__ void __launch_bounds__(192, 1)
+gdr_bwd_chunk_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant__ CUtensorMap m_ds,
+                 const __grid_constant__ CUtensorMap m_du, const __grid_constant__ CUtensorMap m_do,
+                 const __grid_constant__ CUtensorMap m_vt, __nv_bfloat16* __restrict__ dW,
+                 __nv_bfloat16* __restrict__ dQh, __nv_bfloat16* __restrict__ dKt, float* __restrict__ dA,
+                 float* __restrict__ dgC, int DV, int N, int H, int gvec, int* err) {
+  using Lt = tchunk::Layout<DK>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];   // re-aligned to 1024 (the swizzle atom) below
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
+  uint64_t *full = bars, *empty = bars + 2, *acc_full = bars + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* red = reinterpret_cast<float*>(tmem_slot + 2);            // [4] block partial sums
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const long long cidx = blockIdx.x;
+  const long long bh = cidx / N;
+  const int n = static_cast<int>(cidx % N);
+  const int nvb = DV / 64;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1 + 4);      // the MMA commit + the four dgC warps
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&m_st);
+    tma_prefetch_desc(&m_ds);
+    tma_prefetch_desc(&m_du);
+    tma_prefetch_desc(&m_do);
+    tma_prefetch_desc(&m_vt);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Lt::COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int b = static_cast<int>(bh / H), h = static_cast<int>(bh % H);
+      for (int vb = 0; vb < nvb; ++vb) {
+        const int s = vb & 1;
+        if (!mbar_wait(&empty[s], ((vb >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+        uint8_t* st = sm + s * Lt::STAGE;
+        mbar_arrive_expect_tx(&full[s], Lt::STAGE);
+        const int v0 = vb * 64;
+        tma_load_3d(st + Lt::OFF_DO, &m_do, &full[s], v0, h, b * N * C + n * C);
+        tma_load_2d(st + Lt::OFF_DU, &m_du, &full[s], v0, static_cast<int>(cidx * C));
+        tma_load_2d(st + Lt::OFF_VT, &m_vt, &full[s], 0, static_cast<int>(cidx * DV + v0));
+        for (int c = 0; c < DK / 64; ++c)
+          tma_load_2d(st + Lt::OFF_ST + c * 8192, &m_st, &full[s], 64 * c, static_cast<int>(cidx * DV + v0));
+        tma_load_2d(st + Lt::OFF_DS, &m_ds, &full[s], v0, static_cast<int>(cidx * DK));
+      }
+      for (int vb = nvb; vb < nvb + 2; ++vb)      // the ring's last releases land before the CTA retires
+        if (!mbar_wait(&empty[vb & 1], ((vb >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_s = make_idesc_bf16(128, 64, true, false);   // A = S (MN-major), B K-major
+      constexpr uint32_t id_v = make_idesc_bf16(128, 64, false, true);   // A K-major, B = V'^T (MN-major)
+      for (int vb = 0; vb < nvb; ++vb) {
+        const int s = vb & 1;
+        if (!mbar_wait(&full[s], (vb >> 1) & 1, abort_flag, err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t st = smem_u32(sm + s * Lt::STAGE);
+        const uint64_t d_do = make_sw128_desc(st + Lt::OFF_DO, 16, 1024);
+        const uint64_t d_du = make_sw128_desc(st + Lt::OFF_DU, 16, 1024);
+        const uint64_t d_vt = make_sw128_desc(st + Lt::OFF_VT, 8192, 1024);
+        const uint64_t d_st = make_sw128_desc(st + Lt::OFF_ST, 8192, 1024);
+        const uint64_t d_ds = make_sw128_desc(st + Lt::OFF_DS, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {          // 16 values per step
+          const uint32_t acc = (vb | kk) ? 1u : 0u;
+#pragma unroll
+          for (int m = 0; m < Lt::MT; ++m) {
+            tc_mma_f16(tb + Lt::C_DW + 64 * m, desc_add(d_st, m * 16384 + kk * 2048), desc_add(d_du, kk * 32), id_s,
+                       acc);
+            tc_mma_f16(tb + Lt::C_DQ + 64 * m, desc_add(d_st, m * 16384 + kk * 2048), desc_add(d_do, kk * 32), id_s,
+                       acc);
+            tc_mma_f16(tb + Lt::C_DK + 64 * m, desc_add(d_ds, m * 16384 + kk * 32), desc_add(d_vt, kk * 2048), id_v,
+                       acc);
+          }
+          tc_mma_f16(tb + Lt::C_DA, desc_add(d_do, kk * 32), desc_add(d_vt, kk * 2048), id_v, acc);
+        }
+        tc_commit(&empty[s]);
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    // ---------------------------------------------------- dgC, then products
+    const int quarter = warp & 3;
+    const int t = threadIdx.x - 64;                 // 0..127
+    const uint32_t tl = tb + (static_cast<uint32_t>(quarter * 32) << 16);
+    bool ok = true;
+    float dot[DK / 128] = {};                       // rows k = t + 128 i
+    for (int vb = 0; vb < nvb; ++vb) {
+      const int s = vb & 1;
+      ok = ok && mbar_wait(&full[s], (vb >> 1) & 1, abort_flag, err, kErrTimeoutEpilogue);
+      const uint8_t* st = sm + s * Lt::STAGE;
+#pragma unroll
+      for (int i = 0; i < DK / 128; ++i) {
+        const int k = t + 128 * i;
+        const uint8_t* srow = st + Lt::OFF_ST + (k >> 6) * 8192 + (k & 7) * 2;
+        const uint8_t* drow = st + Lt::OFF_DS + k * 128;
+        float acc = 0.f;
+#pragma unroll 8
+        for (int v = 0; v < 64; ++v) {
+          // S^T chunk [v][k]: row v, 16-byte unit ((k & 63) >> 3) ^ (v & 7); dS [k][v]: row k, unit (v >> 3) ^ (k & 7)
+          const float sv = bf2f(*reinterpret_cast<const __nv_bfloat16*>(
+              srow + v * 128 + (((((k & 63) >> 3)) ^ (v & 7)) * 16)));
+          const float dv = bf2f(*reinterpret_cast<const __nv_bfloat16*>(
+              drow + (((v >> 3) ^ (k & 7)) * 16) + (v & 7) * 2));
+          acc = fmaf(sv, dv, acc);
+        }
+        dot[i] += acc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (gvec) {
+#pragma unroll
+      for (int i = 0; i < DK / 128; ++i) dgC[cidx * DK + t + 128 * i] = dot[i];
+    } else {
+      float tot = 0.f;
+#pragma unroll
+      for (int i = 0; i < DK / 128; ++i) tot += dot[i];
+      tot = warp_sum(tot);
+      if (lane == 0) red[quarter] = tot;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (t == 0) dgC[cidx] = red[0] + red[1] + red[2] + red[3];
+    }
+    // products: TMEM lane = key row (dA: query row c < 64), columns = the chunk's 64 tokens
+    ok = ok && mbar_wait(acc_full, 0, abort_flag, err, kErrTimeoutEpilogue);
+    tc_fence_after();
+    const int row = quarter * 32 + lane;
+#pragma unroll 1
+    for (int which = 0; which < 3; ++which) {
+      __nv_bfloat16* out = which == 0 ? dW : (which == 1 ? dQh : dKt);
+      const uint32_t base = which == 0 ? Lt::C_DW : (which == 1 ? Lt::C_DQ : Lt::C_DK);
+      const float sgn = which == 0 ? -1.f : 1.f;
+#pragma unroll 1
+      for (int m = 0; m < Lt::MT; ++m) {
+        uint32_t r0[32], r1[32];
+        tmem_ld_32x32b_x32(tl + base + 64 * m, r0);
+        tmem_ld_32x32b_x32(tl + base + 64 * m + 32, r1);
+        tmem_ld_wait();
+        if (ok) {
+          __nv_bfloat16* dst = out + (cidx * C) * DK + 128 * m + row;
+#pragma unroll
+          for (int c = 0; c < 32; ++c) {
+            dst[(long long)c * DK] = f2bf(sgn * __uint_as_float(r0[c]));
+            dst[(long long)(c + 32) * DK] = f2bf(sgn * __uint_as_float(r1[c]));
+          }
+        }
+      }
+    }
+    {
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32(tl + Lt::C_DA, r0);
+      tmem_ld_32x32b_x32(tl + Lt::C_DA + 32, r1);
+      tmem_ld_wait();
+      if (ok && row < C) {
+        float* dst = dA + (cidx * C + row) * C;
+#pragma unroll
+        for (int c = 0; c < 32; c += 4) {
+          *reinterpret_cast<float4*>(dst + c) = make_float4(__uint_as_float(r0[c]), __uint_as_float(r0[c + 1]),
+                                                            __uint_as_float(r0[c + 2]), __uint_as_float(r0[c + 3]));
+          *reinterpret_cast<float4*>(dst + 32 + c) = make_float4(__uint_as_float(r1[c]), __uint_as_float(r1[c + 1]),
+                                                                 __uint_as_float(r1[c + 2]), __uint_as_float(r1[c + 3]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tb, Lt::COLS);
+  }
+}
+
 // ----------------------------------------------------- single-token decode --
 // S (B, H, dk, dv) fp32 in place; q, k (B, H, dk), v (B, H, dv) bf16; g, beta (B, H)
 // S <- a S;  r = v - S^T k;  S <- S + b k r^T;  o = scale * S^T q
@@ -817,6 +1034,36 @@ int launch_bwd(const GdrRecBwdArgs& a, cudaStream_t st) {
                                               (const __nv_bfloat16*)a.f.Kt, (const __nv_bfloat16*)a.f.A, a.f.gC,
                                               (const __nv_bfloat16*)a.dO, a.dS_final, (__nv_bfloat16*)a.dU,
                                               (__nv_bfloat16*)a.dstates, a.dS0, a.f.N, a.f.DV, a.f.H, a.f.gvec);
+  static const bool no_tc = std::getenv("VAGUS_GDR_NO_TC") != nullptr;
+  if (!no_tc && a.f.err && a.f.DV % 64 == 0) {
+    using Lt = tchunk::Layout<DK>;
+    alignas(64) unsigned char m_st[128], m_ds[128], m_du[128], m_do[128], m_vt[128];
+    const unsigned long long BHN = (unsigned long long)a.f.BH * a.f.N;
+    const unsigned long long d_st[2] = {(unsigned long long)DK, BHN * a.f.DV};
+    const unsigned long long s_st[1] = {(unsigned long long)DK * 2};
+    const unsigned long long d_ds[2] = {(unsigned long long)a.f.DV, BHN * DK};
+    const unsigned long long d_du[2] = {(unsigned long long)a.f.DV, BHN * C};
+    const unsigned long long s_dv[1] = {(unsigned long long)a.f.DV * 2};
+    const unsigned long long d_vt[2] = {(unsigned long long)C, BHN * a.f.DV};
+    const unsigned long long s_vt[1] = {(unsigned long long)C * 2};
+    // dO token-major (B, L, H, DV): {DV, H, B * L}
+    const unsigned long long d_do[3] = {(unsigned long long)a.f.DV, (unsigned long long)a.f.H,
+                                        (unsigned long long)(a.f.BH / a.f.H) * a.f.N * C};
+    const unsigned long long s_do[2] = {(unsigned long long)a.f.DV * 2, (unsigned long long)a.f.H * a.f.DV * 2};
+    const unsigned box64[2] = {64u, 64u}, box_ds[2] = {64u, static_cast<unsigned>(DK)}, box_do[3] = {64u, 1u, 64u};
+    if (!encode_bf16_map(m_st, a.f.states, 2, d_st, s_st, box64) ||
+        !encode_bf16_map(m_ds, a.dstates, 2, d_ds, s_dv, box_ds) ||
+        !encode_bf16_map(m_du, a.dU, 2, d_du, s_dv, box64) || !encode_bf16_map(m_vt, a.f.Vp, 2, d_vt, s_vt, box64) ||
+        !encode_bf16_map(m_do, a.dO, 3, d_do, s_do, box_do))
+      return 2;
+    if (!set_smem(gdr_bwd_chunk_tc<DK>, Lt::SMEM)) return 3;
+    gdr_bwd_chunk_tc<DK><<<static_cast<unsigned>(BHN), 192, Lt::SMEM, st>>>(
+        *reinterpret_cast<const CUtensorMap*>(m_st), *reinterpret_cast<const CUtensorMap*>(m_ds),
+        *reinterpret_cast<const CUtensorMap*>(m_du), *reinterpret_cast<const CUtensorMap*>(m_do),
+        *reinterpret_cast<const CUtensorMap*>(m_vt), (__nv_bfloat16*)a.dW, (__nv_bfloat16*)a.dQh,
+        (__nv_bfloat16*)a.dKt, a.dA, a.dgC, a.f.DV, a.f.N, a.f.H, a.f.gvec, a.f.err);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   dim3 g2(static_cast<unsigned>(a.f.BH * a.f.N), DK / 64);
   gdr_bwd_chunk<<<g2, THREADS, s2, st>>>((const __nv_bfloat16*)a.dU, (const __nv_bfloat16*)a.dO,
                                          (const __nv_bfloat16*)a.f.Vp, (const __nv_bfloat16*)a.f.states,
