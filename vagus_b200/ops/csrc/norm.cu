@@ -237,6 +237,112 @@ __global__ void rmsnorm_gated_bwd_k(const __nv_bfloat16* __restrict__ dy, const 
   for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
 }
 
+// Vectorised gated RMSNorm for head dims 128 / 256 (NV = D / 32 elements per
+// lane, one or two 8-byte / 16-byte loads per tensor): each lane keeps its
+// slice of the row in registers between the two passes, warps stride over
+// rows, and the backward's dgamma stays in registers until one shared-memory
+// reduction and one global atomic per column per CTA (the scalar kernels
+// above issue a shared atomic per element and a global atomic per column per
+// 8 rows).
+template <int NV>
+__device__ __forceinline__ void ld_bf16v(const __nv_bfloat16* p, float (&f)[NV]) {
+  if constexpr (NV == 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(p);
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) { const float2 t = unpack_bf16x2(w[i]); f[2 * i] = t.x; f[2 * i + 1] = t.y; }
+  } else {
+    const uint2 u = *reinterpret_cast<const uint2*>(p);
+    const float2 a = unpack_bf16x2(u.x), b = unpack_bf16x2(u.y);
+    f[0] = a.x; f[1] = a.y; f[2] = b.x; f[3] = b.y;
+  }
+}
+template <int NV>
+__device__ __forceinline__ void st_bf16v(__nv_bfloat16* p, const float (&f)[NV]) {
+  if constexpr (NV == 8) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                              pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  } else {
+    *reinterpret_cast<uint2*>(p) = make_uint2(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]));
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256)
+rmsnorm_gated_fwd_vec_k(const __nv_bfloat16* __restrict__ o, const __nv_bfloat16* __restrict__ g, long long ldg,
+                        int H, const float* __restrict__ gamma, __nv_bfloat16* __restrict__ y,
+                        float* __restrict__ rstd, long long rows, float eps) {
+  constexpr int D = 32 * NV;
+  const int lane = threadIdx.x & 31;
+  const long long w0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const long long nw = (long long)gridDim.x * blockDim.x / 32;
+  float gm[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) gm[i] = gamma[lane * NV + i];
+  for (long long r = w0; r < rows; r += nw) {
+    float ov[NV], gv[NV];
+    ld_bf16v<NV>(o + r * D + lane * NV, ov);
+    ld_bf16v<NV>(g + (r / H) * ldg + (r % H) * D + lane * NV, gv);
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) ss += ov[i] * ov[i];
+    const float rs = rsqrtf(warp_sum(ss) / D + eps);
+    if (lane == 0) rstd[r] = rs;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) ov[i] = ov[i] * rs * gm[i] * silu_f(gv[i]);
+    st_bf16v<NV>(y + r * D + lane * NV, ov);
+  }
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256)
+rmsnorm_gated_bwd_vec_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ o,
+                        const __nv_bfloat16* __restrict__ g, long long ldg, int H, const float* __restrict__ gamma,
+                        const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dO,
+                        __nv_bfloat16* __restrict__ dG, long long lddg, float* __restrict__ dgamma, long long rows) {
+  constexpr int D = 32 * NV;
+  __shared__ float red[8][D];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const long long w0 = ((long long)blockIdx.x * blockDim.x + threadIdx.x) / 32;
+  const long long nw = (long long)gridDim.x * blockDim.x / 32;
+  float gm[NV], acc[NV];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) { gm[i] = gamma[lane * NV + i]; acc[i] = 0.f; }
+  for (long long r = w0; r < rows; r += nw) {
+    float ov[NV], gv[NV], dv[NV];
+    ld_bf16v<NV>(o + r * D + lane * NV, ov);
+    ld_bf16v<NV>(g + (r / H) * ldg + (r % H) * D + lane * NV, gv);
+    ld_bf16v<NV>(dy + r * D + lane * NV, dv);
+    const float rs = rstd[r];
+    float dot = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) dot += dv[i] * silu_f(gv[i]) * gm[i] * ov[i] * rs;
+    dot = warp_sum(dot) / D;
+    float dov[NV], dgv[NV];
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const float sgm = sigmoid_f(gv[i]);
+      const float xh = ov[i] * rs;
+      const float dyn = dv[i] * gv[i] * sgm;                      // grad wrt normalised * gamma
+      dov[i] = rs * (dyn * gm[i] - xh * dot);
+      // d silu(g) / dg = s (1 + g (1 - s))
+      dgv[i] = dv[i] * xh * gm[i] * sgm * (1.f + gv[i] * (1.f - sgm));
+      acc[i] += dyn * xh;
+    }
+    st_bf16v<NV>(dO + r * D + lane * NV, dov);
+    st_bf16v<NV>(dG + (r / H) * lddg + (r % H) * D + lane * NV, dgv);
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) red[warp][lane * NV + i] = acc[i];
+  __syncthreads();
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < 8; ++w) t += red[w][c];
+    atomicAdd(&dgamma[c], t);
+  }
+}
+
 // ------------------------------------------------------- qk_norm_rope --
 // x: (B, L, H, Dh) bf16 contiguous; cos/sin: (L, Dh/2) fp32 (already offset).
 // One warp per (b, l, h) row.
@@ -385,8 +491,36 @@ int rmsnorm_bwd(const void* dy, int dy_f32, const void* x, int x_f32, const floa
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+// grid for the row-striding vector kernels: a few waves of 8-warp CTAs
+int vec_grid(long long rows) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  const long long want = (rows + 7) / 8;
+  return static_cast<int>(std::min<long long>(want, 8LL * sms));
+}
+
+bool gated_vec_ok(const void* a, const void* b, long long ldb, int D) {
+  const int al = D == 256 ? 16 : 8;
+  return (D == 256 || D == 128) && reinterpret_cast<uintptr_t>(a) % al == 0 &&
+         reinterpret_cast<uintptr_t>(b) % al == 0 && (ldb * 2) % al == 0;
+}
+
 int rmsnorm_gated_fwd(const void* o, const void* g, long long ldg, int H, const float* gamma, void* y, int y_f32,
                       float* rstd, long long rows, int D, float eps, cudaStream_t s) {
+  if (!y_f32 && gated_vec_ok(o, g, ldg, D) && gated_vec_ok(y, y, D, D)) {
+    if (D == 256)
+      rmsnorm_gated_fwd_vec_k<8><<<vec_grid(rows), 256, 0, s>>>((const __nv_bfloat16*)o, (const __nv_bfloat16*)g,
+                                                                ldg, H, gamma, (__nv_bfloat16*)y, rstd, rows, eps);
+    else
+      rmsnorm_gated_fwd_vec_k<4><<<vec_grid(rows), 256, 0, s>>>((const __nv_bfloat16*)o, (const __nv_bfloat16*)g,
+                                                                ldg, H, gamma, (__nv_bfloat16*)y, rstd, rows, eps);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   if (y_f32)
     rmsnorm_gated_fwd_k<float><<<blocks_for(rows), 32 * ROWS_PER_CTA, 0, s>>>(
         (const __nv_bfloat16*)o, (const __nv_bfloat16*)g, ldg, H, gamma, (float*)y, rstd, rows, D, eps);
@@ -399,6 +533,17 @@ int rmsnorm_gated_fwd(const void* o, const void* g, long long ldg, int H, const 
 int rmsnorm_gated_bwd(const void* dy, const void* o, const void* g, long long ldg, int H, const float* gamma,
                       const float* rstd, void* dO, void* dG, long long lddg, float* dgamma, long long rows, int D,
                       cudaStream_t s) {
+  if (gated_vec_ok(o, g, ldg, D) && gated_vec_ok(dy, dG, lddg, D) && gated_vec_ok(dO, dO, D, D)) {
+    if (D == 256)
+      rmsnorm_gated_bwd_vec_k<8><<<vec_grid(rows), 256, 0, s>>>(
+          (const __nv_bfloat16*)dy, (const __nv_bfloat16*)o, (const __nv_bfloat16*)g, ldg, H, gamma, rstd,
+          (__nv_bfloat16*)dO, (__nv_bfloat16*)dG, lddg, dgamma, rows);
+    else
+      rmsnorm_gated_bwd_vec_k<4><<<vec_grid(rows), 256, 0, s>>>(
+          (const __nv_bfloat16*)dy, (const __nv_bfloat16*)o, (const __nv_bfloat16*)g, ldg, H, gamma, rstd,
+          (__nv_bfloat16*)dO, (__nv_bfloat16*)dG, lddg, dgamma, rows);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   rmsnorm_gated_bwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, D * sizeof(float), s>>>(
       (const __nv_bfloat16*)dy, (const __nv_bfloat16*)o, (const __nv_bfloat16*)g, ldg, H, gamma, rstd,
       (__nv_bfloat16*)dO, (__nv_bfloat16*)dG, lddg, dgamma, rows, D);
