@@ -42,6 +42,54 @@ __global__ void swiglu_bwd_k(const __nv_bfloat16* __restrict__ ds, const __nv_bf
   }
 }
 
+// 16-byte version (8 features per thread, 32-bit indexing) for F % 8 == 0
+// and rows * F / 8 < 2^31: the element-pair kernels above spend most of their
+// issue slots on 64-bit index division.
+__global__ void swiglu_fwd_v8(const __nv_bfloat16* __restrict__ u, __nv_bfloat16* __restrict__ s, unsigned n8,
+                              unsigned f8) {
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += gridDim.x * blockDim.x) {
+    const unsigned r = i / f8, c = (i - r * f8) * 8;
+    const size_t F = size_t(f8) * 8;
+    const uint4 a = *reinterpret_cast<const uint4*>(u + r * 2 * F + c);
+    const uint4 g = *reinterpret_cast<const uint4*>(u + r * 2 * F + F + c);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w};
+    uint32_t o[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 af = unpack_bf16x2(aw[j]), gf = unpack_bf16x2(gw[j]);
+      o[j] = pack_bf16x2(silu_f(af.x) * gf.x, silu_f(af.y) * gf.y);
+    }
+    *reinterpret_cast<uint4*>(s + r * F + c) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+}
+
+__global__ void swiglu_bwd_v8(const __nv_bfloat16* __restrict__ ds, const __nv_bfloat16* __restrict__ u,
+                              __nv_bfloat16* __restrict__ du, unsigned n8, unsigned f8) {
+  for (unsigned i = blockIdx.x * blockDim.x + threadIdx.x; i < n8; i += gridDim.x * blockDim.x) {
+    const unsigned r = i / f8, c = (i - r * f8) * 8;
+    const size_t F = size_t(f8) * 8;
+    const uint4 a = *reinterpret_cast<const uint4*>(u + r * 2 * F + c);
+    const uint4 g = *reinterpret_cast<const uint4*>(u + r * 2 * F + F + c);
+    const uint4 d = *reinterpret_cast<const uint4*>(ds + r * F + c);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, gw[4] = {g.x, g.y, g.z, g.w}, dw[4] = {d.x, d.y, d.z, d.w};
+    uint32_t oa[4], og[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 af = unpack_bf16x2(aw[j]), gf = unpack_bf16x2(gw[j]), df = unpack_bf16x2(dw[j]);
+      const float sa = sigmoid_f(af.x), sb = sigmoid_f(af.y);
+      oa[j] = pack_bf16x2(df.x * gf.x * sa * (1.f + af.x * (1.f - sa)), df.y * gf.y * sb * (1.f + af.y * (1.f - sb)));
+      og[j] = pack_bf16x2(df.x * af.x * sa, df.y * af.y * sb);
+    }
+    *reinterpret_cast<uint4*>(du + r * 2 * F + c) = make_uint4(oa[0], oa[1], oa[2], oa[3]);
+    *reinterpret_cast<uint4*>(du + r * 2 * F + F + c) = make_uint4(og[0], og[1], og[2], og[3]);
+  }
+}
+
+bool swiglu_v8_ok(const void* a, const void* b, const void* c, long long rows, int F) {
+  auto al = [](const void* p) { return p == nullptr || reinterpret_cast<uintptr_t>(p) % 16 == 0; };
+  return F % 8 == 0 && rows * (long long)(F / 8) < (1LL << 31) && al(a) && al(b) && al(c);
+}
+
 // ------------------------------------------------------- sigmoid gate --
 // y = x * sigmoid(g), all (n) bf16
 
@@ -207,11 +255,22 @@ inline int grid_for(long long n, int t = 256) {
 }  // namespace
 
 int swiglu_fwd(const void* u, void* s, long long rows, int F, cudaStream_t st) {
+  if (swiglu_v8_ok(u, s, nullptr, rows, F)) {
+    const unsigned n8 = static_cast<unsigned>(rows * (F / 8));
+    swiglu_fwd_v8<<<grid_for(n8), 256, 0, st>>>((const __nv_bfloat16*)u, (__nv_bfloat16*)s, n8, F / 8);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   swiglu_fwd_k<<<grid_for(rows * F / 2), 256, 0, st>>>((const __nv_bfloat16*)u, (__nv_bfloat16*)s, rows, F);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
 int swiglu_bwd(const void* ds, const void* u, void* du, long long rows, int F, cudaStream_t st) {
+  if (swiglu_v8_ok(ds, u, du, rows, F)) {
+    const unsigned n8 = static_cast<unsigned>(rows * (F / 8));
+    swiglu_bwd_v8<<<grid_for(n8), 256, 0, st>>>((const __nv_bfloat16*)ds, (const __nv_bfloat16*)u,
+                                                (__nv_bfloat16*)du, n8, F / 8);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   swiglu_bwd_k<<<grid_for(rows * F / 2), 256, 0, st>>>((const __nv_bfloat16*)ds, (const __nv_bfloat16*)u,
                                                         (__nv_bfloat16*)du, rows, F);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
