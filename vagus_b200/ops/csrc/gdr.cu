@@ -512,6 +512,129 @@ gdr_fwd_out(const __nv_bfloat16* __restrict__ Qh, const __nv_bfloat16* __restric
              DVT + PAD, C, DVT);
 }
 
+// ------------------------------------------------ forward output, tcgen05 --
+// O_n^T = S_n^T Qh_n^T + V'^T_n A_n^T on the tensor cores, one CTA per chunk:
+// M = the value dimension (DV/128 tiles), N = the chunk's 64 tokens, K = the
+// key dimension in 64-wide blocks and then the 64 tokens of V'.  Every K block
+// pairs a [DV][64] A-operand tile (S^T block, or V'^T) with a [64][64]
+// B-operand tile (Qh block, or A), both K-major, both by TMA, through a
+// two-stage ring; O^T accumulates in TMEM and the epilogue warps write it
+// token-major.  Every wait is bounded.
+namespace tout {
+template <int DV>
+struct Layout {
+  static constexpr int A_BYTES = DV * 64 * 2, B_BYTES = 64 * 64 * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int OFF_BAR = 2 * STAGE;
+  static constexpr int SMEM = OFF_BAR + 128 + 1024;
+  static constexpr int MT = DV / 128;
+  static constexpr uint32_t COLS = MT == 1 ? 64 : (MT == 2 ? 128 : 256);
+};
+}  // namespace tout
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(192, 1)
+gdr_fwd_out_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant__ CUtensorMap m_qh,
+               const __grid_constant__ CUtensorMap m_vt, const __grid_constant__ CUtensorMap m_a,
+               __nv_bfloat16* __restrict__ O, int N, int H, int* err) {
+  using Lt = tout::Layout<DV>;
+  constexpr int NKB = DK / 64 + 1;                // K blocks: the keys, then the tokens of V'
+  extern __shared__ __align__(128) uint8_t smem_raw[];   // re-aligned to 1024 (the swizzle atom) below
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
+  uint64_t *full = bars, *empty = bars + 2, *acc_full = bars + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const long long cidx = blockIdx.x;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&m_st);
+    tma_prefetch_desc(&m_qh);
+    tma_prefetch_desc(&m_vt);
+    tma_prefetch_desc(&m_a);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Lt::COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      for (int kb = 0; kb < NKB; ++kb) {
+        const int s = kb & 1;
+        if (!mbar_wait(&empty[s], ((kb >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+        uint8_t* a = sm + s * Lt::STAGE;
+        uint8_t* bt = a + Lt::A_BYTES;
+        mbar_arrive_expect_tx(&full[s], Lt::STAGE);
+        const bool keys = kb < DK / 64;
+        for (int m = 0; m < DV / 128; ++m)
+          tma_load_2d(a + m * 16384, keys ? &m_st : &m_vt, &full[s], keys ? 64 * kb : 0,
+                      static_cast<int>(cidx * DV + 128 * m));
+        tma_load_2d(bt, keys ? &m_qh : &m_a, &full[s], keys ? 64 * kb : 0, static_cast<int>(cidx * C));
+      }
+      for (int kb = NKB; kb < NKB + 2; ++kb)
+        if (!mbar_wait(&empty[kb & 1], ((kb >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id = make_idesc_bf16(128, 64, false, false);
+      for (int kb = 0; kb < NKB; ++kb) {
+        const int s = kb & 1;
+        if (!mbar_wait(&full[s], (kb >> 1) & 1, abort_flag, err, kErrTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t a = smem_u32(sm + s * Lt::STAGE);
+        const uint64_t da = make_sw128_desc(a, 16, 1024), db = make_sw128_desc(a + Lt::A_BYTES, 16, 1024);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+          for (int m = 0; m < Lt::MT; ++m)
+            tc_mma_f16(tb + 64 * m, desc_add(da, m * 16384 + kk * 32), desc_add(db, kk * 32), id, (kb | kk) ? 1u : 0u);
+        tc_commit(&empty[s]);
+      }
+      tc_commit(acc_full);
+    }
+  } else {
+    const int quarter = warp & 3;
+    const uint32_t tl = tb + (static_cast<uint32_t>(quarter * 32) << 16);
+    const bool ok = mbar_wait(acc_full, 0, abort_flag, err, kErrTimeoutEpilogue);
+    tc_fence_after();
+    const int v = quarter * 32 + lane;
+    __nv_bfloat16* dst = O + tok_row0(cidx / N, static_cast<int>(cidx % N), N, H, DV) + v;
+#pragma unroll 1
+    for (int m = 0; m < Lt::MT; ++m) {
+      uint32_t r0[32], r1[32];
+      tmem_ld_32x32b_x32(tl + 64 * m, r0);
+      tmem_ld_32x32b_x32(tl + 64 * m + 32, r1);
+      tmem_ld_wait();
+      if (ok) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          dst[(long long)c * H * DV + 128 * m] = f2bf(__uint_as_float(r0[c]));
+          dst[(long long)(c + 32) * H * DV + 128 * m] = f2bf(__uint_as_float(r1[c]));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tb, Lt::COLS);
+  }
+}
+
 // ------------------------------------------------------------ backward scan --
 
 template <int DK>
@@ -1017,6 +1140,29 @@ int launch_fwd(const GdrRecArgs& a, cudaStream_t st) {
     gdr_fwd_scan<DK><<<grid, THREADS, s1, st>>>((const __nv_bfloat16*)a.W, (const __nv_bfloat16*)a.Kt,
                                                 (const __nv_bfloat16*)a.U, a.gC, a.S0, (__nv_bfloat16*)a.Vp,
                                                 (__nv_bfloat16*)a.states, a.S_out, a.N, a.DV, a.gvec);
+  }
+  if (!no_tc && a.err && (a.DV == 128 || a.DV == 256 || a.DV == 512)) {
+    alignas(64) unsigned char m_st[128], m_qh[128], m_vt[128], m_a[128];
+    const unsigned long long BHN = (unsigned long long)a.BH * a.N;
+    const unsigned long long d_st[2] = {(unsigned long long)DK, BHN * a.DV}, s_st[1] = {(unsigned long long)DK * 2};
+    const unsigned long long d_qh[2] = {(unsigned long long)DK, BHN * C};
+    const unsigned long long d_vt[2] = {(unsigned long long)C, BHN * a.DV}, s_c[1] = {(unsigned long long)C * 2};
+    const unsigned long long d_a[2] = {(unsigned long long)C, BHN * C};
+    const unsigned box_a[2] = {64u, 128u}, box_b[2] = {64u, 64u};
+    if (!encode_bf16_map(m_st, a.states, 2, d_st, s_st, box_a) || !encode_bf16_map(m_qh, a.Qh, 2, d_qh, s_st, box_b) ||
+        !encode_bf16_map(m_vt, a.Vp, 2, d_vt, s_c, box_a) || !encode_bf16_map(m_a, a.A, 2, d_a, s_c, box_b))
+      return 2;
+    auto go = [&](auto kern, int smem) -> int {
+      if (!set_smem(kern, smem)) return 3;
+      kern<<<static_cast<unsigned>(BHN), 192, smem, st>>>(
+          *reinterpret_cast<const CUtensorMap*>(m_st), *reinterpret_cast<const CUtensorMap*>(m_qh),
+          *reinterpret_cast<const CUtensorMap*>(m_vt), *reinterpret_cast<const CUtensorMap*>(m_a),
+          (__nv_bfloat16*)a.O, a.N, a.H, a.err);
+      return cudaGetLastError() == cudaSuccess ? 0 : 3;
+    };
+    if (a.DV == 128) return go(gdr_fwd_out_tc<DK, 128>, tout::Layout<128>::SMEM);
+    if (a.DV == 256) return go(gdr_fwd_out_tc<DK, 256>, tout::Layout<256>::SMEM);
+    return go(gdr_fwd_out_tc<DK, 512>, tout::Layout<512>::SMEM);
   }
   dim3 g2(static_cast<unsigned>(a.BH * a.N), a.DV / DVT);
   gdr_fwd_out<DK><<<g2, THREADS, s2, st>>>((const __nv_bfloat16*)a.Qh, (const __nv_bfloat16*)a.A,
