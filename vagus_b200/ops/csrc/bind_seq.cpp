@@ -127,7 +127,7 @@ std::vector<Tensor> gdr_rec_bwd(Tensor W, Tensor Qh, Tensor Kt, Tensor A, Tensor
   auto dU = torch::empty({BH, N, 64, DV}, bf);
   auto dgC = torch::zeros(gC.sizes(), f32);
   auto dS0 = torch::empty({need_dS0 ? BH : 0, DK, DV}, f32);
-  auto dstates = torch::empty({BH, N, DK, DV}, bf);
+  auto dstates = torch::empty({BH, N, DV, DK}, bf);            // value-major, like the forward snapshots
   vagus::GdrRecBwdArgs a;
   a.f = vagus::GdrRecArgs{W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), nullptr,
                           gC.data_ptr<float>(), nullptr, nullptr, Vp.data_ptr(), states.data_ptr(),

@@ -30,7 +30,7 @@
 //   O, dO: token-major (B, N * C, H, DV) bf16 (BH = B * H), the layout of the model's activations
 //   gC, dgC: (BH, N) fp32, or (BH, N, DK) for a per-channel (KDA) gate, where
 //   gC S scales row k of S by gC[k] and dgC[k] = <S_n row k, dS row k>
-//   states: (BH, N, DV, DK) bf16 (S_n^T)   dstates: (BH, N, DK, DV) bf16
+//   states, dstates: (BH, N, DV, DK) bf16 (S_n^T, dL/dS_{n+1}^T: value-major)
 //   dW, dQh, dKt: (BH, N, C, DK) bf16   dA: (BH, N, C, C) fp32
 #include "common.cuh"
 #include "gemm.h"
@@ -635,6 +635,270 @@ gdr_fwd_out_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant__
   }
 }
 
+// ----------------------------------------------------- tcgen05 backward scan --
+// The backward state chain on the tensor cores, transposed like the forward
+// scan (value tile = MMA M = 128), one CTA per (sequence, value tile), with
+// dS^T (value x key, fp32) in TMEM.  Per chunk, last to first:
+//   snapshot  dstates_n = bf16(dS^T)                     (TMA store of the operand tile)
+//   D1 = dV'^T = dO^T A + dS^T Kt^T                       (M = 128, N = 64 tokens)
+//   dU = dV'  (state warps, from D1);  VN = -dV'^T        (bf16 operand tile)
+//   dS^T <- gC dS^T + dO^T Qh + VN W                       (M = 128, N = DK)
+// Warp 0 streams A and Kt (single stage, refilled once D1 is done), dO (two
+// stages: it feeds both products) and Qh, W (single stage, refilled once the
+// state update is done); warp 1 issues the MMAs and the snapshot stores;
+// warps 2-9 (two per TMEM lane quarter) copy / scale the state and turn D1
+// into VN and dU.  Every wait is bounded.
+namespace tbscan {
+constexpr int VT = 128;
+template <int DK>
+struct Layout {
+  static constexpr int K_BYTES = C * DK * 2;     // Kt, Qh, W: DK/64 chunks of [64 tokens x 128 B]
+  static constexpr int DO_BYTES = C * VT * 2;    // dO: 2 chunks of [64 tokens x 64 values]
+  static constexpr int A_BYTES = C * C * 2;
+  static constexpr int DT_BYTES = VT * DK * 2;   // bf16 dS^T: DK/64 chunks of [128 values x 128 B]
+  static constexpr int VN_BYTES = VT * C * 2;    // -dV'^T: [128 values x 64 tokens]
+  static constexpr int OFF_KT = 0, OFF_QH = K_BYTES, OFF_W = 2 * K_BYTES, OFF_DO = 3 * K_BYTES;
+  static constexpr int OFF_A = OFF_DO + 2 * DO_BYTES, OFF_DT = OFF_A + A_BYTES, OFF_VN = OFF_DT + DT_BYTES;
+  static constexpr int OFF_BAR = OFF_VN + VN_BYTES;
+  static constexpr int SMEM = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t C_S = 0, C_D1 = DK, COLS = 512;
+};
+}  // namespace tbscan
+
+template <int DK>
+__global__ void __launch_bounds__(320, 1)
+gdr_bwd_scan_tc(const __grid_constant__ CUtensorMap m_kt, const __grid_constant__ CUtensorMap m_qh,
+                const __grid_constant__ CUtensorMap m_w, const __grid_constant__ CUtensorMap m_a,
+                const __grid_constant__ CUtensorMap m_do, const __grid_constant__ CUtensorMap m_ds,
+                const float* __restrict__ gC, const float* __restrict__ dS_final, __nv_bfloat16* __restrict__ dU,
+                float* __restrict__ dS0, int N, int DV, int H, int gvec, int* err) {
+  using namespace tbscan;
+  using Lt = Layout<DK>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];   // re-aligned to 1024 (the swizzle atom) below
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *skt = sm + Lt::OFF_KT, *sqh = sm + Lt::OFF_QH, *sw = sm + Lt::OFF_W, *sdo = sm + Lt::OFF_DO;
+  uint8_t *sa = sm + Lt::OFF_A, *sdt = sm + Lt::OFF_DT, *svn = sm + Lt::OFF_VN;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sm + Lt::OFF_BAR);
+  uint64_t *a_full = bars, *a_empty = bars + 1, *do_full = bars + 2, *do_empty = bars + 4, *b_full = bars + 6,
+           *b_empty = bars + 7, *dt_ready = bars + 8, *d1_full = bars + 9, *vn_ready = bars + 10, *s2_done = bars + 11;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int tiles_v = DV / VT;
+  const long long bh = blockIdx.x / tiles_v;
+  const int v0 = (blockIdx.x % tiles_v) * VT;
+
+  if (threadIdx.x == 0) {
+    mbar_init(a_full, 1);
+    mbar_init(a_empty, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&do_full[i], 1);
+      mbar_init(&do_empty[i], 1);
+    }
+    mbar_init(b_full, 1);
+    mbar_init(b_empty, 1);
+    mbar_init(dt_ready, 8);
+    mbar_init(d1_full, 1);
+    mbar_init(vn_ready, 8);
+    mbar_init(s2_done, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+    tma_prefetch_desc(&m_kt);
+    tma_prefetch_desc(&m_qh);
+    tma_prefetch_desc(&m_w);
+    tma_prefetch_desc(&m_a);
+    tma_prefetch_desc(&m_do);
+    tma_prefetch_desc(&m_ds);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Lt::COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      const int b = static_cast<int>(bh / H), h = static_cast<int>(bh % H);
+      // j = 0, 1, ... walks the chunks n = N - 1, N - 2, ...
+      for (int j = 0; j < N; ++j) {
+        const int n = N - 1 - j, s = j & 1;
+        const int row = static_cast<int>((bh * N + n) * C);
+        if (!mbar_wait(&do_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(&do_full[s], Lt::DO_BYTES);
+        for (int i = 0; i < 2; ++i)
+          tma_load_3d(sdo + s * Lt::DO_BYTES + i * 8192, &m_do, &do_full[s], v0 + 64 * i, h, b * N * C + n * C);
+        if (!mbar_wait(a_empty, (j & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(a_full, Lt::A_BYTES + Lt::K_BYTES);
+        tma_load_2d(sa, &m_a, a_full, 0, row);
+        for (int c = 0; c < DK / 64; ++c) tma_load_2d(skt + c * 8192, &m_kt, a_full, 64 * c, row);
+        if (!mbar_wait(b_empty, (j & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+        mbar_arrive_expect_tx(b_full, 2 * Lt::K_BYTES);
+        for (int c = 0; c < DK / 64; ++c) {
+          tma_load_2d(sqh + c * 8192, &m_qh, b_full, 64 * c, row);
+          tma_load_2d(sw + c * 8192, &m_w, b_full, 64 * c, row);
+        }
+      }
+      // the last releases land before the CTA retires
+      if (mbar_wait(a_empty, (N & 1) ^ 1, abort_flag, err, kErrTimeoutProducer))
+        mbar_wait(b_empty, (N & 1) ^ 1, abort_flag, err, kErrTimeoutProducer);
+      for (int j = N; j < N + 2; ++j)
+        if (!mbar_wait(&do_empty[j & 1], ((j >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t id_a = make_idesc_bf16(VT, C, true, true);     // dO^T (MN) x A (MN)
+      constexpr uint32_t id_b = make_idesc_bf16(VT, C, false, false);   // dS^T (K) x Kt (K)
+      constexpr uint32_t id_c = make_idesc_bf16(VT, DK, true, true);    // dO^T (MN) x Qh (MN)
+      constexpr uint32_t id_d = make_idesc_bf16(VT, DK, false, true);   // VN (K) x W (MN)
+      const uint64_t d_a = make_sw128_desc(smem_u32(sa), 16, 1024);
+      const uint64_t d_kt = make_sw128_desc(smem_u32(skt), 16, 1024);
+      const uint64_t d_qh = make_sw128_desc(smem_u32(sqh), 8192, 1024);
+      const uint64_t d_w = make_sw128_desc(smem_u32(sw), 8192, 1024);
+      const uint64_t d_dt = make_sw128_desc(smem_u32(sdt), 16, 1024);
+      const uint64_t d_vn = make_sw128_desc(smem_u32(svn), 16, 1024);
+      for (int j = 0; j < N; ++j) {
+        const int n = N - 1 - j, s = j & 1;
+        const int srow = static_cast<int>((bh * N + n) * DV + v0);       // this tile's rows in the value-major dstates
+        const uint64_t d_do = make_sw128_desc(smem_u32(sdo + s * Lt::DO_BYTES), 8192, 1024);
+        if (!mbar_wait(dt_ready, j & 1, abort_flag, err, kErrTimeoutMma)) break;
+        if (!mbar_wait(a_full, j & 1, abort_flag, err, kErrTimeoutMma)) break;
+        if (!mbar_wait(&do_full[s], (j >> 1) & 1, abort_flag, err, kErrTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          tc_mma_f16(tb + Lt::C_D1, desc_add(d_do, kk * 2048), desc_add(d_a, kk * 2048), id_a, kk ? 1u : 0u);
+#pragma unroll
+        for (int c = 0; c < DK / 64; ++c)
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            tc_mma_f16(tb + Lt::C_D1, desc_add(d_dt, c * 16384 + kk * 32), desc_add(d_kt, c * 8192 + kk * 32), id_b,
+                       1u);
+        tc_commit(d1_full);
+        tc_commit(a_empty);
+        for (int c = 0; c < DK / 64; ++c) tma_store_2d(&m_ds, sdt + c * 16384, 64 * c, srow);   // dstates_n
+        bulk_commit();
+        if (!mbar_wait(vn_ready, j & 1, abort_flag, err, kErrTimeoutMma)) break;
+        if (!mbar_wait(b_full, j & 1, abort_flag, err, kErrTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          tc_mma_f16(tb + Lt::C_S, desc_add(d_do, kk * 2048), desc_add(d_qh, kk * 2048), id_c, 1u);
+          tc_mma_f16(tb + Lt::C_S, desc_add(d_vn, kk * 32), desc_add(d_w, kk * 2048), id_d, 1u);
+        }
+        bulk_wait_read<0>();              // the snapshot store has read the dS^T tile
+        tc_commit(s2_done);
+        tc_commit(b_empty);
+        tc_commit(&do_empty[s]);
+      }
+      bulk_wait<0>();
+    }
+  } else {
+    // ------------------------------------------------------------ state warps
+    const int quarter = warp & 3, half = (warp - 2) >> 2;
+    const int v = quarter * 32 + lane;
+    const uint32_t tl = tb + (static_cast<uint32_t>(quarter * 32) << 16);
+    constexpr int NB = DK / 64;
+    const int b0 = half * NB;
+    bool ok = true;
+    auto put_bf16 = [&](int jb, const uint32_t (&r)[32]) {
+      uint8_t* base = sdt + (jb >> 1) * 16384 + v * 128;
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(base + ((((jb & 1) * 4 + u) ^ (v & 7)) * 16)) =
+            make_uint4(pack_bf16x2(__uint_as_float(r[8 * u]), __uint_as_float(r[8 * u + 1])),
+                       pack_bf16x2(__uint_as_float(r[8 * u + 2]), __uint_as_float(r[8 * u + 3])),
+                       pack_bf16x2(__uint_as_float(r[8 * u + 4]), __uint_as_float(r[8 * u + 5])),
+                       pack_bf16x2(__uint_as_float(r[8 * u + 6]), __uint_as_float(r[8 * u + 7])));
+    };
+    auto copy_state = [&]() {
+#pragma unroll 1
+      for (int jb = b0; jb < b0 + NB; ++jb) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * jb), r);
+        tmem_ld_wait();
+        put_bf16(jb, r);
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dt_ready);
+    };
+    auto scale_state = [&](long long ci) {
+      const float g = gvec ? 0.f : gC[ci];
+      const float* gv = gC + ci * DK;
+#pragma unroll 1
+      for (int jb = b0; jb < b0 + NB; ++jb) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * jb), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * (gvec ? gv[32 * jb + e] : g));
+        tmem_st_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * jb), r);
+      }
+      tmem_st_wait();
+    };
+    // initial dS^T
+#pragma unroll 1
+    for (int jb = b0; jb < b0 + NB; ++jb) {
+      uint32_t r[32];
+#pragma unroll
+      for (int e = 0; e < 32; ++e)
+        r[e] = __float_as_uint(dS_final ? dS_final[(bh * DK + 32 * jb + e) * DV + v0 + v] : 0.f);
+      tmem_st_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * jb), r);
+    }
+    tmem_st_wait();
+    for (int j = 0; j < N; ++j) {
+      const int n = N - 1 - j;
+      const long long cidx = bh * N + n;
+      copy_state();                                      // dstates_n and the operand of D1
+      scale_state(cidx);                                 // gC dS^T, before the update accumulates
+      ok = ok && mbar_wait_spin(d1_full, j & 1, abort_flag, err, kErrTimeoutEpilogue);
+      tc_fence_after();
+      uint32_t d[32];
+      tmem_ld_32x32b_x32(tl + Lt::C_D1 + static_cast<uint32_t>(32 * half), d);
+      tmem_ld_wait();
+      // VN row v, tokens 32 half .. : -dV'^T as the K-major operand of the update
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        *reinterpret_cast<uint4*>(svn + v * 128 + (((4 * half + u) ^ (v & 7)) * 16)) =
+            make_uint4(pack_bf16x2(-__uint_as_float(d[8 * u]), -__uint_as_float(d[8 * u + 1])),
+                       pack_bf16x2(-__uint_as_float(d[8 * u + 2]), -__uint_as_float(d[8 * u + 3])),
+                       pack_bf16x2(-__uint_as_float(d[8 * u + 4]), -__uint_as_float(d[8 * u + 5])),
+                       pack_bf16x2(-__uint_as_float(d[8 * u + 6]), -__uint_as_float(d[8 * u + 7])));
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(vn_ready);
+      // dU = dV' (token-major within the chunk), off the critical path
+      __nv_bfloat16* du = dU + (cidx * C + 32 * half) * DV + v0 + v;
+#pragma unroll
+      for (int c = 0; c < 32; ++c) du[(long long)c * DV] = f2bf(__uint_as_float(d[c]));
+      ok = ok && mbar_wait_spin(s2_done, j & 1, abort_flag, err, kErrTimeoutEpilogue);
+      tc_fence_after();
+    }
+    if (dS0) {
+#pragma unroll 1
+      for (int jb = b0; jb < b0 + NB; ++jb) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(tl + Lt::C_S + static_cast<uint32_t>(32 * jb), r);
+        tmem_ld_wait();
+#pragma unroll
+        for (int e = 0; e < 32; ++e) dS0[(bh * DK + 32 * jb + e) * DV + v0 + v] = __uint_as_float(r[e]);
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tb, Lt::COLS);
+  }
+}
+
 // ------------------------------------------------------------ backward scan --
 
 template <int DK>
@@ -711,7 +975,7 @@ gdr_bwd_scan(const __nv_bfloat16* __restrict__ W, const __nv_bfloat16* __restric
         }
     cp_wait_2();                              // G1(n) done (G2(n), G1(n-1) may be in flight)
     __syncthreads();
-    store_tile(dstates + cidx * DK * DV + v0, DV, &sm.dS[0][0], DVT + PAD, DK, DVT);
+    store_tile_t(dstates + (cidx * DV + v0) * DK, DK, &sm.dS[0][0], DVT + PAD, DK, DVT);
 
     // dV' = A^T dO + Kt dS  -> dU (global, via the tile), -dV' (shared)
     {
@@ -771,7 +1035,7 @@ struct ParSmem {
   __nv_bfloat16 dO[2][C][DVT + PAD];
   __nv_bfloat16 VT[2][DVT][C + PAD];     // V'^T
   __nv_bfloat16 ST[2][DVT][64 + PAD];    // S_n^T columns k0..k0+63
-  __nv_bfloat16 dS[2][64][DVT + PAD];
+  __nv_bfloat16 dST[2][DVT][64 + PAD];   // dS_n^T columns k0..k0+63
   float red[THREADS / 32];
   float rowdot[THREADS];                 // per-channel gate: per-row partial sums
 };
@@ -796,7 +1060,7 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
               (long long)H * DV, C, DVT);
     load_tile(&sm.VT[b][0][0], C + PAD, Vp + (cidx * DV + v0) * C, C, DVT, C);
     load_tile(&sm.ST[b][0][0], 64 + PAD, states + (cidx * DV + v0) * DK + k0, DK, DVT, 64);
-    load_tile(&sm.dS[b][0][0], DVT + PAD, dstates + (cidx * DK + k0) * DV + v0, DV, 64, DVT);
+    load_tile(&sm.dST[b][0][0], 64 + PAD, dstates + (cidx * DV + v0) * DK + k0, DK, DVT, 64);
   };
   float aw[1][4][4], aq[1][4][4], ak[1][4][4], aa[1][4][4];
   zero(aw); zero(aq); zero(ak); zero(aa);
@@ -813,12 +1077,12 @@ gdr_bwd_chunk(const __nv_bfloat16* __restrict__ dU, const __nv_bfloat16* __restr
     // dW = -dV' S^T, dQh = dO S^T, dKt = V' dS^T   (64 x 64 blocks, K = value)
     warp_mma<1, 4, false, true>(aw, &sm.dV[b][0][0], DVT + PAD, &sm.ST[b][0][0], 64 + PAD, wm0, wn0, DVT);
     warp_mma<1, 4, false, true>(aq, &sm.dO[b][0][0], DVT + PAD, &sm.ST[b][0][0], 64 + PAD, wm0, wn0, DVT);
-    warp_mma<1, 4, true, false>(ak, &sm.VT[b][0][0], C + PAD, &sm.dS[b][0][0], DVT + PAD, wm0, wn0, DVT);
+    warp_mma<1, 4, true, true>(ak, &sm.VT[b][0][0], C + PAD, &sm.dST[b][0][0], 64 + PAD, wm0, wn0, DVT);
     if (do_dA) warp_mma<1, 4, false, true>(aa, &sm.dO[b][0][0], DVT + PAD, &sm.VT[b][0][0], C + PAD, wm0, wn0, DVT);
     // THREADS is a multiple of 64: every pass of a thread is on key row threadIdx.x % 64
     for (int i = threadIdx.x; i < 64 * DVT; i += THREADS) {
       const int r = i % 64, c = i / 64;             // key r, value c
-      dot += bf2f(sm.ST[b][c][r]) * bf2f(sm.dS[b][r][c]);
+      dot += bf2f(sm.ST[b][c][r]) * bf2f(sm.dST[b][c][r]);
     }
     __syncthreads();
   }
@@ -869,7 +1133,7 @@ namespace tchunk {
 template <int DK>
 struct Layout {
   static constexpr int ST_BYTES = 64 * DK * 2;    // S^T block: DK/64 chunks of [64 v][64 k]
-  static constexpr int DS_BYTES = DK * 64 * 2;    // dS block: [DK k][64 v]
+  static constexpr int DS_BYTES = 64 * DK * 2;    // dS^T block: DK/64 chunks of [64 v][64 k]
   static constexpr int T_BYTES = 64 * 64 * 2;     // dO, dU: [64 c][64 v]; V'^T: [64 v][64 c]
   static constexpr int OFF_DO = 0, OFF_DU = T_BYTES, OFF_VT = 2 * T_BYTES, OFF_ST = 3 * T_BYTES;
   static constexpr int OFF_DS = OFF_ST + ST_BYTES;
@@ -941,7 +1205,8 @@ gdr_bwd_chunk_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant
         tma_load_2d(st + Lt::OFF_VT, &m_vt, &full[s], 0, static_cast<int>(cidx * DV + v0));
         for (int c = 0; c < DK / 64; ++c)
           tma_load_2d(st + Lt::OFF_ST + c * 8192, &m_st, &full[s], 64 * c, static_cast<int>(cidx * DV + v0));
-        tma_load_2d(st + Lt::OFF_DS, &m_ds, &full[s], v0, static_cast<int>(cidx * DK));
+        for (int c = 0; c < DK / 64; ++c)
+          tma_load_2d(st + Lt::OFF_DS + c * 8192, &m_ds, &full[s], 64 * c, static_cast<int>(cidx * DV + v0));
       }
       for (int vb = nvb; vb < nvb + 2; ++vb)      // the ring's last releases land before the CTA retires
         if (!mbar_wait(&empty[vb & 1], ((vb >> 1) & 1) ^ 1, abort_flag, err, kErrTimeoutProducer)) break;
@@ -949,7 +1214,8 @@ gdr_bwd_chunk_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t id_s = make_idesc_bf16(128, 64, true, false);   // A = S (MN-major), B K-major
-      constexpr uint32_t id_v = make_idesc_bf16(128, 64, false, true);   // A K-major, B = V'^T (MN-major)
+      constexpr uint32_t id_v = make_idesc_bf16(128, 64, false, true);   // A = dO K-major, B = V'^T (MN-major)
+      constexpr uint32_t id_k = make_idesc_bf16(128, 64, true, true);    // A = dS (MN-major), B = V'^T (MN-major)
       for (int vb = 0; vb < nvb; ++vb) {
         const int s = vb & 1;
         if (!mbar_wait(&full[s], (vb >> 1) & 1, abort_flag, err, kErrTimeoutMma)) break;
@@ -959,7 +1225,7 @@ gdr_bwd_chunk_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant
         const uint64_t d_du = make_sw128_desc(st + Lt::OFF_DU, 16, 1024);
         const uint64_t d_vt = make_sw128_desc(st + Lt::OFF_VT, 8192, 1024);
         const uint64_t d_st = make_sw128_desc(st + Lt::OFF_ST, 8192, 1024);
-        const uint64_t d_ds = make_sw128_desc(st + Lt::OFF_DS, 16, 1024);
+        const uint64_t d_ds = make_sw128_desc(st + Lt::OFF_DS, 8192, 1024);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {          // 16 values per step
           const uint32_t acc = (vb | kk) ? 1u : 0u;
@@ -969,7 +1235,7 @@ gdr_bwd_chunk_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant
                        acc);
             tc_mma_f16(tb + Lt::C_DQ + 64 * m, desc_add(d_st, m * 16384 + kk * 2048), desc_add(d_do, kk * 32), id_s,
                        acc);
-            tc_mma_f16(tb + Lt::C_DK + 64 * m, desc_add(d_ds, m * 16384 + kk * 32), desc_add(d_vt, kk * 2048), id_v,
+            tc_mma_f16(tb + Lt::C_DK + 64 * m, desc_add(d_ds, m * 16384 + kk * 2048), desc_add(d_vt, kk * 2048), id_k,
                        acc);
           }
           tc_mma_f16(tb + Lt::C_DA, desc_add(d_do, kk * 32), desc_add(d_vt, kk * 2048), id_v, acc);
@@ -992,17 +1258,14 @@ gdr_bwd_chunk_tc(const __grid_constant__ CUtensorMap m_st, const __grid_constant
 #pragma unroll
       for (int i = 0; i < DK / 128; ++i) {
         const int k = t + 128 * i;
-        const uint8_t* srow = st + Lt::OFF_ST + (k >> 6) * 8192 + (k & 7) * 2;
-        const uint8_t* drow = st + Lt::OFF_DS + k * 128;
+        // S^T and dS^T chunks [v][k]: row v, 16-byte unit ((k & 63) >> 3) ^ (v & 7), element k & 7
+        const int off = (k >> 6) * 8192 + (k & 7) * 2;
         float acc = 0.f;
 #pragma unroll 8
         for (int v = 0; v < 64; ++v) {
-          // S^T chunk [v][k]: row v, 16-byte unit ((k & 63) >> 3) ^ (v & 7); dS [k][v]: row k, unit (v >> 3) ^ (k & 7)
-          const float sv = bf2f(*reinterpret_cast<const __nv_bfloat16*>(
-              srow + v * 128 + (((((k & 63) >> 3)) ^ (v & 7)) * 16)));
-          const float dv = bf2f(*reinterpret_cast<const __nv_bfloat16*>(
-              drow + (((v >> 3) ^ (k & 7)) * 16) + (v & 7) * 2));
-          acc = fmaf(sv, dv, acc);
+          const int o = off + v * 128 + ((((k & 63) >> 3) ^ (v & 7)) * 16);
+          acc = fmaf(bf2f(*reinterpret_cast<const __nv_bfloat16*>(st + Lt::OFF_ST + o)),
+                     bf2f(*reinterpret_cast<const __nv_bfloat16*>(st + Lt::OFF_DS + o)), acc);
         }
         dot[i] += acc;
       }
@@ -1175,11 +1438,37 @@ template <int DK>
 int launch_bwd(const GdrRecBwdArgs& a, cudaStream_t st) {
   const size_t s1 = sizeof(BwdScanSmem<DK>), s2 = sizeof(ParSmem);
   if (!set_smem(gdr_bwd_scan<DK>, s1) || !set_smem(gdr_bwd_chunk, s2)) return 3;
+  static const bool no_tc_scan = std::getenv("VAGUS_GDR_NO_TC") != nullptr;
+  if (!no_tc_scan && a.f.err && a.f.DV % tbscan::VT == 0) {
+    using Lt = tbscan::Layout<DK>;
+    alignas(64) unsigned char m_kt[128], m_qh[128], m_w[128], m_a[128], m_do[128], m_ds[128];
+    const unsigned long long BHN = (unsigned long long)a.f.BH * a.f.N;
+    const unsigned long long d_k[2] = {(unsigned long long)DK, BHN * C}, s_k[1] = {(unsigned long long)DK * 2};
+    const unsigned long long d_a[2] = {(unsigned long long)C, BHN * C}, s_a[1] = {(unsigned long long)C * 2};
+    const unsigned long long d_ds[2] = {(unsigned long long)DK, BHN * a.f.DV};
+    const unsigned long long d_do[3] = {(unsigned long long)a.f.DV, (unsigned long long)a.f.H,
+                                        (unsigned long long)(a.f.BH / a.f.H) * a.f.N * C};
+    const unsigned long long s_do[2] = {(unsigned long long)a.f.DV * 2, (unsigned long long)a.f.H * a.f.DV * 2};
+    const unsigned box64[2] = {64u, 64u}, box_ds[2] = {64u, static_cast<unsigned>(tbscan::VT)},
+                   box_do[3] = {64u, 1u, 64u};
+    if (!encode_bf16_map(m_kt, a.f.Kt, 2, d_k, s_k, box64) || !encode_bf16_map(m_qh, a.f.Qh, 2, d_k, s_k, box64) ||
+        !encode_bf16_map(m_w, a.f.W, 2, d_k, s_k, box64) || !encode_bf16_map(m_a, a.f.A, 2, d_a, s_a, box64) ||
+        !encode_bf16_map(m_do, a.dO, 3, d_do, s_do, box_do) ||
+        !encode_bf16_map(m_ds, a.dstates, 2, d_ds, s_k, box_ds))
+      return 2;
+    if (!set_smem(gdr_bwd_scan_tc<DK>, Lt::SMEM)) return 3;
+    gdr_bwd_scan_tc<DK><<<static_cast<unsigned>(a.f.BH * (a.f.DV / tbscan::VT)), 320, Lt::SMEM, st>>>(
+        *reinterpret_cast<const CUtensorMap*>(m_kt), *reinterpret_cast<const CUtensorMap*>(m_qh),
+        *reinterpret_cast<const CUtensorMap*>(m_w), *reinterpret_cast<const CUtensorMap*>(m_a),
+        *reinterpret_cast<const CUtensorMap*>(m_do), *reinterpret_cast<const CUtensorMap*>(m_ds), a.f.gC,
+        a.dS_final, (__nv_bfloat16*)a.dU, a.dS0, a.f.N, a.f.DV, a.f.H, a.f.gvec, a.f.err);
+  } else {
   const int grid = static_cast<int>(a.f.BH * (a.f.DV / DVT));
   gdr_bwd_scan<DK><<<grid, THREADS, s1, st>>>((const __nv_bfloat16*)a.f.W, (const __nv_bfloat16*)a.f.Qh,
                                               (const __nv_bfloat16*)a.f.Kt, (const __nv_bfloat16*)a.f.A, a.f.gC,
                                               (const __nv_bfloat16*)a.dO, a.dS_final, (__nv_bfloat16*)a.dU,
                                               (__nv_bfloat16*)a.dstates, a.dS0, a.f.N, a.f.DV, a.f.H, a.f.gvec);
+  }
   static const bool no_tc = std::getenv("VAGUS_GDR_NO_TC") != nullptr;
   if (!no_tc && a.f.err && a.f.DV % 64 == 0) {
     using Lt = tchunk::Layout<DK>;
@@ -1187,7 +1476,7 @@ int launch_bwd(const GdrRecBwdArgs& a, cudaStream_t st) {
     const unsigned long long BHN = (unsigned long long)a.f.BH * a.f.N;
     const unsigned long long d_st[2] = {(unsigned long long)DK, BHN * a.f.DV};
     const unsigned long long s_st[1] = {(unsigned long long)DK * 2};
-    const unsigned long long d_ds[2] = {(unsigned long long)a.f.DV, BHN * DK};
+    const unsigned long long d_ds[2] = {(unsigned long long)DK, BHN * a.f.DV};
     const unsigned long long d_du[2] = {(unsigned long long)a.f.DV, BHN * C};
     const unsigned long long s_dv[1] = {(unsigned long long)a.f.DV * 2};
     const unsigned long long d_vt[2] = {(unsigned long long)C, BHN * a.f.DV};
@@ -1196,9 +1485,9 @@ int launch_bwd(const GdrRecBwdArgs& a, cudaStream_t st) {
     const unsigned long long d_do[3] = {(unsigned long long)a.f.DV, (unsigned long long)a.f.H,
                                         (unsigned long long)(a.f.BH / a.f.H) * a.f.N * C};
     const unsigned long long s_do[2] = {(unsigned long long)a.f.DV * 2, (unsigned long long)a.f.H * a.f.DV * 2};
-    const unsigned box64[2] = {64u, 64u}, box_ds[2] = {64u, static_cast<unsigned>(DK)}, box_do[3] = {64u, 1u, 64u};
+    const unsigned box64[2] = {64u, 64u}, box_do[3] = {64u, 1u, 64u};
     if (!encode_bf16_map(m_st, a.f.states, 2, d_st, s_st, box64) ||
-        !encode_bf16_map(m_ds, a.dstates, 2, d_ds, s_dv, box_ds) ||
+        !encode_bf16_map(m_ds, a.dstates, 2, d_ds, s_st, box64) ||
         !encode_bf16_map(m_du, a.dU, 2, d_du, s_dv, box64) || !encode_bf16_map(m_vt, a.f.Vp, 2, d_vt, s_vt, box64) ||
         !encode_bf16_map(m_do, a.dO, 3, d_do, s_do, box_do))
       return 2;

@@ -80,7 +80,7 @@ struct GdrRecBwdArgs {
   void* dU;                                        // (BH, N, C, DV) bf16
   float* dgC;                                      // (BH, N) fp32, zero-initialised (atomics)
   float* dS0;                                      // (BH, DK, DV) or null
-  void* dstates;                                   // (BH, N, DK, DV) bf16 scratch: dL/dS per chunk
+  void* dstates;                                   // (BH, N, DV, DK) bf16 scratch: (dL/dS_{n+1})^T per chunk
 };
 int gdr_rec_bwd(const GdrRecBwdArgs& a, cudaStream_t st);
 // gdr_intra.cu: intra-chunk WY / UT stage (scalar gate), forward + backward.
