@@ -77,26 +77,6 @@ __device__ __forceinline__ float ex2_approx(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
-// 2^x on the FMA / integer pipes, for splitting exponential work with the
-// MUFU unit: Cody-Waite style split x = n + f (n = round(x) through the
-// 1.5 * 2^23 rounding constant, f in [-0.5, 0.5]), 2^f by its Taylor series
-// e^(f ln 2) = sum_k (f ln 2)^k / k! to degree 4 (relative error < 5e-5 on
-// the interval), and 2^n added into the exponent bits.  Inputs below -125
-// are clamped there (the result is < 1e-37).
-__device__ __forceinline__ float ex2_poly(float x) {
-  constexpr float c1 = 0.6931471805599453f;      // ln2
-  constexpr float c2 = 0.2402265069591007f;      // ln2^2 / 2
-  constexpr float c3 = 0.0555041086648216f;      // ln2^3 / 6
-  constexpr float c4 = 0.0096181291076285f;      // ln2^4 / 24
-  constexpr float kRound = 12582912.f;           // 1.5 * 2^23
-  x = fmaxf(x, -125.f);
-  const float t = x + kRound;
-  const int n = __float_as_int(t) - __float_as_int(kRound);
-  const float f = x - (t - kRound);
-  const float q = fmaf(fmaf(fmaf(fmaf(c4, f, c3), f, c2), f, c1), f, 1.f);
-  return __int_as_float(__float_as_int(q) + (n << 23));
-}
-
 __device__ __forceinline__ float softplus_f(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
 
 // ------------------------------------------------------------ smem addr --
