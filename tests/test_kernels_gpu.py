@@ -460,3 +460,33 @@ def test_rmsnorm_backward_wide_rows(D):
     assert rel(dx, xr.grad + dres) < 1e-4
     assert rel(dg, gr.grad) < 1e-4
     assert rel(dx16.float(), dx) < 1e-2
+
+
+@pytest.mark.parametrize("mode", [1, 2])
+def test_gemm_scatter_epilogue(mode):
+    """The scatter epilogue (the fused Newton-Schulz product + all-to-all of
+    sharded Muon) on one GPU: destinations are blocks of one local buffer;
+    every row (mode 1) or column (mode 2) block lands where its owner reads
+    it, bit-identical to the plain GEMM with the same alpha / beta epilogue."""
+    from vagus_b200.ops import native
+    nb, M, K, N, world = 3, 256, 192, 512, 4
+    A = torch.randn(nb, M, M, device=DEV).bfloat16()
+    X = torch.randn(nb, M, N, device=DEV).bfloat16()
+    ref = torch.empty(nb, M, N, device=DEV, dtype=torch.bfloat16)
+    _g(A, False, X, True, ref, X, 1.0, 0.5, False, 1, 0)          # B X + 0.5 X
+    span = (M if mode == 1 else N) // world
+    if mode == 1:
+        recv = torch.zeros(world, nb + 2, span, N, device=DEV, dtype=torch.bfloat16)
+        ld, stride = N, span * N
+    else:
+        recv = torch.zeros(world, nb + 2, M, span, device=DEV, dtype=torch.bfloat16)
+        ld, stride = span, M * span
+    dst = [recv[o].data_ptr() for o in range(world)]
+    rc = native().gemm_scatter(A, False, X, True, X, 1.0, 0.5, dst, mode, span, ld, stride, 2)
+    assert rc == 0, rc
+    torch.cuda.synchronize()
+    for o in range(world):
+        got = recv[o, 2:2 + nb]
+        want = ref[:, o * span:(o + 1) * span] if mode == 1 else ref[:, :, o * span:(o + 1) * span]
+        assert torch.equal(got, want), (mode, o)
+        assert recv[o, :2].abs().sum() == 0                           # batch offset respected
