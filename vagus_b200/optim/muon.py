@@ -197,13 +197,15 @@ def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_de
             off = sizes.get(id(group), 0)
             fused[j] = (off, chunk)
             sizes[id(group)] = off + MuonExchange.block_bytes(chunk * ws, rows // ws, cols)
+        from ..parallel.nvlink import same_host
         for j, (shape, dtype, device, idx, group, ws, rank) in enumerate(plan):
             if j in fused and id(group) not in exchanges:
-                exchanges[id(group)] = MuonExchange(group, sizes[id(group)])
+                # CUDA IPC reaches the GPUs of one machine only
+                exchanges[id(group)] = MuonExchange(group, sizes[id(group)]) if same_host(group) else None
         for j in list(fused):
             ex = exchanges[id(plan[j][4])]
-            if ex.slot_bytes < sizes[id(plan[j][4])]:
-                del fused[j]            # the buckets grew past the heap: all-gather this step
+            if ex is None or ex.slot_bytes < sizes[id(plan[j][4])]:
+                del fused[j]            # another machine in the group, or the buckets outgrew the heap
     pending = []
     for j, (shape, dtype, device, idx, group, ws, rank) in enumerate(plan):
         rows, cols = shape

@@ -41,6 +41,22 @@ from ..ops import native
 HEADER = 1024                      # flag words, as comm.cu lays them out
 
 
+_SAME_HOST: dict = {}
+
+
+def same_host(group) -> bool:
+    """True when every rank of ``group`` runs on this machine (CUDA IPC, and
+    so these kernels, only reach GPUs of one node).  Collective over the
+    group; cached per group."""
+    key = id(group)
+    if key not in _SAME_HOST:
+        import socket
+        names = [None] * dist.get_world_size(group)
+        dist.all_gather_object(names, socket.gethostname(), group=group)
+        _SAME_HOST[key] = len(set(names)) == 1
+    return _SAME_HOST[key]
+
+
 class NvlinkHeap:
     """One IPC-shared device heap per rank of ``group``: 2 all-gather slots of
     ``ag_cap`` bytes and 2 reduce-scatter slots of ``rs_cap`` bytes."""
@@ -142,9 +158,12 @@ def _unit_sizes(root, world: int):
 
 def use_nvlink_collectives(root, group=None) -> NvlinkHeap:
     """Install the NVLink collectives on every FSDP unit under ``root``
-    (after ``fully_shard``).  Returns the heap (keep it alive)."""
+    (after ``fully_shard``).  Returns the heap (keep it alive), or None when
+    the group spans several machines (NCCL stays in place)."""
     from torch.distributed.fsdp import FSDPModule
     group = group or dist.group.WORLD
+    if not same_host(group):
+        return None                      # ranks on several machines: FSDP2 keeps NCCL
     world = dist.get_world_size(group)
     biggest = _unit_sizes(root, world)
     heap = NvlinkHeap(group, ag_cap=(biggest // world + 64) * 4, rs_cap=(biggest + 64 * world) * 4)
