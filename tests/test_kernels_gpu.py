@@ -490,3 +490,29 @@ def test_gemm_scatter_epilogue(mode):
         want = ref[:, o * span:(o + 1) * span] if mode == 1 else ref[:, :, o * span:(o + 1) * span]
         assert torch.equal(got, want), (mode, o)
         assert recv[o, :2].abs().sum() == 0                           # batch offset respected
+
+
+def test_bounded_wait_timeout_reports_and_context_survives():
+    """Failure detection on the device without a fault: the cross-GPU epoch
+    barrier waits for a peer flag that nothing sets (a second heap in this
+    process stands in for a peer that never arrives), gives up after its
+    budget, records kErrTimeoutPeer in the host-mapped error word and returns;
+    the host raises on it, and the context keeps working."""
+    import time
+    from vagus_b200 import ops
+    C = ops.native()
+    h0, _ = C.comm_heap_create(4096)
+    h1, _ = C.comm_heap_create(4096)
+    t0 = time.time()
+    C.comm_barrier([h0, h1], 0, 1)
+    torch.cuda.synchronize()
+    waited = time.time() - t0
+    assert C.error_word() == 4, C.error_word()          # kErrTimeoutPeer
+    assert 0.5 < waited < 60, waited
+    with pytest.raises(RuntimeError):
+        ops.check_error()
+    assert C.error_word() == 0
+    a = torch.randn(256, 256, device=DEV)
+    assert torch.allclose(a @ a, (a.double() @ a.double()).float(), rtol=1e-3, atol=1e-3)
+    C.comm_heap_close(h0, True)
+    C.comm_heap_close(h1, True)

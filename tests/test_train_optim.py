@@ -154,3 +154,80 @@ def test_muon_exchange_eligibility_and_layout():
     assert not MuonExchange.eligible((1024, 1024), 2, torch.device("cpu"))
     assert MuonExchange.block_bytes(4, 128, 1024) == 4 * 128 * 1024 * 2
     assert MuonExchange.block_bytes(3, 10, 10) % 256 == 0
+
+
+def test_unreadable_recent_checkpoint_falls_back(tmp_path):
+    """Failure injection on the host: a truncated recent.pt is reported and
+    skipped; the run resumes from the newest readable checkpoint and finishes
+    with the same weights as the uninterrupted run."""
+    run_a = tm.train(_config(tmp_path, "a", 6, permanent_ckpt_interval=3))
+    run_b = tmp_path / "b"
+    run_b.mkdir()
+    shutil.copy(run_a / "ckpt-00000003.pt", run_b / "ckpt-00000003.pt")
+    good = (run_a / "ckpt-00000006.pt").read_bytes()
+    (run_b / "recent.pt").write_bytes(good[: len(good) // 3])          # torn file
+    tm.train(_config(tmp_path, "b", 6, permanent_ckpt_interval=3))
+    a = torch.load(run_a / "ckpt-00000006.pt", weights_only=False)
+    b = torch.load(run_b / "ckpt-00000006.pt", weights_only=False)
+    for k in a["model"]:
+        assert torch.equal(a["model"][k], b["model"][k]), k
+
+
+def test_walltime_deadline_stops_with_checkpoint(tmp_path, monkeypatch):
+    """Failure injection on the host: a job end time already inside the
+    deadline margin stops the run after its first step, by rank consensus,
+    with the recent checkpoint written and no final model."""
+    import time
+    monkeypatch.setenv("SLURM_JOB_END_TIME", str(time.time() + 5.0))
+    run = tm.train(_config(tmp_path, "d", 10, deadline_margin_s=60.0))
+    state = torch.load(run / "recent.pt", weights_only=False)
+    assert state["step"] == 1
+    assert not (run / "model-final.pt").exists()
+
+
+def _dead_rank_worker(rank, port, q):
+    import datetime
+    import os
+    import time
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=10))
+    t = torch.ones(4)
+    dist.all_reduce(t)                       # one healthy step
+    def report(msg):
+        q.put((rank, msg))
+        q.close()
+        q.join_thread()                      # flushed before the hard exit below
+
+    if rank == 1:
+        report("left")
+        os._exit(0)                          # this rank dies between steps, without a goodbye
+    t0 = time.time()
+    try:
+        dist.all_reduce(t)
+        report("no error")
+    except Exception as e:                   # noqa: BLE001 -- the failure this test injects
+        report(f"detected after {time.time() - t0:.1f}s: {type(e).__name__}")
+    os._exit(0)
+
+
+def test_dead_rank_is_detected_by_the_next_collective():
+    """Failure injection among CPU ranks: a gloo rank that exits between
+    steps makes the survivor's next collective fail with an error (within the
+    process-group timeout) instead of hanging."""
+    import socket
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_dead_rank_worker, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=120) for _ in range(2))
+    for p in procs:
+        p.join(timeout=60)
+    assert out[1] == "left"
+    assert out[0].startswith("detected"), out[0]

@@ -174,12 +174,27 @@ def save_checkpoint(run_dir: Path, kind: str, step: int, tokens_seen: int, model
     return path
 
 
+def resume_candidates(run_dir: Path) -> list[Path]:
+    """Checkpoints to resume from, best first: recent.pt, recent-prev.pt, then
+    the permanent checkpoints newest first."""
+    out = [run_dir / n for n in ("recent.pt", "recent-prev.pt") if (run_dir / n).exists()]
+    return out + sorted(run_dir.glob("ckpt-*.pt"), reverse=True)
+
+
 def find_resume(run_dir: Path) -> Path | None:
-    for name in ("recent.pt", "recent-prev.pt"):
-        if (run_dir / name).exists():
-            return run_dir / name
-    ckpts = sorted(run_dir.glob("ckpt-*.pt"))
-    return ckpts[-1] if ckpts else None
+    c = resume_candidates(run_dir)
+    return c[0] if c else None
+
+
+def load_first_readable(cands: list[Path], log=print) -> tuple[Path, dict]:
+    """The first candidate that loads; an unreadable file (truncated, corrupt)
+    is reported and the next one is tried."""
+    for p in cands:
+        try:
+            return p, torch.load(p, map_location="cpu", weights_only=False)
+        except Exception as e:  # noqa: BLE001 -- any failure to read means: try the older file
+            log(f"checkpoint {p.name} is unreadable ({type(e).__name__}: {e}); trying the next")
+    raise RuntimeError(f"no readable checkpoint among {[p.name for p in cands]}")
 
 
 # ------------------------------------------------------------------- training --
@@ -352,7 +367,7 @@ def train(config: TrainConfig, teardown: bool = True):
     if resume_from is not None:
         state: dict = {}
         if is_main or not is_fsdp:
-            state = torch.load(resume_from, map_location="cpu", weights_only=False)
+            resume_from, state = load_first_readable(resume_candidates(run_dir), log)
             assert state["config"]["model_args"] == config.model_args, "checkpoint model_args differ from config"
         load_state(model, optimizer, state, is_fsdp)
         small = [{k: state[k] for k in ("step", "tokens_seen", "loader", "rng")} if state else None]
