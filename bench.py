@@ -48,7 +48,7 @@ CONFIGS = {
         model_args=dict(vocab_size=32000, dim=1024, layer_count=24, head_count=4, key_head_dim=256,
                         value_head_dim=256, ffn_hidden_dim=2816, short_conv_size=4, gate="scalar", delta=True,
                         chunk_size=64, context_len=4096, la_impl="auto"),
-        seq=4096, global_tokens=524288, micro=8, label="340M GDN (4x256, chunk 64), FSDP2+Muon"),
+        seq=4096, global_tokens=524288, micro=16, label="340M GDN (4x256, chunk 64), FSDP2+Muon"),
     # BASELINE config #5
     "hybrid1.3b": dict(
         model_name="GDNLM",
