@@ -126,3 +126,4 @@ int kda_gated_bwd(const float* Q, const float* K, const float* G, const float* d
 }
 
 }  // namespace vagus
+
