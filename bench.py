@@ -1,5 +1,5 @@
 """Headline benchmark: training tokens/s of the 340M gated-DeltaNet LM
-(BASELINE config #3) -- vocab 32000, d_model 1024, 24 layers, 4 heads x 256,
+-- vocab 32000, d_model 1024, 24 layers, 4 heads x 256,
 short conv 4, output gate, chunk 64, SwiGLU 2816, seq 4096, 0.5M tokens per
 optimizer step (Muon + AdamW), synthetic uniform-random tokens, random init.
 
@@ -42,14 +42,14 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 
 CONFIGS = {
-    # BASELINE config #3 (headline)
+    # the headline benchmark: 340M GDN, FSDP2 + Muon
     "gdn340m": dict(
         model_name="GDNLM",
         model_args=dict(vocab_size=32000, dim=1024, layer_count=24, head_count=4, key_head_dim=256,
                         value_head_dim=256, ffn_hidden_dim=2816, short_conv_size=4, gate="scalar", delta=True,
                         chunk_size=64, context_len=4096, la_impl="auto"),
         seq=4096, global_tokens=524288, micro=16, label="340M GDN (4x256, chunk 64), FSDP2+Muon"),
-    # BASELINE config #5
+    # 1.3B hybrid GDN/softmax 3:1, FSDP2 + sharded Muon
     "hybrid1.3b": dict(
         model_name="GDNLM",
         model_args=dict(vocab_size=32000, dim=2048, layer_count=24, head_count=8, key_head_dim=256,
@@ -57,7 +57,7 @@ CONFIGS = {
                         chunk_size=64, layer_pattern="gdn,gdn,gdn,softmax", softmax_head_dim=128,
                         context_len=4096, la_impl="auto"),
         seq=4096, global_tokens=1048576, micro=4, label="1.3B hybrid GDN/softmax 3:1"),
-    # BASELINE config #4 (recipe/model/kda_hybrid_340M.yaml)
+    # 340M hybrid KDA/softmax 3:1 (recipe/model/kda_hybrid_340M.yaml)
     "kda_hybrid340m": dict(
         model_name="GDNLM",
         model_args=dict(vocab_size=32000, dim=1024, layer_count=24, head_count=4, key_head_dim=128,
@@ -65,7 +65,7 @@ CONFIGS = {
                         delta=True, chunk_size=64, layer_pattern="gdn,gdn,gdn,softmax", softmax_head_dim=64,
                         softmax_rope=True, context_len=4096, la_impl="auto"),
         seq=4096, global_tokens=524288, micro=8, label="340M hybrid KDA/softmax 3:1"),
-    # BASELINE config #2
+    # 340M Transformer++, AdamW
     "tpp340m": dict(
         model_name="TransformerPP",
         model_args=dict(vocab_size=32000, dim=1024, head_dim=64, context_len=4096, layer_count=24,
@@ -80,7 +80,7 @@ CONFIGS = {
 }
 
 # Configurations whose reference stock path faulted the GPU on this pool: they
-# are not run again (the fault is recorded in DESIGN.md).
+# are not run again; each entry says what ran and how it failed.
 REFERENCE_FAULTS = {
     "gdn340m": ("reference stock path (fla chunk_gated_delta_rule, head_dim 256) raised CUDA 'misaligned address' "
                 "in fla prepare_wy_repr_bwd (Triton autotune) on B200; not re-run under the GPU-fault policy"),
