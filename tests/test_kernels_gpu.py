@@ -282,6 +282,37 @@ def test_kda_chunk_fwd_bwd(dk, dv, L):
         assert rel(a.grad, b.grad) < 5e-2, (name, rel(a.grad, b.grad))
 
 
+@pytest.mark.parametrize("gate,delta", [("scalar", False), ("vector", False), ("none", True), ("none", False)])
+def test_gla_and_deltanet_chunk_fwd_bwd(gate, delta):
+    """The other members of the family on the same kernels -- gated linear
+    attention (no delta rule) and DeltaNet (no gate) -- against the fp32
+    chunk oracle, outputs, final state and input gradients."""
+    from vagus_b200 import ops
+    from vagus_b200.models.scans import chunk_scan
+    B, L, H, dk, dv = 2, 192, 2, 128, 128
+    q, k, v, _, beta = _gdr_inputs(B, L, H, dk, dv)
+    g = None
+    if gate == "scalar":
+        g = F.logsigmoid(torch.randn(B, L, H, device=DEV) + 2) * 0.5
+    elif gate == "vector":
+        g = F.logsigmoid(torch.randn(B, L, H, dk, device=DEV) + 2) * 0.5
+    S0 = 0.1 * torch.randn(B, H, dk, dv, device=DEV)
+    scale = dk ** -0.5
+    ins = [t.bfloat16().float() for t in (q, k, v)] + [S0]
+    ref_in = [t.clone().requires_grad_(True) for t in ins]
+    o_r, S_r = chunk_scan(ref_in[0], ref_in[1], ref_in[2], g, beta if delta else None, ref_in[3], scale=scale,
+                          delta=delta, chunk_size=64)
+    cu_in = [t.clone().requires_grad_(True) for t in ins]
+    o, S = ops.kda_chunk(cu_in[0].bfloat16(), cu_in[1].bfloat16(), cu_in[2].bfloat16(), g,
+                         beta if delta else None, cu_in[3], scale=scale, delta=delta)
+    assert rel(o, o_r) < 2e-2 and rel(S, S_r) < 2e-2, (rel(o, o_r), rel(S, S_r))
+    do, dS = torch.randn_like(o_r), torch.randn_like(S_r)
+    ((o_r * do).sum() + (S_r * dS).sum()).backward()
+    ((o.float() * do).sum() + (S * dS).sum()).backward()
+    for name, a, b in zip("q k v S0".split(), cu_in, ref_in):
+        assert rel(a.grad, b.grad) < 5e-2, (name, rel(a.grad, b.grad))
+
+
 @pytest.mark.parametrize("dk,dv", [(128, 128), (256, 256), (128, 256)])
 def test_gdr_intra_kernel_matches_torch(dk, dv):
     from vagus_b200.ops import native

@@ -18,10 +18,11 @@ Execution on CUDA (``impl`` 'auto'/'cuda'): the forward of a scalar-gate delta
 layer runs as sm_100a kernels -- one projection GEMM for q/k/v/g, one fused
 short-conv+SiLU+L2norm kernel, the gate/beta kernel, the chunked gated
 delta-rule kernel and the fused RMSNorm*SiLU(gate) kernel -- see
-``vagus_b200.ops.gdn``.  A vector-gate (KDA) delta layer runs its intra-chunk
-stage chunk-parallel in torch and its state recurrence on the same kernels
-(``vagus_b200.ops.kda``).  Everything else (CPU, fp64 tests, Kalman writes)
-runs the pure-torch chunk oracle of ``models.scans``.
+``vagus_b200.ops.gdn``.  The other variants on CUDA -- per-channel gate (KDA),
+no gate (DeltaNet), no delta rule (gated linear attention) -- run their
+intra-chunk stage chunk-parallel in torch and the state recurrence on the
+same kernels (``vagus_b200.ops.kda``).  Everything else (CPU, fp64 tests,
+Kalman writes) runs the pure-torch chunk oracle of ``models.scans``.
 
 Parity: reference ``infra/components/linear_attention.py:505-952``.
 """
@@ -196,8 +197,11 @@ class GatedDeltaNet(nn.Module, Mixer):
                                   chunk_size=self.chunk_size, w=w)
         if self._use_kernels(q) and self.gate == "scalar" and self.delta:
             return ops.gdr_chunk(q, k, v, g, beta, S0, scale=self.scale, chunk_size=self.chunk_size)
-        if self._use_kernels(q) and self.gate == "vector" and self.delta:
-            return ops.kda_chunk(q, k, v, g, beta, S0, scale=self.scale, chunk_size=self.chunk_size)
+        if self._use_kernels(q):
+            # per-channel gate, no gate (DeltaNet), or no delta rule (gated linear attention):
+            # the chunk-parallel intra stage in torch + gated products and the recurrence on the kernels
+            return ops.kda_chunk(q, k, v, g, beta, S0, scale=self.scale, chunk_size=self.chunk_size,
+                                 delta=self.delta)
         return chunk_scan(q, k, v, g, beta, S0, scale=self.scale, delta=self.delta,
                           chunk_size=self.chunk_size)
 

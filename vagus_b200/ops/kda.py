@@ -81,32 +81,36 @@ class _GatedProducts(torch.autograd.Function):
         return dQ, dK, dG
 
 
-def kda_intra(q, k, v, g, beta, scale: float):
+def kda_intra(q, k, v, g, beta, scale: float, delta: bool = True):
     """(W, Qh, Kt, A, U, gamma) of every chunk, fp32, (B, H, N, C, .) layout;
-    q, k (B, L, H, dk), v (B, L, H, dv), g (B, L, H, dk) log decay, beta (B, L, H)."""
+    q, k (B, L, H, dk), v (B, L, H, dv), g (B, L, H, dk) log decay, beta (B, L, H).
+    Without the delta rule (gated linear attention: S <- diag(gamma) S + Kt^T V)
+    W is zero and U = V, so the same recurrence kernels apply."""
     B, L, H, dk = q.shape
     dv = v.shape[-1]
     N = L // CHUNK
     to_c = lambda t, d: t.float().reshape(B, N, CHUNK, H, d).permute(0, 3, 1, 2, 4)   # noqa: E731
     Q, K, V = to_c(q, dk), to_c(k, dk), to_c(v, dv)
     gam = to_c(g, dk).cumsum(3)                                  # (B, H, N, C, dk)
-    b = beta.float().reshape(B, N, CHUNK, H).permute(0, 3, 1, 2)[..., None]   # (B, H, N, C, 1)
     if q.is_cuda:
         Aqk, Akk = _GatedProducts.apply(Q, K, gam)
     else:
         Aqk, Akk = _gated(Q, K, gam, strict=False), _gated(K, K, gam, strict=True)
+    G = gam.exp()
+    Qh = Q * G * scale
+    Kt = K * (gam[..., -1:, :] - gam).exp()
+    A = Aqk * scale
+    if not delta:
+        return torch.zeros_like(K), Qh, Kt, A, V, G[..., -1, :]
+    b = beta.float().reshape(B, N, CHUNK, H).permute(0, 3, 1, 2)[..., None]   # (B, H, N, C, 1)
     Akk = Akk * b
     Tm = Akk + torch.eye(CHUNK, device=q.device, dtype=Akk.dtype)
-    G = gam.exp()
     # T = (I + M)^-1 once (64 right-hand sides), then one batched product for
     # both W and U: far cheaper than a triangular solve with dk + dv columns
     eye = torch.eye(CHUNK, device=q.device, dtype=Akk.dtype).expand_as(Tm)
     T = torch.linalg.solve_triangular(Tm, eye, upper=False, unitriangular=True)
     WU = T @ torch.cat([b * K * G, b * V], dim=-1)
     W, U = WU[..., :dk], WU[..., dk:]
-    Qh = Q * G * scale
-    Kt = K * (gam[..., -1:, :] - gam).exp()
-    A = Aqk * scale
     return W, Qh, Kt, A, U, G[..., -1, :]
 
 
@@ -140,16 +144,24 @@ class _KDARec(torch.autograd.Function):
                 dS0.view(B, Hh, dk, dv) if ctx.has_S0 else None, None)
 
 
-def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64):
+def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64, delta: bool = True):
     """Chunked delta rule with a per-channel gate g (B, L, H, dk) (log decay)
-    on CUDA.  Returns (o (B, L, H, dv) bf16, S (B, H, dk, dv) fp32)."""
+    on CUDA; ``delta=False`` is gated linear attention (beta unused), and a
+    scalar gate (B, L, H) or no gate (None) is broadcast over the channels.
+    Returns (o (B, L, H, dv) bf16, S (B, H, dk, dv) fp32)."""
     assert chunk_size == CHUNK, "the sm_100a recurrence runs 64-token chunks"
     B, L, H, dk = q.shape
+    if g is None:
+        g = torch.zeros(B, L, H, dk, device=q.device, dtype=torch.float32)
+    elif g.dim() == 3:
+        g = g.float()[..., None].expand(B, L, H, dk)
+    if beta is None:
+        beta = torch.zeros(B, L, H, device=q.device, dtype=torch.float32)
     pad = (-L) % CHUNK
     if pad:
         # zero gate and zero write strength: padded tokens leave the state alone
         pz = lambda t: torch.nn.functional.pad(t, [0, 0] * (t.dim() - 2) + [0, pad])   # noqa: E731
         q, k, v, g, beta = pz(q), pz(k), pz(v), pz(g), pz(beta)
-    parts = kda_intra(q, k, v, g, beta, scale)
+    parts = kda_intra(q, k, v, g, beta, scale, delta)
     o, S = _KDARec.apply(*parts, S0, H)
     return (o[:, :L] if pad else o), S
