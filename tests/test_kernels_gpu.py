@@ -282,6 +282,32 @@ def test_kda_chunk_fwd_bwd(dk, dv, L):
         assert rel(a.grad, b.grad) < 5e-2, (name, rel(a.grad, b.grad))
 
 
+def test_asymmetric_write_chunk_fwd_bwd():
+    """An explicit write vector (the Kalman diagonal gain's asymmetric write)
+    on the recurrence kernels vs the fp32 chunk oracle, incl. gradients."""
+    from vagus_b200 import ops
+    from vagus_b200.models.scans import chunk_scan_vec
+    B, L, H, dk, dv = 2, 160, 2, 128, 128
+    q, k, v, _, _ = _gdr_inputs(B, L, H, dk, dv)
+    g = F.logsigmoid(torch.randn(B, L, H, dk, device=DEV) + 2) * 0.5
+    w = 0.5 * torch.rand(B, L, H, dk, device=DEV) * k.float()
+    S0 = 0.1 * torch.randn(B, H, dk, dv, device=DEV)
+    scale = dk ** -0.5
+    ins = [t.bfloat16().float() for t in (q, k, v)] + [g, w, S0]
+    ref_in = [t.clone().requires_grad_(True) for t in ins]
+    o_r, S_r = chunk_scan_vec(ref_in[0], ref_in[1], ref_in[2], ref_in[3], None, ref_in[5], scale=scale,
+                              delta=True, chunk_size=64, w=ref_in[4])
+    cu_in = [t.clone().requires_grad_(True) for t in ins]
+    o, S = ops.kda_chunk(cu_in[0].bfloat16(), cu_in[1].bfloat16(), cu_in[2].bfloat16(), cu_in[3], None, cu_in[5],
+                         scale=scale, w=cu_in[4])
+    assert rel(o, o_r) < 2e-2 and rel(S, S_r) < 2e-2, (rel(o, o_r), rel(S, S_r))
+    do, dS = torch.randn_like(o_r), torch.randn_like(S_r)
+    ((o_r * do).sum() + (S_r * dS).sum()).backward()
+    ((o.float() * do).sum() + (S * dS).sum()).backward()
+    for name, a, b in zip("q k v g w S0".split(), cu_in, ref_in):
+        assert rel(a.grad, b.grad) < 5e-2, (name, rel(a.grad, b.grad))
+
+
 @pytest.mark.parametrize("gate,delta", [("scalar", False), ("vector", False), ("none", True), ("none", False)])
 def test_gla_and_deltanet_chunk_fwd_bwd(gate, delta):
     """The other members of the family on the same kernels -- gated linear
@@ -547,3 +573,56 @@ def test_bounded_wait_timeout_reports_and_context_survives():
     assert torch.allclose(a @ a, (a.double() @ a.double()).float(), rtol=1e-3, atol=1e-3)
     C.comm_heap_close(h0, True)
     C.comm_heap_close(h1, True)
+
+
+@pytest.mark.parametrize("b,L,rest", [(2, 1000, (3,)), (3, 257, (4, 37)), (1, 4096, (2, 128)), (2, 5, (1,))])
+def test_mobius_scan_kernel_fwd_bwd(b, L, rest):
+    """Segmented Mobius scan kernel against the token recurrence in fp64,
+    values and gradients (coefficients shaped like the Kalman precision map)."""
+    from vagus_b200 import ops
+    from vagus_b200.models.kalman import mobius_scan
+    g = torch.Generator(device="cuda").manual_seed(0)
+    shp = (b, L, *rest)
+    m = 2.0 * torch.rand(shp, device="cuda", generator=g)
+    w = 0.05 + torch.rand(shp, device="cuda", generator=g)
+    a = 0.5 + 0.5 * torch.rand(shp, device="cuda", generator=g)
+    coeffs = [1.0 + m * w, m * a, w, a]
+    x0 = 0.5 + torch.rand((b, *rest), device="cuda", generator=g)
+    leaves = [t.clone().requires_grad_(True) for t in coeffs + [x0]]
+    got = ops.mobius_scan(*leaves)
+    ref_leaves = [t.double().clone().requires_grad_(True) for t in coeffs + [x0]]
+    want = mobius_scan(*ref_leaves, impl="recurrent")
+    assert rel(got.double(), want) < 1e-5
+    gO = torch.randn(shp, device="cuda", generator=g)
+    gg = torch.autograd.grad(got, leaves, gO)
+    gw = torch.autograd.grad(want, ref_leaves, gO.double())
+    for x, y in zip(gg, gw):
+        assert rel(x.double(), y) < 1e-4
+    # the model path dispatches to the kernel for CUDA fp32
+    assert rel(mobius_scan(*coeffs, x0).double(), want.detach()) < 1e-5
+
+
+@pytest.mark.parametrize("kalman", ["iso", "diag"])
+def test_kalman_layer_kernels_match_torch_path(kalman):
+    """A Kalman-delta layer in bf16 on the kernels (Mobius scan kernel, the
+    recurrence kernels; the diagonal gain's asymmetric write included) vs the
+    same weights on the fp32 torch path, outputs and input gradients."""
+    from vagus_b200.models.kalman import KalmanDeltaNet
+    torch.manual_seed(0)
+    ref = KalmanDeltaNet(256, 2, 128, 128, kalman=kalman, gate_rank=16, impl="torch").to(DEV)
+    with torch.no_grad():
+        for name, p in ref.named_parameters():
+            if name.startswith("womega2"):
+                p.normal_(0, 0.05)
+    cu = KalmanDeltaNet(256, 2, 128, 128, kalman=kalman, gate_rank=16).to(DEV)
+    cu.load_state_dict(ref.state_dict())
+    cu = cu.bfloat16()
+    x = torch.randn(2, 192, 256, device=DEV)
+    xr = x.clone().requires_grad_(True)
+    xc = x.bfloat16().requires_grad_(True)
+    yr, yc = ref(xr), cu(xc)
+    assert rel(yc, yr) < 3e-2, rel(yc, yr)
+    dy = torch.randn_like(yr)
+    (yr * dy).sum().backward()
+    (yc.float() * dy).sum().backward()
+    assert rel(xc.grad, xr.grad) < 6e-2, rel(xc.grad, xr.grad)

@@ -104,6 +104,18 @@ def _cases(B: int, L: int):
     cases["kda_gated_fwd"] = (lambda: C.kda_gated_fwd(Qg, Kg, Gg), None, kfl)
     cases["kda_gated_bwd"] = (lambda: C.kda_gated_bwd(Qg, Kg, Gg, dA1, dA2), None, 2 * kfl)
 
+    # Kalman precision recurrence (Mobius scan) at the diagonal KDN shape: 4 heads x 128 channels
+    from ..models.kalman import mobius_scan as _mob
+    Rm = 4 * 128
+    cm = [0.05 + torch.rand(B, L, Rm, device=dev) for _ in range(4)]
+    x0m = torch.rand(B, Rm, device=dev) + 0.5
+    mbytes = 5 * B * L * Rm * 4                        # four inputs read (twice: compose, replay) + x written
+    cases["mobius_fwd"] = (lambda: C.mobius_fwd(*cm, x0m), mbytes + 4 * B * L * Rm * 4, None)
+    xm = C.mobius_fwd(*cm, x0m)
+    gm = torch.randn_like(xm)
+    cases["mobius_bwd"] = (lambda: C.mobius_bwd(*cm, x0m, xm, gm), 15 * B * L * Rm * 4, None)
+    cases["mobius_torch"] = (lambda: _mob(*cm, x0m, impl="torch"), mbytes, None)
+
     from ..ops._core import gemm
     a = r(T, D)
     wpk = r(NP, D)

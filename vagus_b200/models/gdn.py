@@ -193,6 +193,8 @@ class GatedDeltaNet(nn.Module, Mixer):
         if w is not None:
             assert self.delta and g is not None and g.dim() == 4, \
                 "the asymmetric chunk form is implemented for the vector gate"
+            if self._use_kernels(q):
+                return ops.kda_chunk(q, k, v, g, None, S0, scale=self.scale, chunk_size=self.chunk_size, w=w)
             return chunk_scan_vec(q, k, v, g, None, S0, scale=self.scale, delta=True,
                                   chunk_size=self.chunk_size, w=w)
         if self._use_kernels(q) and self.gate == "scalar" and self.delta:

@@ -56,8 +56,15 @@ def mobius_scan(A, B, C, D, x0, *, impl: str = "parallel", block: int | None = 2
 
     A..D: (B, L, *rest) non-negative; x0: (B, *rest); returns (B, L, *rest).
     'recurrent' is the definition (test oracle); 'parallel' is the log-depth
-    prefix product (Hillis-Steele doubling on the 2x2 matrices)."""
+    prefix product (Hillis-Steele doubling on the 2x2 matrices), which on
+    CUDA fp32 inputs runs as the segmented scan kernel (``ops.mobius_scan``);
+    'torch' forces the doubling in torch."""
     L = A.shape[1]
+    if impl == "parallel" and A.is_cuda and A.dtype == torch.float32 and L > 0:
+        from .. import ops
+        return ops.mobius_scan(A, B, C, D, x0)
+    if impl == "torch":
+        impl = "parallel"
     if impl == "recurrent":
         x, out = x0, []
         for t in range(L):
@@ -69,7 +76,7 @@ def mobius_scan(A, B, C, D, x0, *, impl: str = "parallel", block: int | None = 2
         pieces, x = [], x0
         for lo in range(0, L, block):
             hi = min(lo + block, L)
-            seg = mobius_scan(A[:, lo:hi], B[:, lo:hi], C[:, lo:hi], D[:, lo:hi], x, impl="parallel", block=None)
+            seg = mobius_scan(A[:, lo:hi], B[:, lo:hi], C[:, lo:hi], D[:, lo:hi], x, impl="torch", block=None)
             pieces.append(seg)
             x = seg[:, -1]
         return torch.cat(pieces, 1)

@@ -13,5 +13,6 @@ from .ce import fused_linear_ce  # noqa: F401
 from .gdn import conv_silu, gdn_mixer, gdr_chunk, gdr_decode  # noqa: F401
 from .kda import kda_chunk  # noqa: F401
 from .linear import linear, linear_residual  # noqa: F401
+from .mobius import mobius_scan  # noqa: F401
 from .pointwise import (embedding, qk_norm_rope, rmsnorm, rmsnorm_gated, rmsnorm_pass, sigmoid_gate,  # noqa: F401
                         swiglu)

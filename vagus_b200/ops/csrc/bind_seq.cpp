@@ -234,9 +234,44 @@ std::vector<Tensor> kda_gated_bwd(Tensor Q, Tensor K, Tensor G, Tensor dAqk, Ten
   return {dQ, dK, dG};
 }
 
+// Mobius-map scan (mobius.cu).  A, B, C, D: (batch, L, R) fp32; x0: (batch, R).
+Tensor mobius_fwd(Tensor A, Tensor B, Tensor C, Tensor D, Tensor x0) {
+  for (auto* t : {&A, &B, &C, &D})
+    TORCH_CHECK(t->is_cuda() && t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 3 &&
+                    t->sizes() == A.sizes(),
+                "mobius_fwd: A, B, C, D (batch, L, R) fp32 contiguous");
+  TORCH_CHECK(x0.is_cuda() && x0.scalar_type() == at::kFloat && x0.is_contiguous() && x0.dim() == 2 &&
+                  x0.size(0) == A.size(0) && x0.size(1) == A.size(2),
+              "mobius_fwd: x0 (batch, R) fp32 contiguous");
+  TORCH_CHECK(A.size(0) <= 65535, "mobius_fwd: batch <= 65535");
+  auto X = torch::empty_like(A);
+  check(vagus::mobius_fwd(A.data_ptr<float>(), B.data_ptr<float>(), C.data_ptr<float>(), D.data_ptr<float>(),
+                          x0.data_ptr<float>(), X.data_ptr<float>(), static_cast<int>(A.size(0)),
+                          static_cast<int>(A.size(1)), static_cast<int>(A.size(2)), stream()),
+        "mobius_fwd");
+  return X;
+}
+
+// -> (gA, gB, gC, gD, gx0)
+std::vector<Tensor> mobius_bwd(Tensor A, Tensor B, Tensor C, Tensor D, Tensor x0, Tensor X, Tensor gO) {
+  gO = gO.contiguous().to(at::kFloat);
+  TORCH_CHECK(X.sizes() == A.sizes() && gO.sizes() == A.sizes() && X.is_contiguous(), "mobius_bwd: shapes");
+  auto gA = torch::empty_like(A), gB = torch::empty_like(A), gC = torch::empty_like(A), gD = torch::empty_like(A);
+  auto gx0 = torch::empty_like(x0);
+  check(vagus::mobius_bwd(A.data_ptr<float>(), B.data_ptr<float>(), C.data_ptr<float>(), D.data_ptr<float>(),
+                          x0.data_ptr<float>(), X.data_ptr<float>(), gO.data_ptr<float>(), gA.data_ptr<float>(),
+                          gB.data_ptr<float>(), gC.data_ptr<float>(), gD.data_ptr<float>(), gx0.data_ptr<float>(),
+                          static_cast<int>(A.size(0)), static_cast<int>(A.size(1)), static_cast<int>(A.size(2)),
+                          stream()),
+        "mobius_bwd");
+  return {gA, gB, gC, gD, gx0};
+}
+
 }  // namespace
 
 void register_seq_ops(pybind11::module& m) {
+  m.def("mobius_fwd", &mobius_fwd);
+  m.def("mobius_bwd", &mobius_bwd);
   m.def("kda_gated_fwd", &kda_gated_fwd);
   m.def("kda_gated_bwd", &kda_gated_bwd);
   m.def("conv_silu_fwd", &conv_silu_fwd);

@@ -138,6 +138,14 @@ int kda_gated_fwd(const float* Q, const float* K, const float* G, float* Aqk, fl
 int kda_gated_bwd(const float* Q, const float* K, const float* G, const float* dAqk, const float* dAkk, float* dQ,
                   float* dK, float* dG, long long chunks, int dk, cudaStream_t st);
 
+// mobius.cu: x_t = (A_t x_{t-1} + B_t) / (C_t x_{t-1} + D_t) along L; A..D, X, gO and the
+// gradients (batch, L, R) fp32 contiguous, x0 and gx0 (batch, R).
+int mobius_fwd(const float* A, const float* B, const float* C, const float* D, const float* x0, float* X, int batch,
+               int L, int R, cudaStream_t st);
+int mobius_bwd(const float* A, const float* B, const float* C, const float* D, const float* x0, const float* X,
+               const float* gO, float* gA, float* gB, float* gC, float* gD, float* gx0, int batch, int L, int R,
+               cudaStream_t st);
+
 // comm.cu: NVLink peer-to-peer all-gather / reduce-scatter over CUDA-IPC
 // shared heaps (see comm.cu for the heap layout and the epoch protocol).
 constexpr int kMaxCommPeers = 16;

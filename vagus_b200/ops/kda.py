@@ -81,17 +81,33 @@ class _GatedProducts(torch.autograd.Function):
         return dQ, dK, dG
 
 
-def kda_intra(q, k, v, g, beta, scale: float, delta: bool = True):
+def kda_intra(q, k, v, g, beta, scale: float, delta: bool = True, w=None):
     """(W, Qh, Kt, A, U, gamma) of every chunk, fp32, (B, H, N, C, .) layout;
     q, k (B, L, H, dk), v (B, L, H, dv), g (B, L, H, dk) log decay, beta (B, L, H).
     Without the delta rule (gated linear attention: S <- diag(gamma) S + Kt^T V)
-    W is zero and U = V, so the same recurrence kernels apply."""
+    W is zero and U = V, so the same recurrence kernels apply.  With an
+    explicit write vector w (B, L, H, dk) (the asymmetric write
+    S <- S + w (v - S^T k)^T, beta unused) the read key k and the write w
+    take separate slots: M = tril(<K, Wr>_g, -1), T = (I + M)^-1, U = T V,
+    W = T (K o e^g), A = scale tril(<Q, Wr>_g), Kt = Wr o e^(g_last - g)."""
     B, L, H, dk = q.shape
     dv = v.shape[-1]
     N = L // CHUNK
     to_c = lambda t, d: t.float().reshape(B, N, CHUNK, H, d).permute(0, 3, 1, 2, 4)   # noqa: E731
     Q, K, V = to_c(q, dk), to_c(k, dk), to_c(v, dv)
     gam = to_c(g, dk).cumsum(3)                                  # (B, H, N, C, dk)
+    if w is not None:
+        # gated products with the write vectors in the column slot (torch,
+        # chunk-parallel; the CUDA products share one column operand)
+        Wr = to_c(w, dk)
+        Aqw, Akw = _gated(Q, Wr, gam, strict=False), _gated(K, Wr, gam, strict=True)
+        G = gam.exp()
+        Tm = Akw + torch.eye(CHUNK, device=q.device, dtype=Akw.dtype)
+        eye = torch.eye(CHUNK, device=q.device, dtype=Akw.dtype).expand_as(Tm)
+        T = torch.linalg.solve_triangular(Tm, eye, upper=False, unitriangular=True)
+        WU = T @ torch.cat([K * G, V], dim=-1)
+        return (WU[..., :dk], Q * G * scale, Wr * (gam[..., -1:, :] - gam).exp(), Aqw * scale, WU[..., dk:],
+                G[..., -1, :])
     if q.is_cuda:
         Aqk, Akk = _GatedProducts.apply(Q, K, gam)
     else:
@@ -144,10 +160,12 @@ class _KDARec(torch.autograd.Function):
                 dS0.view(B, Hh, dk, dv) if ctx.has_S0 else None, None)
 
 
-def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64, delta: bool = True):
+def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64, delta: bool = True, w=None):
     """Chunked delta rule with a per-channel gate g (B, L, H, dk) (log decay)
     on CUDA; ``delta=False`` is gated linear attention (beta unused), and a
     scalar gate (B, L, H) or no gate (None) is broadcast over the channels.
+    ``w`` (B, L, H, dk) is an explicit write vector (the asymmetric write of
+    the Kalman diagonal gain; beta unused).
     Returns (o (B, L, H, dv) bf16, S (B, H, dk, dv) fp32)."""
     assert chunk_size == CHUNK, "the sm_100a recurrence runs 64-token chunks"
     B, L, H, dk = q.shape
@@ -162,6 +180,7 @@ def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64, delta
         # zero gate and zero write strength: padded tokens leave the state alone
         pz = lambda t: torch.nn.functional.pad(t, [0, 0] * (t.dim() - 2) + [0, pad])   # noqa: E731
         q, k, v, g, beta = pz(q), pz(k), pz(v), pz(g), pz(beta)
-    parts = kda_intra(q, k, v, g, beta, scale, delta)
+        w = None if w is None else pz(w)
+    parts = kda_intra(q, k, v, g, beta, scale, delta, w)
     o, S = _KDARec.apply(*parts, S0, H)
     return (o[:, :L] if pad else o), S
