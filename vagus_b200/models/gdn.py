@@ -19,10 +19,11 @@ layer runs as sm_100a kernels -- one projection GEMM for q/k/v/g, one fused
 short-conv+SiLU+L2norm kernel, the gate/beta kernel, the chunked gated
 delta-rule kernel and the fused RMSNorm*SiLU(gate) kernel -- see
 ``vagus_b200.ops.gdn``.  The other variants on CUDA -- per-channel gate (KDA),
-no gate (DeltaNet), no delta rule (gated linear attention) -- run their
-intra-chunk stage chunk-parallel in torch and the state recurrence on the
-same kernels (``vagus_b200.ops.kda``).  Everything else (CPU, fp64 tests,
-Kalman writes) runs the pure-torch chunk oracle of ``models.scans``.
+no gate (DeltaNet), no delta rule (gated linear attention), and the Kalman
+writes (a per-head gain, or an explicit write vector) -- run their
+intra-chunk stage chunk-parallel (gated products on ``csrc/kda.cu``) and
+the state recurrence on the same kernels (``vagus_b200.ops.kda``).  CPU and
+fp64 runs use the pure-torch chunk oracles of ``models.scans``.
 
 Parity: reference ``infra/components/linear_attention.py:505-952``.
 """

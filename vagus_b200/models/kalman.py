@@ -20,10 +20,12 @@ kappa is a vector not parallel to k: the asymmetric write, run by the chunked
 vector-gate scan with an explicit ``w``.
 
 Both uncertainty recurrences are Mobius maps x -> (A x + B) / (C x + D) with
-non-negative coefficients, composed as a prefix product of 2x2 matrices at log
-depth (``mobius_scan``), renormalised after every doubling step (a scalar
-multiple of the matrix is the same map) and blocked so autograd never holds
-more than one block of the doubling tensors.
+non-negative coefficients (``mobius_scan``).  On CUDA fp32 they run on the
+segmented scan kernel (``ops.mobius_scan``: segment maps composed as 2x2
+products, then an exact replay of the recurrence); elsewhere as a torch
+prefix product of the 2x2 matrices at log depth, renormalised after every
+doubling step (a scalar multiple of the matrix is the same map) and blocked
+so autograd never holds more than one block of the doubling tensors.
 
 Parity: reference ``infra/components/kalman_delta.py:1-300``.
 """
