@@ -21,7 +21,8 @@ delta-rule kernel and the fused RMSNorm*SiLU(gate) kernel -- see
 ``vagus_b200.ops.gdn``.  The other variants on CUDA -- per-channel gate (KDA),
 no gate (DeltaNet), no delta rule (gated linear attention), and the Kalman
 writes (a per-head gain, or an explicit write vector) -- run their
-intra-chunk stage chunk-parallel (gated products on ``csrc/kda.cu``) and
+intra-chunk stage chunk-parallel (gated products on ``csrc/kda.cu``; in
+torch for an explicit write vector) and
 the state recurrence on the same kernels (``vagus_b200.ops.kda``).  CPU and
 fp64 runs use the pure-torch chunk oracles of ``models.scans``.
 
