@@ -201,13 +201,14 @@ attn_fwd_kernel(const AttnArgs a) {
 }
 
 // ------------------------------------------------------ tcgen05 forward --
-// One CTA per (128 queries, batch * head), 6 warps:
-//   warp 0      TMA: the Q tile once, then K / V tiles of 128 keys into a
-//               two-stage ring;
+// One CTA per (128 queries, batch * head), 10 warps:
+//   warp 0      TMA: the Q tile once, then K / V tiles of 128 keys (K in a
+//               two-stage ring, V in NV stages);
 //   warp 1      TMEM owner and MMA issuer: S_j = Q K_j^T (M=128, N=128)
-//               into one of two TMEM score buffers, issued one tile ahead,
-//               then O += P_j V_j (M=128, N=D, K=128 keys) into the TMEM
-//               output accumulator;
+//               into a TMEM score buffer (with two buffers, issued one tile
+//               ahead; with one, as soon as the softmax warps have read
+//               S_{j-1}), then O += P_j V_j (M=128, N=D, K=128 keys) into the
+//               TMEM output accumulator;
 //   warps 2-9   softmax, two threads per query row (each half of the key
 //               columns): tcgen05.ld of the score row, running max / sum in
 //               registers (the pair agrees on the max through shared memory),
@@ -216,9 +217,9 @@ attn_fwd_kernel(const AttnArgs a) {
 //               reads; the output is rescaled in TMEM only when the running
 //               max grows by more than 2^8 (otherwise P is taken against the
 //               stale max, at most 256x larger, harmless in fp32 / bf16).
-// Barriers: q_full, k_full[2] / k_empty[2] and v_full[2] / v_empty[2]
+// Barriers: q_full, k_full[2] / k_empty[2] and v_full[NV] / v_empty[NV]
 // (loader <-> MMA; a K stage frees as soon as its score product is done, so
-// K loads run a tile further ahead than V), s_full[2] / s_free[2] (MMA <->
+// K loads run a tile further ahead than V), s_full[NS] / s_free[NS] (MMA <->
 // softmax), p_full (softmax -> MMA), o_done (MMA -> softmax: P buffer free
 // and O stable).  Every wait is bounded.
 extern unsigned long long* g_attn_trace;   // host side of the phase trace (attn_set_trace)
@@ -226,21 +227,31 @@ namespace tcfa {
 constexpr int BQ = 128, BKV = 128, THREADS = 320;   // 10 warps
 constexpr float kRescale = 8.f;     // log2 units
 
+// Head dim 64 runs two CTAs per SM (the two CTAs' tiles interleave on the
+// tensor core and the MUFU): one TMEM score buffer and one V stage, so each
+// CTA holds 256 TMEM columns and under 100 KB of shared memory.  Head dim 128
+// runs one CTA per SM with two score buffers (S_{j+1} computed while the
+// softmax warps work on S_j) and two V stages.
 template <int D>
 struct Layout {
+  static constexpr int CTAS = D == 64 ? 2 : 1;    // CTAs per SM
+  static constexpr int NS = D == 64 ? 1 : 2;      // TMEM score buffers
+  static constexpr int NV = D == 64 ? 1 : 2;      // V stages (K always has 2)
   static constexpr int Q_BYTES = BQ * D * 2;      // D/64 K-major chunks of 16 KB
   static constexpr int K_BYTES = BKV * D * 2;
   static constexpr int V_BYTES = BKV * D * 2;     // 2 key chunks x D/64 MN-major blocks of 8 KB
   static constexpr int P_BYTES = BQ * BKV * 2;    // 2 K-major chunks of 16 KB
   static constexpr int OFF_K = Q_BYTES;
   static constexpr int OFF_V = OFF_K + 2 * K_BYTES;
-  static constexpr int OFF_P = OFF_V + 2 * V_BYTES;
+  static constexpr int OFF_P = OFF_V + NV * V_BYTES;
   static constexpr int OFF_BAR = OFF_P + P_BYTES;
-  // at least 120 KB so one CTA holds an SM (and all 512 TMEM columns)
   // barriers, TMEM slot, then [2][128] row maxima and [2][128] row sums
   static constexpr int BAR_BYTES = 128 + 2 * 2 * BQ * 4;
-  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024 > 120 * 1024 ? OFF_BAR + BAR_BYTES + 1024 : 120 * 1024;
-  static constexpr uint32_t TMEM_S = 0, TMEM_O = 256, TMEM_COLS = 512;
+  static constexpr int SMEM_MIN = CTAS == 1 ? 120 * 1024 : 0;   // one CTA: hold the SM (and its TMEM)
+  static constexpr int SMEM = OFF_BAR + BAR_BYTES + 1024 > SMEM_MIN ? OFF_BAR + BAR_BYTES + 1024 : SMEM_MIN;
+  static constexpr uint32_t TMEM_S = 0, TMEM_O = NS * BKV, TMEM_COLS = NS == 1 ? 256 : 512;
+  static_assert(TMEM_O + D <= TMEM_COLS, "TMEM layout");
+  static_assert(CTAS == 1 || SMEM <= 110 * 1024, "two CTAs per SM must fit the SM's shared memory");
 };
 
 struct Params {
@@ -255,7 +266,7 @@ struct Params {
 }  // namespace tcfa
 
 template <int D>
-__global__ void __launch_bounds__(tcfa::THREADS, 1)
+__global__ void __launch_bounds__(tcfa::THREADS, tcfa::Layout<D>::CTAS)
 attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
             const __grid_constant__ CUtensorMap mv, const tcfa::Params p) {
   using namespace tcfa;
@@ -280,7 +291,21 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int qb = blockIdx.x, bh = blockIdx.y;
+  // causal: within groups of 8 heads, the longest query blocks (most key
+  // tiles) launch first, so a group's last wave holds short blocks; the
+  // resident CTAs share the K / V of at most a few groups (L2 reuse)
+  // (two CTAs per SM only: with one, the plain order measured faster)
+  int qb = blockIdx.x, bh = blockIdx.y;
+  if (Lt::CTAS == 2 && p.causal) {
+    constexpr int G = 8;
+    const int nq = gridDim.x, nbh = gridDim.y;
+    const int lin = blockIdx.y * nq + blockIdx.x;
+    const int grp = lin / (G * nq);
+    const int gsz = min(G, nbh - grp * G);
+    const int within = lin - grp * G * nq;
+    qb = nq - 1 - within / gsz;
+    bh = grp * G + within % gsz;
+  }
   const int b = bh / p.H, h = bh % p.H;
   const int hk = h / (p.H / p.Hk);
   const int q0 = qb * BQ;
@@ -288,7 +313,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   const int q_last = min(q0 + BQ, p.Lq) - 1;
   const int k_end = p.causal ? min(p.Lk, q_last + offs + 1) : p.Lk;
   const int ntiles = k_end > 0 ? (k_end + BKV - 1) / BKV : 0;
-  const bool tracing = p.trace != nullptr && blockIdx.x == gridDim.x - 1 && blockIdx.y == 0;
+  const bool tracing = p.trace != nullptr && qb == static_cast<int>(gridDim.x) - 1 && bh == 0;
 #define VAGUS_TRF(tile, ev)                                                     \
   do {                                                                          \
     if (tracing && (tile) < 32) p.trace[(tile) * 16 + (ev)] = clock64();        \
@@ -336,8 +361,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         return true;
       };
       auto load_v = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) return false;
+        const int s = j % Lt::NV;
+        if (!mbar_wait(&v_empty[s], ((j / Lt::NV) & 1) ^ 1, abort_flag, p.err, kErrTimeoutProducer)) return false;
         mbar_arrive_expect_tx(&v_full[s], Lt::V_BYTES);
         uint8_t* vd = sv + s * Lt::V_BYTES;
         for (int kc = 0; kc < 2; ++kc)
@@ -358,11 +383,13 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       constexpr uint32_t idesc_o = make_idesc_bf16(BQ, D, false, true);
       bool ok = mbar_wait(q_full, 0, abort_flag, p.err, kErrTimeoutMma);
       auto issue_s = [&](int j) -> bool {
-        const int s = j & 1;
+        const int s = j & 1;                    // K stage
+        const int sb = j % Lt::NS;              // score buffer
         if (!mbar_wait(&k_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) return false;
-        if (j >= 2 && !mbar_wait(&s_free[s], ((j >> 1) - 1) & 1, abort_flag, p.err, kErrTimeoutMma)) return false;
+        if (j >= Lt::NS && !mbar_wait(&s_free[sb], ((j / Lt::NS) - 1) & 1, abort_flag, p.err, kErrTimeoutMma))
+          return false;
         tc_fence_after();
-        const uint32_t d = tmem_base + Lt::TMEM_S + static_cast<uint32_t>(s * BKV);
+        const uint32_t d = tmem_base + Lt::TMEM_S + static_cast<uint32_t>(sb * BKV);
         const uint32_t qa = smem_u32(sq), ka = smem_u32(sk + s * Lt::K_BYTES);
 #pragma unroll
         for (int c = 0; c < D / 64; ++c)
@@ -370,7 +397,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           for (int kk = 0; kk < 4; ++kk)
             tc_mma_f16(d, make_sw128_desc(qa + c * 16384 + kk * 32, 16, 1024),
                        make_sw128_desc(ka + c * 16384 + kk * 32, 16, 1024), idesc_s, (c | kk) ? 1u : 0u);
-        tc_commit(&s_full[s]);
+        tc_commit(&s_full[sb]);
         tc_commit(&k_empty[s]);
         return true;
       };
@@ -380,8 +407,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         VAGUS_TRF(j, 0);
         if (!mbar_wait_spin(p_full, j & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         VAGUS_TRF(j, 1);
-        const int s = j & 1;
-        if (!mbar_wait(&v_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
+        const int s = j % Lt::NV;
+        if (!mbar_wait(&v_full[s], (j / Lt::NV) & 1, abort_flag, p.err, kErrTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d = tmem_base + Lt::TMEM_O;
         const uint32_t pa = smem_u32(sp), va = smem_u32(sv + s * Lt::V_BYTES);
@@ -421,8 +448,8 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     // keep meeting at its named barrier, so the remaining tiles run on
     // whatever is in the buffers and the error word reports the failure
     for (int j = 0; j < ntiles; ++j) {
-      const int s = j & 1;
-      ok = ok && mbar_wait_spin(&s_full[s], (j >> 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      const int s = j % Lt::NS;
+      ok = ok && mbar_wait_spin(&s_full[s], (j / Lt::NS) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
       if (warp == 2 && lane == 0) VAGUS_TRF(j, 3);
       tc_fence_after();
       float x[64];
@@ -485,6 +512,11 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         ls0 = ls1 = 0.f;
       }
       l_run += ls0 + ls1;
+      // P packed to bf16 pairs now: the fp32 row is dead before the rescale
+      // below needs its own 32 registers
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) pk[i] = pack_bf16x2(x[2 * i], x[2 * i + 1]);
       if (warp == 2 && lane == 0) VAGUS_TRF(j, 7);
       // PV_{j-1} must be done before P is overwritten or O rescaled
       if (j > 0) ok = ok && mbar_wait_spin(o_done, (j - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
@@ -506,9 +538,7 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       // this half's 64 keys are P chunk `half`: bf16, 128-byte-swizzled K-major
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const float* v8 = &x[8 * u];
-        const uint4 w = make_uint4(pack_bf16x2(v8[0], v8[1]), pack_bf16x2(v8[2], v8[3]),
-                                   pack_bf16x2(v8[4], v8[5]), pack_bf16x2(v8[6], v8[7]));
+        const uint4 w = make_uint4(pk[4 * u], pk[4 * u + 1], pk[4 * u + 2], pk[4 * u + 3]);
         *reinterpret_cast<uint4*>(sp + half * 16384 + row * 128 + ((u ^ (row & 7)) * 16)) = w;
       }
       if (warp == 2 && lane == 0) VAGUS_TRF(j, 9);
@@ -1186,7 +1216,8 @@ int launch_fwd_tc(const AttnArgs& a, cudaStream_t st) {
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(attn_fwd_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(attn_fwd_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(attn_fwd_tc<D>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return 3;
     attr_set[dev] = true;
   }
