@@ -5,7 +5,6 @@ DDP give the same loss and gradient-norm traces for fp32 AdamW and Muon
 import os
 import socket
 
-import pytest
 import torch
 import torch.multiprocessing as mp
 

@@ -17,7 +17,6 @@ state export layout, same stop semantics).
 
 from __future__ import annotations
 
-from pathlib import Path
 from typing import Iterator, Sequence
 
 import torch
