@@ -223,6 +223,32 @@ attn_fwd_kernel(const AttnArgs a) {
 // softmax), p_full (softmax -> MMA), o_done (MMA -> softmax: P buffer free
 // and O stable).  Every wait is bounded.
 extern unsigned long long* g_attn_trace;   // host side of the phase trace (attn_set_trace)
+
+// 2^x on the FMA and integer pipes, for x <= 0 (clamped at -126): x = n + f
+// with n = round(x) (adding and subtracting 1.5 * 2^23 rounds in the
+// mantissa), 2^f by a cubic least-squares fit on [-1/2, 1/2] (maximum
+// relative error 7.5e-5, under half a bf16 ulp: the result is rounded to
+// bf16 for the tensor core), 2^n added to the exponent field.  In the
+// forward's softmax loop 2 of every 8 exponentials take this path and the
+// rest the MUFU unit (measured: 537 -> 523 us at head dim 64; 4 of 8 was
+// slower, and the backward, whose transcendental pipe is the busiest, gained
+// nothing from 2 or 4 of 8).
+__device__ __forceinline__ float ex2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float sh = 12582912.f;
+  const float t = x + sh;
+  const float f = x - (t - sh);
+  float q = fmaf(0.05517146f, f, 0.24261086f);
+  q = fmaf(q, f, 0.69326099f);
+  q = fmaf(q, f, 0.99992809f);
+  return __int_as_float(__float_as_int(q) + ((__float_as_int(t) - __float_as_int(sh)) << 23));
+}
+template <int PX>
+__device__ __forceinline__ float ex2_mix(float x, int i) {
+  if ((i & 7) < PX) return ex2_poly(x);
+  return ex2_approx(x);
+}
+
 namespace tcfa {
 constexpr int BQ = 128, BKV = 128, THREADS = 320;   // 10 warps
 constexpr float kRescale = 8.f;     // log2 units
@@ -265,7 +291,7 @@ struct Params {
 };
 }  // namespace tcfa
 
-template <int D>
+template <int D, int PX>
 __global__ void __launch_bounds__(tcfa::THREADS, tcfa::Layout<D>::CTAS)
 attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUtensorMap mk,
             const __grid_constant__ CUtensorMap mv, const tcfa::Params p) {
@@ -497,12 +523,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       const float nm = (m_run == -INFINITY) ? 0.f : -m_run;
       const float sl2 = (m_run == -INFINITY) ? 0.f : psl2;
       float ls0 = 0.f, ls1 = 0.f;
-      // (a share of these on the FMA pipe, packed f16x2 exponentials, or 16
-      // softmax warps instead of 8 all measured no faster here)
+      // (2 of 8 on the FMA pipe, ex2_poly; packed f16x2 exponentials or 16
+      // softmax warps instead of 8 measured no faster)
 #pragma unroll
       for (int i = 0; i < 64; i += 2) {
-        x[i] = ex2_approx(fmaf(x[i], sl2, nm));
-        x[i + 1] = ex2_approx(fmaf(x[i + 1], sl2, nm));
+        x[i] = ex2_mix<PX>(fmaf(x[i], sl2, nm), i);
+        x[i + 1] = ex2_mix<PX>(fmaf(x[i + 1], sl2, nm), i + 1);
         ls0 += x[i];
         ls1 += x[i + 1];
       }
@@ -1213,18 +1239,19 @@ int launch_fwd_tc(const AttnArgs& a, cudaStream_t st) {
   p.err = a.err;
   p.trace = g_attn_trace;
   static bool attr_set[64] = {};
+  auto kern = attn_fwd_tc<D, 2>;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(attn_fwd_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess ||
-        cudaFuncSetAttribute(attn_fwd_tc<D>, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess ||
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100) != cudaSuccess)
       return 3;
     attr_set[dev] = true;
   }
   dim3 grid(static_cast<unsigned>((a.Lq + tcfa::BQ - 1) / tcfa::BQ), static_cast<unsigned>(a.B * a.H));
-  attn_fwd_tc<D><<<grid, tcfa::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
-                                                         *reinterpret_cast<const CUtensorMap*>(mk),
-                                                         *reinterpret_cast<const CUtensorMap*>(mv), p);
+  kern<<<grid, tcfa::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
+                                               *reinterpret_cast<const CUtensorMap*>(mk),
+                                               *reinterpret_cast<const CUtensorMap*>(mv), p);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -1272,21 +1299,22 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
   p.dk = (__nv_bfloat16*)a.dk; p.dv = (__nv_bfloat16*)a.dv; p.err = f.err;
   p.trace = g_attn_trace;
   static bool attr_set[64] = {};
+  auto kern = attn_bwd_tc<D>;
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 0 && dev < 64 && !attr_set[dev]) {
-    if (cudaFuncSetAttribute(attn_bwd_tc<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess)
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Lt::SMEM) != cudaSuccess)
       return 3;
     attr_set[dev] = true;
   }
   const long long rows = (long long)f.B * f.H * f.Lq;
   attn_bwd_pre<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
   dim3 grid(static_cast<unsigned>((f.Lk + tcbw::KROWS - 1) / tcbw::KROWS), static_cast<unsigned>(f.B * f.Hk));
-  attn_bwd_tc<D><<<grid, tcbw::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
-                                                         *reinterpret_cast<const CUtensorMap*>(mk),
-                                                         *reinterpret_cast<const CUtensorMap*>(mv),
-                                                         *reinterpret_cast<const CUtensorMap*>(mdo),
-                                                         *reinterpret_cast<const CUtensorMap*>(mdq), p);
+  kern<<<grid, tcbw::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
+                                               *reinterpret_cast<const CUtensorMap*>(mk),
+                                               *reinterpret_cast<const CUtensorMap*>(mv),
+                                               *reinterpret_cast<const CUtensorMap*>(mdo),
+                                               *reinterpret_cast<const CUtensorMap*>(mdq), p);
   const long long n = rows * D;
   attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a.dq_acc, (__nv_bfloat16*)a.dq, n,
                                                                               f.scale);
