@@ -101,8 +101,14 @@ def test_benchmarks_run_on_cpu(capsys):
     bench_rope.main(["--B", "1", "--L", "16", "--H", "2", "--dh", "16", "--iters", "2"])
     bench_linear_attention.main(["--B", "1", "--L", "64", "--H", "2", "--dk", "16", "--dv", "16", "--iters", "1",
                                  "--modes", "kda", "gla", "deltanet"])
+    r = bench_linear_attention.main(["--decode", "--B", "1", "--H", "2", "--dk", "16", "--dv", "16", "--prefill", "16",
+                                     "--steps", "3", "--iters", "1", "--modes", "gdn", "kda"])
+    assert set(r) == {"gdn/torch", "kda/torch"} and all(v["decode_ms_per_token"] > 0 for v in r.values())
+    r = bench_attention.main(["--decode", "--B", "1", "--H", "2", "--dh", "16", "--prefill", "16", "--steps", "3",
+                              "--iters", "1", "--kv-heads", "1"])
+    assert r["d16"]["prefill_ms"] > 0
     out = capsys.readouterr().out
-    assert "FAILED" not in out and "sdpa" in out and "fused" in out
+    assert "FAILED" not in out and "sdpa" in out and "fused" in out and "us/token" in out
 
 
 def _free_port():

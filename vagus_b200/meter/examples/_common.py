@@ -44,3 +44,38 @@ def walk(model, tokens, visit) -> None:
     for i, blk in enumerate(model.blocks):
         visit(i, blk, blk.rmsnorm1(x))
         x = blk(x)
+
+
+def decode_bench(layer, x, prefill: int, steps: int, *, iters: int = 5) -> dict:
+    """Streaming timings of one mixer layer on input x (B, prefill + steps, D):
+    the prefill of ``prefill`` tokens through the cache, and the per-token
+    latency of ``steps`` single-token decode steps after it."""
+    from ..core import bench
+    B = x.shape[0]
+    cap = prefill + steps
+
+    @torch.no_grad()
+    def pre():
+        layer.reset_cache(B, cap)
+        return layer.decode_step(x[:, :prefill])
+
+    @torch.no_grad()
+    def full():
+        layer.reset_cache(B, cap)
+        out = layer.decode_step(x[:, :prefill])
+        for t in range(prefill, cap):
+            out = layer.decode_step(x[:, t:t + 1])
+        return out
+
+    rp = bench(pre, name="prefill", device=x.device, warmup=1, iters=iters)
+    rf = bench(full, name="prefill+decode", device=x.device, warmup=1, iters=iters)
+    if rp.failed or rf.failed:
+        raise RuntimeError(rp.error or rf.error)
+    per_tok = (rf.mean_ms - rp.mean_ms) / max(1, steps)
+    return {"prefill_ms": rp.mean_ms, "prefill_tok_s": B * prefill / (rp.mean_ms * 1e-3),
+            "decode_ms_per_token": per_tok, "decode_tok_s": B / (per_tok * 1e-3) if per_tok > 0 else float("inf")}
+
+
+def render_decode(name: str, r: dict) -> str:
+    return (f"  {name:<12} prefill {r['prefill_ms']:8.3f} ms ({r['prefill_tok_s'] / 1e3:8.1f}K tok/s)   "
+            f"decode {r['decode_ms_per_token'] * 1e3:8.1f} us/token ({r['decode_tok_s'] / 1e3:7.1f}K tok/s)")

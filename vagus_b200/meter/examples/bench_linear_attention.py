@@ -4,6 +4,11 @@ per-channel gate / gated linear attention / DeltaNet) against the torch
 chunk oracle (``models.scans.chunk_scan``, fp32).
 
     python -m vagus_b200.meter.examples.bench_linear_attention --B 4 --L 4096 --H 16 --dk 128 --dv 128
+    python -m vagus_b200.meter.examples.bench_linear_attention --decode --B 8 --prefill 2048 --steps 64
+
+``--decode`` times a whole GatedDeltaNet layer streaming through its cache
+(prefill of a prompt, then single-token decode steps on the decode kernel)
+for each mode, against the same layer on the torch path.
 
 Parity: reference ``infra/meter/examples/bench_linear_attention.py`` and
 ``bench_kda_kernel.py`` (there: fla's Triton kernels against a torch scan).
@@ -46,8 +51,13 @@ def main(argv=None):
                     help="gdn (scalar gate), kda (per-channel), gla (no delta rule), deltanet (no gate)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--no-oracle", action="store_true", help="skip the torch scan (slow at large L)")
+    ap.add_argument("--decode", action="store_true", help="streaming prefill / decode of a whole layer")
+    ap.add_argument("--prefill", type=int, default=2048)
+    ap.add_argument("--steps", type=int, default=64)
     a = ap.parse_args(argv)
     dev = "cuda" if torch.cuda.is_available() else "cpu"
+    if a.decode:
+        return decode_main(a, dev)
     scale = a.dk ** -0.5
     for mode in a.modes:
         gate = {"gdn": "scalar", "kda": "vector", "gla": "vector", "deltanet": "none"}[mode]
@@ -76,6 +86,26 @@ def main(argv=None):
         compare(variants, ref=ref, iters=a.iters)
         print(f"{mode}: forward+backward")
         compare({n: fb(f) for n, f in variants.items()}, ref=ref, iters=a.iters)
+
+
+def decode_main(a, dev):
+    from ...models.gdn import GatedDeltaNet
+    from ._common import decode_bench, render_decode
+    dim = a.H * a.dv
+    dt = torch.bfloat16 if dev == "cuda" else torch.float32
+    x = torch.randn(a.B, a.prefill + a.steps, dim, device=dev, dtype=dt)
+    print(f"streaming layer: B={a.B} H={a.H} dk={a.dk} dv={a.dv} prefill={a.prefill} decode steps={a.steps}")
+    out = {}
+    for mode in a.modes:
+        gate = {"gdn": "scalar", "kda": "vector", "gla": "vector", "deltanet": "none"}[mode]
+        for impl in (("auto", "torch") if dev == "cuda" else ("torch",)):
+            torch.manual_seed(0)
+            layer = GatedDeltaNet(dim, a.H, a.dk, a.dv, gate=gate, delta=mode != "gla", gate_rank=16,
+                                  impl=impl).to(dev, dt).eval()
+            r = decode_bench(layer, x, a.prefill, a.steps, iters=a.iters)
+            out[f"{mode}/{impl}"] = r
+            print(render_decode(f"{mode}/{impl}", r))
+    return out
 
 
 if __name__ == "__main__":
