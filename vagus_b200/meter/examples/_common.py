@@ -49,7 +49,8 @@ def walk(model, tokens, visit) -> None:
 def decode_bench(layer, x, prefill: int, steps: int, *, iters: int = 5) -> dict:
     """Streaming timings of one mixer layer on input x (B, prefill + steps, D):
     the prefill of ``prefill`` tokens through the cache, and the per-token
-    latency of ``steps`` single-token decode steps after it."""
+    latency of ``steps`` single-token decode steps after it (each timed run
+    restores the post-prefill cache first; that copy is included)."""
     from ..core import bench
     B = x.shape[0]
     cap = prefill + steps
@@ -59,21 +60,24 @@ def decode_bench(layer, x, prefill: int, steps: int, *, iters: int = 5) -> dict:
         layer.reset_cache(B, cap)
         return layer.decode_step(x[:, :prefill])
 
+    pre()
+    snap = layer.export_cache()
+
     @torch.no_grad()
-    def full():
-        layer.reset_cache(B, cap)
-        out = layer.decode_step(x[:, :prefill])
+    def dec():
+        layer.load_cache(snap, cap)
+        out = None
         for t in range(prefill, cap):
             out = layer.decode_step(x[:, t:t + 1])
         return out
 
     rp = bench(pre, name="prefill", device=x.device, warmup=1, iters=iters)
-    rf = bench(full, name="prefill+decode", device=x.device, warmup=1, iters=iters)
-    if rp.failed or rf.failed:
-        raise RuntimeError(rp.error or rf.error)
-    per_tok = (rf.mean_ms - rp.mean_ms) / max(1, steps)
+    rd = bench(dec, name="decode", device=x.device, warmup=1, iters=iters)
+    if rp.failed or rd.failed:
+        raise RuntimeError(rp.error or rd.error)
+    per_tok = rd.mean_ms / max(1, steps)
     return {"prefill_ms": rp.mean_ms, "prefill_tok_s": B * prefill / (rp.mean_ms * 1e-3),
-            "decode_ms_per_token": per_tok, "decode_tok_s": B / (per_tok * 1e-3) if per_tok > 0 else float("inf")}
+            "decode_ms_per_token": per_tok, "decode_tok_s": B / (per_tok * 1e-3)}
 
 
 def render_decode(name: str, r: dict) -> str:
