@@ -626,3 +626,23 @@ def test_kalman_layer_kernels_match_torch_path(kalman):
     (yr * dy).sum().backward()
     (yc.float() * dy).sum().backward()
     assert rel(xc.grad, xr.grad) < 6e-2, rel(xc.grad, xr.grad)
+
+
+@pytest.mark.parametrize("rows,owners,N,M,K,a_mn,c32", [(520, 8, 4160, 512, 1024, False, False),
+                                                       (512, 2, 1000, 256, 512, False, True),
+                                                       (136, 4, 544, 384, 256, True, False),
+                                                       (256, 3, 700, 128, 192, False, False)])
+def test_gemm_gathered_b(rows, owners, N, M, K, a_mn, c32):
+    """GEMM whose B rows come from several owners' buffers (the row shards of
+    a weight; here separate local allocations stand in for the peers), tiles
+    that straddle an owner boundary included, against the product with the
+    concatenated weight."""
+    from vagus_b200.ops import native
+    W = torch.randn(owners * rows, K, device=DEV).bfloat16()
+    shards = [W[o * rows:(o + 1) * rows].clone() for o in range(owners)]
+    A = torch.randn(K, M, device=DEV).bfloat16() if a_mn else torch.randn(M, K, device=DEV).bfloat16()
+    C = torch.empty(M, N, device=DEV, dtype=torch.float32 if c32 else torch.bfloat16)
+    rc = native().gemm_gather(A, a_mn, [s.data_ptr() for s in shards], rows, K, C)
+    assert rc == 0, rc
+    ref = (A.float().T if a_mn else A.float()) @ W[:N].float().T
+    assert rel(C, ref) < 1e-2, rel(C, ref)

@@ -150,6 +150,32 @@ int64_t gemm_scatter(Tensor A, bool a_mn, Tensor B, bool b_mn, c10::optional<Ten
   return vagus::gemm_launch(g, stream());
 }
 
+// C (M x N) = A @ B^T with B's rows gathered from `srcs` (each `rows` x K,
+// K contiguous, same row pitch) -- e.g. the row shards of a weight on the
+// GPUs of a group through peer mappings (data pointers, as int64).
+int64_t gemm_gather(Tensor A, bool a_mn, std::vector<int64_t> srcs, int64_t rows, int64_t ldb, Tensor C) {
+  need_cuda(A, "A"); need_cuda(C, "C");
+  TORCH_CHECK(A.scalar_type() == at::kBFloat16 && A.dim() == 2 && A.stride(-1) == 1, "gemm_gather: A 2-D bf16");
+  need_bf16_or_f32(C, "C");
+  TORCH_CHECK(C.dim() == 2 && C.stride(-1) == 1, "gemm_gather: C 2-D, inner stride 1");
+  TORCH_CHECK(!srcs.empty() && srcs.size() <= 8, "gemm_gather: 1..8 sources");
+  vagus::GemmArgs g;
+  g.a_mn = a_mn; g.b_mn = false;
+  g.M = static_cast<int>(a_mn ? A.size(1) : A.size(0));
+  g.K = static_cast<int>(a_mn ? A.size(0) : A.size(1));
+  g.N = static_cast<int>(C.size(1));
+  TORCH_CHECK(C.size(0) == g.M, "gemm_gather: C rows");
+  g.A = A.data_ptr(); g.lda = A.stride(0);
+  g.ldb = ldb;
+  g.C = C.data_ptr(); g.ldc = C.stride(0); g.c_f32 = is_f32(C);
+  g.split_k = 1;
+  g.gather_n = static_cast<int>(srcs.size());
+  g.gather_rows = static_cast<int>(rows);
+  for (size_t i = 0; i < srcs.size(); ++i) g.gather_src[i] = reinterpret_cast<const void*>(srcs[i]);
+  g.err = err_ptr();
+  return vagus::gemm_launch(g, stream());
+}
+
 // ------------------------------------------------------------------ norms --
 std::vector<Tensor> rmsnorm_fwd(Tensor x, Tensor gamma, double eps, bool out_f32) {
   need_cuda(x, "x"); need_bf16_or_f32(x, "x");
@@ -345,6 +371,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vagus_b200 sm_100a kernels";
   m.def("error_word", &error_word, "device error word (bounded-wait timeouts); 0 = none");
   m.def("reset_error", &reset_error);
+  m.def("gemm_gather", &gemm_gather);
   m.def("gemm_scatter", &gemm_scatter);
   m.def("gemm", &gemm, "tcgen05 GEMM", py::arg("A"), py::arg("a_mn"), py::arg("B"), py::arg("b_mn"), py::arg("C"),
         py::arg("S") = py::none(), py::arg("alpha") = 1.0, py::arg("beta") = 0.0, py::arg("atomic") = false,

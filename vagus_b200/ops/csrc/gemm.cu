@@ -28,6 +28,7 @@
 #include "gemm.h"
 
 #include <algorithm>
+#include <type_traits>
 #include <cstdio>
 #include <cstdlib>
 #include <mutex>
@@ -224,9 +225,21 @@ struct WorkIter {
   }
 };
 
-template <int BN, bool A_MN, bool B_MN>
+// Per-owner tensor maps of a gathered B operand (GemmArgs::gather_*): a
+// BN-row box map and an 8-row box map over each owner's rows.
+constexpr int kMaxGather = 8;
+struct GatherMaps {
+  CUtensorMap coarse[kMaxGather];
+  CUtensorMap fine[kMaxGather];
+  int rows, owners;
+};
+struct NoGather {};
+
+template <int BN, bool A_MN, bool B_MN, class GM = NoGather>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, const KParams p) {
+gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, const KParams p,
+            const __grid_constant__ GM gm) {
+  constexpr bool kGather = std::is_same<GM, GatherMaps>::value;
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
@@ -294,7 +307,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
           } else {
             tma_load_3d(sa, &mapA, &full_bar[stage], k0, tm * BM, b);
           }
-          if (B_MN) {
+          if constexpr (kGather) {
+            // the tile's B rows from their owners: one box when they lie in
+            // one owner's rows (or in the last owner's, whose rows past its
+            // end only feed masked output columns), else 8-row boxes, each
+            // from the owner of its rows (owner boundaries are multiples of 8)
+            const int n0 = tn * BN;
+            const int o = min(n0 / gm.rows, gm.owners - 1);
+            if (n0 + BN <= (o + 1) * gm.rows || o == gm.owners - 1) {
+              tma_load_3d(sb, &gm.coarse[o], &full_bar[stage], k0, n0 - o * gm.rows, 0);
+            } else {
+              for (int r = 0; r < BN / 8; ++r) {
+                const int g = n0 + 8 * r;
+                const int og = min(g / gm.rows, gm.owners - 1);
+                tma_load_3d(sb + r * 1024, &gm.fine[og], &full_bar[stage], k0, g - og * gm.rows, 0);
+              }
+            }
+          } else if (B_MN) {
             for (int j = 0; j < b_blocks; ++j) tma_load_3d(sb + j * 8192, &mapB, &full_bar[stage], tn * BN + 64 * j, k0, b);
           } else {
             tma_load_3d(sb, &mapB, &full_bar[stage], k0, tn * BN, b);
@@ -650,15 +679,26 @@ int num_sms() {
 
 bool fill_scatter(KParams& p, const GemmArgs& a);
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, class GM = NoGather>
 int launch_t(const GemmArgs& a, cudaStream_t stream) {
   using C = Cfg<BN>;
+  constexpr bool kGather = std::is_same<GM, GatherMaps>::value;
   CUtensorMap ma, mb;
+  GM gm{};
   // A: K-major -> (K, M) rows of K; MN-major -> (M, K) rows of M.
   bool ok = A_MN ? make_map(&ma, a.A, a.M, a.K, a.batch, a.lda, a.strideA, 64)
                  : make_map(&ma, a.A, a.K, a.M, a.batch, a.lda, a.strideA, BM);
-  ok = ok && (B_MN ? make_map(&mb, a.B, a.N, a.K, a.batch, a.ldb, a.strideB, 64)
-                   : make_map(&mb, a.B, a.K, a.N, a.batch, a.ldb, a.strideB, BN));
+  if constexpr (kGather) {
+    gm.rows = a.gather_rows;
+    gm.owners = a.gather_n;
+    for (int o = 0; ok && o < a.gather_n; ++o)
+      ok = make_map(&gm.coarse[o], a.gather_src[o], a.K, a.gather_rows, 1, a.ldb, 0, BN) &&
+           make_map(&gm.fine[o], a.gather_src[o], a.K, a.gather_rows, 1, a.ldb, 0, 8);
+    mb = gm.coarse[0];                       // unused by the gathering kernel
+  } else {
+    ok = ok && (B_MN ? make_map(&mb, a.B, a.N, a.K, a.batch, a.ldb, a.strideB, 64)
+                     : make_map(&mb, a.B, a.K, a.N, a.batch, a.ldb, a.strideB, BN));
+  }
   if (!ok) return 2;
   KParams p;
   p.M = a.M; p.N = a.N; p.K = a.K; p.batch = a.batch;
@@ -680,7 +720,7 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
   }
   if (!fill_scatter(p, a)) return 5;
   const int grid = std::min(p.units, num_sms());
-  auto kern = gemm_kernel<BN, A_MN, B_MN>;
+  auto kern = gemm_kernel<BN, A_MN, B_MN, GM>;
   static bool attr_set[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
@@ -691,7 +731,7 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
   if (std::getenv("VAGUS_GEMM_DEBUG"))
     std::fprintf(stderr, "[gemm] launch grid %d smem %d M %d N %d K %d units %d\n", grid, C::SMEM_BYTES, a.M, a.N,
                  a.K, p.units);
-  kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p);
+  kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, gm);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -835,6 +875,21 @@ bool encode_f32_map(void* map, const void* base, int rank, const unsigned long l
 int gemm_launch(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0 || a.batch <= 0) return 0;
   if (a.K <= 0) return 4;
+  if (a.gather_n > 0) {
+    // gathered B: K-major, one matrix, one-CTA tiles no wider than an owner's rows
+    if (a.gather_n > kMaxGather || a.b_mn || a.batch != 1 || a.gather_rows < 128 || a.gather_rows % 8 ||
+        (long long)a.gather_n * a.gather_rows < a.N || a.K < 64 || (a.ldb % 8) || a.ldb < a.K)
+      return 7;
+    for (int o = 0; o < a.gather_n; ++o)
+      if (!a.gather_src[o] || (reinterpret_cast<uintptr_t>(a.gather_src[o]) & 15u)) return 1;
+    if ((reinterpret_cast<uintptr_t>(a.A) & 15u) || (a.lda % 8)) return 1;
+    const long long a_inner = a.a_mn ? a.M : a.K, a_rows = a.a_mn ? a.K : a.M;
+    if (a_inner < 64 || a_rows < (a.a_mn ? 64 : BM)) return 6;
+    const int bn = (a.block_n == 128 || a.gather_rows < 256 || a.N < 256) ? 128 : 256;
+    if (a.a_mn)
+      return bn == 128 ? launch_t<128, true, false, GatherMaps>(a, stream) : launch_t<256, true, false, GatherMaps>(a, stream);
+    return bn == 128 ? launch_t<128, false, false, GatherMaps>(a, stream) : launch_t<256, false, false, GatherMaps>(a, stream);
+  }
   // TMA: base 16-byte aligned, row pitch a multiple of 16 bytes
   auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
   if (!aligned(a.A) || !aligned(a.B) || (a.lda % 8) || (a.ldb % 8)) return 1;

@@ -34,6 +34,15 @@ struct GemmArgs {
   void* scatter_dst[16] = {};
   long long dst_ld = 0, dst_stride = 0;
   int scatter_batch0 = 0;
+  // Gathered B (K-major, batch 1, one-CTA tiles): B's rows live in gather_n
+  // buffers of gather_rows rows each (row pitch ldb) -- typically the row
+  // shards of a weight held by the GPUs of a group, which the TMA loads of
+  // this GEMM then read over NVLink (no multicast) -- rows
+  // [o * gather_rows, (o + 1) * gather_rows) in gather_src[o].  `B` is not
+  // read.  gather_rows must be a multiple of 8 and at least 128.
+  int gather_n = 0;
+  int gather_rows = 0;
+  const void* gather_src[8] = {};
 };
 
 // Returns 0 on launch, nonzero on argument / encode / launch failure.
