@@ -250,3 +250,58 @@ class MuonExchange:
         for r, b in enumerate(self.bases):
             C.comm_heap_close(b, r == self.rank)
         self.bases = []
+
+
+class PeerRowShards:
+    """A weight whose row shards live in the CUDA-IPC heaps of a group's GPUs
+    and are read in place by the GEMM that consumes the weight: the
+    all-gather fused into that GEMM (``gemm_gather``: per-owner TMA maps over
+    the peers' shards, no multicast), so the gathered weight is never
+    materialised and its bytes cross NVLink inside the product's loads.
+
+    Rank r holds rows ``[r rows, (r + 1) rows)`` of a ``(world rows, cols)``
+    bf16 matrix (``rows`` a multiple of 8, at least 128).  ``publish()`` is
+    the epoch barrier after which the peers may read updated shards;
+    ``linear(x, n)`` is ``x @ W[:n]^T``."""
+
+    def __init__(self, group, rows: int, cols: int):
+        assert rows % 8 == 0 and rows >= 128 and cols % 8 == 0 and cols >= 64, "shard shape"
+        C = native()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        assert self.world <= 8, "at most 8 owners"
+        self.rows, self.cols = rows, cols
+        ptr, handle = C.comm_heap_create(HEADER + (rows * cols * 2 + 255) // 256 * 256)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        self.own = ptr
+        self.bases = [ptr if r == self.rank else C.comm_heap_open(h) for r, h in enumerate(handles)]
+        self.epoch = 0
+        dist.barrier(group=group)
+
+    def local(self) -> torch.Tensor:
+        """This rank's shard, (rows, cols) bf16, writable in place."""
+        return native().comm_heap_view(self.own, HEADER, self.rows * self.cols, torch.bfloat16).view(self.rows,
+                                                                                                     self.cols)
+
+    def publish(self) -> None:
+        self.epoch += 1
+        native().comm_barrier(self.bases, self.rank, self.epoch)
+
+    def linear(self, x: torch.Tensor, n: int | None = None, out_dtype=torch.bfloat16) -> torch.Tensor:
+        n = self.world * self.rows if n is None else n
+        x2 = x.reshape(-1, self.cols)
+        if x2.dtype != torch.bfloat16 or x2.stride(-1) != 1:
+            x2 = x2.to(torch.bfloat16).contiguous()
+        out = torch.empty(x2.shape[0], n, device=x.device, dtype=out_dtype)
+        rc = native().gemm_gather(x2, False, [b + HEADER for b in self.bases], self.rows, self.cols, out)
+        if rc:
+            raise RuntimeError(f"gemm_gather rejected the problem (code {rc})")
+        return out.view(*x.shape[:-1], n)
+
+    def close(self) -> None:
+        C = native()
+        for r, b in enumerate(self.bases):
+            C.comm_heap_close(b, r == self.rank)
+        self.bases = []
