@@ -324,6 +324,10 @@ def train(config: TrainConfig, teardown: bool = True):
 
     amp_dtype = DTYPES[config.dtype]
     assert amp_dtype is not torch.float16, "fp16 (GradScaler) path not implemented"
+    if is_fsdp and device.type == "cpu" and amp_dtype is torch.float32 and config.fsdp_param_dtype != "float32":
+        # CUDA's linear kernels take an fp32 input against bf16 weights; the CPU ops do not
+        raise ValueError(f"on CPU, dtype=float32 needs fsdp_param_dtype=float32 (got {config.fsdp_param_dtype}); "
+                         "bf16 FSDP parameters pair with dtype=bfloat16 (autocast)")
     autocast = torch.autocast(device.type, dtype=amp_dtype) if amp_dtype is not torch.float32 else nullcontext()
     ce_fn = make_ce(config.ce_impl, z_loss=config.z_loss or 0.0, chunk_rows=config.ce_chunk_rows,
                     compute_dtype=amp_dtype if amp_dtype is not torch.float32 else None)
