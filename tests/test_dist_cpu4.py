@@ -1,5 +1,6 @@
 """Four gloo ranks on CPU emulating a 2-node x 2-GPU job: HSDP (2 x 2) and
-FSDP2 (shard 4) loss / gradient-norm traces equal DDP's; the sharded Muon
+FSDP2 (shard 4) loss / gradient-norm traces equal DDP's (fp32; and bf16 HSDP
+vs DDP under bf16 autocast within 1e-3); the sharded Muon
 step is bit-identical to the same step on replicated parameters, buckets
 that do not divide by the world included; and train() under HSDP writes
 checkpoints from which a resumed run reproduces the straight run exactly."""
@@ -30,7 +31,7 @@ def _env(rank, port):
                       LOCAL_RANK=str(rank))
 
 
-def _trace(mode, opt_name, rank, steps=3):
+def _trace(mode, opt_name, rank, steps=3, bf16=False):
     import torch.distributed as dist
     from torch.nn.parallel import DistributedDataParallel as DDP
     from vagus_b200.models import build_model
@@ -48,12 +49,13 @@ def _trace(mode, opt_name, rank, steps=3):
     else:
         mesh = build_mesh(2 if mode == "hsdp" else 4, dev, WORLD)
         model = LMLoss(model, ce)
-        apply_fsdp(model, mesh, "float32", "float32")
+        apply_fsdp(model, mesh, "bfloat16" if bf16 else "float32", "float32")
     args = dict(lr=1e-2, weight_decay=0.1) if opt_name == "adamw" else \
         dict(lr=2e-2, weight_decay=0.1, adamw=dict(lr=1e-2, weight_decay=0.1))
     opt = build_optimizer(opt_name, unwrap(model), args)
+    amp = torch.autocast("cpu", dtype=torch.bfloat16) if bf16 else None
     runner = StepRunner(model, opt, ce, dev, grad_accum_steps=2, grad_clip=1.0, is_fsdp=mode != "ddp",
-                        is_dist=True, mesh=mesh)
+                        is_dist=True, mesh=mesh, autocast=amp)
     g = torch.Generator().manual_seed(123 + rank)
     batches = []
     for _ in range(steps * 2):
@@ -109,6 +111,7 @@ def _worker(rank, port, tmp, q):
         setup_distributed("cpu", timeout_s=120)
         import torch.distributed as dist
         res = {"traces": {o: {m: _trace(m, o, rank) for m in ("ddp", "hsdp", "fsdp")} for o in ("adamw", "muon")},
+               "bf16": {m: _trace(m, "adamw", rank, bf16=True) for m in ("ddp", "hsdp")},
                "muon_bitwise": _sharded_muon_bitwise()}
         from vagus_b200.train import main as tm
         tm.train(_train_cfg(tmp, "a", 6), teardown=False)
@@ -145,6 +148,9 @@ def test_hsdp_fsdp_ddp_parity_sharded_muon_and_resume(tmp_path):
                 for (la, ga), (lb, gb) in zip(tr["ddp"], tr[mode]):
                     assert abs(la - lb) <= tol * max(1.0, abs(la)), (opt_name, mode, la, lb)
                     assert abs(ga - gb) <= tol * max(1.0, abs(ga)) * 10, (opt_name, mode, ga, gb)
+        # bf16: HSDP's bf16 parameter all-gathers vs DDP under bf16 autocast
+        for (la, _), (lb, _) in zip(res["bf16"]["ddp"], res["bf16"]["hsdp"]):
+            assert abs(la - lb) <= 1e-3 * max(1.0, abs(la)), ("bf16", la, lb)
     a = torch.load(tmp_path / "a" / "ckpt-00000006.pt", weights_only=False)
     b = torch.load(tmp_path / "b" / "ckpt-00000006.pt", weights_only=False)
     assert a["step"] == b["step"] == 6 and a["tokens_seen"] == b["tokens_seen"]
