@@ -271,6 +271,8 @@ class PeerRowShards:
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         assert self.world <= 8, "at most 8 owners"
+        if not same_host(group):
+            raise RuntimeError("PeerRowShards: CUDA IPC reaches the GPUs of one machine only")
         self.rows, self.cols = rows, cols
         ptr, handle = C.comm_heap_create(HEADER + (rows * cols * 2 + 255) // 256 * 256)
         handles = [None] * self.world
