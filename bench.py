@@ -348,6 +348,30 @@ def run(args) -> dict:
     torch.cuda.synchronize()
     opt_ms = _max_over_ranks(o0.elapsed_time(o1) / 3, is_dist)
 
+    # opt-in (--exposed-comm, FSDP on our NVLink collectives): the same steps
+    # with the FSDP2 all-gathers / reduce-scatters switched off; the
+    # difference to the timed step is the communication the compute did not hide
+    exposed = None
+    if args.exposed_comm and is_dist and args.impl != "reference" and args.comm == "nvlink":
+        from vagus_b200.parallel import nvlink as nvl
+        nvl.set_dry_run(True)
+        for _ in range(2):
+            step(dev_iter)
+        dist.barrier()
+        torch.cuda.synchronize()
+        d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        d0.record()
+        for _ in range(args.steps):
+            step(dev_iter)
+        d1.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        nvl.set_dry_run(False)
+        dry_ms = _max_over_ranks(d0.elapsed_time(d1) / args.steps, is_dist)
+        exposed = {"ms_per_step_without_fsdp_collectives": round(dry_ms, 2), "exposed_ms": round(ms - dry_ms, 2),
+                   "pct_of_step": round(100.0 * (ms - dry_ms) / ms, 2),
+                   "covers": "FSDP2 parameter all-gathers and gradient reduce-scatters"}
+
     tokens_per_step = cfg["global_tokens"]
     value = tokens_per_step / (ms / 1e3)
     e2e = tokens_per_step / (e2e_ms / 1e3)
@@ -370,6 +394,8 @@ def run(args) -> dict:
         "max_mem_gb": round(torch.cuda.max_memory_allocated() / 1e9, 1),
         "optimizer_step_ms": round(opt_ms, 2),
     }
+    if exposed is not None:
+        out["exposed_comm"] = exposed
     if args.impl == "reference":
         out["impl"] = "reference"
     if is_dist:
@@ -388,6 +414,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gdn340m")
     ap.add_argument("--micro", type=int, default=0, help="sequences per micro-batch (0: the config's default)")
+    ap.add_argument("--exposed-comm", action="store_true",
+                    help="N > 1: also time the steps with the FSDP2 collectives off and report the exposed share")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -231,3 +231,18 @@ def test_dead_rank_is_detected_by_the_next_collective():
         p.join(timeout=60)
     assert out[1] == "left"
     assert out[0].startswith("detected"), out[0]
+
+
+def test_collective_dry_run_switch():
+    """The exposed-communication probe's switch: while on, the FSDP2 hooks
+    return before touching their heap (None here) or any process group."""
+    from vagus_b200.parallel import nvlink
+    ag, rs = nvlink.NvlinkAllGather(None), nvlink.NvlinkReduceScatter(None)
+    nvlink.set_dry_run(True)
+    try:
+        assert ag(torch.empty(4), torch.empty(2), None) is None
+        assert rs(torch.empty(2), torch.empty(4), None, None) is None
+    finally:
+        nvlink.set_dry_run(False)
+    with pytest.raises(AttributeError):
+        ag(torch.empty(4), torch.empty(2), None)          # off again: the real path needs a heap

@@ -84,6 +84,18 @@ class NvlinkHeap:
         self.bases = []
 
 
+_DRY_RUN = False
+
+
+def set_dry_run(on: bool) -> None:
+    """Timing probe: while on, the FSDP2 all-gather / reduce-scatter hooks
+    return without communicating (parameters and gradients are then garbage),
+    so a step timed in this mode is the step's compute alone and the
+    difference to a normal step is its exposed communication."""
+    global _DRY_RUN
+    _DRY_RUN = bool(on)
+
+
 class NvlinkAllGather(AllGather):
     def __init__(self, heap: NvlinkHeap):
         self.heap = heap
@@ -92,6 +104,8 @@ class NvlinkAllGather(AllGather):
         return torch.empty(*size, dtype=dtype, device=device)
 
     def __call__(self, output_tensor, input_tensor, group, async_op: bool = False):
+        if _DRY_RUN:
+            return None
         h = self.heap
         shard_bytes = input_tensor.numel() * input_tensor.element_size()
         if shard_bytes > h.ag_cap or not output_tensor.is_contiguous():
@@ -113,6 +127,8 @@ class NvlinkReduceScatter(ReduceScatter):
         return torch.empty(*size, dtype=dtype, device=device)
 
     def __call__(self, output_tensor, input_tensor, group, op, async_op: bool = False):
+        if _DRY_RUN:
+            return None
         h = self.heap
         if op == dist.ReduceOp.SUM:
             scale = 1.0
