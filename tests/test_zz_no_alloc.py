@@ -1,7 +1,8 @@
 # The allocation-free fused linear cross-entropy entry point, called through
 # its exported C symbol the way a caller that cannot allocate would (for
-# example code inside a captured CUDA graph region, or a host runtime whose
-# own allocator owns the device): every buffer is supplied by the caller and
+# example a host runtime whose own allocator owns the device's memory, or a
+# latency-critical loop that must stay out of the driver's allocation
+# paths): every buffer is supplied by the caller and
 # the routine's own working memory is a fixed device array inside the
 # library.  Checked against the regular fused_linear_ce op on two calls in a
 # row (the second call must not see stale accumulators from the first).

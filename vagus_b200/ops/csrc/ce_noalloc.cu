@@ -1,12 +1,12 @@
 // Allocation-free entry point of the fused linear cross-entropy.
 //
 // Declaration: this entry point has no counterpart in the reference.  It
-// exists for callers that cannot allocate device memory at call time:
-// code running inside a captured or replayed CUDA graph region, code
-// embedded in another runtime whose allocator owns the device (and would
-// deadlock or fragment if a second allocator called cudaMalloc behind its
-// back), and real-time loops that must not hit the driver's allocation
-// paths.  Such a caller still provides every input and output buffer; the
+// exists for callers that cannot allocate device memory at call time: code
+// embedded in another runtime whose own allocator owns the device's memory
+// (a second allocator calling cudaMalloc behind its back would contend with
+// its pool or fragment it), and latency-critical loops that must not enter
+// the driver's allocation paths (cudaMalloc / cudaFree can synchronise the
+// device).  Such a caller still provides every input and output buffer; the
 // only memory this routine needs beyond them -- one chunk of bf16 logits and
 // a few per-row scalars -- lives in a fixed file-scope device array.
 //
