@@ -131,3 +131,16 @@ def test_every_recipe_loads_and_builds():
             assert c.world_size * c.batch_size * c.grad_accum_steps * c.context_len == c.global_batch_tokens, f
         with torch.device("meta"):
             build_model(c.model_name, c.model_args)
+
+
+def test_console_scripts_resolve():
+    """Every console script of pyproject.toml names an importable callable."""
+    import importlib
+    import tomllib
+    from pathlib import Path
+    meta = tomllib.loads((Path(__file__).resolve().parents[1] / "pyproject.toml").read_text())
+    scripts = meta["project"]["scripts"]
+    assert {"vagus-b200-train", "vagus-b200-eval"} <= set(scripts)
+    for target in scripts.values():
+        mod, _, fn = target.partition(":")
+        assert callable(getattr(importlib.import_module(mod), fn)), target
