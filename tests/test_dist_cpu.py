@@ -91,3 +91,75 @@ def test_fsdp_matches_ddp_gloo():
             for (la, ga), (lb, gb) in zip(res[opt_name]["ddp"], res[opt_name]["fsdp"]):
                 assert abs(la - lb) <= tol * max(1.0, abs(la)), (opt_name, la, lb)
                 assert abs(ga - gb) <= tol * max(1.0, abs(ga)) * 10, (opt_name, ga, gb)
+
+
+def _layout_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                          LOCAL_RANK=str(rank))
+        from vagus_b200.parallel import setup_distributed
+        setup_distributed("cpu", timeout_s=120)
+        import torch.distributed as dist
+        from torch.distributed.fsdp import FSDPModule
+        from torch.distributed.fsdp._fully_shard._fsdp_api import AllGather
+        from vagus_b200.models import build_model
+        from vagus_b200.models.losses import make_ce
+        from vagus_b200.parallel import LMLoss, apply_fsdp, build_mesh
+        from vagus_b200.parallel.nvlink import unit_gather_layout
+
+        class Recorder(AllGather):
+            def __init__(self):
+                self.inputs = []
+
+            def allocate(self, size, *, dtype, device):
+                return torch.empty(*size, dtype=dtype, device=device)
+
+            def __call__(self, output_tensor, input_tensor, group, async_op=False):
+                self.inputs.append(input_tensor.detach().clone())
+                return dist.all_gather_into_tensor(output_tensor, input_tensor, group=group, async_op=async_op)
+
+        torch.manual_seed(0)
+        model = LMLoss(build_model("TransformerPP", dict(MODEL, vocab_size=301)), make_ce("full"))
+        apply_fsdp(model, build_mesh(world, torch.device("cpu"), world), "float32", "float32")
+        blk = model.module.blocks[0]
+        rec = Recorder()
+        blk.set_custom_all_gather(rec)
+        assert isinstance(blk, FSDPModule)
+        layout = unit_gather_layout(blk)
+        t = torch.randint(0, 301, (2, 33))
+        model(t[:, :-1], t[:, 1:])                    # one forward: the block's parameters are gathered
+        flat = rec.inputs[0]
+        errs = []
+        assert sum(e["numel"] for e in layout) == flat.numel()
+        assert any(e["shape"][0] % world for e in layout)       # an uneven shard is among them
+        for e in layout:
+            name = e["name"]
+            local = e["param"].to_local().detach().reshape(-1)       # this rank's (unpadded) shard
+            got = flat[e["offset"]:e["offset"] + local.numel()]
+            errs.append((name, (got - local).abs().max().item() if local.numel() else 0.0))
+            assert e["rows"] == -(-e["shape"][0] // world), e
+        dist.destroy_process_group()
+        q.put((rank, errs))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+        q.put((rank, traceback.format_exc() + repr(e)))
+
+
+def test_unit_gather_layout_matches_fsdp_all_gather_input():
+    """The layout that a GEMM reading weight shards in place relies on: each
+    parameter's shard sits at the predicted offset of the flat all-gather
+    input FSDP2 hands to a custom all-gather (3 ranks: 64-row weights are
+    split 22 / 22 / 20 and padded)."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_layout_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=300) for _ in range(world))
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs in results.items():
+        assert not isinstance(errs, str), errs
+        assert errs and all(e == 0.0 for _, e in errs), (rank, errs)

@@ -191,6 +191,31 @@ def use_nvlink_collectives(root, group=None) -> NvlinkHeap:
     return heap
 
 
+def unit_gather_layout(unit) -> list[dict]:
+    """Where each parameter that FSDP2 manages in ``unit`` sits in a rank's
+    flat all-gather input -- and so in every peer's all-gather staging slot,
+    which is what a GEMM that reads a weight's row shards in place needs:
+    FSDP2 concatenates the parameters' dim-0 shards, each padded to
+    ``ceil(rows / world)`` rows, in its parameter order.
+
+    One dict per parameter: ``name`` (relative to ``unit``), ``param`` (the
+    sharded parameter), ``offset`` (elements of the flat input), ``rows``
+    (padded rows per rank), ``shape`` (unsharded) and ``numel``."""
+    group = unit._get_fsdp_state()._fsdp_param_group
+    out: list[dict] = []
+    if group is None:
+        return out
+    names = {id(p): n for n, p in unit.named_parameters()}
+    off = 0
+    for fp in group.fsdp_params:
+        size = fp.padded_sharded_param_size
+        p = fp.sharded_param
+        out.append(dict(name=names.get(id(p)), param=p, offset=off, rows=int(size[0]) if len(size) else 0,
+                        shape=tuple(fp._orig_size), numel=int(size.numel())))
+        off += int(size.numel())
+    return out
+
+
 class MuonExchange:
     """IPC-shared receive buffers for the sharded Muon step's fused
     Newton-Schulz product + scatter (a GEMM followed by an all-to-all, as one
