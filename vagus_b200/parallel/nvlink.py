@@ -23,6 +23,13 @@ step: the last Newton-Schulz GEMM of each orthogonalised matrix scatters its
 output rows from the epilogue straight into the owning ranks' receive buffers
 (peer stores over NVLink), then one epoch barrier.
 
+``PeerRowShards`` is the all-gather fused into the consuming GEMM: a weight's
+row shards stay in the peers' heaps and the gathered-B GEMM reads them in
+place through per-owner TMA maps; ``unit_gather_layout`` gives where each
+FSDP2-managed parameter's shard sits in the all-gather staging slots.
+``set_dry_run`` switches the FSDP2 hooks off for the exposed-communication
+probe of ``bench.py``.
+
 Parity: the reference runs these collectives inside FSDP2 on NCCL
 (``infra/train/main.py:253-275``); the gradient reduction semantics (average
 over the data-parallel group, fp32) are the same.  Its sharded Muon
