@@ -116,7 +116,9 @@ def _layout_worker(rank, world, port, q):
 
             def __call__(self, output_tensor, input_tensor, group, async_op=False):
                 self.inputs.append(input_tensor.detach().clone())
-                return dist.all_gather_into_tensor(output_tensor, input_tensor, group=group, async_op=async_op)
+                dist.all_gather_into_tensor(output_tensor, input_tensor, group=group)
+                self.outputs = getattr(self, "outputs", []) + [output_tensor.detach().clone()]
+                return None
 
         torch.manual_seed(0)
         model = LMLoss(build_model("TransformerPP", dict(MODEL, vocab_size=301)), make_ce("full"))
@@ -138,6 +140,16 @@ def _layout_worker(rank, world, port, q):
             got = flat[e["offset"]:e["offset"] + local.numel()]
             errs.append((name, (got - local).abs().max().item() if local.numel() else 0.0))
             assert e["rows"] == -(-e["shape"][0] // world), e
+        # every rank's staging slot is its flat input: owner r's rows of a weight
+        # start at slot_r + offset, which is what the in-place GEMM reads
+        slots = rec.outputs[0].view(world, -1)
+        for e in layout:
+            if len(e["shape"]) != 2:
+                continue
+            rows, cols = e["rows"], e["shape"][1]
+            w = torch.cat([slots[r, e["offset"]:e["offset"] + rows * cols].view(rows, cols) for r in range(world)])
+            full = e["param"].full_tensor().detach()
+            errs.append((e["name"] + " (from slots)", (w[:e["shape"][0]] - full).abs().max().item()))
         dist.destroy_process_group()
         q.put((rank, errs))
     except Exception as e:  # noqa: BLE001
