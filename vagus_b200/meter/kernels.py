@@ -125,6 +125,14 @@ def _cases(B: int, L: int):
     dwp = torch.zeros(NP, D, device=dev)
     fl = 2 * T * D * NP
     cases["gemm_fwd"] = (lambda: gemm(a, False, wpk, False, c), None, fl)            # x W^T
+    # the same product with W's rows gathered from 8 owners' buffers (the fused
+    # all-gather's GEMM; local buffers stand in for the peers): 520-row shards,
+    # so tiles that straddle an owner boundary take 8-row boxes
+    owners = 8
+    rows_o = ((NP + owners - 1) // owners + 7) // 8 * 8      # rows per owner, a multiple of 8
+    shards = [r(rows_o, D) for _ in range(owners)]
+    ptrs = [t.data_ptr() for t in shards]
+    cases["gemm_gather_fwd"] = (lambda: C.gemm_gather(a, False, ptrs, rows_o, D, c), None, fl)
     cases["gemm_dgrad"] = (lambda: gemm(gp, False, wpk, True, da), None, fl)         # dy W
     cases["gemm_wgrad"] = (lambda: gemm(gp, True, a, True, dwp, atomic=True), None, fl)  # dW += dy^T x
 
