@@ -190,6 +190,18 @@ def test_kda_intra_stage_matches_vector_oracle():
         S = gam[:, :, n, :, None] * S + Kt[:, :, n].transpose(-1, -2) @ Vp
     o = torch.stack(outs, 2).permute(0, 2, 3, 1, 4).reshape(B, L, H, dv)
     assert (o - o_r.float()).abs().max() < 1e-5 and (S - S_r.float()).abs().max() < 1e-5
+    # gated linear attention (no delta rule): W = 0 and U = V on the same recurrence
+    o_r, S_r = chunk_scan_vec(q, k, v, g, None, S0, scale=scale, delta=False, chunk_size=64)
+    W, Qh, Kt, A, U, gam = kda_intra(q, k, v, g, beta, scale, delta=False)
+    assert torch.count_nonzero(W) == 0
+    S = S0.float()
+    outs = []
+    for n in range(L // 64):
+        Vp = U[:, :, n] - W[:, :, n] @ S
+        outs.append(Qh[:, :, n] @ S + A[:, :, n] @ Vp)
+        S = gam[:, :, n, :, None] * S + Kt[:, :, n].transpose(-1, -2) @ Vp
+    o = torch.stack(outs, 2).permute(0, 2, 3, 1, 4).reshape(B, L, H, dv)
+    assert (o - o_r.float()).abs().max() < 1e-5 and (S - S_r.float()).abs().max() < 1e-5
     # the sub-chunk factorisation equals the pairwise definition, also for fast channels
     X, Y = torch.randn(2, 64, 8, dtype=torch.float64), torch.randn(2, 64, 8, dtype=torch.float64)
     gg = (-torch.rand(2, 64, 8, dtype=torch.float64) * 6).cumsum(-2)
