@@ -13,7 +13,7 @@ import torch
 
 from vagus_b200.data.prepare import synthetic_store
 from vagus_b200.meter.examples import (bench_attention, bench_ce, bench_linear_attention, bench_rope,
-                                       probe_attention_health, saturation_curve, write_selectivity)
+                                       probe_attention_health, profile_step, saturation_curve, write_selectivity)
 from vagus_b200.meter.examples._common import parse_ckpts
 from vagus_b200.models import build_model
 
@@ -125,3 +125,12 @@ def test_bench_dist_gloo_two_ranks():
     p = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=240)
     assert p.returncode == 0, p.stderr[-2000:]
     assert "nccl all-gather" in p.stdout and "bus GB/s" in p.stdout
+
+
+def test_profile_step_on_cpu(tmp_path):
+    args = dict(ARGS, layer_pattern="gdn,softmax", layer_count=2)
+    r = profile_step.main(["--args", json.dumps(args), "--batch", "2", "--seq", "32", "--steps", "1", "--warmup", "1",
+                           "--out", str(tmp_path)])
+    assert any(p.endswith(".trace.json") for p in r["traces"].values())
+    assert profile_step.family("gemm_kernel<256, false, false>") == "gemm"
+    assert profile_step.family("gdr_bwd_scan_tc<256>") == "delta-rule"

@@ -7,6 +7,7 @@ benchmarks (CUDA-event timing through ``meter.compare``)
   bench_linear_attention   the chunked delta-rule family on the kernels vs the torch chunk oracle
   bench_rope               fused qk-norm + RoPE vs plain torch
   bench_dist               all-gather / reduce-scatter bus bandwidth: NVLink kernels vs NCCL (torchrun)
+  profile_step             one model's training step under torch.profiler, device time by kernel family
 
 probes on trained checkpoints
   saturation_curve         per-position delta-rule residual |v - S^T k| / |v|: where the state stops learning
