@@ -5,11 +5,12 @@
 #
 #   srun --kill-on-bad-exit=1 recipe/slurm/torchrun_node.sh <train recipe> [key=value ...]
 #
-# --shutdown_timeout gives the workers time to write their recent checkpoint
-# after a SIGTERM / SIGUSR1 (walltime forwarding) before the agent kills them.
+# --signals-to-handle adds SIGUSR1 (the walltime warning the batch script
+# forwards) to the signals torchrun passes on to its workers, whose handler
+# makes the trainer stop at the next step boundary with a checkpoint.
 cd "${VAGUS_B200_HOME:-$HOME/vagus-b200}" || exit 1
 exec python -m torch.distributed.run \
-    --nnodes "${SLURM_NNODES:-1}" --nproc_per_node "${GPUS_PER_NODE:-8}" --node_rank "${SLURM_NODEID:-0}" \
-    --rdzv_backend c10d --rdzv_endpoint "$MASTER_ADDR:$MASTER_PORT" --rdzv_id "${SLURM_JOB_ID:-local}" \
-    --shutdown_timeout 900 \
+    --nnodes "${SLURM_NNODES:-1}" --nproc-per-node "${GPUS_PER_NODE:-8}" --node-rank "${SLURM_NODEID:-0}" \
+    --rdzv-backend c10d --rdzv-endpoint "$MASTER_ADDR:$MASTER_PORT" --rdzv-id "${SLURM_JOB_ID:-local}" \
+    --signals-to-handle SIGTERM,SIGINT,SIGHUP,SIGQUIT,SIGUSR1 \
     -m vagus_b200.train.main "$@"

@@ -1,0 +1,41 @@
+"""The SLURM per-node launcher (recipe/slurm/torchrun_node.sh) run the way
+srun runs it, with the SLURM variables set by hand: torchrun starts two CPU
+workers on gloo that train a tiny recipe to completion (final model written)."""
+
+import os
+import socket
+import subprocess
+from pathlib import Path
+
+import yaml
+
+from vagus_b200.data.prepare import synthetic_store
+
+ROOT = Path(__file__).resolve().parents[1]
+MODEL = dict(vocab_size=300, dim=64, layer_count=2, head_dim=32, context_len=64, ffn_hidden_dim=128)
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_torchrun_node_launcher_trains_a_tiny_recipe(tmp_path):
+    synthetic_store(tmp_path / "tok", tokens=40_000, vocab=300, seed=1)
+    recipe = dict(run_name="launch", data_dir=str(tmp_path / "tok"), model_name="TransformerPP", model_args=MODEL,
+                  optimizer_name="adamw", optimizer_args=dict(lr=1e-3), context_len=32, batch_size=2,
+                  grad_accum_steps=1, train_tokens=4 * 2 * 2 * 32, world_size=2, shard_size=1, device="cpu",
+                  dtype="float32", compile=False, ce_impl="full", run_dir=str(tmp_path / "run"), log_interval=1,
+                  slow_interval=1000, deadline_margin_s=None, recent_ckpt_minutes=1e9)
+    path = tmp_path / "tiny.yaml"
+    path.write_text(yaml.safe_dump(recipe))
+    env = {**os.environ, "VAGUS_B200_HOME": str(ROOT), "SLURM_NNODES": "1", "GPUS_PER_NODE": "2", "SLURM_NODEID": "0",
+           "SLURM_JOB_ID": "cpu-test", "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(_port()),
+           "CUDA_VISIBLE_DEVICES": ""}
+    p = subprocess.run(["bash", str(ROOT / "recipe" / "slurm" / "torchrun_node.sh"), str(path)], env=env,
+                       capture_output=True, text=True, timeout=600)
+    assert p.returncode == 0, (p.stdout[-2000:], p.stderr[-3000:])
+    assert (tmp_path / "run" / "model-final.pt").exists()
