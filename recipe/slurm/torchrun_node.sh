@@ -7,7 +7,8 @@
 #
 # --signals-to-handle adds SIGUSR1 (the walltime warning the batch script
 # forwards) to the signals torchrun passes on to its workers, whose handler
-# makes the trainer stop at the next step boundary with a checkpoint.
+# makes the trainer stop at the next step boundary with a checkpoint (torchrun
+# then exits non-zero; the batch script ignores srun's status and re-queues).
 cd "${VAGUS_B200_HOME:-$HOME/vagus-b200}" || exit 1
 exec python -m torch.distributed.run \
     --nnodes "${SLURM_NNODES:-1}" --nproc-per-node "${GPUS_PER_NODE:-8}" --node-rank "${SLURM_NODEID:-0}" \

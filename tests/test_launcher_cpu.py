@@ -39,3 +39,44 @@ def test_torchrun_node_launcher_trains_a_tiny_recipe(tmp_path):
                        capture_output=True, text=True, timeout=600)
     assert p.returncode == 0, (p.stdout[-2000:], p.stderr[-3000:])
     assert (tmp_path / "run" / "model-final.pt").exists()
+
+
+def test_sigusr1_through_the_launcher_stops_with_a_checkpoint(tmp_path):
+    """The walltime path: SIGUSR1 to the node launcher (what srun relays from
+    the batch script's trap) reaches both workers through torchrun; they stop
+    at a step boundary with a recent checkpoint before the planned end (no
+    final model).  torchrun itself exits non-zero after a forwarded signal;
+    the batch script tolerates that and re-queues the run."""
+    import signal
+    import time
+    synthetic_store(tmp_path / "tok", tokens=200_000, vocab=300, seed=1)
+    recipe = dict(run_name="walltime", data_dir=str(tmp_path / "tok"), model_name="TransformerPP",
+                  model_args=MODEL, optimizer_name="adamw", optimizer_args=dict(lr=1e-3), context_len=32,
+                  batch_size=2, grad_accum_steps=1, train_tokens=100_000 * 2 * 2 * 32, world_size=2, shard_size=1,
+                  device="cpu", dtype="float32", compile=False, ce_impl="full", run_dir=str(tmp_path / "run"),
+                  log_interval=1, slow_interval=100_000, deadline_margin_s=None, recent_ckpt_minutes=1e9)
+    path = tmp_path / "long.yaml"
+    path.write_text(yaml.safe_dump(recipe))
+    env = {**os.environ, "VAGUS_B200_HOME": str(ROOT), "SLURM_NNODES": "1", "GPUS_PER_NODE": "2", "SLURM_NODEID": "0",
+           "SLURM_JOB_ID": "cpu-test", "MASTER_ADDR": "127.0.0.1", "MASTER_PORT": str(_port()),
+           "CUDA_VISIBLE_DEVICES": ""}
+    proc = subprocess.Popen(["bash", str(ROOT / "recipe" / "slurm" / "torchrun_node.sh"), str(path)], env=env,
+                            stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+    metrics = tmp_path / "run" / "metrics.jsonl"
+    try:
+        t0 = time.time()
+        while time.time() - t0 < 300:
+            if metrics.exists() and len(metrics.read_text().splitlines()) >= 3:
+                break
+            if proc.poll() is not None:
+                break
+            time.sleep(0.5)
+        assert proc.poll() is None, "the run ended before the signal"
+        proc.send_signal(signal.SIGUSR1)           # bash exec'd torchrun: this is the agent's pid
+        out, err = proc.communicate(timeout=300)
+    finally:
+        if proc.poll() is None:
+            proc.kill()
+    assert "stop signal received" in out and "final recent checkpoint" in out, (out[-2000:], err[-3000:])
+    assert (tmp_path / "run" / "recent.pt").exists()
+    assert not (tmp_path / "run" / "model-final.pt").exists()
