@@ -27,9 +27,8 @@ wait "$SRUN_PID" 2>/dev/null || true
 # chain guard: resubmit while the run has not written model-final.pt
 RUN=$(python - "$RECIPE" "$@" <<'PY'
 import sys
-from vagus_b200.train.main import TrainConfig
-c = TrainConfig.from_yaml(sys.argv[1], sys.argv[2:])
-print(c.run_dir or "")
+from vagus_b200.train.main import TrainConfig, resolve_run_dir
+print(resolve_run_dir(TrainConfig.from_yaml(sys.argv[1], sys.argv[2:])))
 PY
 )
 if [ -n "$RUN" ] && [ ! -f "$RUN/model-final.pt" ]; then

@@ -80,3 +80,27 @@ def test_sigusr1_through_the_launcher_stops_with_a_checkpoint(tmp_path):
     assert "stop signal received" in out and "final recent checkpoint" in out, (out[-2000:], err[-3000:])
     assert (tmp_path / "run" / "recent.pt").exists()
     assert not (tmp_path / "run" / "model-final.pt").exists()
+
+
+def test_chain_guard_finds_the_run_of_a_recipe_without_run_dir(tmp_path):
+    """The batch script re-queues until <run>/model-final.pt exists; for a
+    recipe that leaves run_dir unset it must look where train() writes
+    (out_root/<run_name>-<commit8>), so its snippet runs the same resolver."""
+    import re
+    import sys
+    from vagus_b200.train import main as tm
+    synthetic_store(tmp_path / "tok", tokens=40_000, vocab=300, seed=1)
+    recipe = dict(run_name="guard", data_dir=str(tmp_path / "tok"), model_name="TransformerPP", model_args=MODEL,
+                  optimizer_name="adamw", optimizer_args=dict(lr=1e-3), context_len=32, batch_size=2,
+                  train_tokens=2 * 2 * 32, device="cpu", dtype="float32", compile=False, ce_impl="full",
+                  out_root=str(tmp_path / "runs"), log_interval=1, slow_interval=1000, deadline_margin_s=None)
+    path = tmp_path / "guard.yaml"
+    path.write_text(yaml.safe_dump(recipe))
+    run = tm.train(tm.TrainConfig.from_yaml(str(path)))
+    assert (run / "model-final.pt").exists()
+    sbatch = (ROOT / "recipe" / "slurm" / "b200_train.sbatch").read_text()
+    snippet = re.search(r"<<'PY'\n(.*?)\nPY\n", sbatch, re.S).group(1)
+    p = subprocess.run([sys.executable, "-", str(path)], input=snippet, capture_output=True, text=True, timeout=120,
+                       cwd=ROOT)
+    assert p.returncode == 0, p.stderr[-2000:]
+    assert Path(p.stdout.strip()) == run

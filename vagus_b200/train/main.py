@@ -272,6 +272,16 @@ def request_stop() -> None:
     _STOP = True
 
 
+def resolve_run_dir(config: TrainConfig, code: dict | None = None) -> Path:
+    """The run's directory: ``run_dir`` when the recipe sets it, else
+    ``<out_root>/<run_name>-<commit8>`` (the code version is part of a run's
+    identity).  Batch scripts call this to find the run they re-queue."""
+    if config.run_dir:
+        return Path(config.run_dir)
+    code = git_state() if code is None else code
+    return Path(config.out_root) / f"{config.run_name}-{(code['commit'] or 'nogit')[:8]}"
+
+
 def train(config: TrainConfig, teardown: bool = True):
     global _STOP
     _STOP = False
@@ -309,8 +319,7 @@ def train(config: TrainConfig, teardown: bool = True):
         torch.backends.cudnn.allow_tf32 = True
 
     code = git_state()
-    commit8 = (code["commit"] or "nogit")[:8]
-    run_dir = Path(config.run_dir) if config.run_dir else Path(config.out_root) / f"{config.run_name}-{commit8}"
+    run_dir = resolve_run_dir(config, code)
     resume_from = find_resume(run_dir) if run_dir.exists() else None
     if run_dir.exists() and resume_from is None and any(run_dir.iterdir()):
         raise FileExistsError(f"{run_dir} exists without checkpoints; refusing a silent overwrite")
