@@ -80,6 +80,17 @@ def test_sigusr1_through_the_launcher_stops_with_a_checkpoint(tmp_path):
     assert "stop signal received" in out and "final recent checkpoint" in out, (out[-2000:], err[-3000:])
     assert (tmp_path / "run" / "recent.pt").exists()
     assert not (tmp_path / "run" / "model-final.pt").exists()
+    # the re-queued job: same recipe, resumes from recent.pt and finishes (a
+    # shorter token budget here so it ends quickly)
+    import torch
+    done = torch.load(tmp_path / "run" / "recent.pt", weights_only=False)["step"]
+    env["MASTER_PORT"] = str(_port())
+    p = subprocess.run(["bash", str(ROOT / "recipe" / "slurm" / "torchrun_node.sh"), str(path),
+                        f"train_tokens={(done + 2) * 2 * 2 * 32}"], env=env, capture_output=True, text=True,
+                       timeout=600)
+    assert p.returncode == 0, (p.stdout[-2000:], p.stderr[-3000:])
+    assert f"resumed from recent.pt at step {done:,}" in p.stdout, p.stdout[-2000:]
+    assert torch.load(tmp_path / "run" / "model-final.pt", weights_only=False)["step"] == done + 2
 
 
 def test_chain_guard_finds_the_run_of_a_recipe_without_run_dir(tmp_path):
