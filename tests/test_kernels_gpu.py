@@ -553,19 +553,32 @@ def test_bounded_wait_timeout_reports_and_context_survives():
     """Failure detection on the device without a fault: the cross-GPU epoch
     barrier waits for a peer flag that nothing sets (a second heap in this
     process stands in for a peer that never arrives), gives up after its
-    budget, records kErrTimeoutPeer in the host-mapped error word and returns;
-    the host raises on it, and the context keeps working."""
+    budget (set to 1 s here), records kErrTimeoutPeer in the host-mapped error
+    word and returns; the host raises on it, and the context keeps working.
+    A second barrier issued after the failure returns at once: the error word
+    ends every later cross-GPU wait."""
     import time
     from vagus_b200 import ops
     C = ops.native()
     h0, _ = C.comm_heap_create(4096)
     h1, _ = C.comm_heap_create(4096)
-    t0 = time.time()
-    C.comm_barrier([h0, h1], 0, 1)
-    torch.cuda.synchronize()
-    waited = time.time() - t0
+    old = C.comm_wait_budget()
+    C.comm_set_wait_budget(1.0)
+    try:
+        t0 = time.time()
+        C.comm_barrier([h0, h1], 0, 1)
+        torch.cuda.synchronize()
+        waited = time.time() - t0
+        C.comm_set_wait_budget(30.0)
+        t1 = time.time()
+        C.comm_barrier([h0, h1], 0, 2)          # the flag never arrives either; the error word ends it
+        torch.cuda.synchronize()
+        second = time.time() - t1
+    finally:
+        C.comm_set_wait_budget(old)
     assert C.error_word() == 4, C.error_word()          # kErrTimeoutPeer
-    assert 0.5 < waited < 60, waited
+    assert 0.5 < waited < 20, waited
+    assert second < 5, second
     with pytest.raises(RuntimeError):
         ops.check_error()
     assert C.error_word() == 0

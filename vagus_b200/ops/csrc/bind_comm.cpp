@@ -17,6 +17,18 @@ using torch::Tensor;
 
 cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// Bound of every cross-GPU flag wait, in ns.  Ranks drift apart by seconds in
+// normal operation (rank 0 writing a checkpoint, a slow read), so this is the
+// process group's timeout rather than the 2 s bound of waits inside one CTA.
+unsigned long long g_peer_wait_ns = 300ull * 1000000000ull;
+
+void comm_set_wait_budget(double seconds) {
+  TORCH_CHECK(seconds > 0.0 && seconds < 86400.0, "comm_set_wait_budget: seconds in (0, 86400)");
+  g_peer_wait_ns = static_cast<unsigned long long>(seconds * 1e9);
+}
+
+double comm_wait_budget() { return static_cast<double>(g_peer_wait_ns) * 1e-9; }
+
 // Allocates this rank's heap (zeroed) and returns (device pointer, IPC handle bytes).
 std::tuple<int64_t, pybind11::bytes> comm_heap_create(int64_t bytes) {
   void* p = nullptr;
@@ -59,7 +71,8 @@ void comm_all_gather(Tensor out, std::vector<int64_t> bases, int64_t rank, int64
   const long long total = out.numel() * out.element_size();
   TORCH_CHECK(total % world == 0, "comm_all_gather: output must split evenly");
   const int rc = vagus::comm_all_gather(peers_of(bases), static_cast<int>(rank), world, static_cast<unsigned>(epoch),
-                                        out.data_ptr(), total / world, slot_cap, vagus_device_error_ptr(), stream());
+                                        out.data_ptr(), total / world, slot_cap, g_peer_wait_ns, vagus_device_error_ptr(),
+                                        stream());
   TORCH_CHECK(rc == 0, "comm_all_gather failed (code ", rc, ")");
 }
 
@@ -74,15 +87,15 @@ void comm_reduce_scatter(Tensor out, Tensor in, std::vector<int64_t> bases, int6
   const int rc = vagus::comm_reduce_scatter(peers_of(bases), static_cast<int>(rank), world,
                                             static_cast<unsigned>(epoch), in.data_ptr(), out.data_ptr(), out.numel(),
                                             static_cast<int>(in.element_size()), static_cast<float>(scale), ag_cap,
-                                            slot_cap, vagus_device_error_ptr(), stream());
+                                            slot_cap, g_peer_wait_ns, vagus_device_error_ptr(), stream());
   TORCH_CHECK(rc == 0, "comm_reduce_scatter failed (code ", rc, ")");
 }
 
 // Epoch barrier over the heaps (the generic flag block).
 void comm_barrier(std::vector<int64_t> bases, int64_t rank, int64_t epoch) {
   const int rc = vagus::comm_barrier(peers_of(bases), static_cast<int>(rank), static_cast<int>(bases.size()),
-                                     vagus::kCommBarFlags, static_cast<unsigned>(epoch), vagus_device_error_ptr(),
-                                     stream());
+                                     vagus::kCommBarFlags, static_cast<unsigned>(epoch), g_peer_wait_ns,
+                                     vagus_device_error_ptr(), stream());
   TORCH_CHECK(rc == 0, "comm_barrier failed (code ", rc, ")");
 }
 
@@ -101,6 +114,8 @@ Tensor comm_heap_view(int64_t ptr, int64_t offset, int64_t numel, at::ScalarType
 
 void register_comm_ops(pybind11::module& m) {
   m.def("comm_barrier", &comm_barrier);
+  m.def("comm_set_wait_budget", &comm_set_wait_budget, "bound of cross-GPU flag waits, seconds");
+  m.def("comm_wait_budget", &comm_wait_budget);
   m.def("comm_heap_view", &comm_heap_view);
   m.def("comm_heap_create", &comm_heap_create);
   m.def("comm_heap_open", &comm_heap_open);

@@ -11,9 +11,12 @@
 //   1. stage:   this rank's contribution -> its own slot (local copy);
 //   2. barrier: publish the copy (system-scope release), store e into every
 //               peer's flag word for this rank, then wait until every peer's
-//               flag in this heap reads >= e (acquire; bounded by a 2 s
-//               budget, after which the error word is set and the kernel
-//               returns);
+//               flag in this heap reads >= e (acquire).  The wait is bounded
+//               by a caller-given budget (the process group's timeout: ranks
+//               legitimately drift apart by seconds -- a checkpoint write, a
+//               slow data read); on expiry, or as soon as the error word
+//               holds an earlier failure, the kernel records
+//               kErrTimeoutPeer and returns;
 //   3. combine: all-gather copies each peer's slot into its place in the
 //               output; reduce-scatter sums this rank's rows of every peer's
 //               slot in fp32, scales (1/world for an average) and casts into
@@ -54,7 +57,8 @@ __global__ void stage_k(uint8_t* slot, const uint8_t* src, long long n) {
 }
 
 // one warp: lane p < world signals peer p and waits for peer p's flag
-__global__ void barrier_k(const CommPeers peers, int rank, int world, int flag_off, uint32_t epoch, int* err) {
+__global__ void barrier_k(const CommPeers peers, int rank, int world, int flag_off, uint32_t epoch,
+                          unsigned long long budget_ns, int* err) {
   const int lane = threadIdx.x;
   __threadfence_system();          // the staging copy (previous kernel) is visible system-wide
   if (lane < world) {
@@ -68,9 +72,13 @@ __global__ void barrier_k(const CommPeers peers, int rank, int world, int flag_o
       const unsigned long long t0 = globaltimer_ns();
       uint32_t spins = 0;
       while (ld_acquire_sys(mine) < epoch) {
-        if (((++spins) & 1023u) == 0u && globaltimer_ns() - t0 > kWaitBudgetNs) {
-          ok = false;
-          break;
+        if (((++spins) & 1023u) == 0u) {
+          // an earlier failure (another wait that ran out) ends this one too,
+          // so a dead peer costs one budget, not one per collective
+          if (globaltimer_ns() - t0 > budget_ns || (err != nullptr && *(volatile int*)err != 0)) {
+            ok = false;
+            break;
+          }
         }
       }
     }
@@ -138,13 +146,13 @@ int grid_for(long long bytes) {
 }  // namespace
 
 int comm_all_gather(const CommPeers& peers, int rank, int world, uint32_t epoch, void* out, long long shard_bytes,
-                    long long slot_cap, int* err, cudaStream_t st) {
+                    long long slot_cap, unsigned long long wait_ns, int* err, cudaStream_t st) {
   if (world < 2 || world > kMaxCommPeers || shard_bytes > slot_cap) return 5;
   const long long slot_off = kCommHeaderBytes + (long long)(epoch & 1u) * slot_cap;
   uint8_t* mine = peers.base[rank] + slot_off;
   uint8_t* o = static_cast<uint8_t*>(out);
   stage_k<<<grid_for(shard_bytes), 256, 0, st>>>(mine, o + (long long)rank * shard_bytes, shard_bytes);
-  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, kCommAgFlags, epoch, err);
+  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, kCommAgFlags, epoch, wait_ns, err);
   dim3 g(static_cast<unsigned>(grid_for(shard_bytes)), static_cast<unsigned>(world));
   gather_k<<<g, 256, 0, st>>>(peers, rank, world, slot_off, o, shard_bytes);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
@@ -152,13 +160,13 @@ int comm_all_gather(const CommPeers& peers, int rank, int world, uint32_t epoch,
 
 int comm_reduce_scatter(const CommPeers& peers, int rank, int world, uint32_t epoch, const void* in, void* out,
                         long long shard_elems, int elem_bytes, float scale, long long ag_cap, long long slot_cap,
-                        int* err, cudaStream_t st) {
+                        unsigned long long wait_ns, int* err, cudaStream_t st) {
   const long long in_bytes = shard_elems * world * elem_bytes;
   if (world < 2 || world > kMaxCommPeers || in_bytes > slot_cap || (elem_bytes != 4 && elem_bytes != 2)) return 5;
   const long long slot_off = kCommHeaderBytes + 2 * ag_cap + (long long)(epoch & 1u) * slot_cap;
   stage_k<<<grid_for(in_bytes), 256, 0, st>>>(peers.base[rank] + slot_off, static_cast<const uint8_t*>(in),
                                               in_bytes);
-  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, kCommRsFlags, epoch, err);
+  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, kCommRsFlags, epoch, wait_ns, err);
   const int g = grid_for(shard_elems * elem_bytes);
   if (elem_bytes == 4)
     reduce_k<float><<<g, 256, 0, st>>>(peers, rank, world, slot_off, static_cast<float*>(out), shard_elems, scale);
@@ -168,9 +176,10 @@ int comm_reduce_scatter(const CommPeers& peers, int rank, int world, uint32_t ep
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
-int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, uint32_t epoch, int* err, cudaStream_t st) {
+int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, uint32_t epoch, unsigned long long wait_ns,
+                 int* err, cudaStream_t st) {
   if (world < 2 || world > kMaxCommPeers || flag_off < 0 || flag_off + 4 * kMaxCommPeers > kCommHeaderBytes) return 5;
-  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, flag_off, epoch, err);
+  barrier_k<<<1, 32, 0, st>>>(peers, rank, world, flag_off, epoch, wait_ns, err);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

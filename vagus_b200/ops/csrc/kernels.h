@@ -28,8 +28,9 @@ int swiglu_fwd(const void* u, void* s, long long rows, int F, cudaStream_t st);
 int swiglu_bwd(const void* ds, const void* u, void* du, long long rows, int F, cudaStream_t st);
 int sigmoid_gate_fwd(const void* x, const void* g, void* y, long long n, cudaStream_t st);
 int sigmoid_gate_bwd(const void* dy, const void* x, const void* g, void* dx, void* dg, long long n, cudaStream_t st);
+// targets >= V are ignored like negative ones; status (optional) then records kErrBadTarget
 int softmax_ce(void* logits, const long long* targets, float* loss, float* lse, long long rows, int V, float scale,
-               float z_coef, cudaStream_t st);
+               float z_coef, cudaStream_t st, int* status = nullptr);
 int embedding_fwd(const float* W, const long long* tok, void* y, int y_f32, long long n, int D, cudaStream_t st);
 int embedding_bwd(const void* dy, int dy_f32, const long long* tok, float* dW, long long n, int D, cudaStream_t st);
 int adamw_step(float* p, const float* g, float* m, float* v, void* shadow, long long n, float lr, float b1, float b2,
@@ -155,15 +156,17 @@ constexpr long long kCommHeaderBytes = 1024;
 struct CommPeers {
   unsigned char* base[kMaxCommPeers];           // every rank's heap, mapped into this process
 };
+// wait_ns bounds every cross-GPU flag wait (the process group's timeout).
 int comm_all_gather(const CommPeers& peers, int rank, int world, unsigned epoch, void* out, long long shard_bytes,
-                    long long slot_cap, int* err, cudaStream_t st);
+                    long long slot_cap, unsigned long long wait_ns, int* err, cudaStream_t st);
 int comm_reduce_scatter(const CommPeers& peers, int rank, int world, unsigned epoch, const void* in, void* out,
                         long long shard_elems, int elem_bytes, float scale, long long ag_cap, long long slot_cap,
-                        int* err, cudaStream_t st);
+                        unsigned long long wait_ns, int* err, cudaStream_t st);
 // Cross-GPU epoch barrier on the flag words at byte offset flag_off of every
 // heap (kMaxCommPeers u32 per heap): publishes this stream's earlier writes
 // (system-scope release), then waits (bounded) until every peer reached epoch.
 constexpr int kCommBarFlags = 512;
-int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, unsigned epoch, int* err, cudaStream_t st);
+int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, unsigned epoch, unsigned long long wait_ns,
+                 int* err, cudaStream_t st);
 
 }  // namespace vagus

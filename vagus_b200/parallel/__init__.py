@@ -46,6 +46,8 @@ def setup_distributed(device: str = "auto", timeout_s: float | None = None):
         kw = {}
         if timeout_s is not None:
             kw["timeout"] = datetime.timedelta(seconds=timeout_s)
+            from .nvlink import set_peer_wait_seconds
+            set_peer_wait_seconds(timeout_s)        # our kernels' cross-GPU waits end with the group's
         if torch.cuda.is_available():
             dev = torch.device(f"cuda:{local}")
             torch.cuda.set_device(dev)

@@ -47,6 +47,44 @@ from ..ops import native
 
 HEADER = 1024                      # flag words, as comm.cu lays them out
 
+# Bound of every cross-GPU flag wait in the kernels, in seconds.  Ranks drift
+# apart by seconds in normal operation (rank 0 writing a checkpoint, a slow
+# data read, garbage collection), so the bound is the process group's
+# timeout, not the 2 s bound of the waits inside one CTA.
+_PEER_WAIT_S = 300.0
+
+
+def set_peer_wait_seconds(seconds: float) -> None:
+    """Bound of the cross-GPU waits of the NVLink collectives (the process
+    group's timeout); on expiry the device error word is set and
+    ``ops.check_error()`` raises."""
+    global _PEER_WAIT_S
+    _PEER_WAIT_S = float(seconds)
+    from ..ops import _core
+    if _core._C is not None:
+        _core._C.comm_set_wait_budget(_PEER_WAIT_S)
+
+
+def open_heaps(group, nbytes: int) -> tuple[int, list[int]]:
+    """Allocate this rank's zeroed device heap of ``nbytes``, share it with
+    the group over CUDA IPC and map every peer's: (own pointer, every rank's
+    base in this process).  Collective over ``group``."""
+    C = native()
+    C.comm_set_wait_budget(_PEER_WAIT_S)
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    ptr, handle = C.comm_heap_create(int(nbytes))
+    handles = [None] * world
+    dist.all_gather_object(handles, handle, group=group)
+    bases = [ptr if r == rank else C.comm_heap_open(h) for r, h in enumerate(handles)]
+    dist.barrier(group=group)
+    return ptr, bases
+
+
+def close_heaps(own: int, bases: list[int]) -> None:
+    C = native()
+    for b in bases:
+        C.comm_heap_close(b, b == own)
+
 
 _SAME_HOST: dict = {}
 
@@ -69,25 +107,17 @@ class NvlinkHeap:
     ``ag_cap`` bytes and 2 reduce-scatter slots of ``rs_cap`` bytes."""
 
     def __init__(self, group, ag_cap: int, rs_cap: int):
-        C = native()
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.ag_cap = (int(ag_cap) + 255) // 256 * 256
         self.rs_cap = (int(rs_cap) + 255) // 256 * 256
-        ptr, handle = C.comm_heap_create(HEADER + 2 * self.ag_cap + 2 * self.rs_cap)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle, group=group)
-        self.own = ptr
-        self.bases = [ptr if r == self.rank else C.comm_heap_open(h) for r, h in enumerate(handles)]
+        self.own, self.bases = open_heaps(group, HEADER + 2 * self.ag_cap + 2 * self.rs_cap)
         self.ag_epoch = 0
         self.rs_epoch = 0
-        dist.barrier(group=group)
 
     def close(self):
-        C = native()
-        for r, b in enumerate(self.bases):
-            C.comm_heap_close(b, r == self.rank)
+        close_heaps(self.own, self.bases)
         self.bases = []
 
 
@@ -239,18 +269,12 @@ class MuonExchange:
     reaches only after applying what it read from the slot."""
 
     def __init__(self, group, slot_bytes: int):
-        C = native()
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
         self.slot_bytes = (int(slot_bytes) + 255) // 256 * 256
-        ptr, handle = C.comm_heap_create(HEADER + 2 * self.slot_bytes)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle, group=group)
-        self.own = ptr
-        self.bases = [ptr if r == self.rank else C.comm_heap_open(h) for r, h in enumerate(handles)]
+        self.own, self.bases = open_heaps(group, HEADER + 2 * self.slot_bytes)
         self.epoch = 0
-        dist.barrier(group=group)
 
     @staticmethod
     def eligible(shape, world: int, device) -> bool:
@@ -294,9 +318,7 @@ class MuonExchange:
         return t.view(n, cols, rows_l).transpose(1, 2) if transposed else t.view(n, rows_l, cols)
 
     def close(self):
-        C = native()
-        for r, b in enumerate(self.bases):
-            C.comm_heap_close(b, r == self.rank)
+        close_heaps(self.own, self.bases)
         self.bases = []
 
 
@@ -314,7 +336,6 @@ class PeerRowShards:
 
     def __init__(self, group, rows: int, cols: int):
         assert rows % 8 == 0 and rows >= 128 and cols % 8 == 0 and cols >= 64, "shard shape"
-        C = native()
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -322,13 +343,8 @@ class PeerRowShards:
         if not same_host(group):
             raise RuntimeError("PeerRowShards: CUDA IPC reaches the GPUs of one machine only")
         self.rows, self.cols = rows, cols
-        ptr, handle = C.comm_heap_create(HEADER + (rows * cols * 2 + 255) // 256 * 256)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle, group=group)
-        self.own = ptr
-        self.bases = [ptr if r == self.rank else C.comm_heap_open(h) for r, h in enumerate(handles)]
+        self.own, self.bases = open_heaps(group, HEADER + (rows * cols * 2 + 255) // 256 * 256)
         self.epoch = 0
-        dist.barrier(group=group)
 
     def local(self) -> torch.Tensor:
         """This rank's shard, (rows, cols) bf16, writable in place."""
@@ -351,7 +367,5 @@ class PeerRowShards:
         return out.view(*x.shape[:-1], n)
 
     def close(self) -> None:
-        C = native()
-        for r, b in enumerate(self.bases):
-            C.comm_heap_close(b, r == self.rank)
+        close_heaps(self.own, self.bases)
         self.bases = []

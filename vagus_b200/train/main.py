@@ -154,9 +154,19 @@ def load_state(model, optimizer, state: dict, is_fsdp: bool) -> None:
 
 def save_checkpoint(run_dir: Path, kind: str, step: int, tokens_seen: int, model, optimizer, loader,
                     config: TrainConfig, is_fsdp: bool = False, is_main: bool = True):
+    """Write a checkpoint from rank 0.  Every rank of a distributed job leaves
+    only when the file is on disk: the others wait at a host barrier, so the
+    next step's collectives never start while rank 0 is still writing (a
+    multi-second skew the cross-GPU waits would otherwise have to absorb)."""
     msd, osd, fmt = gather_state(model, optimizer, is_fsdp)
-    if not is_main:
-        return None
+    path = _write_checkpoint(run_dir, kind, step, tokens_seen, msd, osd, fmt, loader, config) if is_main else None
+    if dist.is_available() and dist.is_initialized() and dist.get_world_size() > 1:
+        dist.barrier()
+    return path
+
+
+def _write_checkpoint(run_dir: Path, kind: str, step: int, tokens_seen: int, msd, osd, fmt: str, loader,
+                      config: TrainConfig) -> Path:
     state = {
         "step": step, "tokens_seen": tokens_seen, "model_name": config.model_name,
         "model_args": config.model_args,
