@@ -8,7 +8,9 @@ optimizer step (Muon + AdamW), synthetic uniform-random tokens, random init.
 For N > 1 launch one rank per GPU with torch.distributed.run (RANK /
 LOCAL_RANK / WORLD_SIZE / MASTER_* come from the environment).  The global
 batch stays 0.5M tokens at every N (strong scaling): each rank runs
-128 / (N * micro) micro-batches of ``micro`` sequences per step.
+128 / (N * micro) micro-batches of ``micro`` sequences per step.  The GDN and
+hybrid configs train under FSDP2, Transformer++ under DDP (BASELINE config
+#2); ``--parallelism`` overrides.
 
 Measurement:
 * ``value``: W untimed warm-up steps, then K steps bracketed by a barrier and
@@ -24,7 +26,8 @@ Measurement:
 
 ``--impl reference`` runs the reference (installed under baseline/_ref)
 through its own public API and stock path: its model registry, fused CE,
-Muon+AdamW factory, regional torch.compile, bf16 autocast, FSDP2 for N > 1.
+Muon+AdamW factory, regional torch.compile, bf16 autocast, FSDP2 or DDP for
+N > 1 as the config says.
 """
 
 from __future__ import annotations
@@ -37,6 +40,7 @@ import subprocess
 import sys
 import tempfile
 import time
+from contextlib import nullcontext
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -70,7 +74,7 @@ CONFIGS = {
         model_name="TransformerPP",
         model_args=dict(vocab_size=32000, dim=1024, head_dim=64, context_len=4096, layer_count=24,
                         ffn_hidden_dim=2816),
-        seq=4096, global_tokens=524288, micro=4, label="340M Transformer++", optimizer="adamw"),
+        seq=4096, global_tokens=524288, micro=4, label="340M Transformer++", optimizer="adamw", parallelism="ddp"),
     # small shape for plumbing checks (not a headline number)
     "tiny": dict(
         model_name="GDNLM",
@@ -201,14 +205,22 @@ def run(args) -> dict:
     rank, world, local = _dist_env()
     cfg = CONFIGS[args.config]
     is_dist = world > 1
+    par = args.parallelism if args.parallelism != "auto" else cfg.get("parallelism", "fsdp")
+    is_fsdp = is_dist and par == "fsdp"
     if is_dist:
         import datetime
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device(f"cuda:{local}"),
                                 timeout=datetime.timedelta(seconds=600))
+        if args.impl != "reference":
+            sys.path.insert(0, str(ROOT))
+            from vagus_b200.parallel.nvlink import set_peer_wait_seconds
+            set_peer_wait_seconds(600)      # the kernels' cross-GPU waits end with the group's timeout
     dev = torch.device(f"cuda:{local}")
     torch.manual_seed(0)
     seq, micro = cfg["seq"], (args.micro or cfg["micro"])
+    if args.global_tokens:
+        cfg = dict(cfg, global_tokens=args.global_tokens)
     per_rank_seqs = cfg["global_tokens"] // seq // world
     micro = min(micro, per_rank_seqs)
     accum = per_rank_seqs // micro
@@ -228,12 +240,15 @@ def run(args) -> dict:
             model.compile_blocks()
         ce = make_ce("liger", z_loss=1e-4, compute_dtype=torch.bfloat16)
         mesh = None
-        if is_dist:
+        if is_fsdp:
             mesh = ref_main.build_mesh(ref_main.TrainConfig(run_name="b", data_dir="", shard_size=world,
                                                             world_size=world), dev, world)
             model = ref_main.LMLoss(model, ce)
             ref_main.apply_fsdp(model, mesh, ref_main.TrainConfig(run_name="b", data_dir="", shard_size=world,
                                                                   world_size=world))
+        elif is_dist:
+            from torch.nn.parallel import DistributedDataParallel as DDP
+            model = DDP(model, device_ids=[dev.index], output_device=dev.index)
         optimizer = build_optimizer(opt_name, ref_main.unwrap(model), json.loads(json.dumps(opt_args)))
         head = ref_main.unwrap(model).head.weight
         autocast = torch.autocast("cuda", dtype=torch.bfloat16)
@@ -241,18 +256,19 @@ def run(args) -> dict:
         def step(batches):
             optimizer.zero_grad(set_to_none=True)
             acc = torch.zeros((), device=dev)
-            for _ in range(accum):
+            for micro_i in range(accum):
                 x, y = next(batches)
                 x = x.to(dev, non_blocking=True)
                 y = y.to(dev, non_blocking=True)
-                with autocast:
-                    if is_dist:
+                sync = model.no_sync() if is_dist and not is_fsdp and micro_i < accum - 1 else nullcontext()
+                with sync, autocast:
+                    if is_fsdp:
                         loss = model(x, y)
                     else:
                         loss = ce(model(x, return_hidden=True), head, y)
                     (loss / accum).backward()
                 acc += loss.detach()
-            if is_dist:
+            if is_fsdp:
                 ref_main.reduce_replicated(model, mesh)
             ref_main.clip_grad_norm(model, 1.0)
             optimizer.step()
@@ -269,12 +285,15 @@ def run(args) -> dict:
         model = build_model(cfg["model_name"], cfg["model_args"]).to(dev)
         ce = make_ce("fused", z_loss=1e-4)
         mesh = None
-        if is_dist:
+        if is_fsdp:
             mesh = build_mesh(world, dev, world)
             model = LMLoss(model, ce)
             apply_fsdp(model, mesh, comm=args.comm)
+        elif is_dist:
+            from torch.nn.parallel import DistributedDataParallel as DDP
+            model = DDP(model, device_ids=[dev.index], output_device=dev.index)
         optimizer = build_optimizer(opt_name, unwrap(model), json.loads(json.dumps(opt_args)))
-        runner = StepRunner(model, optimizer, ce, dev, grad_accum_steps=accum, grad_clip=1.0, is_fsdp=is_dist,
+        runner = StepRunner(model, optimizer, ce, dev, grad_accum_steps=accum, grad_clip=1.0, is_fsdp=is_fsdp,
                             is_dist=is_dist, mesh=mesh)
 
         def step(batches):
@@ -352,7 +371,7 @@ def run(args) -> dict:
     # with the FSDP2 all-gathers / reduce-scatters switched off; the
     # difference to the timed step is the communication the compute did not hide
     exposed = None
-    if args.exposed_comm and is_dist and args.impl != "reference" and args.comm == "nvlink":
+    if args.exposed_comm and is_fsdp and args.impl != "reference" and args.comm == "nvlink":
         from vagus_b200.parallel import nvlink as nvl
         nvl.set_dry_run(True)
         for _ in range(2):
@@ -384,8 +403,9 @@ def run(args) -> dict:
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic uniform-random tokens, random init",
         "config": {"model": cfg["label"], "global_batch": cfg["global_tokens"], "seq_len": seq,
                    "micro_batch": micro, "grad_accum": accum,
-                   "parallelism": f"fsdp{world}" if world > 1 else "single",
-                   "collectives": ("nccl" if args.impl == "reference" else args.comm) if world > 1 else None,
+                   "parallelism": f"{par}{world}" if world > 1 else "single",
+                   "collectives": ("nccl" if args.impl == "reference" or not is_fsdp else args.comm)
+                   if world > 1 else None,
                    "optimizer": opt_name, "l2": "no flush: every step's working set is >> 126 MB L2"},
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 4},
@@ -414,6 +434,10 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="gdn340m")
     ap.add_argument("--micro", type=int, default=0, help="sequences per micro-batch (0: the config's default)")
+    ap.add_argument("--global-tokens", type=int, default=0,
+                    help="tokens per optimizer step (0: the config's; a diagnostic, not the headline batch)")
+    ap.add_argument("--parallelism", choices=["auto", "ddp", "fsdp"], default="auto",
+                    help="N > 1: DDP or FSDP2 (auto: the config's, DDP for tpp340m as BASELINE config #2)")
     ap.add_argument("--exposed-comm", action="store_true",
                     help="N > 1: also time the steps with the FSDP2 collectives off and report the exposed share")
     args = ap.parse_args()
