@@ -25,6 +25,7 @@ enum ErrCode : int {
   kErrTimeoutEpilogue = 3,   // epilogue waited too long for the accumulator
   kErrTimeoutPeer = 4,       // a cross-GPU flag never arrived
   kErrBadArgument = 5,
+  kErrBadTarget = 16,        // a cross-entropy target id >= the vocabulary size
 };
 
 // Wall-clock budget for one wait.  Generous: a healthy wait is microseconds.

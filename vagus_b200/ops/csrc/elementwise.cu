@@ -114,14 +114,17 @@ __global__ void sgate_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfl
 // One CTA per row of bf16 logits (rows, V).  Writes per-row lse and loss
 // (lse - logit[target]) and overwrites the logits with
 //     d = scale * (softmax - onehot) + scale * 2 z_coef lse * softmax.
-// Rows whose target is < 0 are ignored (loss 0, gradient 0).
+// Rows whose target is < 0 are ignored (loss 0, gradient 0).  A target >= V
+// is out of range: the row is ignored the same way (the logits row is never
+// read past its end) and, when `status` is given, kErrBadTarget is recorded
+// there.
 
 constexpr int CE_THREADS = 512;
 
 __global__ void __launch_bounds__(CE_THREADS) softmax_ce_k(__nv_bfloat16* __restrict__ logits,
                                                            const long long* __restrict__ targets,
                                                            float* __restrict__ loss, float* __restrict__ lse_out,
-                                                           int V, float scale, float z_coef) {
+                                                           int V, float scale, float z_coef, int* status) {
   __shared__ float red_m[CE_THREADS / 32], red_s[CE_THREADS / 32];
   __shared__ float bc[2];
   const long long r = blockIdx.x;
@@ -163,7 +166,8 @@ __global__ void __launch_bounds__(CE_THREADS) softmax_ce_k(__nv_bfloat16* __rest
   __syncthreads();
   const float lse = bc[1];
   const long long tgt = targets[r];
-  const bool valid = tgt >= 0;
+  const bool valid = tgt >= 0 && tgt < V;
+  if (tgt >= V && threadIdx.x == 0) record_error(status, kErrBadTarget);
   if (threadIdx.x == 0) {
     lse_out[r] = lse;
     loss[r] = valid ? lse - bf2f(row[tgt]) : 0.f;
@@ -288,10 +292,10 @@ int sigmoid_gate_bwd(const void* dy, const void* x, const void* g, void* dx, voi
 }
 
 int softmax_ce(void* logits, const long long* targets, float* loss, float* lse, long long rows, int V, float scale,
-               float z_coef, cudaStream_t st) {
+               float z_coef, cudaStream_t st, int* status) {
   if (rows <= 0) return 0;
   softmax_ce_k<<<static_cast<unsigned>(rows), CE_THREADS, 0, st>>>((__nv_bfloat16*)logits, targets, loss, lse, V,
-                                                                   scale, z_coef);
+                                                                   scale, z_coef, status);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
