@@ -134,3 +134,29 @@ def test_profile_step_on_cpu(tmp_path):
     assert any(p.endswith(".trace.json") for p in r["traces"].values())
     assert profile_step.family("gemm_kernel<256, false, false>") == "gemm"
     assert profile_step.family("gdr_bwd_scan_tc<256>") == "delta-rule"
+
+
+def test_compare_agreement_is_leafwise():
+    from vagus_b200.meter.compare import agreement, compare
+    a = (torch.ones(3), {"s": torch.zeros(2)})
+    b = (torch.ones(3) * 1.5, {"s": torch.zeros(2)})
+    ag = agreement(b, a)
+    assert ag.leaves == 2 and abs(ag.max_abs - 0.5) < 1e-12 and abs(ag.max_rel - 0.5) < 1e-12
+    assert agreement((torch.ones(3),), a).max_abs == float("inf")          # structure differs
+    assert agreement(torch.ones(2), torch.ones(3)).max_rel == float("inf")  # shape differs
+    x = torch.randn(64, 64)
+    res = compare({"mm": lambda t: t @ t, "mm2": lambda t: (t @ t) * (1 + 1e-3)}, (x,), warmup=1, iters=3,
+                  verbose=False)
+    assert res["mm"].vs_ref is None and 5e-4 < res["mm2"].vs_ref.max_rel < 2e-3
+    assert len(res["mm"].samples) == 3
+
+
+def test_dist_job_time_is_the_slowest_rank_per_iteration():
+    from vagus_b200.meter.core import BenchResult
+    from vagus_b200.meter.dist import job_time, render_dist_table
+
+    def r(s):
+        return BenchResult("f", "cpu", len(s), sum(s) / len(s), 0.0, min(s), max(s), 0.0, None, False, samples=s)
+    res = {0: r([1.0, 5.0, 1.0]), 1: r([4.0, 1.0, 1.0])}
+    assert job_time(res) == (4.0 + 5.0 + 1.0) / 3
+    assert "job step" in render_dist_table(res)

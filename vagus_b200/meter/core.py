@@ -38,6 +38,7 @@ class BenchResult:
     peak_mem: Optional[int]
     mem_exact: bool
     error: Optional[str] = None
+    samples: Optional[list] = None       # per-iteration ms, in order
 
     @property
     def failed(self) -> bool:
@@ -113,4 +114,30 @@ def bench(fn: Callable, args: tuple = (), kwargs: Optional[dict] = None, *, name
         return BenchResult(label, str(device), 0, 0, 0, 0, 0, 0, None, False, error=f"{type(e).__name__}: {e}")
     mean = sum(times) / len(times)
     std = (sum((t - mean) ** 2 for t in times) / len(times)) ** 0.5
-    return BenchResult(label, str(device), len(times), mean, std, min(times), max(times), first, peak, exact)
+    return BenchResult(label, str(device), len(times), mean, std, min(times), max(times), first, peak, exact,
+                       samples=list(times))
+
+
+def format_table(header: list[str], rows: list[list[str]]) -> str:
+    """Left-aligned text table with a rule under the header."""
+    cells = [list(map(str, header))] + [[str(c) for c in r] for r in rows]
+    widths = [max(len(r[i]) if i < len(r) else 0 for r in cells) for i in range(len(header))]
+    out = []
+    for n, r in enumerate(cells):
+        out.append("  ".join(c.ljust(w) for c, w in zip(r, widths)).rstrip())
+        if n == 0:
+            out.append("  ".join("-" * w for w in widths))
+    return "\n".join(out)
+
+
+def fmt_bytes(nbytes: Optional[int], exact: bool = True) -> str:
+    """Human-readable size; ``~`` marks an approximate (RSS-based) figure."""
+    if nbytes is None:
+        return "n/a"
+    units = ["B", "KiB", "MiB", "GiB", "TiB"]
+    k = 0
+    v = float(nbytes)
+    while v >= 1024 and k < len(units) - 1:
+        v /= 1024
+        k += 1
+    return f"{v:.1f} {units[k]}" + ("" if exact else " ~")

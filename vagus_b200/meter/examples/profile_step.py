@@ -14,29 +14,10 @@ from __future__ import annotations
 
 import argparse
 import json
-import re
 
 import torch
 
-# kernel-name families, first match wins
-FAMILIES = [
-    ("gemm", r"gemm|gemv|cutlass|sm100_xmma|nvjet"),
-    ("attention", r"attn|flash|fmha|sdpa"),
-    ("delta-rule", r"gdr|kda|intra|scan|mobius"),
-    ("conv", r"conv"),
-    ("cross-entropy", r"softmax_ce|cross_entropy|\bce_"),
-    ("optimizer", r"adamw|muon|newton|foreach|lerp"),
-    ("collectives", r"nccl|gather_k|reduce_scatter|barrier_k|comm_"),
-    ("norms / pointwise", r"norm|swiglu|silu|rope|gate|elementwise|vectorized|copy|fill|cast|mul|add"),
-]
-
-
-def family(name: str) -> str:
-    low = name.lower()
-    for fam, pat in FAMILIES:
-        if re.search(pat, low):
-            return fam
-    return "other"
+from ..profiling import family  # noqa: F401  (re-exported: kernel-name families)
 
 
 def build(a):
@@ -65,7 +46,7 @@ def main(argv=None):
     from ...models.losses import make_ce
     from ...optim import build_optimizer
     from ...train.main import StepRunner
-    from ..profiling import profile_variants
+    from ..profiling import device_split, profile_variants, render_split
     dev = torch.device("cuda" if torch.cuda.is_available() else "cpu")
     name, margs, model = build(a)
     model = model.to(dev)
@@ -92,17 +73,10 @@ def main(argv=None):
         for _ in range(a.steps):
             step()
         torch.cuda.synchronize()
-    fams: dict[str, float] = {}
-    for ev in prof.key_averages():
-        us = getattr(ev, "self_device_time_total", 0.0) or getattr(ev, "self_cuda_time_total", 0.0)
-        if us > 0:
-            f = family(ev.key)
-            fams[f] = fams.get(f, 0.0) + us / 1e3 / a.steps
-    total = sum(fams.values())
-    print(f"\ndevice time per step by kernel family ({total:.1f} ms):")
-    for f, ms in sorted(fams.items(), key=lambda kv: -kv[1]):
-        print(f"  {f:<18} {ms:9.2f} ms  {100 * ms / total:5.1f} %")
-    return {"traces": {k: str(v) for k, v in traces.items()}, "families_ms": fams}
+    split = device_split(prof, a.steps)
+    print(f"\ndevice time per step by kernel family ({sum(split['families_ms'].values()):.1f} ms):")
+    print(render_split(split))
+    return {"traces": {k: str(v) for k, v in traces.items()}, **split}
 
 
 if __name__ == "__main__":
