@@ -48,7 +48,7 @@ def build_record(run_dir, incidents=(), note: str | None = None) -> dict:
                 "torch": meta.get("torch")},
         "recipe": meta.get("config"),
         "data": meta.get("data"),
-        "results": {"final_step": last.get("step"), "tokens_seen": last.get("tokens_seen"),
+        "results": {"final_step": last.get("step"), "tokens_seen": last.get("tokens", last.get("tokens_seen")),
                     "loss_tail5": statistics.fmean(losses[-5:]) if losses else None,
                     "tokens_per_s_median": statistics.median(tput) if tput else None,
                     "mfu_median": statistics.median(mfu) if mfu else None,
