@@ -11,7 +11,7 @@ shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
 gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
-sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, rmsnorm.  With no
+sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm.  With no
 case names every
 case runs.
 
@@ -135,6 +135,11 @@ def _cases(B: int, L: int):
     cases["gemm_gather_fwd"] = (lambda: C.gemm_gather(a, False, ptrs, rows_o, D, c), None, fl)
     cases["gemm_dgrad"] = (lambda: gemm(gp, False, wpk, True, da), None, fl)         # dy W
     cases["gemm_wgrad"] = (lambda: gemm(gp, True, a, True, dwp, atomic=True), None, fl)  # dW += dy^T x
+    # cuBLAS (torch.matmul) on the same three products, for the comparison on
+    # the same shape; the wgrad one writes a fresh fp32 product (no accumulate)
+    cases["cublas_fwd"] = (lambda: torch.matmul(a, wpk.t()), None, fl)
+    cases["cublas_dgrad"] = (lambda: torch.matmul(gp, wpk), None, fl)
+    cases["cublas_wgrad"] = (lambda: torch.matmul(gp.t(), a), None, fl)
 
     # causal attention at the Transformer++ 340M shape (16 heads of 64) and
     # the hybrid 1.3B softmax layers (16 heads of 128)

@@ -20,7 +20,12 @@ from pathlib import Path
 NAME = "vagus_b200_C"
 HERE = Path(__file__).resolve().parent
 CSRC = HERE / "csrc"
-BUILD_DIR = HERE / "_build"
+# VAGUS_BOUNDS_CHECK=1 selects the bounds-checked build (-DVAGUS_BOUNDS_CHECK:
+# hand-computed global indices are checked against their tensors, a miss is
+# recorded in the device error word and the access skipped), kept in its own
+# directory beside the normal one.
+BOUNDS_CHECK = os.environ.get("VAGUS_BOUNDS_CHECK", "") not in ("", "0")
+BUILD_DIR = HERE / ("_build_bounds" if BOUNDS_CHECK else "_build")
 
 SOURCES = [
     "bindings.cpp", "bind_seq.cpp", "bind_attn.cpp", "bind_comm.cpp",
@@ -31,6 +36,8 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
                      "-diag-suppress=177,550"]
 CXX_FLAGS = ["-O3", "-std=c++17"]
+if BOUNDS_CHECK:
+    CUDA_FLAGS = CUDA_FLAGS + ["-DVAGUS_BOUNDS_CHECK=1"]
 
 
 def _sources() -> list[Path]:

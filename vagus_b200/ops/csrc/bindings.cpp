@@ -1,6 +1,7 @@
 // Python bindings of the sm_100a kernels.  Tensor checks live here; the .cu
 // files see raw pointers only.  Every op runs on the current CUDA stream.
 #include <torch/extension.h>
+#include <vector>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
@@ -31,6 +32,20 @@ int* g_err_dev[64] = {nullptr};
 
 }  // namespace
 
+// Bounds-checked build: every CUDA translation unit registers a function
+// that points its copy of the device-side error-word pointer at a device's
+// error word; they run when that word is created (one context per device).
+namespace {
+std::vector<int (*)(int*)>& bounds_installers() {
+  static std::vector<int (*)(int*)> v;
+  return v;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) void vagus_register_bounds_installer(int (*fn)(int*)) {
+  bounds_installers().push_back(fn);
+}
+
 // Device pointer of this device's error word (shared with the other binding units).
 int* vagus_device_error_ptr() {
   int dev = 0;
@@ -43,6 +58,7 @@ int* vagus_device_error_ptr() {
     TORCH_CHECK(cudaHostGetDevicePointer(&d, h, 0) == cudaSuccess, "cudaHostGetDevicePointer failed");
     g_err_host[dev] = h;
     g_err_dev[dev] = d;
+    for (auto fn : bounds_installers()) TORCH_CHECK(fn(d) == 0, "installing the bounds-check word failed");
   }
   return g_err_dev[dev];
 }
@@ -328,7 +344,7 @@ Tensor embedding_fwd(Tensor W, Tensor tok, bool out_f32) {
   sizes.push_back(D);
   auto y = torch::empty(sizes, W.options().dtype(out_f32 ? at::kFloat : at::kBFloat16));
   check(vagus::embedding_fwd(W.data_ptr<float>(), reinterpret_cast<const long long*>(tok.data_ptr<int64_t>()), y.data_ptr(), out_f32, tok.numel(), D,
-                             stream()), "embedding_fwd");
+                             W.size(0), stream()), "embedding_fwd");
   return y;
 }
 
@@ -337,7 +353,7 @@ void embedding_bwd(Tensor dy, Tensor tok, Tensor dW) {
   tok = tok.contiguous();
   TORCH_CHECK(is_f32(dW) && dW.is_contiguous(), "embedding_bwd: fp32 dW");
   check(vagus::embedding_bwd(dy.data_ptr(), is_f32(dy), reinterpret_cast<const long long*>(tok.data_ptr<int64_t>()), dW.data_ptr<float>(), tok.numel(),
-                             static_cast<int>(dW.size(1)), stream()), "embedding_bwd");
+                             static_cast<int>(dW.size(1)), dW.size(0), stream()), "embedding_bwd");
 }
 
 void adamw_step(Tensor p, Tensor g, Tensor m, Tensor v, c10::optional<Tensor> shadow, double lr, double b1, double b2,
@@ -370,6 +386,8 @@ void register_comm_ops(pybind11::module& m);  // bind_comm.cpp: NVLink peer-to-p
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "vagus_b200 sm_100a kernels";
   m.def("error_word", &error_word, "device error word (bounded-wait timeouts); 0 = none");
+  m.def("bounds_checked", []() { return !bounds_installers().empty(); },
+        "True in the bounds-checked build (VAGUS_BOUNDS_CHECK=1)");
   m.def("reset_error", &reset_error);
   m.def("gemm_gather", &gemm_gather);
   m.def("gemm_scatter", &gemm_scatter);

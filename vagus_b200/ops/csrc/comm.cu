@@ -92,7 +92,7 @@ __global__ void gather_k(const CommPeers peers, int rank, int world, long long s
                          long long n) {
   // blockIdx.y = source rank
   const int src = blockIdx.y;
-  if (src == rank) return;         // already in place
+  if (src == rank || !VAGUS_CHECK(src, world)) return;         // own shard already in place
   copy_bytes(out + (long long)src * n, peers.base[src] + slot_off, n, (long long)blockIdx.x * blockDim.x + threadIdx.x,
              (long long)gridDim.x * blockDim.x);
 }

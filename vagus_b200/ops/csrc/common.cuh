@@ -26,7 +26,28 @@ enum ErrCode : int {
   kErrTimeoutPeer = 4,       // a cross-GPU flag never arrived
   kErrBadArgument = 5,
   kErrBadTarget = 16,        // a cross-entropy target id >= the vocabulary size
+  kErrBounds = 32,           // bounds-checked build: an index fell outside its tensor
 };
+
+// ------------------------------------------------------- bounds checks --
+// VAGUS_CHECK(i, n) guards a hand-computed global index: in the
+// bounds-checked build (-DVAGUS_BOUNDS_CHECK, built by ops/build.py when
+// VAGUS_BOUNDS_CHECK=1) an index outside [0, n) records kErrBounds in the
+// device error word and the guarded access is skipped; in the normal build it
+// is `true` and costs nothing.  Each translation unit holds its own copy of
+// the error-word pointer; the host installs it in every unit when it creates
+// a device's error word (vagus_install_bounds_word in bindings.cpp).
+#if defined(VAGUS_BOUNDS_CHECK)
+static __device__ int* g_bounds_word = nullptr;
+__device__ __forceinline__ bool in_bounds(long long i, long long n) {
+  if (i >= 0 && i < n) return true;
+  if (g_bounds_word != nullptr) atomicCAS(g_bounds_word, 0, static_cast<int>(kErrBounds));
+  return false;
+}
+#define VAGUS_CHECK(i, n) (::vagus::in_bounds(static_cast<long long>(i), static_cast<long long>(n)))
+#else
+#define VAGUS_CHECK(i, n) true
+#endif
 
 // Wall-clock budget for one wait.  Generous: a healthy wait is microseconds.
 constexpr unsigned long long kWaitBudgetNs = 2000000000ull;   // 2 s
@@ -202,6 +223,12 @@ __device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, const void*
                ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(c0), "r"(c1)
                : "memory");
 }
+// Tiled 3-D bulk-tensor store from this CTA's shared memory.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.bulk_group [%0, {%2, %3, %4}], [%1];"
+               ::"l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(smem_src)), "r"(c0), "r"(c1), "r"(c2)
+               : "memory");
+}
 // Tiled 3-D bulk-tensor reduction global += shared (fp32 add, element type
 // from the tensor map), bulk-group completion like the stores.
 __device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, const void* smem_src, int c0, int c1,
@@ -293,6 +320,14 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 }
 
 __device__ __forceinline__ void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// After tmem_ld_wait: ties the loaded registers to a point after the wait, so
+// the compiler cannot move their first use above it (the load's outputs look
+// defined at the load to the compiler, but hold data only after the wait).
+__device__ __forceinline__ void tmem_regs_ready(uint32_t (&r)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) asm volatile("" : "+r"(r[i])::"memory");
+}
 
 // 32 registers -> 32 lanes x 32 consecutive columns (the inverse of the load).
 __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
@@ -409,5 +444,21 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, bool a_mn, 
   return (1u << 4) | (1u << 7) | (1u << 10) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) |
          ((static_cast<uint32_t>(N) >> 3) << 17) | ((static_cast<uint32_t>(M) >> 4) << 24);
 }
+
+
+#if defined(VAGUS_BOUNDS_CHECK) && !defined(__CUDA_ARCH__)
+// Host side of the bounds-checked build: registers, at library load, a
+// function that writes this translation unit's g_bounds_word.
+extern "C" void vagus_register_bounds_installer(int (*fn)(int*));
+namespace {
+struct BoundsWordInstaller {
+  BoundsWordInstaller() { vagus_register_bounds_installer(&install); }
+  static int install(int* word) {
+    return cudaMemcpyToSymbol(g_bounds_word, &word, sizeof(word)) == cudaSuccess ? 0 : 1;
+  }
+};
+static BoundsWordInstaller g_bounds_installer;
+}  // namespace
+#endif
 
 }  // namespace vagus

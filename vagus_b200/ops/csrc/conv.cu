@@ -168,9 +168,11 @@ conv_fwd_k(const __nv_bfloat16* __restrict__ x, long long ldx, const float* __re
         const float rn = rsqrtf(warp_sum(ss) + 1e-6f);
 #pragma unroll
         for (int j = 0; j < VEC; ++j) u[j] *= rn;
-        if (lane == 0) rnorm[(b * L + t) * nH + head] = rn;
+        if (lane == 0 && VAGUS_CHECK((b * L + t) * nH + head, (long long)gridDim.z * L * nH))
+          rnorm[(b * L + t) * nH + head] = rn;
       }
-      store_vec<VEC>(y + (b * L + t) * D + head * HD + lane * VEC, u);
+      if (VAGUS_CHECK((b * L + t) * D + head * HD + lane * VEC + VEC - 1, (long long)gridDim.z * L * D))
+        store_vec<VEC>(y + (b * L + t) * D + head * HD + lane * VEC, u);
     }
   }
 }

@@ -200,10 +200,11 @@ __global__ void __launch_bounds__(CE_THREADS) softmax_ce_k(__nv_bfloat16* __rest
 
 template <typename T>
 __global__ void embedding_bwd_k(const T* __restrict__ dy, const long long* __restrict__ tok,
-                                float* __restrict__ dW, long long n, int D) {
+                                float* __restrict__ dW, long long n, int D, long long V) {
   const long long i = blockIdx.x;
   if (i >= n) return;
   const long long t = tok[i];
+  if (!VAGUS_CHECK(t, V)) return;
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
     float v;
     if constexpr (sizeof(T) == 4) v = dy[i * D + c]; else v = bf2f(dy[i * D + c]);
@@ -213,10 +214,11 @@ __global__ void embedding_bwd_k(const T* __restrict__ dy, const long long* __res
 
 template <typename T>
 __global__ void embedding_fwd_k(const float* __restrict__ W, const long long* __restrict__ tok, T* __restrict__ y,
-                                long long n, int D) {
+                                long long n, int D, long long V) {
   const long long i = blockIdx.x;
   if (i >= n) return;
   const long long t = tok[i];
+  if (!VAGUS_CHECK(t, V)) return;
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
     if constexpr (sizeof(T) == 4) y[i * D + c] = W[t * D + c]; else y[i * D + c] = f2bf(W[t * D + c]);
   }
@@ -299,17 +301,19 @@ int softmax_ce(void* logits, const long long* targets, float* loss, float* lse, 
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
-int embedding_fwd(const float* W, const long long* tok, void* y, int y_f32, long long n, int D, cudaStream_t st) {
+int embedding_fwd(const float* W, const long long* tok, void* y, int y_f32, long long n, int D, long long V,
+                  cudaStream_t st) {
   if (n <= 0) return 0;
-  if (y_f32) embedding_fwd_k<float><<<static_cast<unsigned>(n), 256, 0, st>>>(W, tok, (float*)y, n, D);
-  else embedding_fwd_k<__nv_bfloat16><<<static_cast<unsigned>(n), 256, 0, st>>>(W, tok, (__nv_bfloat16*)y, n, D);
+  if (y_f32) embedding_fwd_k<float><<<static_cast<unsigned>(n), 256, 0, st>>>(W, tok, (float*)y, n, D, V);
+  else embedding_fwd_k<__nv_bfloat16><<<static_cast<unsigned>(n), 256, 0, st>>>(W, tok, (__nv_bfloat16*)y, n, D, V);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
-int embedding_bwd(const void* dy, int dy_f32, const long long* tok, float* dW, long long n, int D, cudaStream_t st) {
+int embedding_bwd(const void* dy, int dy_f32, const long long* tok, float* dW, long long n, int D, long long V,
+                  cudaStream_t st) {
   if (n <= 0) return 0;
-  if (dy_f32) embedding_bwd_k<float><<<static_cast<unsigned>(n), 256, 0, st>>>((const float*)dy, tok, dW, n, D);
-  else embedding_bwd_k<__nv_bfloat16><<<static_cast<unsigned>(n), 256, 0, st>>>((const __nv_bfloat16*)dy, tok, dW, n, D);
+  if (dy_f32) embedding_bwd_k<float><<<static_cast<unsigned>(n), 256, 0, st>>>((const float*)dy, tok, dW, n, D, V);
+  else embedding_bwd_k<__nv_bfloat16><<<static_cast<unsigned>(n), 256, 0, st>>>((const __nv_bfloat16*)dy, tok, dW, n, D, V);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

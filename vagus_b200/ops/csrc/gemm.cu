@@ -17,7 +17,15 @@
 //               tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM
 //               accumulators and tcgen05.commit's the smem slot back;
 //   warps 2-5   epilogue: tcgen05.ld the accumulator (one TMEM lane = one
-//               output row per thread), apply alpha/beta/source, store.
+//               output row per thread; the load of the next 32 columns is
+//               in flight while the current ones are stored), apply
+//               alpha/beta/source, store.  Plain bf16 outputs go out through
+//               TMA: each warp packs its 32 rows x 32 columns into one of two
+//               2 KB shared-memory buffers (64-byte swizzle, conflict-free)
+//               and one lane issues a bulk tensor store, so a tile leaves as
+//               16 coalesced 2 KB boxes per warp instead of 32-row scattered
+//               vector stores; fp32, atomic, source-adding and scatter
+//               epilogues store from registers.
 // The two accumulators let the epilogue of tile i overlap the main loop of
 // tile i+1.  Split-K (mode ATOMIC only) spreads the K range of one tile over
 // several work units when there are fewer tiles than SMs (weight gradients).
@@ -48,8 +56,12 @@ struct Cfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int TMEM_COLS = 2 * BN;   // two accumulators
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/ + 16384 /*epilogue*/;
 };
+
+// Epilogue staging for TMA stores: per epilogue warp two 32 x 32 bf16 boxes.
+constexpr int EPI_BOX_BYTES = 32 * 32 * 2;
+constexpr int EPI_BYTES = 4 * 2 * EPI_BOX_BYTES;
 
 struct KParams {
   int M, N, K, batch;
@@ -64,6 +76,7 @@ struct KParams {
   float alpha, beta;
   int atomic;
   int vec;          // 16-byte vector access is legal for C and S
+  int tma_c;        // plain bf16 output stored through the C tensor map
   int* err;
   // stream-K (atomic outputs, CTA-pair kernel): worker w takes the global
   // k-block range [w * kb_per_worker, (w + 1) * kb_per_worker) of the
@@ -80,6 +93,7 @@ struct KParams {
 __device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row, int col0, const float* v) {
   // v: 32 consecutive values of one output row starting at col0
   if (row >= p.M) return;
+  if (!VAGUS_CHECK(b, p.batch) || !VAGUS_CHECK(col0, p.N)) return;
   const bool full = (col0 + 32 <= p.N) && p.vec;
   if (p.atomic) {
     float* c = reinterpret_cast<float*>(p.C) + (long long)b * p.strideC + (long long)row * p.ldc + col0;
@@ -161,6 +175,62 @@ __device__ __forceinline__ void store_row_chunk(const KParams& p, int b, int row
   }
 }
 
+// One 32-column chunk of one epilogue warp's 32 rows (v: this thread's row).
+// TMA mode: pack to bf16 into the warp's next staging box -- row `lane` at
+// byte lane * 64, 16-byte group q stored at q ^ ((lane >> 1) & 3), which is
+// the tensor map's 64-byte swizzle and spreads a phase's 8 rows over all
+// banks -- then one lane stores the box at (col0, warp_row0, b).  The box
+// written two chunks ago must have been read out first (bulk_wait_read<1>).
+__device__ __forceinline__ void emit_chunk(const KParams& p, const CUtensorMap* mapC, uint8_t* wbuf, int& sel, int b,
+                                           int row, int warp_row0, int col0, const uint32_t (&r)[32], int lane) {
+  const float* v = reinterpret_cast<const float*>(r);
+  if (!p.tma_c) {
+    if (col0 < p.N) store_row_chunk(p, b, row, col0, v);
+    return;
+  }
+  if (col0 >= p.N) return;                 // warp-uniform
+  uint8_t* box = wbuf + sel * EPI_BOX_BYTES;
+  if (lane == 0) bulk_wait_read<1>();
+  __syncwarp();
+  uint32_t w[16];
+#pragma unroll
+  for (int j = 0; j < 16; ++j) w[j] = pack_bf16x2(p.alpha * v[2 * j], p.alpha * v[2 * j + 1]);
+  uint4* dst = reinterpret_cast<uint4*>(box + lane * 64);
+  const int sw = (lane >> 1) & 3;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) dst[q ^ sw] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_3d(mapC, box, col0, warp_row0, b);
+    bulk_commit();
+  }
+  sel ^= 1;
+}
+
+// Drains one epilogue warp's 32 accumulator rows of a tile (NCOL columns from
+// TMEM address t_row): the tcgen05.ld of the next 32 columns is issued before
+// the current ones are converted and stored.
+template <int NCOL>
+__device__ __forceinline__ void drain_rows(const KParams& p, const CUtensorMap* mapC, uint8_t* wbuf, int& sel, int b,
+                                           int row, int warp_row0, int n0, uint32_t t_row, int lane) {
+  uint32_t ra[32], rb[32];
+  tmem_ld_32x32b_x32(t_row, ra);
+#pragma unroll
+  for (int c = 0; c < NCOL; c += 64) {
+    tmem_ld_wait();
+    tmem_regs_ready(ra);
+    if (c + 32 < NCOL) tmem_ld_32x32b_x32(t_row + c + 32, rb);
+    emit_chunk(p, mapC, wbuf, sel, b, row, warp_row0, n0 + c, ra, lane);
+    if (c + 32 < NCOL) {
+      tmem_ld_wait();
+      tmem_regs_ready(rb);
+      if (c + 64 < NCOL) tmem_ld_32x32b_x32(t_row + c + 64, ra);
+      emit_chunk(p, mapC, wbuf, sel, b, row, warp_row0, n0 + c + 32, rb, lane);
+    }
+  }
+}
+
 // Work units.  The first `full_tiles` units are whole tiles (all of K); the
 // remaining tiles (fewer than one wave) are split `rsplit` ways along K so
 // the last wave fills the machine, and their partial products meet in the
@@ -237,15 +307,16 @@ struct NoGather {};
 
 template <int BN, bool A_MN, bool B_MN, class GM = NoGather>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
-gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB, const KParams p,
-            const __grid_constant__ GM gm) {
+gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
+            const __grid_constant__ CUtensorMap mapC, const KParams p, const __grid_constant__ GM gm) {
   constexpr bool kGather = std::is_same<GM, GatherMaps>::value;
   using C = Cfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   // 1024-byte alignment for the swizzle atoms
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE_BYTES);
+  uint8_t* epi = smem + C::STAGES * C::STAGE_BYTES;          // 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi + EPI_BYTES);
   uint64_t* empty_bar = full_bar + C::STAGES;
   uint64_t* acc_full = empty_bar + C::STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -377,6 +448,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
     // ----------------------------------------------------------- epilogue
     const int quarter = warp & 3;              // TMEM lane quarter this warp may touch
     const int row_in_tile = quarter * 32 + lane;
+    uint8_t* wbuf = epi + quarter * 2 * EPI_BOX_BYTES;
+    int sel = 0;
     int local = 0;
     WorkIter it(p, blockIdx.x, gridDim.x);
     int b, tm, tn, kb0, kb1;
@@ -385,19 +458,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CU
       const uint32_t use = static_cast<uint32_t>(local >> 1);
       if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      const int row = tm * BM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_ld_wait();
-        const int col0 = tn * BN + c;
-        if (col0 < p.N) store_row_chunk(p, b, row, col0, reinterpret_cast<const float*>(r));
-      }
+      drain_rows<BN>(p, &mapC, wbuf, sel, b, tm * BM + row_in_tile, tm * BM + quarter * 32, tn * BN, t_row, lane);
       tc_fence_before();
       mbar_arrive(&acc_empty[buf]);
     }
+    if (p.tma_c && lane == 0) bulk_wait<0>();   // stores out of this warp's boxes are complete
   }
 
   tc_fence_before();
@@ -430,18 +496,19 @@ constexpr int A_BYTES = ROWS * BK * 2;
 constexpr int B_BYTES = ROWS * BK * 2;
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int TMEM_COLS = 2 * TN;         // two accumulators (all 512 columns)
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 256 + EPI_BYTES;
 }  // namespace pairk
 
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_pair_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant__ CUtensorMap mapB,
-                 const KParams p) {
+                 const __grid_constant__ CUtensorMap mapC, const KParams p) {
   using namespace pairk;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* tiles = smem;
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint8_t* epi = smem + STAGES * STAGE_BYTES;                // 1024-aligned
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(epi + EPI_BYTES);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_full = empty_bar + STAGES;
   uint64_t* acc_empty = acc_full + 2;
@@ -563,7 +630,9 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant
   } else {
     // ----------------------------------------------------------- epilogue
     const int quarter = warp & 3;
-    const int row_in_tile = (int)rank * ROWS + quarter * 32 + lane;
+    const int warp_row = (int)rank * ROWS + quarter * 32;
+    uint8_t* wbuf = epi + quarter * 2 * EPI_BOX_BYTES;
+    int sel = 0;
     int local = 0;
     WorkIter it(p, cluster, nclusters);
     int b, tm, tn, kb0, kb1;
@@ -572,20 +641,13 @@ gemm_pair_kernel(const __grid_constant__ CUtensorMap mapA, const __grid_constant
       const uint32_t use = static_cast<uint32_t>(local >> 1);
       if (!mbar_wait(&acc_full[buf], use & 1, abort_flag, p.err, kErrTimeoutEpilogue)) break;
       tc_fence_after();
-      const int row = tm * TM + row_in_tile;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(buf * TN);
-#pragma unroll 1
-      for (int c = 0; c < TN; c += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(t_row + c, r);
-        tmem_ld_wait();
-        const int col0 = tn * TN + c;
-        if (col0 < p.N) store_row_chunk(p, b, row, col0, reinterpret_cast<const float*>(r));
-      }
+      drain_rows<TN>(p, &mapC, wbuf, sel, b, tm * TM + warp_row + lane, tm * TM + warp_row, tn * TN, t_row, lane);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[buf]), 0));
     }
+    if (p.tma_c && lane == 0) bulk_wait<0>();
   }
 
   tc_fence_before();
@@ -637,6 +699,27 @@ bool make_map(CUtensorMap* map, const void* base, long long inner, long long row
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (std::getenv("VAGUS_GEMM_DEBUG")) std::fprintf(stderr, "[gemm] encode -> %d\n", (int)r);
   return r == CUDA_SUCCESS;
+}
+
+// C tensor map for the TMA-store epilogue: bf16 (N, M, batch), 32 x 32 boxes,
+// 64-byte swizzle.  False (register stores instead) when the output is not a
+// plain bf16 store, breaks the TMA rules (16-byte base / pitches), is smaller
+// than a box, or VAGUS_GEMM_NO_TMA_STORE is set.
+bool make_c_map(CUtensorMap* map, const GemmArgs& a) {
+  static const bool off = std::getenv("VAGUS_GEMM_NO_TMA_STORE") != nullptr;
+  if (off || a.atomic || a.c_f32 || a.scatter || (a.S != nullptr && a.beta != 0.f)) return false;
+  if ((reinterpret_cast<uintptr_t>(a.C) & 15u) || (a.ldc % 8) || (a.batch > 1 && a.strideC % 8)) return false;
+  if (a.N < 32 || a.M < 32 || a.ldc < a.N) return false;
+  EncodeFn enc = get_encode();
+  if (!enc) return false;
+  const long long bstride = a.batch > 1 ? a.strideC : a.ldc * a.M;
+  cuuint64_t dims[3] = {(cuuint64_t)a.N, (cuuint64_t)a.M, (cuuint64_t)a.batch};
+  cuuint64_t strides[2] = {(cuuint64_t)(a.ldc * 2), (cuuint64_t)(bstride * 2)};
+  cuuint32_t box[3] = {32u, 32u, 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, a.C, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
 }
 
 // Unit plan (see decode_unit): whole tiles for every complete wave, then the
@@ -719,6 +802,8 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
     p.vec = v ? 1 : 0;
   }
   if (!fill_scatter(p, a)) return 5;
+  CUtensorMap mc = ma;                     // a valid map either way; read only when tma_c
+  p.tma_c = make_c_map(&mc, a) ? 1 : 0;
   const int grid = std::min(p.units, num_sms());
   auto kern = gemm_kernel<BN, A_MN, B_MN, GM>;
   static bool attr_set[64] = {};
@@ -731,7 +816,7 @@ int launch_t(const GemmArgs& a, cudaStream_t stream) {
   if (std::getenv("VAGUS_GEMM_DEBUG"))
     std::fprintf(stderr, "[gemm] launch grid %d smem %d M %d N %d K %d units %d\n", grid, C::SMEM_BYTES, a.M, a.N,
                  a.K, p.units);
-  kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, p, gm);
+  kern<<<grid, NUM_THREADS, C::SMEM_BYTES, stream>>>(ma, mb, mc, p, gm);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -787,6 +872,8 @@ int launch_pair(const GemmArgs& a, cudaStream_t stream) {
     p.vec = v ? 1 : 0;
   }
   if (!fill_scatter(p, a)) return 5;
+  CUtensorMap mc = ma;
+  p.tma_c = make_c_map(&mc, a) ? 1 : 0;
   int units = p.units;
   p.streamk = 0;
   p.kb_per_worker = 0;
@@ -824,7 +911,7 @@ int launch_pair(const GemmArgs& a, cudaStream_t stream) {
   if (std::getenv("VAGUS_GEMM_DEBUG"))
     std::fprintf(stderr, "[gemm] pair launch clusters %d smem %d M %d N %d K %d units %d\n", clusters, SMEM_BYTES,
                  a.M, a.N, a.K, units);
-  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, p) != cudaSuccess) return 3;
+  if (cudaLaunchKernelEx(&cfg, kern, ma, mb, mc, p) != cudaSuccess) return 3;
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

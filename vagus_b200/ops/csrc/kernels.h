@@ -31,8 +31,11 @@ int sigmoid_gate_bwd(const void* dy, const void* x, const void* g, void* dx, voi
 // targets >= V are ignored like negative ones; status (optional) then records kErrBadTarget
 int softmax_ce(void* logits, const long long* targets, float* loss, float* lse, long long rows, int V, float scale,
                float z_coef, cudaStream_t st, int* status = nullptr);
-int embedding_fwd(const float* W, const long long* tok, void* y, int y_f32, long long n, int D, cudaStream_t st);
-int embedding_bwd(const void* dy, int dy_f32, const long long* tok, float* dW, long long n, int D, cudaStream_t st);
+// V: rows of the table (token ids are checked against it in the bounds-checked build)
+int embedding_fwd(const float* W, const long long* tok, void* y, int y_f32, long long n, int D, long long V,
+                  cudaStream_t st);
+int embedding_bwd(const void* dy, int dy_f32, const long long* tok, float* dW, long long n, int D, long long V,
+                  cudaStream_t st);
 int adamw_step(float* p, const float* g, float* m, float* v, void* shadow, long long n, float lr, float b1, float b2,
                float eps, float wd, float bc1, float bc2, float gscale, cudaStream_t st);
 int muon_momentum(const float* g, float* buf, void* upd, long long n, float mu, int nesterov, float gscale,

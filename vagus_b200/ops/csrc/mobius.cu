@@ -91,7 +91,7 @@ mobius_fwd_k(const float* __restrict__ A, const float* __restrict__ Bm, const fl
   for (int t = T.lo; t < T.hi; ++t) {
     const long long o = T.base + (long long)t * R;
     x = fmaf(A[o], x, Bm[o]) / fmaf(C[o], x, D[o]);
-    X[o] = x;
+    if (VAGUS_CHECK(o, (long long)gridDim.y * L * R)) X[o] = x;
   }
 }
 
