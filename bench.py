@@ -279,7 +279,7 @@ def run(args) -> dict:
         from vagus_b200.models import build_model
         from vagus_b200.models.losses import make_ce
         from vagus_b200.optim import build_optimizer
-        from vagus_b200.parallel import LMLoss, apply_fsdp, build_mesh, unwrap
+        from vagus_b200.parallel import LMLoss, apply_fsdp, build_mesh, unwrap, wrap_ddp
         from vagus_b200.train.main import StepRunner
         ops.native()
         model = build_model(cfg["model_name"], cfg["model_args"]).to(dev)
@@ -290,8 +290,7 @@ def run(args) -> dict:
             model = LMLoss(model, ce)
             apply_fsdp(model, mesh, comm=args.comm)
         elif is_dist:
-            from torch.nn.parallel import DistributedDataParallel as DDP
-            model = DDP(model, device_ids=[dev.index], output_device=dev.index)
+            model = wrap_ddp(model, dev, comm=args.comm)
         optimizer = build_optimizer(opt_name, unwrap(model), json.loads(json.dumps(opt_args)))
         runner = StepRunner(model, optimizer, ce, dev, grad_accum_steps=accum, grad_clip=1.0, is_fsdp=is_fsdp,
                             is_dist=is_dist, mesh=mesh)
@@ -404,8 +403,7 @@ def run(args) -> dict:
         "config": {"model": cfg["label"], "global_batch": cfg["global_tokens"], "seq_len": seq,
                    "micro_batch": micro, "grad_accum": accum,
                    "parallelism": f"{par}{world}" if world > 1 else "single",
-                   "collectives": ("nccl" if args.impl == "reference" or not is_fsdp else args.comm)
-                   if world > 1 else None,
+                   "collectives": ("nccl" if args.impl == "reference" else args.comm) if world > 1 else None,
                    "optimizer": opt_name, "l2": "no flush: every step's working set is >> 126 MB L2"},
         "e2e": {"value": round(e2e, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": 4},
@@ -428,7 +426,8 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--comm", default="nvlink", choices=["nvlink", "nccl"],
-                    help="FSDP2 collectives of our arm: NVLink peer-to-peer kernels or NCCL")
+                    help="collectives of our arm (FSDP2 all-gather / reduce-scatter, DDP all-reduce): "
+                         "NVLink peer-to-peer kernels or NCCL")
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")

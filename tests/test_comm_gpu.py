@@ -1,6 +1,7 @@
 """NVLink peer-to-peer collectives (ops/csrc/comm.cu) against NCCL, on two
-GPUs: raw all-gather / reduce-scatter over several epochs (slot reuse), and
-FSDP2 with the custom collectives installed against FSDP2 on NCCL."""
+GPUs: raw all-gather / reduce-scatter over several epochs (slot reuse),
+FSDP2 with the custom collectives installed against FSDP2 on NCCL, the fused
+Muon scatter, and the all-reduce (raw and as DDP's bucket hook)."""
 
 import os
 import socket
@@ -164,3 +165,88 @@ def test_muon_fused_scatter_matches_allgather():
         for kind, i, e in errs:
             assert e == 0.0, (rank, kind, i, e)
 
+
+def _allreduce_worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                          NCCL_NVLS_ENABLE="0")
+        torch.cuda.set_device(rank)
+        import datetime
+        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{rank}"),
+                                timeout=datetime.timedelta(seconds=120))
+        from vagus_b200 import ops
+        from vagus_b200.parallel import wrap_ddp
+        from vagus_b200.parallel.nvlink import NvlinkAllReduce
+        ar = NvlinkAllReduce(dist.group.WORLD, 8 << 20)
+        errs = []
+        g = torch.Generator(device="cuda").manual_seed(rank)
+        for it, (n, dt, op) in enumerate([(1, torch.float32, dist.ReduceOp.SUM), (7, torch.float32, dist.ReduceOp.AVG),
+                                           (4099, torch.bfloat16, dist.ReduceOp.AVG),
+                                           (1 << 20, torch.float32, dist.ReduceOp.AVG),
+                                           (123457, torch.float32, dist.ReduceOp.SUM),
+                                           (1 << 20, torch.bfloat16, dist.ReduceOp.SUM)]):
+            x = torch.randn(n, device="cuda", generator=g).to(dt)
+            ref = x.clone()
+            dist.all_reduce(ref, op=op)
+            ar(x, op)
+            tol = 1e-5 if dt == torch.float32 else 2e-2
+            errs.append(("ar", it, ((x.float() - ref.float()).abs().max() / ref.float().abs().max().clamp(min=1)).item(),
+                         tol))
+        big = torch.randn(3 << 20, device="cuda")                   # beyond the slot: NCCL fallback
+        ref = big.clone()
+        dist.all_reduce(ref)
+        ar(big, dist.ReduceOp.SUM)
+        errs.append(("fallback", 0, (big - ref).abs().max().item(), 1e-5))
+        errs.append(("fallback_used", 0, 0.0 if ar.calls["nccl"] == 1 else 1.0, 0.0))
+        torch.cuda.synchronize()
+
+        # DDP with the NVLink bucket all-reduce == DDP on NCCL
+        def trace(comm):
+            torch.manual_seed(0)
+            m = torch.nn.Sequential(torch.nn.Linear(256, 1024), torch.nn.GELU(), torch.nn.Linear(1024, 256)).cuda()
+            ddp = wrap_ddp(m, torch.device(f"cuda:{rank}"), comm)
+            opt = torch.optim.SGD(ddp.parameters(), lr=0.1)
+            out = []
+            for step in range(3):
+                xb = torch.randn(32, 256, device="cuda", generator=torch.Generator(device="cuda").manual_seed(step * 7 + rank))
+                opt.zero_grad()
+                ddp(xb).pow(2).mean().backward()
+                out.append(torch.cat([p.grad.flatten() for p in m.parameters()]).clone())
+                opt.step()
+            used = ddp.nvlink_allreduce.calls["nvlink"] if ddp.nvlink_allreduce is not None else 0
+            return out, used
+        a, _ = trace("nccl")
+        b, used = trace("nvlink")
+        for i, (x, y) in enumerate(zip(a, b)):
+            errs.append(("ddp", i, ((x - y).abs().max() / y.abs().max()).item(), 1e-5))
+        errs.append(("ddp_hook_used", 0, 0.0 if used > 0 else 1.0, 0.0))
+        errs.append(("error_word", 0, float(ops.native().error_word()), 0.0))
+        ar.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, errs))
+    except Exception as e:  # noqa: BLE001
+        import traceback
+        q.put((rank, traceback.format_exc() + repr(e)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_nvlink_all_reduce_and_ddp_hook_match_nccl():
+    """The two-shot NVLink all-reduce equals NCCL's (fp32 / bf16, sum /
+    average, ragged sizes, several epochs over both slots, a too-large
+    tensor through the NCCL fallback), and DDP with it as the bucket
+    communication hook produces the gradients DDP on NCCL does."""
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_allreduce_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in range(world)]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, errs in results:
+        assert not isinstance(errs, str), f"rank {rank}: {errs}"
+        for kind, it, e, tol in errs:
+            assert e <= tol, (rank, kind, it, e)

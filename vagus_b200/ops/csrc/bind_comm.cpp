@@ -91,6 +91,19 @@ void comm_reduce_scatter(Tensor out, Tensor in, std::vector<int64_t> bases, int6
   TORCH_CHECK(rc == 0, "comm_reduce_scatter failed (code ", rc, ")");
 }
 
+// In-place NVLink all-reduce of a contiguous fp32 / bf16 tensor, times scale
+// (heaps: header, two stage slots, two result regions of slot_cap bytes).
+void comm_all_reduce(Tensor buf, std::vector<int64_t> bases, int64_t rank, int64_t epoch, double scale,
+                     int64_t slot_cap) {
+  TORCH_CHECK(buf.is_contiguous() && (buf.scalar_type() == at::kFloat || buf.scalar_type() == at::kBFloat16),
+              "comm_all_reduce: contiguous fp32 / bf16");
+  const int rc = vagus::comm_all_reduce(peers_of(bases), static_cast<int>(rank), static_cast<int>(bases.size()),
+                                        static_cast<unsigned>(epoch), buf.data_ptr(), buf.numel(),
+                                        static_cast<int>(buf.element_size()), static_cast<float>(scale), slot_cap,
+                                        g_peer_wait_ns, vagus_device_error_ptr(), stream());
+  TORCH_CHECK(rc == 0, "comm_all_reduce failed (code ", rc, ")");
+}
+
 // Epoch barrier over the heaps (the generic flag block).
 void comm_barrier(std::vector<int64_t> bases, int64_t rank, int64_t epoch) {
   const int rc = vagus::comm_barrier(peers_of(bases), static_cast<int>(rank), static_cast<int>(bases.size()),
@@ -121,5 +134,6 @@ void register_comm_ops(pybind11::module& m) {
   m.def("comm_heap_open", &comm_heap_open);
   m.def("comm_heap_close", &comm_heap_close);
   m.def("comm_all_gather", &comm_all_gather);
+  m.def("comm_all_reduce", &comm_all_reduce);
   m.def("comm_reduce_scatter", &comm_reduce_scatter);
 }

@@ -27,6 +27,7 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <algorithm>
 #include <cstdint>
 
 namespace vagus {
@@ -136,6 +137,131 @@ __global__ void reduce_k(const CommPeers peers, int rank, int world, long long s
   }
 }
 
+// ----------------------------------------------------------- all-reduce --
+// Two-shot all-reduce over NVLink, three kernels on the caller's stream:
+//   ar_stage_k   copy the buffer into this rank's slot (e & 1); the CTA that
+//                finishes last publishes it: system-scope release of epoch e
+//                into every peer's "staged" flag for this rank;
+//   ar_push_k    every CTA waits (bounded) until all peers staged epoch e,
+//                then reduces its part of this rank's 1/world chunk over the
+//                peers' slots in fp32, applies `scale`, and stores the result
+//                into every rank's result region (e & 1) -- NVLink stores from
+//                the reducing threads; the last CTA publishes "pushed";
+//   ar_finish_k  waits until all peers pushed epoch e, copies the result out.
+// Reuse: slot (e & 1) is rewritten at epoch e + 2 only after this rank's
+// ar_finish_k(e + 1), which follows every peer's ar_push_k(e + 1), which
+// follows their reads of epoch e; the result region likewise.
+struct ArArgs {
+  CommPeers peers;
+  int rank, world;
+  uint32_t epoch;
+  long long n;              // elements
+  long long slot_cap;       // bytes per slot
+  float scale;
+  unsigned long long wait_ns;
+  int* err;
+};
+
+__device__ __forceinline__ uint8_t* ar_slot(const ArArgs& a, int r) {
+  return a.peers.base[r] + kCommHeaderBytes + (long long)(a.epoch & 1u) * a.slot_cap;
+}
+__device__ __forceinline__ uint8_t* ar_result(const ArArgs& a, int r) {
+  return a.peers.base[r] + kCommHeaderBytes + 2 * a.slot_cap + (long long)(a.epoch & 1u) * a.slot_cap;
+}
+
+// The last CTA of the grid to arrive publishes `epoch` into every peer's flag
+// block at flag_off (entry `rank`) after a system-scope fence.
+__device__ __forceinline__ void ar_publish_last(const ArArgs& a, int flag_off, int counter) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(a.peers.base[a.rank] + kCommArCount) + counter;
+    if (atomicAdd(cnt, 1u) == gridDim.x - 1) {
+      *cnt = 0;
+      __threadfence_system();
+      for (int p = 0; p < a.world; ++p)
+        st_release_sys(reinterpret_cast<uint32_t*>(a.peers.base[p] + flag_off) + a.rank, a.epoch);
+    }
+  }
+}
+
+// Every peer's flag at flag_off of this rank's heap reads >= epoch (bounded).
+__device__ __forceinline__ bool ar_wait_all(const ArArgs& a, int flag_off) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint32_t* f = reinterpret_cast<const uint32_t*>(a.peers.base[a.rank] + flag_off);
+    const unsigned long long t0 = globaltimer_ns();
+    for (int p = 0; p < a.world && ok; ++p) {
+      uint32_t spins = 0;
+      while (ld_acquire_sys(f + p) < a.epoch) {
+        if (((++spins) & 1023u) == 0u &&
+            (globaltimer_ns() - t0 > a.wait_ns || (a.err != nullptr && *(volatile int*)a.err != 0))) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+    if (!ok) record_error(a.err, kErrTimeoutPeer);
+  }
+  __syncthreads();
+  return ok != 0;
+}
+
+template <typename T>
+__global__ void ar_stage_k(const ArArgs a, const T* __restrict__ buf) {
+  copy_bytes(ar_slot(a, a.rank), reinterpret_cast<const uint8_t*>(buf), a.n * (long long)sizeof(T),
+             (long long)blockIdx.x * blockDim.x + threadIdx.x, (long long)gridDim.x * blockDim.x);
+  ar_publish_last(a, kCommArStaged, 0);
+}
+
+template <typename T>
+__global__ void ar_push_k(const ArArgs a) {
+  if (!ar_wait_all(a, kCommArStaged)) return;
+  // this rank's chunk [lo, hi), 8-element aligned so vector paths stay aligned
+  const long long per = ((a.n + a.world - 1) / a.world + 7) / 8 * 8;
+  const long long lo = min(a.n, (long long)a.rank * per), hi = min(a.n, lo + per);
+  const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, nt = (long long)gridDim.x * blockDim.x;
+  constexpr int V = 16 / sizeof(T);                      // elements per 16-byte vector
+  const long long nvec = (hi - lo) / V;
+  for (long long v = tid; v < nvec; v += nt) {
+    const long long i = lo + v * V;
+    float acc[V];
+#pragma unroll
+    for (int j = 0; j < V; ++j) acc[j] = 0.f;
+    for (int p = 0; p < a.world; ++p) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(ar_slot(a, p)) + i);
+      const T* e = reinterpret_cast<const T*>(&raw);
+#pragma unroll
+      for (int j = 0; j < V; ++j) acc[j] += to_f<T>(e[j]);
+    }
+    uint4 out;
+    T* o = reinterpret_cast<T*>(&out);
+#pragma unroll
+    for (int j = 0; j < V; ++j) {
+      if constexpr (sizeof(T) == 4) o[j] = a.scale * acc[j];
+      else o[j] = f2bf(a.scale * acc[j]);
+    }
+    for (int p = 0; p < a.world; ++p)
+      *reinterpret_cast<uint4*>(reinterpret_cast<T*>(ar_result(a, p)) + i) = out;
+  }
+  for (long long i = lo + nvec * V + tid; i < hi; i += nt) {      // ragged tail of the chunk
+    float acc = 0.f;
+    for (int p = 0; p < a.world; ++p) acc += to_f<T>(reinterpret_cast<const T*>(ar_slot(a, p))[i]);
+    T r;
+    if constexpr (sizeof(T) == 4) r = a.scale * acc; else r = f2bf(a.scale * acc);
+    for (int p = 0; p < a.world; ++p) reinterpret_cast<T*>(ar_result(a, p))[i] = r;
+  }
+  ar_publish_last(a, kCommArPushed, 1);
+}
+
+template <typename T>
+__global__ void ar_finish_k(const ArArgs a, T* __restrict__ buf) {
+  if (!ar_wait_all(a, kCommArPushed)) return;
+  copy_bytes(reinterpret_cast<uint8_t*>(buf), ar_result(a, a.rank), a.n * (long long)sizeof(T),
+             (long long)blockIdx.x * blockDim.x + threadIdx.x, (long long)gridDim.x * blockDim.x);
+}
+
 int grid_for(long long bytes) {
   long long b = (bytes / 16 + 255) / 256;
   if (b < 1) b = 1;
@@ -173,6 +299,31 @@ int comm_reduce_scatter(const CommPeers& peers, int rank, int world, uint32_t ep
   else
     reduce_k<__nv_bfloat16><<<g, 256, 0, st>>>(peers, rank, world, slot_off, static_cast<__nv_bfloat16*>(out),
                                                shard_elems, scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int comm_all_reduce(const CommPeers& peers, int rank, int world, uint32_t epoch, void* buf, long long n, int elem_bytes,
+                    float scale, long long slot_cap, unsigned long long wait_ns, int* err, cudaStream_t st) {
+  const long long bytes = n * elem_bytes;
+  if (world < 2 || world > kMaxCommPeers || bytes > slot_cap || (elem_bytes != 4 && elem_bytes != 2) ||
+      (reinterpret_cast<uintptr_t>(buf) & 15u) || (slot_cap & 255))
+    return 5;
+  if (n == 0) return 0;
+  ArArgs a;
+  a.peers = peers; a.rank = rank; a.world = world; a.epoch = epoch; a.n = n; a.slot_cap = slot_cap;
+  a.scale = scale; a.wait_ns = wait_ns; a.err = err;
+  // the waiting kernels keep their grids within one wave (one CTA per SM at most)
+  const int g_copy = std::min(grid_for(bytes), 148);
+  const int g_push = std::min(grid_for(bytes / world), 148);
+  if (elem_bytes == 4) {
+    ar_stage_k<float><<<g_copy, 256, 0, st>>>(a, static_cast<const float*>(buf));
+    ar_push_k<float><<<g_push, 256, 0, st>>>(a);
+    ar_finish_k<float><<<g_copy, 256, 0, st>>>(a, static_cast<float*>(buf));
+  } else {
+    ar_stage_k<__nv_bfloat16><<<g_copy, 256, 0, st>>>(a, static_cast<const __nv_bfloat16*>(buf));
+    ar_push_k<__nv_bfloat16><<<g_push, 256, 0, st>>>(a);
+    ar_finish_k<__nv_bfloat16><<<g_copy, 256, 0, st>>>(a, static_cast<__nv_bfloat16*>(buf));
+  }
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

@@ -169,6 +169,16 @@ int comm_reduce_scatter(const CommPeers& peers, int rank, int world, unsigned ep
 // heap (kMaxCommPeers u32 per heap): publishes this stream's earlier writes
 // (system-scope release), then waits (bounded) until every peer reached epoch.
 constexpr int kCommBarFlags = 512;
+// all-reduce: "slot staged" flags, "result pushed" flags, two CTA counters
+constexpr int kCommArStaged = 640;
+constexpr int kCommArPushed = 768;
+constexpr int kCommArCount = 896;
+// NVLink all-reduce of `n` elements (fp32 or bf16) of `buf` in place, times
+// `scale`, over heaps laid out [header][slot 0][slot 1][result 0][result 1]
+// (slot_cap bytes each); three launches, no extra synchronisation (see comm.cu).
+int comm_all_reduce(const CommPeers& peers, int rank, int world, unsigned epoch, void* buf, long long n,
+                    int elem_bytes, float scale, long long slot_cap, unsigned long long wait_ns, int* err,
+                    cudaStream_t st);
 int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, unsigned epoch, unsigned long long wait_ns,
                  int* err, cudaStream_t st);
 

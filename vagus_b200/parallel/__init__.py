@@ -112,11 +112,44 @@ def apply_fsdp(root: LMLoss, mesh, param_dtype: str = "bfloat16", reduce_dtype: 
                     reshard_after_forward=reshard_after_forward)
     fully_shard(root, mesh=mesh, mp_policy=root_mp, ignored_params=ignored)
     root.nvlink_heap = None
+    root.nvlink_allreduce = None
     if comm == "nvlink" and mesh.ndim == 1 and mesh.device_type == "cuda" and mesh.size() > 1:
-        from .nvlink import use_nvlink_collectives
+        from .nvlink import NvlinkAllReduce, use_nvlink_collectives
         root.nvlink_heap = use_nvlink_collectives(root, mesh.get_group())
+        if root.nvlink_heap is not None:
+            # the replicated 1-D gradients and the gradient-norm partial sums
+            cap = sum(p.numel() * 4 for p in root.replicated) + 4096
+            root.nvlink_allreduce = NvlinkAllReduce(mesh.get_group(), cap)
     elif comm not in ("nccl", "nvlink"):
         raise ValueError(f"unknown FSDP collective backend {comm!r} (nccl | nvlink)")
+
+
+def wrap_ddp(model: nn.Module, device: torch.device, comm: str = "nvlink") -> nn.Module:
+    """torch DDP around ``model``; with ``comm="nvlink"`` (CUDA, one machine)
+    its bucket all-reduce runs on our NVLink all-reduce kernels through a DDP
+    communication hook instead of NCCL."""
+    from torch.nn.parallel import DistributedDataParallel as DDP
+    cuda = device.type == "cuda"
+    ddp = DDP(model, device_ids=[device.index] if cuda else None, output_device=device.index if cuda else None)
+    ddp.nvlink_allreduce = None
+    if comm == "nvlink" and cuda:
+        from .nvlink import NvlinkAllReduce, ddp_bucket_cap, same_host
+        if same_host(dist.group.WORLD):
+            ar = NvlinkAllReduce(dist.group.WORLD, ddp_bucket_cap(model))
+            ddp.register_comm_hook(None, ar.ddp_hook)
+            ddp.nvlink_allreduce = ar
+    elif comm not in ("nccl", "nvlink"):
+        raise ValueError(f"unknown DDP collective backend {comm!r} (nccl | nvlink)")
+    return ddp
+
+
+def _all_reduce(model: nn.Module, t: torch.Tensor, op=dist.ReduceOp.AVG, group=None) -> None:
+    """All-reduce through the model's NVLink all-reduce when it has one."""
+    ar = getattr(model, "nvlink_allreduce", None)
+    if ar is not None and group is None:
+        ar(t, op)
+    else:
+        dist.all_reduce(t, op=op, group=group)
 
 
 def reduce_replicated(root: LMLoss, mesh=None) -> None:
@@ -124,7 +157,7 @@ def reduce_replicated(root: LMLoss, mesh=None) -> None:
     if not grads:
         return
     flat = torch.cat([g.flatten() for g in grads])
-    dist.all_reduce(flat, op=dist.ReduceOp.AVG)
+    _all_reduce(root, flat, dist.ReduceOp.AVG)
     torch._foreach_copy_(grads, list(flat.split([g.numel() for g in grads])))
 
 
@@ -156,7 +189,14 @@ def clip_grad_norm(model: nn.Module, max_norm: float | None) -> torch.Tensor:
     sharded = [p for p in params if isinstance(p.grad, DTensor)]
     plain = [p for p in params if not isinstance(p.grad, DTensor)]
     sq = torch.zeros((), device=params[0].grad.device if params else "cpu")
-    for group in (sharded, plain):
+    ar = getattr(model, "nvlink_allreduce", None)
+    if sharded and ar is not None:
+        # pure FSDP on NVLink: the local shards' squared norm, summed by one all-reduce on our kernel
+        local = [p.grad.to_local() for p in sharded]
+        part = torch.stack(torch._foreach_norm([t.float() for t in local])).square().sum().reshape(1)
+        ar(part, dist.ReduceOp.SUM)
+        sq = sq + part[0]
+    for group in ((plain,) if sharded and ar is not None else (sharded, plain)):
         if group:
             n = torch.nn.utils.get_total_norm(cast(list, [p.grad for p in group]), 2.0)
             if isinstance(n, DTensor):

@@ -27,8 +27,10 @@ output rows from the epilogue straight into the owning ranks' receive buffers
 row shards stay in the peers' heaps and the gathered-B GEMM reads them in
 place through per-owner TMA maps; ``unit_gather_layout`` gives where each
 FSDP2-managed parameter's shard sits in the all-gather staging slots.
-``set_dry_run`` switches the FSDP2 hooks off for the exposed-communication
-probe of ``bench.py``.
+``NvlinkAllReduce`` is the all-reduce on the same heaps: DDP's bucket
+all-reduce (as a DDP communication hook), FSDP's replicated-parameter
+average and the gradient-norm sum.  ``set_dry_run`` switches the FSDP2
+hooks off for the exposed-communication probe of ``bench.py``.
 
 Parity: the reference runs these collectives inside FSDP2 on NCCL
 (``infra/train/main.py:253-275``); the gradient reduction semantics (average
@@ -181,6 +183,60 @@ class NvlinkReduceScatter(ReduceScatter):
         native().comm_reduce_scatter(output_tensor, input_tensor.contiguous(), h.bases, h.rank, h.rs_epoch, scale,
                                      h.ag_cap, h.rs_cap)
         return None
+
+
+class NvlinkAllReduce:
+    """In-place all-reduce (sum or average) of fp32 / bf16 tensors over a
+    group on our NVLink kernels (``comm.cu``: stage into this rank's heap
+    slot, each rank reduces its 1/world chunk over the peers' slots in fp32
+    and stores the result into every rank's result region, copy out -- three
+    launches, the 1/world of an average folded into the reduction).
+
+    Tensors that are not contiguous, not 16-byte aligned or larger than the
+    heap's slots go to NCCL; the choice depends only on sizes and dtypes,
+    which are the same on every rank.  ``ddp_hook`` is a DDP communication
+    hook (``DistributedDataParallel.register_comm_hook``) averaging each
+    gradient bucket this way."""
+
+    def __init__(self, group, cap_bytes: int):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.slot = (int(cap_bytes) + 255) // 256 * 256
+        self.own, self.bases = open_heaps(group, HEADER + 4 * self.slot)
+        self.epoch = 0
+        self.calls = {"nvlink": 0, "nccl": 0}
+
+    def __call__(self, t: torch.Tensor, op=dist.ReduceOp.AVG) -> None:
+        ok = (op in (dist.ReduceOp.SUM, dist.ReduceOp.AVG) and t.is_cuda and t.is_contiguous()
+              and t.dtype in (torch.float32, torch.bfloat16) and t.numel() * t.element_size() <= self.slot
+              and t.data_ptr() % 16 == 0)
+        if not ok:
+            self.calls["nccl"] += 1
+            dist.all_reduce(t, op=op, group=self.group)
+            return
+        self.calls["nvlink"] += 1
+        self.epoch += 1
+        scale = 1.0 / self.world if op == dist.ReduceOp.AVG else 1.0
+        native().comm_all_reduce(t, self.bases, self.rank, self.epoch, scale, self.slot)
+
+    def ddp_hook(self, _state, bucket) -> torch.futures.Future:
+        buf = bucket.buffer()
+        self(buf, dist.ReduceOp.AVG)
+        fut: torch.futures.Future = torch.futures.Future()
+        fut.set_result(buf)                 # stream-ordered: later users run after our kernels
+        return fut
+
+    def close(self) -> None:
+        close_heaps(self.own, self.bases)
+        self.bases = []
+
+
+def ddp_bucket_cap(model, bucket_cap_mb: float = 25.0) -> int:
+    """Bytes a DDP gradient bucket can reach: a bucket closes once it holds
+    ``bucket_cap_mb``, so it is at most that plus the largest parameter."""
+    largest = max((p.numel() * p.element_size() for p in model.parameters() if p.requires_grad), default=0)
+    return int(bucket_cap_mb * 2 ** 20) + largest
 
 
 def _unit_sizes(root, world: int):

@@ -46,7 +46,7 @@ from ..models import build_model
 from ..models.io import export_slim
 from ..models.losses import make_ce
 from ..optim import build_optimizer
-from ..parallel import (DTYPES, LMLoss, apply_fsdp, build_mesh, clip_grad_norm, optimizer_members,
+from ..parallel import (DTYPES, LMLoss, apply_fsdp, build_mesh, clip_grad_norm, optimizer_members, wrap_ddp,
                         reduce_replicated, setup_distributed, unsharded, unwrap)
 from ..utils import atomic_write, git_state
 from .metrics import FAST_METRICS, SLOW_METRICS, MetricCtx, Monitor
@@ -85,6 +85,7 @@ class TrainConfig:
     fsdp_reduce_dtype: str = "float32"
     fsdp_reshard_after_forward: bool = True
     fsdp_comm: str = "nvlink"          # FSDP2 all-gather / reduce-scatter: our NVLink kernels or "nccl"
+    ddp_comm: str = "nvlink"           # DDP bucket all-reduce: our NVLink kernel (a DDP comm hook) or "nccl"
     grad_clip: float | None = 1.0
     z_loss: float | None = None
     ce_impl: str = "liger"
@@ -359,9 +360,7 @@ def train(config: TrainConfig, teardown: bool = True):
         apply_fsdp(model, mesh, config.fsdp_param_dtype, config.fsdp_reduce_dtype, config.fsdp_reshard_after_forward,
                    comm=config.fsdp_comm if device.type == "cuda" else "nccl")
     elif is_dist:
-        from torch.nn.parallel import DistributedDataParallel as DDP
-        model = DDP(model, device_ids=[device.index] if device.type == "cuda" else None,
-                    output_device=device.index if device.type == "cuda" else None)
+        model = wrap_ddp(model, device, config.ddp_comm if device.type == "cuda" else "nccl")
     optimizer = build_optimizer(config.optimizer_name, unwrap(model), config.optimizer_args)
     sched = build_schedule(config.schedule_name, config.schedule_args)
 
