@@ -5,18 +5,17 @@
                  uint64 ``.idx.npy`` of document offsets.  Windows are read
                  with ``os.pread`` (the GIL is released during the disk wait);
                  memmaps stay for document addressing.
-``WindowLoader`` uniform non-overlapping windows of context_len + 1 tokens,
-                 reshuffled per epoch by ``default_rng((seed, epoch))``, ranks
-                 taking interleaved slices of the global order (global batch
-                 g = batch_in_epoch * world + rank), exactly resumable from
-                 (epoch, batch_in_epoch) with a fingerprint of the order-defining
-                 parameters.  A background thread prefetches batches into
-                 pinned host memory so the host -> device copy can overlap the
-                 step.  The batch sequence is a pure function of (seed, epoch,
-                 rank, batch index) and identical with or without prefetch.
+``WindowOrder``  the data-order contract: non-overlapping windows of
+                 context_len + 1 tokens, permuted per epoch by
+                 ``default_rng((seed, epoch))``, global batch g = b * world +
+                 rank, and the fingerprint of everything the order depends on.
+``WindowLoader`` one rank's batches in that order, read by a prefetch thread
+                 into pinned host memory, exactly resumable from (epoch, batch
+                 in epoch); the sequence is the same with or without prefetch.
 
-Parity: reference ``infra/dataset/loader.py:31-246`` (format, window policy,
-order, state dict and fingerprint are the same).
+Parity: reference ``infra/dataset/loader.py`` (store format, window policy,
+order, state dict and fingerprint are the same, so a run resumes and pairs
+across frameworks on identical data).
 """
 
 from __future__ import annotations
@@ -78,105 +77,144 @@ class TokenStore:
                 pass
 
 
+class WindowOrder:
+    """Which windows a rank reads, batch by batch: the data-order contract.
+
+    Window w of a shard spans tokens [w L, w L + L + 1) (L = context_len).
+    Epoch e visits all windows in ``default_rng((seed, e)).permutation``
+    order (unshuffled: store order); global batch g of an epoch is the
+    ``batch_size`` windows at positions [g B, g B + B) of that order, and rank
+    R of W takes global batches g = b W + R for its b-th batch.  The
+    fingerprint names every parameter the order depends on, so a resume
+    under a different one is refused."""
+
+    def __init__(self, store: "TokenStore", context_len: int, batch_size: int, seed: int, rank: int, world: int,
+                 shuffle: bool):
+        self.L, self.B, self.seed, self.rank, self.world, self.shuffle = \
+            context_len, batch_size, seed, rank, world, shuffle
+        counts = [(n - 1) // context_len for n in store.shard_tokens]
+        first = np.cumsum([0] + store.shard_tokens[:-1])
+        # flat start (in the concatenated store) of every window, store order
+        self.starts = (np.concatenate([f + context_len * np.arange(c, dtype=np.int64) for c, f in zip(counts, first)])
+                       if counts else np.zeros(0, dtype=np.int64))
+        self.shard_edges = np.cumsum([0] + store.shard_tokens)
+        self.windows = len(self.starts)
+        self.batches_per_epoch = self.windows // (world * batch_size)
+        self._cached: tuple[int, np.ndarray] | None = None
+
+    def fingerprint(self) -> tuple:
+        return (self.windows, self.L, self.B, self.seed, self.world, self.shuffle)
+
+    def epoch_starts(self, epoch: int) -> np.ndarray:
+        if not self.shuffle:
+            return self.starts
+        if self._cached is None or self._cached[0] != epoch:
+            perm = np.random.default_rng((self.seed, epoch)).permutation(self.windows)
+            self._cached = (epoch, self.starts[perm])
+        return self._cached[1]
+
+    def batch(self, epoch: int, b: int) -> tuple[np.ndarray, np.ndarray]:
+        """(shard, offset in shard) of the windows of this rank's batch b."""
+        g = b * self.world + self.rank
+        flat = self.epoch_starts(epoch)[g * self.B:(g + 1) * self.B]
+        shard = np.searchsorted(self.shard_edges, flat, side="right") - 1
+        return shard, flat - self.shard_edges[shard]
+
+
+class _Prefetcher:
+    """A daemon thread running ``produce`` ahead of the consumer into a
+    bounded queue; an exception in the thread is raised in the consumer, and
+    ``close`` stops the thread at its next hand-off."""
+
+    def __init__(self, produce, depth: int):
+        self.q: queue.Queue = queue.Queue(maxsize=depth)
+        self.stop = threading.Event()
+        self.thread = threading.Thread(target=self._run, args=(produce,), daemon=True, name="WindowLoader-prefetch")
+        self.thread.start()
+
+    def _run(self, produce) -> None:
+        try:
+            for item in produce:
+                while not self.stop.is_set():
+                    try:
+                        self.q.put(item, timeout=1.0)
+                        break
+                    except queue.Full:
+                        continue
+                if self.stop.is_set():
+                    return
+        except BaseException as e:  # noqa: BLE001 -- handed to the consumer
+            self.q.put(e)
+
+    def __iter__(self):
+        while True:
+            item = self.q.get()
+            if isinstance(item, BaseException):
+                raise item
+            yield item
+
+    def close(self) -> None:
+        self.stop.set()
+
+
 class WindowLoader:
+    """Batches (x, y) of int64 token windows (B, L) for one rank, in the
+    order of ``WindowOrder``, from a background prefetcher into pinned host
+    memory (``pin_memory`` on CUDA hosts) so the copy to the device can
+    overlap the step.  ``state_dict`` / ``load_state_dict`` resume exactly at
+    (epoch, batch in epoch)."""
+
     def __init__(self, store: TokenStore, context_len: int, batch_size: int, *, seed: int = 0, rank: int = 0,
                  world_size: int = 1, shuffle: bool = True, prefetch: int = 4, pin_memory: bool = False):
-        assert context_len > 0 and batch_size > 0
-        assert 0 <= rank < world_size
-        assert prefetch >= 0
+        if context_len <= 0 or batch_size <= 0 or not 0 <= rank < world_size or prefetch < 0:
+            raise ValueError("WindowLoader: bad context_len / batch_size / rank / prefetch")
         self.store = store
-        self.context_len = context_len
-        self.batch_size = batch_size
-        self.seed = seed
-        self.rank = rank
-        self.world_size = world_size
-        self.shuffle = shuffle
-        self.prefetch = prefetch
+        self.context_len, self.batch_size, self.seed = context_len, batch_size, seed
+        self.rank, self.world_size, self.shuffle, self.prefetch = rank, world_size, shuffle, prefetch
         self.pin_memory = pin_memory and torch.cuda.is_available()
-        # window k of a shard starts at k * context_len and spans context_len + 1 tokens
-        per_shard = [(n - 1) // context_len for n in store.shard_tokens]
-        bases = np.cumsum([0] + store.shard_tokens[:-1])
-        self._starts = (np.concatenate([b + np.arange(w, dtype=np.int64) * context_len
-                                        for w, b in zip(per_shard, bases)])
-                        if per_shard else np.zeros(0, dtype=np.int64))
-        self._shard_base = np.cumsum([0] + store.shard_tokens)
-        self.window_count = len(self._starts)
-        self.batches_per_epoch = self.window_count // (world_size * batch_size)
-        assert self.batches_per_epoch > 0, "fewer windows than one global batch"
+        self.order = WindowOrder(store, context_len, batch_size, seed, rank, world_size, shuffle)
+        self.window_count = self.order.windows
+        self.batches_per_epoch = self.order.batches_per_epoch
+        if self.batches_per_epoch <= 0:
+            raise ValueError(f"the store holds {self.window_count} windows of {context_len + 1} tokens: fewer than "
+                             f"one global batch ({world_size} x {batch_size})")
         self.tokens_per_batch = batch_size * context_len
         self.epoch = 0
         self.batch_in_epoch = 0
 
-    def _epoch_order(self, epoch: int) -> np.ndarray:
-        if not self.shuffle:
-            return self._starts
-        return self._starts[np.random.default_rng((self.seed, epoch)).permutation(self.window_count)]
-
-    def _fingerprint(self) -> tuple:
-        return (self.window_count, self.context_len, self.batch_size, self.seed, self.world_size, self.shuffle)
-
     def state_dict(self) -> dict:
-        return {"epoch": self.epoch, "batch_in_epoch": self.batch_in_epoch, "fingerprint": self._fingerprint()}
+        return {"epoch": self.epoch, "batch_in_epoch": self.batch_in_epoch, "fingerprint": self.order.fingerprint()}
 
     def load_state_dict(self, state: dict) -> None:
-        if tuple(state["fingerprint"]) != self._fingerprint():
-            raise ValueError("loader state was produced under a different data order (fingerprint mismatch)")
+        if tuple(state["fingerprint"]) != self.order.fingerprint():
+            raise ValueError(f"this checkpoint's data order {tuple(state['fingerprint'])} differs from the loader's "
+                             f"{self.order.fingerprint()} (windows, context, batch, seed, world, shuffle)")
         self.epoch = state["epoch"]
         self.batch_in_epoch = state["batch_in_epoch"]
 
-    def _gather(self, flat_starts: np.ndarray):
+    def _read(self, epoch: int, b: int):
+        shard, off = self.order.batch(epoch, b)
         L = self.context_len
-        out = torch.empty((len(flat_starts), L + 1), dtype=torch.int64, pin_memory=self.pin_memory)
-        arr = out.numpy()
-        for row, flat in enumerate(flat_starts):
-            s = int(np.searchsorted(self._shard_base, flat, side="right")) - 1
-            arr[row] = self.store.read_window(s, int(flat - self._shard_base[s]), L + 1)
-        return out[:, :-1], out[:, 1:]
+        buf = torch.empty((self.batch_size, L + 1), dtype=torch.int64, pin_memory=self.pin_memory)
+        rows = buf.numpy()
+        for i in range(self.batch_size):
+            rows[i] = self.store.read_window(int(shard[i]), int(off[i]), L + 1)
+        return epoch, b, buf[:, :-1], buf[:, 1:]
 
-    def _produce(self, epoch: int, batch_in_epoch: int):
-        B, W, R = self.batch_size, self.world_size, self.rank
+    def _batches(self, epoch: int, b: int):
         while True:
-            order = self._epoch_order(epoch)
-            while batch_in_epoch < self.batches_per_epoch:
-                g = batch_in_epoch * W + R
-                x, y = self._gather(order[g * B:(g + 1) * B])
-                yield epoch, batch_in_epoch, x, y
-                batch_in_epoch += 1
-            epoch += 1
-            batch_in_epoch = 0
+            while b < self.batches_per_epoch:
+                yield self._read(epoch, b)
+                b += 1
+            epoch, b = epoch + 1, 0
 
     def __iter__(self):
-        src = self._produce(self.epoch, self.batch_in_epoch)
-        if self.prefetch == 0:
-            for epoch, b, x, y in src:
-                self.epoch, self.batch_in_epoch = epoch, b + 1
-                yield x, y
-            return
-        q: queue.Queue = queue.Queue(maxsize=self.prefetch)
-        stop = threading.Event()
-
-        def reader():
-            try:
-                for item in src:
-                    while not stop.is_set():
-                        try:
-                            q.put(item, timeout=1.0)
-                            break
-                        except queue.Full:
-                            pass
-                    else:
-                        return
-            except BaseException as e:  # surfaced in the consumer
-                q.put(e)
-
-        threading.Thread(target=reader, daemon=True, name="WindowLoader-prefetch").start()
+        src = self._batches(self.epoch, self.batch_in_epoch)
+        pre = _Prefetcher(src, self.prefetch) if self.prefetch else None
         try:
-            while True:
-                item = q.get()
-                if isinstance(item, BaseException):
-                    raise item
-                epoch, b, x, y = item
-                self.epoch, self.batch_in_epoch = epoch, b + 1
+            for epoch, b, x, y in (pre if pre is not None else src):
+                self.epoch, self.batch_in_epoch = epoch, b + 1      # the position after this batch
                 yield x, y
         finally:
-            stop.set()
+            if pre is not None:
+                pre.close()

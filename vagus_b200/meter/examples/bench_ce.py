@@ -1,6 +1,8 @@
 """Linear cross-entropy over the vocabulary: the fused kernel path
 (``make_ce('fused')``, logits never materialised in full) against the plain
-path (``make_ce('full')``), forward+backward time and peak memory.
+path (``make_ce('full')``) and, when it is installed, liger's fused linear
+cross-entropy (the reference's default), forward+backward time and peak
+memory, z-loss 1e-4 in all three.
 
     python -m vagus_b200.meter.examples.bench_ce --T 32768 --D 1024 --V 32000
 """
@@ -34,6 +36,18 @@ def main(argv=None):
             loss = ce(h, w, y)
             return torch.autograd.grad(loss, (h, w))[0]
         variants[impl] = run
+    if dev == "cuda":
+        try:
+            from liger_kernel.transformers.fused_linear_cross_entropy import LigerFusedLinearCrossEntropyLoss
+        except ImportError:
+            LigerFusedLinearCrossEntropyLoss = None
+        if LigerFusedLinearCrossEntropyLoss is not None:
+            lg = LigerFusedLinearCrossEntropyLoss(lse_square_scale=1e-4)
+
+            def run_liger():
+                loss = lg(w, h.view(-1, a.D), y.view(-1))
+                return torch.autograd.grad(loss, (h, w))[0]
+            variants["liger"] = run_liger
     compare(variants, ref="full", iters=a.iters)
 
 
