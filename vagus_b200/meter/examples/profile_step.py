@@ -64,7 +64,7 @@ def main(argv=None):
         loss, _z, _g = runner.step(iter([batch]))
         return loss
 
-    traces = profile_variants({name: step}, steps=a.steps, warmup=a.warmup, out_dir=a.out)
+    traces = profile_variants({name: step}, steps=a.steps, warmup=a.warmup, out_dir=a.out, device=dev)
     if dev.type != "cuda" or not traces:
         return {"traces": {k: str(v) for k, v in traces.items()}}
     # device time by family, from a second, quiet profile

@@ -48,9 +48,11 @@ def is_own_kernel(kernel: str) -> bool:
 
 
 def device_split(prof, steps: int = 1) -> dict:
-    """Device ms per step by family and by origin from a finished profile."""
+    """Device ms per step by family, by origin and by kernel from a finished
+    profile."""
     fams: dict[str, float] = {}
     origin = {"own": 0.0, "library": 0.0}
+    kernels: dict[str, list] = {}
     for ev in prof.key_averages():
         us = getattr(ev, "self_device_time_total", 0.0) or getattr(ev, "self_cuda_time_total", 0.0)
         if us <= 0 or getattr(ev, "device_type", None) is not None and "CUDA" not in str(ev.device_type):
@@ -58,24 +60,39 @@ def device_split(prof, steps: int = 1) -> dict:
         ms = us / 1e3 / max(1, steps)
         fams[family(ev.key)] = fams.get(family(ev.key), 0.0) + ms
         origin["own" if is_own_kernel(ev.key) else "library"] += ms
-    return {"families_ms": fams, "origin_ms": origin}
+        k = kernels.setdefault(ev.key, [0.0, 0])
+        k[0] += ms
+        k[1] += ev.count // max(1, steps)
+    return {"families_ms": fams, "origin_ms": origin, "kernels": kernels}
 
 
-def render_split(split: dict) -> str:
+def _short(kernel: str, width: int = 90) -> str:
+    name = kernel.replace("(anonymous namespace)::", "")
+    name = re.sub(r"^void |\(.*$", "", name)
+    return name if len(name) <= width else name[:width - 3] + "..."
+
+
+def render_split(split: dict, top: int = 25) -> str:
     fams, origin = split["families_ms"], split["origin_ms"]
     total = sum(fams.values()) or 1.0
     rows = [[f, f"{ms:.2f}", f"{100 * ms / total:.1f} %"] for f, ms in sorted(fams.items(), key=lambda kv: -kv[1])]
     rows += [[f"[{k} kernels]", f"{v:.2f}", f"{100 * v / total:.1f} %"] for k, v in origin.items()]
-    return format_table(["family", "ms / step", "share"], rows)
+    text = format_table(["family", "ms / step", "share"], rows)
+    kern = sorted(split.get("kernels", {}).items(), key=lambda kv: -kv[1][0])[:top]
+    if kern:
+        krows = [[_short(k), str(n), f"{ms:.2f}", f"{100 * ms / total:.1f} %"] for k, (ms, n) in kern]
+        text += "\n\n" + format_table(["kernel", "calls / step", "ms / step", "share"], krows)
+    return text
 
 
 def profile_variants(variants: dict[str, Callable], args: tuple = (), kwargs: Optional[dict] = None, *,
                      steps: int = 5, warmup: int = 3, out_dir: str = "profile-output",
-                     row_limit: int = 12) -> dict[str, pathlib.Path]:
+                     row_limit: int = 12, device=None) -> dict[str, pathlib.Path]:
     """Profile each variant ``steps`` times after ``warmup`` calls; returns
-    ``{name: trace path}`` (a variant that raises is reported and skipped)."""
+    ``{name: trace path}`` (a variant that raises is reported and skipped).
+    ``device``: where the variants run when no argument tells (closures)."""
     kwargs = kwargs or {}
-    device = infer_device(args, kwargs)
+    device = device if device is not None else infer_device(args, kwargs)
     cuda = device.type == "cuda"
     activities = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if cuda else [])
     out = pathlib.Path(out_dir)

@@ -22,6 +22,7 @@
 #include "kernels.h"
 
 #include <algorithm>
+#include <cstdlib>
 
 namespace vagus {
 namespace {
@@ -341,6 +342,201 @@ conv_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict
   }
 }
 
+// ----------------------------------------------------- backward, one pass --
+// For heads of 128 / 256 channels: a pair of warps (64 lanes, VEC = HD / 64
+// channels each) walks a run of RW consecutive tokens once, with the last
+// K - 1 inputs and the last K - 1 values of du = dL/du in registers:
+//   token t:  u(t) from x[t-3..t];  du(t) through the L2 norm (the head's dot
+//             product is a warp sum plus one exchange between the pair's two
+//             warps) and SiLU;  dw[k] += du(t) x[t-3+k] for the run's own
+//             tokens;  dx[t-3] = sum_i w[3-i] du(t-3+i) is then complete.
+// The run reads x and dy straight from global memory (each warp pair's row is
+// one contiguous 2 * HD-byte segment), with the next two tokens' loads in
+// flight; its K - 1 right-context tokens are recomputed (3 / RW extra work).
+// No shared-memory staging, no block-wide barriers: the cost per element is
+// the arithmetic of the chain rule.  dw is summed over the CTA's pairs in
+// shared memory and added with one atomic per (channel, tap) per CTA.
+constexpr int RUN = 64;                     // tokens per warp-pair run
+
+template <int VEC>
+__device__ __forceinline__ void ldg_row(const __nv_bfloat16* p, bool ok, uint32_t (&r)[VEC / 2]) {
+  if constexpr (VEC == 4) {
+    uint2 t = ok ? __ldg(reinterpret_cast<const uint2*>(p)) : make_uint2(0u, 0u);
+    r[0] = t.x; r[1] = t.y;
+  } else {
+    r[0] = ok ? __ldg(reinterpret_cast<const unsigned int*>(p)) : 0u;
+  }
+}
+
+template <int VEC>
+__device__ __forceinline__ void unpack_row(const uint32_t (&r)[VEC / 2], float (&v)[VEC]) {
+#pragma unroll
+  for (int j = 0; j < VEC / 2; ++j) {
+    const float2 f = unpack_bf16x2(r[j]);
+    v[2 * j] = f.x;
+    v[2 * j + 1] = f.y;
+  }
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(THREADS, 2)
+conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
+               const float* __restrict__ w, const float* __restrict__ rnorm, __nv_bfloat16* __restrict__ dx,
+               long long lddx, float* __restrict__ dw, long long L, int D, int l2) {
+  constexpr int K = 4;
+  constexpr int HD = VEC * 64;
+  constexpr int PAIRS = WARPS / 2;
+  __shared__ float dot_x[PAIRS][2][2];       // [pair][warp of the pair][token parity]
+  __shared__ float red[PAIRS][K][HD];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int pair = warp >> 1, half = warp & 1;
+  const int ch = (half * 32 + lane) * VEC;  // first channel of this thread within the head
+  const long long b = blockIdx.z;
+  const int head = blockIdx.y;
+  const int nH = D / HD;
+  const int c0 = head * HD + ch;
+  float wr[K][VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const float4 t = *reinterpret_cast<const float4*>(w + (long long)(c0 + j) * K);
+    wr[0][j] = t.x; wr[1][j] = t.y; wr[2][j] = t.z; wr[3][j] = t.w;
+  }
+  float dwa[K][VEC];
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) dwa[k][j] = 0.f;
+  const long long runs = (L + RUN - 1) / RUN;
+  const int bar = 1 + pair;                 // named barrier of this warp pair (0 is __syncthreads)
+  for (long long run = (long long)blockIdx.x * PAIRS + pair; run < runs; run += (long long)gridDim.x * PAIRS) {
+    const long long t0 = run * RUN;
+    const long long t_end = min(L, t0 + RUN);            // the run's own tokens end here
+    const __nv_bfloat16* xb = x + b * L * ldx + c0;
+    const __nv_bfloat16* gb = dy + b * L * D + c0;
+    float xw[K - 1][VEC];                                 // x[t-1], x[t-2], x[t-3]
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) {
+      const long long t = t0 - 1 - i;
+      uint32_t r[VEC / 2];
+      ldg_row<VEC>(xb + t * ldx, t >= 0, r);
+      unpack_row<VEC>(r, xw[i]);
+    }
+    float dw3[K - 1][VEC];                                // du(t-1), du(t-2), du(t-3)
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i)
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) dw3[i][j] = 0.f;
+    // two tokens of loads in flight
+    uint32_t qx[2][VEC / 2], qg[2][VEC / 2];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      const long long t = t0 + p;
+      ldg_row<VEC>(xb + t * ldx, t < L, qx[p]);
+      ldg_row<VEC>(gb + t * D, t < L, qg[p]);
+    }
+    const long long t_last = min(L, t0 + RUN + K - 1);   // du needed up to here (exclusive)
+    for (long long t = t0; t < t_last; ++t) {
+      float xc[VEC], g[VEC];
+      unpack_row<VEC>(qx[0], xc);
+      unpack_row<VEC>(qg[0], g);
+#pragma unroll
+      for (int j = 0; j < VEC / 2; ++j) { qx[0][j] = qx[1][j]; qg[0][j] = qg[1][j]; }
+      {
+        const long long tn = t + 2;
+        const bool ok = tn < t_last;
+        ldg_row<VEC>(xb + tn * ldx, ok, qx[1]);
+        ldg_row<VEC>(gb + tn * D, ok, qg[1]);
+      }
+      float u[VEC], sg[VEC], z[VEC];
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        u[j] = wr[3][j] * xc[j] + wr[2][j] * xw[0][j] + wr[1][j] * xw[1][j] + wr[0][j] * xw[2][j];
+        sg[j] = sigmoid_f(u[j]);
+        z[j] = u[j] * sg[j];
+        dot += g[j] * z[j];
+      }
+      if (l2) {
+        dot = warp_sum(dot);
+        const int par = static_cast<int>(t & 1);
+        if (lane == 0) dot_x[pair][half][par] = dot;
+        asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
+        dot += dot_x[pair][half ^ 1][par];
+        const float rn = rnorm[(b * L + t) * nH + head];
+        const float c3 = rn * rn * rn * dot;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) g[j] = rn * g[j] - c3 * z[j];
+      }
+      float du[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) du[j] = g[j] * sg[j] * (1.f + u[j] * (1.f - sg[j]));
+      if (t < t_end) {                                    // the run's own token: weight gradient
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          dwa[0][j] += du[j] * xw[2][j];
+          dwa[1][j] += du[j] * xw[1][j];
+          dwa[2][j] += du[j] * xw[0][j];
+          dwa[3][j] += du[j] * xc[j];
+        }
+      }
+      const long long s = t - (K - 1);                    // dx[s] needs du(s .. s + 3)
+      if (s >= t0) {
+        float o[VEC];
+#pragma unroll
+        for (int j = 0; j < VEC; ++j)
+          o[j] = wr[3][j] * dw3[2][j] + wr[2][j] * dw3[1][j] + wr[1][j] * dw3[0][j] + wr[0][j] * du[j];
+        if (VAGUS_CHECK((b * L + s) * lddx + c0 + VEC - 1, (long long)gridDim.z * L * lddx)) {
+          __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
+          if constexpr (VEC == 4)
+            *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+          else
+            *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        xw[2][j] = xw[1][j]; xw[1][j] = xw[0][j]; xw[0][j] = xc[j];
+        dw3[2][j] = dw3[1][j]; dw3[1][j] = dw3[0][j]; dw3[0][j] = du[j];
+      }
+    }
+    // tokens past the end of the sequence have du = 0 (dy is zero there):
+    // the run's last K - 1 dx rows, when the sequence ends inside the halo
+    for (long long s = max(t0, t_last - (K - 1)); s < t_end; ++s) {
+      // du(s + i) for s + i < t_last sits in dw3 at index t_last - 1 - (s + i)
+      float o[VEC];
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) {
+        float acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < K; ++i) {
+          const long long tt = s + i;
+          const long long back = t_last - 1 - tt;           // 0 .. 2 inside the window
+          if (tt < t_last && back < K - 1) acc += wr[K - 1 - i][j] * dw3[back][j];
+        }
+        o[j] = acc;
+      }
+      __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
+      if constexpr (VEC == 4)
+        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+      else
+        *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
+    }
+  }
+  // dw: sum over the CTA's pairs, one atomic per (channel, tap)
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) red[pair][k][ch + j] = dwa[k][j];
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < HD * K; idx += THREADS) {
+    const int c = idx / K, k = idx - c * K;
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < PAIRS; ++q) sum += red[q][k][c];
+    atomicAdd(&dw[(long long)(head * HD + c) * K + k], sum);
+  }
+}
+
 template <int VEC, int K>
 int launch_fwd(const void* xp, long long ldx, const float* w, void* y, float* rnorm, long long B, long long L, int D,
                int l2, cudaStream_t st) {
@@ -399,6 +595,25 @@ int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w,
       lddx % 8)
     return 5;
   int rc = 5;
+  static const bool old_bwd = std::getenv("VAGUS_CONV_STAGED_BWD") != nullptr;
+  if ((head_dim == 256 || head_dim == 128) && !old_bwd) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long runs = (L + RUN - 1) / RUN;
+    const long long ctas_per_seq = (runs + WARPS / 2 - 1) / (WARPS / 2);
+    const long long seqs = B * (D / head_dim);
+    // about two waves of CTAs in flight; each CTA loops over runs of its (batch, head)
+    const long long bx = std::max<long long>(1, std::min<long long>(ctas_per_seq, (4LL * sms + seqs - 1) / seqs));
+    dim3 grid(static_cast<unsigned>(bx), D / head_dim, static_cast<unsigned>(B));
+    if (head_dim == 256)
+      conv_bwd_run_k<4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
+                                                  (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
+    else
+      conv_bwd_run_k<2><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
+                                                  (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   if (head_dim == 256) rc = launch_bwd<8, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
   else if (head_dim == 128) rc = launch_bwd<4, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
   else if (head_dim == 64) rc = launch_bwd<2, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
