@@ -185,9 +185,10 @@ def _conv_ref(x, w, hd, l2):
 
 
 @pytest.mark.parametrize("l2", [True, False])
-def test_conv_silu(l2):
+@pytest.mark.parametrize("L,hd", [(150, 256), (67, 128), (5, 256), (300, 64)])
+def test_conv_silu(l2, L, hd):
     from vagus_b200.ops import native
-    B, L, D, K, hd = 2, 150, 512, 4, 256
+    B, D, K = 2, 512, 4
     big = torch.randn(B, L, 3 * D, device=DEV).bfloat16()
     x = big[:, :, D:2 * D]
     w = 0.3 * torch.randn(D, 1, K, device=DEV)

@@ -351,7 +351,7 @@ conv_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict
 //             warps) and SiLU;  dw[k] += du(t) x[t-3+k] for the run's own
 //             tokens;  dx[t-3] = sum_i w[3-i] du(t-3+i) is then complete.
 // The run reads x and dy straight from global memory (each warp pair's row is
-// one contiguous 2 * HD-byte segment), with the next two tokens' loads in
+// one contiguous 2 * HD-byte segment), with the next four tokens' loads in
 // flight; its K - 1 right-context tokens are recomputed (3 / RW extra work).
 // No shared-memory staging, no block-wide barriers: the cost per element is
 // the arithmetic of the chain rule.  dw is summed over the CTA's pairs in
@@ -426,77 +426,85 @@ conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __rest
     for (int i = 0; i < K - 1; ++i)
 #pragma unroll
       for (int j = 0; j < VEC; ++j) dw3[i][j] = 0.f;
-    // two tokens of loads in flight
-    uint32_t qx[2][VEC / 2], qg[2][VEC / 2];
-#pragma unroll
-    for (int p = 0; p < 2; ++p) {
-      const long long t = t0 + p;
-      ldg_row<VEC>(xb + t * ldx, t < L, qx[p]);
-      ldg_row<VEC>(gb + t * D, t < L, qg[p]);
-    }
+    // PF tokens of loads in flight in a register queue (slot 0 = token t)
+    constexpr int PF = 4;
+    uint32_t qx[PF][VEC / 2], qg[PF][VEC / 2];
     const long long t_last = min(L, t0 + RUN + K - 1);   // du needed up to here (exclusive)
+#pragma unroll
+    for (int p = 0; p < PF; ++p) {
+      const long long t = t0 + p;
+      ldg_row<VEC>(xb + t * ldx, t < t_last, qx[p]);
+      ldg_row<VEC>(gb + t * D, t < t_last, qg[p]);
+    }
+    const __nv_bfloat16* nx = xb + (t0 + PF) * ldx;       // the next token to fetch
+    const __nv_bfloat16* ng = gb + (t0 + PF) * D;
     for (long long t = t0; t < t_last; ++t) {
-      float xc[VEC], g[VEC];
-      unpack_row<VEC>(qx[0], xc);
-      unpack_row<VEC>(qg[0], g);
-#pragma unroll
-      for (int j = 0; j < VEC / 2; ++j) { qx[0][j] = qx[1][j]; qg[0][j] = qg[1][j]; }
       {
-        const long long tn = t + 2;
-        const bool ok = tn < t_last;
-        ldg_row<VEC>(xb + tn * ldx, ok, qx[1]);
-        ldg_row<VEC>(gb + tn * D, ok, qg[1]);
-      }
-      float u[VEC], sg[VEC], z[VEC];
-      float dot = 0.f;
+        float xc[VEC], g[VEC];
+        unpack_row<VEC>(qx[0], xc);
+        unpack_row<VEC>(qg[0], g);
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        u[j] = wr[3][j] * xc[j] + wr[2][j] * xw[0][j] + wr[1][j] * xw[1][j] + wr[0][j] * xw[2][j];
-        sg[j] = sigmoid_f(u[j]);
-        z[j] = u[j] * sg[j];
-        dot += g[j] * z[j];
-      }
-      if (l2) {
-        dot = warp_sum(dot);
-        const int par = static_cast<int>(t & 1);
-        if (lane == 0) dot_x[pair][half][par] = dot;
-        asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
-        dot += dot_x[pair][half ^ 1][par];
-        const float rn = rnorm[(b * L + t) * nH + head];
-        const float c3 = rn * rn * rn * dot;
+        for (int p = 0; p + 1 < PF; ++p)
 #pragma unroll
-        for (int j = 0; j < VEC; ++j) g[j] = rn * g[j] - c3 * z[j];
-      }
-      float du[VEC];
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) du[j] = g[j] * sg[j] * (1.f + u[j] * (1.f - sg[j]));
-      if (t < t_end) {                                    // the run's own token: weight gradient
+          for (int j = 0; j < VEC / 2; ++j) { qx[p][j] = qx[p + 1][j]; qg[p][j] = qg[p + 1][j]; }
+        {
+          const bool ok = t + PF < t_last;
+          ldg_row<VEC>(nx, ok, qx[PF - 1]);
+          ldg_row<VEC>(ng, ok, qg[PF - 1]);
+          nx += ldx;
+          ng += D;
+        }
+        float u[VEC], sg[VEC], z[VEC];
+        float dot = 0.f;
 #pragma unroll
         for (int j = 0; j < VEC; ++j) {
-          dwa[0][j] += du[j] * xw[2][j];
-          dwa[1][j] += du[j] * xw[1][j];
-          dwa[2][j] += du[j] * xw[0][j];
-          dwa[3][j] += du[j] * xc[j];
+          u[j] = wr[3][j] * xc[j] + wr[2][j] * xw[0][j] + wr[1][j] * xw[1][j] + wr[0][j] * xw[2][j];
+          sg[j] = sigmoid_f(u[j]);
+          z[j] = u[j] * sg[j];
+          dot += g[j] * z[j];
         }
-      }
-      const long long s = t - (K - 1);                    // dx[s] needs du(s .. s + 3)
-      if (s >= t0) {
-        float o[VEC];
+        if (l2) {
+          const float rn = rnorm[(b * L + t) * nH + head];
+          dot = warp_sum(dot);
+          const int par = static_cast<int>(t & 1);
+          if (lane == 0) dot_x[pair][half][par] = dot;
+          asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
+          dot += dot_x[pair][half ^ 1][par];
+          const float c3 = rn * rn * rn * dot;
 #pragma unroll
-        for (int j = 0; j < VEC; ++j)
-          o[j] = wr[3][j] * dw3[2][j] + wr[2][j] * dw3[1][j] + wr[1][j] * dw3[0][j] + wr[0][j] * du[j];
-        if (VAGUS_CHECK((b * L + s) * lddx + c0 + VEC - 1, (long long)gridDim.z * L * lddx)) {
-          __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
-          if constexpr (VEC == 4)
-            *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
-          else
-            *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
+          for (int j = 0; j < VEC; ++j) g[j] = rn * g[j] - c3 * z[j];
         }
-      }
+        float du[VEC];
 #pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        xw[2][j] = xw[1][j]; xw[1][j] = xw[0][j]; xw[0][j] = xc[j];
-        dw3[2][j] = dw3[1][j]; dw3[1][j] = dw3[0][j]; dw3[0][j] = du[j];
+        for (int j = 0; j < VEC; ++j) du[j] = g[j] * sg[j] * (1.f + u[j] * (1.f - sg[j]));
+        if (t < t_end) {                                  // the run's own token: weight gradient
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) {
+            dwa[0][j] += du[j] * xw[2][j];
+            dwa[1][j] += du[j] * xw[1][j];
+            dwa[2][j] += du[j] * xw[0][j];
+            dwa[3][j] += du[j] * xc[j];
+          }
+        }
+        const long long s = t - (K - 1);                  // dx[s] needs du(s .. s + 3)
+        if (s >= t0) {
+          float o[VEC];
+#pragma unroll
+          for (int j = 0; j < VEC; ++j)
+            o[j] = wr[3][j] * dw3[2][j] + wr[2][j] * dw3[1][j] + wr[1][j] * dw3[0][j] + wr[0][j] * du[j];
+          if (VAGUS_CHECK((b * L + s) * lddx + c0 + VEC - 1, (long long)gridDim.z * L * lddx)) {
+            __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
+            if constexpr (VEC == 4)
+              *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+            else
+              *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          xw[2][j] = xw[1][j]; xw[1][j] = xw[0][j]; xw[0][j] = xc[j];
+          dw3[2][j] = dw3[1][j]; dw3[1][j] = dw3[0][j]; dw3[0][j] = du[j];
+        }
       }
     }
     // tokens past the end of the sequence have du = 0 (dy is zero there):
@@ -595,8 +603,8 @@ int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w,
       lddx % 8)
     return 5;
   int rc = 5;
-  static const bool old_bwd = std::getenv("VAGUS_CONV_STAGED_BWD") != nullptr;
-  if ((head_dim == 256 || head_dim == 128) && !old_bwd) {
+  static const bool staged = std::getenv("VAGUS_CONV_STAGED") != nullptr;
+  if ((head_dim == 256 || head_dim == 128) && !staged) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
