@@ -283,6 +283,34 @@ def test_kda_chunk_fwd_bwd(dk, dv, L):
         assert rel(a.grad, b.grad) < 5e-2, (name, rel(a.grad, b.grad))
 
 
+@pytest.mark.parametrize("dv", [128, 256])
+def test_kda_intra_kernels_match_fp32_oracle(dv):
+    """The fused KDA intra-chunk kernels (per-channel cumulative decay, gated
+    products, WY transform; and their backward) against the torch intra stage
+    run in fp32 on the CPU (plain gated products and triangular solve)."""
+    from vagus_b200.ops import native
+    from vagus_b200.ops.kda import kda_intra
+    B, L, H, dk = 2, 192, 2, 128
+    q, k, v, _, beta = _gdr_inputs(B, L, H, dk, dv)
+    g = F.logsigmoid(torch.randn(B, L, H, dk, device=DEV) + 2) * 0.5
+    q, k, v = (t.bfloat16() for t in (q, k, v))
+    scale = dk ** -0.5
+    outs = native().kda_intra_fwd(q, k, v, g.contiguous(), beta.contiguous(), scale)
+    ins = [t.float().cpu().requires_grad_(True) for t in (q, k, v, g, beta)]
+    ref = kda_intra(*ins, scale)
+    for name, a, r in zip(("W", "Qh", "Kt", "A", "U", "gC"), outs, ref):
+        assert rel(a.float().cpu().view(r.shape), r.detach()) < 1e-2, (name, rel(a.float().cpu().view(r.shape), r))
+    gen = torch.Generator().manual_seed(3)
+    ups = [torch.randn(r.shape, generator=gen).bfloat16().float() for r in ref]
+    sum(((r * u).sum() for r, u in zip(ref, ups))).backward()
+    flat = lambda t: t.reshape(B * H, L // 64, *t.shape[3:]).contiguous().to(DEV)   # noqa: E731
+    dW, dQh, dKt, dA, dU, dgC = (flat(u) for u in ups)
+    grads = native().kda_intra_bwd(q, k, v, g.contiguous(), beta.contiguous(), dW.bfloat16(), dQh.bfloat16(),
+                                   dKt.bfloat16(), dA, dU.bfloat16(), dgC, scale)
+    for name, a, r in zip(("dq", "dk", "dv", "dg", "dbeta"), grads, ins):
+        assert rel(a.float().cpu(), r.grad) < 2e-2, (name, rel(a.float().cpu(), r.grad))
+
+
 def test_asymmetric_write_chunk_fwd_bwd():
     """An explicit write vector (the Kalman diagonal gain's asymmetric write)
     on the recurrence kernels vs the fp32 chunk oracle, incl. gradients."""

@@ -10,7 +10,8 @@ public ``train()`` entry point, and the collectives under host skew.
   racing into the next step's collectives), writes a permanent checkpoint at
   step 3, finishes, and a second run resumed from that checkpoint ends where
   the straight run ended.  The weight-gradient GEMMs accumulate with atomics,
-  so the two runs agree to a tolerance, not bit for bit.
+  so runs agree to a tolerance, not bit for bit: the resumed run must sit as
+  close to the straight run as a second straight run does.
 
 Reference behaviour: ``infra/train/main.py:714-723`` (rank 0 writes, NCCL
 waits for it)."""
@@ -139,6 +140,7 @@ def _train_worker(rank, port, tmp, q):
 
         tm._write_checkpoint = slow_write
         tm.train(_train_cfg(tmp, "a", 6, recent_minutes=0.0), teardown=False)
+        tm.train(_train_cfg(tmp, "a2", 6, recent_minutes=1e9), teardown=False)
         if rank == 0:
             os.makedirs(os.path.join(tmp, "b"))
             shutil.copy(os.path.join(tmp, "a", "ckpt-00000003.pt"), os.path.join(tmp, "b", "ckpt-00000003.pt"))
@@ -164,8 +166,11 @@ def test_train_nvlink_fsdp_slow_checkpoint_and_resume(tmp_path):
     assert results[0]["slow_write_done"]
     assert (tmp_path / "a" / "recent.pt").exists()
     a = torch.load(tmp_path / "a" / "ckpt-00000006.pt", weights_only=False)
+    a2 = torch.load(tmp_path / "a2" / "ckpt-00000006.pt", weights_only=False)
     b = torch.load(tmp_path / "b" / "ckpt-00000006.pt", weights_only=False)
     assert a["step"] == b["step"] == 6 and a["tokens_seen"] == b["tokens_seen"]
     for k in a["model"]:
-        x, y = a["model"][k].float(), b["model"][k].float()
-        assert (x - y).norm() <= 1e-2 * max(1e-3, x.norm().item()), k
+        # the resumed run is as close to the straight run as a second straight run is
+        x, x2, y = (t["model"][k].float() for t in (a, a2, b))
+        noise = (x - x2).norm().item()
+        assert (x - y).norm() <= 3 * noise + 1e-3 * max(1e-3, x.norm().item()), (k, (x - y).norm().item(), noise)

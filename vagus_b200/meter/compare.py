@@ -20,8 +20,7 @@ from typing import Any, Callable, Iterator, Optional
 
 import torch
 
-from ..utils import infer_device
-from .core import BenchResult, bench, fmt_bytes, format_table
+from .core import BenchResult, bench, fmt_bytes, format_table, timing_device
 
 
 @dataclass
@@ -70,14 +69,14 @@ def agreement(out: Any, ref: Any) -> Optional[Agreement]:
 
 def compare(variants: dict[str, Callable], args: tuple = (), kwargs: Optional[dict] = None, *,
             ref: Optional[str] = None, warmup: int = 10, iters: int = 50, check: bool = True,
-            verbose: bool = True) -> dict[str, BenchResult]:
+            verbose: bool = True, device: Optional[torch.device] = None) -> dict[str, BenchResult]:
     """Time every variant on ``args`` / ``kwargs`` and (``check``) compare
     its output with variant ``ref`` (default: the first).  Returns
     ``{name: BenchResult}``; each result carries ``.vs_ref`` (an
     ``Agreement`` or None)."""
     kwargs = kwargs or {}
     ref = ref or next(iter(variants))
-    device = infer_device(args, kwargs)
+    device = device or timing_device(args, kwargs)
     results: dict[str, BenchResult] = {}
     outputs: dict[str, Any] = {}
     for name, fn in variants.items():

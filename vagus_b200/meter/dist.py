@@ -22,8 +22,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-from ..utils import infer_device
-from .core import BenchResult, bench, format_table
+from .core import BenchResult, bench, format_table, timing_device
 
 
 def _barrier(device: torch.device) -> None:
@@ -40,7 +39,7 @@ def dist_bench(fn: Callable, args: tuple = (), kwargs: Optional[dict] = None, *,
     group."""
     assert dist.is_initialized(), "init_process_group first"
     rank, world = dist.get_rank(), dist.get_world_size()
-    device = infer_device(args, kwargs or {})
+    device = timing_device(args, kwargs or {})
     _barrier(device)                     # a late starter must not read as a straggler
     res = bench(fn, args, kwargs, name=name, device=device, warmup=warmup, iters=iters)
     # fixed-size exchange: [failed flag, mean, std, min, max, first, peak, iters samples]

@@ -18,8 +18,7 @@ from typing import Callable, Optional
 
 from torch.profiler import ProfilerActivity, profile
 
-from ..utils import infer_device
-from .core import format_table, synchronize
+from .core import format_table, synchronize, timing_device
 
 # kernel-name families, first match wins
 FAMILIES = [
@@ -92,7 +91,7 @@ def profile_variants(variants: dict[str, Callable], args: tuple = (), kwargs: Op
     ``{name: trace path}`` (a variant that raises is reported and skipped).
     ``device``: where the variants run when no argument tells (closures)."""
     kwargs = kwargs or {}
-    device = device if device is not None else infer_device(args, kwargs)
+    device = device if device is not None else timing_device(args, kwargs)
     cuda = device.type == "cuda"
     activities = [ProfilerActivity.CPU] + ([ProfilerActivity.CUDA] if cuda else [])
     out = pathlib.Path(out_dir)

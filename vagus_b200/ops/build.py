@@ -30,7 +30,7 @@ BUILD_DIR = HERE / ("_build_bounds" if BOUNDS_CHECK else "_build")
 SOURCES = [
     "bindings.cpp", "bind_seq.cpp", "bind_attn.cpp", "bind_comm.cpp",
     "gemm.cu", "norm.cu", "elementwise.cu", "conv.cu", "gdn_gates.cu", "gdr.cu", "gdr_intra.cu", "attention.cu",
-    "comm.cu", "ce_noalloc.cu", "kda.cu", "mobius.cu",
+    "comm.cu", "ce_noalloc.cu", "kda.cu", "kda_intra.cu", "mobius.cu",
 ]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CUDA_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",

@@ -234,6 +234,66 @@ std::vector<Tensor> kda_gated_bwd(Tensor Q, Tensor K, Tensor G, Tensor dAqk, Ten
   return {dQ, dK, dG};
 }
 
+// Per-channel-gate intra-chunk stage (kda_intra.cu).  q, k (B, L, H, DK), v
+// (B, L, H, DV) bf16; g (B, L, H, DK), beta (B, L, H) fp32; L a multiple of 64.
+// -> (W, Qh, Kt, A, U, gC), chunk-major (B * H, N, 64, .).
+std::vector<Tensor> kda_intra_fwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, double scale) {
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous() && g.is_contiguous() &&
+                  beta.is_contiguous() && q.scalar_type() == at::kBFloat16 && g.scalar_type() == at::kFloat &&
+                  beta.scalar_type() == at::kFloat,
+              "kda_intra_fwd: contiguous bf16 q / k / v, fp32 g / beta");
+  const int B = q.size(0), L = q.size(1), H = q.size(2), DK = q.size(3), DV = v.size(3);
+  TORCH_CHECK(L % 64 == 0 && k.sizes() == q.sizes() && g.sizes() == q.sizes() && v.size(1) == L &&
+                  beta.numel() == (long long)B * L * H,
+              "kda_intra_fwd: q / k / g (B, L, H, dk), v (B, L, H, dv), beta (B, L, H), L a multiple of 64");
+  const int N = L / 64;
+  auto bf = q.options();
+  auto W = torch::empty({B * H, N, 64, DK}, bf), Qh = torch::empty_like(W), Kt = torch::empty_like(W);
+  auto A = torch::empty({B * H, N, 64, 64}, bf), U = torch::empty({B * H, N, 64, DV}, bf);
+  auto gC = torch::empty({B * H, N, DK}, g.options());
+  check(vagus::kda_intra_fwd(q.data_ptr(), k.data_ptr(), v.data_ptr(), g.data_ptr<float>(), beta.data_ptr<float>(),
+                             W.data_ptr(), Qh.data_ptr(), Kt.data_ptr(), A.data_ptr(), U.data_ptr(),
+                             gC.data_ptr<float>(), B, L, H, DK, DV, static_cast<float>(scale), stream()),
+        "kda_intra_fwd");
+  return {W, Qh, Kt, A, U, gC};
+}
+
+// -> (dq, dk, dv, dg, dbeta), token-major like the inputs.
+std::vector<Tensor> kda_intra_bwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor dW, Tensor dQh,
+                                  Tensor dKt, Tensor dA, Tensor dU, Tensor dgC, double scale) {
+  dW = dW.contiguous(); dQh = dQh.contiguous(); dKt = dKt.contiguous(); dU = dU.contiguous();
+  dA = dA.contiguous().to(at::kFloat);
+  dgC = dgC.contiguous().to(at::kFloat);
+  TORCH_CHECK(dW.scalar_type() == at::kBFloat16 && dQh.scalar_type() == at::kBFloat16 &&
+                  dKt.scalar_type() == at::kBFloat16 && dU.scalar_type() == at::kBFloat16,
+              "kda_intra_bwd: bf16 dW / dQh / dKt / dU");
+  const int B = q.size(0), L = q.size(1), H = q.size(2), DK = q.size(3), DV = v.size(3);
+  TORCH_CHECK(L % 64 == 0 && dW.numel() == q.numel() && dQh.numel() == q.numel() && dKt.numel() == q.numel() &&
+                  dU.numel() == v.numel() && dA.numel() == (long long)B * H * L * 64 &&
+                  dgC.numel() == (long long)B * H * (L / 64) * DK,
+              "kda_intra_bwd: gradient shapes do not match the forward's outputs");
+  const long long chunks = (long long)B * H * (L / 64);
+  auto f32 = g.options();
+  auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
+  auto dg = torch::empty_like(g), dbeta = torch::empty_like(beta);
+  auto work = torch::empty({9, chunks, 64, DK}, f32);
+  auto dAw = torch::empty({2, chunks, 64, 64}, f32);
+  vagus::KdaIntraBwdArgs a;
+  a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.g = g.data_ptr<float>();
+  a.beta = beta.data_ptr<float>(); a.dW = dW.data_ptr(); a.dQh = dQh.data_ptr(); a.dKt = dKt.data_ptr();
+  a.dU = dU.data_ptr(); a.dA = dA.data_ptr<float>(); a.dgC = dgC.data_ptr<float>();
+  a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr(); a.dg = dg.data_ptr<float>();
+  a.dbeta = dbeta.data_ptr<float>();
+  float* w = work.data_ptr<float>();
+  const long long slab = chunks * 64 * DK;
+  a.Qf = w; a.Kf = w + slab; a.Gf = w + 2 * slab; a.dQe = w + 3 * slab; a.dKe = w + 4 * slab; a.dGe = w + 5 * slab;
+  a.dQg = w + 6 * slab; a.dKg = w + 7 * slab; a.dGg = w + 8 * slab;
+  a.dAqk = dAw.data_ptr<float>(); a.dAkk = a.dAqk + chunks * 64 * 64;
+  a.B = B; a.L = L; a.H = H; a.DK = DK; a.DV = DV; a.scale = static_cast<float>(scale);
+  check(vagus::kda_intra_bwd(a, stream()), "kda_intra_bwd");
+  return {dq, dk, dv, dg, dbeta};
+}
+
 // Mobius-map scan (mobius.cu).  A, B, C, D: (batch, L, R) fp32; x0: (batch, R).
 Tensor mobius_fwd(Tensor A, Tensor B, Tensor C, Tensor D, Tensor x0) {
   for (auto* t : {&A, &B, &C, &D})
@@ -283,4 +343,6 @@ void register_seq_ops(pybind11::module& m) {
   m.def("gdr_decode", &gdr_decode);
   m.def("gdr_intra_fwd", &gdr_intra_fwd);
   m.def("gdr_intra_bwd", &gdr_intra_bwd);
+  m.def("kda_intra_fwd", &kda_intra_fwd);
+  m.def("kda_intra_bwd", &kda_intra_bwd);
 }

@@ -1,0 +1,588 @@
+// Intra-chunk stage of the chunked delta rule with a per-channel (Kimi-delta,
+// KDA) gate, forward and backward, one CTA per (batch, head, 64-token chunk).
+//
+// With gamma the in-chunk cumulative log decay of every key channel
+// (gamma_ic = sum_{t <= i} g_tc, non-increasing in i) and G = exp(gamma), the
+// gated inner products
+//     <X_i, Y_j>_g = sum_c X_ic Y_jc exp(gamma_ic - gamma_jc)        (j <= i)
+// give  Akk = strict_lower(<K, K>_g),  Aqk = lower(<Q, K>_g),  and
+//     M  = diag(b) Akk,   T = (I + M)^{-1}
+//     W  = T diag(b) (K o G)          U  = T diag(b) V
+//     Qh = s Q o G    Kt = K o exp(gamma_C - gamma)    A = s Aqk    gC = exp(gamma_C)
+// which the recurrence kernels (gdr.cu, per-channel decay) consume.
+//
+// The gated products are formed without the overflow of exp(+gamma) that
+// factorising exp(gamma_i - gamma_j) through the chunk start would hit for
+// fast channels: the chunk is cut into four 16-token blocks;
+//   * for a block pair I > J the decay factorises through r_J = gamma at the
+//     last token of block J:  exp(gamma_i - gamma_j) = exp(gamma_i - r_J)
+//     exp(r_J - gamma_j), both factors <= 1, so
+//     <X, K>_g over (I, J) = (X_I o exp(gamma_I - r_J)) (K_J o exp(r_J - gamma_J))^T,
+//     a 16 x 16 x dk product on the tensor cores (mma.sync, bf16 operands);
+//   * inside a block the decay is taken elementwise (fp32).
+// The backward uses the same split: for I > J with P = X_I o exp(gamma_I - r_J)
+// and R = K_J o exp(r_J - gamma_J), dP = dA R and dR = dA^T P are tensor-core
+// products, and the r_J terms of the chain rule cancel exactly (the product
+// does not depend on r_J), so gamma receives dP o P on block I and -dR o R on
+// block J; inside a block the elementwise terms.  The WY part is the scalar
+// gate's (gdr_intra.cu) with G per channel.
+//
+// Token-major inputs: q, k (B, L, H, DK), v (B, L, H, DV) bf16; g (B, L, H, DK)
+// and beta (B, L, H) fp32.  Chunk-major outputs (BH, N, C, .) as the
+// recurrence kernels expect.  Reference behaviour: fla chunk_kda's intra-chunk
+// stage (the oracle is models/scans.py chunk_scan_vec).
+#include "common.cuh"
+#include "kernels.h"
+#include "mma.cuh"
+#include "tri_inverse.cuh"
+
+namespace vagus {
+namespace {
+
+using namespace mma;
+using wy::tri_inverse_inplace;
+
+constexpr int C = 64;
+constexpr int BLK = 16;
+constexpr int THREADS = 256;
+
+template <int DK, int DV>
+struct KdaFwdSmem {
+  __nv_bfloat16 Q[C][DK + PAD];
+  __nv_bfloat16 K[C][DK + PAD];          // K, then diag(b) (K o G)
+  float gam[C][DK];                      // cumulative log decay per channel
+  __nv_bfloat16 R[BLK][DK + PAD];        // K_J o exp(r_J - gamma_J)
+  __nv_bfloat16 P[6][BLK][DK + PAD];     // Q_I / K_I o exp(gamma_I - r_J), I = J+1..3
+  float Aqk[C][C + 1];
+  float M[C][C + 1];                     // Akk, then M = diag(b) Akk, then T (in place)
+  __nv_bfloat16 Tb[C][C + PAD];
+  __nv_bfloat16 V[C][DV + PAD];          // V, then diag(b) V
+  float beta[C];
+};
+
+// g (token-major, this chunk's rows) -> gam = per-channel inclusive prefix sum
+template <int DK>
+__device__ __forceinline__ void load_cumsum(float (*gam)[DK], const float* g, long long gld) {
+  for (int idx = threadIdx.x; idx < C * DK / 4; idx += THREADS) {
+    const int i = idx / (DK / 4), c = (idx % (DK / 4)) * 4;
+    *reinterpret_cast<float4*>(&gam[i][c]) = *reinterpret_cast<const float4*>(g + i * gld + c);
+  }
+  __syncthreads();
+  for (int c = threadIdx.x; c < DK; c += THREADS) {
+    float s = 0.f;
+    for (int i = 0; i < C; ++i) {
+      s += gam[i][c];
+      gam[i][c] = s;
+    }
+  }
+  __syncthreads();
+}
+
+// Shared-memory operands of the gated products.
+template <int DK>
+struct GatedView {
+  __nv_bfloat16 (*Q)[DK + PAD];
+  __nv_bfloat16 (*K)[DK + PAD];
+  float (*gam)[DK];
+  __nv_bfloat16 (*R)[DK + PAD];          // [BLK] rows
+  __nv_bfloat16 (*P)[BLK][DK + PAD];     // [6] tiles
+  float (*Aqk)[C + 1];
+  float (*M)[C + 1];
+};
+
+// The gated products of the chunk into Aqk (lower, diagonal included) and
+// Akk (strictly lower, into M), both zero above.
+template <int DK>
+__device__ __forceinline__ void gated_products(const GatedView<DK>& sm) {
+  const int warp = threadIdx.x >> 5;
+  for (int idx = threadIdx.x; idx < C * C; idx += THREADS) {
+    sm.Aqk[idx / C][idx % C] = 0.f;
+    sm.M[idx / C][idx % C] = 0.f;
+  }
+  __syncthreads();
+  // inside the 16-token blocks: elementwise decay
+  for (int it = threadIdx.x; it < 4 * BLK * BLK; it += THREADS) {
+    const int blk = it / (BLK * BLK), i = (it / BLK) % BLK, j = it % BLK;
+    if (j > i) continue;
+    const int ri = blk * BLK + i, rj = blk * BLK + j;
+    float aq = 0.f, ak = 0.f;
+#pragma unroll 4
+    for (int c = 0; c < DK; c += 2) {
+      const float2 qi = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[ri][c]));
+      const float2 ki = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[ri][c]));
+      const float2 kj = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[rj][c]));
+      const float2 gi = *reinterpret_cast<const float2*>(&sm.gam[ri][c]);
+      const float2 gj = *reinterpret_cast<const float2*>(&sm.gam[rj][c]);
+      const float e0 = __expf(gi.x - gj.x) * kj.x, e1 = __expf(gi.y - gj.y) * kj.y;
+      aq = fmaf(qi.x, e0, fmaf(qi.y, e1, aq));
+      ak = fmaf(ki.x, e0, fmaf(ki.y, e1, ak));
+    }
+    sm.Aqk[ri][rj] = aq;
+    if (j < i) sm.M[ri][rj] = ak;
+  }
+  // across blocks: factorised through r_J, on the tensor cores
+  for (int J = 0; J < 3; ++J) {
+    __syncthreads();                                   // P / R free
+    const int rJ = J * BLK + BLK - 1;
+    for (int idx = threadIdx.x; idx < BLK * DK; idx += THREADS) {
+      const int j = idx / DK, c = idx % DK;
+      sm.R[j][c] = f2bf(bf2f(sm.K[J * BLK + j][c]) * __expf(sm.gam[rJ][c] - sm.gam[J * BLK + j][c]));
+    }
+    const int nI = 3 - J;
+    for (int idx = threadIdx.x; idx < nI * BLK * DK; idx += THREADS) {
+      const int t = idx / (BLK * DK), i = (idx / DK) % BLK, c = idx % DK;
+      const int row = (J + 1 + t) * BLK + i;
+      const float a = __expf(sm.gam[row][c] - sm.gam[rJ][c]);
+      sm.P[2 * t][i][c] = f2bf(bf2f(sm.Q[row][c]) * a);
+      sm.P[2 * t + 1][i][c] = f2bf(bf2f(sm.K[row][c]) * a);
+    }
+    __syncthreads();
+    if (warp < 2 * nI) {
+      const int t = warp >> 1, isk = warp & 1;
+      float acc[1][2][4];
+      zero(acc);
+      warp_mma<1, 2, false, false>(acc, &sm.P[warp][0][0], DK + PAD, &sm.R[0][0], DK + PAD, 0, 0, DK);
+      float (*dst)[C + 1] = isk ? sm.M : sm.Aqk;
+      const int I = J + 1 + t;
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dst[I * BLK + frag_row(0, e)][J * BLK + frag_col(nt, e)] = acc[0][nt][e];
+    }
+  }
+  __syncthreads();
+}
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(THREADS, 1)
+kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                     const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
+                     const float* __restrict__ beta, __nv_bfloat16* __restrict__ Wo, __nv_bfloat16* __restrict__ Qho,
+                     __nv_bfloat16* __restrict__ Kto, __nv_bfloat16* __restrict__ Ao, __nv_bfloat16* __restrict__ Uo,
+                     float* __restrict__ gCo, int L, int H, float scale) {
+  using S = KdaFwdSmem<DK, DV>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int N = gridDim.x;
+  const long long cidx = ((long long)b * H + h) * N + n;
+  const long long tok0 = (long long)b * L + (long long)n * C;
+  const int warp = threadIdx.x >> 5;
+  load_tile(&sm.Q[0][0], DK + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  load_tile(&sm.V[0][0], DV + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
+  cp_commit();
+  if (threadIdx.x < C) sm.beta[threadIdx.x] = beta[(tok0 + threadIdx.x) * H + h];
+  load_cumsum<DK>(sm.gam, g + (tok0 * H + h) * DK, (long long)H * DK);
+  cp_wait_all();
+  __syncthreads();
+  gated_products<DK>(GatedView<DK>{sm.Q, sm.K, sm.gam, sm.R, sm.P, sm.Aqk, sm.M});
+
+  // A = s Aqk; M = diag(b) Akk -> T
+  for (int idx = threadIdx.x; idx < C * C / 2; idx += THREADS) {
+    const int i = idx / (C / 2), j = (idx % (C / 2)) * 2;
+    *reinterpret_cast<uint32_t*>(Ao + (cidx * C + i) * C + j) = pack_bf16x2(scale * sm.Aqk[i][j], scale * sm.Aqk[i][j + 1]);
+    sm.M[i][j] *= sm.beta[i];
+    sm.M[i][j + 1] *= sm.beta[i];
+  }
+  __syncthreads();
+  tri_inverse_inplace(sm.M);
+  for (int idx = threadIdx.x; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.M[idx / C][idx % C]);
+
+  // Qh, Kt, gC out; K -> diag(b) (K o G); V -> diag(b) V
+  for (int idx = threadIdx.x; idx < C * DK / 2; idx += THREADS) {
+    const int i = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
+    const float2 gi = *reinterpret_cast<const float2*>(&sm.gam[i][c]);
+    const float2 gl = *reinterpret_cast<const float2*>(&sm.gam[C - 1][c]);
+    const float2 qv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[i][c]));
+    const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
+    const float G0 = __expf(gi.x), G1 = __expf(gi.y);
+    *reinterpret_cast<uint32_t*>(Qho + (cidx * C + i) * DK + c) = pack_bf16x2(scale * qv.x * G0, scale * qv.y * G1);
+    *reinterpret_cast<uint32_t*>(Kto + (cidx * C + i) * DK + c) =
+        pack_bf16x2(kv.x * __expf(gl.x - gi.x), kv.y * __expf(gl.y - gi.y));
+    const float bi = sm.beta[i];
+    *reinterpret_cast<uint32_t*>(&sm.K[i][c]) = pack_bf16x2(bi * kv.x * G0, bi * kv.y * G1);
+    if (i == C - 1) { gCo[cidx * DK + c] = G0; gCo[cidx * DK + c + 1] = G1; }
+  }
+  for (int idx = threadIdx.x; idx < C * DV / 2; idx += THREADS) {
+    const int i = idx / (DV / 2), c = (idx % (DV / 2)) * 2;
+    const float2 vv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.V[i][c]));
+    *reinterpret_cast<uint32_t*>(&sm.V[i][c]) = pack_bf16x2(sm.beta[i] * vv.x, sm.beta[i] * vv.y);
+  }
+  __syncthreads();
+
+  // W = T Xw, U = T Xu: warp tile 16 rows x half of the columns
+  const int m0 = (warp & 3) * 16;
+  {
+    constexpr int NT = DK / 16;
+    float acc[1][NT][4];
+    zero(acc);
+    const int c0 = (warp >> 2) * (DK / 2);
+    warp_mma<1, NT, false, true>(acc, &sm.Tb[0][0], C + PAD, &sm.K[0][0], DK + PAD, m0, c0, C);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(Wo + (cidx * C + i) * DK + c) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
+      }
+  }
+  {
+    constexpr int NT = DV / 16;
+    float acc[1][NT][4];
+    zero(acc);
+    const int c0 = (warp >> 2) * (DV / 2);
+    warp_mma<1, NT, false, true>(acc, &sm.Tb[0][0], C + PAD, &sm.V[0][0], DV + PAD, m0, c0, C);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(Uo + (cidx * C + i) * DV + c) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
+      }
+  }
+}
+
+// ---------------------------------------------------------------- backward --
+// The backward is three kernels:
+//   kda_intra_bwd_kernel (below, one CTA per chunk): recomputes gamma, the
+//     gated products and T, runs the WY backward --
+//         dXw = T^T dW, dXu = T^T dU, dT = dW Xw^T + dU Xu^T,
+//         dM = -strict_lower(T^T dT T^T), dAkk = diag(b) dM, dAqk = s dA
+//     -- writes dv and dbeta, the elementwise parts of dq / dk / dgamma
+//         dq_e = s dQh o G,  dk_e = dKt o E + b dXw o G,
+//         dgamma_e = s dQh o Q o G - dKt o K o E + b dXw o K o G
+//                    (+ column sums of dKt o K o E and dgC o G_C on the last row)
+//     (E = exp(gamma_C - gamma)), and fp32 chunk-major Q, K, gamma, dAqk, dAkk;
+//   kda_gated_bwd (kda.cu): the gated products' gradients dQ_g, dK_g, dgamma_g;
+//   kda_finish_kernel: dq = dq_e + dQ_g, dk = dk_e + dK_g (bf16 token-major),
+//     dg = reverse cumsum over the chunk of dgamma_e + dgamma_g.
+template <int DK, int DV>
+struct KdaBwdSmem {
+  __nv_bfloat16 Q[C][DK + PAD];
+  __nv_bfloat16 K[C][DK + PAD];
+  float gam[C][DK];
+  // scratch: the gated products' R and P tiles, then XW = diag(b) (K o G)
+  // and the dW tile (later T^T dT, bf16 C x C)
+  static constexpr int PR_BYTES = (1 + 6) * BLK * (DK + PAD) * 2;
+  static constexpr int XD_BYTES = 2 * C * (DK + PAD) * 2;
+  __align__(16) unsigned char scratch[PR_BYTES > XD_BYTES ? PR_BYTES : XD_BYTES];
+  __device__ __nv_bfloat16 (*R())[DK + PAD] { return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch); }
+  __device__ __nv_bfloat16 (*P())[BLK][DK + PAD] {
+    return reinterpret_cast<__nv_bfloat16 (*)[BLK][DK + PAD]>(scratch + BLK * (DK + PAD) * 2);
+  }
+  __device__ __nv_bfloat16 (*XW())[DK + PAD] { return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch); }
+  __device__ __nv_bfloat16 (*DW())[DK + PAD] {
+    return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch + C * (DK + PAD) * 2);
+  }
+  float Aqk[C][C + 1];                   // products, then Akk kept for dbeta
+  float M[C][C + 1];                     // Akk -> M -> T
+  __nv_bfloat16 Tb[C][C + PAD];
+  __nv_bfloat16 V[C][DV + PAD];
+  __nv_bfloat16 DU[C][DV + PAD];
+  __nv_bfloat16 DT[C][C + PAD];
+  float beta[C];
+  float rw[C], ru[C], rm[C];
+  float colk[DK];                        // sum_i dKt o K o E per channel
+};
+
+// out[i] += sum over this warp's fragment columns of acc[i][c] * X[i][c] (bf16 X)
+template <int NT>
+__device__ __forceinline__ void frag_row_dot(const float (&acc)[1][NT][4], const __nv_bfloat16* X, int ldx, int m0,
+                                             int c0, float* out) {
+  float part[2] = {0.f, 0.f};
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+      part[e >> 1] += acc[0][nt][e] * bf2f(X[i * ldx + c]);
+    }
+#pragma unroll
+  for (int r = 0; r < 2; ++r) {
+    float sum = part[r];
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    if ((threadIdx.x & 3) == 0) atomicAdd(&out[m0 + ((threadIdx.x & 31) >> 2) + 8 * r], sum);
+  }
+}
+
+template <int DK, int DV>
+__global__ void __launch_bounds__(THREADS, 1)
+kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+                     const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
+                     const float* __restrict__ beta, const __nv_bfloat16* __restrict__ dW,
+                     const __nv_bfloat16* __restrict__ dQh, const __nv_bfloat16* __restrict__ dKt,
+                     const float* __restrict__ dA, const __nv_bfloat16* __restrict__ dU,
+                     const float* __restrict__ dgC, __nv_bfloat16* __restrict__ dv, float* __restrict__ dbeta,
+                     float* __restrict__ Qf, float* __restrict__ Kf, float* __restrict__ Gf,
+                     float* __restrict__ dAqk, float* __restrict__ dAkk, float* __restrict__ dQe,
+                     float* __restrict__ dKe, float* __restrict__ dGe, int L, int H, float scale) {
+  using S = KdaBwdSmem<DK, DV>;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  S& sm = *reinterpret_cast<S*>(smem_raw);
+  const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int N = gridDim.x;
+  const long long cidx = ((long long)b * H + h) * N + n;
+  const long long tok0 = (long long)b * L + (long long)n * C;
+  const int warp = threadIdx.x >> 5;
+  const int tid = threadIdx.x;
+  load_tile(&sm.Q[0][0], DK + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
+  load_tile(&sm.V[0][0], DV + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
+  load_tile(&sm.DU[0][0], DV + PAD, dU + cidx * C * DV, DV, C, DV);
+  cp_commit();
+  if (tid < C) {
+    sm.beta[tid] = beta[(tok0 + tid) * H + h];
+    sm.rw[tid] = sm.ru[tid] = sm.rm[tid] = 0.f;
+  }
+  for (int c = tid; c < DK; c += THREADS) sm.colk[c] = 0.f;
+  load_cumsum<DK>(sm.gam, g + (tok0 * H + h) * DK, (long long)H * DK);
+  cp_wait_all();
+  __syncthreads();
+  gated_products<DK>(GatedView<DK>{sm.Q, sm.K, sm.gam, sm.R(), sm.P(), sm.Aqk, sm.M});
+  __nv_bfloat16 (*XW)[DK + PAD] = sm.XW();
+  __nv_bfloat16 (*DWt)[DK + PAD] = sm.DW();
+
+  // fp32 copies for the gated-products backward; keep Akk; M = diag(b) Akk -> T
+  const long long cbase = cidx * C * DK;
+  for (int idx = tid; idx < C * DK; idx += THREADS) {
+    const int i = idx / DK, c = idx % DK;
+    Qf[cbase + idx] = bf2f(sm.Q[i][c]);
+    Kf[cbase + idx] = bf2f(sm.K[i][c]);
+    Gf[cbase + idx] = sm.gam[i][c];
+  }
+  for (int idx = tid; idx < C * C; idx += THREADS) {
+    const int i = idx / C, j = idx % C;
+    const float akk = sm.M[i][j];
+    sm.Aqk[i][j] = akk;
+    sm.M[i][j] = sm.beta[i] * akk;
+    dAqk[cidx * C * C + idx] = j <= i ? scale * dA[cidx * C * C + idx] : 0.f;
+  }
+  __syncthreads();
+  tri_inverse_inplace(sm.M);
+  for (int idx = tid; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.M[idx / C][idx % C]);
+  // XW = diag(b) (K o G); dW tile
+  for (int idx = tid; idx < C * DK / 2; idx += THREADS) {
+    const int i = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
+    const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
+    const float2 gi = *reinterpret_cast<const float2*>(&sm.gam[i][c]);
+    const float bi = sm.beta[i];
+    *reinterpret_cast<uint32_t*>(&XW[i][c]) = pack_bf16x2(bi * kv.x * __expf(gi.x), bi * kv.y * __expf(gi.y));
+  }
+  load_tile(&DWt[0][0], DK + PAD, dW + cbase, DK, C, DK);
+  cp_commit();
+  cp_wait_all();
+  __syncthreads();
+
+  const int m0 = (warp & 3) * 16;
+  {
+    // dXu = T^T dU  ->  dv = diag(b) dXu ; ru += dXu . V
+    constexpr int NT = DV / 16;
+    const int c0 = (warp >> 2) * (DV / 2);
+    float acc[1][NT][4];
+    zero(acc);
+    warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &sm.DU[0][0], DV + PAD, m0, c0, C);
+    frag_row_dot<NT>(acc, &sm.V[0][0], DV + PAD, m0, c0, sm.ru);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(dv + ((tok0 + i) * H + h) * DV + c) =
+            pack_bf16x2(sm.beta[i] * acc[0][nt][e], sm.beta[i] * acc[0][nt][e + 1]);
+      }
+  }
+  {
+    // dXw = T^T dW, and every elementwise term of (i, c) in the same pass
+    constexpr int NT = DK / 16;
+    const int c0 = (warp >> 2) * (DK / 2);
+    float acc[1][NT][4];
+    zero(acc);
+    warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &DWt[0][0], DK + PAD, m0, c0, C);
+    float part[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        const float gi = sm.gam[i][c], G = __expf(gi), E = __expf(sm.gam[C - 1][c] - gi);
+        const float qv = bf2f(sm.Q[i][c]), kv = bf2f(sm.K[i][c]);
+        const float dqh = bf2f(dQh[cbase + i * DK + c]), dkt = bf2f(dKt[cbase + i * DK + c]);
+        const float dxw = acc[0][nt][e], bi = sm.beta[i];
+        part[e >> 1] += dxw * kv * G;
+        const float kte = dkt * kv * E;
+        atomicAdd(&sm.colk[c], kte);
+        dQe[cbase + i * DK + c] = scale * dqh * G;
+        dKe[cbase + i * DK + c] = dkt * E + bi * dxw * G;
+        dGe[cbase + i * DK + c] = scale * dqh * qv * G - kte + bi * dxw * kv * G;
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float sum = part[r];
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if ((threadIdx.x & 3) == 0) atomicAdd(&sm.rw[m0 + ((threadIdx.x & 31) >> 2) + 8 * r], sum);
+    }
+  }
+  __syncthreads();
+  // dT = dW XW^T + (dU V^T) diag(b)  (bf16 into DT)
+  {
+    float a1[1][4][4], a2[1][4][4];
+    zero(a1);
+    zero(a2);
+    const int n0 = (warp >> 2) * 32;
+    warp_mma<1, 4, false, false>(a1, &DWt[0][0], DK + PAD, &XW[0][0], DK + PAD, m0, n0, DK);
+    warp_mma<1, 4, false, false>(a2, &sm.DU[0][0], DV + PAD, &sm.V[0][0], DV + PAD, m0, n0, DV);
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(&sm.DT[i][j]) =
+            pack_bf16x2(a1[0][nt][e] + sm.beta[j] * a2[0][nt][e], a1[0][nt][e + 1] + sm.beta[j + 1] * a2[0][nt][e + 1]);
+      }
+  }
+  __syncthreads();
+  // P = T^T dT (bf16, over the dW tile), dM = -strict_lower(P T^T)
+  __nv_bfloat16 (*Pb)[DK + PAD] = DWt;
+  {
+    float p[1][4][4];
+    zero(p);
+    const int n0 = (warp >> 2) * 32;
+    warp_mma<1, 4, true, true>(p, &sm.Tb[0][0], C + PAD, &sm.DT[0][0], C + PAD, m0, n0, C);
+    __syncthreads();                                       // dW tile consumed everywhere
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; e += 2) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+        *reinterpret_cast<uint32_t*>(&Pb[i][j]) = pack_bf16x2(p[0][nt][e], p[0][nt][e + 1]);
+      }
+  }
+  __syncthreads();
+  {
+    float dm[1][4][4];
+    zero(dm);
+    const int n0 = (warp >> 2) * 32;
+    warp_mma<1, 4, false, false>(dm, &Pb[0][0], DK + PAD, &sm.Tb[0][0], C + PAD, m0, n0, C);
+    float part[2] = {0.f, 0.f};
+#pragma unroll
+    for (int nt = 0; nt < 4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
+        const float dmv = j < i ? -dm[0][nt][e] : 0.f;
+        part[e >> 1] += dmv * sm.Aqk[i][j];
+        dAkk[cidx * C * C + i * C + j] = sm.beta[i] * dmv;
+      }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      float sum = part[r];
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if ((threadIdx.x & 3) == 0) atomicAdd(&sm.rm[m0 + ((threadIdx.x & 31) >> 2) + 8 * r], sum);
+    }
+  }
+  __syncthreads();
+  if (tid < C) dbeta[(tok0 + tid) * H + h] = sm.rw[tid] + sm.ru[tid] + sm.rm[tid];
+  // the last row's dgamma takes the column sums and dgC G_C
+  for (int c = tid; c < DK; c += THREADS) {
+    const float gl = __expf(sm.gam[C - 1][c]);
+    dGe[cbase + (C - 1) * DK + c] += sm.colk[c] + dgC[cidx * DK + c] * gl;
+  }
+}
+
+// dq, dk (bf16 token-major) = elementwise + gated parts; dg = reverse cumsum
+// over the chunk of dgamma (fp32 token-major); one thread per (chunk, channel)
+__global__ void kda_finish_kernel(const float* __restrict__ dQe, const float* __restrict__ dKe,
+                                  const float* __restrict__ dGe, const float* __restrict__ dQg,
+                                  const float* __restrict__ dKg, const float* __restrict__ dGg,
+                                  __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk,
+                                  float* __restrict__ dg, int L, int H, int N, int DK) {
+  const long long cidx = blockIdx.x;                        // (b * H + h) * N + n
+  const int c = threadIdx.x;
+  if (c >= DK) return;
+  const long long bh = cidx / N, n = cidx % N;
+  const long long b = bh / H, h = bh % H;
+  const long long tok0 = b * L + n * C;
+  const long long base = cidx * C * DK + c;
+  float run = 0.f;
+  for (int i = C - 1; i >= 0; --i) {
+    const long long o = base + (long long)i * DK;
+    const long long t = ((tok0 + i) * H + h) * DK + c;
+    run += dGe[o] + dGg[o];
+    dg[t] = run;
+    dq[t] = f2bf(dQe[o] + dQg[o]);
+    dk[t] = f2bf(dKe[o] + dKg[o]);
+  }
+}
+
+}  // namespace
+
+template <int DK, int DV>
+static int launch_kda_bwd(const KdaIntraBwdArgs& a, cudaStream_t st) {
+  const int smem = sizeof(KdaBwdSmem<DK, DV>);
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(kda_intra_bwd_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return 3;
+    attr[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>(a.L / C), static_cast<unsigned>(a.H), static_cast<unsigned>(a.B));
+  kda_intra_bwd_kernel<DK, DV><<<grid, THREADS, smem, st>>>(
+      (const __nv_bfloat16*)a.q, (const __nv_bfloat16*)a.k, (const __nv_bfloat16*)a.v, a.g, a.beta,
+      (const __nv_bfloat16*)a.dW, (const __nv_bfloat16*)a.dQh, (const __nv_bfloat16*)a.dKt, a.dA,
+      (const __nv_bfloat16*)a.dU, a.dgC, (__nv_bfloat16*)a.dv, a.dbeta, a.Qf, a.Kf, a.Gf, a.dAqk, a.dAkk, a.dQe,
+      a.dKe, a.dGe, a.L, a.H, a.scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+template <int DK, int DV>
+static int launch_kda_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta, void* W,
+                          void* Qh, void* Kt, void* A, void* U, float* gC, int B, int L, int H, float scale,
+                          cudaStream_t st) {
+  const int smem = sizeof(KdaFwdSmem<DK, DV>);
+  static bool attr[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 0 && dev < 64 && !attr[dev]) {
+    if (cudaFuncSetAttribute(kda_intra_fwd_kernel<DK, DV>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+        cudaSuccess)
+      return 3;
+    attr[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>(L / C), static_cast<unsigned>(H), static_cast<unsigned>(B));
+  kda_intra_fwd_kernel<DK, DV><<<grid, THREADS, smem, st>>>(
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, (__nv_bfloat16*)W,
+      (__nv_bfloat16*)Qh, (__nv_bfloat16*)Kt, (__nv_bfloat16*)A, (__nv_bfloat16*)U, gC, L, H, scale);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int kda_intra_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta, void* W, void* Qh,
+                  void* Kt, void* A, void* U, float* gC, int B, int L, int H, int DK, int DV, float scale,
+                  cudaStream_t st) {
+  if (L % C) return 5;
+  if (DK == 128 && DV == 128) return launch_kda_fwd<128, 128>(q, k, v, g, beta, W, Qh, Kt, A, U, gC, B, L, H, scale, st);
+  if (DK == 128 && DV == 256) return launch_kda_fwd<128, 256>(q, k, v, g, beta, W, Qh, Kt, A, U, gC, B, L, H, scale, st);
+  return 5;
+}
+
+int kda_intra_bwd(const KdaIntraBwdArgs& a, cudaStream_t st) {
+  if (a.L % C) return 5;
+  int rc = 5;
+  if (a.DK == 128 && a.DV == 128) rc = launch_kda_bwd<128, 128>(a, st);
+  else if (a.DK == 128 && a.DV == 256) rc = launch_kda_bwd<128, 256>(a, st);
+  if (rc) return rc;
+  const long long chunks = (long long)a.B * a.H * (a.L / C);
+  if ((rc = kda_gated_bwd(a.Qf, a.Kf, a.Gf, a.dAqk, a.dAkk, a.dQg, a.dKg, a.dGg, chunks, a.DK, st)) != 0) return rc;
+  kda_finish_kernel<<<static_cast<unsigned>(chunks), a.DK, 0, st>>>(a.dQe, a.dKe, a.dGe, a.dQg, a.dKg, a.dGg,
+                                                                     (__nv_bfloat16*)a.dq, (__nv_bfloat16*)a.dk,
+                                                                     a.dg, a.L, a.H, a.L / C, a.DK);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+}  // namespace vagus

@@ -142,6 +142,28 @@ int kda_gated_fwd(const float* Q, const float* K, const float* G, float* Aqk, fl
 int kda_gated_bwd(const float* Q, const float* K, const float* G, const float* dAqk, const float* dAkk, float* dQ,
                   float* dK, float* dG, long long chunks, int dk, cudaStream_t st);
 
+// kda_intra.cu: the per-channel-gate intra-chunk stage (DK = 128, DV = 128 / 256).
+// Forward: q, k (B, L, H, DK), v (B, L, H, DV) bf16, g (B, L, H, DK), beta (B, L, H)
+// fp32 -> W, Qh, Kt (BH, N, 64, DK), A (BH, N, 64, 64), U (BH, N, 64, DV) bf16 and
+// gC (BH, N, DK) fp32.
+int kda_intra_fwd(const void* q, const void* k, const void* v, const float* g, const float* beta, void* W, void* Qh,
+                  void* Kt, void* A, void* U, float* gC, int B, int L, int H, int DK, int DV, float scale,
+                  cudaStream_t st);
+struct KdaIntraBwdArgs {
+  const void *q, *k, *v;
+  const float *g, *beta;
+  const void *dW, *dQh, *dKt, *dU;        // chunk-major bf16
+  const float *dA, *dgC;                  // (BH, N, 64, 64), (BH, N, DK) fp32
+  void *dq, *dk, *dv;                     // token-major bf16
+  float *dg, *dbeta;                      // token-major fp32
+  // chunk-major fp32 work buffers, (BH, N, 64, DK) unless noted
+  float *Qf, *Kf, *Gf, *dQe, *dKe, *dGe, *dQg, *dKg, *dGg;
+  float *dAqk, *dAkk;                     // (BH, N, 64, 64)
+  int B, L, H, DK, DV;
+  float scale;
+};
+int kda_intra_bwd(const KdaIntraBwdArgs& a, cudaStream_t st);
+
 // mobius.cu: x_t = (A_t x_{t-1} + B_t) / (C_t x_{t-1} + D_t) along L; A..D, X, gO and the
 // gradients (batch, L, R) fp32 contiguous, x0 and gx0 (batch, R).
 int mobius_fwd(const float* A, const float* B, const float* C, const float* D, const float* x0, float* X, int batch,

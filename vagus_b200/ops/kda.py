@@ -1,9 +1,15 @@
 """Chunked delta rule with a per-channel (Kimi-delta, KDA) gate on CUDA.
 
-The intra-chunk stage runs in torch, chunk-parallel over the whole sequence
-(fp32); the sequential state recurrence runs on the GDR recurrence kernels
+For key head dim 128 (value head dim 128 or 256) with the delta rule the
+whole layer runs on our kernels (``_KDAFused``): the intra-chunk stage in
+``csrc/kda_intra.cu`` (per-channel cumulative decay, gated products on the
+tensor cores across 16-token blocks and elementwise inside them, the WY
+transform) and the state recurrence on the GDR recurrence kernels
 (``csrc/gdr.cu``: tcgen05 forward scan, chunk-parallel output and gradient
-kernels), whose chunk decay gC becomes a per-key-channel vector.
+kernels), whose chunk decay gC is a per-key-channel vector.  Other variants
+(no delta rule, an explicit write vector, other head dims) run the intra
+stage below in torch, chunk-parallel over the whole sequence (fp32), on the
+same recurrence kernels.
 
 Per chunk of C = 64 tokens with in-chunk cumulative log decay g_i (a dk
 vector, non-increasing in i), gated inner products
@@ -160,6 +166,43 @@ class _KDARec(torch.autograd.Function):
                 dS0.view(B, Hh, dk, dv) if ctx.has_S0 else None, None)
 
 
+class _KDAFused(torch.autograd.Function):
+    """The whole chunked KDA layer on our kernels: the intra-chunk stage
+    (``kda_intra.cu``: per-channel cumulative decay, gated products, WY
+    transform) and the state recurrence (``gdr.cu``), forward and backward,
+    with no autograd graph in between.  q, k (B, L, H, dk), v (B, L, H, dv)
+    bf16, g (B, L, H, dk) and beta (B, L, H) fp32, L a multiple of 64."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, g, beta, S0, scale: float):
+        C = native()
+        B, L, H, dk = q.shape
+        dv = v.shape[-1]
+        W, Qh, Kt, A, U, gC = C.kda_intra_fwd(q, k, v, g, beta, scale)
+        S0f = None if S0 is None else S0.float().reshape(B * H, dk, dv).contiguous()
+        o, Vp, states, S_out = C.gdr_rec_fwd(W, Qh, Kt, A, U, gC, S0f, True, H)
+        ctx.save_for_backward(q, k, v, g, beta, W, Qh, Kt, A, Vp, gC, states)
+        ctx.scale, ctx.has_S0, ctx.shape = scale, S0 is not None, (B, H, dk, dv)
+        return o, S_out.view(B, H, dk, dv)
+
+    @staticmethod
+    def backward(ctx, do, dS):
+        q, k, v, g, beta, W, Qh, Kt, A, Vp, gC, states = ctx.saved_tensors
+        B, H, dk, dv = ctx.shape
+        C = native()
+        dSf = None if dS is None else dS.float().reshape(B * H, dk, dv).contiguous()
+        dW, dQh, dKt, dA, dU, dgC, dS0 = C.gdr_rec_bwd(W, Qh, Kt, A, Vp, gC, states,
+                                                        do.to(torch.bfloat16).contiguous(), dSf, ctx.has_S0)
+        dq, dk_, dv_, dg, dbeta = C.kda_intra_bwd(q, k, v, g, beta, dW.to(torch.bfloat16), dQh.to(torch.bfloat16),
+                                                   dKt.to(torch.bfloat16), dA, dU.to(torch.bfloat16), dgC, ctx.scale)
+        return dq, dk_, dv_, dg, dbeta, (dS0.view(B, H, dk, dv) if ctx.has_S0 else None), None
+
+
+def _fused_ok(q, v, delta, w) -> bool:
+    return (q.is_cuda and delta and w is None and q.shape[-1] == 128 and v.shape[-1] in (128, 256)
+            and q.shape[1] % CHUNK == 0)
+
+
 def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64, delta: bool = True, w=None):
     """Chunked delta rule with a per-channel gate g (B, L, H, dk) (log decay)
     on CUDA; ``delta=False`` is gated linear attention (beta unused), and a
@@ -181,6 +224,10 @@ def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64, delta
         pz = lambda t: torch.nn.functional.pad(t, [0, 0] * (t.dim() - 2) + [0, pad])   # noqa: E731
         q, k, v, g, beta = pz(q), pz(k), pz(v), pz(g), pz(beta)
         w = None if w is None else pz(w)
+    if _fused_ok(q, v, delta, w):
+        bf = lambda t: t.to(torch.bfloat16).contiguous()   # noqa: E731
+        o, S = _KDAFused.apply(bf(q), bf(k), bf(v), g.float().contiguous(), beta.float().contiguous(), S0, scale)
+        return (o[:, :L] if pad else o), S
     parts = kda_intra(q, k, v, g, beta, scale, delta, w)
     o, S = _KDARec.apply(*parts, S0, H)
     return (o[:, :L] if pad else o), S

@@ -220,10 +220,11 @@ class NvlinkAllReduce:
         scale = 1.0 / self.world if op == dist.ReduceOp.AVG else 1.0
         native().comm_all_reduce(t, self.bases, self.rank, self.epoch, scale, self.slot)
 
-    def ddp_hook(self, _state, bucket) -> torch.futures.Future:
+    def ddp_hook(self, _state, bucket):
+        # no return annotation: DDP's hook check accepts only none or exactly Future[Tensor]
         buf = bucket.buffer()
         self(buf, dist.ReduceOp.AVG)
-        fut: torch.futures.Future = torch.futures.Future()
+        fut = torch.futures.Future()
         fut.set_result(buf)                 # stream-ordered: later users run after our kernels
         return fut
 
