@@ -148,8 +148,10 @@ def _muon_worker(rank, world, port, q):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_muon_fused_scatter_matches_allgather():
-    """The sharded Muon step with the Newton-Schulz product scattered to the
-    row owners from the GEMM epilogue equals the all-gather path bit for bit."""
+    """The sharded Muon step with the momentum row shards pushed to the
+    matrices' owners and the Newton-Schulz product scattered back to the row
+    owners from the GEMM epilogue equals the all-gather path bit for bit
+    (a bucket of three matrices over two ranks exercises the zero padding)."""
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()

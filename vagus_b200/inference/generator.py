@@ -137,7 +137,7 @@ class Generator:
         """A snapshot from which ``load_state`` resumes exactly: the model's
         cache, the stream record and the sampling RNG."""
         s = self.streams
-        return {"model_cache": self.model.export_cache(),
+        return {"cache": self.model.export_cache(),
                 "streams": {"rows": s.rows, "capacity": s.capacity, "consumed": s.consumed,
                             "head": None if s.head is None else s.head.clone()},
                 "rng": self.rng.get_state()}
@@ -145,7 +145,7 @@ class Generator:
     def load_state(self, state: dict, max_len: int | None = None) -> None:
         rec = state["streams"]
         cap = self._capacity(max_len or rec["capacity"])
-        self.model.load_cache(state["model_cache"], max_cache_len=cap)
+        self.model.load_cache(state["cache"], max_cache_len=cap)
         head = rec["head"]
         self.streams = _Streams(rows=rec["rows"], capacity=cap, consumed=rec["consumed"],
                                 head=None if head is None else head.to(self.device))

@@ -69,17 +69,21 @@ def agreement(out: Any, ref: Any) -> Optional[Agreement]:
 
 def compare(variants: dict[str, Callable], args: tuple = (), kwargs: Optional[dict] = None, *,
             ref: Optional[str] = None, warmup: int = 10, iters: int = 50, check: bool = True,
-            verbose: bool = True, device: Optional[torch.device] = None) -> dict[str, BenchResult]:
+            verbose: bool = True, device: Optional[torch.device] = None,
+            progress: bool = False) -> dict[str, BenchResult]:
     """Time every variant on ``args`` / ``kwargs`` and (``check``) compare
     its output with variant ``ref`` (default: the first).  Returns
     ``{name: BenchResult}``; each result carries ``.vs_ref`` (an
-    ``Agreement`` or None)."""
+    ``Agreement`` or None).  ``progress`` names each variant (flushed)
+    before it runs, so a crash inside one is attributed."""
     kwargs = kwargs or {}
     ref = ref or next(iter(variants))
     device = device or timing_device(args, kwargs)
     results: dict[str, BenchResult] = {}
     outputs: dict[str, Any] = {}
     for name, fn in variants.items():
+        if progress:
+            print(f"[meter] timing {name}", flush=True)
         r = bench(fn, args, kwargs, name=name, device=device, warmup=warmup, iters=iters)
         r.vs_ref = None
         results[name] = r

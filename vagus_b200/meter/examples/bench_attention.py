@@ -13,7 +13,9 @@ decode steps (lower-right causal attention over the cache).
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import math
+import sys
 
 import torch
 import torch.nn.functional as F
@@ -41,7 +43,12 @@ def main(argv=None):
     ap.add_argument("--prefill", type=int, default=2048)
     ap.add_argument("--steps", type=int, default=64)
     ap.add_argument("--kv-heads", type=int, default=None, help="GQA: key/value heads (default: H)")
+    ap.add_argument("--variants", nargs="+", default=None, help="subset of ours / sdpa / naive")
     a = ap.parse_args(argv)
+    try:
+        faulthandler.enable(file=sys.__stderr__)   # a native crash prints every thread's Python stack
+    except (AttributeError, OSError, ValueError):  # no real stderr (captured)
+        pass
     dev = "cuda" if torch.cuda.is_available() else "cpu"
     if a.decode:
         return decode_main(a, dev)
@@ -52,8 +59,11 @@ def main(argv=None):
                     "sdpa": lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True)}
         if not a.no_naive:
             variants["naive"] = lambda: naive(q, k, v)
+        if a.variants:
+            variants = {n: f for n, f in variants.items() if n in a.variants}
+        ref = "sdpa" if "sdpa" in variants else next(iter(variants))
         print(f"\nforward  B={a.B} H={a.H} L={a.L} dh={dh}")
-        compare(variants, ref="sdpa", iters=a.iters)
+        compare(variants, ref=ref, iters=a.iters, progress=True)
         do = torch.randn_like(q)
 
         def fb(fn):
@@ -62,7 +72,7 @@ def main(argv=None):
                 return torch.autograd.grad(out, (q, k, v), do)[0]
             return run
         print(f"forward+backward  B={a.B} H={a.H} L={a.L} dh={dh}")
-        compare({n: fb(f) for n, f in variants.items()}, ref="sdpa", iters=a.iters)
+        compare({n: fb(f) for n, f in variants.items()}, ref=ref, iters=a.iters, progress=True)
 
 
 def decode_main(a, dev):

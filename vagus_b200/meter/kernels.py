@@ -11,7 +11,7 @@ shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
 gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
-sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm.  With no
+sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, kda_intra_fwd, kda_intra_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm.  With no
 case names every
 case runs.
 
@@ -103,6 +103,20 @@ def _cases(B: int, L: int):
     kfl = Nq * 64 * 65 // 2 * dkk * 4                 # pairs x channels x (exp-weighted FMAs)
     cases["kda_gated_fwd"] = (lambda: C.kda_gated_fwd(Qg, Kg, Gg), None, kfl)
     cases["kda_gated_bwd"] = (lambda: C.kda_gated_bwd(Qg, Kg, Gg, dA1, dA2), None, 2 * kfl)
+    # the fused KDA intra stage (kda_intra.cu) at the same shape, value head dim 256
+    qa = torch.nn.functional.normalize(torch.randn(B, L, 4, dkk, device=dev), dim=-1).to(bf)
+    ka = torch.nn.functional.normalize(torch.randn(B, L, 4, dkk, device=dev), dim=-1).to(bf)
+    va = r(B, L, 4, 256)
+    ga = -torch.rand(B, L, 4, dkk, device=dev) * 0.05
+    ba = torch.rand(B, L, 4, device=dev)
+    kda_in = (qa, ka, va, ga, ba, dkk ** -0.5)
+    # per chunk: two gated products (64 x 64 x 128), W = T(bGK), U = T(bV), the 64 x 64 inverse
+    kintra = Nq * (2 * 2 * 64 * 64 * dkk + 2 * 64 * 64 * (dkk + 256) + 2 * 64 ** 3 // 3)
+    cases["kda_intra_fwd"] = (lambda: C.kda_intra_fwd(*kda_in), None, kintra)
+    kout = C.kda_intra_fwd(*kda_in)
+    kgr = [torch.randn_like(t).to(t.dtype) for t in kout]
+    cases["kda_intra_bwd"] = (lambda: C.kda_intra_bwd(*kda_in[:5], kgr[0], kgr[1], kgr[2], kgr[3].float(), kgr[4],
+                                                      kgr[5], kda_in[5]), None, 2 * kintra)
 
     # Kalman precision recurrence (Mobius scan) at the diagonal KDN shape: 4 heads x 128 channels
     from ..models.kalman import mobius_scan as _mob

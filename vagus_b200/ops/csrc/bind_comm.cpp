@@ -112,6 +112,17 @@ void comm_barrier(std::vector<int64_t> bases, int64_t rank, int64_t epoch) {
   TORCH_CHECK(rc == 0, "comm_barrier failed (code ", rc, ")");
 }
 
+// Push the blocks of a contiguous tensor to their owners' heaps (see comm.cu).
+void comm_scatter_blocks(std::vector<int64_t> bases, int64_t slot_off, Tensor src, int64_t blk_bytes, int64_t nblk,
+                         int64_t per_rank, int64_t dst_stride, int64_t dst_off) {
+  TORCH_CHECK(src.is_cuda() && src.is_contiguous() && src.numel() * src.element_size() >= blk_bytes * nblk,
+              "comm_scatter_blocks: contiguous CUDA source of nblk blocks");
+  const int rc = vagus::comm_scatter_blocks(peers_of(bases), static_cast<int>(bases.size()), slot_off, src.data_ptr(),
+                                            blk_bytes, static_cast<int>(nblk), static_cast<int>(per_rank), dst_stride,
+                                            dst_off, stream());
+  TORCH_CHECK(rc == 0, "comm_scatter_blocks failed (code ", rc, ")");
+}
+
 // A tensor over `numel` elements of this process's heap at byte offset
 // `offset` (no ownership: the heap outlives it).
 Tensor comm_heap_view(int64_t ptr, int64_t offset, int64_t numel, at::ScalarType dtype) {
@@ -127,6 +138,7 @@ Tensor comm_heap_view(int64_t ptr, int64_t offset, int64_t numel, at::ScalarType
 
 void register_comm_ops(pybind11::module& m) {
   m.def("comm_barrier", &comm_barrier);
+  m.def("comm_scatter_blocks", &comm_scatter_blocks);
   m.def("comm_set_wait_budget", &comm_set_wait_budget, "bound of cross-GPU flag waits, seconds");
   m.def("comm_wait_budget", &comm_wait_budget);
   m.def("comm_heap_view", &comm_heap_view);

@@ -327,6 +327,32 @@ int comm_all_reduce(const CommPeers& peers, int rank, int world, uint32_t epoch,
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
+// ------------------------------------------------------- block scatter --
+// Block g of `src` (blk bytes each) goes to rank g / per_rank, into its heap
+// at slot_off + (g % per_rank) * dst_stride + dst_off: one pass of NVLink
+// stores from this GPU, no staging.  The caller's epoch barrier publishes it.
+__global__ void scatter_blocks_k(const CommPeers peers, int world, long long slot_off, const uint8_t* __restrict__ src,
+                                 long long blk, int per_rank, long long dst_stride, long long dst_off) {
+  const int g = blockIdx.y;
+  const int owner = g / per_rank;
+  if (!VAGUS_CHECK(owner, world)) return;
+  uint8_t* dst = peers.base[owner] + slot_off + (long long)(g % per_rank) * dst_stride + dst_off;
+  copy_bytes(dst, src + (long long)g * blk, blk, (long long)blockIdx.x * blockDim.x + threadIdx.x,
+             (long long)gridDim.x * blockDim.x);
+}
+
+int comm_scatter_blocks(const CommPeers& peers, int world, long long slot_off, const void* src, long long blk_bytes,
+                        int nblk, int per_rank, long long dst_stride, long long dst_off, cudaStream_t st) {
+  if (world < 2 || world > kMaxCommPeers || nblk <= 0 || nblk > 65535 || per_rank <= 0 || blk_bytes <= 0 ||
+      (nblk - 1) / per_rank >= world || slot_off < kCommHeaderBytes)
+    return 5;
+  const long long vec = (blk_bytes + 15) / 16;
+  const int gx = static_cast<int>(std::min<long long>((vec + 255) / 256, std::max(1, 296 / nblk)));
+  scatter_blocks_k<<<dim3(gx, nblk), 256, 0, st>>>(peers, world, slot_off, static_cast<const uint8_t*>(src), blk_bytes,
+                                                  per_rank, dst_stride, dst_off);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
 int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, uint32_t epoch, unsigned long long wait_ns,
                  int* err, cudaStream_t st) {
   if (world < 2 || world > kMaxCommPeers || flag_off < 0 || flag_off + 4 * kMaxCommPeers > kCommHeaderBytes) return 5;

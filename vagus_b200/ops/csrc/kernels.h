@@ -203,5 +203,10 @@ int comm_all_reduce(const CommPeers& peers, int rank, int world, unsigned epoch,
                     cudaStream_t st);
 int comm_barrier(const CommPeers& peers, int rank, int world, int flag_off, unsigned epoch, unsigned long long wait_ns,
                  int* err, cudaStream_t st);
+// Block g (blk_bytes each) of src -> heap of rank g / per_rank at
+// slot_off + (g % per_rank) * dst_stride + dst_off (peer stores; publish with
+// comm_barrier).
+int comm_scatter_blocks(const CommPeers& peers, int world, long long slot_off, const void* src, long long blk_bytes,
+                        int nblk, int per_rank, long long dst_stride, long long dst_off, cudaStream_t st);
 
 }  // namespace vagus

@@ -165,12 +165,14 @@ def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_de
     """Muon for row-sharded DTensor parameters (FSDP2 / HSDP).
 
     ``exchanges`` (a dict, kept by the optimizer) turns on the fused NVLink
-    path on CUDA: the final Newton-Schulz product of each orthogonalised
-    matrix is written by the GEMM epilogue straight into the row owners'
-    receive buffers on the other GPUs (``parallel.nvlink.MuonExchange``), one
-    epoch barrier follows, and each rank applies the rows it received -- in
-    place of an all-gather of every full result, which moves ``world`` times
-    the bytes.  Buckets the fused path cannot take keep the all-gather."""
+    path on CUDA (``parallel.nvlink.MuonExchange``): every rank pushes its
+    momentum row shard of each matrix to the matrix's owner (one barrier),
+    the owner orthogonalises its matrices, the final Newton-Schulz product of
+    each is written by the GEMM epilogue straight into the row owners'
+    receive buffers on the other GPUs, one epoch barrier follows, and each
+    rank applies the rows it received -- in place of two all-gathers of every
+    full matrix, which move ``world`` times the bytes.  Buckets the fused
+    path cannot take keep the all-gathers."""
     P = [p.to_local() for p in params]
     G = [g.to_local() for g in grads]
     Bf = [b.to_local() for b in momentum_bufs]
@@ -206,10 +208,26 @@ def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_de
             ex = exchanges[id(plan[j][4])]
             if ex is None or ex.slot_bytes < sizes[id(plan[j][4])]:
                 del fused[j]            # another machine in the group, or the buckets outgrew the heap
+    # fused buckets: each momentum row shard goes straight to the matrix's owner
+    # (one NVLink push per bucket and one barrier), not an all-gather of all of them
+    for j in fused:
+        shape, _, _, idx, group, ws, rank = plan[j]
+        local = torch.stack([updates[i] for i in idx]).to(torch.bfloat16)
+        exchanges[id(group)].push_inputs(fused[j][0], local, fused[j][1])
+    for ex in {id(exchanges[id(plan[j][4])]): exchanges[id(plan[j][4])] for j in fused}.values():
+        ex.barrier()
     pending = []
     for j, (shape, dtype, device, idx, group, ws, rank) in enumerate(plan):
         rows, cols = shape
         n = len(idx)
+        if j in fused:
+            ex = exchanges[id(group)]
+            off, chunk = fused[j]
+            mine = ex.received_inputs(off, n, chunk, rows, cols)
+            X, coeffs, transposed = _ns_prepare(mine, ns_steps, eps, ns_coeffs)
+            _ns_kernels(X.contiguous(), coeffs, last=ex.scatter_fn(off, rank * chunk, rows // ws, cols, transposed))
+            pending.append((ex, off, idx, shape, dtype, rows // ws, transposed))
+            continue
         local = torch.stack([updates[i] for i in idx]).to(torch.bfloat16)
         if ws > 1:
             rows_l = rows // ws
@@ -225,13 +243,6 @@ def muon_update_sharded(params, grads, momentum_bufs, *, lr, momentum, weight_de
         mine = full[rank * chunk:(rank + 1) * chunk]
         if mine.size(0) < chunk:
             mine = torch.cat([mine, full.new_zeros((chunk - mine.size(0), rows, cols))])
-        if j in fused:
-            ex = exchanges[id(group)]
-            off = fused[j][0]
-            X, coeffs, transposed = _ns_prepare(mine, ns_steps, eps, ns_coeffs)
-            _ns_kernels(X.contiguous(), coeffs, last=ex.scatter_fn(off, rank * chunk, rows_l, cols, transposed))
-            pending.append((ex, off, idx, shape, dtype, rows_l, transposed))
-            continue
         mine = newton_schulz(mine, steps=ns_steps, eps=eps, scheme=ns_coeffs)
         if ws > 1:
             out = torch.empty((chunk * ws, rows, cols), dtype=mine.dtype, device=device)

@@ -311,9 +311,10 @@ def unit_gather_layout(unit) -> list[dict]:
 
 
 class MuonExchange:
-    """IPC-shared receive buffers for the sharded Muon step's fused
-    Newton-Schulz product + scatter (a GEMM followed by an all-to-all, as one
-    kernel over NVLink).
+    """IPC-shared receive buffers for the sharded Muon step: the momentum
+    row shards pushed to the matrices' owners (``push_inputs``, in place of an
+    all-gather), and the fused Newton-Schulz product + scatter of the results
+    (a GEMM followed by an all-to-all, as one kernel over NVLink).
 
     Each rank's heap holds two slots (alternating by epoch) of ``slot_bytes``;
     a bucket of ``n`` same-shape matrices, row-sharded ``world`` ways, owns a
@@ -364,6 +365,30 @@ class MuonExchange:
             if rc:
                 raise RuntimeError(f"gemm_scatter rejected the problem (code {rc})")
         return last
+
+    def push_inputs(self, off: int, local: torch.Tensor, chunk: int) -> None:
+        """Send this rank's row shard of each of a bucket's matrices to the
+        matrix's owner (the rank that orthogonalises it): matrix g of ``local``
+        (n, rows_l, cols) bf16 lands in rank ``g // chunk``'s block at
+        ``(g % chunk, rank rows_l : (rank + 1) rows_l)``, laid out (chunk, rows,
+        cols), in the next epoch's slot.  Only the owner's rows cross NVLink,
+        1/world of what an all-gather of every full momentum moves."""
+        n, rows_l, cols = local.shape
+        rows = rows_l * self.world
+        blk = rows_l * cols * 2
+        native().comm_scatter_blocks(self.bases, self._slot(self.epoch + 1), local.contiguous(), blk, n, chunk,
+                                     rows * cols * 2, off + self.rank * blk)
+
+    def received_inputs(self, off: int, n: int, chunk: int, rows: int, cols: int) -> torch.Tensor:
+        """This rank's ``chunk`` full matrices of the bucket, (chunk, rows,
+        cols) bf16 in the heap; the padding past the bucket's ``n`` matrices is
+        zeroed (nobody sends it)."""
+        t = native().comm_heap_view(self.own, self._slot(self.epoch) + off, chunk * rows * cols,
+                                    torch.bfloat16).view(chunk, rows, cols)
+        real = max(0, min(chunk, n - self.rank * chunk))
+        if real < chunk:
+            t[real:].zero_()
+        return t
 
     def barrier(self):
         self.epoch += 1
