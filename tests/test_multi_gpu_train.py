@@ -146,6 +146,12 @@ def _train_worker(rank, port, tmp, q):
             shutil.copy(os.path.join(tmp, "a", "ckpt-00000003.pt"), os.path.join(tmp, "b", "ckpt-00000003.pt"))
         dist.barrier()
         tm.train(_train_cfg(tmp, "b", 6, recent_minutes=1e9), teardown=False)
+        if rank == 0:
+            os.makedirs(os.path.join(tmp, "c"))
+            shutil.copy(os.path.join(tmp, "a", "ckpt-00000003.pt"), os.path.join(tmp, "c", "ckpt-00000003.pt"))
+        dist.barrier()
+        # resume at step 3 with nothing left to train: the final checkpoint is the loaded state, saved again
+        tm.train(_train_cfg(tmp, "c", 3, recent_minutes=1e9), teardown=False)
         torch.cuda.synchronize()
         word = ops.native().error_word()
         dist.barrier()
@@ -165,6 +171,17 @@ def test_train_nvlink_fsdp_slow_checkpoint_and_resume(tmp_path):
         assert res["error_word"] == 0, (rank, res)
     assert results[0]["slow_write_done"]
     assert (tmp_path / "a" / "recent.pt").exists()
+    # load + save round trip: model and optimizer state bit for bit
+    a3 = torch.load(tmp_path / "a" / "ckpt-00000003.pt", weights_only=False)
+    c3 = torch.load(tmp_path / "c" / "ckpt-00000003.pt", weights_only=False)
+    for k in a3["model"]:
+        assert torch.equal(a3["model"][k], c3["model"][k]), ("round trip model", k)
+    flat = lambda sd: {f"{k}/{n}": t for k, st in sd["optimizer"]["state"].items()   # noqa: E731
+                       for n, t in st.items() if torch.is_tensor(t)}
+    fa, fc = flat(a3), flat(c3)
+    assert fa.keys() == fc.keys() and len(fa) > 0, ("round trip optimizer keys", sorted(fa)[:4], sorted(fc)[:4])
+    for k in fa:
+        assert torch.equal(fa[k], fc[k]), ("round trip optimizer", k)
     a = torch.load(tmp_path / "a" / "ckpt-00000006.pt", weights_only=False)
     a2 = torch.load(tmp_path / "a2" / "ckpt-00000006.pt", weights_only=False)
     b = torch.load(tmp_path / "b" / "ckpt-00000006.pt", weights_only=False)
@@ -173,4 +190,17 @@ def test_train_nvlink_fsdp_slow_checkpoint_and_resume(tmp_path):
         # the resumed run is as close to the straight run as a second straight run is
         x, x2, y = (t["model"][k].float() for t in (a, a2, b))
         noise = (x - x2).norm().item()
-        assert (x - y).norm() <= 3 * noise + 1e-3 * max(1e-3, x.norm().item()), (k, (x - y).norm().item(), noise)
+        assert (x - y).norm() <= 3 * noise + 1e-3 * max(1e-3, x.norm().item()), \
+            (k, (x - y).norm().item(), noise, _losses(tmp_path))
+
+
+def _losses(tmp):
+    """Per-step training loss of each run (diagnostic for a failed comparison)."""
+    import json
+    out = {}
+    for run in ("a", "a2", "b"):
+        f = tmp / run / "metrics.jsonl"
+        if f.exists():
+            rows = [json.loads(line) for line in f.read_text().splitlines() if line.strip()]
+            out[run] = [(r.get("step"), r.get("loss")) for r in rows if "loss" in r]
+    return out

@@ -34,6 +34,8 @@ std::tuple<int64_t, pybind11::bytes> comm_heap_create(int64_t bytes) {
   void* p = nullptr;
   TORCH_CHECK(cudaMalloc(&p, static_cast<size_t>(bytes)) == cudaSuccess, "comm heap: cudaMalloc failed");
   TORCH_CHECK(cudaMemset(p, 0, static_cast<size_t>(bytes)) == cudaSuccess, "comm heap: cudaMemset failed");
+  // zeroed before any peer can map it (the flags start below every epoch)
+  TORCH_CHECK(cudaDeviceSynchronize() == cudaSuccess, "comm heap: synchronise after zeroing failed");
   cudaIpcMemHandle_t h;
   TORCH_CHECK(cudaIpcGetMemHandle(&h, p) == cudaSuccess, "comm heap: cudaIpcGetMemHandle failed");
   return {reinterpret_cast<int64_t>(p), pybind11::bytes(reinterpret_cast<const char*>(&h), sizeof(h))};

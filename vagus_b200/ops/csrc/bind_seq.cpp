@@ -272,23 +272,14 @@ std::vector<Tensor> kda_intra_bwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor
                   dU.numel() == v.numel() && dA.numel() == (long long)B * H * L * 64 &&
                   dgC.numel() == (long long)B * H * (L / 64) * DK,
               "kda_intra_bwd: gradient shapes do not match the forward's outputs");
-  const long long chunks = (long long)B * H * (L / 64);
-  auto f32 = g.options();
   auto dq = torch::empty_like(q), dk = torch::empty_like(k), dv = torch::empty_like(v);
   auto dg = torch::empty_like(g), dbeta = torch::empty_like(beta);
-  auto work = torch::empty({9, chunks, 64, DK}, f32);
-  auto dAw = torch::empty({2, chunks, 64, 64}, f32);
   vagus::KdaIntraBwdArgs a;
   a.q = q.data_ptr(); a.k = k.data_ptr(); a.v = v.data_ptr(); a.g = g.data_ptr<float>();
   a.beta = beta.data_ptr<float>(); a.dW = dW.data_ptr(); a.dQh = dQh.data_ptr(); a.dKt = dKt.data_ptr();
   a.dU = dU.data_ptr(); a.dA = dA.data_ptr<float>(); a.dgC = dgC.data_ptr<float>();
   a.dq = dq.data_ptr(); a.dk = dk.data_ptr(); a.dv = dv.data_ptr(); a.dg = dg.data_ptr<float>();
   a.dbeta = dbeta.data_ptr<float>();
-  float* w = work.data_ptr<float>();
-  const long long slab = chunks * 64 * DK;
-  a.Qf = w; a.Kf = w + slab; a.Gf = w + 2 * slab; a.dQe = w + 3 * slab; a.dKe = w + 4 * slab; a.dGe = w + 5 * slab;
-  a.dQg = w + 6 * slab; a.dKg = w + 7 * slab; a.dGg = w + 8 * slab;
-  a.dAqk = dAw.data_ptr<float>(); a.dAkk = a.dAqk + chunks * 64 * 64;
   a.B = B; a.L = L; a.H = H; a.DK = DK; a.DV = DV; a.scale = static_cast<float>(scale);
   check(vagus::kda_intra_bwd(a, stream()), "kda_intra_bwd");
   return {dq, dk, dv, dg, dbeta};

@@ -244,29 +244,57 @@ kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
 }
 
 // ---------------------------------------------------------------- backward --
-// The backward is three kernels:
-//   kda_intra_bwd_kernel (below, one CTA per chunk): recomputes gamma, the
-//     gated products and T, runs the WY backward --
-//         dXw = T^T dW, dXu = T^T dU, dT = dW Xw^T + dU Xu^T,
-//         dM = -strict_lower(T^T dT T^T), dAkk = diag(b) dM, dAqk = s dA
-//     -- writes dv and dbeta, the elementwise parts of dq / dk / dgamma
-//         dq_e = s dQh o G,  dk_e = dKt o E + b dXw o G,
-//         dgamma_e = s dQh o Q o G - dKt o K o E + b dXw o K o G
-//                    (+ column sums of dKt o K o E and dgC o G_C on the last row)
-//     (E = exp(gamma_C - gamma)), and fp32 chunk-major Q, K, gamma, dAqk, dAkk;
-//   kda_gated_bwd (kda.cu): the gated products' gradients dQ_g, dK_g, dgamma_g;
-//   kda_finish_kernel: dq = dq_e + dQ_g, dk = dk_e + dK_g (bf16 token-major),
-//     dg = reverse cumsum over the chunk of dgamma_e + dgamma_g.
+// One kernel per chunk (one CTA, eight warps):
+//   1. recompute gamma, the gated products and T;
+//   2. WY backward --
+//        dXw = T^T dW, dXu = T^T dU, dT = dW Xw^T + dU Xu^T,
+//        dM = -strict_lower(T^T dT T^T), dAkk = diag(b) dM, dAqk = s dA
+//      -- giving dv and dbeta, and the elementwise parts of dq / dk / dgamma
+//        dq_e = s dQh o G,  dk_e = dKt o E + b dXw o G,
+//        dgamma_e = s dQh o Q o G - dKt o K o E + b dXw o K o G
+//      (E = exp(gamma_C - gamma); the last row also takes the column sums of
+//      dKt o K o E and dgC o G_C), held in registers in the mma fragment
+//      layout (warp w: rows 16 (w & 3).., key channels 64 (w >> 2)..);
+//   3. the gated products' backward, in the same fragment layout:
+//        dQ[i]  = sum_j dAqk[i,j] K_j e^(gamma_i - gamma_j)        (row role)
+//        dKr[i] = sum_j dAkk[i,j] K_j e^(gamma_i - gamma_j)        (row role)
+//        dKc[j] = sum_i (dAqk[i,j] Q_i + dAkk[i,j] K_i) e^(gamma_i - gamma_j)
+//      and dgamma_g = Q o dQ + K o (dKr - dKc).  Across 16-token blocks the
+//      decay factorises through one reference row per block, both factors
+//      <= 1: block I's row role through r = 16 I - 1 (the row just before
+//      it) over all earlier keys at once,
+//        dQ[I] += e^(gamma_I - gamma_r) o (dAqk[I, :16 I] (K[:16 I] o e^(gamma_r - gamma)))
+//      and block J's column role through r = 16 J + 15 (its last row) over
+//      all later rows; these are mma.sync products over bf16 operands built
+//      once per chunk.  Inside a block the decay is taken elementwise (fp32);
+//   4. dq, dk (bf16) and dg = reverse cumsum over the chunk of dgamma (fp32)
+//      written token-major.
 template <int DK, int DV>
 struct KdaBwdSmem {
+  static constexpr int RK = 96;          // rows of the factorised operands: 16 + 32 + 48
   __nv_bfloat16 Q[C][DK + PAD];
   __nv_bfloat16 K[C][DK + PAD];
-  float gam[C][DK];
-  // scratch: the gated products' R and P tiles, then XW = diag(b) (K o G)
-  // and the dW tile (later T^T dT, bf16 C x C)
+  float gam[C][DK];                      // cumulative log decay; dgamma at the end
+  // scratch A: the products' R / P tiles; then XW = diag(b) (K o G) and the dW
+  // tile (later T^T dT); then Kr = the row-role key operands
   static constexpr int PR_BYTES = (1 + 6) * BLK * (DK + PAD) * 2;
   static constexpr int XD_BYTES = 2 * C * (DK + PAD) * 2;
-  __align__(16) unsigned char scratch[PR_BYTES > XD_BYTES ? PR_BYTES : XD_BYTES];
+  static constexpr int KR_BYTES = RK * (DK + PAD) * 2;
+  static constexpr int A_BYTES = PR_BYTES > XD_BYTES ? (PR_BYTES > KR_BYTES ? PR_BYTES : KR_BYTES)
+                                                     : (XD_BYTES > KR_BYTES ? XD_BYTES : KR_BYTES);
+  __align__(16) unsigned char scratch[A_BYTES];
+  float Aqk[C][C + 1];                   // products, then Akk (for dbeta), then dAqk
+  float M[C][C + 1];                     // Akk -> M -> T, then dAkk
+  __nv_bfloat16 Tb[C][C + PAD];          // T, then dAqk (bf16)
+  __nv_bfloat16 DT[C][C + PAD];          // dT, then dAkk (bf16)
+  // scratch B: V and dU; then Qc, Kc = the column-role operands
+  static constexpr int VU_BYTES = 2 * C * (DV + PAD) * 2;
+  static constexpr int QK_BYTES = 2 * RK * (DK + PAD) * 2;
+  __align__(16) unsigned char scratch2[VU_BYTES > QK_BYTES ? VU_BYTES : QK_BYTES];
+  float beta[C];
+  float rw[C], ru[C], rm[C];
+  float colk[DK];                        // sum_i dKt o K o E per channel (+ dgC G_C)
+
   __device__ __nv_bfloat16 (*R())[DK + PAD] { return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch); }
   __device__ __nv_bfloat16 (*P())[BLK][DK + PAD] {
     return reinterpret_cast<__nv_bfloat16 (*)[BLK][DK + PAD]>(scratch + BLK * (DK + PAD) * 2);
@@ -275,16 +303,21 @@ struct KdaBwdSmem {
   __device__ __nv_bfloat16 (*DW())[DK + PAD] {
     return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch + C * (DK + PAD) * 2);
   }
-  float Aqk[C][C + 1];                   // products, then Akk kept for dbeta
-  float M[C][C + 1];                     // Akk -> M -> T
-  __nv_bfloat16 Tb[C][C + PAD];
-  __nv_bfloat16 V[C][DV + PAD];
-  __nv_bfloat16 DU[C][DV + PAD];
-  __nv_bfloat16 DT[C][C + PAD];
-  float beta[C];
-  float rw[C], ru[C], rm[C];
-  float colk[DK];                        // sum_i dKt o K o E per channel
+  __device__ __nv_bfloat16 (*Kr())[DK + PAD] { return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch); }
+  __device__ __nv_bfloat16 (*V())[DV + PAD] { return reinterpret_cast<__nv_bfloat16 (*)[DV + PAD]>(scratch2); }
+  __device__ __nv_bfloat16 (*DU())[DV + PAD] {
+    return reinterpret_cast<__nv_bfloat16 (*)[DV + PAD]>(scratch2 + C * (DV + PAD) * 2);
+  }
+  __device__ __nv_bfloat16 (*Qc())[DK + PAD] { return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch2); }
+  __device__ __nv_bfloat16 (*Kc())[DK + PAD] {
+    return reinterpret_cast<__nv_bfloat16 (*)[DK + PAD]>(scratch2 + RK * (DK + PAD) * 2);
+  }
 };
+
+// row offset of block I's (I = 1..3) row-role operand in Kr, and of block J's
+// (J = 0..2) column-role operands in Qc / Kc
+__device__ __forceinline__ int kr_off(int I) { return (I - 1) * I * 8; }                   // 0, 16, 48
+__device__ __forceinline__ int qc_off(int J) { return J == 0 ? 0 : (J == 1 ? 48 : 80); }
 
 // out[i] += sum over this warp's fragment columns of acc[i][c] * X[i][c] (bf16 X)
 template <int NT>
@@ -314,11 +347,11 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
                      const float* __restrict__ beta, const __nv_bfloat16* __restrict__ dW,
                      const __nv_bfloat16* __restrict__ dQh, const __nv_bfloat16* __restrict__ dKt,
                      const float* __restrict__ dA, const __nv_bfloat16* __restrict__ dU,
-                     const float* __restrict__ dgC, __nv_bfloat16* __restrict__ dv, float* __restrict__ dbeta,
-                     float* __restrict__ Qf, float* __restrict__ Kf, float* __restrict__ Gf,
-                     float* __restrict__ dAqk, float* __restrict__ dAkk, float* __restrict__ dQe,
-                     float* __restrict__ dKe, float* __restrict__ dGe, int L, int H, float scale) {
+                     const float* __restrict__ dgC, __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk,
+                     __nv_bfloat16* __restrict__ dv, float* __restrict__ dg, float* __restrict__ dbeta, int L, int H,
+                     float scale) {
   using S = KdaBwdSmem<DK, DV>;
+  constexpr int NTK = DK / 16;           // fragment column tiles of a warp's DK / 2 channels
   extern __shared__ __align__(128) uint8_t smem_raw[];
   S& sm = *reinterpret_cast<S*>(smem_raw);
   const int n = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
@@ -327,10 +360,12 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   const long long tok0 = (long long)b * L + (long long)n * C;
   const int warp = threadIdx.x >> 5;
   const int tid = threadIdx.x;
+  __nv_bfloat16 (*Vs)[DV + PAD] = sm.V();
+  __nv_bfloat16 (*DUs)[DV + PAD] = sm.DU();
   load_tile(&sm.Q[0][0], DK + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
   load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
-  load_tile(&sm.V[0][0], DV + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
-  load_tile(&sm.DU[0][0], DV + PAD, dU + cidx * C * DV, DV, C, DV);
+  load_tile(&Vs[0][0], DV + PAD, v + (tok0 * H + h) * DV, (long long)H * DV, C, DV);
+  load_tile(&DUs[0][0], DV + PAD, dU + cidx * C * DV, DV, C, DV);
   cp_commit();
   if (tid < C) {
     sm.beta[tid] = beta[(tok0 + tid) * H + h];
@@ -344,25 +379,18 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   __nv_bfloat16 (*XW)[DK + PAD] = sm.XW();
   __nv_bfloat16 (*DWt)[DK + PAD] = sm.DW();
 
-  // fp32 copies for the gated-products backward; keep Akk; M = diag(b) Akk -> T
-  const long long cbase = cidx * C * DK;
-  for (int idx = tid; idx < C * DK; idx += THREADS) {
-    const int i = idx / DK, c = idx % DK;
-    Qf[cbase + idx] = bf2f(sm.Q[i][c]);
-    Kf[cbase + idx] = bf2f(sm.K[i][c]);
-    Gf[cbase + idx] = sm.gam[i][c];
-  }
+  // keep Akk (for dbeta); M = diag(b) Akk -> T
   for (int idx = tid; idx < C * C; idx += THREADS) {
     const int i = idx / C, j = idx % C;
     const float akk = sm.M[i][j];
     sm.Aqk[i][j] = akk;
     sm.M[i][j] = sm.beta[i] * akk;
-    dAqk[cidx * C * C + idx] = j <= i ? scale * dA[cidx * C * C + idx] : 0.f;
   }
   __syncthreads();
   tri_inverse_inplace(sm.M);
   for (int idx = tid; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.M[idx / C][idx % C]);
   // XW = diag(b) (K o G); dW tile
+  const long long cbase = cidx * C * DK;
   for (int idx = tid; idx < C * DK / 2; idx += THREADS) {
     const int i = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
     const float2 kv = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
@@ -376,33 +404,34 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   __syncthreads();
 
   const int m0 = (warp & 3) * 16;
+  const int c0 = (warp >> 2) * (DK / 2);
   {
     // dXu = T^T dU  ->  dv = diag(b) dXu ; ru += dXu . V
     constexpr int NT = DV / 16;
-    const int c0 = (warp >> 2) * (DV / 2);
+    const int v0 = (warp >> 2) * (DV / 2);
     float acc[1][NT][4];
     zero(acc);
-    warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &sm.DU[0][0], DV + PAD, m0, c0, C);
-    frag_row_dot<NT>(acc, &sm.V[0][0], DV + PAD, m0, c0, sm.ru);
+    warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &DUs[0][0], DV + PAD, m0, v0, C);
+    frag_row_dot<NT>(acc, &Vs[0][0], DV + PAD, m0, v0, sm.ru);
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; e += 2) {
-        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        const int i = m0 + frag_row(0, e), c = v0 + frag_col(nt, e);
         *reinterpret_cast<uint32_t*>(dv + ((tok0 + i) * H + h) * DV + c) =
             pack_bf16x2(sm.beta[i] * acc[0][nt][e], sm.beta[i] * acc[0][nt][e + 1]);
       }
   }
+  // the running gradients of this warp's fragment: dq, dk, dgamma
+  float Rq[NTK][4], Rk[NTK][4], Rg[NTK][4];
   {
     // dXw = T^T dW, and every elementwise term of (i, c) in the same pass
-    constexpr int NT = DK / 16;
-    const int c0 = (warp >> 2) * (DK / 2);
-    float acc[1][NT][4];
+    float acc[1][NTK][4];
     zero(acc);
-    warp_mma<1, NT, true, true>(acc, &sm.Tb[0][0], C + PAD, &DWt[0][0], DK + PAD, m0, c0, C);
+    warp_mma<1, NTK, true, true>(acc, &sm.Tb[0][0], C + PAD, &DWt[0][0], DK + PAD, m0, c0, C);
     float part[2] = {0.f, 0.f};
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NTK; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
@@ -413,9 +442,9 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
         part[e >> 1] += dxw * kv * G;
         const float kte = dkt * kv * E;
         atomicAdd(&sm.colk[c], kte);
-        dQe[cbase + i * DK + c] = scale * dqh * G;
-        dKe[cbase + i * DK + c] = dkt * E + bi * dxw * G;
-        dGe[cbase + i * DK + c] = scale * dqh * qv * G - kte + bi * dxw * kv * G;
+        Rq[nt][e] = scale * dqh * G;
+        Rk[nt][e] = dkt * E + bi * dxw * G;
+        Rg[nt][e] = scale * dqh * qv * G - kte + bi * dxw * kv * G;
       }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -433,7 +462,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
     zero(a2);
     const int n0 = (warp >> 2) * 32;
     warp_mma<1, 4, false, false>(a1, &DWt[0][0], DK + PAD, &XW[0][0], DK + PAD, m0, n0, DK);
-    warp_mma<1, 4, false, false>(a2, &sm.DU[0][0], DV + PAD, &sm.V[0][0], DV + PAD, m0, n0, DV);
+    warp_mma<1, 4, false, false>(a2, &DUs[0][0], DV + PAD, &Vs[0][0], DV + PAD, m0, n0, DV);
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
@@ -462,11 +491,14 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   }
   __syncthreads();
   {
+    // dAkk = diag(b) dM into M (T is in Tb from here on); dAqk = s lower(dA)
+    // into Aqk once this element's Akk has been used for dbeta
     float dm[1][4][4];
     zero(dm);
     const int n0 = (warp >> 2) * 32;
     warp_mma<1, 4, false, false>(dm, &Pb[0][0], DK + PAD, &sm.Tb[0][0], C + PAD, m0, n0, C);
     float part[2] = {0.f, 0.f};
+    const float* dAc = dA + cidx * C * C;
 #pragma unroll
     for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
@@ -474,7 +506,8 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
         const int i = m0 + frag_row(0, e), j = n0 + frag_col(nt, e);
         const float dmv = j < i ? -dm[0][nt][e] : 0.f;
         part[e >> 1] += dmv * sm.Aqk[i][j];
-        dAkk[cidx * C * C + i * C + j] = sm.beta[i] * dmv;
+        sm.M[i][j] = sm.beta[i] * dmv;
+        sm.Aqk[i][j] = j <= i ? scale * dAc[i * C + j] : 0.f;
       }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
@@ -486,35 +519,138 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   }
   __syncthreads();
   if (tid < C) dbeta[(tok0 + tid) * H + h] = sm.rw[tid] + sm.ru[tid] + sm.rm[tid];
-  // the last row's dgamma takes the column sums and dgC G_C
-  for (int c = tid; c < DK; c += THREADS) {
-    const float gl = __expf(sm.gam[C - 1][c]);
-    dGe[cbase + (C - 1) * DK + c] += sm.colk[c] + dgC[cidx * DK + c] * gl;
-  }
-}
 
-// dq, dk (bf16 token-major) = elementwise + gated parts; dg = reverse cumsum
-// over the chunk of dgamma (fp32 token-major); one thread per (chunk, channel)
-__global__ void kda_finish_kernel(const float* __restrict__ dQe, const float* __restrict__ dKe,
-                                  const float* __restrict__ dGe, const float* __restrict__ dQg,
-                                  const float* __restrict__ dKg, const float* __restrict__ dGg,
-                                  __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk,
-                                  float* __restrict__ dg, int L, int H, int N, int DK) {
-  const long long cidx = blockIdx.x;                        // (b * H + h) * N + n
-  const int c = threadIdx.x;
-  if (c >= DK) return;
-  const long long bh = cidx / N, n = cidx % N;
-  const long long b = bh / H, h = bh % H;
-  const long long tok0 = b * L + n * C;
-  const long long base = cidx * C * DK + c;
-  float run = 0.f;
-  for (int i = C - 1; i >= 0; --i) {
-    const long long o = base + (long long)i * DK;
-    const long long t = ((tok0 + i) * H + h) * DK + c;
-    run += dGe[o] + dGg[o];
-    dg[t] = run;
-    dq[t] = f2bf(dQe[o] + dQg[o]);
-    dk[t] = f2bf(dKe[o] + dKg[o]);
+  // ---- the gated products' backward
+  // bf16 dAqk / dAkk over T / dT; factorised operands; the last row's extra
+  // dgamma terms (column sums, dgC G_C) folded into colk
+  for (int idx = tid; idx < C * C / 2; idx += THREADS) {
+    const int i = idx / (C / 2), j = (idx % (C / 2)) * 2;
+    *reinterpret_cast<uint32_t*>(&sm.Tb[i][j]) = pack_bf16x2(sm.Aqk[i][j], sm.Aqk[i][j + 1]);
+    *reinterpret_cast<uint32_t*>(&sm.DT[i][j]) = pack_bf16x2(sm.M[i][j], sm.M[i][j + 1]);
+  }
+  for (int c = tid; c < DK; c += THREADS) sm.colk[c] += dgC[cidx * DK + c] * __expf(sm.gam[C - 1][c]);
+  __nv_bfloat16 (*Kr)[DK + PAD] = sm.Kr();
+  __nv_bfloat16 (*Qc)[DK + PAD] = sm.Qc();
+  __nv_bfloat16 (*Kc)[DK + PAD] = sm.Kc();
+  for (int idx = tid; idx < S::RK * DK / 2; idx += THREADS) {
+    const int row = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
+    // Kr: block I (rows kr_off(I).. of 16 I) = K[t] o e^(gamma_r - gamma_t), r = 16 I - 1
+    const int I = row < 16 ? 1 : (row < 48 ? 2 : 3);
+    const int t = row - kr_off(I), r = 16 * I - 1;
+    const float2 gr = *reinterpret_cast<const float2*>(&sm.gam[r][c]);
+    const float2 gt = *reinterpret_cast<const float2*>(&sm.gam[t][c]);
+    const float2 kt = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[t][c]));
+    *reinterpret_cast<uint32_t*>(&Kr[row][c]) =
+        pack_bf16x2(kt.x * __expf(gr.x - gt.x), kt.y * __expf(gr.y - gt.y));
+    // Qc / Kc: block J (rows qc_off(J).. of 48 - 16 J) = X[u] o e^(gamma_u - gamma_r), u > r = 16 J + 15
+    const int J = row < 48 ? 0 : (row < 80 ? 1 : 2);
+    const int u = 16 * (J + 1) + row - qc_off(J), rj = 16 * J + 15;
+    const float2 gj = *reinterpret_cast<const float2*>(&sm.gam[rj][c]);
+    const float2 gu = *reinterpret_cast<const float2*>(&sm.gam[u][c]);
+    const float2 qu = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[u][c]));
+    const float2 ku = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[u][c]));
+    const float e0 = __expf(gu.x - gj.x), e1 = __expf(gu.y - gj.y);
+    *reinterpret_cast<uint32_t*>(&Qc[row][c]) = pack_bf16x2(qu.x * e0, qu.y * e1);
+    *reinterpret_cast<uint32_t*>(&Kc[row][c]) = pack_bf16x2(ku.x * e0, ku.y * e1);
+  }
+  __syncthreads();
+  const int blk = warp & 3;
+  if (blk >= 1) {
+    // row role of block blk over keys [0, 16 blk), through r = 16 blk - 1
+    float x1[1][NTK][4], x2[1][NTK][4];
+    zero(x1);
+    zero(x2);
+    warp_mma<1, NTK, false, true>(x1, &sm.Tb[0][0], C + PAD, &Kr[kr_off(blk)][0], DK + PAD, m0, c0, 16 * blk);
+    warp_mma<1, NTK, false, true>(x2, &sm.DT[0][0], C + PAD, &Kr[kr_off(blk)][0], DK + PAD, m0, c0, 16 * blk);
+    const int r = 16 * blk - 1;
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        const float f = __expf(sm.gam[i][c] - sm.gam[r][c]);
+        const float a = x1[0][nt][e] * f, bk = x2[0][nt][e] * f;
+        Rq[nt][e] += a;
+        Rk[nt][e] += bk;
+        Rg[nt][e] += bf2f(sm.Q[i][c]) * a + bf2f(sm.K[i][c]) * bk;
+      }
+  }
+  if (blk <= 2) {
+    // column role of block blk over rows [16 (blk + 1), 64), through r = 16 blk + 15
+    float x3[1][NTK][4];
+    zero(x3);
+    const int kk = C - 16 * (blk + 1);
+    warp_mma<1, NTK, true, true>(x3, &sm.Tb[16 * (blk + 1)][16 * blk], C + PAD, &Qc[qc_off(blk)][0], DK + PAD, 0, c0,
+                                 kk);
+    warp_mma<1, NTK, true, true>(x3, &sm.DT[16 * (blk + 1)][16 * blk], C + PAD, &Kc[qc_off(blk)][0], DK + PAD, 0, c0,
+                                 kk);
+    const int r = 16 * blk + 15;
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int j = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+        const float x = x3[0][nt][e] * __expf(sm.gam[r][c] - sm.gam[j][c]);
+        Rk[nt][e] += x;
+        Rg[nt][e] -= bf2f(sm.K[j][c]) * x;
+      }
+  }
+  // inside the 16-token block: elementwise decay, two channels at a time
+  {
+    const int b0 = 16 * blk;
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int hr = 0; hr < 2; ++hr) {
+        const int i = m0 + frag_row(0, 2 * hr), c = c0 + frag_col(nt, 0);
+        const float2 gi = *reinterpret_cast<const float2*>(&sm.gam[i][c]);
+        float2 rq = make_float2(0.f, 0.f), rk = make_float2(0.f, 0.f), cl = make_float2(0.f, 0.f);
+        for (int j = b0; j <= i; ++j) {              // row role: keys j <= i of the block
+          const float2 gj = *reinterpret_cast<const float2*>(&sm.gam[j][c]);
+          const float2 kj = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[j][c]));
+          const float e0 = __expf(gi.x - gj.x) * kj.x, e1 = __expf(gi.y - gj.y) * kj.y;
+          const float aq = sm.Aqk[i][j], ak = sm.M[i][j];
+          rq.x = fmaf(aq, e0, rq.x); rq.y = fmaf(aq, e1, rq.y);
+          rk.x = fmaf(ak, e0, rk.x); rk.y = fmaf(ak, e1, rk.y);
+        }
+        for (int u = i; u < b0 + BLK; ++u) {         // column role: rows u >= i of the block
+          const float2 gu = *reinterpret_cast<const float2*>(&sm.gam[u][c]);
+          const float2 qu = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[u][c]));
+          const float2 ku = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[u][c]));
+          const float aq = sm.Aqk[u][i], ak = sm.M[u][i];
+          const float e0 = __expf(gu.x - gi.x), e1 = __expf(gu.y - gi.y);
+          cl.x = fmaf(fmaf(aq, qu.x, ak * ku.x), e0, cl.x);
+          cl.y = fmaf(fmaf(aq, qu.y, ak * ku.y), e1, cl.y);
+        }
+        const float2 qi = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[i][c]));
+        const float2 ki = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
+        Rq[nt][2 * hr] += rq.x;
+        Rq[nt][2 * hr + 1] += rq.y;
+        Rk[nt][2 * hr] += rk.x + cl.x;
+        Rk[nt][2 * hr + 1] += rk.y + cl.y;
+        Rg[nt][2 * hr] += qi.x * rq.x + ki.x * (rk.x - cl.x);
+        Rg[nt][2 * hr + 1] += qi.y * rq.y + ki.y * (rk.y - cl.y);
+      }
+  }
+  __syncthreads();                                   // gamma, Q, K read by every warp: gamma becomes dgamma
+#pragma unroll
+  for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
+      const long long t = ((tok0 + i) * H + h) * DK + c;
+      *reinterpret_cast<uint32_t*>(dq + t) = pack_bf16x2(Rq[nt][e], Rq[nt][e + 1]);
+      *reinterpret_cast<uint32_t*>(dk + t) = pack_bf16x2(Rk[nt][e], Rk[nt][e + 1]);
+      *reinterpret_cast<float2*>(&sm.gam[i][c]) = make_float2(Rg[nt][e], Rg[nt][e + 1]);
+    }
+  __syncthreads();
+  // dg = reverse cumsum of dgamma over the chunk (the last row with its extra terms)
+  for (int c = tid; c < DK; c += THREADS) {
+    float run = sm.colk[c];
+    for (int i = C - 1; i >= 0; --i) {
+      run += sm.gam[i][c];
+      dg[((tok0 + i) * H + h) * DK + c] = run;
+    }
   }
 }
 
@@ -536,8 +672,8 @@ static int launch_kda_bwd(const KdaIntraBwdArgs& a, cudaStream_t st) {
   kda_intra_bwd_kernel<DK, DV><<<grid, THREADS, smem, st>>>(
       (const __nv_bfloat16*)a.q, (const __nv_bfloat16*)a.k, (const __nv_bfloat16*)a.v, a.g, a.beta,
       (const __nv_bfloat16*)a.dW, (const __nv_bfloat16*)a.dQh, (const __nv_bfloat16*)a.dKt, a.dA,
-      (const __nv_bfloat16*)a.dU, a.dgC, (__nv_bfloat16*)a.dv, a.dbeta, a.Qf, a.Kf, a.Gf, a.dAqk, a.dAkk, a.dQe,
-      a.dKe, a.dGe, a.L, a.H, a.scale);
+      (const __nv_bfloat16*)a.dU, a.dgC, (__nv_bfloat16*)a.dq, (__nv_bfloat16*)a.dk, (__nv_bfloat16*)a.dv, a.dg,
+      a.dbeta, a.L, a.H, a.scale);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -577,12 +713,7 @@ int kda_intra_bwd(const KdaIntraBwdArgs& a, cudaStream_t st) {
   if (a.DK == 128 && a.DV == 128) rc = launch_kda_bwd<128, 128>(a, st);
   else if (a.DK == 128 && a.DV == 256) rc = launch_kda_bwd<128, 256>(a, st);
   if (rc) return rc;
-  const long long chunks = (long long)a.B * a.H * (a.L / C);
-  if ((rc = kda_gated_bwd(a.Qf, a.Kf, a.Gf, a.dAqk, a.dAkk, a.dQg, a.dKg, a.dGg, chunks, a.DK, st)) != 0) return rc;
-  kda_finish_kernel<<<static_cast<unsigned>(chunks), a.DK, 0, st>>>(a.dQe, a.dKe, a.dGe, a.dQg, a.dKg, a.dGg,
-                                                                     (__nv_bfloat16*)a.dq, (__nv_bfloat16*)a.dk,
-                                                                     a.dg, a.L, a.H, a.L / C, a.DK);
-  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  return 0;
 }
 
 }  // namespace vagus

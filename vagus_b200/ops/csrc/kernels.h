@@ -156,9 +156,6 @@ struct KdaIntraBwdArgs {
   const float *dA, *dgC;                  // (BH, N, 64, 64), (BH, N, DK) fp32
   void *dq, *dk, *dv;                     // token-major bf16
   float *dg, *dbeta;                      // token-major fp32
-  // chunk-major fp32 work buffers, (BH, N, 64, DK) unless noted
-  float *Qf, *Kf, *Gf, *dQe, *dKe, *dGe, *dQg, *dKg, *dGg;
-  float *dAqk, *dAkk;                     // (BH, N, 64, 64)
   int B, L, H, DK, DV;
   float scale;
 };
