@@ -39,7 +39,9 @@ class _Attn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, do):
         q, k, v, o, lse = ctx.saved_tensors
-        dq, dk, dv = native().attn_bwd(q, k, v, o, lse, do.contiguous(), ctx.causal, 1.0 / math.sqrt(q.shape[-1]))
+        # dO arrives in o's (token-major) layout from the head concat; the
+        # gradients leave in the layouts of q, k, v: no transposing copies
+        dq, dk, dv = native().attn_bwd(q, k, v, o, lse, do, ctx.causal, 1.0 / math.sqrt(q.shape[-1]))
         return dq, dk, dv, None
 
 

@@ -762,15 +762,15 @@ attn_bwd_kernel(const AttnBwdArgs a) {
   }
   cp_wait_all();                                       // K / V copies (no query block ran)
   // dK (scaled), dV out
-  __nv_bfloat16* dKg = reinterpret_cast<__nv_bfloat16*>(a.dk) + ((long long)b * f.Hk + hk) * f.Lk * D;
-  __nv_bfloat16* dVg = reinterpret_cast<__nv_bfloat16*>(a.dv) + ((long long)b * f.Hk + hk) * f.Lk * DV;
+  __nv_bfloat16* dKg = reinterpret_cast<__nv_bfloat16*>(a.dk) + b * a.sdk_b + hk * a.sdk_h;
+  __nv_bfloat16* dVg = reinterpret_cast<__nv_bfloat16*>(a.dv) + b * a.sdv_b + hk * a.sdv_h;
 #pragma unroll
   for (int nt = 0; nt < NK; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       const int r = sm0 + frag_row(0, e), c = (warp >> 2) * (D / 2) + frag_col(nt, e);
       if (k0 + r < f.Lk)
-        *reinterpret_cast<uint32_t*>(dKg + (long long)(k0 + r) * D + c) =
+        *reinterpret_cast<uint32_t*>(dKg + (long long)(k0 + r) * a.sdk_l + c) =
             pack_bf16x2(f.scale * dk[0][nt][e], f.scale * dk[0][nt][e + 1]);
     }
 #pragma unroll
@@ -779,16 +779,22 @@ attn_bwd_kernel(const AttnBwdArgs a) {
     for (int e = 0; e < 4; e += 2) {
       const int r = sm0 + frag_row(0, e), c = (warp >> 2) * (DV / 2) + frag_col(nt, e);
       if (k0 + r < f.Lk)
-        *reinterpret_cast<uint32_t*>(dVg + (long long)(k0 + r) * DV + c) = pack_bf16x2(dv[0][nt][e], dv[0][nt][e + 1]);
+        *reinterpret_cast<uint32_t*>(dVg + (long long)(k0 + r) * a.sdv_l + c) = pack_bf16x2(dv[0][nt][e], dv[0][nt][e + 1]);
     }
 }
 
-// dq = scale * dq_acc (bf16)
-__global__ void attn_bwd_post(const float* __restrict__ acc, __nv_bfloat16* __restrict__ dq, long long n, float scale) {
+// dq = scale * dq_acc (bf16), dq_acc (B * H, Lq, D) contiguous into dq's strides
+__global__ void attn_bwd_post(const AttnBwdArgs a) {
   const long long i = ((long long)blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  const int D = a.f.D;
+  const long long n = a.f.B * a.f.H * a.f.Lq * D;
   if (i >= n) return;
-  const float4 v = *reinterpret_cast<const float4*>(acc + i);
-  *reinterpret_cast<uint2*>(dq + i) = make_uint2(pack_bf16x2(scale * v.x, scale * v.y), pack_bf16x2(scale * v.z, scale * v.w));
+  const long long row = i / D, bh = row / a.f.Lq;
+  const long long d = i - row * D, l = row - bh * a.f.Lq, b = bh / a.f.H, h = bh - b * a.f.H;
+  const float4 v = *reinterpret_cast<const float4*>(a.dq_acc + i);
+  const float sc = a.f.scale;
+  *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(a.dq) + b * a.sdq_b + h * a.sdq_h + l * a.sdq_l + d) =
+      make_uint2(pack_bf16x2(sc * v.x, sc * v.y), pack_bf16x2(sc * v.z, sc * v.w));
 }
 
 // ----------------------------------------------------- tcgen05 backward --
@@ -844,6 +850,7 @@ struct Params {
   float* dq_acc;
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
+  long long sdk_b, sdk_h, sdk_l, sdv_b, sdv_h, sdv_l;   // element strides of dk / dv
   int* err;
   unsigned long long* trace;   // phase clock of CTA (0, 0), [step][16]; null: off
 };
@@ -1169,7 +1176,8 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     if (have) tc_fence_after();
 #pragma unroll
     for (int which = 0; which < 2; ++which) {
-      __nv_bfloat16* out = (which == 0 ? p.dk : p.dv) + (((long long)b * p.Hk + hk) * p.Lk) * D;
+      __nv_bfloat16* out = which == 0 ? p.dk + b * p.sdk_b + hk * p.sdk_h : p.dv + b * p.sdv_b + hk * p.sdv_h;
+      const long long s_l = which == 0 ? p.sdk_l : p.sdv_l;
       const uint32_t base = which == 0 ? Lt::C_DK : Lt::C_DV;
       const float sc = which == 0 ? p.scale : 1.f;
 #pragma unroll
@@ -1184,7 +1192,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           for (int e = 0; e < 32; ++e) r[e] = 0u;
         }
         if (kj < p.Lk) {
-          __nv_bfloat16* dst = out + (long long)kj * D + col;
+          __nv_bfloat16* dst = out + (long long)kj * s_l + col;
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             const float* f = reinterpret_cast<const float*>(&r[e]);
@@ -1297,6 +1305,8 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
   p.sl2 = f.scale * kLog2e; p.scale = f.scale;
   p.lse = f.lse; p.delta = a.delta; p.dq_acc = a.dq_acc;
   p.dk = (__nv_bfloat16*)a.dk; p.dv = (__nv_bfloat16*)a.dv; p.err = f.err;
+  p.sdk_b = a.sdk_b; p.sdk_h = a.sdk_h; p.sdk_l = a.sdk_l;
+  p.sdv_b = a.sdv_b; p.sdv_h = a.sdv_h; p.sdv_l = a.sdv_l;
   p.trace = g_attn_trace;
   static bool attr_set[64] = {};
   auto kern = attn_bwd_tc<D>;
@@ -1316,8 +1326,7 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
                                                *reinterpret_cast<const CUtensorMap*>(mdo),
                                                *reinterpret_cast<const CUtensorMap*>(mdq), p);
   const long long n = rows * D;
-  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a.dq_acc, (__nv_bfloat16*)a.dq, n,
-                                                                              f.scale);
+  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -1330,8 +1339,7 @@ int launch_bwd(const AttnBwdArgs& a, cudaStream_t st) {
   dim3 grid(static_cast<unsigned>((a.f.Lk + BKEYS - 1) / BKEYS), static_cast<unsigned>(a.f.B * a.f.Hk));
   attn_bwd_kernel<D, DV><<<grid, BWARPS * 32, sm, st>>>(a);
   const long long n = rows * a.f.D;
-  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a.dq_acc, (__nv_bfloat16*)a.dq, n,
-                                                                              a.f.scale);
+  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -1363,6 +1371,11 @@ void attn_set_trace(unsigned long long* buf) { g_attn_trace = buf; }
 
 int attn_bwd(const AttnBwdArgs& a, cudaStream_t st) {
   if (!strides_ok(a.f) || !aligned16(a.dO) || a.f.Lq <= 0 || a.f.Lk <= 0) return 5;
+  // gradient outputs: 16-byte aligned rows (8-element strides) for the vector stores
+  const long long gs[] = {a.sdq_b, a.sdq_h, a.sdq_l, a.sdk_b, a.sdk_h, a.sdk_l, a.sdv_b, a.sdv_h, a.sdv_l};
+  for (long long x : gs)
+    if (x % 8) return 5;
+  if (!aligned16(a.dq) || !aligned16(a.dk) || !aligned16(a.dv)) return 5;
   static const bool no_tc = std::getenv("VAGUS_ATTN_NO_TC") != nullptr;
   if (!no_tc && a.f.err && a.f.Lq >= 128 && a.f.Lk >= 128 && a.f.D == a.f.Dv && (a.f.D == 64 || a.f.D == 128))
     return a.f.D == 64 ? launch_bwd_tc<64>(a, st) : launch_bwd_tc<128>(a, st);

@@ -38,25 +38,45 @@ vagus::AttnArgs make_args(const Tensor& q, const Tensor& k, const Tensor& v, con
 }
 
 // q (B, H, Lq, D), k (B, Hk, Lk, D), v (B, Hk, Lk, Dv) -> o (B, H, Lq, Dv), lse (B, H, Lq)
+// o is token-major underneath, (B, Lq, H, Dv) viewed as (B, H, Lq, Dv): the
+// head concat that follows (transpose + reshape to (B, Lq, H Dv)) is a view
 std::vector<Tensor> attn_fwd(Tensor q, Tensor k, Tensor v, bool causal, double scale) {
-  auto o = torch::empty({q.size(0), q.size(1), q.size(2), v.size(3)}, q.options());
+  auto o = torch::empty({q.size(0), q.size(2), q.size(1), v.size(3)}, q.options()).transpose(1, 2);
   auto lse = torch::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat));
   auto a = make_args(q, k, v, o, lse, causal, scale);
   check(vagus::attn_fwd(a, stream()), "attn_fwd");
   return {o, lse};
 }
 
-// o and dO contiguous (as attn_fwd returns them) -> dq, dk, dv contiguous
+// A gradient in the layout of x where that layout is dense with 8-element
+// strides (so the gradient flows back through x's views without a copy),
+// else contiguous.
+Tensor grad_like(const Tensor& x) {
+  auto t = torch::empty_like(x);
+  bool ok = t.stride(3) == 1;
+  for (int d = 0; d < 3; ++d) ok = ok && t.stride(d) % 8 == 0;
+  return ok ? t : torch::empty(x.sizes(), x.options());
+}
+
+// dO in o's layout (copied into it when the strides differ) -> dq, dk, dv in
+// the layouts of q, k, v
 std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, Tensor dO, bool causal,
                              double scale) {
-  TORCH_CHECK(o.is_contiguous() && dO.is_contiguous() && lse.is_contiguous(), "attn_bwd: contiguous o, dO, lse");
+  TORCH_CHECK(lse.is_contiguous() && dO.sizes() == o.sizes(), "attn_bwd: contiguous lse, dO shaped like o");
+  if (dO.strides() != o.strides()) {
+    auto t = torch::empty_like(o);
+    t.copy_(dO);
+    dO = t;
+  }
+  TORCH_CHECK(dO.strides() == o.strides(), "attn_bwd: o must be dense (dO takes its strides)");
   auto a = make_args(q, k, v, o, lse, causal, scale);
   vagus::AttnBwdArgs b;
   b.f = a;
   b.dO = dO.data_ptr();
-  auto dq = torch::empty({q.size(0), q.size(1), q.size(2), q.size(3)}, q.options());
-  auto dk = torch::empty({k.size(0), k.size(1), k.size(2), k.size(3)}, k.options());
-  auto dv = torch::empty({v.size(0), v.size(1), v.size(2), v.size(3)}, v.options());
+  auto dq = grad_like(q), dk = grad_like(k), dv = grad_like(v);
+  b.sdq_b = dq.stride(0); b.sdq_h = dq.stride(1); b.sdq_l = dq.stride(2);
+  b.sdk_b = dk.stride(0); b.sdk_h = dk.stride(1); b.sdk_l = dk.stride(2);
+  b.sdv_b = dv.stride(0); b.sdv_h = dv.stride(1); b.sdv_l = dv.stride(2);
   auto dq_acc = torch::empty({q.size(0), q.size(1), q.size(2), q.size(3)}, q.options().dtype(at::kFloat));
   auto delta = torch::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat));
   b.dq = dq.data_ptr(); b.dk = dk.data_ptr(); b.dv = dv.data_ptr();

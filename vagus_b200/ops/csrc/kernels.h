@@ -125,7 +125,8 @@ int attn_fwd(const AttnArgs& a, cudaStream_t st);
 struct AttnBwdArgs {
   AttnArgs f;
   const void* dO;            // like o (same strides)
-  void* dq; void* dk; void* dv;   // contiguous (B, H, Lq, D), (B, Hk, Lk, D), (B, Hk, Lk, Dv) bf16
+  void* dq; void* dk; void* dv;   // (B, H, Lq, D), (B, Hk, Lk, D), (B, Hk, Lk, Dv) bf16, strided:
+  long long sdq_b, sdq_h, sdq_l, sdk_b, sdk_h, sdk_l, sdv_b, sdv_h, sdv_l;   // element strides (unit inner)
   float* dq_acc;             // fp32 scratch (B, H, Lq, D)
   float* delta;              // fp32 scratch (B, H, Lq)
 };
