@@ -45,12 +45,13 @@ using wy::tri_inverse_inplace;
 constexpr int C = 64;
 constexpr int BLK = 16;
 constexpr int THREADS = 256;
+constexpr int GP = 4;                    // fp32 padding of the gamma rows: rows 8 apart share a bank, not all
 
 template <int DK, int DV>
 struct KdaFwdSmem {
   __nv_bfloat16 Q[C][DK + PAD];
   __nv_bfloat16 K[C][DK + PAD];          // K, then diag(b) (K o G)
-  float gam[C][DK];                      // cumulative log decay per channel
+  float gam[C][DK + GP];                 // cumulative log decay per channel
   __nv_bfloat16 R[BLK][DK + PAD];        // K_J o exp(r_J - gamma_J)
   __nv_bfloat16 P[6][BLK][DK + PAD];     // Q_I / K_I o exp(gamma_I - r_J), I = J+1..3
   float Aqk[C][C + 1];
@@ -62,7 +63,7 @@ struct KdaFwdSmem {
 
 // g (token-major, this chunk's rows) -> gam = per-channel inclusive prefix sum
 template <int DK>
-__device__ __forceinline__ void load_cumsum(float (*gam)[DK], const float* g, long long gld) {
+__device__ __forceinline__ void load_cumsum(float (*gam)[DK + GP], const float* g, long long gld) {
   for (int idx = threadIdx.x; idx < C * DK / 4; idx += THREADS) {
     const int i = idx / (DK / 4), c = (idx % (DK / 4)) * 4;
     *reinterpret_cast<float4*>(&gam[i][c]) = *reinterpret_cast<const float4*>(g + i * gld + c);
@@ -83,7 +84,7 @@ template <int DK>
 struct GatedView {
   __nv_bfloat16 (*Q)[DK + PAD];
   __nv_bfloat16 (*K)[DK + PAD];
-  float (*gam)[DK];
+  float (*gam)[DK + GP];
   __nv_bfloat16 (*R)[DK + PAD];          // [BLK] rows
   __nv_bfloat16 (*P)[BLK][DK + PAD];     // [6] tiles
   float (*Aqk)[C + 1];
@@ -274,7 +275,7 @@ struct KdaBwdSmem {
   static constexpr int RK = 96;          // rows of the factorised operands: 16 + 32 + 48
   __nv_bfloat16 Q[C][DK + PAD];
   __nv_bfloat16 K[C][DK + PAD];
-  float gam[C][DK];                      // cumulative log decay; dgamma at the end
+  float gam[C][DK + GP];                 // cumulative log decay; dgamma at the end
   // scratch A: the products' R / P tiles; then XW = diag(b) (K o G) and the dW
   // tile (later T^T dT); then Kr = the row-role key operands
   static constexpr int PR_BYTES = (1 + 6) * BLK * (DK + PAD) * 2;
@@ -595,55 +596,78 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
         Rg[nt][e] -= bf2f(sm.K[j][c]) * x;
       }
   }
-  // inside the 16-token block: elementwise decay, two channels at a time
-  {
-    const int b0 = 16 * blk;
+  // inside the 16-token blocks, one thread per (block, channel): the block's
+  // Q, K, gamma of that channel in registers, each pair's decay computed once
+  // for all three sums; the fragment-layout parts meet them in shared memory
+  // (dq, dk parts over the now free operand scratch, dgamma over gamma)
+  constexpr int SP = DK + GP;
+  constexpr int NI = 4 * DK / THREADS;                 // (block, channel) items per thread
+  float (*Sq)[SP] = reinterpret_cast<float (*)[SP]>(sm.scratch);
+  float (*Sk)[SP] = reinterpret_cast<float (*)[SP]>(sm.scratch2);
+  static_assert(sizeof(sm.scratch) >= sizeof(float) * C * SP && sizeof(sm.scratch2) >= sizeof(float) * C * SP,
+                "dq / dk staging");
+  const int ic = tid % DK;
+  float gl[NI][BLK];                                   // gamma of the items' rows, log2 units
+  __syncthreads();                                     // off-diagonal products done: operand scratch free
 #pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
+  for (int it = 0; it < NI; ++it) {
+    const int b0 = BLK * (tid / DK + it * (THREADS / DK));
 #pragma unroll
-      for (int hr = 0; hr < 2; ++hr) {
-        const int i = m0 + frag_row(0, 2 * hr), c = c0 + frag_col(nt, 0);
-        const float2 gi = *reinterpret_cast<const float2*>(&sm.gam[i][c]);
-        float2 rq = make_float2(0.f, 0.f), rk = make_float2(0.f, 0.f), cl = make_float2(0.f, 0.f);
-        for (int j = b0; j <= i; ++j) {              // row role: keys j <= i of the block
-          const float2 gj = *reinterpret_cast<const float2*>(&sm.gam[j][c]);
-          const float2 kj = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[j][c]));
-          const float e0 = __expf(gi.x - gj.x) * kj.x, e1 = __expf(gi.y - gj.y) * kj.y;
-          const float aq = sm.Aqk[i][j], ak = sm.M[i][j];
-          rq.x = fmaf(aq, e0, rq.x); rq.y = fmaf(aq, e1, rq.y);
-          rk.x = fmaf(ak, e0, rk.x); rk.y = fmaf(ak, e1, rk.y);
-        }
-        for (int u = i; u < b0 + BLK; ++u) {         // column role: rows u >= i of the block
-          const float2 gu = *reinterpret_cast<const float2*>(&sm.gam[u][c]);
-          const float2 qu = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[u][c]));
-          const float2 ku = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[u][c]));
-          const float aq = sm.Aqk[u][i], ak = sm.M[u][i];
-          const float e0 = __expf(gu.x - gi.x), e1 = __expf(gu.y - gi.y);
-          cl.x = fmaf(fmaf(aq, qu.x, ak * ku.x), e0, cl.x);
-          cl.y = fmaf(fmaf(aq, qu.y, ak * ku.y), e1, cl.y);
-        }
-        const float2 qi = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[i][c]));
-        const float2 ki = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[i][c]));
-        Rq[nt][2 * hr] += rq.x;
-        Rq[nt][2 * hr + 1] += rq.y;
-        Rk[nt][2 * hr] += rk.x + cl.x;
-        Rk[nt][2 * hr + 1] += rk.y + cl.y;
-        Rg[nt][2 * hr] += qi.x * rq.x + ki.x * (rk.x - cl.x);
-        Rg[nt][2 * hr + 1] += qi.y * rq.y + ki.y * (rk.y - cl.y);
-      }
+    for (int i = 0; i < BLK; ++i) gl[it][i] = sm.gam[b0 + i][ic] * 1.4426950408889634f;
   }
-  __syncthreads();                                   // gamma, Q, K read by every warp: gamma becomes dgamma
 #pragma unroll
   for (int nt = 0; nt < NTK; ++nt)
 #pragma unroll
     for (int e = 0; e < 4; e += 2) {
       const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
-      const long long t = ((tok0 + i) * H + h) * DK + c;
-      *reinterpret_cast<uint32_t*>(dq + t) = pack_bf16x2(Rq[nt][e], Rq[nt][e + 1]);
-      *reinterpret_cast<uint32_t*>(dk + t) = pack_bf16x2(Rk[nt][e], Rk[nt][e + 1]);
+      *reinterpret_cast<float2*>(&Sq[i][c]) = make_float2(Rq[nt][e], Rq[nt][e + 1]);
+      *reinterpret_cast<float2*>(&Sk[i][c]) = make_float2(Rk[nt][e], Rk[nt][e + 1]);
+    }
+  __syncthreads();                                     // gamma read by every item: it becomes dgamma
+#pragma unroll
+  for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; e += 2) {
+      const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
       *reinterpret_cast<float2*>(&sm.gam[i][c]) = make_float2(Rg[nt][e], Rg[nt][e + 1]);
     }
   __syncthreads();
+#pragma unroll
+  for (int it = 0; it < NI; ++it) {
+    const int b0 = BLK * (tid / DK + it * (THREADS / DK));
+    float qv[BLK], kv[BLK], rq[BLK], rk[BLK], cl[BLK];
+#pragma unroll
+    for (int i = 0; i < BLK; ++i) {
+      qv[i] = bf2f(sm.Q[b0 + i][ic]);
+      kv[i] = bf2f(sm.K[b0 + i][ic]);
+      rq[i] = rk[i] = cl[i] = 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < BLK; ++i) {
+#pragma unroll
+      for (int j = 0; j <= i; ++j) {
+        const float aq = sm.Aqk[b0 + i][b0 + j], ak = sm.M[b0 + i][b0 + j];   // one address per warp
+        const float e = j == i ? 1.f : ex2_approx(gl[it][i] - gl[it][j]);
+        const float t = kv[j] * e;
+        rq[i] = fmaf(aq, t, rq[i]);
+        rk[i] = fmaf(ak, t, rk[i]);                    // dAkk is zero on the diagonal
+        cl[j] = fmaf(fmaf(aq, qv[i], ak * kv[i]), e, cl[j]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < BLK; ++i) {
+      Sq[b0 + i][ic] += rq[i];
+      Sk[b0 + i][ic] += rk[i] + cl[i];
+      sm.gam[b0 + i][ic] += qv[i] * rq[i] + kv[i] * (rk[i] - cl[i]);
+    }
+  }
+  __syncthreads();
+  for (int idx = tid; idx < C * DK / 2; idx += THREADS) {
+    const int i = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
+    const long long t = ((tok0 + i) * H + h) * DK + c;
+    *reinterpret_cast<uint32_t*>(dq + t) = pack_bf16x2(Sq[i][c], Sq[i][c + 1]);
+    *reinterpret_cast<uint32_t*>(dk + t) = pack_bf16x2(Sk[i][c], Sk[i][c + 1]);
+  }
   // dg = reverse cumsum of dgamma over the chunk (the last row with its extra terms)
   for (int c = tid; c < DK; c += THREADS) {
     float run = sm.colk[c];
