@@ -336,4 +336,9 @@ void register_seq_ops(pybind11::module& m) {
   m.def("gdr_intra_bwd", &gdr_intra_bwd);
   m.def("kda_intra_fwd", &kda_intra_fwd);
   m.def("kda_intra_bwd", &kda_intra_bwd);
+  // buf: int64 device tensor of 32 entries, or None
+  m.def("kda_set_trace", [](c10::optional<Tensor> buf) {
+    if (buf) TORCH_CHECK(buf->is_cuda() && buf->numel() >= 32 && buf->element_size() == 8, "kda_set_trace: 32 x u64");
+    vagus::kda_set_trace(buf ? reinterpret_cast<unsigned long long*>(buf->data_ptr()) : nullptr);
+  });
 }

@@ -47,6 +47,14 @@ constexpr int BLK = 16;
 constexpr int THREADS = 256;
 constexpr int GP = 4;                    // fp32 padding of the gamma rows: rows 8 apart share a bank, not all
 
+// Phase clock of CTA (0, 0, 0): clock64() at phase boundaries into
+// trace[event] (forward events 0..15, backward 16..31); null: off.
+#define KDA_TR(ev)                                                                                     \
+  do {                                                                                                 \
+    if (trace != nullptr && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0) \
+      trace[ev] = clock64();                                                                           \
+  } while (0)
+
 template <int DK, int DV>
 struct KdaFwdSmem {
   __nv_bfloat16 Q[C][DK + PAD];
@@ -94,34 +102,51 @@ struct GatedView {
 // The gated products of the chunk into Aqk (lower, diagonal included) and
 // Akk (strictly lower, into M), both zero above.
 template <int DK>
-__device__ __forceinline__ void gated_products(const GatedView<DK>& sm) {
+__device__ __forceinline__ void gated_products(const GatedView<DK>& sm, unsigned long long* trace, int ev) {
   const int warp = threadIdx.x >> 5;
   for (int idx = threadIdx.x; idx < C * C; idx += THREADS) {
     sm.Aqk[idx / C][idx % C] = 0.f;
     sm.M[idx / C][idx % C] = 0.f;
   }
   __syncthreads();
-  // inside the 16-token blocks: elementwise decay
-  for (int it = threadIdx.x; it < 4 * BLK * BLK; it += THREADS) {
-    const int blk = it / (BLK * BLK), i = (it / BLK) % BLK, j = it % BLK;
-    if (j > i) continue;
+  // inside the 16-token blocks: elementwise decay.  Work items are the
+  // blocks' 4 x 136 pairs (j <= i) x two halves of the channels; the halves of
+  // a pair sit on neighbouring lanes and meet through one shuffle
+  constexpr int PAIRS = BLK * (BLK + 1) / 2;
+  constexpr int ITEMS = 4 * PAIRS * 2;
+  for (int base = 0; base < ITEMS; base += THREADS) {
+    const int it = base + threadIdx.x;
+    const bool active = it < ITEMS;
+    const int pr = active ? it >> 1 : 0, hf = it & 1;
+    const int blk = pr / PAIRS, p = pr % PAIRS;
+    int i = static_cast<int>((sqrtf(8.f * p + 1.f) - 1.f) * 0.5f);   // triangular index -> (i, j)
+    while ((i + 1) * (i + 2) / 2 <= p) ++i;
+    while (i * (i + 1) / 2 > p) --i;
+    const int j = p - i * (i + 1) / 2;
     const int ri = blk * BLK + i, rj = blk * BLK + j;
     float aq = 0.f, ak = 0.f;
+    if (active) {
 #pragma unroll 4
-    for (int c = 0; c < DK; c += 2) {
-      const float2 qi = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[ri][c]));
-      const float2 ki = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[ri][c]));
-      const float2 kj = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[rj][c]));
-      const float2 gi = *reinterpret_cast<const float2*>(&sm.gam[ri][c]);
-      const float2 gj = *reinterpret_cast<const float2*>(&sm.gam[rj][c]);
-      const float e0 = __expf(gi.x - gj.x) * kj.x, e1 = __expf(gi.y - gj.y) * kj.y;
-      aq = fmaf(qi.x, e0, fmaf(qi.y, e1, aq));
-      ak = fmaf(ki.x, e0, fmaf(ki.y, e1, ak));
+      for (int c = hf * (DK / 2); c < (hf + 1) * (DK / 2); c += 2) {
+        const float2 qi = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.Q[ri][c]));
+        const float2 ki = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[ri][c]));
+        const float2 kj = unpack_bf16x2(*reinterpret_cast<const uint32_t*>(&sm.K[rj][c]));
+        const float2 gi = *reinterpret_cast<const float2*>(&sm.gam[ri][c]);
+        const float2 gj = *reinterpret_cast<const float2*>(&sm.gam[rj][c]);
+        const float e0 = __expf(gi.x - gj.x) * kj.x, e1 = __expf(gi.y - gj.y) * kj.y;
+        aq = fmaf(qi.x, e0, fmaf(qi.y, e1, aq));
+        ak = fmaf(ki.x, e0, fmaf(ki.y, e1, ak));
+      }
     }
-    sm.Aqk[ri][rj] = aq;
-    if (j < i) sm.M[ri][rj] = ak;
+    aq += __shfl_xor_sync(0xffffffffu, aq, 1);
+    ak += __shfl_xor_sync(0xffffffffu, ak, 1);
+    if (active && hf == 0) {
+      sm.Aqk[ri][rj] = aq;
+      if (j < i) sm.M[ri][rj] = ak;
+    }
   }
   // across blocks: factorised through r_J, on the tensor cores
+  KDA_TR(ev);
   for (int J = 0; J < 3; ++J) {
     __syncthreads();                                   // P / R free
     const int rJ = J * BLK + BLK - 1;
@@ -160,7 +185,7 @@ kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
                      const __nv_bfloat16* __restrict__ v, const float* __restrict__ g,
                      const float* __restrict__ beta, __nv_bfloat16* __restrict__ Wo, __nv_bfloat16* __restrict__ Qho,
                      __nv_bfloat16* __restrict__ Kto, __nv_bfloat16* __restrict__ Ao, __nv_bfloat16* __restrict__ Uo,
-                     float* __restrict__ gCo, int L, int H, float scale) {
+                     float* __restrict__ gCo, int L, int H, float scale, unsigned long long* trace) {
   using S = KdaFwdSmem<DK, DV>;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   S& sm = *reinterpret_cast<S*>(smem_raw);
@@ -168,6 +193,7 @@ kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   const int N = gridDim.x;
   const long long cidx = ((long long)b * H + h) * N + n;
   const long long tok0 = (long long)b * L + (long long)n * C;
+  KDA_TR(0);
   const int warp = threadIdx.x >> 5;
   load_tile(&sm.Q[0][0], DK + PAD, q + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
   load_tile(&sm.K[0][0], DK + PAD, k + (tok0 * H + h) * DK, (long long)H * DK, C, DK);
@@ -177,7 +203,9 @@ kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   load_cumsum<DK>(sm.gam, g + (tok0 * H + h) * DK, (long long)H * DK);
   cp_wait_all();
   __syncthreads();
-  gated_products<DK>(GatedView<DK>{sm.Q, sm.K, sm.gam, sm.R, sm.P, sm.Aqk, sm.M});
+  KDA_TR(1);
+  gated_products<DK>(GatedView<DK>{sm.Q, sm.K, sm.gam, sm.R, sm.P, sm.Aqk, sm.M}, trace, 2);
+  KDA_TR(3);
 
   // A = s Aqk; M = diag(b) Akk -> T
   for (int idx = threadIdx.x; idx < C * C / 2; idx += THREADS) {
@@ -188,6 +216,7 @@ kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   }
   __syncthreads();
   tri_inverse_inplace(sm.M);
+  KDA_TR(4);
   for (int idx = threadIdx.x; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.M[idx / C][idx % C]);
 
   // Qh, Kt, gC out; K -> diag(b) (K o G); V -> diag(b) V
@@ -212,6 +241,7 @@ kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   }
   __syncthreads();
 
+  KDA_TR(5);
   // W = T Xw, U = T Xu: warp tile 16 rows x half of the columns
   const int m0 = (warp & 3) * 16;
   {
@@ -242,6 +272,8 @@ kda_intra_fwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
         *reinterpret_cast<uint32_t*>(Uo + (cidx * C + i) * DV + c) = pack_bf16x2(acc[0][nt][e], acc[0][nt][e + 1]);
       }
   }
+  __syncthreads();
+  KDA_TR(6);
 }
 
 // ---------------------------------------------------------------- backward --
@@ -350,7 +382,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
                      const float* __restrict__ dA, const __nv_bfloat16* __restrict__ dU,
                      const float* __restrict__ dgC, __nv_bfloat16* __restrict__ dq, __nv_bfloat16* __restrict__ dk,
                      __nv_bfloat16* __restrict__ dv, float* __restrict__ dg, float* __restrict__ dbeta, int L, int H,
-                     float scale) {
+                     float scale, unsigned long long* trace) {
   using S = KdaBwdSmem<DK, DV>;
   constexpr int NTK = DK / 16;           // fragment column tiles of a warp's DK / 2 channels
   extern __shared__ __align__(128) uint8_t smem_raw[];
@@ -359,6 +391,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   const int N = gridDim.x;
   const long long cidx = ((long long)b * H + h) * N + n;
   const long long tok0 = (long long)b * L + (long long)n * C;
+  KDA_TR(16);
   const int warp = threadIdx.x >> 5;
   const int tid = threadIdx.x;
   __nv_bfloat16 (*Vs)[DV + PAD] = sm.V();
@@ -376,7 +409,9 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   load_cumsum<DK>(sm.gam, g + (tok0 * H + h) * DK, (long long)H * DK);
   cp_wait_all();
   __syncthreads();
-  gated_products<DK>(GatedView<DK>{sm.Q, sm.K, sm.gam, sm.R(), sm.P(), sm.Aqk, sm.M});
+  KDA_TR(17);
+  gated_products<DK>(GatedView<DK>{sm.Q, sm.K, sm.gam, sm.R(), sm.P(), sm.Aqk, sm.M}, trace, 18);
+  KDA_TR(19);
   __nv_bfloat16 (*XW)[DK + PAD] = sm.XW();
   __nv_bfloat16 (*DWt)[DK + PAD] = sm.DW();
 
@@ -389,6 +424,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   }
   __syncthreads();
   tri_inverse_inplace(sm.M);
+  KDA_TR(20);
   for (int idx = tid; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.M[idx / C][idx % C]);
   // XW = diag(b) (K o G); dW tile
   const long long cbase = cidx * C * DK;
@@ -426,27 +462,49 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
   // the running gradients of this warp's fragment: dq, dk, dgamma
   float Rq[NTK][4], Rk[NTK][4], Rg[NTK][4];
   {
-    // dXw = T^T dW, and every elementwise term of (i, c) in the same pass
+    // dXw = T^T dW, and every elementwise term of (i, c) in the same pass;
+    // dQh / dKt come in as bf16 pairs, all issued before the product
+    uint32_t dqh2[NTK][2], dkt2[NTK][2];
+#pragma unroll
+    for (int nt = 0; nt < NTK; ++nt)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const long long o = cbase + (long long)(m0 + frag_row(0, 2 * r)) * DK + c0 + frag_col(nt, 0);
+        dqh2[nt][r] = __ldg(reinterpret_cast<const unsigned int*>(dQh + o));
+        dkt2[nt][r] = __ldg(reinterpret_cast<const unsigned int*>(dKt + o));
+      }
     float acc[1][NTK][4];
     zero(acc);
     warp_mma<1, NTK, true, true>(acc, &sm.Tb[0][0], C + PAD, &DWt[0][0], DK + PAD, m0, c0, C);
     float part[2] = {0.f, 0.f};
 #pragma unroll
-    for (int nt = 0; nt < NTK; ++nt)
+    for (int nt = 0; nt < NTK; ++nt) {
+      float ck[2] = {0.f, 0.f};                        // this column pair's share of colk
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         const int i = m0 + frag_row(0, e), c = c0 + frag_col(nt, e);
         const float gi = sm.gam[i][c], G = __expf(gi), E = __expf(sm.gam[C - 1][c] - gi);
         const float qv = bf2f(sm.Q[i][c]), kv = bf2f(sm.K[i][c]);
-        const float dqh = bf2f(dQh[cbase + i * DK + c]), dkt = bf2f(dKt[cbase + i * DK + c]);
+        const float2 dq2 = unpack_bf16x2(dqh2[nt][e >> 1]), dk2 = unpack_bf16x2(dkt2[nt][e >> 1]);
+        const float dqh = (e & 1) ? dq2.y : dq2.x, dkt = (e & 1) ? dk2.y : dk2.x;
         const float dxw = acc[0][nt][e], bi = sm.beta[i];
         part[e >> 1] += dxw * kv * G;
         const float kte = dkt * kv * E;
-        atomicAdd(&sm.colk[c], kte);
+        ck[e & 1] += kte;
         Rq[nt][e] = scale * dqh * G;
         Rk[nt][e] = dkt * E + bi * dxw * G;
         Rg[nt][e] = scale * dqh * qv * G - kte + bi * dxw * kv * G;
       }
+      // the warp's 16 rows of the two columns: lanes with equal (lane & 3) hold them
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float v = ck[u];
+        v += __shfl_xor_sync(0xffffffffu, v, 4);
+        v += __shfl_xor_sync(0xffffffffu, v, 8);
+        v += __shfl_xor_sync(0xffffffffu, v, 16);
+        if ((threadIdx.x & 31) < 4) atomicAdd(&sm.colk[c0 + frag_col(nt, u)], v);
+      }
+    }
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       float sum = part[r];
@@ -456,6 +514,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
     }
   }
   __syncthreads();
+  KDA_TR(21);
   // dT = dW XW^T + (dU V^T) diag(b)  (bf16 into DT)
   {
     float a1[1][4][4], a2[1][4][4];
@@ -474,6 +533,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
       }
   }
   __syncthreads();
+  KDA_TR(22);
   // P = T^T dT (bf16, over the dW tile), dM = -strict_lower(P T^T)
   __nv_bfloat16 (*Pb)[DK + PAD] = DWt;
   {
@@ -519,6 +579,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
     }
   }
   __syncthreads();
+  KDA_TR(23);
   if (tid < C) dbeta[(tok0 + tid) * H + h] = sm.rw[tid] + sm.ru[tid] + sm.rm[tid];
 
   // ---- the gated products' backward
@@ -555,6 +616,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
     *reinterpret_cast<uint32_t*>(&Kc[row][c]) = pack_bf16x2(ku.x * e0, ku.y * e1);
   }
   __syncthreads();
+  KDA_TR(24);
   const int blk = warp & 3;
   if (blk >= 1) {
     // row role of block blk over keys [0, 16 blk), through r = 16 blk - 1
@@ -608,6 +670,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
                 "dq / dk staging");
   const int ic = tid % DK;
   float gl[NI][BLK];                                   // gamma of the items' rows, log2 units
+  KDA_TR(25);
   __syncthreads();                                     // off-diagonal products done: operand scratch free
 #pragma unroll
   for (int it = 0; it < NI; ++it) {
@@ -662,6 +725,7 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
     }
   }
   __syncthreads();
+  KDA_TR(26);
   for (int idx = tid; idx < C * DK / 2; idx += THREADS) {
     const int i = idx / (DK / 2), c = (idx % (DK / 2)) * 2;
     const long long t = ((tok0 + i) * H + h) * DK + c;
@@ -676,9 +740,12 @@ kda_intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* _
       dg[((tok0 + i) * H + h) * DK + c] = run;
     }
   }
+  KDA_TR(27);
 }
 
 }  // namespace
+
+unsigned long long* g_kda_trace = nullptr;   // host side of the phase trace (kda_set_trace)
 
 template <int DK, int DV>
 static int launch_kda_bwd(const KdaIntraBwdArgs& a, cudaStream_t st) {
@@ -697,7 +764,7 @@ static int launch_kda_bwd(const KdaIntraBwdArgs& a, cudaStream_t st) {
       (const __nv_bfloat16*)a.q, (const __nv_bfloat16*)a.k, (const __nv_bfloat16*)a.v, a.g, a.beta,
       (const __nv_bfloat16*)a.dW, (const __nv_bfloat16*)a.dQh, (const __nv_bfloat16*)a.dKt, a.dA,
       (const __nv_bfloat16*)a.dU, a.dgC, (__nv_bfloat16*)a.dq, (__nv_bfloat16*)a.dk, (__nv_bfloat16*)a.dv, a.dg,
-      a.dbeta, a.L, a.H, a.scale);
+      a.dbeta, a.L, a.H, a.scale, g_kda_trace);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -718,7 +785,7 @@ static int launch_kda_fwd(const void* q, const void* k, const void* v, const flo
   dim3 grid(static_cast<unsigned>(L / C), static_cast<unsigned>(H), static_cast<unsigned>(B));
   kda_intra_fwd_kernel<DK, DV><<<grid, THREADS, smem, st>>>(
       (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, g, beta, (__nv_bfloat16*)W,
-      (__nv_bfloat16*)Qh, (__nv_bfloat16*)Kt, (__nv_bfloat16*)A, (__nv_bfloat16*)U, gC, L, H, scale);
+      (__nv_bfloat16*)Qh, (__nv_bfloat16*)Kt, (__nv_bfloat16*)A, (__nv_bfloat16*)U, gC, L, H, scale, g_kda_trace);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
@@ -730,6 +797,8 @@ int kda_intra_fwd(const void* q, const void* k, const void* v, const float* g, c
   if (DK == 128 && DV == 256) return launch_kda_fwd<128, 256>(q, k, v, g, beta, W, Qh, Kt, A, U, gC, B, L, H, scale, st);
   return 5;
 }
+
+void kda_set_trace(unsigned long long* buf) { g_kda_trace = buf; }
 
 int kda_intra_bwd(const KdaIntraBwdArgs& a, cudaStream_t st) {
   if (a.L % C) return 5;
