@@ -117,8 +117,8 @@ __device__ __forceinline__ void read_weights(const float* ws, int cl, float (&wr
     for (int j = 0; j < VEC; ++j) wr[i][j] = ws[i * HD + cl + j];
 }
 
-template <int VEC, int K>
-__global__ void __launch_bounds__(THREADS, 2)
+template <int VEC, int K, int MINB>
+__global__ void __launch_bounds__(THREADS, MINB)
 conv_fwd_k(const __nv_bfloat16* __restrict__ x, long long ldx, const float* __restrict__ w,
            __nv_bfloat16* __restrict__ y, float* __restrict__ rnorm, long long L, int D, int l2) {
   constexpr int HD = VEC * 32;
@@ -378,7 +378,7 @@ __device__ __forceinline__ void unpack_row(const uint32_t (&r)[VEC / 2], float (
   }
 }
 
-template <int VEC>
+template <int VEC, int PF>
 __global__ void __launch_bounds__(THREADS, 2)
 conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
                const float* __restrict__ w, const float* __restrict__ rnorm, __nv_bfloat16* __restrict__ dx,
@@ -427,7 +427,6 @@ conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __rest
 #pragma unroll
       for (int j = 0; j < VEC; ++j) dw3[i][j] = 0.f;
     // PF tokens of loads in flight in a register queue (slot 0 = token t)
-    constexpr int PF = 4;
     uint32_t qx[PF][VEC / 2], qg[PF][VEC / 2];
     const long long t_last = min(L, t0 + RUN + K - 1);   // du needed up to here (exclusive)
 #pragma unroll
@@ -551,8 +550,10 @@ int launch_fwd(const void* xp, long long ldx, const float* w, void* y, float* rn
   constexpr int HD = VEC * 32;
   const int smem = HD * K * 4 + (TF + K - 1) * HD * 2;
   dim3 grid(static_cast<unsigned>((L + TF - 1) / TF), D / HD, static_cast<unsigned>(B));
-  conv_fwd_k<VEC, K><<<grid, THREADS, smem, st>>>((const __nv_bfloat16*)xp, ldx, w, (__nv_bfloat16*)y, rnorm, L, D,
-                                                  l2);
+  // three CTAs per SM (registers capped at 80: a few spilled, measured 107 -> 101 us at B = 16): one
+  // CTA's staging loads overlap the others' arithmetic
+  conv_fwd_k<VEC, K, 3><<<grid, THREADS, smem, st>>>((const __nv_bfloat16*)xp, ldx, w, (__nv_bfloat16*)y, rnorm, L, D,
+                                                     l2);
   return 0;
 }
 
@@ -614,12 +615,14 @@ int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w,
     // about two waves of CTAs in flight; each CTA loops over runs of its (batch, head)
     const long long bx = std::max<long long>(1, std::min<long long>(ctas_per_seq, (4LL * sms + seqs - 1) / seqs));
     dim3 grid(static_cast<unsigned>(bx), D / head_dim, static_cast<unsigned>(B));
+    // PF = 4 tokens of loads in flight per lane (6 and 8 measured no faster: the per-token chain,
+    // not the loads, sets the pace)
     if (head_dim == 256)
-      conv_bwd_run_k<4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
-                                                  (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
+      conv_bwd_run_k<4, 4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
+                                                     (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
     else
-      conv_bwd_run_k<2><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
-                                                  (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
+      conv_bwd_run_k<2, 4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
+                                                     (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
   if (head_dim == 256) rc = launch_bwd<8, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
