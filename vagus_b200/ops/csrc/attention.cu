@@ -824,7 +824,7 @@ __global__ void attn_bwd_post(const AttnBwdArgs a) {
 // delta = rowsum(dO o O) comes from the pre-pass and dq is scaled / rounded
 // by the post-pass of the mma.sync backward above.  Every wait is bounded.
 namespace tcbw {
-constexpr int KROWS = 128, THREADS = 320;
+constexpr int KROWS = 128, THREADS = 448;     // 14 warps: TMA, MMA, 8 softmax, 4 dQ readout
 template <int D>
 struct Layout {
   static constexpr int QROWS = D == 64 ? 128 : 64;
@@ -905,7 +905,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
     mbar_init(s_full, 1);
     mbar_init(p_full, 8);
     mbar_init(dq_full, 1);
-    mbar_init(dq_free, 8);
+    mbar_init(dq_free, 4);
     mbar_init(s_free, 8);
     *abort_flag = 0;
     fence_mbar_init();
@@ -1025,6 +1025,56 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         VAGUS_TR(st, 5);
       }
     }
+  } else if (warp >= 10) {
+    // ------------------------------------------------------ dQ readout
+    // dQ of each step (complete in TMEM) -> fp32 staging tile -> one bulk
+    // reduction into dq_acc (the tensor map clips rows past Lq); off the
+    // softmax warps' path, so their next step overlaps it.  Warp w reads TMEM
+    // lanes 32 (w & 3) ..; each thread one row (query for D = 64, dim for 128).
+    const int quarter = warp & 3;
+    const int row = quarter * 32 + lane;
+    const int tq = threadIdx.x - 320;                    // 0..127
+    const uint32_t tl = tb + (static_cast<uint32_t>(quarter * 32) << 16);
+    bool ok = true;
+    for (int st = 0; st < nsteps; ++st) {
+      const int h = hk * group + st / per_head, q0 = (qb0 + st % per_head) * QROWS;
+      ok = ok && mbar_wait(dq_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+      tc_fence_after();
+      uint32_t r[64];
+      tmem_ld_32x32b_x32(tl + Lt::C_DQ, *reinterpret_cast<uint32_t(*)[32]>(&r[0]));
+      tmem_ld_32x32b_x32(tl + Lt::C_DQ + 32u, *reinterpret_cast<uint32_t(*)[32]>(&r[32]));
+      tmem_ld_wait();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(dq_free);
+      if (tq == 0) bulk_wait_read<0>();                 // the previous reduction has read the tile
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        if constexpr (D == 64) {
+          // dims 32 hf ..: 128-byte swizzled [128 rows][32 fp32] tile per half
+          uint8_t* base = sdq + hf * 16384 + row * 128;
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            *reinterpret_cast<uint4*>(base + ((u ^ (row & 7)) * 16)) =
+                make_uint4(r[32 * hf + 4 * u], r[32 * hf + 4 * u + 1], r[32 * hf + 4 * u + 2], r[32 * hf + 4 * u + 3]);
+        } else {
+          // dQ^T row = dim `row`, columns = queries 32 hf ..: plain [64 queries][128 dims] tile
+          float* base = reinterpret_cast<float*>(sdq) + (32 * hf) * 128 + row;
+#pragma unroll
+          for (int e = 0; e < 32; ++e) base[e * 128] = __uint_as_float(r[32 * hf + e]);
+        }
+      }
+      fence_proxy_async_smem();
+      asm volatile("bar.sync 2, 128;" ::: "memory");
+      if (tq == 0 && ok) {
+        const int bh = b * p.H + h;
+        tma_reduce_add_3d(&mdq, sdq, 0, q0, bh);
+        if constexpr (D == 64) tma_reduce_add_3d(&mdq, sdq + 16384, 32, q0, bh);
+        bulk_commit();
+      }
+    }
+    if (tq == 0) bulk_wait<0>();                         // reductions performed before the CTA retires
   } else {
     const int quarter = warp & 3;
     const int half = (warp - 2) >> 2;
@@ -1046,41 +1096,6 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       if (t < QROWS) s_lse[(st & 1) * QROWS + t] = v;
       else if (t < 2 * QROWS) s_delta[(st & 1) * QROWS + t - QROWS] = v;
     };
-    // dQ of step sto (complete in TMEM) -> fp32 staging tile -> one bulk
-    // reduction into dq_acc (the tensor map clips rows past Lq)
-    auto dq_out = [&](int sto) {
-      const int h = hk * group + sto / per_head, q0 = (qb0 + sto % per_head) * QROWS;
-      tc_fence_after();
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tl + Lt::C_DQ + static_cast<uint32_t>(32 * half), r);
-      tmem_ld_wait();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(dq_free);
-      if (t == 0) bulk_wait_read<0>();                  // the previous reduction has read the tile
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if constexpr (D == 64) {
-        // dQ row `row` (query q0 + row), dims 32 half ..: 128-byte swizzled [128 rows][32 fp32] tile per half
-        uint8_t* base = sdq + half * 16384 + row * 128;
-#pragma unroll
-        for (int u = 0; u < 8; ++u)
-          *reinterpret_cast<uint4*>(base + ((u ^ (row & 7)) * 16)) = make_uint4(r[4 * u], r[4 * u + 1], r[4 * u + 2],
-                                                                                 r[4 * u + 3]);
-      } else {
-        // dQ^T row = dim `row`, columns = queries 32 half ..: plain [64 queries][128 dims] tile
-        float* base = reinterpret_cast<float*>(sdq) + (32 * half) * 128 + row;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) base[e * 128] = __uint_as_float(r[e]);
-      }
-      fence_proxy_async_smem();
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (t == 0 && ok) {
-        const int bh = b * p.H + h;
-        tma_reduce_add_3d(&mdq, sdq, 0, q0, bh);
-        if constexpr (D == 64) tma_reduce_add_3d(&mdq, sdq + 16384, 32, q0, bh);
-        bulk_commit();
-      }
-    };
     put_stat(0, fetch_stat(0));
     // kernel parameters in registers: the lambdas above take `p` by reference,
     // and reads through that reference inside the hot loop are memory loads
@@ -1092,6 +1107,7 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       const float* lse_s = s_lse + (st & 1) * QROWS + HALF * half;
       const float* del_s = s_delta + (st & 1) * QROWS + HALF * half;
       asm volatile("bar.sync 1, 256;" ::: "memory");     // this step's statistics are in place
+      const float nxt = fetch_stat(st + 1);              // the next step's, in flight during this one
       ok = ok && mbar_wait(s_full, st & 1, abort_flag, p.err, kErrTimeoutEpilogue);
       if (t == 0) VAGUS_TR(st, 6);
       tc_fence_after();
@@ -1114,29 +1130,34 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           if (lane == 0) mbar_arrive(s_free);
         }
         if (t == 0 && c == 0) VAGUS_TR(st, 7);
-        float ls[32], dl[32];
-#pragma unroll
-        for (int i = 0; i < 32; i += 4) {
-          const float4 a4 = *reinterpret_cast<const float4*>(lse_s + 32 * c + i);
-          const float4 d4 = *reinterpret_cast<const float4*>(del_s + 32 * c + i);
-          ls[i] = a4.x; ls[i + 1] = a4.y; ls[i + 2] = a4.z; ls[i + 3] = a4.w;
-          dl[i] = d4.x; dl[i + 1] = d4.y; dl[i + 2] = d4.z; dl[i + 3] = d4.w;
-        }
+        // lse / delta 4 at a time (shared-memory broadcasts): no 32-wide register copies
         if (full) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const float pr = ex2_approx(fmaf(sv[i], sl2, -ls[i]));
-            sv[i] = pr;
-            dp[i] = pr * (dp[i] - dl[i]);
+          for (int i = 0; i < 32; i += 4) {
+            const float4 a4 = *reinterpret_cast<const float4*>(lse_s + 32 * c + i);
+            const float4 d4 = *reinterpret_cast<const float4*>(del_s + 32 * c + i);
+            const float la[4] = {a4.x, a4.y, a4.z, a4.w}, da[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const float pr = ex2_approx(fmaf(sv[i + u], sl2, -la[u]));
+              sv[i + u] = pr;
+              dp[i + u] = pr * (dp[i + u] - da[u]);
+            }
           }
         } else {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int qi = qbase + 32 * c + i;
-            const bool vis = kj < Lk && qi < Lq && (!causal || kj <= qi + offs);
-            const float pr = vis ? ex2_approx(fmaf(sv[i], sl2, -ls[i])) : 0.f;
-            sv[i] = pr;
-            dp[i] = pr * (dp[i] - dl[i]);
+          for (int i = 0; i < 32; i += 4) {
+            const float4 a4 = *reinterpret_cast<const float4*>(lse_s + 32 * c + i);
+            const float4 d4 = *reinterpret_cast<const float4*>(del_s + 32 * c + i);
+            const float la[4] = {a4.x, a4.y, a4.z, a4.w}, da[4] = {d4.x, d4.y, d4.z, d4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int qi = qbase + 32 * c + i + u;
+              const bool vis = kj < Lk && qi < Lq && (!causal || kj <= qi + offs);
+              const float pr = vis ? ex2_approx(fmaf(sv[i + u], sl2, -la[u])) : 0.f;
+              sv[i + u] = pr;
+              dp[i + u] = pr * (dp[i + u] - da[u]);
+            }
           }
         }
         if (t == 0) VAGUS_TR(st, c == 0 ? 13 : 15);
@@ -1161,16 +1182,11 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
       __syncwarp();
       if (t == 0) VAGUS_TR(st, 8);
       if (lane == 0) mbar_arrive(p_full);
-      const float nxt = fetch_stat(st + 1);              // in flight during the dQ readout
-      if (st > 0) dq_out(st - 1);
-      if (t == 0) VAGUS_TR(st, 11);
       put_stat(st + 1, nxt);
+      if (t == 0) VAGUS_TR(st, 11);
     }
-    if (nsteps > 0) {
-      ok = ok && mbar_wait(dq_full, (nsteps - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
-      dq_out(nsteps - 1);
-    }
-    if (t == 0) bulk_wait<0>();                          // reductions performed before the CTA retires
+    // the last step's products (dV, dK, dQ) are complete once dq_full fires
+    if (nsteps > 0) ok = ok && mbar_wait(dq_full, (nsteps - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
     // dK (scaled) and dV rows of this CTA's keys
     const bool have = ok && nsteps > 0;
     if (have) tc_fence_after();
