@@ -841,6 +841,11 @@ struct Layout {
   static constexpr uint32_t C_S = 0, C_DP = QROWS, C_DV = 2 * QROWS, C_DK = 2 * QROWS + D, C_DQ = 384,
                             COLS = 512;
   static_assert(C_DK + D <= C_DQ, "TMEM columns");
+  // head dim 64: P^T as bf16 pairs in the last 64 columns, the A operand of dV += P^T dO
+  // straight from tensor memory (no shared-memory copy); head dim 128 has no room left
+  static constexpr bool P_TMEM = D == 64;
+  static constexpr uint32_t C_PT = C_DQ + 64;
+  static_assert(!P_TMEM || C_PT + QROWS / 2 <= COLS, "TMEM columns for P^T");
 };
 struct Params {
   int Lq, Lk, H, Hk, causal;
@@ -881,7 +886,15 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  const int kb = blockIdx.x, bhk = blockIdx.y;
+  // causal, head dim 64: key blocks near the start see the most query blocks;
+  // launch them first (all heads' key block 0, then block 1, ...) so the last
+  // wave holds the short CTAs (930 -> 820 us at B = 4, 16 heads, L = 4096).
+  // Head dim 128 keeps the head-major order: there the heads' shared Q / dO
+  // reads in L2 are worth more (1347 vs 1418 us).
+  const int lin = blockIdx.y * gridDim.x + blockIdx.x;
+  const bool lpt = D == 64 && p.causal;
+  const int kb = lpt ? lin / gridDim.y : blockIdx.x;
+  const int bhk = lpt ? lin % gridDim.y : blockIdx.y;
   const int b = bhk / p.Hk, hk = bhk % p.Hk;
   const int group = p.H / p.Hk;
   const int k0 = kb * KROWS;
@@ -1005,7 +1018,11 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
         for (int j = 0; j < QROWS / 16; ++j) {
           const uint32_t acc = (st > 0 || j > 0) ? 1u : 0u;
           const uint32_t a_off = static_cast<uint32_t>((j >> 2) * 16384 + (j & 3) * 32);
-          tc_mma_f16(tb + Lt::C_DV, desc_add(dp_k, a_off), desc_add(ddo_mn, j * 2048), id_kv, acc);
+          if constexpr (Lt::P_TMEM)
+            tc_mma_f16_ts(tb + Lt::C_DV, tb + Lt::C_PT + static_cast<uint32_t>(8 * j), desc_add(ddo_mn, j * 2048),
+                          id_kv, acc);
+          else
+            tc_mma_f16(tb + Lt::C_DV, desc_add(dp_k, a_off), desc_add(ddo_mn, j * 2048), id_kv, acc);
           tc_mma_f16(tb + Lt::C_DK, desc_add(ds_k, a_off), desc_add(dq_mn, j * 2048), id_kv, acc);
         }
         VAGUS_TR(st, 3);
@@ -1161,7 +1178,16 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
           }
         }
         if (t == 0) VAGUS_TR(st, c == 0 ? 13 : 15);
-        if (c == 0 && st > 0) ok = ok && mbar_wait(dq_full, (st - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+        if (c == 0 && st > 0) {
+          ok = ok && mbar_wait(dq_full, (st - 1) & 1, abort_flag, p.err, kErrTimeoutEpilogue);
+          tc_fence_after();                              // P^T in TMEM is rewritten after step st - 1's products
+        }
+        if constexpr (Lt::P_TMEM) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int u = 0; u < 16; ++u) pk[u] = pack_bf16x2(sv[2 * u], sv[2 * u + 1]);
+          tmem_st_32x32b_x16(tl + Lt::C_PT + static_cast<uint32_t>((HALF * half + 32 * c) / 2), pk);
+        }
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
           const int col = HALF * half + 32 * c + 8 * u;  // query column inside the block
@@ -1169,14 +1195,16 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
               static_cast<uint32_t>((col >> 6) * 16384 + row * 128 + ((((col & 63) >> 3) ^ (row & 7)) * 16));
           const float* a8 = &sv[8 * u];
           const float* d8 = &dp[8 * u];
-          *reinterpret_cast<uint4*>(spt + off) = make_uint4(pack_bf16x2(a8[0], a8[1]), pack_bf16x2(a8[2], a8[3]),
-                                                            pack_bf16x2(a8[4], a8[5]), pack_bf16x2(a8[6], a8[7]));
+          if constexpr (!Lt::P_TMEM)
+            *reinterpret_cast<uint4*>(spt + off) = make_uint4(pack_bf16x2(a8[0], a8[1]), pack_bf16x2(a8[2], a8[3]),
+                                                              pack_bf16x2(a8[4], a8[5]), pack_bf16x2(a8[6], a8[7]));
           *reinterpret_cast<uint4*>(sdst + off) = make_uint4(pack_bf16x2(d8[0], d8[1]), pack_bf16x2(d8[2], d8[3]),
                                                              pack_bf16x2(d8[4], d8[5]), pack_bf16x2(d8[6], d8[7]));
         }
         if (t == 0 && c == 0) VAGUS_TR(st, 14);
       }
       if (t == 0) VAGUS_TR(st, 12);
+      if constexpr (Lt::P_TMEM) tmem_st_wait();
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
