@@ -282,6 +282,7 @@ struct Layout {
 
 struct Params {
   int Lq, Lk, H, Hk, causal;
+  int lpt;                         // causal order: 0 plain, g > 0 longest query blocks first in groups of g heads
   float sl2;                       // scale * log2(e)
   void* o;
   long long so_b, so_h, so_l;
@@ -317,13 +318,12 @@ attn_fwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  // causal: within groups of 8 heads, the longest query blocks (most key
+  // causal: within groups of p.lpt heads, the longest query blocks (most key
   // tiles) launch first, so a group's last wave holds short blocks; the
   // resident CTAs share the K / V of at most a few groups (L2 reuse)
-  // (two CTAs per SM only: with one, the plain order measured faster)
   int qb = blockIdx.x, bh = blockIdx.y;
-  if (Lt::CTAS == 2 && p.causal) {
-    constexpr int G = 8;
+  if (p.lpt > 0 && p.causal) {
+    const int G = p.lpt;
     const int nq = gridDim.x, nbh = gridDim.y;
     const int lin = blockIdx.y * nq + blockIdx.x;
     const int grp = lin / (G * nq);
@@ -856,6 +856,7 @@ struct Params {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   long long sdk_b, sdk_h, sdk_l, sdv_b, sdv_h, sdv_l;   // element strides of dk / dv
+  int lpt;                     // causal CTA order: 0 key-block-major per head, 1 key block first, g > 1 in groups of g
   int* err;
   unsigned long long* trace;   // phase clock of CTA (0, 0), [step][16]; null: off
 };
@@ -886,15 +887,25 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
-  // causal, head dim 64: key blocks near the start see the most query blocks;
-  // launch them first (all heads' key block 0, then block 1, ...) so the last
-  // wave holds the short CTAs (930 -> 820 us at B = 4, 16 heads, L = 4096).
-  // Head dim 128 keeps the head-major order: there the heads' shared Q / dO
-  // reads in L2 are worth more (1347 vs 1418 us).
-  const int lin = blockIdx.y * gridDim.x + blockIdx.x;
-  const bool lpt = D == 64 && p.causal;
-  const int kb = lpt ? lin / gridDim.y : blockIdx.x;
-  const int bhk = lpt ? lin % gridDim.y : blockIdx.y;
+  // causal: key blocks near the start see the most query blocks; launch them
+  // first (key block 0 of every head of a group, then block 1, ...) so the
+  // last wave holds the short CTAs
+  int kb = blockIdx.x, bhk = blockIdx.y;
+  if (p.causal) {
+    const int mode = p.lpt;                            // 0 plain, 1 all heads, g > 1: groups of g heads
+    const int nk = gridDim.x, nbh = gridDim.y;
+    const int lin = blockIdx.y * nk + blockIdx.x;
+    if (mode == 1) {
+      kb = lin / nbh;
+      bhk = lin % nbh;
+    } else if (mode > 1) {
+      const int grp = lin / (mode * nk);
+      const int gsz = min(mode, nbh - grp * mode);
+      const int within = lin - grp * mode * nk;
+      kb = within / gsz;
+      bhk = grp * mode + within % gsz;
+    }
+  }
   const int b = bhk / p.Hk, hk = bhk % p.Hk;
   const int group = p.H / p.Hk;
   const int k0 = kb * KROWS;
@@ -1285,6 +1296,9 @@ int launch_fwd_tc(const AttnArgs& a, cudaStream_t st) {
     return 2;
   tcfa::Params p;
   p.Lq = a.Lq; p.Lk = a.Lk; p.H = a.H; p.Hk = a.Hk; p.causal = a.causal;
+  // causal order, measured at B = 4, 16 heads, L = 4096 (plain order: 310 / 425 us): groups of 8 heads
+  // at head dim 64 (282 us), of 4 at 128 (403 us)
+  p.lpt = D == 64 ? 8 : 4;
   p.sl2 = a.scale * kLog2e;
   p.o = a.o; p.so_b = a.so_b; p.so_h = a.so_h; p.so_l = a.so_l;
   p.lse = a.lse;
@@ -1351,6 +1365,10 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
   p.dk = (__nv_bfloat16*)a.dk; p.dv = (__nv_bfloat16*)a.dv; p.err = f.err;
   p.sdk_b = a.sdk_b; p.sdk_h = a.sdk_h; p.sdk_l = a.sdk_l;
   p.sdv_b = a.sdv_b; p.sdv_h = a.sdv_h; p.sdv_l = a.sdv_l;
+  // causal order, measured at B = 4, 16 heads, L = 4096: head dim 64 key block first across all heads
+  // (905 -> 814 us), head dim 128 in groups of 4 heads (1386 -> 1317 us; all heads at once lost
+  // the heads' shared Q / dO reads in L2: 1433 us)
+  p.lpt = D == 64 ? 1 : 4;
   p.trace = g_attn_trace;
   static bool attr_set[64] = {};
   auto kern = attn_bwd_tc<D>;
