@@ -444,6 +444,33 @@ def test_gdn_mixer_matches_torch_path():
         assert rel(p.grad, pr.grad) < 8e-2, (n, rel(p.grad, pr.grad))
 
 
+@pytest.mark.parametrize("dv", [128, 256])
+def test_kda_mixer_matches_torch_path(dv):
+    """The fused per-channel-gate layer (packed projection, KDA gate kernels,
+    conv, fused KDA chunk, gated norm) against the same layer on the torch
+    path (fp32 chunk oracle under bf16 autocast): output, input gradient and
+    every parameter gradient."""
+    from vagus_b200.models.gdn import GatedDeltaNet
+    torch.manual_seed(0)
+    m = GatedDeltaNet(256, 2, 128, dv, gate="vector", gate_rank=64, impl="cuda").to(DEV)
+    m_ref = GatedDeltaNet(256, 2, 128, dv, gate="vector", gate_rank=64, impl="torch").to(DEV)
+    m_ref.load_state_dict(m.state_dict())
+    x = torch.randn(2, 130, 256, device=DEV)
+    assert m._fused_kda_ok(x.bfloat16())
+    xa = x.bfloat16().requires_grad_(True)
+    y = m(xa)
+    xb = x.bfloat16().float().requires_grad_(True)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        yr = m_ref(xb)
+    dy = torch.randn_like(yr.float())
+    (y.float() * dy).sum().backward()
+    (yr.float() * dy).sum().backward()
+    assert rel(y, yr) < 3e-2, rel(y, yr)
+    assert rel(xa.grad, xb.grad) < 5e-2, rel(xa.grad, xb.grad)
+    for (n, p), (_, pr) in zip(m.named_parameters(), m_ref.named_parameters()):
+        assert p.grad is not None and rel(p.grad, pr.grad) < 8e-2, (n, rel(p.grad, pr.grad))
+
+
 def test_rmsnorm_pass_fuses_residual_gradient():
     """The (norm, identity) node adds both gradients in the norm kernel and
     hands the next linear_residual backward a bf16 copy; gradients match the

@@ -227,12 +227,29 @@ class GatedDeltaNet(nn.Module, Mixer):
                 and self.key_head_dim in (128, 256) and self.value_head_dim % 64 == 0 and self.chunk_size == 64
                 and self.dim % 64 == 0 and x.shape[0] * x.shape[1] >= 128)
 
+    def _fused_kda_ok(self, x: torch.Tensor) -> bool:
+        """The fused per-channel-gate layer (``ops.kda_mixer``): softplus gate,
+        delta rule, short conv, key head dim 128, value head dim 128 / 256."""
+        return (x.is_cuda and self.impl != "torch" and self.gate == "vector" and self.delta
+                and self.gate_lower_bound is None and self.short_conv_size is not None
+                and type(self)._write is GatedDeltaNet._write and self.key_head_dim == 128
+                and self.value_head_dim in (128, 256) and self.chunk_size == 64 and self.dim % 64 == 0
+                and self.gate_rank % 8 == 0 and self.gate_rank >= 64 and x.shape[0] * x.shape[1] >= 128)
+
+    def _mixer(self, x):
+        """The gated, normalised head concat on a fused path, or None."""
+        if self._fused_ok(x):
+            return ops.gdn_mixer(self, x)
+        if self._fused_kda_ok(x):
+            return ops.kda_mixer(self, x)
+        return None
+
     # --- training / stateless ---------------------------------------------
 
     def forward(self, x, is_causal: bool = True):
         assert is_causal, "linear attention is causal by construction"
-        if self._fused_ok(x):
-            o = ops.gdn_mixer(self, x)
+        o = self._mixer(x)
+        if o is not None:
             return ops.linear(o, self.wo.weight) if self.out_proj else o
         qp, kp, vp = ops.linear(x, self.wq.weight), ops.linear(x, self.wk.weight), ops.linear(x, self.wv.weight)
         q, k, v = self._heads(qp, kp, vp)
@@ -244,8 +261,9 @@ class GatedDeltaNet(nn.Module, Mixer):
     def forward_pre_out(self, x, is_causal: bool = True):
         """The gated, normalised head concat (the input of ``wo``).  Lets a
         block fuse ``wo`` with its residual add."""
-        if self._fused_ok(x):
-            return ops.gdn_mixer(self, x)
+        o = self._mixer(x)
+        if o is not None:
+            return o
         qp, kp, vp = ops.linear(x, self.wq.weight), ops.linear(x, self.wk.weight), ops.linear(x, self.wv.weight)
         q, k, v = self._heads(qp, kp, vp)
         g, beta = self._gates(x)

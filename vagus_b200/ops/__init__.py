@@ -11,6 +11,7 @@ from ._core import BF16, check_error, kernels_active, native  # noqa: F401
 from .attention import attention, attention_ref  # noqa: F401
 from .ce import fused_linear_ce  # noqa: F401
 from .gdn import conv_silu, gdn_mixer, gdr_chunk, gdr_decode  # noqa: F401
+from .kda import kda_mixer  # noqa: F401
 from .kda import kda_chunk  # noqa: F401
 from .linear import linear, linear_residual  # noqa: F401
 from .mobius import mobius_scan  # noqa: F401

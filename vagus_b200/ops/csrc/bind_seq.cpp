@@ -258,6 +258,45 @@ std::vector<Tensor> kda_intra_fwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor
   return {W, Qh, Kt, A, U, gC};
 }
 
+// KDA gates: f (T, H dk) bf16 view (inner stride 1), b (T, H) bf16 view -> (g (T, H dk), beta (T, H)) fp32
+std::vector<Tensor> kda_gates_fwd(Tensor f, Tensor b, Tensor A_log, Tensor dt_bias, int64_t H, int64_t dk) {
+  TORCH_CHECK(f.dim() == 2 && b.dim() == 2 && f.stride(1) == 1 && b.stride(1) == 1 && f.size(1) == H * dk &&
+                  b.size(1) == H && f.size(0) == b.size(0) && f.scalar_type() == at::kBFloat16 &&
+                  b.scalar_type() == at::kBFloat16,
+              "kda_gates_fwd: f (T, H dk), b (T, H) bf16 row views");
+  A_log = A_log.to(at::kFloat).contiguous();
+  dt_bias = dt_bias.to(at::kFloat).contiguous();
+  const long long T = f.size(0);
+  auto g = torch::empty({T, H * dk}, f.options().dtype(at::kFloat));
+  auto beta = torch::empty({T, H}, f.options().dtype(at::kFloat));
+  check(vagus::kda_gates_fwd(f.data_ptr(), f.stride(0), b.data_ptr(), b.stride(0), A_log.data_ptr<float>(),
+                             dt_bias.data_ptr<float>(), g.data_ptr<float>(), beta.data_ptr<float>(), T,
+                             static_cast<int>(H), static_cast<int>(dk), stream()),
+        "kda_gates_fwd");
+  return {g, beta};
+}
+
+// -> (dA_log (H), ddt_bias (H dk)); df, db written into the given bf16 views
+std::vector<Tensor> kda_gates_bwd(Tensor dg, Tensor dbeta, Tensor f, Tensor b, Tensor A_log, Tensor dt_bias, Tensor df,
+                                  Tensor db, int64_t H, int64_t dk) {
+  dg = dg.contiguous().to(at::kFloat);
+  dbeta = dbeta.contiguous().to(at::kFloat);
+  const long long T = f.size(0);
+  TORCH_CHECK(dg.numel() == T * H * dk && dbeta.numel() == T * H && df.stride(1) == 1 && db.stride(1) == 1 &&
+                  df.size(0) == T && df.size(1) == H * dk && db.size(1) == H,
+              "kda_gates_bwd: shapes");
+  A_log = A_log.to(at::kFloat).contiguous();
+  dt_bias = dt_bias.to(at::kFloat).contiguous();
+  auto dA = torch::zeros({H}, dg.options());
+  auto ddt = torch::zeros({H * dk}, dg.options());
+  check(vagus::kda_gates_bwd(dg.data_ptr<float>(), dbeta.data_ptr<float>(), f.data_ptr(), f.stride(0), b.data_ptr(),
+                             b.stride(0), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), df.data_ptr(),
+                             df.stride(0), db.data_ptr(), db.stride(0), dA.data_ptr<float>(), ddt.data_ptr<float>(), T,
+                             static_cast<int>(H), static_cast<int>(dk), stream()),
+        "kda_gates_bwd");
+  return {dA, ddt};
+}
+
 // -> (dq, dk, dv, dg, dbeta), token-major like the inputs.
 std::vector<Tensor> kda_intra_bwd(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor dW, Tensor dQh,
                                   Tensor dKt, Tensor dA, Tensor dU, Tensor dgC, double scale) {
@@ -335,6 +374,8 @@ void register_seq_ops(pybind11::module& m) {
   m.def("gdr_intra_fwd", &gdr_intra_fwd);
   m.def("gdr_intra_bwd", &gdr_intra_bwd);
   m.def("kda_intra_fwd", &kda_intra_fwd);
+  m.def("kda_gates_fwd", &kda_gates_fwd);
+  m.def("kda_gates_bwd", &kda_gates_bwd);
   m.def("kda_intra_bwd", &kda_intra_bwd);
   // buf: int64 device tensor of 32 entries, or None
   m.def("kda_set_trace", [](c10::optional<Tensor> buf) {

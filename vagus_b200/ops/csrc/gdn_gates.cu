@@ -56,6 +56,79 @@ __global__ void gates_bwd_k(const float* __restrict__ dg, const float* __restric
   }
 }
 
+// Per-channel (KDA) gate from the low-rank projection f (T x H dk, bf16,
+// row pitch ldf) and the write strength from b (T x H, bf16, pitch ldb):
+//   g[t, h dk + c] = -exp(A_log[h]) * softplus(f + dt_bias[h dk + c])   (fp32)
+//   beta[t, h]     = sigmoid(b)
+// One CTA row-strides over tokens, a thread owns 4 adjacent channels.
+__global__ void kda_gates_fwd_k(const __nv_bfloat16* __restrict__ f, long long ldf,
+                                const __nv_bfloat16* __restrict__ b, long long ldb, const float* __restrict__ A_log,
+                                const float* __restrict__ dt_bias, float* __restrict__ g, float* __restrict__ beta,
+                                long long T, int H, int dk) {
+  const int HK = H * dk;
+  const int c = 4 * threadIdx.x;
+  const bool act = c < HK;
+  const int h = act ? c / dk : 0;
+  const float A = act ? __expf(A_log[h]) : 0.f;
+  const float4 bias = act ? *reinterpret_cast<const float4*>(dt_bias + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  for (long long t = blockIdx.x; t < T; t += gridDim.x) {
+    if (act) {
+      const uint2 u = *reinterpret_cast<const uint2*>(f + t * ldf + c);
+      const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+      *reinterpret_cast<float4*>(g + t * HK + c) =
+          make_float4(-A * softplus_f(f0.x + bias.x), -A * softplus_f(f0.y + bias.y), -A * softplus_f(f1.x + bias.z),
+                      -A * softplus_f(f1.y + bias.w));
+    }
+    if (threadIdx.x < H) beta[t * H + threadIdx.x] = sigmoid_f(bf2f(b[t * ldb + threadIdx.x]));
+  }
+}
+
+// Backward: df = dg (-A) sigmoid(f + dt_bias) (bf16, pitch lddf), db = dbeta
+// beta (1 - beta) (bf16, pitch lddb), and dA_log[h] += sum dg g, ddt[hc] +=
+// sum df -- per-thread register sums over the CTA's tokens, one atomic each.
+__global__ void kda_gates_bwd_k(const float* __restrict__ dg, const float* __restrict__ dbeta,
+                                const __nv_bfloat16* __restrict__ f, long long ldf,
+                                const __nv_bfloat16* __restrict__ b, long long ldb, const float* __restrict__ A_log,
+                                const float* __restrict__ dt_bias, __nv_bfloat16* __restrict__ df, long long lddf,
+                                __nv_bfloat16* __restrict__ db, long long lddb, float* __restrict__ dA_log,
+                                float* __restrict__ ddt, long long T, int H, int dk) {
+  const int HK = H * dk;
+  const int c = 4 * threadIdx.x;
+  const bool act = c < HK;
+  const int h = act ? c / dk : 0;
+  const float A = act ? __expf(A_log[h]) : 0.f;
+  const float4 bias = act ? *reinterpret_cast<const float4*>(dt_bias + c) : make_float4(0.f, 0.f, 0.f, 0.f);
+  float sa = 0.f, sd0 = 0.f, sd1 = 0.f, sd2 = 0.f, sd3 = 0.f;
+  for (long long t = blockIdx.x; t < T; t += gridDim.x) {
+    if (act) {
+      const uint2 u = *reinterpret_cast<const uint2*>(f + t * ldf + c);
+      const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
+      const float x[4] = {f0.x + bias.x, f0.y + bias.y, f1.x + bias.z, f1.y + bias.w};
+      const float4 d4 = *reinterpret_cast<const float4*>(dg + t * HK + c);
+      const float d[4] = {d4.x, d4.y, d4.z, d4.w};
+      float o[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        o[j] = d[j] * (-A) * sigmoid_f(x[j]);       // d softplus = sigmoid
+        sa += d[j] * (-A) * softplus_f(x[j]);       // dg / dA_log = g
+      }
+      sd0 += o[0]; sd1 += o[1]; sd2 += o[2]; sd3 += o[3];
+      *reinterpret_cast<uint2*>(df + t * lddf + c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+    }
+    if (threadIdx.x < H) {
+      const float sb = sigmoid_f(bf2f(b[t * ldb + threadIdx.x]));
+      db[t * lddb + threadIdx.x] = f2bf(dbeta[t * H + threadIdx.x] * sb * (1.f - sb));
+    }
+  }
+  if (act) {
+    atomicAdd(&ddt[c], sd0);
+    atomicAdd(&ddt[c + 1], sd1);
+    atomicAdd(&ddt[c + 2], sd2);
+    atomicAdd(&ddt[c + 3], sd3);
+    atomicAdd(&dA_log[h], sa);
+  }
+}
+
 inline int grid_for(long long n) {
   long long g = (n + 255) / 256;
   return static_cast<int>(g > 1184 ? 1184 : (g < 1 ? 1 : g));
@@ -75,6 +148,30 @@ int gdn_gates_bwd(const float* dg, const float* dbeta, const void* ab, long long
   if (H > 64) return 5;
   gates_bwd_k<<<grid_for(T * H), 256, 0, st>>>(dg, dbeta, (const __nv_bfloat16*)ab, ld, A_log, dt_bias,
                                                (__nv_bfloat16*)dab, dA_log, ddt_bias, T, H);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int kda_gates_fwd(const void* f, long long ldf, const void* b, long long ldb, const float* A_log, const float* dt_bias,
+                  float* g, float* beta, long long T, int H, int dk, cudaStream_t st) {
+  const int HK = H * dk;
+  if (HK % 4 || HK / 4 > 1024 || H > HK / 4 || ldf % 4 || (reinterpret_cast<uintptr_t>(f) & 7u)) return 5;
+  const int grid = static_cast<int>(T < 1184 ? (T < 1 ? 1 : T) : 1184);
+  kda_gates_fwd_k<<<grid, HK / 4, 0, st>>>((const __nv_bfloat16*)f, ldf, (const __nv_bfloat16*)b, ldb, A_log, dt_bias,
+                                          g, beta, T, H, dk);
+  return cudaGetLastError() == cudaSuccess ? 0 : 3;
+}
+
+int kda_gates_bwd(const float* dg, const float* dbeta, const void* f, long long ldf, const void* b, long long ldb,
+                  const float* A_log, const float* dt_bias, void* df, long long lddf, void* db, long long lddb,
+                  float* dA_log, float* ddt, long long T, int H, int dk, cudaStream_t st) {
+  const int HK = H * dk;
+  if (HK % 4 || HK / 4 > 1024 || H > HK / 4 || ldf % 4 || lddf % 4 || (reinterpret_cast<uintptr_t>(f) & 7u) ||
+      (reinterpret_cast<uintptr_t>(df) & 7u))
+    return 5;
+  const int grid = static_cast<int>(T < 592 ? (T < 1 ? 1 : T) : 592);
+  kda_gates_bwd_k<<<grid, HK / 4, 0, st>>>(dg, dbeta, (const __nv_bfloat16*)f, ldf, (const __nv_bfloat16*)b, ldb,
+                                          A_log, dt_bias, (__nv_bfloat16*)df, lddf, (__nv_bfloat16*)db, lddb, dA_log,
+                                          ddt, T, H, dk);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 

@@ -56,6 +56,15 @@ int gdn_gates_fwd(const void* ab, long long ld, const float* A_log, const float*
 int gdn_gates_bwd(const float* dg, const float* dbeta, const void* ab, long long ld, const float* A_log,
                   const float* dt_bias, void* dab, float* dA_log, float* ddt_bias, long long T, int H,
                   cudaStream_t st);
+// Per-channel (KDA) gate g (T x H dk fp32) from the low-rank projection f
+// (T x H dk bf16, pitch ldf) and beta (T x H fp32) from b (bf16, pitch ldb),
+// and the backward (df, db bf16 into the packed gradient; dA_log, ddt_bias
+// accumulated).
+int kda_gates_fwd(const void* f, long long ldf, const void* b, long long ldb, const float* A_log, const float* dt_bias,
+                  float* g, float* beta, long long T, int H, int dk, cudaStream_t st);
+int kda_gates_bwd(const float* dg, const float* dbeta, const void* f, long long ldf, const void* b, long long ldb,
+                  const float* A_log, const float* dt_bias, void* df, long long lddf, void* db, long long lddb,
+                  float* dA_log, float* ddt, long long T, int H, int dk, cudaStream_t st);
 
 // gdr.cu: inter-chunk state recurrence of the chunked gated delta rule
 // (scalar gate), forward scan and reverse-scan backward (see gdr.cu).

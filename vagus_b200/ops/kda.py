@@ -35,7 +35,7 @@ from __future__ import annotations
 
 import torch
 
-from ._core import native
+from ._core import BF16, as_bf16_2d, gemm, native
 
 CHUNK = 64
 SUB = 16
@@ -166,6 +166,33 @@ class _KDARec(torch.autograd.Function):
                 dS0.view(B, Hh, dk, dv) if ctx.has_S0 else None, None)
 
 
+def _kda_core_fwd(q, k, v, g, beta, S0, scale: float):
+    """The fused KDA chunk forward: intra kernels + recurrence.  q, k, v bf16
+    (B, L, H, .), g (B, L, H, dk) and beta (B, L, H) fp32.  Returns
+    (o (B, L, H, dv) bf16, S (B * H, dk, dv) fp32, saved tensors)."""
+    C = native()
+    B, L, H, dk = q.shape
+    dv = v.shape[-1]
+    W, Qh, Kt, A, U, gC = C.kda_intra_fwd(q, k, v, g, beta, scale)
+    S0f = None if S0 is None else S0.float().reshape(B * H, dk, dv).contiguous()
+    o, Vp, states, S_out = C.gdr_rec_fwd(W, Qh, Kt, A, U, gC, S0f, True, H)
+    return o, S_out, (q, k, v, g, beta, W, Qh, Kt, A, Vp, gC, states)
+
+
+def _kda_core_bwd(saved, do, dS, scale: float, need_dS0: bool):
+    """(dq, dk, dv, dg, dbeta, dS0) of ``_kda_core_fwd``."""
+    q, k, v, g, beta, W, Qh, Kt, A, Vp, gC, states = saved
+    B, L, H, dk = q.shape
+    dv = v.shape[-1]
+    C = native()
+    dSf = None if dS is None else dS.float().reshape(B * H, dk, dv).contiguous()
+    dW, dQh, dKt, dA, dU, dgC, dS0 = C.gdr_rec_bwd(W, Qh, Kt, A, Vp, gC, states,
+                                                    do.to(torch.bfloat16).contiguous(), dSf, need_dS0)
+    dq, dk_, dv_, dg, dbeta = C.kda_intra_bwd(q, k, v, g, beta, dW.to(torch.bfloat16), dQh.to(torch.bfloat16),
+                                               dKt.to(torch.bfloat16), dA, dU.to(torch.bfloat16), dgC, scale)
+    return dq, dk_, dv_, dg, dbeta, dS0
+
+
 class _KDAFused(torch.autograd.Function):
     """The whole chunked KDA layer on our kernels: the intra-chunk stage
     (``kda_intra.cu``: per-channel cumulative decay, gated products, WY
@@ -175,26 +202,17 @@ class _KDAFused(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, q, k, v, g, beta, S0, scale: float):
-        C = native()
         B, L, H, dk = q.shape
         dv = v.shape[-1]
-        W, Qh, Kt, A, U, gC = C.kda_intra_fwd(q, k, v, g, beta, scale)
-        S0f = None if S0 is None else S0.float().reshape(B * H, dk, dv).contiguous()
-        o, Vp, states, S_out = C.gdr_rec_fwd(W, Qh, Kt, A, U, gC, S0f, True, H)
-        ctx.save_for_backward(q, k, v, g, beta, W, Qh, Kt, A, Vp, gC, states)
+        o, S_out, saved = _kda_core_fwd(q, k, v, g, beta, S0, scale)
+        ctx.save_for_backward(*saved)
         ctx.scale, ctx.has_S0, ctx.shape = scale, S0 is not None, (B, H, dk, dv)
         return o, S_out.view(B, H, dk, dv)
 
     @staticmethod
     def backward(ctx, do, dS):
-        q, k, v, g, beta, W, Qh, Kt, A, Vp, gC, states = ctx.saved_tensors
         B, H, dk, dv = ctx.shape
-        C = native()
-        dSf = None if dS is None else dS.float().reshape(B * H, dk, dv).contiguous()
-        dW, dQh, dKt, dA, dU, dgC, dS0 = C.gdr_rec_bwd(W, Qh, Kt, A, Vp, gC, states,
-                                                        do.to(torch.bfloat16).contiguous(), dSf, ctx.has_S0)
-        dq, dk_, dv_, dg, dbeta = C.kda_intra_bwd(q, k, v, g, beta, dW.to(torch.bfloat16), dQh.to(torch.bfloat16),
-                                                   dKt.to(torch.bfloat16), dA, dU.to(torch.bfloat16), dgC, ctx.scale)
+        dq, dk_, dv_, dg, dbeta, dS0 = _kda_core_bwd(ctx.saved_tensors, do, dS, ctx.scale, ctx.has_S0)
         return dq, dk_, dv_, dg, dbeta, (dS0.view(B, H, dk, dv) if ctx.has_S0 else None), None
 
 
@@ -231,3 +249,113 @@ def kda_chunk(q, k, v, g, beta, S0, *, scale: float, chunk_size: int = 64, delta
     parts = kda_intra(q, k, v, g, beta, scale, delta, w)
     o, S = _KDARec.apply(*parts, S0, H)
     return (o[:, :L] if pad else o), S
+
+
+# ------------------------------------------------------------- fused layer --
+
+def _packed_weight_kda(m):
+    """bf16 rows [wq; wk; wv; wg; wa1; wb; 0-pad] of a per-channel-gate layer:
+    every projection of the layer input is one GEMM (the gate's second,
+    low-rank factor wa2 runs on its output)."""
+    from .gdn import _PAD
+    ws = [m.wq.weight, m.wk.weight, m.wv.weight, m.wg.weight, m.wa1.weight, m.wb.weight]
+    n = sum(w.shape[0] for w in ws)
+    pad = (-n) % 64
+    key = ("kda_pad", pad, m.dim)
+    zeros = _PAD.get(key)
+    if zeros is None or zeros.device != ws[0].device:
+        zeros = torch.zeros(pad, m.dim, device=ws[0].device, dtype=torch.float32)
+        _PAD[key] = zeros
+    return BF16.get_cat(ws + [zeros]), n
+
+
+class _KDAMixer(torch.autograd.Function):
+    """h (B, L, D) bf16 -> the gated normalised head concat (B, L, H dv) of a
+    per-channel-gate (KDA) layer.  Column layout of the packed projection P:
+    [q | k | v | gate | a1 (rank R) | b | pad]; f = a1 wa2^T is the gate's
+    pre-activation."""
+
+    @staticmethod
+    def forward(ctx, h, Wp, wq, wk, wv, wg, wa1, wb, wa2, A_log, dt_bias, cq, ck, cv, gamma, meta):
+        H, dk, dv, R, eps, scale = meta
+        B, L, Dm = h.shape
+        Hk, Hv = H * dk, H * dv
+        h2 = as_bf16_2d(h)
+        T = h2.shape[0]
+        NP = Wp.shape[0]
+        P = torch.empty(T, NP, device=h.device, dtype=torch.bfloat16)
+        gemm(h2, False, Wp, False, P)
+        P3 = P.view(B, L, NP)
+        oa = 2 * Hk + 2 * Hv                                  # a1 | b column offset
+        a1 = P[:, oa:oa + R]
+        w2 = BF16.get(wa2)
+        F = torch.empty(T, Hk, device=h.device, dtype=torch.bfloat16)
+        gemm(a1, False, w2, False, F)                         # f = a1 wa2^T
+        C = native()
+        g, beta = C.kda_gates_fwd(F, P[:, oa + R:oa + R + H], A_log, dt_bias, H, dk)
+        cq, ck, cv = cq.float().contiguous(), ck.float().contiguous(), cv.float().contiguous()
+        q, rq = C.conv_silu_fwd(P3[:, :, :Hk], cq, dk, True)
+        k, rk = C.conv_silu_fwd(P3[:, :, Hk:2 * Hk], ck, dk, True)
+        v, _ = C.conv_silu_fwd(P3[:, :, 2 * Hk:2 * Hk + Hv], cv, dv, False)
+        o, _S, ksaved = _kda_core_fwd(q.view(B, L, H, dk), k.view(B, L, H, dk), v.view(B, L, H, dv),
+                                      g.view(B, L, H, dk), beta.view(B, L, H), None, scale)
+        o = o.contiguous()
+        y, rstd = C.rmsnorm_gated_fwd(o.view(T, H, dv), P[:, 2 * Hk + Hv:oa], gamma.float().contiguous(), eps, H)
+        ctx.dims = (B, L, Dm, H, dk, dv, R, NP)
+        ctx.scale = scale
+        ctx.save_for_backward(h2, Wp, P, F, w2, rq, rk, o, rstd, A_log, dt_bias, cq, ck, cv, gamma, *ksaved)
+        return y.view(B, L, Hv)
+
+    @staticmethod
+    def backward(ctx, dy):
+        B, L, Dm, H, dk, dv, R, NP = ctx.dims
+        Hk, Hv = H * dk, H * dv
+        oa = 2 * Hk + 2 * Hv
+        sv = ctx.saved_tensors
+        h2, Wp, P, F, w2, rq, rk, o, rstd, A_log, dt_bias, cq, ck, cv, gamma = sv[:15]
+        ksaved = sv[15:]
+        T = h2.shape[0]
+        C = native()
+        dP = torch.empty(T, NP, device=h2.device, dtype=torch.bfloat16)
+        if NP > oa + R + H:
+            dP[:, oa + R + H:].zero_()
+        do, dgamma = C.rmsnorm_gated_bwd(dy.reshape(T, Hv).to(torch.bfloat16), o.view(T, H, dv),
+                                         P[:, 2 * Hk + Hv:oa], gamma.float().contiguous(), rstd,
+                                         dP[:, 2 * Hk + Hv:oa], H)
+        gq, gk, gv, gg, gb, _ = _kda_core_bwd(ksaved, do.view(B, L, H, dv), None, ctx.scale, False)
+        dF = torch.empty(T, Hk, device=h2.device, dtype=torch.bfloat16)
+        dA_log, ddt = C.kda_gates_bwd(gg.reshape(T, Hk), gb.reshape(T, H), F, P[:, oa + R:oa + R + H], A_log,
+                                      dt_bias, dF, dP[:, oa + R:oa + R + H], H, dk)
+        gemm(dF, False, w2, True, dP[:, oa:oa + R])                          # da1 = df wa2
+        dwa2 = torch.zeros(Hk, R, device=h2.device, dtype=torch.float32)
+        gemm(dF, True, P[:, oa:oa + R], True, dwa2, atomic=True)             # dwa2 = df^T a1
+        P3, dP3 = P.view(B, L, NP), dP.view(B, L, NP)
+        dcq = torch.zeros(cq.numel(), device=h2.device, dtype=torch.float32)
+        dck = torch.zeros(ck.numel(), device=h2.device, dtype=torch.float32)
+        dcv = torch.zeros(cv.numel(), device=h2.device, dtype=torch.float32)
+        C.conv_silu_bwd(gq.reshape(B, L, Hk), P3[:, :, :Hk], cq, rq, dP3[:, :, :Hk], dcq, dk, True)
+        C.conv_silu_bwd(gk.reshape(B, L, Hk), P3[:, :, Hk:2 * Hk], ck, rk, dP3[:, :, Hk:2 * Hk], dck, dk, True)
+        C.conv_silu_bwd(gv.reshape(B, L, Hv), P3[:, :, 2 * Hk:2 * Hk + Hv], cv, rq, dP3[:, :, 2 * Hk:2 * Hk + Hv],
+                        dcv, dv, False)
+        dh = torch.empty(T, Dm, device=h2.device, dtype=torch.bfloat16)
+        gemm(dP, False, Wp, True, dh)                                          # dh = dP Wp
+        dWp = torch.zeros(NP, Dm, device=h2.device, dtype=torch.float32)
+        gemm(dP, True, h2, True, dWp, atomic=True)                             # dWp = dP^T h
+        dwq, dwk, dwv, dwg, dwa1, dwb = dWp[:oa + R + H].split([Hk, Hk, Hv, Hv, R, H], 0)
+        return (dh.view(B, L, Dm), None, dwq, dwk, dwv, dwg, dwa1, dwb, dwa2, dA_log, ddt.view_as(dt_bias),
+                dcq.view_as(cq), dck.view_as(ck), dcv.view_as(cv), dgamma, None)
+
+
+def kda_mixer(m, x):
+    """Fused forward of a per-channel-gate delta-rule layer (short conv,
+    softplus gate) up to the input of ``wo``."""
+    B, L, _ = x.shape
+    meta = (m.head_count, m.key_head_dim, m.value_head_dim, m.gate_rank, m.o_norm.eps, m.scale)
+    pad = (-L) % CHUNK
+    if pad:
+        x = torch.nn.functional.pad(x, (0, 0, 0, pad))
+    Wp, _ = _packed_weight_kda(m)
+    y = _KDAMixer.apply(x.to(torch.bfloat16), Wp, m.wq.weight, m.wk.weight, m.wv.weight, m.wg.weight,
+                        m.wa1.weight, m.wb.weight, m.wa2.weight, m.A_log, m.dt_bias, m.conv_q.conv.weight,
+                        m.conv_k.conv.weight, m.conv_v.conv.weight, m.o_norm.gamma, meta)
+    return y[:, :L] if pad else y
