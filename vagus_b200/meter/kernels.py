@@ -11,7 +11,7 @@ shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
 gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
-sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, kda_intra_fwd, kda_intra_bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm.  With no
+sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, kda_intra_fwd, kda_intra_bwd, kda_gates_fwd / bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm.  With no
 case names every
 case runs.
 
@@ -113,6 +113,15 @@ def _cases(B: int, L: int):
     # per chunk: two gated products (64 x 64 x 128), W = T(bGK), U = T(bV), the 64 x 64 inverse
     kintra = Nq * (2 * 2 * 64 * 64 * dkk + 2 * 64 * 64 * (dkk + 256) + 2 * 64 ** 3 // 3)
     cases["kda_intra_fwd"] = (lambda: C.kda_intra_fwd(*kda_in), None, kintra)
+    # the per-channel gate from the low-rank projection (4 heads x 128 channels) and its backward
+    fg = r(B * L, 4 * dkk)
+    bg = r(B * L, 4)
+    A_lg, dtb = torch.randn(4, device=dev) * 0.1, torch.randn(4 * dkk, device=dev) * 0.1
+    cases["kda_gates_fwd"] = (lambda: C.kda_gates_fwd(fg, bg, A_lg, dtb, 4, dkk), B * L * 4 * dkk * (2 + 4), None)
+    dgg, dbg = torch.randn(B * L, 4 * dkk, device=dev), torch.randn(B * L, 4, device=dev)
+    dfg, dbb = torch.empty_like(fg), torch.empty_like(bg)
+    cases["kda_gates_bwd"] = (lambda: C.kda_gates_bwd(dgg, dbg, fg, bg, A_lg, dtb, dfg, dbb, 4, dkk),
+                              B * L * 4 * dkk * (4 + 2 + 2), None)
     kout = C.kda_intra_fwd(*kda_in)
     kgr = [torch.randn_like(t).to(t.dtype) for t in kout]
     cases["kda_intra_bwd"] = (lambda: C.kda_intra_bwd(*kda_in[:5], kgr[0], kgr[1], kgr[2], kgr[3].float(), kgr[4],

@@ -71,15 +71,24 @@ __global__ void kda_gates_fwd_k(const __nv_bfloat16* __restrict__ f, long long l
   const int h = act ? c / dk : 0;
   const float A = act ? __expf(A_log[h]) : 0.f;
   const float4 bias = act ? *reinterpret_cast<const float4*>(dt_bias + c) : make_float4(0.f, 0.f, 0.f, 0.f);
-  for (long long t = blockIdx.x; t < T; t += gridDim.x) {
-    if (act) {
-      const uint2 u = *reinterpret_cast<const uint2*>(f + t * ldf + c);
-      const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
-      *reinterpret_cast<float4*>(g + t * HK + c) =
-          make_float4(-A * softplus_f(f0.x + bias.x), -A * softplus_f(f0.y + bias.y), -A * softplus_f(f1.x + bias.z),
-                      -A * softplus_f(f1.y + bias.w));
+  constexpr int RU = 4;                              // rows per iteration, loads issued together
+  for (long long t0 = (long long)blockIdx.x * RU; t0 < T; t0 += (long long)gridDim.x * RU) {
+    uint2 u[RU];
+#pragma unroll
+    for (int r = 0; r < RU; ++r)
+      if (act && t0 + r < T) u[r] = *reinterpret_cast<const uint2*>(f + (t0 + r) * ldf + c);
+#pragma unroll
+    for (int r = 0; r < RU; ++r) {
+      const long long t = t0 + r;
+      if (t >= T) break;
+      if (act) {
+        const float2 f0 = unpack_bf16x2(u[r].x), f1 = unpack_bf16x2(u[r].y);
+        *reinterpret_cast<float4*>(g + t * HK + c) =
+            make_float4(-A * softplus_f(f0.x + bias.x), -A * softplus_f(f0.y + bias.y),
+                        -A * softplus_f(f1.x + bias.z), -A * softplus_f(f1.y + bias.w));
+      }
+      if (threadIdx.x < H) beta[t * H + threadIdx.x] = sigmoid_f(bf2f(b[t * ldb + threadIdx.x]));
     }
-    if (threadIdx.x < H) beta[t * H + threadIdx.x] = sigmoid_f(bf2f(b[t * ldb + threadIdx.x]));
   }
 }
 
@@ -99,25 +108,40 @@ __global__ void kda_gates_bwd_k(const float* __restrict__ dg, const float* __res
   const float A = act ? __expf(A_log[h]) : 0.f;
   const float4 bias = act ? *reinterpret_cast<const float4*>(dt_bias + c) : make_float4(0.f, 0.f, 0.f, 0.f);
   float sa = 0.f, sd0 = 0.f, sd1 = 0.f, sd2 = 0.f, sd3 = 0.f;
-  for (long long t = blockIdx.x; t < T; t += gridDim.x) {
-    if (act) {
-      const uint2 u = *reinterpret_cast<const uint2*>(f + t * ldf + c);
-      const float2 f0 = unpack_bf16x2(u.x), f1 = unpack_bf16x2(u.y);
-      const float x[4] = {f0.x + bias.x, f0.y + bias.y, f1.x + bias.z, f1.y + bias.w};
-      const float4 d4 = *reinterpret_cast<const float4*>(dg + t * HK + c);
-      const float d[4] = {d4.x, d4.y, d4.z, d4.w};
-      float o[4];
+  // RU rows per iteration, their loads issued together (memory-level parallelism)
+  constexpr int RU = 4;
+  for (long long t0 = (long long)blockIdx.x * RU; t0 < T; t0 += (long long)gridDim.x * RU) {
+    uint2 u[RU];
+    float4 d4[RU];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        o[j] = d[j] * (-A) * sigmoid_f(x[j]);       // d softplus = sigmoid
-        sa += d[j] * (-A) * softplus_f(x[j]);       // dg / dA_log = g
+    for (int r = 0; r < RU; ++r) {
+      const long long t = t0 + r;
+      if (act && t < T) {
+        u[r] = *reinterpret_cast<const uint2*>(f + t * ldf + c);
+        d4[r] = *reinterpret_cast<const float4*>(dg + t * HK + c);
       }
-      sd0 += o[0]; sd1 += o[1]; sd2 += o[2]; sd3 += o[3];
-      *reinterpret_cast<uint2*>(df + t * lddf + c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
     }
-    if (threadIdx.x < H) {
-      const float sb = sigmoid_f(bf2f(b[t * ldb + threadIdx.x]));
-      db[t * lddb + threadIdx.x] = f2bf(dbeta[t * H + threadIdx.x] * sb * (1.f - sb));
+#pragma unroll
+    for (int r = 0; r < RU; ++r) {
+      const long long t = t0 + r;
+      if (t >= T) break;
+      if (act) {
+        const float2 f0 = unpack_bf16x2(u[r].x), f1 = unpack_bf16x2(u[r].y);
+        const float x[4] = {f0.x + bias.x, f0.y + bias.y, f1.x + bias.z, f1.y + bias.w};
+        const float d[4] = {d4[r].x, d4[r].y, d4[r].z, d4[r].w};
+        float o[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          o[j] = d[j] * (-A) * sigmoid_f(x[j]);       // d softplus = sigmoid
+          sa += d[j] * (-A) * softplus_f(x[j]);       // dg / dA_log = g
+        }
+        sd0 += o[0]; sd1 += o[1]; sd2 += o[2]; sd3 += o[3];
+        *reinterpret_cast<uint2*>(df + t * lddf + c) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+      }
+      if (threadIdx.x < H) {
+        const float sb = sigmoid_f(bf2f(b[t * ldb + threadIdx.x]));
+        db[t * lddb + threadIdx.x] = f2bf(dbeta[t * H + threadIdx.x] * sb * (1.f - sb));
+      }
     }
   }
   if (act) {
@@ -125,6 +149,16 @@ __global__ void kda_gates_bwd_k(const float* __restrict__ dg, const float* __res
     atomicAdd(&ddt[c + 1], sd1);
     atomicAdd(&ddt[c + 2], sd2);
     atomicAdd(&ddt[c + 3], sd3);
+  }
+  // dA_log: lanes of one head reduce first (a warp's 128 channels lie in one head when dk is a
+  // multiple of 128), so each head takes a few atomics per CTA instead of one per thread
+  const unsigned lanes_act = __ballot_sync(0xffffffffu, act);
+  const int h0 = __shfl_sync(0xffffffffu, h, 0);
+  const bool one_head = __all_sync(0xffffffffu, !act || h == h0);
+  if (one_head) {
+    const float tot = warp_sum(act ? sa : 0.f);
+    if ((threadIdx.x & 31) == 0 && lanes_act) atomicAdd(&dA_log[h0], tot);
+  } else if (act) {
     atomicAdd(&dA_log[h], sa);
   }
 }
@@ -155,7 +189,8 @@ int kda_gates_fwd(const void* f, long long ldf, const void* b, long long ldb, co
                   float* g, float* beta, long long T, int H, int dk, cudaStream_t st) {
   const int HK = H * dk;
   if (HK % 4 || HK / 4 > 1024 || H > HK / 4 || ldf % 4 || (reinterpret_cast<uintptr_t>(f) & 7u)) return 5;
-  const int grid = static_cast<int>(T < 1184 ? (T < 1 ? 1 : T) : 1184);
+  const long long rows4 = (T + 3) / 4;
+  const int grid = static_cast<int>(rows4 < 2368 ? (rows4 < 1 ? 1 : rows4) : 2368);
   kda_gates_fwd_k<<<grid, HK / 4, 0, st>>>((const __nv_bfloat16*)f, ldf, (const __nv_bfloat16*)b, ldb, A_log, dt_bias,
                                           g, beta, T, H, dk);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
@@ -168,7 +203,8 @@ int kda_gates_bwd(const float* dg, const float* dbeta, const void* f, long long 
   if (HK % 4 || HK / 4 > 1024 || H > HK / 4 || ldf % 4 || lddf % 4 || (reinterpret_cast<uintptr_t>(f) & 7u) ||
       (reinterpret_cast<uintptr_t>(df) & 7u))
     return 5;
-  const int grid = static_cast<int>(T < 592 ? (T < 1 ? 1 : T) : 592);
+  const long long rows4 = (T + 3) / 4;
+  const int grid = static_cast<int>(rows4 < 592 ? (rows4 < 1 ? 1 : rows4) : 592);
   kda_gates_bwd_k<<<grid, HK / 4, 0, st>>>(dg, dbeta, (const __nv_bfloat16*)f, ldf, (const __nv_bfloat16*)b, ldb,
                                           A_log, dt_bias, (__nv_bfloat16*)df, lddf, (__nv_bfloat16*)db, lddb, dA_log,
                                           ddt, T, H, dk);
