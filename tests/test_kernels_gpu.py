@@ -148,11 +148,14 @@ def test_rmsnorm_gated_and_swiglu_and_sgate():
     assert rel(z, zr) < 1e-2 and rel(xx.grad, xr2.grad) < 1e-2 and rel(gg.grad, gr2.grad) < 1e-2
 
 
+@pytest.mark.parametrize("D", [64, 128])
 @pytest.mark.parametrize("norm,rope", [(True, True), (False, True), (True, False)])
-def test_qk_norm_rope(norm, rope):
+def test_qk_norm_rope(norm, rope, D):
+    """qk-norm + RoPE (vectorised kernels at head dims 64 / 128; 222 rows, not
+    a multiple of the rows a warp covers) against fp32 torch, incl. gradients."""
     from vagus_b200 import ops
     from vagus_b200.models.rope import RoPE
-    B, L, H, D = 2, 37, 3, 64
+    B, L, H = 2, 37, 3
     x = torch.randn(B, L, H, D, device=DEV).bfloat16().requires_grad_(True)
     gm = (1 + 0.1 * torch.randn(D, device=DEV)).requires_grad_(True) if norm else None
     rp = RoPE(H * D, D, 64).to(DEV)

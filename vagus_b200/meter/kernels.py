@@ -11,7 +11,7 @@ shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
 conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
 gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
-sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, kda_intra_fwd, kda_intra_bwd, kda_gates_fwd / bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm.  With no
+sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, kda_intra_fwd, kda_intra_bwd, kda_gates_fwd / bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm, rope_fwd / bwd.  With no
 case names every
 case runs.
 
@@ -189,6 +189,15 @@ def _cases(B: int, L: int):
     xs = r(T, D)
     gamma = torch.ones(D, device=dev)
     cases["rmsnorm"] = (lambda: C.rmsnorm_fwd(xs, gamma, 1e-6, False), 2 * T * D * 2, None)
+    # qk-norm + RoPE at the Transformer++ shape (16 heads x 64)
+    xr4 = r(B, L, 16, 64)
+    gr4 = torch.ones(64, device=dev)
+    cs = torch.randn(L, 32, device=dev)
+    sn = torch.randn(L, 32, device=dev)
+    cases["rope_fwd"] = (lambda: C.qk_norm_rope_fwd(xr4, gr4, cs, sn, 1e-6), 2 * xr4.numel() * 2, None)
+    y4, rs4 = C.qk_norm_rope_fwd(xr4, gr4, cs, sn, 1e-6)
+    dy4 = torch.randn_like(y4)
+    cases["rope_bwd"] = (lambda: C.qk_norm_rope_bwd(dy4, xr4, gr4, cs, sn, rs4), 3 * xr4.numel() * 2, None)
     return cases
 
 

@@ -438,6 +438,151 @@ __global__ void qk_norm_rope_bwd_k(const __nv_bfloat16* __restrict__ dy, const _
 
 inline int blocks_for(long long rows) { return static_cast<int>((rows + ROWS_PER_CTA - 1) / ROWS_PER_CTA); }
 
+// Vectorised qk-norm + RoPE for head dims 64 / 128: a thread owns 8 adjacent
+// channels (one 16-byte load), D / 8 lanes share a row (the norm is a
+// shuffle reduction over them), so a warp covers 256 / D rows per pass;
+// CTAs stride over the rows.  The backward keeps its gamma-gradient partials
+// in registers across all rows it visits and adds them once per CTA.
+template <int D>
+__global__ void __launch_bounds__(256)
+qk_norm_rope_fwd_v(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma,
+                   const float* __restrict__ cosv, const float* __restrict__ sinv, __nv_bfloat16* __restrict__ y,
+                   float* __restrict__ rstd, long long rows, int L, int H, float eps) {
+  constexpr int TPR = D / 8, RPW = 32 / TPR, HALF = D / 2;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int sub = lane % TPR, rw = lane / TPR;
+  const int c0 = 8 * sub;
+  float gm[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) gm[j] = gamma ? gamma[c0 + j] : 1.f;
+  const long long step = (long long)gridDim.x * 8 * RPW;
+  for (long long base = ((long long)blockIdx.x * 8 + warp) * RPW; base < rows; base += step) {
+    const long long r = base + rw;
+    const bool valid = r < rows;
+    float v[8];
+    {
+      const uint4 u = valid ? *reinterpret_cast<const uint4*>(x + r * D + c0) : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) { const float2 f = unpack_bf16x2(w[j]); v[2 * j] = f.x; v[2 * j + 1] = f.y; }
+    }
+    if (gamma) {
+      float ss = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+#pragma unroll
+      for (int o = 1; o < TPR; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+      const float rs = rsqrtf(ss / D + eps);
+      if (valid && sub == 0) rstd[r] = rs;
+      // the normalised value is rounded to the input dtype before gamma, as in the unfused form
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = bf2f(f2bf(v[j] * rs)) * gm[j];
+    }
+    if (cosv && valid) {
+      const long long l = (r / H) % L;
+      const float4 c4 = *reinterpret_cast<const float4*>(cosv + l * HALF + 4 * sub);
+      const float4 s4 = *reinterpret_cast<const float4*>(sinv + l * HALF + 4 * sub);
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = v[2 * j], b = v[2 * j + 1];
+        v[2 * j] = a * cc[j] - b * sn[j];
+        v[2 * j + 1] = a * sn[j] + b * cc[j];
+      }
+    }
+    if (valid)
+      *reinterpret_cast<uint4*>(y + r * D + c0) =
+          make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(256)
+qk_norm_rope_bwd_v(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
+                   const float* __restrict__ gamma, const float* __restrict__ cosv, const float* __restrict__ sinv,
+                   const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx, float* __restrict__ dgamma,
+                   long long rows, int L, int H) {
+  constexpr int TPR = D / 8, RPW = 32 / TPR, HALF = D / 2;
+  __shared__ float sg[D];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int sub = lane % TPR, rw = lane / TPR;
+  const int c0 = 8 * sub;
+  if (gamma) {
+    for (int c = threadIdx.x; c < D; c += blockDim.x) sg[c] = 0.f;
+    __syncthreads();
+  }
+  float gm[8], acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) { gm[j] = gamma ? gamma[c0 + j] : 1.f; acc[j] = 0.f; }
+  const long long step = (long long)gridDim.x * 8 * RPW;
+  for (long long base = ((long long)blockIdx.x * 8 + warp) * RPW; base < rows; base += step) {
+    const long long r = base + rw;
+    const bool valid = r < rows;
+    float d[8], xv[8];
+    {
+      const uint4 u = valid ? *reinterpret_cast<const uint4*>(dy + r * D + c0) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 q = valid && gamma ? *reinterpret_cast<const uint4*>(x + r * D + c0) : make_uint4(0u, 0u, 0u, 0u);
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w}, wq[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 f = unpack_bf16x2(w[j]); d[2 * j] = f.x; d[2 * j + 1] = f.y;
+        f = unpack_bf16x2(wq[j]); xv[2 * j] = f.x; xv[2 * j + 1] = f.y;
+      }
+    }
+    if (cosv && valid) {                                  // un-rotate: the transpose of the rotation
+      const long long l = (r / H) % L;
+      const float4 c4 = *reinterpret_cast<const float4*>(cosv + l * HALF + 4 * sub);
+      const float4 s4 = *reinterpret_cast<const float4*>(sinv + l * HALF + 4 * sub);
+      const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float a = d[2 * j], b = d[2 * j + 1];
+        d[2 * j] = a * cc[j] + b * sn[j];
+        d[2 * j + 1] = -a * sn[j] + b * cc[j];
+      }
+    }
+    if (gamma) {
+      const float rs = valid ? rstd[r] : 0.f;
+      float dot = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float xh = xv[j] * rs;
+        dot += d[j] * gm[j] * xh;
+        acc[j] += d[j] * xh;
+      }
+#pragma unroll
+      for (int o = 1; o < TPR; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+      dot /= D;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) d[j] = rs * (d[j] * gm[j] - xv[j] * rs * dot);
+    }
+    if (valid)
+      *reinterpret_cast<uint4*>(dx + r * D + c0) =
+          make_uint4(pack_bf16x2(d[0], d[1]), pack_bf16x2(d[2], d[3]), pack_bf16x2(d[4], d[5]), pack_bf16x2(d[6], d[7]));
+  }
+  if (gamma) {
+    // lanes with the same `sub` hold the same channels: reduce over the warp's rows, then the CTA's
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v = acc[j];
+#pragma unroll
+      for (int o = TPR; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+      acc[j] = v;
+    }
+    if (rw == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) atomicAdd(&sg[c0 + j], acc[j]);
+    }
+    __syncthreads();
+    for (int c = threadIdx.x; c < D; c += blockDim.x) atomicAdd(&dgamma[c], sg[c]);
+  }
+}
+
+inline int vec_rope_grid(long long rows, int rpw) {
+  const long long want = (rows + 8LL * rpw - 1) / (8LL * rpw);
+  return static_cast<int>(std::min<long long>(std::max<long long>(want, 1), 148LL * 8));
+}
+
 }  // namespace
 
 int rmsnorm_fwd(const void* x, int x_f32, const float* gamma, void* y, int y_f32, float* rstd, long long rows, int D,
@@ -552,6 +697,17 @@ int rmsnorm_gated_bwd(const void* dy, const void* o, const void* g, long long ld
 
 int qk_norm_rope_fwd(const void* x, const float* gamma, const float* cosv, const float* sinv, void* y, float* rstd,
                      long long rows, int L, int H, int D, float eps, cudaStream_t s) {
+  const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
+  if (al && D == 64) {
+    qk_norm_rope_fwd_v<64><<<vec_rope_grid(rows, 4), 256, 0, s>>>((const __nv_bfloat16*)x, gamma, cosv, sinv,
+                                                                  (__nv_bfloat16*)y, rstd, rows, L, H, eps);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
+  if (al && D == 128) {
+    qk_norm_rope_fwd_v<128><<<vec_rope_grid(rows, 2), 256, 0, s>>>((const __nv_bfloat16*)x, gamma, cosv, sinv,
+                                                                   (__nv_bfloat16*)y, rstd, rows, L, H, eps);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   qk_norm_rope_fwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, 0, s>>>((const __nv_bfloat16*)x, gamma, cosv, sinv,
                                                                      (__nv_bfloat16*)y, rstd, rows, L, H, D, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
@@ -559,6 +715,20 @@ int qk_norm_rope_fwd(const void* x, const float* gamma, const float* cosv, const
 
 int qk_norm_rope_bwd(const void* dy, const void* x, const float* gamma, const float* cosv, const float* sinv,
                      const float* rstd, void* dx, float* dgamma, long long rows, int L, int H, int D, cudaStream_t s) {
+  const bool al = ((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dx)) &
+                   15u) == 0;
+  if (al && D == 64) {
+    qk_norm_rope_bwd_v<64><<<vec_rope_grid(rows, 4), 256, 0, s>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x,
+                                                                  gamma, cosv, sinv, rstd, (__nv_bfloat16*)dx, dgamma,
+                                                                  rows, L, H);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
+  if (al && D == 128) {
+    qk_norm_rope_bwd_v<128><<<vec_rope_grid(rows, 2), 256, 0, s>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x,
+                                                                   gamma, cosv, sinv, rstd, (__nv_bfloat16*)dx, dgamma,
+                                                                   rows, L, H);
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   qk_norm_rope_bwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, gamma ? D * sizeof(float) : 0, s>>>(
       (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, gamma, cosv, sinv, rstd, (__nv_bfloat16*)dx, dgamma, rows, L,
       H, D);
