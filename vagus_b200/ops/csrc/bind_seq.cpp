@@ -377,6 +377,10 @@ void register_seq_ops(pybind11::module& m) {
   m.def("kda_gates_fwd", &kda_gates_fwd);
   m.def("kda_gates_bwd", &kda_gates_bwd);
   m.def("kda_intra_bwd", &kda_intra_bwd);
+  m.def("gdr_intra_set_trace", [](c10::optional<Tensor> buf) {
+    if (buf) TORCH_CHECK(buf->is_cuda() && buf->numel() >= 8 && buf->element_size() == 8, "gdr_intra_set_trace: 8 x u64");
+    vagus::gdr_intra_set_trace(buf ? reinterpret_cast<unsigned long long*>(buf->data_ptr()) : nullptr);
+  });
   // buf: int64 device tensor of 32 entries, or None
   m.def("kda_set_trace", [](c10::optional<Tensor> buf) {
     if (buf) TORCH_CHECK(buf->is_cuda() && buf->numel() >= 32 && buf->element_size() == 8, "kda_set_trace: 32 x u64");

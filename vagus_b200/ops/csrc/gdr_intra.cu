@@ -230,6 +230,16 @@ struct BwdSmem {
   float dgam[C];
 };
 
+// Phase clock of the backward's CTA (0, 0, 0): clock64() at phase boundaries
+// into g_gdr_intra_trace[event] (16 u64); null: off.
+__device__ unsigned long long* g_gdr_intra_trace_dev = nullptr;
+#define GDR_TR(ev)                                                                                       \
+  do {                                                                                                   \
+    unsigned long long* tr_ = g_gdr_intra_trace_dev;                                                     \
+    if (tr_ != nullptr && threadIdx.x == 0 && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)    \
+      tr_[ev] = clock64();                                                                               \
+  } while (0)
+
 template <int NT>
 __device__ __forceinline__ void row_dot_accumulate(const float (&acc)[1][NT][4], const __nv_bfloat16* X, int ldx,
                                                    int m0, int c0, float* out) {
@@ -277,6 +287,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   const long long qld = (long long)H * DK, vld = (long long)H * DV;
 
   // ---- phase 1: K, Q; gates; KK, QK (kept in registers); M -> T
+  GDR_TR(0);
   load_tile(&sm.K[0][0], KP, krow, qld, C, DK);
   load_tile(&sm.H0[0][0], HP, qrow, qld, C, HK);
   load_tile(&sm.H1[0][0], HP, qrow + HK, qld, C, HK);
@@ -304,7 +315,9 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
       sm.F[i][j] = (j < i) ? sm.beta[i] * kk[0][nt][e] * __expf(sm.gam[i] - sm.gam[j]) : 0.f;
     }
   __syncthreads();
+  GDR_TR(1);
   tri_inverse_inplace(sm.F);
+  GDR_TR(2);
   for (int idx = tid; idx < C * C; idx += THREADS) sm.Tb[idx / C][idx % C] = f2bf(sm.F[idx / C][idx % C]);
 
   // ---- pass A over feature halves: dV, row dots, dT partial products
@@ -351,6 +364,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   }
   __syncthreads();
 
+  GDR_TR(3);
   // ---- dT = (dW K^T) diag(b G) + (dU V^T) diag(b)  (bf16 into H0)
 #pragma unroll
   for (int nt = 0; nt < 4; ++nt)
@@ -381,6 +395,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   warp_mma<1, 4, false, false>(dm, &sm.H1[0][0], HP, &sm.Tb[0][0], C + PAD, m0, n0, C);
   __syncthreads();                            // P (H1) consumed
 
+  GDR_TR(4);
   // ---- elementwise on the fragments: dKK (into F), dQK (bf16 into H1),
   //      gate gradients of D, dbeta partials
   {
@@ -461,6 +476,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
     }
   }
 
+  GDR_TR(5);
   // ---- pass B over feature halves: dK, dQ
   const float glast = sm.gam[C - 1];
 #pragma unroll 1
@@ -538,6 +554,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
   }
   __syncthreads();
 
+  GDR_TR(6);
   // ---- per-row scalars, reverse cumsum
   if (warp == 0) {
     float dgl[2], tail = 0.f;
@@ -563,6 +580,7 @@ intra_bwd_kernel(const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __res
     dg[(tok0 + 2 * lane + 1) * H + h] = s - dgl[0];
     dg[(tok0 + 2 * lane) * H + h] = s;
   }
+  GDR_TR(7);
 }
 
 template <int DK, int DV>
@@ -599,6 +617,10 @@ int gdr_intra_fwd(const GdrIntraArgs& a, cudaStream_t st) {
   if (a.DK == 128 && a.DV == 128) return launch_fwd<128, 128>(a, st);
   if (a.DK == 128 && a.DV == 256) return launch_fwd<128, 256>(a, st);
   return 5;
+}
+
+void gdr_intra_set_trace(unsigned long long* buf) {
+  cudaMemcpyToSymbol(g_gdr_intra_trace_dev, &buf, sizeof(buf));
 }
 
 int gdr_intra_bwd(const GdrIntraBwdArgs& a, cudaStream_t st) {

@@ -174,6 +174,9 @@ int kda_intra_bwd(const KdaIntraBwdArgs& a, cudaStream_t st);
 // boundaries into buf[event] (forward 0..15, backward 16..31; device memory,
 // 32 u64); null switches it off.
 void kda_set_trace(unsigned long long* buf);
+// Phase clock of the GDN intra backward's CTA (0, 0, 0) (8 u64 of device
+// memory); null switches it off.
+void gdr_intra_set_trace(unsigned long long* buf);
 
 // mobius.cu: x_t = (A_t x_{t-1} + B_t) / (C_t x_{t-1} + D_t) along L; A..D, X, gO and the
 // gradients (batch, L, R) fp32 contiguous, x0 and gx0 (batch, R).
