@@ -642,6 +642,99 @@ __global__ void attn_bwd_pre(const AttnBwdArgs a) {
   for (int c = lane; c < a.f.D; c += 32) dq[c] = 0.f;
 }
 
+// Vectorised pre-pass for head dims 64 / 128: DV / 8 lanes per row (16-byte
+// loads of O and dO), rows striding over the grid; dq_acc zeroed with 16-byte
+// stores.
+template <int DV>
+__global__ void __launch_bounds__(256) attn_bwd_pre_v(const AttnBwdArgs a) {
+  constexpr int TPR = DV / 8, RPW = 32 / TPR;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int sub = lane % TPR, rw = lane / TPR;
+  const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
+  const int D = a.f.D;
+  const long long step = (long long)gridDim.x * 8 * RPW;
+  for (long long base = ((long long)blockIdx.x * 8 + warp) * RPW; base < rows; base += step) {
+    const long long row = base + rw;
+    const bool valid = row < rows;
+    float s = 0.f;
+    if (valid) {
+      const int qi = static_cast<int>(row % a.f.Lq);
+      const long long bh = row / a.f.Lq;
+      const long long b = bh / a.f.H, h = bh % a.f.H;
+      const long long off = b * a.f.so_b + h * a.f.so_h + qi * a.f.so_l + 8 * sub;
+      const uint4 ou = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.f.o) + off);
+      const uint4 du = *reinterpret_cast<const uint4*>(reinterpret_cast<const __nv_bfloat16*>(a.dO) + off);
+      const uint32_t ow[4] = {ou.x, ou.y, ou.z, ou.w}, dw[4] = {du.x, du.y, du.z, du.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 of = unpack_bf16x2(ow[j]), df = unpack_bf16x2(dw[j]);
+        s += of.x * df.x + of.y * df.y;
+      }
+    }
+#pragma unroll
+    for (int o = 1; o < TPR; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    if (valid) {
+      if (sub == 0) a.delta[row] = s;
+      float4* dq = reinterpret_cast<float4*>(a.dq_acc + row * D);
+      for (int c = sub; c < D / 4; c += TPR) dq[c] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+}
+
+__global__ void attn_bwd_post(const AttnBwdArgs a);
+
+// dq = scale * dq_acc for head dims 64 / 128: D / 8 lanes per row, 8 values per
+// lane (two 16-byte loads, one 16-byte store into dq's strides)
+template <int D>
+__global__ void __launch_bounds__(256) attn_bwd_post_v(const AttnBwdArgs a) {
+  constexpr int TPR = D / 8, RPW = 32 / TPR;
+  const int warp = threadIdx.x / 32, lane = threadIdx.x & 31;
+  const int sub = lane % TPR, rw = lane / TPR;
+  const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
+  const float sc = a.f.scale;
+  const long long step = (long long)gridDim.x * 8 * RPW;
+  for (long long base = ((long long)blockIdx.x * 8 + warp) * RPW; base < rows; base += step) {
+    const long long row = base + rw;
+    if (row >= rows) continue;
+    const long long bh = row / a.f.Lq, l = row - bh * a.f.Lq, b = bh / a.f.H, h = bh - b * a.f.H;
+    const float4* src = reinterpret_cast<const float4*>(a.dq_acc + row * D + 8 * sub);
+    const float4 v0 = src[0], v1 = src[1];
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.dq) + b * a.sdq_b + h * a.sdq_h + l * a.sdq_l +
+                              8 * sub) =
+        make_uint4(pack_bf16x2(sc * v0.x, sc * v0.y), pack_bf16x2(sc * v0.z, sc * v0.w),
+                   pack_bf16x2(sc * v1.x, sc * v1.y), pack_bf16x2(sc * v1.z, sc * v1.w));
+  }
+}
+
+void launch_bwd_post(const AttnBwdArgs& a, cudaStream_t st) {
+  const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
+  if ((a.f.D == 64 || a.f.D == 128) && (reinterpret_cast<uintptr_t>(a.dq) & 15u) == 0) {
+    const int rpw = 32 / (a.f.D / 8);
+    const long long want = (rows + 8LL * rpw - 1) / (8LL * rpw);
+    const int grid = static_cast<int>(std::min<long long>(std::max<long long>(want, 1), 148LL * 8));
+    if (a.f.D == 64) attn_bwd_post_v<64><<<grid, 256, 0, st>>>(a);
+    else attn_bwd_post_v<128><<<grid, 256, 0, st>>>(a);
+    return;
+  }
+  const long long n = rows * a.f.D;
+  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a);
+}
+
+void launch_bwd_pre(const AttnBwdArgs& a, cudaStream_t st) {
+  const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
+  const bool vec = (a.f.Dv == 64 || a.f.Dv == 128) && a.f.D % 4 == 0 && a.f.so_l % 8 == 0 && a.f.so_h % 8 == 0 &&
+                   a.f.so_b % 8 == 0 && ((reinterpret_cast<uintptr_t>(a.f.o) | reinterpret_cast<uintptr_t>(a.dO)) & 15u) == 0;
+  if (vec) {
+    const int rpw = 32 / (a.f.Dv / 8);
+    const long long want = (rows + 8LL * rpw - 1) / (8LL * rpw);
+    const int grid = static_cast<int>(std::min<long long>(std::max<long long>(want, 1), 148LL * 8));
+    if (a.f.Dv == 64) attn_bwd_pre_v<64><<<grid, 256, 0, st>>>(a);
+    else attn_bwd_pre_v<128><<<grid, 256, 0, st>>>(a);
+    return;
+  }
+  attn_bwd_pre<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+}
+
 template <int D, int DV>
 struct BwdSmem {
   __nv_bfloat16 K[BKEYS][D + PAD];
@@ -1380,28 +1473,26 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
     attr_set[dev] = true;
   }
   const long long rows = (long long)f.B * f.H * f.Lq;
-  attn_bwd_pre<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+  launch_bwd_pre(a, st);
   dim3 grid(static_cast<unsigned>((f.Lk + tcbw::KROWS - 1) / tcbw::KROWS), static_cast<unsigned>(f.B * f.Hk));
   kern<<<grid, tcbw::THREADS, Lt::SMEM, st>>>(*reinterpret_cast<const CUtensorMap*>(mq),
                                                *reinterpret_cast<const CUtensorMap*>(mk),
                                                *reinterpret_cast<const CUtensorMap*>(mv),
                                                *reinterpret_cast<const CUtensorMap*>(mdo),
                                                *reinterpret_cast<const CUtensorMap*>(mdq), p);
-  const long long n = rows * D;
-  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a);
+  launch_bwd_post(a, st);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
 template <int D, int DV>
 int launch_bwd(const AttnBwdArgs& a, cudaStream_t st) {
   const long long rows = (long long)a.f.B * a.f.H * a.f.Lq;
-  attn_bwd_pre<<<static_cast<unsigned>((rows + 7) / 8), 256, 0, st>>>(a);
+  launch_bwd_pre(a, st);
   const size_t sm = sizeof(BwdSmem<D, DV>);
   if (!set_smem(attn_bwd_kernel<D, DV>, sm)) return 3;
   dim3 grid(static_cast<unsigned>((a.f.Lk + BKEYS - 1) / BKEYS), static_cast<unsigned>(a.f.B * a.f.Hk));
   attn_bwd_kernel<D, DV><<<grid, BWARPS * 32, sm, st>>>(a);
-  const long long n = rows * a.f.D;
-  attn_bwd_post<<<static_cast<unsigned>((n / 4 + 255) / 256), 256, 0, st>>>(a);
+  launch_bwd_post(a, st);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
