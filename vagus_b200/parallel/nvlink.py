@@ -223,10 +223,30 @@ class NvlinkAllReduce:
     def ddp_hook(self, _state, bucket):
         # no return annotation: DDP's hook check accepts only none or exactly Future[Tensor]
         buf = bucket.buffer()
-        self(buf, dist.ReduceOp.AVG)
-        fut = torch.futures.Future()
-        fut.set_result(buf)                 # stream-ordered: later users run after our kernels
+        if not buf.is_cuda:
+            self(buf, dist.ReduceOp.AVG)
+            fut = torch.futures.Future()
+            fut.set_result(buf)
+            return fut
+        # On a side stream, so the bucket's all-reduce overlaps the rest of the
+        # backward (as DDP's own NCCL all-reduce does).  The future is
+        # CUDA-aware: setting it inside the side stream records an event there,
+        # and whoever waits on it (DDP copying the bucket back into the
+        # gradients) waits for that event on its own stream.
+        side = self._side_stream(buf.device)
+        side.wait_stream(torch.cuda.current_stream(buf.device))
+        with torch.cuda.stream(side):
+            self(buf, dist.ReduceOp.AVG)
+            fut = torch.futures.Future(devices=[buf.device])
+            fut.set_result(buf)
         return fut
+
+    def _side_stream(self, device):
+        st = getattr(self, "_stream", None)
+        if st is None or st.device != device:
+            st = torch.cuda.Stream(device=device)
+            self._stream = st
+        return st
 
     def close(self) -> None:
         close_heaps(self.own, self.bases)
