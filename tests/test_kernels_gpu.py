@@ -176,6 +176,88 @@ def test_qk_norm_rope(norm, rope, D):
         assert rel(gm.grad, gr.grad) < 2e-2
 
 
+def test_qk_norm_rope_pitched():
+    """The RoPE kernels on a column slice of a packed projection (token pitch
+    wider than the heads), writing the input gradient into a slice of a packed
+    gradient: same values as on dense copies."""
+    from vagus_b200.ops import native
+    from vagus_b200.models.rope import RoPE
+    B, L, H, D, NP, c0 = 2, 45, 3, 64, 512, 128
+    P = torch.randn(B, L, NP, device=DEV).bfloat16()
+    x = P[:, :, c0:c0 + H * D].view(B, L, H, D)
+    gm = 1 + 0.1 * torch.randn(D, device=DEV)
+    cos, sin = (t.float().contiguous() for t in RoPE(H * D, D, 64).to(DEV).tables(L, 3))
+    C = native()
+    y, rs = C.qk_norm_rope_fwd(x, gm, cos, sin, 1e-6)
+    y0, rs0 = C.qk_norm_rope_fwd(x.contiguous(), gm, cos, sin, 1e-6)
+    assert torch.equal(y, y0) and torch.equal(rs, rs0)
+    dy = torch.randn(B, L, H, D, device=DEV).bfloat16()
+    dP = torch.zeros(B, L, NP, device=DEV, dtype=torch.bfloat16)
+    dx_slice = dP[:, :, c0:c0 + H * D].view(B, L, H, D)
+    _, dg = C.qk_norm_rope_bwd(dy, x, gm, cos, sin, rs, dx_slice)
+    dx0, dg0 = C.qk_norm_rope_bwd(dy, x.contiguous(), gm, cos, sin, rs0)
+    assert torch.equal(dx_slice, dx0) and rel(dg, dg0) < 1e-5
+    assert dP[:, :, :c0].abs().sum() == 0 and dP[:, :, c0 + H * D:].abs().sum() == 0
+
+
+@pytest.mark.parametrize("H,Hk,D,vm,rope,qkn", [(8, 8, 64, 1, True, False), (4, 2, 128, 1, True, True),
+                                                  (4, 2, 64, 2, False, False), (4, 4, 64, 1, False, True)])
+def test_attention_layer_fused_matches_fp32(H, Hk, D, vm, rope, qkn):
+    """The fused layer (q / k / v packed into one GEMM, RoPE on slices of it,
+    attention reading v out of it, one dgrad and one wgrad GEMM) against the
+    same module run unfused in fp32: output, input gradient, every weight
+    gradient and the qk-norm gains."""
+    from vagus_b200 import ops
+    from vagus_b200.models.attention import SoftmaxAttention
+    from vagus_b200.models.rope import RoPE
+    B, L, dim = 2, 256, H * D
+    m = SoftmaxAttention(dim, H, Hk, vm, qk_norm=qkn, rope=RoPE(dim, D, L) if rope else None).to(DEV)
+    if qkn:
+        with torch.no_grad():
+            m.q_norm.gamma.add_(0.1 * torch.randn_like(m.q_norm.gamma))
+            m.k_norm.gamma.add_(0.1 * torch.randn_like(m.k_norm.gamma))
+    x = torch.randn(B, L, dim, device=DEV)
+    xb = x.bfloat16().requires_grad_(True)
+    assert ops.attention_layer_ok(m, xb)
+    y = m.forward_pre_out(xb)
+    dy = torch.randn_like(y, dtype=torch.float32)
+    (y.float() * dy).sum().backward()
+    got = {n: p.grad.clone() for n, p in m.named_parameters() if p.grad is not None}
+    m.zero_grad()
+    xr = x.clone().requires_grad_(True)
+    assert not ops.attention_layer_ok(m, xr)
+    yr = m.forward_pre_out(xr)
+    (yr * dy).sum().backward()
+    assert rel(y, yr) < 2e-2 and rel(xb.grad, xr.grad) < 3e-2
+    ref = {n: p.grad for n, p in m.named_parameters() if p.grad is not None}
+    assert set(got) == set(ref) and {"wq.weight", "wk.weight", "wv.weight"} <= set(got)
+    for n, g in ref.items():
+        assert rel(got[n], g) < 3e-2, n
+
+
+def test_transformerpp_bf16_matches_cpu_fp32():
+    """A small Transformer++ (head dim 64, fused attention layers, SwiGLU,
+    fused CE) under bf16 autocast on the GPU against the same weights in fp32
+    on the CPU: loss and every parameter gradient."""
+    from vagus_b200.models import build_model
+    from vagus_b200.models.losses import make_ce
+    args = dict(vocab_size=2048, dim=256, head_dim=64, context_len=512, layer_count=2, ffn_hidden_dim=704)
+    model = build_model("TransformerPP", args).to(DEV)
+    ref = build_model("TransformerPP", args)
+    ref.load_state_dict({k: v.detach().cpu() for k, v in model.state_dict().items()})
+    tok = torch.randint(0, 2048, (2, 257), device=DEV)
+    with torch.autocast("cuda", dtype=torch.bfloat16):
+        loss = make_ce("fused")(model(tok[:, :-1], return_hidden=True), model.head.weight, tok[:, 1:])
+    loss.backward()
+    tc = tok.cpu()
+    loss_ref = make_ce("full")(ref(tc[:, :-1], return_hidden=True), ref.head.weight, tc[:, 1:])
+    loss_ref.backward()
+    assert abs(loss.item() - loss_ref.item()) <= 1e-2 * abs(loss_ref.item())
+    got = dict(model.named_parameters())
+    for n, p in ref.named_parameters():
+        assert rel(got[n].grad.cpu(), p.grad) < 5e-2, n
+
+
 def _conv_ref(x, w, hd, l2):
     D, K = w.shape[0], w.shape[-1]
     y = F.conv1d(F.pad(x.transpose(1, 2), (K - 1, 0)), w, groups=D).transpose(1, 2)

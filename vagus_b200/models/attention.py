@@ -103,7 +103,11 @@ class SoftmaxAttention(nn.Module, Mixer):
         return ops.linear(out, self.wo.weight) if self.out_proj else out
 
     def forward_pre_out(self, x, is_causal: bool = True):
-        """The (gated) head concat that feeds ``wo``."""
+        """The (gated) head concat that feeds ``wo``.  On CUDA in bf16 without
+        short conv or output gate the q / k / v projections run as one packed
+        GEMM inside ``ops.attention_layer``."""
+        if ops.attention_layer_ok(self, x):
+            return ops.attention_layer(self, x, is_causal)
         B, L = x.shape[0], x.shape[1]
         qp, kp, vp = ops.linear(x, self.wq.weight), ops.linear(x, self.wk.weight), ops.linear(x, self.wv.weight)
         if self.short_conv_size is not None:

@@ -8,7 +8,7 @@ falling back to eager PyTorch.
 """
 
 from ._core import BF16, check_error, kernels_active, native  # noqa: F401
-from .attention import attention, attention_ref  # noqa: F401
+from .attention import attention, attention_ref, attention_layer, attention_layer_ok  # noqa: F401
 from .ce import fused_linear_ce  # noqa: F401
 from .gdn import conv_silu, gdn_mixer, gdr_chunk, gdr_decode  # noqa: F401
 from .kda import kda_mixer  # noqa: F401

@@ -58,10 +58,22 @@ Tensor grad_like(const Tensor& x) {
   return ok ? t : torch::empty(x.sizes(), x.options());
 }
 
+// A caller-given gradient buffer (a slice of a packed projection's gradient,
+// say) or a fresh one in the layout of x
+Tensor grad_out(const c10::optional<Tensor>& given, const Tensor& x, const char* what) {
+  if (!given.has_value() || !given->defined()) return grad_like(x);
+  const Tensor& t = *given;
+  TORCH_CHECK(t.sizes() == x.sizes() && t.scalar_type() == at::kBFloat16 && t.is_cuda(), "attn_bwd: ", what,
+              " must be shaped like its input, bf16 on the GPU");
+  return t;
+}
+
 // dO in o's layout (copied into it when the strides differ) -> dq, dk, dv in
-// the layouts of q, k, v
+// the layouts of q, k, v, or written into the given buffers (any strides that
+// are multiples of 8 elements)
 std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, Tensor dO, bool causal,
-                             double scale) {
+                             double scale, c10::optional<Tensor> dq_out, c10::optional<Tensor> dk_out,
+                             c10::optional<Tensor> dv_out) {
   TORCH_CHECK(lse.is_contiguous() && dO.sizes() == o.sizes(), "attn_bwd: contiguous lse, dO shaped like o");
   if (dO.strides() != o.strides()) {
     auto t = torch::empty_like(o);
@@ -73,7 +85,7 @@ std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse,
   vagus::AttnBwdArgs b;
   b.f = a;
   b.dO = dO.data_ptr();
-  auto dq = grad_like(q), dk = grad_like(k), dv = grad_like(v);
+  auto dq = grad_out(dq_out, q, "dq_out"), dk = grad_out(dk_out, k, "dk_out"), dv = grad_out(dv_out, v, "dv_out");
   b.sdq_b = dq.stride(0); b.sdq_h = dq.stride(1); b.sdq_l = dq.stride(2);
   b.sdk_b = dk.stride(0); b.sdk_h = dk.stride(1); b.sdk_l = dk.stride(2);
   b.sdv_b = dv.stride(0); b.sdv_h = dv.stride(1); b.sdv_l = dv.stride(2);
@@ -89,7 +101,10 @@ std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse,
 
 void register_attn_ops(pybind11::module& m) {
   m.def("attn_fwd", &attn_fwd);
-  m.def("attn_bwd", &attn_bwd);
+  m.def("attn_bwd", &attn_bwd, pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("o"),
+        pybind11::arg("lse"), pybind11::arg("dO"), pybind11::arg("causal"), pybind11::arg("scale"),
+        pybind11::arg("dq_out") = pybind11::none(), pybind11::arg("dk_out") = pybind11::none(),
+        pybind11::arg("dv_out") = pybind11::none());
   // buf: int64 device tensor of 512 entries, or None
   m.def("attn_set_trace", [](c10::optional<Tensor> buf) {
     if (buf) TORCH_CHECK(buf->is_cuda() && buf->numel() >= 512 && buf->element_size() == 8, "attn_set_trace: 512 x u64");

@@ -255,34 +255,59 @@ std::vector<Tensor> rmsnorm_gated_bwd(Tensor dy, Tensor o, Tensor g, Tensor gamm
   return {dO, dgamma};
 }
 
-// x: (B, L, H, D) bf16 contiguous; cos/sin (L, D/2) fp32 or undefined
+// Token pitch (elements) of a (B, L, H, D) tensor whose heads of one token are
+// dense and whose tokens are evenly spaced (a column slice of a packed
+// projection, for instance); -1 when the layout is not of that form.
+int64_t token_pitch(const Tensor& t) {
+  if (t.dim() != 4 || t.stride(3) != 1 || t.stride(2) != t.size(3)) return -1;
+  if (t.size(0) > 1 && t.stride(0) != t.size(1) * t.stride(1)) return -1;
+  return t.stride(1);
+}
+
+Tensor pitched(const Tensor& t) { return token_pitch(t) > 0 ? t : t.contiguous(); }
+
+// x: (B, L, H, D) bf16 with a token pitch (dense or a column slice of a packed
+// projection); cos/sin (L, D/2) fp32 or undefined.  y is dense.
 std::vector<Tensor> qk_norm_rope_fwd(Tensor x, c10::optional<Tensor> gamma, c10::optional<Tensor> cosv,
                                      c10::optional<Tensor> sinv, double eps) {
-  TORCH_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && x.dim() == 4, "qk_norm_rope: (B,L,H,D) bf16");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.dim() == 4, "qk_norm_rope: (B,L,H,D) bf16");
+  x = pitched(x);
   const int L = static_cast<int>(x.size(1)), H = static_cast<int>(x.size(2)), D = static_cast<int>(x.size(3));
   const int64_t rows = x.numel() / D;
-  auto y = torch::empty_like(x);
+  auto y = torch::empty(x.sizes(), x.options());
   auto rstd = torch::empty({rows}, x.options().dtype(at::kFloat));
   const bool hg = gamma.has_value() && gamma->defined(), hr = cosv.has_value() && cosv->defined();
   check(vagus::qk_norm_rope_fwd(x.data_ptr(), hg ? gamma->data_ptr<float>() : nullptr,
                                 hr ? cosv->data_ptr<float>() : nullptr, hr ? sinv->data_ptr<float>() : nullptr,
-                                y.data_ptr(), rstd.data_ptr<float>(), rows, L, H, D, static_cast<float>(eps), stream()),
+                                y.data_ptr(), rstd.data_ptr<float>(), rows, L, H, D, static_cast<float>(eps),
+                                token_pitch(x), 0, stream()),
         "qk_norm_rope_fwd");
   return {y, rstd};
 }
 
+// dy, x and dx_out may each carry a token pitch; dx is dense when dx_out is not given
 std::vector<Tensor> qk_norm_rope_bwd(Tensor dy, Tensor x, c10::optional<Tensor> gamma, c10::optional<Tensor> cosv,
-                                     c10::optional<Tensor> sinv, Tensor rstd) {
-  dy = dy.contiguous();
+                                     c10::optional<Tensor> sinv, Tensor rstd, c10::optional<Tensor> dx_out) {
+  dy = pitched(dy);
+  x = pitched(x);
+  TORCH_CHECK(dy.sizes() == x.sizes(), "qk_norm_rope_bwd: dy shaped like x");
   const int L = static_cast<int>(x.size(1)), H = static_cast<int>(x.size(2)), D = static_cast<int>(x.size(3));
   const int64_t rows = x.numel() / D;
-  auto dx = torch::empty_like(x);
+  Tensor dx;
+  if (dx_out.has_value() && dx_out->defined()) {
+    dx = *dx_out;
+    TORCH_CHECK(dx.sizes() == x.sizes() && dx.scalar_type() == at::kBFloat16 && token_pitch(dx) > 0,
+                "qk_norm_rope_bwd: dx_out (B, L, H, D) bf16 with a token pitch");
+  } else {
+    dx = torch::empty(x.sizes(), x.options());
+  }
   const bool hg = gamma.has_value() && gamma->defined(), hr = cosv.has_value() && cosv->defined();
   auto dgamma = torch::zeros({hg ? D : 0}, x.options().dtype(at::kFloat));
   check(vagus::qk_norm_rope_bwd(dy.data_ptr(), x.data_ptr(), hg ? gamma->data_ptr<float>() : nullptr,
                                 hr ? cosv->data_ptr<float>() : nullptr, hr ? sinv->data_ptr<float>() : nullptr,
                                 rstd.data_ptr<float>(), dx.data_ptr(), hg ? dgamma.data_ptr<float>() : nullptr, rows,
-                                L, H, D, stream()), "qk_norm_rope_bwd");
+                                L, H, D, token_pitch(dy), token_pitch(x), token_pitch(dx), stream()),
+        "qk_norm_rope_bwd");
   return {dx, dgamma};
 }
 
@@ -399,7 +424,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rmsnorm_gated_fwd", &rmsnorm_gated_fwd);
   m.def("rmsnorm_gated_bwd", &rmsnorm_gated_bwd);
   m.def("qk_norm_rope_fwd", &qk_norm_rope_fwd);
-  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd);
+  m.def("qk_norm_rope_bwd", &qk_norm_rope_bwd, py::arg("dy"), py::arg("x"), py::arg("gamma"), py::arg("cosv"),
+        py::arg("sinv"), py::arg("rstd"), py::arg("dx_out") = py::none());
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
   m.def("sigmoid_gate_fwd", &sigmoid_gate_fwd);

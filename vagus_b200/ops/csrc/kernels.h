@@ -18,10 +18,12 @@ int rmsnorm_gated_fwd(const void* o, const void* g, long long ldg, int H, const 
 int rmsnorm_gated_bwd(const void* dy, const void* o, const void* g, long long ldg, int H, const float* gamma,
                       const float* rstd, void* dO, void* dG, long long lddg, float* dgamma, long long rows, int D,
                       cudaStream_t s);
+// ld*: token pitch (elements) of each (B, L, H, D) operand; 0 means dense (H * D)
 int qk_norm_rope_fwd(const void* x, const float* gamma, const float* cosv, const float* sinv, void* y, float* rstd,
-                     long long rows, int L, int H, int D, float eps, cudaStream_t s);
+                     long long rows, int L, int H, int D, float eps, long long ldx, long long ldy, cudaStream_t s);
 int qk_norm_rope_bwd(const void* dy, const void* x, const float* gamma, const float* cosv, const float* sinv,
-                     const float* rstd, void* dx, float* dgamma, long long rows, int L, int H, int D, cudaStream_t s);
+                     const float* rstd, void* dx, float* dgamma, long long rows, int L, int H, int D, long long lddy,
+                     long long ldx, long long lddx, cudaStream_t s);
 
 // elementwise.cu
 int swiglu_fwd(const void* u, void* s, long long rows, int F, cudaStream_t st);

@@ -447,7 +447,7 @@ template <int D>
 __global__ void __launch_bounds__(256)
 qk_norm_rope_fwd_v(const __nv_bfloat16* __restrict__ x, const float* __restrict__ gamma,
                    const float* __restrict__ cosv, const float* __restrict__ sinv, __nv_bfloat16* __restrict__ y,
-                   float* __restrict__ rstd, long long rows, int L, int H, float eps) {
+                   float* __restrict__ rstd, long long rows, int L, int H, float eps, long long ldx, long long ldy) {
   constexpr int TPR = D / 8, RPW = 32 / TPR, HALF = D / 2;
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int sub = lane % TPR, rw = lane / TPR;
@@ -459,9 +459,10 @@ qk_norm_rope_fwd_v(const __nv_bfloat16* __restrict__ x, const float* __restrict_
   for (long long base = ((long long)blockIdx.x * 8 + warp) * RPW; base < rows; base += step) {
     const long long r = base + rw;
     const bool valid = r < rows;
+    const long long t = r / H, hd = (r - t * H) * D;    // token, channel offset of the head in the token
     float v[8];
     {
-      const uint4 u = valid ? *reinterpret_cast<const uint4*>(x + r * D + c0) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 u = valid ? *reinterpret_cast<const uint4*>(x + t * ldx + hd + c0) : make_uint4(0u, 0u, 0u, 0u);
       const uint32_t w[4] = {u.x, u.y, u.z, u.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) { const float2 f = unpack_bf16x2(w[j]); v[2 * j] = f.x; v[2 * j + 1] = f.y; }
@@ -479,7 +480,7 @@ qk_norm_rope_fwd_v(const __nv_bfloat16* __restrict__ x, const float* __restrict_
       for (int j = 0; j < 8; ++j) v[j] = bf2f(f2bf(v[j] * rs)) * gm[j];
     }
     if (cosv && valid) {
-      const long long l = (r / H) % L;
+      const long long l = t % L;
       const float4 c4 = *reinterpret_cast<const float4*>(cosv + l * HALF + 4 * sub);
       const float4 s4 = *reinterpret_cast<const float4*>(sinv + l * HALF + 4 * sub);
       const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -491,7 +492,7 @@ qk_norm_rope_fwd_v(const __nv_bfloat16* __restrict__ x, const float* __restrict_
       }
     }
     if (valid)
-      *reinterpret_cast<uint4*>(y + r * D + c0) =
+      *reinterpret_cast<uint4*>(y + t * ldy + hd + c0) =
           make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
   }
 }
@@ -501,7 +502,7 @@ __global__ void __launch_bounds__(256)
 qk_norm_rope_bwd_v(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x,
                    const float* __restrict__ gamma, const float* __restrict__ cosv, const float* __restrict__ sinv,
                    const float* __restrict__ rstd, __nv_bfloat16* __restrict__ dx, float* __restrict__ dgamma,
-                   long long rows, int L, int H) {
+                   long long rows, int L, int H, long long lddy, long long ldx, long long lddx) {
   constexpr int TPR = D / 8, RPW = 32 / TPR, HALF = D / 2;
   __shared__ float sg[D];
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -518,10 +519,12 @@ qk_norm_rope_bwd_v(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
   for (long long base = ((long long)blockIdx.x * 8 + warp) * RPW; base < rows; base += step) {
     const long long r = base + rw;
     const bool valid = r < rows;
+    const long long t = r / H, hd = (r - t * H) * D;
     float d[8], xv[8];
     {
-      const uint4 u = valid ? *reinterpret_cast<const uint4*>(dy + r * D + c0) : make_uint4(0u, 0u, 0u, 0u);
-      const uint4 q = valid && gamma ? *reinterpret_cast<const uint4*>(x + r * D + c0) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 u = valid ? *reinterpret_cast<const uint4*>(dy + t * lddy + hd + c0) : make_uint4(0u, 0u, 0u, 0u);
+      const uint4 q =
+          valid && gamma ? *reinterpret_cast<const uint4*>(x + t * ldx + hd + c0) : make_uint4(0u, 0u, 0u, 0u);
       const uint32_t w[4] = {u.x, u.y, u.z, u.w}, wq[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
@@ -530,7 +533,7 @@ qk_norm_rope_bwd_v(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
       }
     }
     if (cosv && valid) {                                  // un-rotate: the transpose of the rotation
-      const long long l = (r / H) % L;
+      const long long l = t % L;
       const float4 c4 = *reinterpret_cast<const float4*>(cosv + l * HALF + 4 * sub);
       const float4 s4 = *reinterpret_cast<const float4*>(sinv + l * HALF + 4 * sub);
       const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
@@ -557,7 +560,7 @@ qk_norm_rope_bwd_v(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __
       for (int j = 0; j < 8; ++j) d[j] = rs * (d[j] * gm[j] - xv[j] * rs * dot);
     }
     if (valid)
-      *reinterpret_cast<uint4*>(dx + r * D + c0) =
+      *reinterpret_cast<uint4*>(dx + t * lddx + hd + c0) =
           make_uint4(pack_bf16x2(d[0], d[1]), pack_bf16x2(d[2], d[3]), pack_bf16x2(d[4], d[5]), pack_bf16x2(d[6], d[7]));
   }
   if (gamma) {
@@ -696,39 +699,50 @@ int rmsnorm_gated_bwd(const void* dy, const void* o, const void* g, long long ld
 }
 
 int qk_norm_rope_fwd(const void* x, const float* gamma, const float* cosv, const float* sinv, void* y, float* rstd,
-                     long long rows, int L, int H, int D, float eps, cudaStream_t s) {
-  const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0;
+                     long long rows, int L, int H, int D, float eps, long long ldx, long long ldy, cudaStream_t s) {
+  const long long dense = static_cast<long long>(H) * D;
+  if (ldx <= 0) ldx = dense;
+  if (ldy <= 0) ldy = dense;
+  const bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y)) & 15u) == 0 && ldx % 8 == 0 &&
+                  ldy % 8 == 0;
   if (al && D == 64) {
     qk_norm_rope_fwd_v<64><<<vec_rope_grid(rows, 4), 256, 0, s>>>((const __nv_bfloat16*)x, gamma, cosv, sinv,
-                                                                  (__nv_bfloat16*)y, rstd, rows, L, H, eps);
+                                                                  (__nv_bfloat16*)y, rstd, rows, L, H, eps, ldx, ldy);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
   if (al && D == 128) {
     qk_norm_rope_fwd_v<128><<<vec_rope_grid(rows, 2), 256, 0, s>>>((const __nv_bfloat16*)x, gamma, cosv, sinv,
-                                                                   (__nv_bfloat16*)y, rstd, rows, L, H, eps);
+                                                                   (__nv_bfloat16*)y, rstd, rows, L, H, eps, ldx, ldy);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
+  if (ldx != dense || ldy != dense) return 5;          // the row-per-warp kernel reads dense rows only
   qk_norm_rope_fwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, 0, s>>>((const __nv_bfloat16*)x, gamma, cosv, sinv,
                                                                      (__nv_bfloat16*)y, rstd, rows, L, H, D, eps);
   return cudaGetLastError() == cudaSuccess ? 0 : 3;
 }
 
 int qk_norm_rope_bwd(const void* dy, const void* x, const float* gamma, const float* cosv, const float* sinv,
-                     const float* rstd, void* dx, float* dgamma, long long rows, int L, int H, int D, cudaStream_t s) {
+                     const float* rstd, void* dx, float* dgamma, long long rows, int L, int H, int D, long long lddy,
+                     long long ldx, long long lddx, cudaStream_t s) {
+  const long long dense = static_cast<long long>(H) * D;
+  if (lddy <= 0) lddy = dense;
+  if (ldx <= 0) ldx = dense;
+  if (lddx <= 0) lddx = dense;
   const bool al = ((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(dx)) &
-                   15u) == 0;
+                   15u) == 0 && lddy % 8 == 0 && ldx % 8 == 0 && lddx % 8 == 0;
   if (al && D == 64) {
     qk_norm_rope_bwd_v<64><<<vec_rope_grid(rows, 4), 256, 0, s>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x,
                                                                   gamma, cosv, sinv, rstd, (__nv_bfloat16*)dx, dgamma,
-                                                                  rows, L, H);
+                                                                  rows, L, H, lddy, ldx, lddx);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
   if (al && D == 128) {
     qk_norm_rope_bwd_v<128><<<vec_rope_grid(rows, 2), 256, 0, s>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)x,
                                                                    gamma, cosv, sinv, rstd, (__nv_bfloat16*)dx, dgamma,
-                                                                   rows, L, H);
+                                                                   rows, L, H, lddy, ldx, lddx);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
+  if (lddy != dense || ldx != dense || lddx != dense) return 5;
   qk_norm_rope_bwd_k<<<blocks_for(rows), 32 * ROWS_PER_CTA, gamma ? D * sizeof(float) : 0, s>>>(
       (const __nv_bfloat16*)dy, (const __nv_bfloat16*)x, gamma, cosv, sinv, rstd, (__nv_bfloat16*)dx, dgamma, rows, L,
       H, D);
