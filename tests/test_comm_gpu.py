@@ -4,7 +4,7 @@ FSDP2 with the custom collectives installed against FSDP2 on NCCL, the fused
 Muon scatter, and the all-reduce (raw and as DDP's bucket hook)."""
 
 import os
-import socket
+import tempfile
 
 import pytest
 import torch
@@ -14,21 +14,18 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _rdzv():
+    """A file rendezvous for the spawned ranks: no TCP port to collide with."""
+    return "file://" + os.path.join(tempfile.mkdtemp(prefix="vagus_rdzv_"), "store")
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, rdzv, q):
     try:
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world))
         torch.cuda.set_device(rank)
         import datetime
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{rank}"),
-                                timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world,
+                                device_id=torch.device(f"cuda:{rank}"), timeout=datetime.timedelta(seconds=120))
         from vagus_b200 import ops
         from vagus_b200.parallel.nvlink import NvlinkAllGather, NvlinkHeap, NvlinkReduceScatter
         heap = NvlinkHeap(dist.group.WORLD, ag_cap=1 << 20, rs_cap=4 << 20)
@@ -93,8 +90,8 @@ def test_nvlink_collectives_match_nccl():
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    rdzv = _rdzv()
+    procs = [ctx.Process(target=_worker, args=(r, world, rdzv, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
@@ -107,13 +104,13 @@ def test_nvlink_collectives_match_nccl():
             assert e <= tol, (rank, kind, it, e)
 
 
-def _muon_worker(rank, world, port, q):
+def _muon_worker(rank, world, rdzv, q):
     try:
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world))
         torch.cuda.set_device(rank)
         import datetime
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{rank}"),
-                                timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world,
+                                device_id=torch.device(f"cuda:{rank}"), timeout=datetime.timedelta(seconds=120))
         from torch.distributed.device_mesh import init_device_mesh
         from torch.distributed.tensor import Shard, distribute_tensor
         from vagus_b200 import ops
@@ -155,8 +152,8 @@ def test_muon_fused_scatter_matches_allgather():
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_muon_worker, args=(r, world, port, q)) for r in range(world)]
+    rdzv = _rdzv()
+    procs = [ctx.Process(target=_muon_worker, args=(r, world, rdzv, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]
@@ -168,14 +165,14 @@ def test_muon_fused_scatter_matches_allgather():
             assert e == 0.0, (rank, kind, i, e)
 
 
-def _allreduce_worker(rank, world, port, q):
+def _allreduce_worker(rank, world, rdzv, q):
     try:
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world),
                           NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
         import datetime
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{rank}"),
-                                timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world,
+                                device_id=torch.device(f"cuda:{rank}"), timeout=datetime.timedelta(seconds=120))
         from vagus_b200 import ops
         from vagus_b200.parallel import wrap_ddp
         from vagus_b200.parallel.nvlink import NvlinkAllReduce
@@ -241,8 +238,8 @@ def test_nvlink_all_reduce_and_ddp_hook_match_nccl():
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_allreduce_worker, args=(r, world, port, q)) for r in range(world)]
+    rdzv = _rdzv()
+    procs = [ctx.Process(target=_allreduce_worker, args=(r, world, rdzv, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]

@@ -4,7 +4,7 @@ gathered-B GEMM reads the peer's rows over NVLink inside its own TMA loads;
 the product equals all-gather + matmul."""
 
 import os
-import socket
+import tempfile
 
 import pytest
 import torch
@@ -14,21 +14,18 @@ import torch.multiprocessing as mp
 pytestmark = pytest.mark.gpu
 
 
-def _port():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    p = s.getsockname()[1]
-    s.close()
-    return p
+def _rdzv():
+    """A file rendezvous for the spawned ranks: no TCP port to collide with."""
+    return "file://" + os.path.join(tempfile.mkdtemp(prefix="vagus_rdzv_"), "store")
 
 
-def _ag_gemm_worker(rank, world, port, q):
+def _ag_gemm_worker(rank, world, rdzv, q):
     try:
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world))
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world))
         torch.cuda.set_device(rank)
         import datetime
-        dist.init_process_group("nccl", device_id=torch.device(f"cuda:{rank}"),
-                                timeout=datetime.timedelta(seconds=120))
+        dist.init_process_group("nccl", init_method=rdzv, rank=rank, world_size=world,
+                                device_id=torch.device(f"cuda:{rank}"), timeout=datetime.timedelta(seconds=120))
         from vagus_b200 import ops
         from vagus_b200.parallel.nvlink import PeerRowShards
         errs = []
@@ -63,8 +60,8 @@ def test_gathered_weight_gemm_matches_allgather():
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_ag_gemm_worker, args=(r, world, port, q)) for r in range(world)]
+    rdzv = _rdzv()
+    procs = [ctx.Process(target=_ag_gemm_worker, args=(r, world, rdzv, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in range(world)]

@@ -544,6 +544,190 @@ conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __rest
   }
 }
 
+// --------------------------------------------- backward, U tokens per step --
+// The run kernel above with the token loop unrolled U ways.  The U tokens'
+// chains (input window, SiLU, the head's dot product, du) interleave; the
+// pair's dot-product exchange is one barrier per step instead of one per
+// token; the loads run two steps (2 U tokens) ahead in two register sets that
+// alternate between the steps, so the prefetch queue costs no register moves.
+// Per element only x, g f and z f stay live across the exchange, where
+// z = silu(u) and f = silu'(u) = s (1 + u - z):  du = rn g f - c3 z f with
+// c3 = rn^3 <g, z>_head under the L2 norm, du = g f without it.
+template <int VEC, int U, int NT, int MINB>
+__global__ void __launch_bounds__(NT, MINB)
+conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
+                const float* __restrict__ w, const float* __restrict__ rnorm, __nv_bfloat16* __restrict__ dx,
+                long long lddx, float* __restrict__ dw, long long L, int D, int l2) {
+  constexpr int K = 4;
+  constexpr int HD = VEC * 64;
+  constexpr int PAIRS = NT / 64;
+  __shared__ float dot_x[PAIRS][2][2][U];     // [pair][warp of the pair][step parity][token]
+  __shared__ float red[PAIRS][K][HD];
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int pair = warp >> 1, half = warp & 1;
+  const int ch = (half * 32 + lane) * VEC;   // first channel of this thread within the head
+  const long long b = blockIdx.z;
+  const int head = blockIdx.y;
+  const int nH = D / HD;
+  const int c0 = head * HD + ch;
+  float wr[K][VEC];
+#pragma unroll
+  for (int j = 0; j < VEC; ++j) {
+    const float4 t = *reinterpret_cast<const float4*>(w + (long long)(c0 + j) * K);
+    wr[0][j] = t.x; wr[1][j] = t.y; wr[2][j] = t.z; wr[3][j] = t.w;
+  }
+  float dwa[K][VEC];
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) dwa[k][j] = 0.f;
+  const long long runs = (L + RUN - 1) / RUN;
+  const int bar = 1 + pair;                  // named barrier of this warp pair (0 is __syncthreads)
+  const __nv_bfloat16* xb = x + b * L * ldx + c0;
+  const __nv_bfloat16* gb = dy + b * L * D + c0;
+  int par = 0;
+  for (long long run = (long long)blockIdx.x * PAIRS + pair; run < runs; run += (long long)gridDim.x * PAIRS) {
+    const long long t0 = run * RUN;
+    const long long t_end = min(L, t0 + RUN);          // the run's own tokens end here
+    const long long t_load = min(L, t0 + RUN + K - 1); // du is needed up to here (exclusive)
+    float xw[K - 1][VEC], dw3[K - 1][VEC];             // x and du of the 1st .. 3rd token before the step
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) {
+      const long long t = t0 - 1 - i;
+      uint32_t r[VEC / 2];
+      ldg_row<VEC>(xb + t * ldx, t >= 0, r);
+      unpack_row<VEC>(r, xw[i]);
+#pragma unroll
+      for (int j = 0; j < VEC; ++j) dw3[i][j] = 0.f;
+    }
+    uint32_t ax[U][VEC / 2], ag[U][VEC / 2], bx[U][VEC / 2], bg[U][VEC / 2];
+    auto load_step = [&](uint32_t (&qx)[U][VEC / 2], uint32_t (&qg)[U][VEC / 2], long long ts) {
+#pragma unroll
+      for (int i = 0; i < U; ++i) {
+        const long long t = ts + i;
+        const bool ok = t < t_load;
+        ldg_row<VEC>(xb + t * ldx, ok, qx[i]);
+        ldg_row<VEC>(gb + t * D, ok, qg[i]);
+      }
+    };
+    // one step: du of tokens ts .. ts + U - 1, dx of tokens ts - 3 .. ts + U - 4
+    auto step = [&](uint32_t (&qx)[U][VEC / 2], uint32_t (&qg)[U][VEC / 2], long long ts) {
+      float xc[U][VEC], gf[U][VEC], zf[U][VEC], dot[U], rn[U];
+#pragma unroll
+      for (int i = 0; i < U; ++i) {
+        unpack_row<VEC>(qx[i], xc[i]);
+        unpack_row<VEC>(qg[i], gf[i]);
+        rn[i] = l2 && ts + i < L ? __ldg(rnorm + (b * L + ts + i) * nH + head) : 0.f;
+      }
+      load_step(qx, qg, ts + 2 * U);                   // refill this set two steps ahead
+      // x of token ts + m for m in [-3, U)
+      auto X = [&](int m, int j) -> float { return m >= 0 ? xc[m][j] : xw[-1 - m][j]; };
+#pragma unroll
+      for (int i = 0; i < U; ++i) {
+        dot[i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          const float u = wr[3][j] * X(i, j) + wr[2][j] * X(i - 1, j) + wr[1][j] * X(i - 2, j) + wr[0][j] * X(i - 3, j);
+          const float sg = sigmoid_f(u);
+          const float z = u * sg;
+          const float f = sg * (1.f + u - z);
+          dot[i] += gf[i][j] * z;
+          gf[i][j] *= f;
+          zf[i][j] = z * f;
+        }
+      }
+      if (l2) {
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1)
+#pragma unroll
+          for (int i = 0; i < U; ++i) dot[i] += __shfl_xor_sync(0xffffffffu, dot[i], o);
+        if (lane == 0)
+#pragma unroll
+          for (int i = 0; i < U; ++i) dot_x[pair][half][par][i] = dot[i];
+        asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
+#pragma unroll
+        for (int i = 0; i < U; ++i) {
+          const float c3 = rn[i] * rn[i] * rn[i] * (dot[i] + dot_x[pair][half ^ 1][par][i]);
+#pragma unroll
+          for (int j = 0; j < VEC; ++j) gf[i][j] = rn[i] * gf[i][j] - c3 * zf[i][j];     // du
+        }
+        par ^= 1;
+      }
+#pragma unroll
+      for (int i = 0; i < U; ++i) {
+        if (ts + i < t_end) {                          // the run's own token: weight gradient
+#pragma unroll
+          for (int k = 0; k < K; ++k)
+#pragma unroll
+            for (int j = 0; j < VEC; ++j) dwa[k][j] += gf[i][j] * X(i - (K - 1) + k, j);
+        }
+      }
+      // du of token ts + m for m in [-3, U)
+      auto DU = [&](int m, int j) -> float { return m >= 0 ? gf[m][j] : dw3[-1 - m][j]; };
+#pragma unroll
+      for (int i = 0; i < U; ++i) {
+        const long long s = ts - (K - 1) + i;          // dx[s] needs du(s .. s + 3)
+        if (s >= t0 && s < t_end) {
+          float o[VEC];
+#pragma unroll
+          for (int j = 0; j < VEC; ++j)
+            o[j] = wr[3][j] * DU(i - 3, j) + wr[2][j] * DU(i - 2, j) + wr[1][j] * DU(i - 1, j) + wr[0][j] * DU(i, j);
+          if (VAGUS_CHECK((b * L + s) * lddx + c0 + VEC - 1, (long long)gridDim.z * L * lddx)) {
+            __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
+            if constexpr (VEC == 4)
+              *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+            else
+              *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
+          }
+        }
+      }
+      // slide the windows by U tokens (highest index first: it reads the lower, older entries)
+#pragma unroll
+      for (int k = K - 2; k >= 0; --k)
+#pragma unroll
+        for (int j = 0; j < VEC; ++j) {
+          xw[k][j] = U - 1 - k >= 0 ? xc[U - 1 - k >= 0 ? U - 1 - k : 0][j] : xw[k - U >= 0 ? k - U : 0][j];
+          dw3[k][j] = U - 1 - k >= 0 ? gf[U - 1 - k >= 0 ? U - 1 - k : 0][j] : dw3[k - U >= 0 ? k - U : 0][j];
+        }
+    };
+    load_step(ax, ag, t0);
+    load_step(bx, bg, t0 + U);
+    for (long long ts = t0;; ts += 2 * U) {
+      if (ts - (K - 1) >= t_end) break;                // pair-uniform
+      step(ax, ag, ts);
+      if (ts + U - (K - 1) >= t_end) break;
+      step(bx, bg, ts + U);
+    }
+  }
+  // dw: sum over the CTA's pairs, one atomic per (channel, tap)
+#pragma unroll
+  for (int k = 0; k < K; ++k)
+#pragma unroll
+    for (int j = 0; j < VEC; ++j) red[pair][k][ch + j] = dwa[k][j];
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < HD * K; idx += NT) {
+    const int c = idx / K, k = idx - c * K;
+    float sum = 0.f;
+#pragma unroll
+    for (int q = 0; q < PAIRS; ++q) sum += red[q][k][c];
+    atomicAdd(&dw[(long long)(head * HD + c) * K + k], sum);
+  }
+}
+
+template <int VEC, int U, int NT, int MINB>
+void launch_bwd_step(const void* dy, const void* xp, long long ldx, const float* w, const float* rnorm, void* dx,
+                     long long lddx, float* dw, long long B, long long L, int D, int head_dim, int l2, int sms,
+                     cudaStream_t st) {
+  const long long runs = (L + RUN - 1) / RUN;
+  const long long ctas_per_seq = (runs + NT / 64 - 1) / (NT / 64);
+  const long long seqs = B * (D / head_dim);
+  // about two waves of CTAs; each CTA loops over runs of its (batch, head)
+  const long long bx = std::max<long long>(1, std::min<long long>(ctas_per_seq, (2LL * MINB * sms + seqs - 1) / seqs));
+  dim3 grid(static_cast<unsigned>(bx), D / head_dim, static_cast<unsigned>(B));
+  conv_bwd_step_k<VEC, U, NT, MINB><<<grid, NT, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w,
+                                                         rnorm, (__nv_bfloat16*)dx, lddx, dw, L, D, l2);
+}
+
 template <int VEC, int K>
 int launch_fwd(const void* xp, long long ldx, const float* w, void* y, float* rnorm, long long B, long long L, int D,
                int l2, cudaStream_t st) {
@@ -605,6 +789,21 @@ int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w,
     return 5;
   int rc = 5;
   static const bool staged = std::getenv("VAGUS_CONV_STAGED") != nullptr;
+  static const int variant = std::getenv("VAGUS_CONV_BWD") ? std::atoi(std::getenv("VAGUS_CONV_BWD")) : 0;
+  if ((head_dim == 256 || head_dim == 128) && !staged && variant > 0) {
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (head_dim == 256) {
+      if (variant == 1) launch_bwd_step<4, 4, 128, 3>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
+      else if (variant == 2) launch_bwd_step<4, 2, 256, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
+      else if (variant == 3) launch_bwd_step<4, 2, 128, 3>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
+      else launch_bwd_step<4, 4, 128, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
+    } else {
+      launch_bwd_step<2, 4, 128, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
+    }
+    return cudaGetLastError() == cudaSuccess ? 0 : 3;
+  }
   if ((head_dim == 256 || head_dim == 128) && !staged) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
