@@ -343,8 +343,8 @@ conv_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict
 }
 
 // ----------------------------------------------------- backward, one pass --
-// For heads of 128 / 256 channels: a pair of warps (64 lanes, VEC = HD / 64
-// channels each) walks a run of RW consecutive tokens once, with the last
+// For heads of 128 channels (256 take the step kernel below): a pair of warps (64 lanes, VEC = HD / 64
+// channels each) walks a run of run_len consecutive tokens once, with the last
 // K - 1 inputs and the last K - 1 values of du = dL/du in registers:
 //   token t:  u(t) from x[t-3..t];  du(t) through the L2 norm (the head's dot
 //             product is a warp sum plus one exchange between the pair's two
@@ -352,11 +352,10 @@ conv_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict
 //             tokens;  dx[t-3] = sum_i w[3-i] du(t-3+i) is then complete.
 // The run reads x and dy straight from global memory (each warp pair's row is
 // one contiguous 2 * HD-byte segment), with the next four tokens' loads in
-// flight; its K - 1 right-context tokens are recomputed (3 / RW extra work).
+// flight; its K - 1 right-context tokens are recomputed (3 / run_len extra work).
 // No shared-memory staging, no block-wide barriers: the cost per element is
 // the arithmetic of the chain rule.  dw is summed over the CTA's pairs in
 // shared memory and added with one atomic per (channel, tap) per CTA.
-constexpr int RUN = 64;                     // tokens per warp-pair run
 
 template <int VEC>
 __device__ __forceinline__ void ldg_row(const __nv_bfloat16* p, bool ok, uint32_t (&r)[VEC / 2]) {
@@ -382,7 +381,7 @@ template <int VEC, int PF>
 __global__ void __launch_bounds__(THREADS, 2)
 conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
                const float* __restrict__ w, const float* __restrict__ rnorm, __nv_bfloat16* __restrict__ dx,
-               long long lddx, float* __restrict__ dw, long long L, int D, int l2) {
+               long long lddx, float* __restrict__ dw, long long L, int D, int l2, int run_len) {
   constexpr int K = 4;
   constexpr int HD = VEC * 64;
   constexpr int PAIRS = WARPS / 2;
@@ -406,11 +405,11 @@ conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __rest
   for (int k = 0; k < K; ++k)
 #pragma unroll
     for (int j = 0; j < VEC; ++j) dwa[k][j] = 0.f;
-  const long long runs = (L + RUN - 1) / RUN;
+  const long long runs = (L + run_len - 1) / run_len;
   const int bar = 1 + pair;                 // named barrier of this warp pair (0 is __syncthreads)
   for (long long run = (long long)blockIdx.x * PAIRS + pair; run < runs; run += (long long)gridDim.x * PAIRS) {
-    const long long t0 = run * RUN;
-    const long long t_end = min(L, t0 + RUN);            // the run's own tokens end here
+    const long long t0 = run * run_len;
+    const long long t_end = min(L, t0 + run_len);            // the run's own tokens end here
     const __nv_bfloat16* xb = x + b * L * ldx + c0;
     const __nv_bfloat16* gb = dy + b * L * D + c0;
     float xw[K - 1][VEC];                                 // x[t-1], x[t-2], x[t-3]
@@ -428,7 +427,7 @@ conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __rest
       for (int j = 0; j < VEC; ++j) dw3[i][j] = 0.f;
     // PF tokens of loads in flight in a register queue (slot 0 = token t)
     uint32_t qx[PF][VEC / 2], qg[PF][VEC / 2];
-    const long long t_last = min(L, t0 + RUN + K - 1);   // du needed up to here (exclusive)
+    const long long t_last = min(L, t0 + run_len + K - 1);   // du needed up to here (exclusive)
 #pragma unroll
     for (int p = 0; p < PF; ++p) {
       const long long t = t0 + p;
@@ -557,7 +556,7 @@ template <int VEC, int U, int NT, int MINB>
 __global__ void __launch_bounds__(NT, MINB)
 conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
                 const float* __restrict__ w, const float* __restrict__ rnorm, __nv_bfloat16* __restrict__ dx,
-                long long lddx, float* __restrict__ dw, long long L, int D, int l2) {
+                long long lddx, float* __restrict__ dw, long long L, int D, int l2, int run_len) {
   constexpr int K = 4;
   constexpr int HD = VEC * 64;
   constexpr int PAIRS = NT / 64;
@@ -581,15 +580,15 @@ conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __res
   for (int k = 0; k < K; ++k)
 #pragma unroll
     for (int j = 0; j < VEC; ++j) dwa[k][j] = 0.f;
-  const long long runs = (L + RUN - 1) / RUN;
+  const long long runs = (L + run_len - 1) / run_len;
   const int bar = 1 + pair;                  // named barrier of this warp pair (0 is __syncthreads)
   const __nv_bfloat16* xb = x + b * L * ldx + c0;
   const __nv_bfloat16* gb = dy + b * L * D + c0;
   int par = 0;
   for (long long run = (long long)blockIdx.x * PAIRS + pair; run < runs; run += (long long)gridDim.x * PAIRS) {
-    const long long t0 = run * RUN;
-    const long long t_end = min(L, t0 + RUN);          // the run's own tokens end here
-    const long long t_load = min(L, t0 + RUN + K - 1); // du is needed up to here (exclusive)
+    const long long t0 = run * run_len;
+    const long long t_end = min(L, t0 + run_len);          // the run's own tokens end here
+    const long long t_load = min(L, t0 + run_len + K - 1); // du is needed up to here (exclusive)
     float xw[K - 1][VEC], dw3[K - 1][VEC];             // x and du of the 1st .. 3rd token before the step
 #pragma unroll
     for (int i = 0; i < K - 1; ++i) {
@@ -714,18 +713,44 @@ conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __res
   }
 }
 
+// Grid of the step kernel: CTA c of sequence (b, head) takes tokens
+// [c * PAIRS * run_len, (c + 1) * PAIRS * run_len), one run per warp pair.
+// The CTAs per sequence fill one wave of resident CTAs (nb per SM) when the
+// sequences allow it, so no CTA starts late and every pair's run has the same
+// length.
+struct RunGrid {
+  dim3 grid;
+  int run_len;
+};
+
+inline RunGrid run_grid(long long B, long long L, int D, int head_dim, int pairs, int nb, int sms) {
+  const long long seqs = B * (D / head_dim);
+  const long long resident = static_cast<long long>(std::max(nb, 1)) * sms;
+  long long cps = std::max<long long>(1, resident / seqs);            // CTAs per sequence
+  long long run_len = (L + cps * pairs - 1) / (cps * pairs);
+  run_len = std::max<long long>(32, (run_len + 3) / 4 * 4);           // a whole number of 4-token steps
+  cps = std::max<long long>(1, (L + run_len * pairs - 1) / (run_len * pairs));
+  RunGrid g;
+  g.grid = dim3(static_cast<unsigned>(cps), D / head_dim, static_cast<unsigned>(B));
+  g.run_len = static_cast<int>(run_len);
+  return g;
+}
+
+template <typename Kern>
+int resident_ctas(Kern k, int threads) {
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, k, threads, 0) != cudaSuccess) nb = 1;
+  return nb;
+}
+
 template <int VEC, int U, int NT, int MINB>
 void launch_bwd_step(const void* dy, const void* xp, long long ldx, const float* w, const float* rnorm, void* dx,
                      long long lddx, float* dw, long long B, long long L, int D, int head_dim, int l2, int sms,
                      cudaStream_t st) {
-  const long long runs = (L + RUN - 1) / RUN;
-  const long long ctas_per_seq = (runs + NT / 64 - 1) / (NT / 64);
-  const long long seqs = B * (D / head_dim);
-  // about two waves of CTAs; each CTA loops over runs of its (batch, head)
-  const long long bx = std::max<long long>(1, std::min<long long>(ctas_per_seq, (2LL * MINB * sms + seqs - 1) / seqs));
-  dim3 grid(static_cast<unsigned>(bx), D / head_dim, static_cast<unsigned>(B));
-  conv_bwd_step_k<VEC, U, NT, MINB><<<grid, NT, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w,
-                                                         rnorm, (__nv_bfloat16*)dx, lddx, dw, L, D, l2);
+  static const int nb = resident_ctas(conv_bwd_step_k<VEC, U, NT, MINB>, NT);
+  const RunGrid g = run_grid(B, L, D, head_dim, NT / 64, nb, sms);
+  conv_bwd_step_k<VEC, U, NT, MINB><<<g.grid, NT, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w,
+                                                           rnorm, (__nv_bfloat16*)dx, lddx, dw, L, D, l2, g.run_len);
 }
 
 template <int VEC, int K>
@@ -789,39 +814,29 @@ int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w,
     return 5;
   int rc = 5;
   static const bool staged = std::getenv("VAGUS_CONV_STAGED") != nullptr;
-  static const int variant = std::getenv("VAGUS_CONV_BWD") ? std::atoi(std::getenv("VAGUS_CONV_BWD")) : 0;
-  if ((head_dim == 256 || head_dim == 128) && !staged && variant > 0) {
+  if (head_dim == 256 && !staged) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (head_dim == 256) {
-      if (variant == 1) launch_bwd_step<4, 4, 128, 3>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
-      else if (variant == 2) launch_bwd_step<4, 2, 256, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
-      else if (variant == 3) launch_bwd_step<4, 2, 128, 3>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
-      else launch_bwd_step<4, 4, 128, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
-    } else {
-      launch_bwd_step<2, 4, 128, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
-    }
+    // four tokens per step, two CTAs of two warp pairs per SM (251 registers): at B = 8 / 16 x
+    // 4096 tokens, 4 heads of 256, 92 / 205 us against the one-token run kernel's 110 / 231 us
+    launch_bwd_step<4, 4, 128, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
-  if ((head_dim == 256 || head_dim == 128) && !staged) {
+  if (head_dim == 128 && !staged) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long long runs = (L + RUN - 1) / RUN;
+    const int run_len = 64;
+    const long long runs = (L + run_len - 1) / run_len;
     const long long ctas_per_seq = (runs + WARPS / 2 - 1) / (WARPS / 2);
     const long long seqs = B * (D / head_dim);
     // about two waves of CTAs in flight; each CTA loops over runs of its (batch, head)
     const long long bx = std::max<long long>(1, std::min<long long>(ctas_per_seq, (4LL * sms + seqs - 1) / seqs));
     dim3 grid(static_cast<unsigned>(bx), D / head_dim, static_cast<unsigned>(B));
-    // PF = 4 tokens of loads in flight per lane (6 and 8 measured no faster: the per-token chain,
-    // not the loads, sets the pace)
-    if (head_dim == 256)
-      conv_bwd_run_k<4, 4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
-                                                     (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
-    else
-      conv_bwd_run_k<2, 4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
-                                                     (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm);
+    // PF = 4 tokens of loads in flight per lane (6 and 8 measured no faster)
+    conv_bwd_run_k<2, 4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
+                                                   (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm, run_len);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
   if (head_dim == 256) rc = launch_bwd<8, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
