@@ -200,13 +200,15 @@ def test_qk_norm_rope_pitched():
     assert dP[:, :, :c0].abs().sum() == 0 and dP[:, :, c0 + H * D:].abs().sum() == 0
 
 
-@pytest.mark.parametrize("H,Hk,D,vm,rope,qkn", [(8, 8, 64, 1, True, False), (4, 2, 128, 1, True, True),
+@pytest.mark.parametrize("H,Hk,D,vm,rope,qkn", [(8, 8, 64, 1, True, False), (4, 2, 128, 1, True, False),
+                                                  (4, 2, 128, 1, True, True), (4, 2, 64, 2, True, False),
                                                   (4, 2, 64, 2, False, False), (4, 4, 64, 1, False, True)])
 def test_attention_layer_fused_matches_fp32(H, Hk, D, vm, rope, qkn):
     """The fused layer (q / k / v packed into one GEMM, RoPE on slices of it,
-    attention reading v out of it, one dgrad and one wgrad GEMM) against the
-    same module run unfused in fp32: output, input gradient, every weight
-    gradient and the qk-norm gains."""
+    attention reading v out of it, one dgrad and one wgrad GEMM; with RoPE
+    alone the attention backward un-rotates dq / dk itself) against the same
+    module run unfused in fp32: output, input gradient, every weight gradient
+    and the qk-norm gains."""
     from vagus_b200 import ops
     from vagus_b200.models.attention import SoftmaxAttention
     from vagus_b200.models.rope import RoPE

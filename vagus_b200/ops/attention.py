@@ -61,7 +61,9 @@ class _AttnLayer(torch.autograd.Function):
     qk-norm + RoPE kernel (one launch over both when neither has a norm gain),
     v is read by the attention kernels straight out of P, and the backward
     writes dv, then the un-rotated dq / dk, into one gradient dP, so the input
-    gradient and the three weight gradients are one GEMM each."""
+    gradient and the three weight gradients are one GEMM each.  With RoPE and
+    no qk norm the attention backward applies the rotation's transpose itself
+    (tcgen05 path: sequences of 128+ tokens, equal q / v head dims)."""
 
     @staticmethod
     def forward(ctx, x, Wp, wq, wk, wv, qg, kg, cos, sin, meta):
@@ -106,7 +108,10 @@ class _AttnLayer(torch.autograd.Function):
         dk_slice = dP4[:, :, Nq:Nq + Nk].view(B, L, Hk, D)
         dv_slice = dP4[:, :, Nq + Nk:].view(B, L, Hk, Dv)
         joint = rotate and qg is None and kg is None
-        if not rotate:
+        # RoPE alone: the tcgen05 backward un-rotates dq / dk itself (its dQ pass
+        # and dK epilogue) and writes them straight into dP
+        fused_rope = joint and cos is not None and L >= 128 and D == Dv
+        if not rotate or fused_rope:
             dq, dk = dq_slice, dk_slice
         elif joint:
             dqk = torch.empty(B, L, H + Hk, D, device=x2.device, dtype=torch.bfloat16)
@@ -117,13 +122,14 @@ class _AttnLayer(torch.autograd.Function):
         v = P4[:, :, Nq + Nk:].view(B, L, Hk, Dv)
         dO = dy.to(torch.bfloat16).view(B, L, H, Dv).transpose(1, 2)
         C.attn_bwd(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2), o, lse, dO, causal, 1.0 / math.sqrt(D),
-                   dq.transpose(1, 2), dk.transpose(1, 2), dv_slice.transpose(1, 2))
+                   dq.transpose(1, 2), dk.transpose(1, 2), dv_slice.transpose(1, 2),
+                   cos if fused_rope else None, sin if fused_rope else None)
         dqg = dkg = None
-        if joint:
+        if joint and not fused_rope:
             none = torch.empty(0, device=x2.device, dtype=torch.float32)
             C.qk_norm_rope_bwd(dqk, P4[:, :, :Nq + Nk].view(B, L, H + Hk, D), None, cos, sin, none,
                                dP4[:, :, :Nq + Nk].view(B, L, H + Hk, D))
-        elif rotate:
+        elif rotate and not joint:
             none = torch.empty(0, device=x2.device, dtype=torch.float32)
             _, g1 = C.qk_norm_rope_bwd(dq, P4[:, :, :Nq].view(B, L, H, D), qg, cos, sin,
                                        none if rq is None else rq, dq_slice)

@@ -683,6 +683,21 @@ __global__ void __launch_bounds__(256) attn_bwd_pre_v(const AttnBwdArgs a) {
 
 __global__ void attn_bwd_post(const AttnBwdArgs a);
 
+// The transpose of RoPE's interleaved-pair rotation on 8 adjacent channels
+// (4 pairs): (d0, d1) <- (d0 c + d1 s, -d0 s + d1 c) with the pairs' angles at
+// table entries [t0, t0 + 4) (16-byte aligned).
+__device__ __forceinline__ void unrotate8(float (&d)[8], const float* cosv, const float* sinv, long long t0) {
+  const float4 c4 = *reinterpret_cast<const float4*>(cosv + t0);
+  const float4 s4 = *reinterpret_cast<const float4*>(sinv + t0);
+  const float cc[4] = {c4.x, c4.y, c4.z, c4.w}, sn[4] = {s4.x, s4.y, s4.z, s4.w};
+#pragma unroll
+  for (int m = 0; m < 4; ++m) {
+    const float x0 = d[2 * m], x1 = d[2 * m + 1];
+    d[2 * m] = x0 * cc[m] + x1 * sn[m];
+    d[2 * m + 1] = -x0 * sn[m] + x1 * cc[m];
+  }
+}
+
 // dq = scale * dq_acc for head dims 64 / 128: D / 8 lanes per row, 8 values per
 // lane (two 16-byte loads, one 16-byte store into dq's strides)
 template <int D>
@@ -699,10 +714,11 @@ __global__ void __launch_bounds__(256) attn_bwd_post_v(const AttnBwdArgs a) {
     const long long bh = row / a.f.Lq, l = row - bh * a.f.Lq, b = bh / a.f.H, h = bh - b * a.f.H;
     const float4* src = reinterpret_cast<const float4*>(a.dq_acc + row * D + 8 * sub);
     const float4 v0 = src[0], v1 = src[1];
+    float d[8] = {sc * v0.x, sc * v0.y, sc * v0.z, sc * v0.w, sc * v1.x, sc * v1.y, sc * v1.z, sc * v1.w};
+    if (a.rope_cos) unrotate8(d, a.rope_cos, a.rope_sin, l * (D / 2) + 4 * sub);
     *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(a.dq) + b * a.sdq_b + h * a.sdq_h + l * a.sdq_l +
                               8 * sub) =
-        make_uint4(pack_bf16x2(sc * v0.x, sc * v0.y), pack_bf16x2(sc * v0.z, sc * v0.w),
-                   pack_bf16x2(sc * v1.x, sc * v1.y), pack_bf16x2(sc * v1.z, sc * v1.w));
+        make_uint4(pack_bf16x2(d[0], d[1]), pack_bf16x2(d[2], d[3]), pack_bf16x2(d[4], d[5]), pack_bf16x2(d[6], d[7]));
   }
 }
 
@@ -949,6 +965,8 @@ struct Params {
   __nv_bfloat16* dk;
   __nv_bfloat16* dv;
   long long sdk_b, sdk_h, sdk_l, sdv_b, sdv_h, sdv_l;   // element strides of dk / dv
+  const float* rope_cos;       // (Lk, D / 2) or null: dK leaves un-rotated at its key positions
+  const float* rope_sin;
   int lpt;                     // causal CTA order: 0 key-block-major per head, 1 key block first, g > 1 in groups of g
   int* err;
   unsigned long long* trace;   // phase clock of CTA (0, 0), [step][16]; null: off
@@ -1344,9 +1362,12 @@ attn_bwd_tc(const __grid_constant__ CUtensorMap mq, const __grid_constant__ CUte
 #pragma unroll
           for (int e = 0; e < 32; e += 8) {
             const float* f = reinterpret_cast<const float*>(&r[e]);
-            *reinterpret_cast<uint4*>(dst + e) =
-                make_uint4(pack_bf16x2(sc * f[0], sc * f[1]), pack_bf16x2(sc * f[2], sc * f[3]),
-                           pack_bf16x2(sc * f[4], sc * f[5]), pack_bf16x2(sc * f[6], sc * f[7]));
+            float d[8];
+#pragma unroll
+            for (int m = 0; m < 8; ++m) d[m] = sc * f[m];
+            if (which == 0 && p.rope_cos) unrotate8(d, p.rope_cos, p.rope_sin, (long long)kj * (D / 2) + (col + e) / 2);
+            *reinterpret_cast<uint4*>(dst + e) = make_uint4(pack_bf16x2(d[0], d[1]), pack_bf16x2(d[2], d[3]),
+                                                            pack_bf16x2(d[4], d[5]), pack_bf16x2(d[6], d[7]));
           }
         }
       }
@@ -1458,6 +1479,7 @@ int launch_bwd_tc(const AttnBwdArgs& a, cudaStream_t st) {
   p.dk = (__nv_bfloat16*)a.dk; p.dv = (__nv_bfloat16*)a.dv; p.err = f.err;
   p.sdk_b = a.sdk_b; p.sdk_h = a.sdk_h; p.sdk_l = a.sdk_l;
   p.sdv_b = a.sdv_b; p.sdv_h = a.sdv_h; p.sdv_l = a.sdv_l;
+  p.rope_cos = a.rope_cos; p.rope_sin = a.rope_sin;
   // causal order, measured at B = 4, 16 heads, L = 4096: head dim 64 key block first across all heads
   // (905 -> 814 us), head dim 128 in groups of 4 heads (1386 -> 1317 us; all heads at once lost
   // the heads' shared Q / dO reads in L2: 1433 us)
@@ -1530,8 +1552,12 @@ int attn_bwd(const AttnBwdArgs& a, cudaStream_t st) {
     if (x % 8) return 5;
   if (!aligned16(a.dq) || !aligned16(a.dk) || !aligned16(a.dv)) return 5;
   static const bool no_tc = std::getenv("VAGUS_ATTN_NO_TC") != nullptr;
-  if (!no_tc && a.f.err && a.f.Lq >= 128 && a.f.Lk >= 128 && a.f.D == a.f.Dv && (a.f.D == 64 || a.f.D == 128))
-    return a.f.D == 64 ? launch_bwd_tc<64>(a, st) : launch_bwd_tc<128>(a, st);
+  const bool tc = !no_tc && a.f.err && a.f.Lq >= 128 && a.f.Lk >= 128 && a.f.D == a.f.Dv &&
+                  (a.f.D == 64 || a.f.D == 128);
+  // un-rotating dq / dk is a step of the tcgen05 path's dQ pass and dK epilogue only
+  if (a.rope_cos && (!tc || !a.rope_sin || a.f.Lq != a.f.Lk || !aligned16(a.rope_cos) || !aligned16(a.rope_sin)))
+    return 5;
+  if (tc) return a.f.D == 64 ? launch_bwd_tc<64>(a, st) : launch_bwd_tc<128>(a, st);
   if (a.f.D == 64 && a.f.Dv == 64) return launch_bwd<64, 64>(a, st);
   if (a.f.D == 128 && a.f.Dv == 128) return launch_bwd<128, 128>(a, st);
   if (a.f.D == 64 && a.f.Dv == 128) return launch_bwd<64, 128>(a, st);

@@ -73,7 +73,8 @@ Tensor grad_out(const c10::optional<Tensor>& given, const Tensor& x, const char*
 // are multiples of 8 elements)
 std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse, Tensor dO, bool causal,
                              double scale, c10::optional<Tensor> dq_out, c10::optional<Tensor> dk_out,
-                             c10::optional<Tensor> dv_out) {
+                             c10::optional<Tensor> dv_out, c10::optional<Tensor> rope_cos,
+                             c10::optional<Tensor> rope_sin) {
   TORCH_CHECK(lse.is_contiguous() && dO.sizes() == o.sizes(), "attn_bwd: contiguous lse, dO shaped like o");
   if (dO.strides() != o.strides()) {
     auto t = torch::empty_like(o);
@@ -93,6 +94,15 @@ std::vector<Tensor> attn_bwd(Tensor q, Tensor k, Tensor v, Tensor o, Tensor lse,
   auto delta = torch::empty({q.size(0), q.size(1), q.size(2)}, q.options().dtype(at::kFloat));
   b.dq = dq.data_ptr(); b.dk = dk.data_ptr(); b.dv = dv.data_ptr();
   b.dq_acc = dq_acc.data_ptr<float>(); b.delta = delta.data_ptr<float>();
+  if (rope_cos.has_value() && rope_cos->defined()) {
+    TORCH_CHECK(rope_sin.has_value() && rope_sin->defined(), "attn_bwd: rope_cos needs rope_sin");
+    for (const Tensor* t : {&*rope_cos, &*rope_sin})
+      TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->dim() == 2 && t->size(0) == k.size(2) &&
+                      t->size(1) == q.size(3) / 2,
+                  "attn_bwd: RoPE tables (Lk, D / 2) fp32 contiguous");
+    b.rope_cos = rope_cos->data_ptr<float>();
+    b.rope_sin = rope_sin->data_ptr<float>();
+  }
   check(vagus::attn_bwd(b, stream()), "attn_bwd");
   return {dq, dk, dv};
 }
@@ -104,7 +114,8 @@ void register_attn_ops(pybind11::module& m) {
   m.def("attn_bwd", &attn_bwd, pybind11::arg("q"), pybind11::arg("k"), pybind11::arg("v"), pybind11::arg("o"),
         pybind11::arg("lse"), pybind11::arg("dO"), pybind11::arg("causal"), pybind11::arg("scale"),
         pybind11::arg("dq_out") = pybind11::none(), pybind11::arg("dk_out") = pybind11::none(),
-        pybind11::arg("dv_out") = pybind11::none());
+        pybind11::arg("dv_out") = pybind11::none(), pybind11::arg("rope_cos") = pybind11::none(),
+        pybind11::arg("rope_sin") = pybind11::none());
   // buf: int64 device tensor of 512 entries, or None
   m.def("attn_set_trace", [](c10::optional<Tensor> buf) {
     if (buf) TORCH_CHECK(buf->is_cuda() && buf->numel() >= 512 && buf->element_size() == 8, "attn_set_trace: 512 x u64");

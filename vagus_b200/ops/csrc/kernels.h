@@ -140,6 +140,12 @@ struct AttnBwdArgs {
   long long sdq_b, sdq_h, sdq_l, sdk_b, sdk_h, sdk_l, sdv_b, sdv_h, sdv_l;   // element strides (unit inner)
   float* dq_acc;             // fp32 scratch (B, H, Lq, D)
   float* delta;              // fp32 scratch (B, H, Lq)
+  // optional RoPE tables (L, D / 2) fp32, Lq == Lk == L: q and k were rotated by
+  // interleaved pairs at their positions, and dq / dk leave un-rotated (the
+  // rotation's transpose applied in the dQ pass and the dK epilogue; the
+  // tcgen05 path at head dims 64 / 128 only)
+  const float* rope_cos = nullptr;
+  const float* rope_sin = nullptr;
 };
 int attn_bwd(const AttnBwdArgs& a, cudaStream_t st);
 // Phase clock of the tcgen05 backward's CTA (0, 0): clock64() at 16 phase
