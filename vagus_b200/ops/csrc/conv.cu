@@ -587,39 +587,47 @@ conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __res
   int par = 0;
   for (long long run = (long long)blockIdx.x * PAIRS + pair; run < runs; run += (long long)gridDim.x * PAIRS) {
     const long long t0 = run * run_len;
-    const long long t_end = min(L, t0 + run_len);          // the run's own tokens end here
-    const long long t_load = min(L, t0 + run_len + K - 1); // du is needed up to here (exclusive)
+    // token offsets within the run are 32-bit: m = t - t0
+    const int n_end = static_cast<int>(min(L, t0 + run_len) - t0);          // the run's own tokens
+    const int n_load = static_cast<int>(min(L, t0 + run_len + K - 1) - t0); // du is needed below this
+    const __nv_bfloat16* xr = xb + t0 * ldx;
+    const __nv_bfloat16* gr = gb + t0 * D;
+    const float* rr = l2 ? rnorm + (b * L + t0) * nH + head : nullptr;
+    __nv_bfloat16* dxr = dx + (b * L + t0) * lddx + c0;
     float xw[K - 1][VEC], dw3[K - 1][VEC];             // x and du of the 1st .. 3rd token before the step
 #pragma unroll
     for (int i = 0; i < K - 1; ++i) {
-      const long long t = t0 - 1 - i;
       uint32_t r[VEC / 2];
-      ldg_row<VEC>(xb + t * ldx, t >= 0, r);
+      ldg_row<VEC>(xr - (long long)(1 + i) * ldx, t0 - 1 - i >= 0, r);
       unpack_row<VEC>(r, xw[i]);
 #pragma unroll
       for (int j = 0; j < VEC; ++j) dw3[i][j] = 0.f;
     }
     uint32_t ax[U][VEC / 2], ag[U][VEC / 2], bx[U][VEC / 2], bg[U][VEC / 2];
-    auto load_step = [&](uint32_t (&qx)[U][VEC / 2], uint32_t (&qg)[U][VEC / 2], long long ts) {
+    auto load_step = [&](uint32_t (&qx)[U][VEC / 2], uint32_t (&qg)[U][VEC / 2], int ms) {
+      const __nv_bfloat16* px = xr + (long long)ms * ldx;
+      const __nv_bfloat16* pg = gr + (long long)ms * D;
 #pragma unroll
       for (int i = 0; i < U; ++i) {
-        const long long t = ts + i;
-        const bool ok = t < t_load;
-        ldg_row<VEC>(xb + t * ldx, ok, qx[i]);
-        ldg_row<VEC>(gb + t * D, ok, qg[i]);
+        const bool ok = ms + i < n_load;
+        ldg_row<VEC>(px, ok, qx[i]);
+        ldg_row<VEC>(pg, ok, qg[i]);
+        px += ldx;
+        pg += D;
       }
     };
-    // one step: du of tokens ts .. ts + U - 1, dx of tokens ts - 3 .. ts + U - 4
-    auto step = [&](uint32_t (&qx)[U][VEC / 2], uint32_t (&qg)[U][VEC / 2], long long ts) {
+    // one step: du of tokens ms .. ms + U - 1, dx of tokens ms - 3 .. ms + U - 4 (run offsets)
+    auto step = [&](uint32_t (&qx)[U][VEC / 2], uint32_t (&qg)[U][VEC / 2], int ms) {
       float xc[U][VEC], gf[U][VEC], zf[U][VEC], dot[U], rn[U];
 #pragma unroll
       for (int i = 0; i < U; ++i) {
         unpack_row<VEC>(qx[i], xc[i]);
         unpack_row<VEC>(qg[i], gf[i]);
-        rn[i] = l2 && ts + i < L ? __ldg(rnorm + (b * L + ts + i) * nH + head) : 0.f;
+        // past n_load du is never used: rn only has to be finite there
+        rn[i] = l2 && ms + i < n_load ? __ldg(rr + (ms + i) * nH) : 0.f;
       }
-      load_step(qx, qg, ts + 2 * U);                   // refill this set two steps ahead
-      // x of token ts + m for m in [-3, U)
+      load_step(qx, qg, ms + 2 * U);                   // refill this set two steps ahead
+      // x of token ms + m for m in [-3, U)
       auto X = [&](int m, int j) -> float { return m >= 0 ? xc[m][j] : xw[-1 - m][j]; };
 #pragma unroll
       for (int i = 0; i < U; ++i) {
@@ -654,29 +662,29 @@ conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __res
       }
 #pragma unroll
       for (int i = 0; i < U; ++i) {
-        if (ts + i < t_end) {                          // the run's own token: weight gradient
+        if (ms + i < n_end) {                          // the run's own token: weight gradient
 #pragma unroll
           for (int k = 0; k < K; ++k)
 #pragma unroll
             for (int j = 0; j < VEC; ++j) dwa[k][j] += gf[i][j] * X(i - (K - 1) + k, j);
         }
       }
-      // du of token ts + m for m in [-3, U)
+      // du of token ms + m for m in [-3, U)
       auto DU = [&](int m, int j) -> float { return m >= 0 ? gf[m][j] : dw3[-1 - m][j]; };
+      __nv_bfloat16* pd = dxr + (long long)(ms - (K - 1)) * lddx;
 #pragma unroll
-      for (int i = 0; i < U; ++i) {
-        const long long s = ts - (K - 1) + i;          // dx[s] needs du(s .. s + 3)
-        if (s >= t0 && s < t_end) {
+      for (int i = 0; i < U; ++i, pd += lddx) {
+        const int sm = ms - (K - 1) + i;               // dx[sm] needs du(sm .. sm + 3)
+        if (sm >= 0 && sm < n_end) {
           float o[VEC];
 #pragma unroll
           for (int j = 0; j < VEC; ++j)
             o[j] = wr[3][j] * DU(i - 3, j) + wr[2][j] * DU(i - 2, j) + wr[1][j] * DU(i - 1, j) + wr[0][j] * DU(i, j);
-          if (VAGUS_CHECK((b * L + s) * lddx + c0 + VEC - 1, (long long)gridDim.z * L * lddx)) {
-            __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
+          if (VAGUS_CHECK((b * L + t0 + sm) * lddx + c0 + VEC - 1, (long long)gridDim.z * L * lddx)) {
             if constexpr (VEC == 4)
-              *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
+              *reinterpret_cast<uint2*>(pd) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
             else
-              *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
+              *reinterpret_cast<uint32_t*>(pd) = pack_bf16x2(o[0], o[1]);
           }
         }
       }
@@ -689,13 +697,13 @@ conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __res
           dw3[k][j] = U - 1 - k >= 0 ? gf[U - 1 - k >= 0 ? U - 1 - k : 0][j] : dw3[k - U >= 0 ? k - U : 0][j];
         }
     };
-    load_step(ax, ag, t0);
-    load_step(bx, bg, t0 + U);
-    for (long long ts = t0;; ts += 2 * U) {
-      if (ts - (K - 1) >= t_end) break;                // pair-uniform
-      step(ax, ag, ts);
-      if (ts + U - (K - 1) >= t_end) break;
-      step(bx, bg, ts + U);
+    load_step(ax, ag, 0);
+    load_step(bx, bg, U);
+    for (int ms = 0;; ms += 2 * U) {
+      if (ms - (K - 1) >= n_end) break;                // pair-uniform
+      step(ax, ag, ms);
+      if (ms + U - (K - 1) >= n_end) break;
+      step(bx, bg, ms + U);
     }
   }
   // dw: sum over the CTA's pairs, one atomic per (channel, tap)
@@ -818,8 +826,9 @@ int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w,
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // four tokens per step, two CTAs of two warp pairs per SM (251 registers): at B = 8 / 16 x
-    // 4096 tokens, 4 heads of 256, 92 / 205 us against the one-token run kernel's 110 / 231 us
+    // four tokens per step, two CTAs of two warp pairs per SM (237 registers): at B = 8 / 16 x
+    // 4096 tokens, 4 heads of 256, 86 / 174 us against the one-token run kernel's 110 / 231 us
+    // (95 / 205 us with 64-bit token arithmetic per access instead of run-relative offsets)
     launch_bwd_step<4, 4, 128, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
