@@ -9,7 +9,7 @@ measured peak (``MEASURED_PEAKS.json`` at the repository root: STREAM-style
 copy bandwidth and the cuBLAS bf16 GEMM rate).  Inputs are random; the
 shapes are those of one micro-batch of the 340M GDN model (dim 1024, 4 heads
 of 256, conv 4, packed projection width 4160) unless overridden.  Cases:
-conv_fwd, conv_bwd, gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
+conv_fwd, conv_bwd (and conv_fwd_h128 / conv_bwd_h128: heads of 128), gates, gdr_intra_fwd, gdr_fwd (intra + recurrence),
 gdr_bwd, gdr_rec_fwd, gdr_rec_bwd, gdr_intra_bwd, attn_fwd_d64 / d128,
 sdpa_fwd_d64 / d128 (torch's library kernel, for comparison), attn_bwd_d64 / d128, sdpa_bwd_d64 / d128, kda_gated_fwd, kda_gated_bwd, kda_intra_fwd, kda_intra_bwd, kda_gates_fwd / bwd, gemm_fwd, gemm_dgrad, gemm_wgrad, cublas_fwd / dgrad / wgrad (the same shapes on cuBLAS), rmsnorm, rope_fwd / bwd.  With no
 case names every
@@ -61,6 +61,10 @@ def _cases(B: int, L: int):
     mb = T * D * 2
     cases["conv_fwd"] = (lambda: C.conv_silu_fwd(x, w, hd, True), 2 * mb, None)
     cases["conv_bwd"] = (lambda: C.conv_silu_bwd(dy, x, w, rn, dP[:, :, :D], dw, hd, True), 3 * mb, None)
+    # the same stream split into heads of 128 (the per-channel-gate layers' q / k)
+    y1, rn1 = C.conv_silu_fwd(x, w, 128, True)
+    cases["conv_fwd_h128"] = (lambda: C.conv_silu_fwd(x, w, 128, True), 2 * mb, None)
+    cases["conv_bwd_h128"] = (lambda: C.conv_silu_bwd(dy, x, w, rn1, dP[:, :, :D], dw, 128, True), 3 * mb, None)
 
     ab = P.reshape(T, NP)[:, 4 * D:4 * D + 2 * H]
     A_log, dt_bias = torch.randn(H, device=dev), torch.randn(H, device=dev)

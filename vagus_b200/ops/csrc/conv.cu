@@ -13,11 +13,13 @@
 // a column block of a wider packed matrix (row pitch ldx); dx is written with
 // its own pitch into the packed gradient.
 //
-// Backward: phase 1 recomputes u, z and forms du = dL/du for T + K - 1 rows
-// into shared memory (fp32); phase 2 gives dx[t] = sum_i w[K-1-i] du[t+i] and
-// accumulates dw in registers.  Backward CTAs are persistent over the tiles of
-// their (batch, head), so dw is reduced over warps in shared memory and added
-// with one atomic per (channel, tap) per CTA.
+// Backward, heads of 128 / 256: warp pairs walk runs of tokens in registers,
+// four tokens per step (conv_bwd_step_k below).  Other head dims: phase 1
+// recomputes u, z and forms du = dL/du for T + K - 1 rows into shared memory
+// (fp32); phase 2 gives dx[t] = sum_i w[K-1-i] du[t+i] and accumulates dw in
+// registers; CTAs are persistent over the tiles of their (batch, head), so dw
+// is reduced over warps in shared memory and added with one atomic per
+// (channel, tap) per CTA.
 #include "common.cuh"
 #include "kernels.h"
 
@@ -342,20 +344,26 @@ conv_bwd_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict
   }
 }
 
-// ----------------------------------------------------- backward, one pass --
-// For heads of 128 channels (256 take the step kernel below): a pair of warps (64 lanes, VEC = HD / 64
-// channels each) walks a run of run_len consecutive tokens once, with the last
-// K - 1 inputs and the last K - 1 values of du = dL/du in registers:
+// ------------------------------------------------- backward, token runs --
+// For heads of 128 / 256 channels: a pair of warps (64 lanes, VEC = HD / 64
+// channels each) walks a run of consecutive tokens once, U = 4 tokens per
+// step, with the last K - 1 inputs and the last K - 1 values of du = dL/du in
+// registers:
 //   token t:  u(t) from x[t-3..t];  du(t) through the L2 norm (the head's dot
 //             product is a warp sum plus one exchange between the pair's two
-//             warps) and SiLU;  dw[k] += du(t) x[t-3+k] for the run's own
-//             tokens;  dx[t-3] = sum_i w[3-i] du(t-3+i) is then complete.
-// The run reads x and dy straight from global memory (each warp pair's row is
-// one contiguous 2 * HD-byte segment), with the next four tokens' loads in
-// flight; its K - 1 right-context tokens are recomputed (3 / run_len extra work).
-// No shared-memory staging, no block-wide barriers: the cost per element is
-// the arithmetic of the chain rule.  dw is summed over the CTA's pairs in
-// shared memory and added with one atomic per (channel, tap) per CTA.
+//             warps, once per step for the step's U tokens) and SiLU;
+//             dw[k] += du(t) x[t-3+k] for the run's own tokens;
+//             dx[t-3] = sum_i w[3-i] du(t-3+i) is then complete.
+// The U tokens' chains interleave.  x and dy come straight from global memory
+// (each warp pair's row is one contiguous 2 * HD-byte segment) two steps ahead,
+// in two register sets that alternate between the steps, so the prefetch queue
+// costs no register moves; the run's K - 1 right-context tokens are recomputed.
+// Token offsets inside a run are 32-bit and the pointers advance per step.
+// Per element only x, g f and z f stay live across the exchange, where
+// z = silu(u) and f = silu'(u) = s (1 + u - z):  du = rn g f - c3 z f with
+// c3 = rn^3 <g, z>_head under the L2 norm, du = g f without it.  dw is summed
+// over the CTA's pairs in shared memory and added with one atomic per
+// (channel, tap) per CTA.
 
 template <int VEC>
 __device__ __forceinline__ void ldg_row(const __nv_bfloat16* p, bool ok, uint32_t (&r)[VEC / 2]) {
@@ -377,181 +385,6 @@ __device__ __forceinline__ void unpack_row(const uint32_t (&r)[VEC / 2], float (
   }
 }
 
-template <int VEC, int PF>
-__global__ void __launch_bounds__(THREADS, 2)
-conv_bwd_run_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
-               const float* __restrict__ w, const float* __restrict__ rnorm, __nv_bfloat16* __restrict__ dx,
-               long long lddx, float* __restrict__ dw, long long L, int D, int l2, int run_len) {
-  constexpr int K = 4;
-  constexpr int HD = VEC * 64;
-  constexpr int PAIRS = WARPS / 2;
-  __shared__ float dot_x[PAIRS][2][2];       // [pair][warp of the pair][token parity]
-  __shared__ float red[PAIRS][K][HD];
-  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
-  const int pair = warp >> 1, half = warp & 1;
-  const int ch = (half * 32 + lane) * VEC;  // first channel of this thread within the head
-  const long long b = blockIdx.z;
-  const int head = blockIdx.y;
-  const int nH = D / HD;
-  const int c0 = head * HD + ch;
-  float wr[K][VEC];
-#pragma unroll
-  for (int j = 0; j < VEC; ++j) {
-    const float4 t = *reinterpret_cast<const float4*>(w + (long long)(c0 + j) * K);
-    wr[0][j] = t.x; wr[1][j] = t.y; wr[2][j] = t.z; wr[3][j] = t.w;
-  }
-  float dwa[K][VEC];
-#pragma unroll
-  for (int k = 0; k < K; ++k)
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) dwa[k][j] = 0.f;
-  const long long runs = (L + run_len - 1) / run_len;
-  const int bar = 1 + pair;                 // named barrier of this warp pair (0 is __syncthreads)
-  for (long long run = (long long)blockIdx.x * PAIRS + pair; run < runs; run += (long long)gridDim.x * PAIRS) {
-    const long long t0 = run * run_len;
-    const long long t_end = min(L, t0 + run_len);            // the run's own tokens end here
-    const __nv_bfloat16* xb = x + b * L * ldx + c0;
-    const __nv_bfloat16* gb = dy + b * L * D + c0;
-    float xw[K - 1][VEC];                                 // x[t-1], x[t-2], x[t-3]
-#pragma unroll
-    for (int i = 0; i < K - 1; ++i) {
-      const long long t = t0 - 1 - i;
-      uint32_t r[VEC / 2];
-      ldg_row<VEC>(xb + t * ldx, t >= 0, r);
-      unpack_row<VEC>(r, xw[i]);
-    }
-    float dw3[K - 1][VEC];                                // du(t-1), du(t-2), du(t-3)
-#pragma unroll
-    for (int i = 0; i < K - 1; ++i)
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) dw3[i][j] = 0.f;
-    // PF tokens of loads in flight in a register queue (slot 0 = token t)
-    uint32_t qx[PF][VEC / 2], qg[PF][VEC / 2];
-    const long long t_last = min(L, t0 + run_len + K - 1);   // du needed up to here (exclusive)
-#pragma unroll
-    for (int p = 0; p < PF; ++p) {
-      const long long t = t0 + p;
-      ldg_row<VEC>(xb + t * ldx, t < t_last, qx[p]);
-      ldg_row<VEC>(gb + t * D, t < t_last, qg[p]);
-    }
-    const __nv_bfloat16* nx = xb + (t0 + PF) * ldx;       // the next token to fetch
-    const __nv_bfloat16* ng = gb + (t0 + PF) * D;
-    for (long long t = t0; t < t_last; ++t) {
-      {
-        float xc[VEC], g[VEC];
-        unpack_row<VEC>(qx[0], xc);
-        unpack_row<VEC>(qg[0], g);
-#pragma unroll
-        for (int p = 0; p + 1 < PF; ++p)
-#pragma unroll
-          for (int j = 0; j < VEC / 2; ++j) { qx[p][j] = qx[p + 1][j]; qg[p][j] = qg[p + 1][j]; }
-        {
-          const bool ok = t + PF < t_last;
-          ldg_row<VEC>(nx, ok, qx[PF - 1]);
-          ldg_row<VEC>(ng, ok, qg[PF - 1]);
-          nx += ldx;
-          ng += D;
-        }
-        float u[VEC], sg[VEC], z[VEC];
-        float dot = 0.f;
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          u[j] = wr[3][j] * xc[j] + wr[2][j] * xw[0][j] + wr[1][j] * xw[1][j] + wr[0][j] * xw[2][j];
-          sg[j] = sigmoid_f(u[j]);
-          z[j] = u[j] * sg[j];
-          dot += g[j] * z[j];
-        }
-        if (l2) {
-          const float rn = rnorm[(b * L + t) * nH + head];
-          dot = warp_sum(dot);
-          const int par = static_cast<int>(t & 1);
-          if (lane == 0) dot_x[pair][half][par] = dot;
-          asm volatile("bar.sync %0, 64;" ::"r"(bar) : "memory");
-          dot += dot_x[pair][half ^ 1][par];
-          const float c3 = rn * rn * rn * dot;
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) g[j] = rn * g[j] - c3 * z[j];
-        }
-        float du[VEC];
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) du[j] = g[j] * sg[j] * (1.f + u[j] * (1.f - sg[j]));
-        if (t < t_end) {                                  // the run's own token: weight gradient
-#pragma unroll
-          for (int j = 0; j < VEC; ++j) {
-            dwa[0][j] += du[j] * xw[2][j];
-            dwa[1][j] += du[j] * xw[1][j];
-            dwa[2][j] += du[j] * xw[0][j];
-            dwa[3][j] += du[j] * xc[j];
-          }
-        }
-        const long long s = t - (K - 1);                  // dx[s] needs du(s .. s + 3)
-        if (s >= t0) {
-          float o[VEC];
-#pragma unroll
-          for (int j = 0; j < VEC; ++j)
-            o[j] = wr[3][j] * dw3[2][j] + wr[2][j] * dw3[1][j] + wr[1][j] * dw3[0][j] + wr[0][j] * du[j];
-          if (VAGUS_CHECK((b * L + s) * lddx + c0 + VEC - 1, (long long)gridDim.z * L * lddx)) {
-            __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
-            if constexpr (VEC == 4)
-              *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
-            else
-              *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < VEC; ++j) {
-          xw[2][j] = xw[1][j]; xw[1][j] = xw[0][j]; xw[0][j] = xc[j];
-          dw3[2][j] = dw3[1][j]; dw3[1][j] = dw3[0][j]; dw3[0][j] = du[j];
-        }
-      }
-    }
-    // tokens past the end of the sequence have du = 0 (dy is zero there):
-    // the run's last K - 1 dx rows, when the sequence ends inside the halo
-    for (long long s = max(t0, t_last - (K - 1)); s < t_end; ++s) {
-      // du(s + i) for s + i < t_last sits in dw3 at index t_last - 1 - (s + i)
-      float o[VEC];
-#pragma unroll
-      for (int j = 0; j < VEC; ++j) {
-        float acc = 0.f;
-#pragma unroll
-        for (int i = 0; i < K; ++i) {
-          const long long tt = s + i;
-          const long long back = t_last - 1 - tt;           // 0 .. 2 inside the window
-          if (tt < t_last && back < K - 1) acc += wr[K - 1 - i][j] * dw3[back][j];
-        }
-        o[j] = acc;
-      }
-      __nv_bfloat16* dst = dx + (b * L + s) * lddx + c0;
-      if constexpr (VEC == 4)
-        *reinterpret_cast<uint2*>(dst) = make_uint2(pack_bf16x2(o[0], o[1]), pack_bf16x2(o[2], o[3]));
-      else
-        *reinterpret_cast<uint32_t*>(dst) = pack_bf16x2(o[0], o[1]);
-    }
-  }
-  // dw: sum over the CTA's pairs, one atomic per (channel, tap)
-#pragma unroll
-  for (int k = 0; k < K; ++k)
-#pragma unroll
-    for (int j = 0; j < VEC; ++j) red[pair][k][ch + j] = dwa[k][j];
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < HD * K; idx += THREADS) {
-    const int c = idx / K, k = idx - c * K;
-    float sum = 0.f;
-#pragma unroll
-    for (int q = 0; q < PAIRS; ++q) sum += red[q][k][c];
-    atomicAdd(&dw[(long long)(head * HD + c) * K + k], sum);
-  }
-}
-
-// --------------------------------------------- backward, U tokens per step --
-// The run kernel above with the token loop unrolled U ways.  The U tokens'
-// chains (input window, SiLU, the head's dot product, du) interleave; the
-// pair's dot-product exchange is one barrier per step instead of one per
-// token; the loads run two steps (2 U tokens) ahead in two register sets that
-// alternate between the steps, so the prefetch queue costs no register moves.
-// Per element only x, g f and z f stay live across the exchange, where
-// z = silu(u) and f = silu'(u) = s (1 + u - z):  du = rn g f - c3 z f with
-// c3 = rn^3 <g, z>_head under the L2 norm, du = g f without it.
 template <int VEC, int U, int NT, int MINB>
 __global__ void __launch_bounds__(NT, MINB)
 conv_bwd_step_k(const __nv_bfloat16* __restrict__ dy, const __nv_bfloat16* __restrict__ x, long long ldx,
@@ -822,30 +655,18 @@ int conv_silu_bwd(const void* dy, const void* xp, long long ldx, const float* w,
     return 5;
   int rc = 5;
   static const bool staged = std::getenv("VAGUS_CONV_STAGED") != nullptr;
-  if (head_dim == 256 && !staged) {
+  if ((head_dim == 256 || head_dim == 128) && !staged) {
     int dev = 0, sms = 148;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // four tokens per step, two CTAs of two warp pairs per SM (237 registers): at B = 8 / 16 x
-    // 4096 tokens, 4 heads of 256, 86 / 174 us against the one-token run kernel's 110 / 231 us
-    // (95 / 205 us with 64-bit token arithmetic per access instead of run-relative offsets)
-    launch_bwd_step<4, 4, 128, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
-    return cudaGetLastError() == cudaSuccess ? 0 : 3;
-  }
-  if (head_dim == 128 && !staged) {
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int run_len = 64;
-    const long long runs = (L + run_len - 1) / run_len;
-    const long long ctas_per_seq = (runs + WARPS / 2 - 1) / (WARPS / 2);
-    const long long seqs = B * (D / head_dim);
-    // about two waves of CTAs in flight; each CTA loops over runs of its (batch, head)
-    const long long bx = std::max<long long>(1, std::min<long long>(ctas_per_seq, (4LL * sms + seqs - 1) / seqs));
-    dim3 grid(static_cast<unsigned>(bx), D / head_dim, static_cast<unsigned>(B));
-    // PF = 4 tokens of loads in flight per lane (6 and 8 measured no faster)
-    conv_bwd_run_k<2, 4><<<grid, THREADS, 0, st>>>((const __nv_bfloat16*)dy, (const __nv_bfloat16*)xp, ldx, w, rnorm,
-                                                   (__nv_bfloat16*)dx, lddx, dw, L, D, l2norm, run_len);
+    // At B = 8 x 4096 tokens, D = 1024: heads of 256 (237 registers, two CTAs of two pairs per
+    // SM) 86 us (174 us at B = 16), heads of 128 (128 registers, four CTAs per SM) 94 us; one
+    // token per iteration on a persistent grid took 110 / 204 us (231 us at B = 16, heads of
+    // 256), and the step kernel with 64-bit index products per access 95 us at heads of 256.
+    if (head_dim == 256)
+      launch_bwd_step<4, 4, 128, 2>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
+    else
+      launch_bwd_step<2, 4, 128, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, head_dim, l2norm, sms, st);
     return cudaGetLastError() == cudaSuccess ? 0 : 3;
   }
   if (head_dim == 256) rc = launch_bwd<8, 4>(dy, xp, ldx, w, rnorm, dx, lddx, dw, B, L, D, l2norm, st);
