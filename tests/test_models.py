@@ -217,3 +217,32 @@ def test_transformer_pp_generation_and_flops():
     assert m.attn_flops_per_token(2048) == 12 * 2 * 64 * 2048
     assert m.max_stream_len == 32
     assert set(m.metric_hooks()["slow"][0](MetricCtx(model=m, last_batch=ids))) == {"attn_logit_max"}
+
+
+def test_packed_attention_layer_gating(monkeypatch):
+    """Which softmax-attention layers and inputs take the packed q / k / v path
+    (``ops.attention_layer``): CUDA input in bf16 (or under bf16 autocast), no
+    short conv or output gate, head dims 64 / 128, GEMM-sized projections.
+    Checked on a stand-in for a CUDA tensor and for the extension, since only
+    the predicate runs."""
+    from types import SimpleNamespace
+    from vagus_b200 import ops
+    from vagus_b200.models.rope import RoPE
+    import vagus_b200.ops.attention as attn_ops
+    monkeypatch.setattr(attn_ops, "native", lambda: SimpleNamespace(attn_fwd=None))
+
+    def x_like(B, L, D, cuda=True, dtype=torch.bfloat16):
+        return SimpleNamespace(is_cuda=cuda, dtype=dtype, shape=(B, L, D), dim=lambda: 3)
+
+    def layer(dim=512, H=8, Hk=None, vm=1, **kw):
+        return SoftmaxAttention(dim, H, Hk, vm, rope=RoPE(dim, dim // H, 256), **kw)
+
+    assert ops.attention_layer_ok(layer(), x_like(2, 256, 512))
+    assert ops.attention_layer_ok(layer(Hk=2, qk_norm=True), x_like(2, 256, 512))
+    assert ops.attention_layer_ok(layer(H=4), x_like(2, 256, 512))                 # head dim 128
+    assert not ops.attention_layer_ok(layer(), x_like(2, 256, 512, cuda=False))
+    assert not ops.attention_layer_ok(layer(), x_like(2, 256, 512, dtype=torch.float32))
+    assert not ops.attention_layer_ok(layer(short_conv_size=4), x_like(2, 256, 512))
+    assert not ops.attention_layer_ok(layer(out_gate=True), x_like(2, 256, 512))
+    assert not ops.attention_layer_ok(layer(H=16), x_like(2, 256, 512))            # head dim 32
+    assert not ops.attention_layer_ok(layer(), x_like(1, 64, 512))                 # 64 tokens: below a GEMM tile
