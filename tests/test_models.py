@@ -228,7 +228,8 @@ def test_packed_attention_layer_gating(monkeypatch):
     from types import SimpleNamespace
     from vagus_b200 import ops
     from vagus_b200.models.rope import RoPE
-    import vagus_b200.ops.attention as attn_ops
+    import importlib
+    attn_ops = importlib.import_module("vagus_b200.ops.attention")   # the module, not the function ops.attention
     monkeypatch.setattr(attn_ops, "native", lambda: SimpleNamespace(attn_fwd=None))
 
     def x_like(B, L, D, cuda=True, dtype=torch.bfloat16):
